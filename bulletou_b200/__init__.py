@@ -1,0 +1,31 @@
+"""bulletou_b200 -- B200-native (sm_100a) implementation of BulletOu's training hot path.
+
+The compute lives in libbulletou_b200.so (hand-written CUDA behind a C ABI that
+mirrors the reference's cuda-cpp backend); this package is the host-side
+mirror of the reference's Rust crate API (see cuda_cpp.py) plus the seeded
+synthetic data generator used by tests and benchmarks.
+"""
+from ._lib import CudaCppError, Library, library, reference_library  # noqa: F401
+from .cuda_cpp import (  # noqa: F401
+    FLT_MAX,
+    NNUE_HALFKP_256X2_32_32,
+    Context,
+    Event,
+    F32Buffer,
+    GraphExec,
+    I32Buffer,
+    KpptTableTrainStepRunner,
+    NnueForwardHostWeights,
+    NnueForwardShape,
+    NnueTrainStepHostBatch,
+    NnueTrainStepRunner,
+    RAdamUpdateParams,
+    RangerUpdateParams,
+    ScalarLossKind,
+    nnue_forward_host,
+    ranger_update_device,
+    ranger_update_host,
+    scalar_loss_host,
+)
+
+__version__ = "0.1.0"

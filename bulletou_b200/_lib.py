@@ -1,0 +1,187 @@
+"""ctypes binding of the C ABI (include/bulletou_cuda_cpp.h, include/bulletou_b200.h).
+
+The same binding drives this package's sm_100a library (libbulletou_b200.so,
+the product) and, for parity tests and the reference timing arm only, the
+reference backend built from its own sources (exported with a ``refx_``
+prefix).  There is no fallback: if the library is missing the import fails
+loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+P = ctypes.c_void_p
+Z = ctypes.c_size_t
+I = ctypes.c_int
+F = ctypes.c_float
+U64 = ctypes.c_uint64
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+LIBRARY_PATH = PACKAGE_DIR / "libbulletou_b200.so"
+
+
+class CudaCppError(RuntimeError):
+    """Non-zero status from the C ABI; the message is the library's last error
+    (mirrors CudaCppError in crates/cuda_cpp/src/lib.rs:19-37)."""
+
+    def __init__(self, message: str, code: int = -1):
+        super().__init__(message)
+        self.code = code
+
+
+class RangerStep(ctypes.Structure):
+    """BulletOuB200RangerStep."""
+
+    _fields_ = [
+        ("norm_loss_rate", F), ("norm_loss_before", I), ("gradient_factor", F), ("learning_rate", F),
+        ("step_size", F), ("use_denom", I), ("decay", F), ("beta1", F), ("beta2", F), ("epsilon", F),
+        ("min_weight", F), ("max_weight", F), ("do_lookahead", I), ("lookahead_alpha", F),
+        ("clip_after_lookahead", I),
+    ]
+
+
+class LossSpec(ctypes.Structure):
+    """BulletOuB200LossSpec."""
+
+    _fields_ = [("kind", I), ("output_inv_scale", F), ("loss_pow_exp", F), ("loss_param", F),
+                ("finalize_loss", I), ("normalizer", Z)]
+
+
+_BUF = P  # handle pointers are opaque
+SIGNATURES: dict[str, list] = {
+    # runtime
+    "bulletou_cuda_cpp_last_error": [P, Z],
+    "bulletou_cuda_cpp_device_name": [I, P, Z],
+    "bulletou_cuda_cpp_context_create": [I, P],
+    "bulletou_cuda_cpp_context_destroy": [P],
+    "bulletou_cuda_cpp_context_synchronize": [P],
+    "bulletou_cuda_cpp_event_create": [P, P],
+    "bulletou_cuda_cpp_event_destroy": [P],
+    "bulletou_cuda_cpp_event_record": [P, P],
+    "bulletou_cuda_cpp_event_wait": [P, P],
+    "bulletou_cuda_cpp_event_synchronize": [P],
+    "bulletou_cuda_cpp_event_elapsed_ms": [P, P, P],
+    "bulletou_cuda_cpp_graph_begin_capture": [P],
+    "bulletou_cuda_cpp_graph_end_capture": [P, P],
+    "bulletou_cuda_cpp_graph_destroy": [P],
+    "bulletou_cuda_cpp_graph_launch": [P, P],
+    "bulletou_cuda_cpp_f32_buffer_create": [P, Z, P],
+    "bulletou_cuda_cpp_f32_buffer_destroy": [P],
+    "bulletou_cuda_cpp_i32_buffer_create": [P, Z, P],
+    "bulletou_cuda_cpp_i32_buffer_destroy": [P],
+    "bulletou_cuda_cpp_pinned_f32_buffer_create": [P, Z, P],
+    "bulletou_cuda_cpp_pinned_f32_buffer_destroy": [P],
+    "bulletou_cuda_cpp_pinned_i32_buffer_create": [P, Z, P],
+    "bulletou_cuda_cpp_pinned_i32_buffer_destroy": [P],
+    "bulletou_cuda_cpp_f32_upload_staged": [P, P, P, P, Z],
+    "bulletou_cuda_cpp_i32_upload_staged": [P, P, P, P, Z],
+    "bulletou_cuda_cpp_i32_upload": [P, P, P, Z],
+    "bulletou_cuda_cpp_i32_download": [P, P, P, Z],
+    "bulletou_cuda_cpp_i32_copy_device": [P, P, P, Z],
+    "bulletou_cuda_cpp_f32_upload": [P, P, P, Z],
+    "bulletou_cuda_cpp_f32_download": [P, P, P, Z],
+    "bulletou_cuda_cpp_f32_copy_device": [P, P, P, Z],
+    "bulletou_cuda_cpp_f32_fill": [P, P, F, Z],
+    "bulletou_cuda_cpp_axpy_device": [P, Z, F, P, P, P],
+    "bulletou_cuda_cpp_axpy_host": [I, Z, F, P, P, P],
+    # optimizers
+    "bulletou_cuda_cpp_ranger_update_device": [P, F, I, Z, F, F, F, I, F, F, F, F, F, F, I, F, I, P, P, P, P, P, P],
+    "bulletou_cuda_cpp_ranger_update_host": [I, Z, F, F, F, I, F, F, F, F, F, F, I, F, I, P, P, P, P, P],
+    "bulletou_cuda_cpp_sgd_momentum_update_device": [P, Z, F, F, F, F, F, F, P, P, P, P, P],
+    # HalfKP
+    "bulletou_cuda_cpp_nnue_forward_device": [P, Z, Z, Z, Z, Z, Z] + [P] * 16,
+    "bulletou_cuda_cpp_nnue_forward_host": [I, Z, Z, Z, Z, Z, Z] + [P] * 11,
+    "bulletou_cuda_cpp_nnue_backward_device": [P, Z, Z, Z, Z, Z, Z] + [P] * 24 + [I],
+    "bulletou_cuda_cpp_nnue_train_warmup_device": [P, Z, Z, Z, Z, Z, Z] + [P] * 16,
+    # loss
+    "bulletou_cuda_cpp_scalar_loss_device_with_finalize": [P, I, F, F, F, Z] + [P] * 7 + [I],
+    "bulletou_cuda_cpp_scalar_loss_device": [P, I, F, F, F, Z] + [P] * 7,
+    "bulletou_cuda_cpp_scalar_loss_host": [I, I, F, F, F, Z] + [P] * 7,
+    # KPPT
+    "bulletou_cuda_cpp_kppt_forward_device": [P, Z, Z, Z] + [P] * 9,
+    "bulletou_cuda_cpp_kppt_backward_device": [P, Z, Z, Z] + [P] * 10,
+    # additive B200 entries
+    "bulletou_b200_version": [P, Z],
+    "bulletou_b200_context_create_on_stream": [I, P, P],
+    "bulletou_b200_context_stream": [P, P],
+    "bulletou_b200_f32_buffer_ptr": [P, P],
+    "bulletou_b200_i32_buffer_ptr": [P, P],
+    "bulletou_b200_i32_upload_pinned": [P, P, P, Z],
+    "bulletou_b200_f32_upload_pinned": [P, P, P, Z],
+    "bulletou_b200_f32_download_pinned": [P, P, P, Z],
+    "bulletou_b200_pinned_f32_ptr": [P, P],
+    "bulletou_b200_pinned_i32_ptr": [P, P],
+    "bulletou_b200_f32_buffer_view": [P, Z, Z, P],
+    "bulletou_b200_profile_begin": [P, Z],
+    "bulletou_b200_profile_end": [P, P, Z, P, P],
+    "bulletou_b200_nnue_train_step_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P],
+    "bulletou_b200_nnue_dense_gradient_len": [Z, Z, Z, P],
+    "bulletou_b200_nnue_local_gradients_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P],
+    "bulletou_b200_kppt_train_step_device": [P, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P],
+}
+
+
+class Library:
+    """One loaded backend library.  ``kind`` is "b200" or "reference"."""
+
+    def __init__(self, path: str | os.PathLike, kind: str = "b200"):
+        self.path = str(path)
+        self.kind = kind
+        self.prefix = "refx_" if kind == "reference" else ""
+        self._cdll = ctypes.CDLL(self.path, mode=os.RTLD_LOCAL)
+        self._fns: dict[str, object] = {}
+
+    def has(self, name: str) -> bool:
+        try:
+            getattr(self._cdll, self.prefix + name)
+            return True
+        except AttributeError:
+            return False
+
+    def fn(self, name: str):
+        f = self._fns.get(name)
+        if f is None:
+            f = getattr(self._cdll, self.prefix + name)
+            f.argtypes = SIGNATURES[name]
+            f.restype = I
+            self._fns[name] = f
+        return f
+
+    def last_error(self) -> str:
+        buf = ctypes.create_string_buffer(1024)
+        self.fn("bulletou_cuda_cpp_last_error")(buf, len(buf))
+        return buf.value.decode(errors="replace")
+
+    def call(self, name: str, *args) -> None:
+        rc = self.fn(name)(*args)
+        if rc != 0:
+            raise CudaCppError(f"{name}: {self.last_error()}", rc)
+
+
+_default: Library | None = None
+
+
+def library() -> Library:
+    """The product library (loaded once).  Raises if it has not been built."""
+    global _default
+    if _default is None:
+        if not LIBRARY_PATH.exists():
+            raise ImportError(
+                f"{LIBRARY_PATH} is missing: build it with `make -C bulletou_b200/csrc` "
+                "(or __graft_entry__.build()); there is no CPU fallback")
+        _default = Library(LIBRARY_PATH, "b200")
+    return _default
+
+
+def reference_library(path: str | os.PathLike | None = None) -> Library:
+    """The reference backend built by oracle/build_ref.sh (test/bench only)."""
+    p = Path(path) if path else PACKAGE_DIR.parent / "oracle" / "_ref" / "libref_cudacpp.so"
+    if not p.exists():
+        raise FileNotFoundError(f"reference backend not built: {p} (run oracle/build_ref.sh)")
+    return Library(p, "reference")
+
+
+def exported_names() -> list[str]:
+    return list(SIGNATURES)

@@ -1,0 +1,92 @@
+// Inverse index of a sparse batch ("which (sample, perspective) pairs touched
+// feature-transformer row r") and the warp-per-row kernels that consume it.
+//
+// The reference scatters every (sample, slot, column) gradient with a float
+// atomicAdd into a dense gradient table (HalfKP, cu:5301-5354), or builds a
+// similar count/scan/scatter index for SFNN (cu:4442-4580) and then gathers.
+// Here the index feeds one kernel per row that sums the row's pre-activation
+// gradients in ascending (sample, perspective) order -- deterministic up to
+// kSortCap occurrences per row -- and either applies the optimizer in the
+// same pass (the gradient is never written) or writes/accumulates the
+// gradient row.
+#pragma once
+
+#include <climits>
+
+#include "common.cuh"
+#include "optim.cuh"
+
+namespace bou {
+
+constexpr int kRowWarps = 8;         // warps per CTA in the row kernels
+constexpr int kSortCap = 512;        // per-warp SMEM sort capacity (entries)
+
+// Row ids touched by one sparse feature id.  HalfKP factorization (input_size
+// == 125388 + 1548): feature f < 125388 maps to rows 1548+f and f % 1548,
+// cu:1004-1019; every other valid id maps to itself.
+struct RowMap {
+    int input_size;
+    int factorized;  // 1 when input_size == 126936
+    __device__ __forceinline__ int rows(int f, int* r0, int* r1) const {
+        if (f < 0 || f >= input_size) return 0;
+        if (factorized && f < 125388) {
+            *r0 = 1548 + f;
+            *r1 = f % 1548;
+            return 2;
+        }
+        *r0 = f;
+        return 1;
+    }
+};
+
+inline RowMap make_row_map(size_t input_size) {
+    RowMap m;
+    m.input_size = static_cast<int>(input_size);
+    m.factorized = input_size == 125388 + 1548 ? 1 : 0;
+    return m;
+}
+
+struct InverseIndex {
+    int* offsets = nullptr;   // [n_rows + 1]
+    int* entries = nullptr;   // [n_entries] entry id = 2*sample + perspective
+    int* counts = nullptr;    // [n_rows + 1] scratch
+    int n_rows = 0;
+    size_t capacity = 0;
+};
+
+// Builds the index for `batch` samples x `max_active` slots x 2 perspectives
+// into context scratch.  Enqueued on ctx->stream.
+int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
+                        size_t max_active, size_t input_size, size_t n_rows, InverseIndex* out);
+
+// Parameters of the per-row consumer kernels.
+struct RowGradientSource {
+    const float* base[2];  // perspective 0 / 1 pre-activation gradients
+    size_t sample_stride;  // floats between consecutive samples in base[p]
+};
+
+enum RowMode : int {
+    kRowRanger = 0,       // sum + Ranger update (gradient never materialised)
+    kRowWrite = 1,        // gradient row overwritten with the sum
+    kRowAccumulate = 2,   // gradient row += sum
+};
+
+struct RowKernelArgs {
+    const int* offsets;
+    const int* entries;
+    int n_rows;
+    int row_begin;  // first row handled (for row-sharded updates)
+    int width;      // floats per row
+    RowGradientSource src;
+    float* weights;
+    float* momentum;
+    float* velocity;
+    float* slow;
+    float* gradients;  // kRowWrite / kRowAccumulate target, row-major [n_rows][width] relative to row_begin
+    RangerArgs ranger;
+    int skip_quiet;
+};
+
+int launch_row_kernel(BulletOuCudaCppContext* ctx, int mode, const RowKernelArgs& args, int rows_to_process);
+
+}  // namespace bou

@@ -1,0 +1,169 @@
+/*
+ * bulletou_b200.h — additive C ABI of libbulletou_b200.so.
+ *
+ * These entries have no one-to-one counterpart in the reference backend; they
+ * are what a train-step runner calls instead of the reference's sequence of
+ * forward / loss / backward / per-group optimizer calls.  Each one names the
+ * reference sequence it replaces.  Existing bulletou_cuda_cpp_* signatures are
+ * unchanged (see bulletou_cuda_cpp.h); handles and error convention are shared.
+ */
+#ifndef BULLETOU_B200_H
+#define BULLETOU_B200_H
+
+#include <stddef.h>
+
+#include "bulletou_cuda_cpp.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* One Ranger (RAdam + Lookahead) step, exactly the scalars that
+ * crates/cuda_cpp/src/lib.rs:9518-9544 passes to
+ * bulletou_cuda_cpp_ranger_update_device for every parameter group. */
+typedef struct BulletOuB200RangerStep {
+    float norm_loss_rate;
+    int norm_loss_before;
+    float gradient_factor;
+    float learning_rate;
+    float step_size;
+    int use_denom;
+    float decay;
+    float beta1;
+    float beta2;
+    float epsilon;
+    float min_weight;
+    float max_weight;
+    int do_lookahead;
+    float lookahead_alpha;
+    int clip_after_lookahead;
+} BulletOuB200RangerStep;
+
+/* Scalar loss selection, as bulletou_cuda_cpp_scalar_loss_device_with_finalize
+ * (cu:11809).  `normalizer` replaces the batch size as the divisor of the
+ * output gradient (0 = batch); a data-parallel rank passes the global batch so
+ * that summing rank gradients gives the global-batch mean gradient. */
+typedef struct BulletOuB200LossSpec {
+    int kind;
+    float output_inv_scale;
+    float loss_pow_exp;
+    float loss_param;
+    int finalize_loss;
+    size_t normalizer;
+} BulletOuB200LossSpec;
+
+/* HalfKP parameter groups, in the update order of NnueTrainStepRunner
+ * (lib.rs:5964-6024): l0w, l0b, l1w, l1b, l2w, l2b, outw, outb. */
+#define BULLETOU_B200_NNUE_GROUPS 8
+
+/* Library / device queries. */
+int bulletou_b200_version(char* out, size_t out_len);
+/* Creates a context that enqueues on an existing CUDA stream (not owned), so
+ * the library's work orders with a host framework's stream (e.g. the stream a
+ * collective library uses). */
+int bulletou_b200_context_create_on_stream(int device, void* stream, BulletOuCudaCppContext** out);
+int bulletou_b200_context_stream(const BulletOuCudaCppContext* ctx, void** out);
+/* Raw device pointer of a buffer (for zero-copy interop with collectives). */
+int bulletou_b200_f32_buffer_ptr(const BulletOuCudaCppF32Buffer* buffer, void** out);
+int bulletou_b200_i32_buffer_ptr(const BulletOuCudaCppI32Buffer* buffer, void** out);
+/* Asynchronous H2D copy straight from a pinned buffer (no staging memcpy),
+ * and D2H into one; enqueued on the context stream, non-blocking. */
+int bulletou_b200_i32_upload_pinned(BulletOuCudaCppContext* ctx, BulletOuCudaCppI32Buffer* dst,
+    const BulletOuCudaCppPinnedI32Buffer* src, size_t len);
+int bulletou_b200_f32_upload_pinned(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* dst,
+    const BulletOuCudaCppPinnedF32Buffer* src, size_t len);
+int bulletou_b200_f32_download_pinned(BulletOuCudaCppContext* ctx, BulletOuCudaCppPinnedF32Buffer* dst,
+    const BulletOuCudaCppF32Buffer* src, size_t len);
+/* Host pointer of a pinned buffer. */
+int bulletou_b200_pinned_f32_ptr(const BulletOuCudaCppPinnedF32Buffer* buffer, void** out);
+int bulletou_b200_pinned_i32_ptr(const BulletOuCudaCppPinnedI32Buffer* buffer, void** out);
+/* Non-owning view [offset, offset+len) of a buffer; destroy with
+ * bulletou_cuda_cpp_f32_buffer_destroy (frees only the handle). */
+int bulletou_b200_f32_buffer_view(const BulletOuCudaCppF32Buffer* buffer, size_t offset, size_t len,
+    BulletOuCudaCppF32Buffer** out);
+
+/* Stage profiler (the counterpart of the reference's profiled steps,
+ * lib.rs:5858-5928): while enabled, the fused train steps record a CUDA event
+ * on the context stream at each phase boundary (no host synchronization).
+ * profile_begin reserves room for `max_marks` events; profile_end waits for
+ * the stream and returns in ms_out[i] the summed time between consecutive
+ * marks i and i+1 of every step (phase i), in *steps_out the steps recorded
+ * and in *phases_out the phases per step.  HalfKP phases: 0 inverse index,
+ * 1 fused forward/loss/backward, 2 dense weight gradients, 3 small-parameter
+ * Ranger + loss finalize, 4 feature-transformer row gradient + Ranger. */
+int bulletou_b200_profile_begin(BulletOuCudaCppContext* ctx, size_t max_marks);
+int bulletou_b200_profile_end(BulletOuCudaCppContext* ctx, float* ms_out, size_t ms_len, size_t* steps_out,
+    size_t* phases_out);
+
+/* One complete HalfKP train step on device-resident batch buffers.
+ *
+ * Replaces NnueTrainStepRunner::step_no_readback_with_loss_finalize
+ * (lib.rs:5748-5799): nnue_forward_device (cu:10864) ->
+ * scalar_loss_device_with_finalize (cu:11809) ->
+ * nnue_backward_device(zero_l0_gradients = 0) (cu:12069) -> 8 x
+ * ranger_update_device (cu:10576).  The feature-transformer gradient is never
+ * materialised: a per-row inverse index of the batch feeds a row kernel that
+ * sums the rows' gradients and applies Ranger in the same pass.
+ *
+ * params/momentum/velocity/slow_params: 8 handles each (group order above).
+ * output [batch] receives the network output; per_sample, mean_output_gradients
+ * [batch], weighted_sum and mean [1] follow the scalar-loss contract. */
+int bulletou_b200_nnue_train_step_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2, size_t l3,
+    size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* targets, const BulletOuCudaCppF32Buffer* entry_weights,
+    const BulletOuB200LossSpec* loss, const BulletOuB200RangerStep* ranger,
+    BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* const* momentum,
+    BulletOuCudaCppF32Buffer* const* velocity, BulletOuCudaCppF32Buffer* const* slow_params,
+    BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean);
+
+/* Length of the packed small-parameter gradient used by the data-parallel
+ * phases: l0b | l1w | l1b | l2w | l2b | outw | outb. */
+int bulletou_b200_nnue_dense_gradient_len(size_t l1, size_t l2, size_t l3, size_t* out);
+
+/* Data-parallel phase 1: forward + loss + backward of a rank's local batch.
+ * Overwrites ft_gradients [input_size*l1] with this batch's feature-transformer
+ * gradient and dense_gradients [dense_gradient_len] with the packed
+ * small-parameter gradient.  Between this and the optimizer the caller
+ * reduce-scatters ft_gradients by row shard and all-reduces dense_gradients;
+ * the update itself is bulletou_cuda_cpp_ranger_update_device on views. */
+int bulletou_b200_nnue_local_gradients_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2, size_t l3,
+    size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* targets, const BulletOuCudaCppF32Buffer* entry_weights,
+    const BulletOuB200LossSpec* loss, BulletOuCudaCppF32Buffer* const* params,
+    BulletOuCudaCppF32Buffer* ft_gradients, BulletOuCudaCppF32Buffer* dense_gradients,
+    BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean);
+
+/* One complete KPPT scalar-table train step (one component table).
+ * Replaces KpptTableTrainStepRunner::step_no_readback_with_loss_finalize
+ * (lib.rs:4962-5036): kppt_forward_device (cu:11887) -> scalar loss ->
+ * kppt_backward_device (cu:11934) -> ranger_update_device over table_w,
+ * table_b, outw, outb (lib.rs:5037-5066).  The table gradient lives in a
+ * context-owned table that is only ever zero between steps: the fused
+ * forward/loss kernel scatters into it and the table's Ranger pass resets it
+ * in the same sweep, so the reference's whole-table zero fill disappears.
+ * params/momentum/velocity/slow_params: 4 handles each
+ * (table_w [input_size], table_b [1], outw [2], outb [1]). */
+int bulletou_b200_kppt_train_step_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* targets, const BulletOuCudaCppF32Buffer* entry_weights,
+    const BulletOuB200LossSpec* loss, const BulletOuB200RangerStep* ranger,
+    BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* const* momentum,
+    BulletOuCudaCppF32Buffer* const* velocity, BulletOuCudaCppF32Buffer* const* slow_params,
+    BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BULLETOU_B200_H */

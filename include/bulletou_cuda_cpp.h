@@ -1,0 +1,214 @@
+/*
+ * bulletou_cuda_cpp.h — drop-in C ABI of the BulletOu cuda-cpp backend,
+ * implemented from scratch for NVIDIA B200 (sm_100a) by libbulletou_b200.so.
+ *
+ * Every entry below has the same name, argument order, argument meaning,
+ * ownership rule and error convention as the reference backend's C ABI in
+ * yaneurao/BulletOu crates/cuda_cpp/cpp/bulletou_cuda_backend.cu (cited as
+ * "cu:LINE"), whose Rust declarations live in crates/cuda_cpp/src/lib.rs
+ * `mod ffi` (lib.rs:9605-10640).  A Rust build that links this library
+ * instead of the reference's static `bulletou_cuda_cpp_backend` needs no
+ * change to lib.rs.
+ *
+ * Conventions (cu:209-272, cu:5397-5570):
+ *   - every call returns 0 on success; on failure it returns -1, or the
+ *     cudaError_t code, and stores a message in a thread-local string read by
+ *     bulletou_cuda_cpp_last_error();
+ *   - handles are opaque and owned by the caller, who destroys them
+ *     explicitly; destroy(NULL) is a no-op returning 0;
+ *   - buffer arguments are validated (non-null, same device as the context,
+ *     length >= the length the call needs) before anything is enqueued;
+ *   - all work is enqueued asynchronously on the context's stream; only
+ *     *_synchronize, *_download and *_host entries block.
+ */
+#ifndef BULLETOU_CUDA_CPP_H
+#define BULLETOU_CUDA_CPP_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct BulletOuCudaCppContext BulletOuCudaCppContext;             /* cu:99 */
+typedef struct BulletOuCudaCppF32Buffer BulletOuCudaCppF32Buffer;         /* cu:173 */
+typedef struct BulletOuCudaCppI32Buffer BulletOuCudaCppI32Buffer;         /* cu:189 */
+typedef struct BulletOuCudaCppPinnedF32Buffer BulletOuCudaCppPinnedF32Buffer; /* cu:195 */
+typedef struct BulletOuCudaCppPinnedI32Buffer BulletOuCudaCppPinnedI32Buffer; /* cu:201 */
+typedef struct BulletOuCudaCppEvent BulletOuCudaCppEvent;                 /* cu:207 */
+typedef struct BulletOuCudaCppGraphExec BulletOuCudaCppGraphExec;         /* cu:212 */
+typedef struct BulletOuCudaCppHalfMoments BulletOuCudaCppHalfMoments;     /* cu:179 (fp16 optimizer moments; not supported: calls that receive one fail) */
+
+/* ---- errors, device, context (cu:9471-9677) ---- */
+int bulletou_cuda_cpp_last_error(char* out, size_t out_len);                           /* cu:9471 */
+int bulletou_cuda_cpp_device_name(int device, char* out, size_t out_len);              /* cu:9481 */
+int bulletou_cuda_cpp_context_create(int device, BulletOuCudaCppContext** out);        /* cu:9503 */
+int bulletou_cuda_cpp_context_destroy(BulletOuCudaCppContext* ctx);                    /* cu:9545 */
+int bulletou_cuda_cpp_context_synchronize(BulletOuCudaCppContext* ctx);                /* cu:9667 */
+
+/* ---- events and CUDA graphs (cu:9678-9857) ---- */
+int bulletou_cuda_cpp_event_create(BulletOuCudaCppContext* ctx, BulletOuCudaCppEvent** out);   /* cu:9678 */
+int bulletou_cuda_cpp_event_destroy(BulletOuCudaCppEvent* event);                               /* cu:9699 */
+int bulletou_cuda_cpp_event_record(BulletOuCudaCppContext* ctx, BulletOuCudaCppEvent* event);   /* cu:9719 */
+int bulletou_cuda_cpp_event_wait(BulletOuCudaCppContext* ctx, BulletOuCudaCppEvent* event);     /* cu:9730 */
+int bulletou_cuda_cpp_event_synchronize(BulletOuCudaCppEvent* event);                           /* cu:9741 */
+int bulletou_cuda_cpp_event_elapsed_ms(BulletOuCudaCppEvent* start, BulletOuCudaCppEvent* stop, float* out_ms); /* cu:9756 */
+int bulletou_cuda_cpp_graph_begin_capture(BulletOuCudaCppContext* ctx);                         /* cu:9777 */
+int bulletou_cuda_cpp_graph_end_capture(BulletOuCudaCppContext* ctx, BulletOuCudaCppGraphExec** out); /* cu:9788 */
+int bulletou_cuda_cpp_graph_destroy(BulletOuCudaCppGraphExec* graph);                           /* cu:9820 */
+int bulletou_cuda_cpp_graph_launch(BulletOuCudaCppContext* ctx, BulletOuCudaCppGraphExec* graph); /* cu:9847 */
+
+/* ---- device and pinned buffers (cu:9858-10033) ---- */
+int bulletou_cuda_cpp_f32_buffer_create(BulletOuCudaCppContext* ctx, size_t len, BulletOuCudaCppF32Buffer** out); /* cu:9858 */
+int bulletou_cuda_cpp_f32_buffer_destroy(BulletOuCudaCppF32Buffer* buffer);                    /* cu:9882 */
+int bulletou_cuda_cpp_i32_buffer_create(BulletOuCudaCppContext* ctx, size_t len, BulletOuCudaCppI32Buffer** out); /* cu:9902 */
+int bulletou_cuda_cpp_i32_buffer_destroy(BulletOuCudaCppI32Buffer* buffer);                    /* cu:9926 */
+int bulletou_cuda_cpp_pinned_f32_buffer_create(BulletOuCudaCppContext* ctx, size_t len, BulletOuCudaCppPinnedF32Buffer** out); /* cu:9946 */
+int bulletou_cuda_cpp_pinned_f32_buffer_destroy(BulletOuCudaCppPinnedF32Buffer* buffer);       /* cu:9970 */
+int bulletou_cuda_cpp_pinned_i32_buffer_create(BulletOuCudaCppContext* ctx, size_t len, BulletOuCudaCppPinnedI32Buffer** out); /* cu:9990 */
+int bulletou_cuda_cpp_pinned_i32_buffer_destroy(BulletOuCudaCppPinnedI32Buffer* buffer);       /* cu:10014 */
+
+/* ---- transfers and fills (cu:10034-10306) ---- */
+int bulletou_cuda_cpp_f32_upload_staged(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* dst,
+    BulletOuCudaCppPinnedF32Buffer* staging, const float* src, size_t len);                    /* cu:10034 */
+int bulletou_cuda_cpp_i32_upload_staged(BulletOuCudaCppContext* ctx, BulletOuCudaCppI32Buffer* dst,
+    BulletOuCudaCppPinnedI32Buffer* staging, const int* src, size_t len);                      /* cu:10059 */
+int bulletou_cuda_cpp_i32_upload(BulletOuCudaCppContext* ctx, BulletOuCudaCppI32Buffer* dst, const int* src, size_t len); /* cu:10084 */
+int bulletou_cuda_cpp_i32_download(BulletOuCudaCppContext* ctx, const BulletOuCudaCppI32Buffer* src, int* dst, size_t len); /* cu:10105 */
+int bulletou_cuda_cpp_i32_copy_device(BulletOuCudaCppContext* ctx, BulletOuCudaCppI32Buffer* dst,
+    const BulletOuCudaCppI32Buffer* src, size_t len);                                           /* cu:10131 */
+int bulletou_cuda_cpp_f32_upload(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* dst, const float* src, size_t len); /* cu:10153 */
+int bulletou_cuda_cpp_f32_download(BulletOuCudaCppContext* ctx, const BulletOuCudaCppF32Buffer* src, float* dst, size_t len); /* cu:10174 */
+int bulletou_cuda_cpp_f32_copy_device(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* dst,
+    const BulletOuCudaCppF32Buffer* src, size_t len);                                           /* cu:10200 */
+int bulletou_cuda_cpp_f32_fill(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* dst, float value, size_t len); /* cu:10222 */
+int bulletou_cuda_cpp_axpy_device(BulletOuCudaCppContext* ctx, size_t len, float a,
+    const BulletOuCudaCppF32Buffer* x, const BulletOuCudaCppF32Buffer* y, BulletOuCudaCppF32Buffer* out); /* cu:10281 */
+int bulletou_cuda_cpp_axpy_host(int device, size_t len, float a, const float* x, const float* y, float* out); /* cu:13536 */
+
+/* ---- optimizers (cu:10554-10699, 14087) ----
+ * RAdam + Lookahead ("Ranger") over one parameter group; gradients are reset
+ * to zero in the same pass.  step_size/use_denom come from the host-side
+ * RAdam step scale (lib.rs:9268-9288).  half_moments must be NULL here. */
+int bulletou_cuda_cpp_ranger_update_device(
+    BulletOuCudaCppContext* ctx, float norm_loss_rate, int norm_loss_before, size_t len,
+    float gradient_factor, float learning_rate, float step_size, int use_denom, float decay,
+    float beta1, float beta2, float epsilon, float min_weight, float max_weight,
+    int do_lookahead, float lookahead_alpha, int clip_after_lookahead,
+    BulletOuCudaCppF32Buffer* gradients, BulletOuCudaCppF32Buffer* weights,
+    BulletOuCudaCppF32Buffer* momentum, BulletOuCudaCppF32Buffer* velocity,
+    BulletOuCudaCppF32Buffer* slow_params, BulletOuCudaCppHalfMoments* half_moments);     /* cu:10576 */
+int bulletou_cuda_cpp_ranger_update_host(
+    int device, size_t len,
+    float gradient_factor, float learning_rate, float step_size, int use_denom, float decay,
+    float beta1, float beta2, float epsilon, float min_weight, float max_weight,
+    int do_lookahead, float lookahead_alpha, int clip_after_lookahead,
+    float* gradients, float* weights, float* momentum, float* velocity, float* slow_params); /* cu:14087 */
+/* SGD with momentum and a compensated (two-float) master weight; `remainder`
+ * is the low part of the weight. */
+int bulletou_cuda_cpp_sgd_momentum_update_device(
+    BulletOuCudaCppContext* ctx, size_t len, float gradient_factor, float learning_rate,
+    float decay, float beta, float min_weight, float max_weight,
+    BulletOuCudaCppF32Buffer* gradients, BulletOuCudaCppF32Buffer* weights,
+    BulletOuCudaCppF32Buffer* momentum, BulletOuCudaCppF32Buffer* remainder,
+    BulletOuCudaCppHalfMoments* half_moments);                                                 /* cu:10554 */
+
+/* ---- HalfKP / KP NNUE  (input -> l1 (x2 perspectives) -> l2 -> l3 -> 1) ----
+ * Shapes: l0w[input_size][l1] feature-major; l1w[2*l1][l2], l2w[l2][l3] and
+ * outw[l3] input-major (cu:1083-1100).  Sparse inputs are [batch][max_active]
+ * int32 feature ids; ids < 0 or >= input_size are padding.  When
+ * input_size == 125388 + 1548 the table is factorized: rows [0,1548) are
+ * virtual piece rows and feature f < 125388 reads rows 1548+f and f%1548
+ * (cu:1004-1019). */
+int bulletou_cuda_cpp_nnue_forward_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2, size_t l3,
+    size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* l0w, const BulletOuCudaCppF32Buffer* l0b,
+    const BulletOuCudaCppF32Buffer* l1w, const BulletOuCudaCppF32Buffer* l1b,
+    const BulletOuCudaCppF32Buffer* l2w, const BulletOuCudaCppF32Buffer* l2b,
+    const BulletOuCudaCppF32Buffer* outw, const BulletOuCudaCppF32Buffer* outb,
+    BulletOuCudaCppF32Buffer* stm_l0, BulletOuCudaCppF32Buffer* nstm_l0,
+    BulletOuCudaCppF32Buffer* combined, BulletOuCudaCppF32Buffer* hidden1,
+    BulletOuCudaCppF32Buffer* hidden2, BulletOuCudaCppF32Buffer* output);                  /* cu:10864 */
+int bulletou_cuda_cpp_nnue_forward_host(
+    int device, size_t input_size, size_t l1, size_t l2, size_t l3, size_t batch, size_t max_active,
+    const int* stm_indices, const int* nstm_indices,
+    const float* l0w, const float* l0b, const float* l1w, const float* l1b,
+    const float* l2w, const float* l2b, const float* outw, const float* outb, float* output); /* cu:11670 */
+/* Backward of the forward above.  l0w_gradients ACCUMULATES (it is zeroed
+ * first only when zero_l0_gradients != 0); every other gradient is
+ * overwritten (cu:9142-9290). */
+int bulletou_cuda_cpp_nnue_backward_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2, size_t l3,
+    size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* combined, const BulletOuCudaCppF32Buffer* hidden1,
+    const BulletOuCudaCppF32Buffer* hidden2, const BulletOuCudaCppF32Buffer* stm_l0,
+    const BulletOuCudaCppF32Buffer* nstm_l0, const BulletOuCudaCppF32Buffer* l1w,
+    const BulletOuCudaCppF32Buffer* l2w, const BulletOuCudaCppF32Buffer* outw,
+    const BulletOuCudaCppF32Buffer* mean_output_gradients,
+    BulletOuCudaCppF32Buffer* hidden2_gradients, BulletOuCudaCppF32Buffer* hidden1_gradients,
+    BulletOuCudaCppF32Buffer* combined_gradients, BulletOuCudaCppF32Buffer* stm_l0_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_gradients, BulletOuCudaCppF32Buffer* l0w_gradients,
+    BulletOuCudaCppF32Buffer* l0b_gradients, BulletOuCudaCppF32Buffer* l1w_gradients,
+    BulletOuCudaCppF32Buffer* l1b_gradients, BulletOuCudaCppF32Buffer* l2w_gradients,
+    BulletOuCudaCppF32Buffer* l2b_gradients, BulletOuCudaCppF32Buffer* outw_gradients,
+    BulletOuCudaCppF32Buffer* outb_gradients, int zero_l0_gradients);                       /* cu:12069 */
+int bulletou_cuda_cpp_nnue_train_warmup_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2, size_t l3,
+    size_t batch, size_t max_active,
+    const BulletOuCudaCppF32Buffer* combined, const BulletOuCudaCppF32Buffer* hidden1,
+    const BulletOuCudaCppF32Buffer* hidden2, const BulletOuCudaCppF32Buffer* l1w,
+    const BulletOuCudaCppF32Buffer* l2w, const BulletOuCudaCppF32Buffer* outw,
+    const BulletOuCudaCppF32Buffer* mean_output_gradients,
+    BulletOuCudaCppF32Buffer* hidden2_gradients, BulletOuCudaCppF32Buffer* hidden1_gradients,
+    BulletOuCudaCppF32Buffer* combined_gradients, BulletOuCudaCppF32Buffer* l1w_gradients,
+    BulletOuCudaCppF32Buffer* l1b_gradients, BulletOuCudaCppF32Buffer* l2w_gradients,
+    BulletOuCudaCppF32Buffer* l2b_gradients, BulletOuCudaCppF32Buffer* outw_gradients,
+    BulletOuCudaCppF32Buffer* outb_gradients);                                                 /* cu:12169 */
+
+/* ---- scalar value loss (cu:2719-2860, 8891-8968, 11809-11885, 11984) ----
+ * kind 0 = sigmoid(out*inv_scale) vs target, |err|^pow_exp; kind 1 = win-rate
+ * model (loss_param = in_offset/scaling, output_inv_scale = output scale);
+ * kind 2 = BCE with logits (loss_param = error-weight k, 0 = plain). */
+int bulletou_cuda_cpp_scalar_loss_device_with_finalize(
+    BulletOuCudaCppContext* ctx, int kind, float output_inv_scale, float loss_pow_exp, float loss_param,
+    size_t batch, const BulletOuCudaCppF32Buffer* outputs, const BulletOuCudaCppF32Buffer* targets,
+    const BulletOuCudaCppF32Buffer* entry_weights, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean, int finalize_loss);                                        /* cu:11809 */
+int bulletou_cuda_cpp_scalar_loss_device(
+    BulletOuCudaCppContext* ctx, int kind, float output_inv_scale, float loss_pow_exp, float unused_loss_param,
+    size_t batch, const BulletOuCudaCppF32Buffer* outputs, const BulletOuCudaCppF32Buffer* targets,
+    const BulletOuCudaCppF32Buffer* entry_weights, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean);                                                           /* cu:11856 */
+int bulletou_cuda_cpp_scalar_loss_host(
+    int device, int kind, float output_inv_scale, float loss_pow_exp, float unused_loss_param, size_t batch,
+    const float* outputs, const float* targets, const float* entry_weights,
+    float* per_sample, float* mean_output_gradients, float* weighted_sum, float* mean);       /* cu:11984 */
+
+/* ---- KPPT scalar tables (cu:8970-9140, 11887-11983) ----
+ * out = outw[0]*(b + sum table_w[stm ids]) + outw[1]*(b + sum table_w[nstm ids]) + outb.
+ * The backward zero-fills every gradient it writes, then accumulates. */
+int bulletou_cuda_cpp_kppt_forward_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* table_w, const BulletOuCudaCppF32Buffer* table_b,
+    const BulletOuCudaCppF32Buffer* outw, const BulletOuCudaCppF32Buffer* outb,
+    BulletOuCudaCppF32Buffer* stm_eval, BulletOuCudaCppF32Buffer* nstm_eval,
+    BulletOuCudaCppF32Buffer* outputs);                                                        /* cu:11887 */
+int bulletou_cuda_cpp_kppt_backward_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* stm_eval, const BulletOuCudaCppF32Buffer* nstm_eval,
+    const BulletOuCudaCppF32Buffer* outw, const BulletOuCudaCppF32Buffer* mean_output_gradients,
+    BulletOuCudaCppF32Buffer* table_w_gradients, BulletOuCudaCppF32Buffer* table_b_gradients,
+    BulletOuCudaCppF32Buffer* outw_gradients, BulletOuCudaCppF32Buffer* outb_gradients);      /* cu:11934 */
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BULLETOU_CUDA_CPP_H */

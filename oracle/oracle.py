@@ -1,0 +1,178 @@
+"""TEST INFRASTRUCTURE ONLY -- numpy/ctypes driver of the C oracle
+(oracle/bulletou_oracle.c).  Only tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg import this module, as the checker; the product
+(bulletou_b200) never does.
+
+Orchestrates the reference runner's order for one train step
+(crates/cuda_cpp/src/lib.rs:5748-5799): forward -> scalar loss -> backward ->
+Ranger on each parameter group in the order l0w, l0b, l1w, l1b, l2w, l2b,
+outw, outb (lib.rs:5964-6024), with the RAdam step scale of lib.rs:9268-9288
+and Lookahead every `lookahead_period` steps (lib.rs:9345-9348).
+"""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "liboracle.so"
+FLT_MAX = float(np.finfo(np.float32).max)
+
+_lib = None
+
+
+def build() -> Path:
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < (HERE / "bulletou_oracle.c").stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        _lib = ctypes.CDLL(str(LIB_PATH))
+        i64, f, i, p = ctypes.c_int64, ctypes.c_float, ctypes.c_int, ctypes.c_void_p
+        _lib.oracle_nnue_forward.argtypes = [i64] * 6 + [p] * 16
+        _lib.oracle_scalar_loss.argtypes = [i, f, f, f, i64, f] + [p] * 7
+        _lib.oracle_nnue_backward.argtypes = [i64] * 6 + [p] * 24
+        _lib.oracle_radam_step_scale.argtypes = [ctypes.c_uint64, f, f, f, p, p]
+        _lib.oracle_ranger_update.argtypes = [i64, f, f, f, i, f, f, f, f, f, f, i, f, i] + [p] * 5
+        _lib.oracle_kppt_forward.argtypes = [i64] * 3 + [p] * 9
+        _lib.oracle_kppt_backward.argtypes = [i64] * 3 + [p] * 11
+        for fn in (_lib.oracle_nnue_forward, _lib.oracle_scalar_loss, _lib.oracle_nnue_backward,
+                   _lib.oracle_radam_step_scale, _lib.oracle_ranger_update, _lib.oracle_kppt_forward,
+                   _lib.oracle_kppt_backward):
+            fn.restype = None
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags.c_contiguous
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def _f(a):
+    return np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+
+
+def _i(a):
+    return np.ascontiguousarray(a, dtype=np.int32).reshape(-1)
+
+
+NAMES = ("l0w", "l0b", "l1w", "l1b", "l2w", "l2b", "outw", "outb")
+
+
+def nnue_forward(shape, stm, nstm, batch, max_active, weights: dict) -> dict:
+    input_size, l1, l2, l3 = shape
+    w = [_f(weights[n]) for n in NAMES]
+    out = {k: np.zeros(n, np.float32) for k, n in (("stm_l0", batch * l1), ("nstm_l0", batch * l1),
+                                                    ("combined", batch * 2 * l1), ("hidden1", batch * l2),
+                                                    ("hidden2", batch * l3), ("output", batch))}
+    s, n = _i(stm), _i(nstm)
+    lib().oracle_nnue_forward(input_size, l1, l2, l3, batch, max_active, _p(s), _p(n), *[_p(a) for a in w],
+                              *[_p(out[k]) for k in ("stm_l0", "nstm_l0", "combined", "hidden1", "hidden2", "output")])
+    return out
+
+
+def scalar_loss(kind: int, inv_scale: float, pow_exp: float, param: float, outputs, targets, entry_weights,
+                normalizer: float | None = None) -> dict:
+    o, t, w = _f(outputs), _f(targets), _f(entry_weights)
+    n = o.size
+    ps, mg = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    ws, mean = np.zeros(1, np.float32), np.zeros(1, np.float32)
+    lib().oracle_scalar_loss(kind, inv_scale, pow_exp, param, n, float(n if normalizer is None else normalizer),
+                             _p(o), _p(t), _p(w), _p(ps), _p(mg), _p(ws), _p(mean))
+    return {"per_sample": ps, "mean_output_gradients": mg, "weighted_sum": float(ws[0]), "mean": float(mean[0])}
+
+
+def nnue_backward(shape, stm, nstm, batch, max_active, fwd: dict, weights: dict, mog, l0w_grad=None) -> dict:
+    input_size, l1, l2, l3 = shape
+    g = {k: np.zeros(n, np.float32) for k, n in (
+        ("hidden2_gradients", batch * l3), ("hidden1_gradients", batch * l2), ("combined_gradients", batch * 2 * l1),
+        ("stm_l0_gradients", batch * l1), ("nstm_l0_gradients", batch * l1), ("l0w_gradients", input_size * l1),
+        ("l0b_gradients", l1), ("l1w_gradients", 2 * l1 * l2), ("l1b_gradients", l2), ("l2w_gradients", l2 * l3),
+        ("l2b_gradients", l3), ("outw_gradients", l3), ("outb_gradients", 1))}
+    if l0w_grad is not None:
+        g["l0w_gradients"][:] = _f(l0w_grad)
+    scratch = np.zeros(max(2 * l1 * l2, l2 * l3) + l1 + l2 + l3 + 64, np.float64)
+    s, n = _i(stm), _i(nstm)
+    mog = _f(mog)
+    w1, w2, wo = _f(weights["l1w"]), _f(weights["l2w"]), _f(weights["outw"])
+    fw = {k: _f(fwd[k]) for k in ("combined", "hidden1", "hidden2", "stm_l0", "nstm_l0")}
+    lib().oracle_nnue_backward(input_size, l1, l2, l3, batch, max_active, _p(s), _p(n), _p(fw["combined"]),
+                               _p(fw["hidden1"]), _p(fw["hidden2"]), _p(fw["stm_l0"]), _p(fw["nstm_l0"]),
+                               _p(w1), _p(w2), _p(wo), _p(mog),
+                               *[_p(g[k]) for k in ("hidden2_gradients", "hidden1_gradients", "combined_gradients",
+                                                    "stm_l0_gradients", "nstm_l0_gradients", "l0w_gradients",
+                                                    "l0b_gradients", "l1w_gradients", "l1b_gradients",
+                                                    "l2w_gradients", "l2b_gradients", "outw_gradients",
+                                                    "outb_gradients")], _p(scratch))
+    return g
+
+
+def radam_step_scale(step: int, beta1=0.9, beta2=0.999, n_sma_threshold=5.0):
+    ss = ctypes.c_float()
+    ud = ctypes.c_int()
+    lib().oracle_radam_step_scale(step, beta1, beta2, n_sma_threshold, ctypes.byref(ss), ctypes.byref(ud))
+    return ss.value, bool(ud.value)
+
+
+def ranger_update(grads, weights, momentum, velocity, slow, *, step: int, learning_rate=0.001, beta1=0.9,
+                  beta2=0.999, epsilon=1e-8, decay=0.0, gradient_factor=1.0, min_weight=-FLT_MAX,
+                  max_weight=FLT_MAX, lookahead_alpha=0.5, lookahead_period=6, clip_after_lookahead=True,
+                  n_sma_threshold=5.0) -> None:
+    """In place on float32 arrays."""
+    ss, ud = radam_step_scale(step, beta1, beta2, n_sma_threshold)
+    do_la = int(step % lookahead_period == 0)
+    lib().oracle_ranger_update(weights.size, gradient_factor, learning_rate, ss, int(ud), decay, beta1, beta2, epsilon,
+                               min_weight, max_weight, do_la, lookahead_alpha, int(clip_after_lookahead),
+                               _p(grads), _p(weights), _p(momentum), _p(velocity), _p(slow))
+
+
+class NnueTrainer:
+    """CPU reference runner for HalfKP: weights, Ranger state, one step at a time."""
+
+    def __init__(self, shape, weights: dict):
+        self.shape = tuple(shape)
+        self.w = {n: _f(weights[n]).copy() for n in NAMES}
+        self.m = {n: np.zeros_like(self.w[n]) for n in NAMES}
+        self.v = {n: np.zeros_like(self.w[n]) for n in NAMES}
+        self.slow = {n: self.w[n].copy() for n in NAMES}
+        self.l0w_grad = np.zeros_like(self.w["l0w"])
+
+    def step(self, stm, nstm, batch, max_active, targets, entry_weights, *, loss_kind=0, inv_scale=1.0, pow_exp=2.0,
+             loss_param=0.0, **ranger) -> dict:
+        fwd = nnue_forward(self.shape, stm, nstm, batch, max_active, self.w)
+        loss = scalar_loss(loss_kind, inv_scale, pow_exp, loss_param, fwd["output"], targets, entry_weights)
+        g = nnue_backward(self.shape, stm, nstm, batch, max_active, fwd, self.w, loss["mean_output_gradients"],
+                          self.l0w_grad)
+        for n in NAMES:
+            grad = g[f"{n}_gradients"]
+            ranger_update(grad, self.w[n], self.m[n], self.v[n], self.slow[n], **ranger)
+        self.l0w_grad[:] = 0.0
+        return {"forward": fwd, "loss": loss, "gradients": g}
+
+
+def kppt_forward(input_size, stm, nstm, batch, max_active, table_w, table_b, outw, outb) -> dict:
+    out = {k: np.zeros(batch, np.float32) for k in ("stm_eval", "nstm_eval", "output")}
+    s, n = _i(stm), _i(nstm)
+    tw, tb, ow, ob = _f(table_w), _f(np.atleast_1d(table_b)), _f(outw), _f(np.atleast_1d(outb))
+    lib().oracle_kppt_forward(input_size, batch, max_active, _p(s), _p(n), _p(tw), _p(tb), _p(ow), _p(ob),
+                              _p(out["stm_eval"]), _p(out["nstm_eval"]), _p(out["output"]))
+    return out
+
+
+def kppt_backward(input_size, stm, nstm, batch, max_active, fwd: dict, outw, mog) -> dict:
+    acc = np.zeros(input_size, np.float64)
+    g = {"table_w": np.zeros(input_size, np.float32), "table_b": np.zeros(1, np.float32),
+         "outw": np.zeros(2, np.float32), "outb": np.zeros(1, np.float32)}
+    s, n = _i(stm), _i(nstm)
+    ow, mg = _f(outw), _f(mog)
+    lib().oracle_kppt_backward(input_size, batch, max_active, _p(s), _p(n), _p(fwd["stm_eval"]), _p(fwd["nstm_eval"]),
+                               _p(ow), _p(mg), _p(acc), _p(g["table_w"]), _p(g["table_b"]), _p(g["outw"]),
+                               _p(g["outb"]))
+    return g
