@@ -216,9 +216,12 @@ def test_ranger_device_vs_oracle_random(ctx, n, step):
     st = RangerDeviceState(*[bo.F32Buffer.from_host(ctx, a) for a in arrs])
     bo.ranger_update_device(ctx, params, st)
     oracle.ranger_update(*arrs, step=step, learning_rate=1e-3, decay=1e-4, min_weight=-0.1, max_weight=0.1)
+    # EMA updates cancel (m = b1*m + (1-b1)*g); GPU FMA contraction vs the
+    # oracle's separate roundings differ by ~1 ulp of the *terms*, so the bound
+    # is relative to the tensor's scale.
     for name, buf, ref in zip(("grad", "w", "m", "v", "slow"), (st.gradients, st.weights, st.momentum, st.velocity,
                                                                 st.slow_params), arrs):
-        assert_close(buf.download(), ref, 2e-6, 1e-10, name)
+        assert_close_scaled(buf.download(), ref, 2e-6, name)
 
 
 def test_zero_radam_skip_bitwise_vs_reference(ctx, ref_ctx, goldens):
