@@ -45,7 +45,9 @@ ACTIVE = 38
 SHAPE = (125388, 256, 32, 32)
 N_BATCHES = 8
 METRIC = "train positions/sec (HalfKP 256x2-32-32-1, batch 16384)"
-PHASES = ("inverse_index", "fused_fwd_loss_bwd", "dense_weight_grads", "small_param_ranger", "ft_row_grad_ranger")
+PHASES = ("inverse_index", "king_sort", "ft_gather", "dense_fwd_loss_bwd", "batch_reduce", "small_param_ranger",
+          "ft_row_grad_ranger")
+LAUNCHES_PER_STEP = 13  # index 5 + king sort 3 + gather, dense, reduce, finalize, rows
 
 
 def parse_args():
@@ -230,7 +232,7 @@ def run_b200(args, rank, world, local, dist):
     # ---- device-resident timed region (+ stage profile) ----
     lib = ctx.lib
     start, stop = bo.Event(ctx), bo.Event(ctx)
-    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 6 * args.steps + 8)
+    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 8 * args.steps + 8)
     with ClockSampler(local) as clocks:
         start.record(ctx)
         for i in range(args.steps):
@@ -288,7 +290,7 @@ def run_b200(args, rank, world, local, dist):
         "total_ms": total_ms, "phase_ms": phase_ms, "clocks": clk,
         "e2e": {"value": e2e_steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps},
-        "gpu_launches": 7 * args.steps,
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "final_loss": losses[-1],
     }
 
@@ -358,12 +360,14 @@ def roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0):
         # the inverse index (entries + offsets)
         "ft_row_grad_ranger": rows * width * 4 * (6 + 2 * lookahead_frac) + 2 * batch * width * 4
                               + 4 * (entries + rows + 1),
-        # gathered FT rows (2*A rows of 1 KB per position; L2-served) + indices
-        # + activations / pre-activation gradients written
-        "fused_fwd_loss_bwd": 2 * batch * ACTIVE * width * 4 + 2 * batch * ACTIVE * 4 + 2 * batch * 2 * width * 4
-                              + batch * (32 * 3 + 4 * 4),
-        "dense_weight_grads": batch * 2 * width * 4 + batch * 32 * 3 * 4,
+        # logical bytes of the gathered FT rows (2*A rows of 1 KB per position,
+        # L2-served after the king sort) + indices + activations written
+        "ft_gather": 2 * batch * ACTIVE * width * 4 + 2 * batch * ACTIVE * 4 + 2 * batch * width * 4,
+        # activations read, pre-activation gradients written, small per-position vectors
+        "dense_fwd_loss_bwd": 2 * (2 * batch * width * 4) + batch * 4 * (32 * 4 + 4 * 4),
+        "batch_reduce": 2 * (2 * batch * width * 4) + batch * 4 * (32 * 4 + 2),
         "inverse_index": 4 * (entries * 3 + rows * 4),
+        "king_sort": 4 * (2 * batch * 4),
         "small_param_ranger": 0.0,
     }
     dom = max(phase_ms, key=phase_ms.get)

@@ -96,6 +96,7 @@ enum ScratchSlot : int {
     kScratchKppt = 10,
     kScratchHost = 11,
     kScratchActivations = 12,
+    kScratchKingSort = 13,
 };
 
 int ok();

@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "loss.cuh"
 #include "optim.cuh"
+#include "halfkp_fast.cuh"
 #include "sparse_rows.cuh"
 
 namespace bou {
@@ -41,8 +42,6 @@ int loss_args(const BulletOuB200LossSpec* loss, size_t batch, LossArgs* out);
 using namespace bou;
 
 namespace {
-
-constexpr unsigned kFull = 0xffffffffu;
 
 __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
 __device__ __forceinline__ float crelu_grad(float activation, float g) {
@@ -214,466 +213,15 @@ int generic_dense_backward(BulletOuCudaCppContext* ctx, const NnueDims& d, const
     return check_launch("nnue dense backward launch");
 }
 
-// ---------------------------------------------------------------------------
-// Production-shape fused kernels: l1 = L1 (256 or 512), l2 = l3 = 32.
-// ---------------------------------------------------------------------------
+bool is_fast_shape(const NnueDims& d) { return halfkp_fast_shape(d.l1, d.l2, d.l3, d.batch, d.max_active); }
 
-constexpr int kFusedWarps = 8;
-constexpr int kW1Pad = 33;  // padded row stride of l1w in shared memory (bank-conflict free both ways)
-
-struct FusedArgs {
-    const int* stm;
-    const int* nstm;
-    int max_active;
-    int batch;
-    RowMap map;
-    const float* l0w;
-    const float* l0b;
-    const float* l1w;
-    const float* l1b;
-    const float* l2w;
-    const float* l2b;
-    const float* outw;
-    const float* outb;
-    // forward outputs (any may be null in training mode except combined/hidden1)
-    float* stm_l0;
-    float* nstm_l0;
-    float* combined;  // [B][2*L1] = [stm | nstm] after ClippedReLU
-    float* hidden1;   // [B][32]
-    float* hidden2;   // [B][32]
-    float* output;    // [B]
-    // training
-    const float* targets;
-    const float* entry_weights;
-    LossArgs loss;
-    float* per_sample;
-    float* mog;
-    float* g1;       // [B][32] masked hidden1 gradient
-    float* g2;       // [B][32] masked hidden2 gradient
-    float* pregrad;  // [B][2*L1] masked feature-transformer gradient
-    float* vec_partials;  // [grid][vec_len]
-};
-
-template <int L1>
-struct FusedLayout {
-    static constexpr int kIn = 2 * L1;                     // L1 layer inputs
-    static constexpr int kW1 = kIn * kW1Pad;               // floats
-    static constexpr int kW2 = 32 * kW1Pad;
-    static constexpr int kAct = kFusedWarps * kIn;
-    static constexpr int kG1 = kFusedWarps * 32;
-    static constexpr int kVec = L1 + 32 + 32 + 32 + 1 + 1;  // l0b | l1b | l2b | outw | outb | loss
-    static constexpr size_t kSmemBytes = static_cast<size_t>(kW1 + kW2 + 32 + kAct + kG1) * sizeof(float);
-};
-
-template <int Q>
-__device__ __forceinline__ void add_row(float (&acc)[Q][8], const float* __restrict__ l0w, int row, int lane) {
-    const float* p = l0w + static_cast<size_t>(row) * (Q * 256) + lane * 8;
-#pragma unroll
-    for (int q = 0; q < Q; ++q) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(p + q * 256));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(p + q * 256 + 4));
-        acc[q][0] += a.x; acc[q][1] += a.y; acc[q][2] += a.z; acc[q][3] += a.w;
-        acc[q][4] += b.x; acc[q][5] += b.y; acc[q][6] += b.z; acc[q][7] += b.w;
-    }
+HalfkpWeights halfkp_weights(const float* const* w) {
+    return HalfkpWeights{w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]};
 }
 
-template <int Q>
-__device__ __forceinline__ void add_row_pair(float (&acc)[Q][8], const float* __restrict__ l0w, int r0, int r1, int lane) {
-    const float* p0 = l0w + static_cast<size_t>(r0) * (Q * 256) + lane * 8;
-    const float* p1 = l0w + static_cast<size_t>(r1) * (Q * 256) + lane * 8;
-#pragma unroll
-    for (int q = 0; q < Q; ++q) {
-        const float4 a0 = __ldg(reinterpret_cast<const float4*>(p0 + q * 256));
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(p0 + q * 256 + 4));
-        const float4 a1 = __ldg(reinterpret_cast<const float4*>(p1 + q * 256));
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(p1 + q * 256 + 4));
-        acc[q][0] += a0.x + a1.x; acc[q][1] += a0.y + a1.y; acc[q][2] += a0.z + a1.z; acc[q][3] += a0.w + a1.w;
-        acc[q][4] += b0.x + b1.x; acc[q][5] += b0.y + b1.y; acc[q][6] += b0.z + b1.z; acc[q][7] += b0.w + b1.w;
-    }
-}
-
-// Gathers one perspective: acc = bias + sum over the position's valid slots,
-// in slot order (the reference's order, cu:1037-1050).
-template <int Q>
-__device__ __forceinline__ void gather_perspective(float (&acc)[Q][8], const int* __restrict__ idx, int max_active,
-                                                   const RowMap& map, const float* __restrict__ l0w,
-                                                   const float* __restrict__ l0b, int lane) {
-#pragma unroll
-    for (int q = 0; q < Q; ++q) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(l0b + q * 256 + lane * 8));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(l0b + q * 256 + lane * 8 + 4));
-        acc[q][0] = a.x; acc[q][1] = a.y; acc[q][2] = a.z; acc[q][3] = a.w;
-        acc[q][4] = b.x; acc[q][5] = b.y; acc[q][6] = b.z; acc[q][7] = b.w;
-    }
-    for (int c0 = 0; c0 < max_active; c0 += 32) {
-        const int mine = c0 + lane < max_active ? __ldg(idx + c0 + lane) : -1;
-        const int cnt = min(32, max_active - c0);
-        if (map.factorized) {
-            for (int s = 0; s < cnt; ++s) {
-                const int f = __shfl_sync(kFull, mine, s);
-                int r0, r1;
-                const int n = map.rows(f, &r0, &r1);
-                if (n == 1) add_row<Q>(acc, l0w, r0, lane);
-                else if (n == 2) add_row_pair<Q>(acc, l0w, r0, r1, lane);
-            }
-        } else {
-            int s = 0;
-            // Four rows in flight per lane; adds stay in slot order.
-            for (; s + 4 <= cnt; s += 4) {
-                int f[4];
-                bool ok[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    f[u] = __shfl_sync(kFull, mine, s + u);
-                    ok[u] = f[u] >= 0 && f[u] < map.input_size;
-                }
-                float4 x[4][Q][2];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float* p = l0w + static_cast<size_t>(ok[u] ? f[u] : 0) * (Q * 256) + lane * 8;
-#pragma unroll
-                    for (int q = 0; q < Q; ++q) {
-                        if (ok[u]) {
-                            x[u][q][0] = __ldg(reinterpret_cast<const float4*>(p + q * 256));
-                            x[u][q][1] = __ldg(reinterpret_cast<const float4*>(p + q * 256 + 4));
-                        }
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    if (!ok[u]) continue;
-#pragma unroll
-                    for (int q = 0; q < Q; ++q) {
-                        acc[q][0] += x[u][q][0].x; acc[q][1] += x[u][q][0].y;
-                        acc[q][2] += x[u][q][0].z; acc[q][3] += x[u][q][0].w;
-                        acc[q][4] += x[u][q][1].x; acc[q][5] += x[u][q][1].y;
-                        acc[q][6] += x[u][q][1].z; acc[q][7] += x[u][q][1].w;
-                    }
-                }
-            }
-            for (; s < cnt; ++s) {
-                const int f = __shfl_sync(kFull, mine, s);
-                if (f >= 0 && f < map.input_size) add_row<Q>(acc, l0w, f, lane);
-            }
-        }
-    }
-}
-
-template <int L1, bool kTrain>
-__global__ void __launch_bounds__(kFusedWarps * 32, 2) halfkp_fused_kernel(FusedArgs a) {
-    using Lay = FusedLayout<L1>;
-    constexpr int Q = L1 / 256;
-    constexpr int kIn = Lay::kIn;
-    extern __shared__ float4 smem4[];
-    float* smem = reinterpret_cast<float*>(smem4);
-    float* w1s = smem;                     // [kIn][33]
-    float* w2s = w1s + Lay::kW1;           // [32][33]
-    float* outw_s = w2s + Lay::kW2;        // [32]
-    float* act_all = outw_s + 32;          // [warps][kIn]
-    float* g1_all = act_all + Lay::kAct;   // [warps][32]
-
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < kIn * 32; i += blockDim.x) w1s[(i >> 5) * kW1Pad + (i & 31)] = a.l1w[i];
-    for (int i = threadIdx.x; i < 32 * 32; i += blockDim.x) w2s[(i >> 5) * kW1Pad + (i & 31)] = a.l2w[i];
-    if (threadIdx.x < 32) outw_s[threadIdx.x] = a.outw[threadIdx.x];
-    __syncthreads();
-
-    float* act = act_all + warp * kIn;
-    float* g1s = g1_all + warp * 32;
-    const float b1 = a.l1b[lane];
-    const float b2 = a.l2b[lane];
-    const float bout = a.outb[0];
-
-    // per-lane gradient accumulators (training only)
-    float acc_l0b[L1 / 32];
-#pragma unroll
-    for (int r = 0; r < L1 / 32; ++r) acc_l0b[r] = 0.0f;
-    float acc_b1 = 0.0f, acc_b2 = 0.0f, acc_out = 0.0f, acc_outb = 0.0f, acc_loss = 0.0f;
-
-    const int stride = gridDim.x * kFusedWarps;
-    for (int b = blockIdx.x * kFusedWarps + warp; b < a.batch; b += stride) {
-        // ---- feature transformer, both perspectives ----
-        float acc[Q][8];
-        const size_t ibase = static_cast<size_t>(b) * a.max_active;
-#pragma unroll
-        for (int persp = 0; persp < 2; ++persp) {
-            gather_perspective<Q>(acc, (persp == 0 ? a.stm : a.nstm) + ibase, a.max_active, a.map, a.l0w, a.l0b, lane);
-#pragma unroll
-            for (int q = 0; q < Q; ++q) {
-                float4 lo, hi;
-                lo.x = crelu01(acc[q][0]); lo.y = crelu01(acc[q][1]); lo.z = crelu01(acc[q][2]); lo.w = crelu01(acc[q][3]);
-                hi.x = crelu01(acc[q][4]); hi.y = crelu01(acc[q][5]); hi.z = crelu01(acc[q][6]); hi.w = crelu01(acc[q][7]);
-                const int col = q * 256 + lane * 8;
-                *reinterpret_cast<float4*>(act + persp * L1 + col) = lo;
-                *reinterpret_cast<float4*>(act + persp * L1 + col + 4) = hi;
-                float* combined_row = a.combined + static_cast<size_t>(b) * kIn + persp * L1 + col;
-                *reinterpret_cast<float4*>(combined_row) = lo;
-                *reinterpret_cast<float4*>(combined_row + 4) = hi;
-                if (!kTrain) {
-                    float* pr = (persp == 0 ? a.stm_l0 : a.nstm_l0) + static_cast<size_t>(b) * L1 + col;
-                    *reinterpret_cast<float4*>(pr) = lo;
-                    *reinterpret_cast<float4*>(pr + 4) = hi;
-                }
-            }
-        }
-        __syncwarp();
-        // ---- L1: lane j owns output j; sequential FMA over inputs ----
-        float h = b1;
-        const float4* act4 = reinterpret_cast<const float4*>(act);
-#pragma unroll 4
-        for (int i4 = 0; i4 < kIn / 4; ++i4) {
-            const float4 x = act4[i4];
-            const float* w = w1s + (i4 * 4) * kW1Pad + lane;
-            h = fmaf(x.x, w[0], h);
-            h = fmaf(x.y, w[kW1Pad], h);
-            h = fmaf(x.z, w[2 * kW1Pad], h);
-            h = fmaf(x.w, w[3 * kW1Pad], h);
-        }
-        const float h1 = crelu01(h);
-        // ---- L2 ----
-        float h2v = b2;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) h2v = fmaf(__shfl_sync(kFull, h1, j), w2s[j * kW1Pad + lane], h2v);
-        const float h2 = crelu01(h2v);
-        // ---- output ----
-        float out = bout;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) out = fmaf(__shfl_sync(kFull, h2, k), outw_s[k], out);
-        a.hidden1[static_cast<size_t>(b) * 32 + lane] = h1;
-        if (!kTrain) {
-            a.hidden2[static_cast<size_t>(b) * 32 + lane] = h2;
-            if (lane == 0) a.output[b] = out;
-            __syncwarp();
-            continue;
-        }
-        // ---- loss ----
-        float gout = 0.0f;
-        const float ps = sample_loss(a.loss, out, a.targets[b], a.entry_weights[b], &gout);
-        if (lane == 0) {
-            a.output[b] = out;
-            a.per_sample[b] = ps;
-            a.mog[b] = gout;
-            acc_loss += ps;
-            acc_outb += gout;
-        }
-        // ---- backward through the dense layers ----
-        const float g2 = crelu_grad(h2, gout * outw_s[lane]);
-        acc_out = fmaf(gout, h2, acc_out);
-        acc_b2 += g2;
-        float d1 = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 32; ++k) d1 = fmaf(__shfl_sync(kFull, g2, k), w2s[lane * kW1Pad + k], d1);
-        const float g1 = crelu_grad(h1, d1);
-        acc_b1 += g1;
-        a.g1[static_cast<size_t>(b) * 32 + lane] = g1;
-        a.g2[static_cast<size_t>(b) * 32 + lane] = g2;
-        g1s[lane] = g1;
-        __syncwarp();
-        // ---- feature-transformer pre-activation gradient ----
-        float* pg_row = a.pregrad + static_cast<size_t>(b) * kIn;
-        float pg_first[L1 / 32];
-#pragma unroll
-        for (int r = 0; r < kIn / 32; ++r) {
-            const int i = lane + 32 * r;
-            const float* w = w1s + i * kW1Pad;
-            float d = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) d = fmaf(g1s[j], w[j], d);
-            const float pg = crelu_grad(act[i], d);
-            pg_row[i] = pg;
-            if (r < L1 / 32) pg_first[r] = pg;
-            else acc_l0b[r - L1 / 32] += pg_first[r - L1 / 32] + pg;
-        }
-        __syncwarp();
-    }
-
-    if (!kTrain) return;
-    // ---- CTA reduction of the per-lane accumulators, fixed warp order ----
-    __syncthreads();
-    float* red = act_all;  // reuse: [warps][kVec]
-    constexpr int kVec = Lay::kVec;
-    float* mine = red + warp * kVec;
-#pragma unroll
-    for (int r = 0; r < L1 / 32; ++r) mine[lane + 32 * r] = acc_l0b[r];
-    mine[L1 + lane] = acc_b1;
-    mine[L1 + 32 + lane] = acc_b2;
-    mine[L1 + 64 + lane] = acc_out;
-    if (lane == 0) {
-        mine[L1 + 96] = acc_outb;
-        mine[L1 + 97] = acc_loss;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < kVec; e += blockDim.x) {
-        float s = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kFusedWarps; ++w) s += red[w * kVec + e];
-        a.vec_partials[static_cast<size_t>(blockIdx.x) * kVec + e] = s;
-    }
-}
-
-// dW1[i][j] = sum_b act[b][i] * g1[b][j] and dW2[j][k] = sum_b h1[b][j] * g2[b][k]
-// over one chunk of positions per CTA; per-CTA partials reduced later.
-constexpr int kTile = 16;
-
-template <int IN>
-__global__ void __launch_bounds__(256) halfkp_dense_grad_kernel(const float* __restrict__ act, const float* __restrict__ g1,
-                                                                const float* __restrict__ h1, const float* __restrict__ g2,
-                                                                int batch, int chunk, float* __restrict__ w1_partials,
-                                                                float* __restrict__ w2_partials) {
-    // blockIdx.y selects a 512-input slice of the L1 inputs
-    __shared__ __align__(16) float act_s[kTile][512];
-    __shared__ float g1_s[kTile][32];
-    __shared__ float h1_s[kTile][32];
-    __shared__ float g2_s[kTile][32];
-    const int t = threadIdx.x;
-    const int j = t & 31, ib = t >> 5;
-    const int slice = blockIdx.y * 512;
-    const bool do_w2 = blockIdx.y == 0;
-    float acc[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
-    float acc2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const int b0 = blockIdx.x * chunk;
-    const int b1 = min(batch, b0 + chunk);
-    for (int base = b0; base < b1; base += kTile) {
-        const int np = min(kTile, b1 - base);
-        for (int e = t; e < kTile * 128; e += 256) {
-            const int p = e >> 7, c4 = e & 127;
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (p < np) v = *reinterpret_cast<const float4*>(act + static_cast<size_t>(base + p) * IN + slice + c4 * 4);
-            *reinterpret_cast<float4*>(&act_s[p][c4 * 4]) = v;
-        }
-        for (int e = t; e < kTile * 32; e += 256) {
-            const int p = e >> 5, c = e & 31;
-            const size_t off = static_cast<size_t>(base + p) * 32 + c;
-            g1_s[p][c] = p < np ? g1[off] : 0.0f;
-            if (do_w2) {
-                h1_s[p][c] = p < np ? h1[off] : 0.0f;
-                g2_s[p][c] = p < np ? g2[off] : 0.0f;
-            }
-        }
-        __syncthreads();
-        for (int p = 0; p < np; ++p) {
-            const float g = g1_s[p][j];
-            const float4* row = reinterpret_cast<const float4*>(&act_s[p][ib * 64]);
-#pragma unroll
-            for (int i4 = 0; i4 < 16; ++i4) {
-                const float4 x = row[i4];
-                acc[i4 * 4 + 0] = fmaf(x.x, g, acc[i4 * 4 + 0]);
-                acc[i4 * 4 + 1] = fmaf(x.y, g, acc[i4 * 4 + 1]);
-                acc[i4 * 4 + 2] = fmaf(x.z, g, acc[i4 * 4 + 2]);
-                acc[i4 * 4 + 3] = fmaf(x.w, g, acc[i4 * 4 + 3]);
-            }
-            if (do_w2) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int e = t + 256 * q;
-                    acc2[q] = fmaf(h1_s[p][e >> 5], g2_s[p][e & 31], acc2[q]);
-                }
-            }
-        }
-        __syncthreads();
-    }
-    float* outp = w1_partials + static_cast<size_t>(blockIdx.x) * IN * 32;
-#pragma unroll
-    for (int ii = 0; ii < 64; ++ii) outp[static_cast<size_t>(slice + ib * 64 + ii) * 32 + j] = acc[ii];
-    if (do_w2) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) w2_partials[static_cast<size_t>(blockIdx.x) * 1024 + t + 256 * q] = acc2[q];
-    }
-}
-
-// Packed small-parameter layout: l0b | l1w | l1b | l2w | l2b | outw | outb.
-struct SmallGroups {
-    float* w[7];
-    float* m[7];
-    float* v[7];
-    float* s[7];
-    int begin[8];  // packed offsets; begin[7] = total
-};
-
-template <int L1>
-__global__ void halfkp_finalize_kernel(const float* __restrict__ vec_partials, int n_vec_parts,
-                                       const float* __restrict__ w1_partials, const float* __restrict__ w2_partials,
-                                       int n_dense_parts, SmallGroups groups, RangerArgs ranger, int write_mode,
-                                       float* __restrict__ dense_out, float* __restrict__ weighted_sum,
-                                       float* __restrict__ mean, float batch_f, int finalize) {
-    using Lay = FusedLayout<L1>;
-    constexpr int kVec = Lay::kVec;
-    const int total = groups.begin[7];
-    const int e = blockIdx.x * blockDim.x + threadIdx.x;
-    if (finalize && e == 0) {
-        float s = 0.0f;
-        for (int p = 0; p < n_vec_parts; ++p) s += vec_partials[static_cast<size_t>(p) * kVec + L1 + 97];
-        *weighted_sum = s;
-        *mean = s / batch_f;
-    }
-    if (e >= total) return;
-    int g = 0;
-    while (e >= groups.begin[g + 1]) ++g;
-    const int k = e - groups.begin[g];
-    float grad = 0.0f;
-    if (g == 1 || g == 3) {
-        const float* src = g == 1 ? w1_partials : w2_partials;
-        const size_t n = g == 1 ? static_cast<size_t>(2 * L1 * 32) : 1024;
-        for (int p = 0; p < n_dense_parts; ++p) grad += src[static_cast<size_t>(p) * n + k];
-    } else {
-        const int vec_off = g == 0 ? 0 : g == 2 ? L1 : g == 4 ? L1 + 32 : g == 5 ? L1 + 64 : L1 + 96;
-        for (int p = 0; p < n_vec_parts; ++p) grad += vec_partials[static_cast<size_t>(p) * kVec + vec_off + k];
-    }
-    if (write_mode) {
-        dense_out[e] = grad;
-        return;
-    }
-    float w = groups.w[g][k], m = groups.m[g][k], v = groups.v[g][k];
-    radam_coordinate(ranger.gradient_factor * grad, ranger, w, m, v);
-    if (ranger.do_lookahead) {
-        w = lookahead_coordinate(w, groups.s[g][k], ranger);
-        groups.s[g][k] = w;
-    }
-    groups.w[g][k] = w;
-    groups.m[g][k] = m;
-    groups.v[g][k] = v;
-}
-
-bool is_fast_shape(const NnueDims& d) {
-    return (d.l1 == 256 || d.l1 == 512) && d.l2 == 32 && d.l3 == 32 && d.batch <= static_cast<size_t>(INT_MAX / 1024) &&
-           d.max_active <= 4096;
-}
-
-template <int L1, bool kTrain>
-int launch_fused(BulletOuCudaCppContext* ctx, const FusedArgs& a, int* grid_out) {
-    using Lay = FusedLayout<L1>;
-    static bool configured[2] = {false, false};
-    auto kernel = halfkp_fused_kernel<L1, kTrain>;
-    const size_t smem = Lay::kSmemBytes;
-    cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (st != cudaSuccess) return fail("cudaFuncSetAttribute fused nnue", st);
-    (void)configured;
-    const int per_sm = 2;
-    int grid = ctx->sm_count * per_sm;
-    const int needed = (a.batch + kFusedWarps - 1) / kFusedWarps;
-    if (grid > needed) grid = needed;
-    if (grid < 1) grid = 1;
-    kernel<<<grid, kFusedWarps * 32, smem, ctx->stream>>>(a);
-    *grid_out = grid;
-    return check_launch("fused nnue kernel launch");
-}
-
-template <bool kTrain>
-int launch_fused_any(BulletOuCudaCppContext* ctx, size_t l1, const FusedArgs& a, int* grid) {
-    return l1 == 256 ? launch_fused<256, kTrain>(ctx, a, grid) : launch_fused<512, kTrain>(ctx, a, grid);
-}
-
-FusedArgs fused_args_base(const NnueDims& d, const int* stm, const int* nstm, const float* const* w) {
-    FusedArgs a{};
-    a.stm = stm;
-    a.nstm = nstm;
-    a.max_active = static_cast<int>(d.max_active);
-    a.batch = static_cast<int>(d.batch);
-    a.map = make_row_map(d.input_size);
-    a.l0w = w[0]; a.l0b = w[1]; a.l1w = w[2]; a.l1b = w[3]; a.l2w = w[4]; a.l2b = w[5]; a.outw = w[6]; a.outb = w[7];
-    return a;
+HalfkpDims halfkp_dims(const NnueDims& d) {
+    return HalfkpDims{static_cast<int>(d.input_size), static_cast<int>(d.l1), static_cast<int>(d.batch),
+                      static_cast<int>(d.max_active)};
 }
 
 size_t dense_len(size_t l1, size_t l2, size_t l3) { return l1 + 2 * l1 * l2 + l2 + l2 * l3 + l3 + l3 + 1; }
@@ -695,9 +243,6 @@ struct TrainScratch {
     float* g1;
     float* g2;
     float* pregrad;
-    float* vec_partials;
-    float* w1_partials;
-    float* w2_partials;
     // generic path extras
     float* stm_l0;
     float* nstm_l0;
@@ -709,10 +254,8 @@ struct TrainScratch {
     float* small_grads;  // packed dense gradient
 };
 
-int alloc_train_scratch(BulletOuCudaCppContext* ctx, const NnueDims& d, bool fast, int fused_grid, int dense_parts,
-                        TrainScratch* s) {
+int alloc_train_scratch(BulletOuCudaCppContext* ctx, const NnueDims& d, bool fast, TrainScratch* s) {
     const size_t B = d.batch, in = 2 * d.l1;
-    // one slab for the per-position activations and gradients
     size_t floats = 0;
     auto take = [&](size_t n) {
         size_t off = floats;
@@ -720,7 +263,7 @@ int alloc_train_scratch(BulletOuCudaCppContext* ctx, const NnueDims& d, bool fas
         return off;
     };
     const size_t o_comb = take(B * in), o_h1 = take(B * d.l2), o_h2 = take(B * d.l3), o_g1 = take(B * d.l2),
-                 o_g2 = take(B * d.l3), o_pg = take(B * in);
+                 o_g2 = take(B * d.l3), o_pg = take(B * in), o_small = take(dense_len(d.l1, d.l2, d.l3));
     size_t o_stm = 0, o_nstm = 0, o_h2g = 0, o_h1g = 0, o_cg = 0, o_sg = 0, o_ng = 0;
     if (!fast) {
         o_stm = take(B * d.l1); o_nstm = take(B * d.l1); o_h2g = take(B * d.l3); o_h1g = take(B * d.l2);
@@ -731,23 +274,10 @@ int alloc_train_scratch(BulletOuCudaCppContext* ctx, const NnueDims& d, bool fas
         return -1;
     float* f = static_cast<float*>(slab);
     s->combined = f + o_comb; s->hidden1 = f + o_h1; s->hidden2 = f + o_h2; s->g1 = f + o_g1; s->g2 = f + o_g2;
-    s->pregrad = f + o_pg;
+    s->pregrad = f + o_pg; s->small_grads = f + o_small;
     s->stm_l0 = fast ? nullptr : f + o_stm; s->nstm_l0 = fast ? nullptr : f + o_nstm;
     s->h2g = fast ? nullptr : f + o_h2g; s->h1g = fast ? nullptr : f + o_h1g; s->cg = fast ? nullptr : f + o_cg;
     s->stm_g = fast ? nullptr : f + o_sg; s->nstm_g = fast ? nullptr : f + o_ng;
-    // partial sums
-    size_t pfloats = 0;
-    size_t o_vec = 0, o_w1 = 0, o_w2 = 0, o_small = 0;
-    const size_t kvec = d.l1 + 98;
-    o_vec = pfloats; pfloats += (static_cast<size_t>(fused_grid) * kvec + 63) & ~static_cast<size_t>(63);
-    o_w1 = pfloats; pfloats += (static_cast<size_t>(dense_parts) * in * 32 + 63) & ~static_cast<size_t>(63);
-    o_w2 = pfloats; pfloats += (static_cast<size_t>(dense_parts) * 1024 + 63) & ~static_cast<size_t>(63);
-    o_small = pfloats; pfloats += (dense_len(d.l1, d.l2, d.l3) + 63) & ~static_cast<size_t>(63);
-    void* parts = nullptr;
-    if (scratch_slot(ctx, kScratchDensePartials, pfloats * sizeof(float), &parts, "cudaMalloc nnue step partials") != 0)
-        return -1;
-    float* p = static_cast<float*>(parts);
-    s->vec_partials = p + o_vec; s->w1_partials = p + o_w1; s->w2_partials = p + o_w2; s->small_grads = p + o_small;
     return 0;
 }
 
@@ -801,70 +331,38 @@ int nnue_step(BulletOuCudaCppContext* ctx, const NnueDims& d, const StepIO& io, 
     const bool norm_before = update && ranger_step->norm_loss_rate != 0.0f && ranger_step->norm_loss_before;
     const bool norm_after = update && ranger_step->norm_loss_rate != 0.0f && !ranger_step->norm_loss_before;
     const size_t group_lens[8] = {n_rows * d.l1, d.l1, in * d.l2, d.l2, d.l2 * d.l3, d.l3, d.l3, 1};
-    ctx->prof_marks_per_step = 6;
+    ctx->prof_marks_per_step = 8;
     prof_mark(ctx);
     // Inverse index of the batch (depends only on the sparse inputs).
     InverseIndex index;
     if (build_inverse_index(ctx, io.stm, io.nstm, d.batch, d.max_active, d.input_size, n_rows, &index) != 0) return -1;
+    prof_mark(ctx);
 
-    const int fused_grid_max = ctx->sm_count * 2;
-    const int chunk = 128;
-    const int dense_parts = static_cast<int>((d.batch + chunk - 1) / chunk);
     TrainScratch s{};
-    if (alloc_train_scratch(ctx, d, fast, fused_grid_max, dense_parts, &s) != 0) return -1;
+    if (alloc_train_scratch(ctx, d, fast, &s) != 0) return -1;
     float* const* w = io.w;
     const float* wc[8] = {w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]};
     const SmallGroups groups = small_groups(d, io);
     float* pregrad_stm = nullptr;
     float* pregrad_nstm = nullptr;
     size_t pregrad_stride = 0;
+    RangerArgs fa = ra;
+    if (norm_after) fa.do_lookahead = 0;
 
-    prof_mark(ctx);
     if (fast) {
-        FusedArgs a = fused_args_base(d, io.stm, io.nstm, wc);
-        a.combined = s.combined;
-        a.hidden1 = s.hidden1;
-        a.output = io.output;
-        a.targets = io.targets;
-        a.entry_weights = io.entry_weights;
-        a.loss = la;
-        a.per_sample = io.per_sample;
-        a.mog = io.mog;
-        a.g1 = s.g1;
-        a.g2 = s.g2;
-        a.pregrad = s.pregrad;
-        a.vec_partials = s.vec_partials;
-        int grid = 0;
-        if (launch_fused_any<true>(ctx, d.l1, a, &grid) != 0) return -1;
-        prof_mark(ctx);
-        const dim3 dgrid(static_cast<unsigned>(dense_parts), static_cast<unsigned>(in / 512));
-        if (d.l1 == 256)
-            halfkp_dense_grad_kernel<512><<<dgrid, 256, 0, ctx->stream>>>(s.combined, s.g1, s.hidden1, s.g2,
-                                                                         static_cast<int>(d.batch), chunk,
-                                                                         s.w1_partials, s.w2_partials);
-        else
-            halfkp_dense_grad_kernel<1024><<<dgrid, 256, 0, ctx->stream>>>(s.combined, s.g1, s.hidden1, s.g2,
-                                                                          static_cast<int>(d.batch), chunk,
-                                                                          s.w1_partials, s.w2_partials);
-        if (check_launch("nnue dense gradient launch") != 0) return -1;
+        const HalfkpDims hd = halfkp_dims(d);
+        const HalfkpActivations ha{s.combined, s.hidden1, s.hidden2, io.output, s.g1,
+                                   s.g2,       s.pregrad, io.per_sample, io.mog};
+        if (halfkp_fast_forward_backward(ctx, hd, make_row_map(d.input_size), io.stm, io.nstm, halfkp_weights(wc), ha,
+                                         io.targets, io.entry_weights, &la, nullptr, nullptr) != 0)
+            return -1;
         prof_mark(ctx);
         if (norm_before)
             for (int g = 0; g < 8; ++g)
                 if (apply_norm_loss(ctx, w[g], group_lens[g], ranger_step->norm_loss_rate) != 0) return -1;
-        RangerArgs fa = ra;
-        if (norm_after) fa.do_lookahead = 0;
-        const int total = groups.begin[7];
-        const int fblocks = (total + 255) / 256;
-        const float batch_f = static_cast<float>(d.batch);
-        if (d.l1 == 256)
-            halfkp_finalize_kernel<256><<<fblocks, 256, 0, ctx->stream>>>(
-                s.vec_partials, grid, s.w1_partials, s.w2_partials, dense_parts, groups, fa, update ? 0 : 1,
-                dense_grad, io.weighted_sum, io.mean, batch_f, finalize);
-        else
-            halfkp_finalize_kernel<512><<<fblocks, 256, 0, ctx->stream>>>(
-                s.vec_partials, grid, s.w1_partials, s.w2_partials, dense_parts, groups, fa, update ? 0 : 1,
-                dense_grad, io.weighted_sum, io.mean, batch_f, finalize);
-        if (check_launch("nnue finalize launch") != 0) return -1;
+        if (halfkp_fast_small_params(ctx, hd, ha, groups, update ? &fa : nullptr, dense_grad, io.weighted_sum,
+                                     io.mean, finalize) != 0)
+            return -1;
         prof_mark(ctx);
         pregrad_stm = s.pregrad;
         pregrad_nstm = s.pregrad + d.l1;
@@ -887,8 +385,6 @@ int nnue_step(BulletOuCudaCppContext* ctx, const NnueDims& d, const StepIO& io, 
             if (norm_before)
                 for (int k = 0; k < 8; ++k)
                     if (apply_norm_loss(ctx, w[k], group_lens[k], ranger_step->norm_loss_rate) != 0) return -1;
-            RangerArgs fa = ra;
-            if (norm_after) fa.do_lookahead = 0;
             for (int k = 0; k < 7; ++k)
                 if (launch_ranger(ctx, group_lens[k + 1], fa, sg + g.begin[k], w[k + 1], io.m[k + 1], io.v[k + 1],
                                   io.s[k + 1]) != 0)
@@ -901,9 +397,7 @@ int nnue_step(BulletOuCudaCppContext* ctx, const NnueDims& d, const StepIO& io, 
         pregrad_stm = s.stm_g;
         pregrad_nstm = s.nstm_g;
         pregrad_stride = d.l1;
-        prof_mark(ctx);
-        prof_mark(ctx);
-        prof_mark(ctx);
+        for (int k = 0; k < 5; ++k) prof_mark(ctx);
     }
 
     // Feature-transformer rows: sum each row's gradient from the index, then
@@ -969,15 +463,11 @@ int bulletou_cuda_cpp_nnue_forward_device(
     const float* w[8] = {l0w->ptr, l0b->ptr, l1w->ptr, l1b->ptr, l2w->ptr, l2b->ptr, outw->ptr, outb->ptr};
     int rc;
     if (is_fast_shape(d)) {
-        FusedArgs a = fused_args_base(d, stm_indices->ptr, nstm_indices->ptr, w);
-        a.stm_l0 = stm_l0->ptr;
-        a.nstm_l0 = nstm_l0->ptr;
-        a.combined = combined->ptr;
-        a.hidden1 = hidden1->ptr;
-        a.hidden2 = hidden2->ptr;
-        a.output = output->ptr;
-        int grid = 0;
-        rc = launch_fused_any<false>(ctx, l1, a, &grid);
+        const HalfkpActivations ha{combined->ptr, hidden1->ptr, hidden2->ptr, output->ptr, nullptr,
+                                   nullptr,       nullptr,      nullptr,      nullptr};
+        rc = halfkp_fast_forward_backward(ctx, halfkp_dims(d), make_row_map(input_size), stm_indices->ptr,
+                                          nstm_indices->ptr, halfkp_weights(w), ha, nullptr, nullptr, nullptr,
+                                          stm_l0->ptr, nstm_l0->ptr);
     } else {
         rc = generic_forward(ctx, d, stm_indices->ptr, nstm_indices->ptr, w, stm_l0->ptr, nstm_l0->ptr, combined->ptr,
                              hidden1->ptr, hidden2->ptr, output->ptr);

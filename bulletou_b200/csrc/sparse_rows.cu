@@ -18,53 +18,90 @@ __global__ void count_rows_kernel(const int* __restrict__ stm, const int* __rest
     if (n == 2) atomicAdd(&counts[r1], 1);
 }
 
-// Exclusive scan of counts[0, n) into offsets[0, n], one CTA of 1024 threads,
-// 4 consecutive counts per thread per tile.
-__global__ void __launch_bounds__(1024) scan_rows_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
-                                                         int n) {
-    __shared__ int warp_sums[32];
-    __shared__ int carry_s;
+// Exclusive scan of counts[0, n) into offsets[0, n] in three deterministic
+// passes: tile sums (4096 counts per CTA), a scan of the tile sums, and the
+// per-tile rescan that adds the tile's offset.
+constexpr int kScanThreads = 1024;
+constexpr int kScanTile = 4 * kScanThreads;
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) carry_s = 0;
-    __syncthreads();
-    for (int base = 0; base < n; base += 4096) {
-        const int i0 = base + threadIdx.x * 4;
-        int v[4];
+    int incl = v;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = (i0 + q < n) ? counts[i0 + q] : 0;
-        const int local = v[0] + v[1] + v[2] + v[3];
-        int incl = local;
+    for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += o;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = warp_sums[lane];
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
-            const int o = __shfl_up_sync(0xffffffffu, incl, d);
-            if (lane >= d) incl += o;
+            const int o = __shfl_up_sync(0xffffffffu, w, d);
+            if (lane >= d) w += o;
         }
-        if (lane == 31) warp_sums[warp] = incl;
-        __syncthreads();
-        if (warp == 0) {
-            int w = warp_sums[lane];
-#pragma unroll
-            for (int d = 1; d < 32; d <<= 1) {
-                const int o = __shfl_up_sync(0xffffffffu, w, d);
-                if (lane >= d) w += o;
-            }
-            warp_sums[lane] = w;  // inclusive prefix of warp totals
-        }
-        __syncthreads();
-        const int carry = carry_s;
-        int run = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - local;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            if (i0 + q < n) offsets[i0 + q] = run;
-            run += v[q];
-        }
-        __syncthreads();
-        if (threadIdx.x == 1023) carry_s = carry + warp_sums[31];
-        __syncthreads();
+        warp_sums[lane] = w;
     }
-    if (threadIdx.x == 0) offsets[n] = carry_s;
+    __syncthreads();
+    const int excl = (warp > 0 ? warp_sums[warp - 1] : 0) + incl - v;
+    *total = warp_sums[31];
+    return excl;
 }
 
+__global__ void __launch_bounds__(kScanThreads) scan_tile_sums_kernel(const int* __restrict__ counts, int n,
+                                                                      int* __restrict__ tile_sums) {
+    __shared__ int warp_sums[32];
+    const int i0 = blockIdx.x * kScanTile + threadIdx.x * 4;
+    int v = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v += (i0 + q < n) ? counts[i0 + q] : 0;
+    int total = 0;
+    block_exclusive_scan(v, warp_sums, &total);
+    if (threadIdx.x == 0) tile_sums[blockIdx.x] = total;
+}
+
+// One CTA: exclusive scan of the tile sums in place; tile_sums[tiles] = grand total.
+__global__ void __launch_bounds__(kScanThreads) scan_tile_offsets_kernel(int* __restrict__ tile_sums, int tiles) {
+    __shared__ int warp_sums[32];
+    __shared__ int carry_s;
+    if (threadIdx.x == 0) carry_s = 0;
+    __syncthreads();
+    for (int base = 0; base < tiles; base += kScanThreads) {
+        const int i = base + threadIdx.x;
+        const int v = i < tiles ? tile_sums[i] : 0;
+        int total = 0;
+        const int excl = block_exclusive_scan(v, warp_sums, &total);
+        const int carry = carry_s;
+        if (i < tiles) tile_sums[i] = carry + excl;
+        __syncthreads();
+        if (threadIdx.x == 0) carry_s = carry + total;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) tile_sums[tiles] = carry_s;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const int* __restrict__ counts, int n,
+                                                                  const int* __restrict__ tile_offsets, int tiles,
+                                                                  int* __restrict__ offsets) {
+    __shared__ int warp_sums[32];
+    const int i0 = blockIdx.x * kScanTile + threadIdx.x * 4;
+    int v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[q] = (i0 + q < n) ? counts[i0 + q] : 0;
+    int total = 0;
+    int run = tile_offsets[blockIdx.x] + block_exclusive_scan(v[0] + v[1] + v[2] + v[3], warp_sums, &total);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (i0 + q < n) offsets[i0 + q] = run;
+        run += v[q];
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) offsets[n] = tile_offsets[tiles];
+}
+
+// Scatters entry ids into their rows.  Slots are claimed by decrementing the
+// row's count, which leaves every count at zero for the next build (so the
+// count array needs no clearing between steps).
 __global__ void fill_rows_kernel(const int* __restrict__ stm, const int* __restrict__ nstm, size_t slots,
                                  size_t max_active, RowMap map, const int* __restrict__ offsets,
                                  int* __restrict__ cursor, int* __restrict__ entries) {
@@ -76,8 +113,8 @@ __global__ void fill_rows_kernel(const int* __restrict__ stm, const int* __restr
     const int entry = static_cast<int>((s / max_active) * 2 + persp);
     int r0, r1;
     const int n = map.rows(f, &r0, &r1);
-    if (n >= 1) entries[offsets[r0] + atomicAdd(&cursor[r0], 1)] = entry;
-    if (n == 2) entries[offsets[r1] + atomicAdd(&cursor[r1], 1)] = entry;
+    if (n >= 1) entries[offsets[r0] + atomicSub(&cursor[r0], 1) - 1] = entry;
+    if (n == 2) entries[offsets[r1] + atomicSub(&cursor[r1], 1) - 1] = entry;
 }
 
 __device__ __forceinline__ int warp_sort_ascending(int v, int lane) {
@@ -181,6 +218,19 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_kernel(RowKernelArgs a, in
     for (int col0 = 0; col0 < a.width; col0 += 32 * VEC) {
         const int c = col0 + lane * VEC;
         const bool active = c < a.width;
+        // Optimizer state (or the gradient row being accumulated) does not
+        // depend on the entry list: issue those loads first so their HBM
+        // latency overlaps the gather of the batch's gradient rows.
+        float w[VEC], m[VEC], v[VEC];
+        if (active) {
+            if constexpr (MODE == kRowRanger) {
+                load_vec<VEC>(a.weights + row_off + c, w);
+                load_vec<VEC>(a.momentum + row_off + c, m);
+                load_vec<VEC>(a.velocity + row_off + c, v);
+            } else if constexpr (MODE == kRowAccumulate) {
+                load_vec<VEC>(a.gradients + out_off + c, w);
+            }
+        }
         float acc[VEC];
 #pragma unroll
         for (int i = 0; i < VEC; ++i) acc[i] = 0.0f;
@@ -213,16 +263,10 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_kernel(RowKernelArgs a, in
         if constexpr (MODE == kRowWrite) {
             store_vec<VEC>(a.gradients + out_off + c, acc);
         } else if constexpr (MODE == kRowAccumulate) {
-            float g[VEC];
-            load_vec<VEC>(a.gradients + out_off + c, g);
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) g[i] += acc[i];
-            store_vec<VEC>(a.gradients + out_off + c, g);
+            for (int i = 0; i < VEC; ++i) w[i] += acc[i];
+            store_vec<VEC>(a.gradients + out_off + c, w);
         } else {
-            float w[VEC], m[VEC], v[VEC];
-            load_vec<VEC>(a.weights + row_off + c, w);
-            load_vec<VEC>(a.momentum + row_off + c, m);
-            load_vec<VEC>(a.velocity + row_off + c, v);
             if (n == 0 && a.skip_quiet && !a.ranger.do_lookahead) {
                 bool quiet = true;
 #pragma unroll
@@ -230,11 +274,11 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_kernel(RowKernelArgs a, in
                     quiet = quiet && (__float_as_uint(m[i]) | __float_as_uint(v[i])) == 0u && weight_is_quiet(w[i], a.ranger);
                 if (quiet) continue;
             }
+            float s[VEC];
+            if (a.ranger.do_lookahead) load_vec<VEC>(a.slow + row_off + c, s);
 #pragma unroll
             for (int i = 0; i < VEC; ++i) radam_coordinate(a.ranger.gradient_factor * acc[i], a.ranger, w[i], m[i], v[i]);
             if (a.ranger.do_lookahead) {
-                float s[VEC];
-                load_vec<VEC>(a.slow + row_off + c, s);
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) w[i] = lookahead_coordinate(w[i], s[i], a.ranger);
                 store_vec<VEC>(a.slow + row_off + c, w);
@@ -264,38 +308,46 @@ int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* 
     const RowMap map = make_row_map(input_size);
     const size_t slots = batch * max_active;
     const size_t max_entries = 2 * slots * (map.factorized ? 2 : 1);
-    if (n_rows >= static_cast<size_t>(INT_MAX) || max_entries >= static_cast<size_t>(INT_MAX) ||
+    if (n_rows >= static_cast<size_t>(INT_MAX) - kScanTile || max_entries >= static_cast<size_t>(INT_MAX) ||
         2 * batch >= static_cast<size_t>(INT_MAX))
         return fail_message("sparse index: batch or table too large for 32-bit row indexing");
-    void *counts = nullptr, *offsets = nullptr, *entries = nullptr, *cursor = nullptr;
+    const int tiles = static_cast<int>((n_rows + kScanTile - 1) / kScanTile);
+    void *counts = nullptr, *offsets = nullptr, *entries = nullptr, *tile_sums = nullptr;
+    const bool fresh = ctx->scratch[kScratchCsrCounts].bytes < (n_rows + 1) * sizeof(int);
     if (scratch_slot(ctx, kScratchCsrCounts, (n_rows + 1) * sizeof(int), &counts, "cudaMalloc sparse counts") != 0 ||
         scratch_slot(ctx, kScratchCsrOffsets, (n_rows + 1) * sizeof(int), &offsets, "cudaMalloc sparse offsets") != 0 ||
-        scratch_slot(ctx, kScratchCsrCursor, (n_rows + 1) * sizeof(int), &cursor, "cudaMalloc sparse cursor") != 0 ||
+        scratch_slot(ctx, kScratchCsrCursor, (tiles + 1) * sizeof(int), &tile_sums, "cudaMalloc sparse tiles") != 0 ||
         scratch_slot(ctx, kScratchCsrEntries, max_entries * sizeof(int), &entries, "cudaMalloc sparse entries") != 0)
         return -1;
-    cudaError_t st = cudaMemsetAsync(counts, 0, (n_rows + 1) * sizeof(int), ctx->stream);
-    if (st == cudaSuccess) st = cudaMemsetAsync(cursor, 0, (n_rows + 1) * sizeof(int), ctx->stream);
-    if (st != cudaSuccess) return fail("cudaMemsetAsync sparse index", st);
+    if (fresh) {
+        // counts are left at zero by every fill; clear them once per allocation
+        cudaError_t st = cudaMemsetAsync(counts, 0, ctx->scratch[kScratchCsrCounts].bytes, ctx->stream);
+        if (st != cudaSuccess) return fail("cudaMemsetAsync sparse counts", st);
+    }
     const int threads = 256;
     int blocks = 0;
     if (grid_1d(2 * slots, threads, &blocks, "sparse count") != 0) return -1;
+    int* c = static_cast<int*>(counts);
+    int* o = static_cast<int*>(offsets);
+    int* t = static_cast<int*>(tile_sums);
     if (blocks > 0) {
-        count_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, map, static_cast<int*>(counts));
+        count_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, map, c);
         if (check_launch("sparse count launch") != 0) return -1;
     }
-    scan_rows_kernel<<<1, 1024, 0, ctx->stream>>>(static_cast<int*>(counts), static_cast<int*>(offsets),
-                                                   static_cast<int>(n_rows));
+    const int n = static_cast<int>(n_rows);
+    scan_tile_sums_kernel<<<tiles, kScanThreads, 0, ctx->stream>>>(c, n, t);
+    scan_tile_offsets_kernel<<<1, kScanThreads, 0, ctx->stream>>>(t, tiles);
+    scan_apply_kernel<<<tiles, kScanThreads, 0, ctx->stream>>>(c, n, t, tiles, o);
     if (check_launch("sparse scan launch") != 0) return -1;
     if (blocks > 0) {
-        fill_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, max_active, map,
-                                                             static_cast<int*>(offsets), static_cast<int*>(cursor),
+        fill_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, max_active, map, o, c,
                                                              static_cast<int*>(entries));
         if (check_launch("sparse fill launch") != 0) return -1;
     }
-    out->offsets = static_cast<int*>(offsets);
+    out->offsets = o;
     out->entries = static_cast<int*>(entries);
-    out->counts = static_cast<int*>(counts);
-    out->n_rows = static_cast<int>(n_rows);
+    out->counts = c;
+    out->n_rows = n;
     out->capacity = max_entries;
     return 0;
 }
