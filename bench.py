@@ -251,45 +251,45 @@ def run_b200(args, rank, world, local, dist):
     phase_ms = {PHASES[p]: ms[p] / max(1, nsteps.value) for p in range(nphases.value)}
     clk = clocks.summary()
     # ---- end to end through the public API, host (pinned) buffers ----
-    runner_e2e = runner
-    bind_batch(runner_e2e, (bo.I32Buffer(ctx, args.batch * ACTIVE), bo.I32Buffer(ctx, args.batch * ACTIVE),
-                            bo.F32Buffer(ctx, args.batch), bo.F32Buffer(ctx, args.batch)))
-    s_pin, n_pin, t_pin, w_pin = runner_e2e.pinned_staging()
-    mean_host = bo.cuda_cpp.PinnedF32Buffer(ctx, 1)
-    e2e_steps = max(5, args.steps // 2)
-    for i in range(2):  # warm the path
+    # The reference runner's pipelined step (lib.rs:5801): uploads of step i+1
+    # on a second stream overlap step i; per step the batch is copied H2D from
+    # pinned host memory and the step's mean loss is copied D2H.
+    from bulletou_b200.cuda_cpp import NnueTrainStepHostBatch, NnueTrainStepUploadSlot, PinnedF32Buffer
+
+    upload_ctx = bo.Context(local)
+    sources = []
+    for b in batches:  # the data loader's output: batches already in pinned host memory
+        slot = NnueTrainStepUploadSlot(ctx, args.batch, ACTIVE)
+        slot.fill(NnueTrainStepHostBatch(b["stm"], b["nstm"], b["targets"], b["entry_weights"], args.batch, ACTIVE))
+        sources.append(slot)
+    e2e_steps = max(8, args.steps)
+    loss_ring = [PinnedF32Buffer(ctx, 1) for _ in range(e2e_steps)]
+    for i in range(3):  # warm the pipelined path
         step += 1
-        b = batches[i % N_BATCHES]
-        np.copyto(s_pin.host(), b["stm"]); np.copyto(n_pin.host(), b["nstm"])
-        np.copyto(t_pin.host(), b["targets"]); np.copyto(w_pin.host(), b["entry_weights"])
-        runner_e2e.upload_pinned()
-        runner_e2e.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=True)
-        lib.call("bulletou_b200_f32_download_pinned", ctx.as_ptr(), mean_host.as_ptr(),
-                 runner_e2e.loss_workspace.mean.as_ptr(), 1)
-        ctx.synchronize()
+        runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv, None, True,
+                                                             sources[i % N_BATCHES], loss_ring[i])
+    ctx.synchronize()
+    upload_ctx.synchronize()
     h2d = 0
     e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    t0 = time.perf_counter()
     e0.record(ctx)
-    losses = []
     for i in range(e2e_steps):
         step += 1
-        b = batches[i % N_BATCHES]
-        np.copyto(s_pin.host(), b["stm"]); np.copyto(n_pin.host(), b["nstm"])
-        np.copyto(t_pin.host(), b["targets"]); np.copyto(w_pin.host(), b["entry_weights"])
-        h2d = runner_e2e.upload_pinned()
-        runner_e2e.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=True)
-        lib.call("bulletou_b200_f32_download_pinned", ctx.as_ptr(), mean_host.as_ptr(),
-                 runner_e2e.loss_workspace.mean.as_ptr(), 1)
-        ctx.synchronize()
-        losses.append(float(mean_host.host()[0]))
+        h2d = runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv, None,
+                                                                   True, sources[i % N_BATCHES], loss_ring[i])
     e1.record(ctx)
     e1.synchronize()
-    e2e_ms = max_over_ranks(dist, e1.elapsed_ms_since(e0))
+    wall_ms = (time.perf_counter() - t0) * 1000.0
+    losses = [float(r.host()[0]) for r in loss_ring]
+    e2e_ms = max_over_ranks(dist, max(e1.elapsed_ms_since(e0), wall_ms))
     assert all(np.isfinite(losses)), "non-finite loss"
     return {
         "total_ms": total_ms, "phase_ms": phase_ms, "clocks": clk,
         "e2e": {"value": e2e_steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
-                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps},
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
+                "path": "NnueTrainStepRunner.step_pipelined_no_readback_with_loss_finalize (2 upload slots, "
+                        "second stream), inputs in pinned host memory, mean loss copied D2H every step"},
         "gpu_launches": LAUNCHES_PER_STEP * args.steps,
         "final_loss": losses[-1],
     }
@@ -322,27 +322,33 @@ def run_reference(args, local):
         stop.synchronize()
     total_ms = stop.elapsed_ms_since(start)
     clk = clocks.summary()
-    # end to end through the reference API: pinned staged uploads, loss read back
-    bind_batch(runner, (bo.I32Buffer(ctx, args.batch * ACTIVE), bo.I32Buffer(ctx, args.batch * ACTIVE),
-                        bo.F32Buffer(ctx, args.batch), bo.F32Buffer(ctx, args.batch)))
-    pins = (bo.cuda_cpp.PinnedI32Buffer(ctx, args.batch * ACTIVE), bo.cuda_cpp.PinnedI32Buffer(ctx, args.batch * ACTIVE),
-            bo.cuda_cpp.PinnedF32Buffer(ctx, args.batch), bo.cuda_cpp.PinnedF32Buffer(ctx, args.batch))
-    e2e_steps = max(5, args.steps // 2)
+    # end to end through the reference API: the pipelined runner step
+    # (lib.rs:5801) with staged pinned uploads on a second stream; the mean
+    # loss is read back every step (the reference ABI's download is synchronous)
+    from bulletou_b200.cuda_cpp import NnueTrainStepHostBatch
+
+    upload_ctx = bo.Context(local, lib)
+    hbs = [NnueTrainStepHostBatch(b["stm"], b["nstm"], b["targets"], b["entry_weights"], args.batch, ACTIVE)
+           for b in batches]
+    e2e_steps = max(8, args.steps // 2)
+    for i in range(2):
+        step += 1
+        runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv,
+                                                             hbs[i % N_BATCHES], True)
+        runner.loss_workspace.mean.download(ctx)
+    ctx.synchronize()
     e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    t0 = time.perf_counter()
     e0.record(ctx)
+    h2d = 0
     for i in range(e2e_steps):
         step += 1
-        b = batches[i % N_BATCHES]
-        pins[0].upload_to_device(ctx, runner.stm_indices, b["stm"])
-        pins[1].upload_to_device(ctx, runner.nstm_indices, b["nstm"])
-        pins[2].upload_to_device(ctx, runner.targets, b["targets"])
-        pins[3].upload_to_device(ctx, runner.entry_weights, b["entry_weights"])
-        runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=True)
+        h2d = runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv,
+                                                                   hbs[i % N_BATCHES], True)
         runner.loss_workspace.mean.download(ctx)
     e1.record(ctx)
     e1.synchronize()
-    e2e_ms = e1.elapsed_ms_since(e0)
-    h2d = 4 * (2 * args.batch * ACTIVE + 2 * args.batch)
+    e2e_ms = max(e1.elapsed_ms_since(e0), (time.perf_counter() - t0) * 1000.0)
     return {"total_ms": total_ms, "clocks": clk,
             "e2e": {"value": e2e_steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": e2e_steps}}

@@ -44,61 +44,96 @@ __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f),
 __device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f && a < 1.0f ? g : 0.0f; }
 
 // ------------------------------------------------------------------ king sort
-__global__ void king_count_kernel(const int* __restrict__ stm, const int* __restrict__ nstm, int batch, int A,
-                                  int input_size, int* __restrict__ keys, int* __restrict__ counts) {
+// Stable counting sort of half-positions h = 2*sample + perspective by king.
+// Three deterministic passes (no global atomics): per-block key histograms,
+// per-key bases over blocks, and an ordered scatter (within a bucket, h ascending).
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+
+__device__ __forceinline__ int half_position_key(const int* __restrict__ stm, const int* __restrict__ nstm, int h, int A,
+                                                 int input_size) {
+    const int* idx = ((h & 1) ? nstm : stm) + static_cast<size_t>(h >> 1) * A;
+    for (int s = 0; s < A; ++s) {
+        const int f = __ldg(idx + s);
+        if (f >= 0 && f < input_size) return min(f / kPiecesPerKing, kKingKeys - 1);
+    }
+    return kKingKeys - 1;
+}
+
+__global__ void __launch_bounds__(kSortThreads) king_hist_kernel(const int* __restrict__ stm,
+                                                                 const int* __restrict__ nstm, int n_half, int A,
+                                                                 int input_size, int* __restrict__ keys,
+                                                                 int* __restrict__ block_hist) {
     __shared__ int hist[kKingKeys];
     for (int i = threadIdx.x; i < kKingKeys; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    const int h = blockIdx.x * blockDim.x + threadIdx.x;
-    if (h < 2 * batch) {
-        const int* idx = ((h & 1) ? nstm : stm) + static_cast<size_t>(h >> 1) * A;
-        int key = kKingKeys - 1;
-        for (int s = 0; s < A; ++s) {
-            const int f = __ldg(idx + s);
-            if (f >= 0 && f < input_size) {
-                key = min(f / kPiecesPerKing, kKingKeys - 1);
-                break;
-            }
-        }
-        keys[h] = key;
-        atomicAdd(&hist[key], 1);
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < kKingKeys; i += blockDim.x)
-        if (hist[i] != 0) atomicAdd(&counts[i], hist[i]);
-}
-
-// Exclusive offsets of the king buckets; clears the counts for the next step
-// and the scatter cursors for this one.
-__global__ void king_scan_kernel(int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ cursor) {
-    if (threadIdx.x == 0) {
-        int run = 0;
-        for (int k = 0; k < kKingKeys; ++k) {
-            offsets[k] = run;
-            run += counts[k];
-            counts[k] = 0;
-        }
-    }
-    for (int k = threadIdx.x; k < kKingKeys; k += blockDim.x) cursor[k] = 0;
-}
-
-__global__ void king_scatter_kernel(const int* __restrict__ keys, int n_half, const int* __restrict__ offsets,
-                                    int* __restrict__ cursor, int* __restrict__ order) {
-    __shared__ int hist[kKingKeys];
-    __shared__ int base[kKingKeys];
-    for (int i = threadIdx.x; i < kKingKeys; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
-    const int h = blockIdx.x * blockDim.x + threadIdx.x;
-    int key = 0, local = 0;
+    const int h = blockIdx.x * kSortThreads + threadIdx.x;
     if (h < n_half) {
-        key = keys[h];
-        local = atomicAdd(&hist[key], 1);
+        const int key = half_position_key(stm, nstm, h, A, input_size);
+        keys[h] = key;
+        atomicAdd(&hist[key], 1);  // counts only: order-independent
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < kKingKeys; i += blockDim.x)
-        if (hist[i] != 0) base[i] = atomicAdd(&cursor[i], hist[i]);
+    for (int i = threadIdx.x; i < kKingKeys; i += blockDim.x) block_hist[blockIdx.x * kKingKeys + i] = hist[i];
+}
+
+// One CTA: king_off[k] = first slot of bucket k (king_off[82] = n_half); block_hist
+// becomes, per (block, key), the first slot of that block's items of that key.
+__global__ void __launch_bounds__(128) king_bases_kernel(int* __restrict__ block_hist, int nblocks,
+                                                         int* __restrict__ king_off) {
+    __shared__ int total[kKingKeys];
+    const int k = threadIdx.x;
+    if (k < kKingKeys) {
+        int s = 0;
+#pragma unroll 8
+        for (int b = 0; b < nblocks; ++b) s += block_hist[b * kKingKeys + k];
+        total[k] = s;
+    }
     __syncthreads();
-    if (h < n_half) order[offsets[key] + base[key] + local] = h;
+    if (k == 0) {
+        int run = 0;
+        for (int i = 0; i < kKingKeys; ++i) {
+            const int t = total[i];
+            total[i] = run;
+            run += t;
+        }
+        king_off[kKingKeys] = run;
+    }
+    __syncthreads();
+    if (k < kKingKeys) {
+        int run = total[k];
+        king_off[k] = run;
+#pragma unroll 8
+        for (int b = 0; b < nblocks; ++b) {
+            const int c = block_hist[b * kKingKeys + k];
+            block_hist[b * kKingKeys + k] = run;
+            run += c;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kSortThreads) king_scatter_kernel(const int* __restrict__ keys, int n_half,
+                                                                    const int* __restrict__ block_base,
+                                                                    int* __restrict__ order, int* __restrict__ slot_of,
+                                                                    const int* __restrict__ king_off) {
+    __shared__ int wcount[kSortWarps][kKingKeys];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < kSortWarps * kKingKeys; i += blockDim.x) (&wcount[0][0])[i] = 0;
+    __syncthreads();
+    const int h = blockIdx.x * kSortThreads + threadIdx.x;
+    const bool valid = h < n_half;
+    const int key = valid ? keys[h] : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (valid && rank == 0) wcount[warp][key] = __popc(peers);
+    __syncthreads();
+    if (valid) {
+        int before = 0;
+        for (int w = 0; w < warp; ++w) before += wcount[w][key];
+        const int pos = block_base[blockIdx.x * kKingKeys + key] + before + rank;
+        order[pos] = h;
+        if (slot_of != nullptr) slot_of[h] = pos - king_off[key];
+    }
 }
 
 // ------------------------------------------------------------------ gather
@@ -441,6 +476,9 @@ __global__ void __launch_bounds__(256) halfkp_reduce_kernel(HalfkpActivations a,
     __shared__ float g1_s[kReduceTile][32];
     __shared__ float h1_s[kReduceTile][32];
     __shared__ float g2_s[kReduceTile][32];
+    __shared__ float h2_s[kReduceTile][32];
+    __shared__ float mog_s[kReduceTile];
+    __shared__ float ps_s[kReduceTile];
     const int t = threadIdx.x;
     const int j = t & 31, ib = t >> 5;
     const int slice = blockIdx.y * kSlice;
@@ -471,23 +509,38 @@ __global__ void __launch_bounds__(256) halfkp_reduce_kernel(HalfkpActivations a,
         }
         if (lead) {
             // l0 bias: column sums of the pre-activation gradient (stm + nstm)
-            for (int p = 0; p < np; ++p) {
-                const float* pg = a.pregrad + static_cast<size_t>(base + p) * kIn;
+            float sv[kReduceTile][L1 / 256], nv[kReduceTile][L1 / 256];
 #pragma unroll
-                for (int r = 0; r < L1 / 256; ++r) acc_l0b[r] += __ldg(pg + r * 256 + t) + __ldg(pg + L1 + r * 256 + t);
-            }
-            if (t < 98) {
-                for (int p = 0; p < np; ++p) {
-                    const size_t b = base + p;
-                    if (t < 32) acc_vec += a.g1[b * 32 + t];
-                    else if (t < 64) acc_vec += a.g2[b * 32 + t - 32];
-                    else if (t < 96) acc_vec = fmaf(a.mog[b], a.hidden2[b * 32 + t - 64], acc_vec);
-                    else if (t == 96) acc_vec += a.mog[b];
-                    else acc_vec += a.per_sample[b];
+            for (int p = 0; p < kReduceTile; ++p) {
+                const float* pg = a.pregrad + static_cast<size_t>(base + min(p, np - 1)) * kIn;
+#pragma unroll
+                for (int r = 0; r < L1 / 256; ++r) {
+                    sv[p][r] = __ldg(pg + r * 256 + t);
+                    nv[p][r] = __ldg(pg + L1 + r * 256 + t);
                 }
             }
+            for (int p = 0; p < np; ++p)
+#pragma unroll
+                for (int r = 0; r < L1 / 256; ++r) acc_l0b[r] += sv[p][r] + nv[p][r];
+        }
+        for (int e = t; e < kReduceTile * 32; e += 256) {
+            const int p = e >> 5, c = e & 31;
+            h2_s[p][c] = (lead && p < np) ? a.hidden2[static_cast<size_t>(base + p) * 32 + c] : 0.0f;
+        }
+        if (t < kReduceTile) {
+            mog_s[t] = (lead && t < np) ? a.mog[base + t] : 0.0f;
+            ps_s[t] = (lead && t < np) ? a.per_sample[base + t] : 0.0f;
         }
         __syncthreads();
+        if (lead && t < 98) {
+            for (int p = 0; p < np; ++p) {
+                if (t < 32) acc_vec += g1_s[p][t];
+                else if (t < 64) acc_vec += g2_s[p][t - 32];
+                else if (t < 96) acc_vec = fmaf(mog_s[p], h2_s[p][t - 64], acc_vec);
+                else if (t == 96) acc_vec += mog_s[p];
+                else acc_vec += ps_s[p];
+            }
+        }
         for (int p = 0; p < np; ++p) {
             const float g = g1_s[p][j];
             const float4* row = reinterpret_cast<const float4*>(&act_s[p][ib * kIPer]);
@@ -602,24 +655,20 @@ int halfkp_fast_forward_backward(BulletOuCudaCppContext* ctx, const HalfkpDims& 
                                  const float* targets, const float* entry_weights, const LossArgs* loss,
                                  float* stm_l0, float* nstm_l0) {
     const int n_half = 2 * d.batch;
-    // king sort scratch: keys [2B], order [2B], counts/offsets/cursor [3 x 82]
+    const int nblocks = (n_half + kSortThreads - 1) / kSortThreads;
+    // king sort scratch (fixed layout at the slot's start):
+    // king_off [83] | keys [2B] | order [2B] | block_hist [nblocks x 82]
     void* sort_mem = nullptr;
-    const size_t sort_bytes = (2 * static_cast<size_t>(n_half) + 3 * kKingKeys) * sizeof(int);
-    const bool fresh = ctx->scratch[kScratchKingSort].bytes < sort_bytes;
-    if (scratch_slot(ctx, kScratchKingSort, sort_bytes, &sort_mem, "cudaMalloc king sort") != 0) return -1;
-    int* keys = static_cast<int*>(sort_mem);
+    const size_t sort_ints = kKingKeys + 1 + 2 * static_cast<size_t>(n_half) + static_cast<size_t>(nblocks) * kKingKeys;
+    if (scratch_slot(ctx, kScratchKingSort, sort_ints * sizeof(int), &sort_mem, "cudaMalloc king sort") != 0) return -1;
+    int* king_off = static_cast<int*>(sort_mem);
+    int* keys = king_off + kKingKeys + 1;
     int* order = keys + n_half;
-    int* counts = order + n_half;
-    int* offsets = counts + kKingKeys;
-    int* cursor = offsets + kKingKeys;
-    if (fresh) {
-        cudaError_t st = cudaMemsetAsync(counts, 0, kKingKeys * sizeof(int), ctx->stream);
-        if (st != cudaSuccess) return fail("cudaMemsetAsync king counts", st);
-    }
-    const int blocks = (n_half + 255) / 256;
-    king_count_kernel<<<blocks, 256, 0, ctx->stream>>>(stm, nstm, d.batch, d.max_active, d.input_size, keys, counts);
-    king_scan_kernel<<<1, 128, 0, ctx->stream>>>(counts, offsets, cursor);
-    king_scatter_kernel<<<blocks, 256, 0, ctx->stream>>>(keys, n_half, offsets, cursor, order);
+    int* block_hist = order + n_half;
+    king_hist_kernel<<<nblocks, kSortThreads, 0, ctx->stream>>>(stm, nstm, n_half, d.max_active, d.input_size, keys,
+                                                               block_hist);
+    king_bases_kernel<<<1, 128, 0, ctx->stream>>>(block_hist, nblocks, king_off);
+    king_scatter_kernel<<<nblocks, kSortThreads, 0, ctx->stream>>>(keys, n_half, block_hist, order, nullptr, king_off);
     if (check_launch("king sort launch") != 0) return -1;
     prof_mark(ctx);
     const int rc = d.l1 == 256 ? launch_gather<1>(ctx, order, n_half, stm, nstm, d.max_active, map, w.l0w, w.l0b,

@@ -186,7 +186,7 @@ __device__ __forceinline__ void store_vec(float* p, const float* in) {
 }
 
 template <int VEC, int MODE>
-__global__ void __launch_bounds__(kRowWarps * 32) row_kernel(RowKernelArgs a, int rows_to_process) {
+__global__ void __launch_bounds__(kRowWarps * 32, 3) row_kernel(RowKernelArgs a, int rows_to_process) {
     __shared__ int sort_buf[kRowWarps][kSortCap];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int local = blockIdx.x * kRowWarps + warp;

@@ -714,6 +714,56 @@ class RangerParamState:
                 "slow_params": self.slow_params.download(ctx)}
 
 
+class NnueTrainStepUploadSlot:
+    """Device batch buffers + pinned staging + upload/compute events
+    (NnueTrainStepUploadSlot, lib.rs:5509-5600).  Before a slot is refilled,
+    the previous upload must have finished (the pinned memory is reused) and
+    the compute stream must be done with the device buffers."""
+
+    def __init__(self, ctx: Context, batch_size: int, max_active: int):
+        n = batch_size * max_active
+        self.stm_indices, self.nstm_indices = I32Buffer(ctx, n), I32Buffer(ctx, n)
+        self.targets, self.entry_weights = F32Buffer(ctx, batch_size), F32Buffer(ctx, batch_size)
+        self.pinned = (PinnedI32Buffer(ctx, n), PinnedI32Buffer(ctx, n), PinnedF32Buffer(ctx, batch_size),
+                       PinnedF32Buffer(ctx, batch_size))
+        self.upload_ready = Event(ctx)
+        self.compute_done = Event(ctx)
+        self.in_use = False
+
+    def fill(self, batch: "NnueTrainStepHostBatch") -> None:
+        for dst, src in zip(self.pinned, (batch.stm_indices, batch.nstm_indices, batch.targets, batch.entry_weights)):
+            np.copyto(dst.host(), np.asarray(src).reshape(-1))
+
+    def upload(self, upload_ctx: Context, batch, pinned_source=None) -> int:
+        lib = upload_ctx.lib
+        if self.in_use:
+            self.upload_ready.synchronize()
+            self.compute_done.wait(upload_ctx)
+        if not lib.has("bulletou_b200_i32_upload_pinned"):
+            # the reference ABI: staged uploads (host memcpy into the pinned
+            # staging buffer, then an async copy), lib.rs:5552-5575
+            if batch is None:
+                raise CudaCppError("this backend needs host batch arrays for staged uploads")
+            self.pinned[0].upload_to_device(upload_ctx, self.stm_indices, batch.stm_indices)
+            self.pinned[1].upload_to_device(upload_ctx, self.nstm_indices, batch.nstm_indices)
+            self.pinned[2].upload_to_device(upload_ctx, self.targets, batch.targets)
+            self.pinned[3].upload_to_device(upload_ctx, self.entry_weights, batch.entry_weights)
+            self.upload_ready.record(upload_ctx)
+            self.in_use = True
+            return 4 * sum(x.length for x in self.pinned)
+        src = pinned_source.pinned if pinned_source is not None else self.pinned
+        if pinned_source is None:
+            self.fill(batch)
+        c = upload_ctx.as_ptr()
+        lib.call("bulletou_b200_i32_upload_pinned", c, self.stm_indices.as_ptr(), src[0].as_ptr(), src[0].length)
+        lib.call("bulletou_b200_i32_upload_pinned", c, self.nstm_indices.as_ptr(), src[1].as_ptr(), src[1].length)
+        lib.call("bulletou_b200_f32_upload_pinned", c, self.targets.as_ptr(), src[2].as_ptr(), src[2].length)
+        lib.call("bulletou_b200_f32_upload_pinned", c, self.entry_weights.as_ptr(), src[3].as_ptr(), src[3].length)
+        self.upload_ready.record(upload_ctx)
+        self.in_use = True
+        return 4 * sum(x.length for x in src)
+
+
 class NnueTrainStepRunner:
     """HalfKP train-step runner (lib.rs:5590-6024).
 
@@ -842,6 +892,37 @@ class NnueTrainStepRunner:
                              self.weights, fws, lw.mean_output_gradients, bws, False)
         for g, w, st in zip(bws.param_gradients(), self.weights, self.optimizer_states):
             ranger_update_device(ctx, params, RangerDeviceState(g, w, st.momentum, st.velocity, st.slow_params))
+
+    # -- pipelined steps (lib.rs:5509-5600, 5801-5856) ----------------------
+    def upload_slots(self, count: int = 2) -> list["NnueTrainStepUploadSlot"]:
+        if getattr(self, "_slots", None) is None or len(self._slots) != count:
+            self._slots = [NnueTrainStepUploadSlot(self.ctx, self.batch_size, self.max_active) for _ in range(count)]
+            self._next_slot = 0
+        return self._slots
+
+    def step_pipelined_no_readback_with_loss_finalize(self, ctx: Context, upload_ctx: Context,
+                                                      params: RangerUpdateParams, loss_kind: ScalarLossKind,
+                                                      output_inv_scale: float, batch: "NnueTrainStepHostBatch | None",
+                                                      finalize_loss: bool = True,
+                                                      pinned_source: "NnueTrainStepUploadSlot | None" = None,
+                                                      loss_out: "PinnedF32Buffer | None" = None) -> int:
+        """Upload on `upload_ctx` into the next slot, hand off with an event,
+        run the step on `ctx`, then (optionally) an async D2H of the mean loss
+        into `loss_out`.  Returns H2D bytes.  `pinned_source` uploads straight
+        from an already-filled pinned slot instead of staging `batch`."""
+        slots = self.upload_slots()
+        slot = slots[self._next_slot]
+        self._next_slot = (self._next_slot + 1) % len(slots)
+        nbytes = slot.upload(upload_ctx, batch, pinned_source)
+        slot.upload_ready.wait(ctx)
+        self.stm_indices, self.nstm_indices = slot.stm_indices, slot.nstm_indices
+        self.targets, self.entry_weights = slot.targets, slot.entry_weights
+        self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
+        if loss_out is not None:
+            self.lib.call("bulletou_b200_f32_download_pinned", ctx.as_ptr(), loss_out.as_ptr(),
+                          self.loss_workspace.mean.as_ptr(), 1)
+        slot.compute_done.record(ctx)
+        return nbytes
 
     # -- readback ----------------------------------------------------------
     def read_loss(self, ctx: Optional[Context] = None) -> ScalarLossReadback:
