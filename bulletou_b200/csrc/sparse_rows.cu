@@ -185,33 +185,50 @@ __device__ __forceinline__ void store_vec(float* p, const float* in) {
     }
 }
 
+// One CTA per chunk of kRowChunk consecutive rows.  The chunk's offsets and
+// its (contiguous) entry range are first copied into shared memory with
+// coalesced loads, so the only global reads left per row are the independent
+// gradient-row gathers (L2) and the optimizer-state rows (HBM).
 template <int VEC, int MODE>
 __global__ void __launch_bounds__(kRowWarps * 32, 3) row_kernel(RowKernelArgs a, int rows_to_process) {
     __shared__ int sort_buf[kRowWarps][kSortCap];
+    __shared__ int off_s[kRowChunk + 1];
+    __shared__ int ent_s[kChunkEntryCap];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int local = blockIdx.x * kRowWarps + warp;
-    if (local >= rows_to_process) return;
+    const int chunk0 = blockIdx.x * kRowChunk;
+    const int chunk_rows = min(kRowChunk, rows_to_process - chunk0);
+    for (int i = threadIdx.x; i <= chunk_rows; i += blockDim.x) off_s[i] = a.offsets[a.row_begin + chunk0 + i];
+    __syncthreads();
+    const int e_begin = off_s[0];
+    const int e_count = off_s[chunk_rows] - e_begin;
+    const bool cached = e_count <= kChunkEntryCap;
+    if (cached)
+        for (int i = threadIdx.x; i < e_count; i += blockDim.x) ent_s[i] = a.entries[e_begin + i];
+    __syncthreads();
+    for (int lr = warp; lr < chunk_rows; lr += kRowWarps) {
+    const int local = chunk0 + lr;
     const int row = a.row_begin + local;
-    const int beg = a.offsets[row];
-    const int n = a.offsets[row + 1] - beg;
+    const int beg = off_s[lr] - e_begin;
+    const int n = off_s[lr + 1] - off_s[lr];
+    const int* elist = cached ? ent_s + beg : a.entries + e_begin + beg;
 
     int mine = INT_MAX;
-    int mode = 0;  // 0: register list, 1: sorted SMEM list, 2: unsorted global list
+    int mode = 0;  // 0: register list, 1: sorted SMEM list, 2: unsorted list
     if (n <= 32) {
-        mine = lane < n ? a.entries[beg + lane] : INT_MAX;
+        mine = lane < n ? elist[lane] : INT_MAX;
         mine = warp_sort_ascending(mine, lane);
     } else if (n <= kSortCap) {
         int size = 64;
         while (size < n) size <<= 1;
         int* buf = sort_buf[warp];
-        for (int i = lane; i < size; i += 32) buf[i] = i < n ? a.entries[beg + i] : INT_MAX;
+        for (int i = lane; i < size; i += 32) buf[i] = i < n ? elist[i] : INT_MAX;
         __syncwarp();
         smem_sort_ascending(buf, size, lane);
         mode = 1;
     } else {
         mode = 2;
     }
-    const int* list = mode == 1 ? sort_buf[warp] : a.entries + beg;
+    const int* list = mode == 1 ? sort_buf[warp] : elist;
 
     const size_t row_off = static_cast<size_t>(row) * a.width;
     const size_t out_off = static_cast<size_t>(local) * a.width;
@@ -288,11 +305,13 @@ __global__ void __launch_bounds__(kRowWarps * 32, 3) row_kernel(RowKernelArgs a,
             store_vec<VEC>(a.velocity + row_off + c, v);
         }
     }
+    __syncwarp();
+    }
 }
 
 template <int MODE>
 int launch_row_mode(BulletOuCudaCppContext* ctx, const RowKernelArgs& a, int rows, int vec) {
-    const int blocks = (rows + kRowWarps - 1) / kRowWarps;
+    const int blocks = (rows + kRowChunk - 1) / kRowChunk;
     if (vec == 8) row_kernel<8, MODE><<<blocks, kRowWarps * 32, 0, ctx->stream>>>(a, rows);
     else if (vec == 4) row_kernel<4, MODE><<<blocks, kRowWarps * 32, 0, ctx->stream>>>(a, rows);
     else row_kernel<1, MODE><<<blocks, kRowWarps * 32, 0, ctx->stream>>>(a, rows);

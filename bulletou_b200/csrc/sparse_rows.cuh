@@ -20,6 +20,8 @@ namespace bou {
 
 constexpr int kRowWarps = 8;         // warps per CTA in the row kernels
 constexpr int kSortCap = 512;        // per-warp SMEM sort capacity (entries)
+constexpr int kRowChunk = 64;        // rows per CTA in the row kernels
+constexpr int kChunkEntryCap = 4096; // entries of a chunk staged in SMEM (else read from global)
 
 // Row ids touched by one sparse feature id.  HalfKP factorization (input_size
 // == 125388 + 1548): feature f < 125388 maps to rows 1548+f and f % 1548,
