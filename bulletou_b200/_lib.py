@@ -116,6 +116,7 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_f32_buffer_view": [P, Z, Z, P],
     "bulletou_b200_profile_begin": [P, Z],
     "bulletou_b200_profile_end": [P, P, Z, P, P],
+    "bulletou_b200_nnue_forward_device_noalloc": [P, Z, Z, Z, Z, Z, Z] + [P] * 16,
     "bulletou_b200_nnue_train_step_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P],
     "bulletou_b200_nnue_dense_gradient_len": [Z, Z, Z, P],
     "bulletou_b200_nnue_local_gradients_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P],

@@ -23,6 +23,8 @@
 //   4. reduce     -- every small-parameter gradient (dW1, dW2, biases, output
 //      layer, l0 bias) and the loss sum as per-chunk partial sums (fixed order).
 //   5. finalize   -- partials summed in chunk order; Ranger on the small groups.
+#include <mutex>
+
 #include "halfkp_fast.cuh"
 
 namespace bou {
@@ -717,3 +719,109 @@ int halfkp_fast_small_params(BulletOuCudaCppContext* ctx, const HalfkpDims& d, c
 }
 
 }  // namespace bou
+
+// ---------------------------------------------------------------------------
+// Allocation-free HalfKP forward (bulletou_b200_nnue_forward_device_noalloc).
+//
+// The only scratch the production-shape forward needs is the king sort's
+// (bucket offsets, keys, order, per-block histograms).  Here it lives in one
+// file-scope device array sized for kNoAllocMaxBatch positions, so the entry
+// point never calls cudaMalloc: it is usable by callers that cannot allocate
+// device memory at run time.  Every kernel overwrites each scratch word before
+// reading it, so nothing needs clearing between calls; the array is shared by
+// all calls on a device, so calls whose work overlaps on the GPU race.
+namespace bou {
+namespace {
+
+constexpr int kNoAllocMaxBatch = 65536;
+constexpr int kNoAllocMaxHalf = 2 * kNoAllocMaxBatch;
+constexpr int kNoAllocMaxBlocks = (kNoAllocMaxHalf + kSortThreads - 1) / kSortThreads;
+constexpr size_t kNoAllocInts =
+    (kKingKeys + 1) + 2 * static_cast<size_t>(kNoAllocMaxHalf) + static_cast<size_t>(kNoAllocMaxBlocks) * kKingKeys;
+constexpr int kNoAllocMaxDevices = 64;
+
+__device__ __align__(256) int g_noalloc_king_scratch[kNoAllocInts];
+
+std::mutex g_noalloc_mutex;
+int* g_noalloc_device_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the static scratch on `device` (which must be current);
+// resolved once per device.
+int noalloc_scratch(int device, int** out) {
+    if (device < 0 || device >= kNoAllocMaxDevices) return fail_messagef("no-allocation forward: device %d unsupported", device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_device_ptr[device] == nullptr) {
+        void* p = nullptr;
+        cudaError_t st = cudaGetSymbolAddress(&p, g_noalloc_king_scratch);
+        if (st != cudaSuccess) return fail("cudaGetSymbolAddress no-allocation scratch", st);
+        g_noalloc_device_ptr[device] = static_cast<int*>(p);
+    }
+    *out = g_noalloc_device_ptr[device];
+    return 0;
+}
+
+}  // namespace
+}  // namespace bou
+
+extern "C" int bulletou_b200_nnue_forward_device_noalloc(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2, size_t l3, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* l0w, const BulletOuCudaCppF32Buffer* l0b, const BulletOuCudaCppF32Buffer* l1w,
+    const BulletOuCudaCppF32Buffer* l1b, const BulletOuCudaCppF32Buffer* l2w, const BulletOuCudaCppF32Buffer* l2b,
+    const BulletOuCudaCppF32Buffer* outw, const BulletOuCudaCppF32Buffer* outb, BulletOuCudaCppF32Buffer* stm_l0,
+    BulletOuCudaCppF32Buffer* nstm_l0, BulletOuCudaCppF32Buffer* combined, BulletOuCudaCppF32Buffer* hidden1,
+    BulletOuCudaCppF32Buffer* hidden2, BulletOuCudaCppF32Buffer* output) {
+    using namespace bou;
+    if (input_size == 0 || l1 == 0 || l2 == 0 || l3 == 0 || batch == 0 || max_active == 0)
+        return fail_message("NNUE shape, batch and max_active must be greater than zero");
+    if (!halfkp_fast_shape(l1, l2, l3, batch, max_active))
+        return fail_message("no-allocation forward supports l1 in {256, 512}, l2 = l3 = 32 and max_active <= 4096; "
+                            "use bulletou_cuda_cpp_nnue_forward_device for other shapes");
+    if (batch > static_cast<size_t>(kNoAllocMaxBatch))
+        return fail_messagef("no-allocation forward: batch %zu exceeds its static scratch limit of %d positions",
+                             batch, kNoAllocMaxBatch);
+    if (input_size > static_cast<size_t>(INT_MAX / 2))
+        return fail_message("no-allocation forward: input_size too large");
+    if (validate_i32(ctx, stm_indices, batch * max_active, "stm_indices") != 0 ||
+        validate_i32(ctx, nstm_indices, batch * max_active, "nstm_indices") != 0 ||
+        validate_f32(ctx, l0w, input_size * l1, "l0w") != 0 || validate_f32(ctx, l0b, l1, "l0b") != 0 ||
+        validate_f32(ctx, l1w, l1 * 2 * l2, "l1w") != 0 || validate_f32(ctx, l1b, l2, "l1b") != 0 ||
+        validate_f32(ctx, l2w, l2 * l3, "l2w") != 0 || validate_f32(ctx, l2b, l3, "l2b") != 0 ||
+        validate_f32(ctx, outw, l3, "outw") != 0 || validate_f32(ctx, outb, 1, "outb") != 0 ||
+        validate_f32(ctx, stm_l0, batch * l1, "stm_l0") != 0 || validate_f32(ctx, nstm_l0, batch * l1, "nstm_l0") != 0 ||
+        validate_f32(ctx, combined, batch * l1 * 2, "combined") != 0 ||
+        validate_f32(ctx, hidden1, batch * l2, "hidden1") != 0 || validate_f32(ctx, hidden2, batch * l3, "hidden2") != 0 ||
+        validate_f32(ctx, output, batch, "output") != 0)
+        return -1;
+    if (set_device(ctx) != 0) return -1;
+    int* scratch = nullptr;
+    if (noalloc_scratch(ctx->device, &scratch) != 0) return -1;
+    const HalfkpDims d{static_cast<int>(input_size), static_cast<int>(l1), static_cast<int>(batch),
+                       static_cast<int>(max_active)};
+    const RowMap map = make_row_map(input_size);
+    const int n_half = 2 * d.batch;
+    const int nblocks = (n_half + kSortThreads - 1) / kSortThreads;
+    int* king_off = scratch;
+    int* keys = king_off + kKingKeys + 1;
+    int* order = keys + n_half;
+    int* block_hist = order + n_half;
+    king_hist_kernel<<<nblocks, kSortThreads, 0, ctx->stream>>>(stm_indices->ptr, nstm_indices->ptr, n_half,
+                                                               d.max_active, d.input_size, keys, block_hist);
+    king_bases_kernel<<<1, 128, 0, ctx->stream>>>(block_hist, nblocks, king_off);
+    king_scatter_kernel<<<nblocks, kSortThreads, 0, ctx->stream>>>(keys, n_half, block_hist, order, nullptr, king_off);
+    if (check_launch("no-allocation king sort launch") != 0) return -1;
+    const int rc = d.l1 == 256 ? launch_gather<1>(ctx, order, n_half, stm_indices->ptr, nstm_indices->ptr,
+                                                  d.max_active, map, l0w->ptr, l0b->ptr, combined->ptr, stm_l0->ptr,
+                                                  nstm_l0->ptr)
+                               : launch_gather<2>(ctx, order, n_half, stm_indices->ptr, nstm_indices->ptr,
+                                                  d.max_active, map, l0w->ptr, l0b->ptr, combined->ptr, stm_l0->ptr,
+                                                  nstm_l0->ptr);
+    if (rc != 0) return -1;
+    DenseArgs da{};
+    da.batch = d.batch;
+    da.w = HalfkpWeights{l0w->ptr, l0b->ptr, l1w->ptr, l1b->ptr, l2w->ptr, l2b->ptr, outw->ptr, outb->ptr};
+    da.a = HalfkpActivations{combined->ptr, hidden1->ptr, hidden2->ptr, output->ptr, nullptr,
+                             nullptr,       nullptr,      nullptr,      nullptr};
+    const int rd = d.l1 == 256 ? launch_dense<256, false>(ctx, da) : launch_dense<512, false>(ctx, da);
+    return rd == 0 ? ok() : rd;
+}

@@ -120,6 +120,32 @@ int bulletou_b200_nnue_train_step_device(
     BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
     BulletOuCudaCppF32Buffer* mean);
 
+/* HalfKP forward that allocates no device memory.  No counterpart in the
+ * reference backend.  It is for callers that must not call cudaMalloc while
+ * they run -- an engine or server that evaluates positions inside its own
+ * fixed memory budget, or code running where allocation is forbidden or
+ * would stall other work -- and who still want the production-shape kernels.
+ * Same arguments and outputs as bulletou_cuda_cpp_nnue_forward_device; only
+ * l1 in {256, 512}, l2 = l3 = 32, max_active <= 4096 and batch <= 65536
+ * positions are accepted (anything larger is rejected with an error).  Its
+ * scratch is one static device array of 1.2 MB that every GPU loading the
+ * library holds until exit; the first call on a device looks up that array's
+ * device address (make that first call before any stream capture).  Nothing
+ * in the array needs clearing between calls, but all calls on a device share
+ * it: calls whose work overlaps on the GPU (other streams, other threads)
+ * race and must be serialized by the caller. */
+int bulletou_b200_nnue_forward_device_noalloc(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2, size_t l3,
+    size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppF32Buffer* l0w, const BulletOuCudaCppF32Buffer* l0b,
+    const BulletOuCudaCppF32Buffer* l1w, const BulletOuCudaCppF32Buffer* l1b,
+    const BulletOuCudaCppF32Buffer* l2w, const BulletOuCudaCppF32Buffer* l2b,
+    const BulletOuCudaCppF32Buffer* outw, const BulletOuCudaCppF32Buffer* outb,
+    BulletOuCudaCppF32Buffer* stm_l0, BulletOuCudaCppF32Buffer* nstm_l0,
+    BulletOuCudaCppF32Buffer* combined, BulletOuCudaCppF32Buffer* hidden1,
+    BulletOuCudaCppF32Buffer* hidden2, BulletOuCudaCppF32Buffer* output);
+
 /* Length of the packed small-parameter gradient used by the data-parallel
  * phases: l0b | l1w | l1b | l2w | l2b | outw | outb. */
 int bulletou_b200_nnue_dense_gradient_len(size_t l1, size_t l2, size_t l3, size_t* out);
