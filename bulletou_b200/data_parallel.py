@@ -1,0 +1,289 @@
+"""Data-parallel HalfKP training over torch.distributed (NCCL on GPUs, gloo on CPU).
+
+The reference trains on one GPU (no collectives, cu:9503-9545); this module is
+the additive multi-GPU layer.  Positions are independent, so the only
+exchange is the gradient sum:
+
+    local step      forward + loss + backward of the rank's batch, the loss
+                    gradient normalised by the *global* batch
+                    (bulletou_b200_nnue_local_gradients_device): FT gradient
+                    rows [R][L1] and the packed small-parameter gradient
+    reduce-scatter  FT gradient by contiguous row shard (in place)
+    all-reduce      packed small-parameter gradient
+    Ranger          owned FT rows only (optimizer state is sharded: m, v and
+                    slow hold just the rank's rows) + all small groups
+                    (replicated, identical on every rank)
+    all-gather      updated FT rows (in place), so every rank holds the full
+                    table for the next forward
+
+The FT table and its gradient are padded to a multiple of the world size in
+rows (padding rows are never referenced by a feature).  A step on N ranks of
+batch B equals one single-GPU step on the concatenated batch of N*B up to
+summation order.
+
+`NnueDataParallelTrainer` holds the orchestration; the arithmetic comes from a
+backend: `B200Backend` (the CUDA library, zero-copy torch views of its
+buffers, collectives ordered on the library's stream) for training, and, in
+tests, a CPU backend built on the oracle so the sharding and collective logic
+runs on gloo without a GPU.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from .cuda_cpp import (NNUE_WEIGHT_NAMES, F32Buffer, I32Buffer, NnueForwardHostWeights, RangerDeviceState,
+                       RangerUpdateParams, ScalarLossKind, ScalarLossWorkspace, ranger_update_device)
+
+
+@dataclass(frozen=True)
+class ShardLayout:
+    """Row sharding of the FT table over `world` ranks."""
+
+    rows: int
+    width: int
+    world: int
+    rank: int
+
+    @property
+    def rows_padded(self) -> int:
+        return -(-self.rows // self.world) * self.world
+
+    @property
+    def shard_rows(self) -> int:
+        return self.rows_padded // self.world
+
+    @property
+    def row_begin(self) -> int:
+        return self.rank * self.shard_rows
+
+    @property
+    def real_rows(self) -> int:
+        """Owned rows that exist (the last shard may end in padding)."""
+        return max(0, min(self.rows, self.row_begin + self.shard_rows) - self.row_begin)
+
+
+def dense_gradient_layout(l1: int, l2: int, l3: int) -> list[tuple[str, int, int]]:
+    """(group, offset, length) of the packed small-parameter gradient:
+    l0b | l1w | l1b | l2w | l2b | outw | outb."""
+    sizes = [("l0b", l1), ("l1w", 2 * l1 * l2), ("l1b", l2), ("l2w", l2 * l3), ("l2b", l3), ("outw", l3), ("outb", 1)]
+    out, off = [], 0
+    for name, n in sizes:
+        out.append((name, off, n))
+        off += n
+    return out
+
+
+class B200Backend:
+    """libbulletou_b200 on one GPU; the context runs on torch's current stream
+    so NCCL collectives issued through torch order with the library's work."""
+
+    def __init__(self, device: int, lib=None):
+        import torch
+
+        from . import cuda_cpp as cc
+
+        self.torch = torch
+        self.device = device
+        stream = torch.cuda.current_stream(device).cuda_stream
+        self.ctx = cc.Context(device, lib, stream=stream)
+        self.lib = self.ctx.lib
+
+    def zeros(self, n: int) -> F32Buffer:
+        b = F32Buffer(self.ctx, n)
+        b.fill(0.0)
+        return b
+
+    def from_host(self, a) -> F32Buffer:
+        return F32Buffer.from_host(self.ctx, a)
+
+    def tensor(self, buf) -> "object":
+        return self.torch.as_tensor(buf, device=f"cuda:{self.device}")
+
+    def local_gradients(self, tr: "NnueDataParallelTrainer", loss_spec) -> None:
+        sh = tr.shape
+        arr = ctypes.c_void_p * 8
+        params = arr(*[w.as_ptr().value for w in tr.weights])
+        lw = tr.loss_workspace
+        self.lib.call("bulletou_b200_nnue_local_gradients_device", self.ctx.as_ptr(), sh.input_size, sh.l1, sh.l2,
+                      sh.l3, tr.batch_size, tr.max_active, tr.stm_indices.as_ptr(), tr.nstm_indices.as_ptr(),
+                      tr.targets.as_ptr(), tr.entry_weights.as_ptr(), ctypes.byref(loss_spec), params,
+                      tr.ft_grad.as_ptr(), tr.dense_grad.as_ptr(), tr.output.as_ptr(), lw.per_sample.as_ptr(),
+                      lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(), lw.mean.as_ptr())
+
+    def ranger(self, params: RangerUpdateParams, grad, weights, m, v, slow) -> None:
+        ranger_update_device(self.ctx, params, RangerDeviceState(grad, weights, m, v, slow))
+
+    def view(self, buf: F32Buffer, offset: int, length: int) -> F32Buffer:
+        return buf.view(offset, length)
+
+    def download(self, buf: F32Buffer) -> np.ndarray:
+        return buf.download()
+
+
+class NnueDataParallelTrainer:
+    """One rank of data-parallel HalfKP training (any backend, any collective group)."""
+
+    def __init__(self, backend, dist, initial_weights: NnueForwardHostWeights, batch_size: int, max_active: int):
+        initial_weights.validate()
+        self.backend = backend
+        self.dist = dist
+        self.world = dist.get_world_size()
+        self.rank = dist.get_rank()
+        self.shape = initial_weights.shape
+        self.batch_size = batch_size
+        self.max_active = max_active
+        sh = self.shape
+        self.layout = ShardLayout(sh.input_size, sh.l1, self.world, self.rank)
+        lay = self.layout
+        arrays = initial_weights.arrays()
+        l0w = np.zeros(lay.rows_padded * sh.l1, np.float32)
+        l0w[: arrays[0].size] = arrays[0]
+        self.weights = [backend.from_host(l0w)] + [backend.from_host(a) for a in arrays[1:]]
+        # optimizer state: owned FT rows only; small groups replicated
+        own = slice(lay.row_begin * sh.l1, (lay.row_begin + lay.real_rows) * sh.l1)
+        n_own = lay.real_rows * sh.l1
+        self.ft_state = (backend.zeros(n_own), backend.zeros(n_own), backend.from_host(l0w[own]))
+        self.small_state = [(backend.zeros(a.size), backend.zeros(a.size), backend.from_host(a)) for a in arrays[1:]]
+        self.ft_grad = backend.zeros(lay.rows_padded * sh.l1)
+        self.dense_layout = dense_gradient_layout(sh.l1, sh.l2, sh.l3)
+        self.dense_grad = backend.zeros(self.dense_layout[-1][1] + 1)
+        ctx = getattr(backend, "ctx", None)
+        n = batch_size * max_active
+        if ctx is not None:
+            self.stm_indices, self.nstm_indices = I32Buffer(ctx, n), I32Buffer(ctx, n)
+            self.targets, self.entry_weights = F32Buffer(ctx, batch_size), F32Buffer(ctx, batch_size)
+            self.output = F32Buffer(ctx, batch_size)
+            self.loss_workspace = ScalarLossWorkspace(ctx, batch_size)
+        # views for the update and the collectives
+        self.ft_grad_shard = backend.view(self.ft_grad, lay.row_begin * sh.l1, lay.real_rows * sh.l1)
+        self.l0w_shard = backend.view(self.weights[0], lay.row_begin * sh.l1, lay.real_rows * sh.l1)
+        self.dense_views = [backend.view(self.dense_grad, off, n) for _, off, n in self.dense_layout]
+        self._t_ft_grad = backend.tensor(self.ft_grad)
+        self._t_l0w = backend.tensor(self.weights[0])
+        self._t_dense = backend.tensor(self.dense_grad)
+
+    def upload_batch(self, stm, nstm, targets, entry_weights) -> None:
+        self.stm_indices.upload(stm)
+        self.nstm_indices.upload(nstm)
+        self.targets.upload(targets)
+        self.entry_weights.upload(entry_weights)
+
+    def exchange_and_update(self, params: RangerUpdateParams) -> None:
+        lay, sh = self.layout, self.shape
+        chunk = lay.shard_rows * sh.l1
+        shard_t = self._t_ft_grad[self.rank * chunk:(self.rank + 1) * chunk]
+        self.dist.reduce_scatter_tensor(shard_t, self._t_ft_grad)
+        self.dist.all_reduce(self._t_dense)
+        if lay.real_rows > 0:
+            m, v, slow = self.ft_state
+            self.backend.ranger(params, self.ft_grad_shard, self.l0w_shard, m, v, slow)
+        for view, w, (m, v, slow) in zip(self.dense_views, self.weights[1:], self.small_state):
+            self.backend.ranger(params, view, w, m, v, slow)
+        own_t = self._t_l0w[self.rank * chunk:(self.rank + 1) * chunk]
+        self.dist.all_gather_into_tensor(self._t_l0w, own_t)
+
+    def step_device(self, params: RangerUpdateParams, loss_kind: ScalarLossKind, output_inv_scale: float,
+                    finalize_loss: bool = True) -> None:
+        spec = loss_kind.spec(output_inv_scale, finalize_loss, normalizer=self.batch_size * self.world)
+        self.backend.local_gradients(self, spec)
+        self.exchange_and_update(params)
+
+    def read_weights(self) -> dict:
+        out = {n: self.backend.download(w) for n, w in zip(NNUE_WEIGHT_NAMES, self.weights)}
+        out["l0w"] = out["l0w"][: self.shape.input_size * self.shape.l1]
+        return out
+
+
+def run_data_parallel_bench(args, rank: int, world: int, local: int, dist):
+    """bench.py's N>1 arm: weak scaling, args.batch positions per rank."""
+    import time
+
+    import torch
+
+    import bench
+    import bulletou_b200 as bo
+    from bulletou_b200 import synthetic
+    from bulletou_b200.cuda_cpp import PinnedF32Buffer, PinnedI32Buffer
+
+    backend = B200Backend(local)
+    w = synthetic.halfkp_weights(synthetic.rng_for(7))
+    tr = NnueDataParallelTrainer(backend, dist, bo.NnueForwardHostWeights(bo.NnueForwardShape(*bench.SHAPE), **w),
+                                 args.batch, bench.ACTIVE)
+    batches = bench.make_batches(args.batch, rank)
+    dev = bench.device_batches(backend.ctx, batches)
+    loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
+    inv = 1.0 / 600.0
+    step = 0
+
+    def bind(i):
+        tr.stm_indices, tr.nstm_indices, tr.targets, tr.entry_weights = dev[i % len(dev)]
+
+    for i in range(args.warmup):
+        step += 1
+        bind(i)
+        tr.step_device(bench.ranger(step), loss_kind, inv, finalize_loss=False)
+    torch.cuda.synchronize()
+    dist.barrier()
+    lib, ctx = backend.lib, backend.ctx
+    start, stop = bo.Event(ctx), bo.Event(ctx)
+    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 8 * args.steps + 8)
+    with bench.ClockSampler(local) as clocks:
+        start.record(ctx)
+        for i in range(args.steps):
+            step += 1
+            bind(i)
+            tr.step_device(bench.ranger(step), loss_kind, inv, finalize_loss=False)
+        stop.record(ctx)
+        stop.synchronize()
+    ms = (ctypes.c_float * 8)()
+    nsteps, nphases = ctypes.c_size_t(), ctypes.c_size_t()
+    lib.call("bulletou_b200_profile_end", ctx.as_ptr(), ms, 8, ctypes.byref(nsteps), ctypes.byref(nphases))
+    torch.cuda.synchronize()
+    dist.barrier()
+    total_ms = bench.max_over_ranks(dist, stop.elapsed_ms_since(start))
+    phase_ms = {bench.PHASES[p]: ms[p] / max(1, nsteps.value) for p in range(nphases.value)}
+    # end to end: per step H2D from pinned host memory, step, D2H of the mean loss
+    pins = []
+    for b in batches:
+        p = (PinnedI32Buffer(ctx, b["stm"].size), PinnedI32Buffer(ctx, b["nstm"].size),
+             PinnedF32Buffer(ctx, args.batch), PinnedF32Buffer(ctx, args.batch))
+        for dst, src in zip(p, (b["stm"], b["nstm"], b["targets"], b["entry_weights"])):
+            np.copyto(dst.host(), src)
+        pins.append(p)
+    in_bufs = (I32Buffer(ctx, args.batch * bench.ACTIVE), I32Buffer(ctx, args.batch * bench.ACTIVE),
+               F32Buffer(ctx, args.batch), F32Buffer(ctx, args.batch))
+    tr.stm_indices, tr.nstm_indices, tr.targets, tr.entry_weights = in_bufs
+    e2e_steps = max(8, args.steps)
+    ring = [PinnedF32Buffer(ctx, 1) for _ in range(e2e_steps)]
+    dist.barrier()
+    e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    t0 = time.perf_counter()
+    e0.record(ctx)
+    h2d = 0
+    for i in range(e2e_steps):
+        step += 1
+        p = pins[i % len(pins)]
+        c = ctx.as_ptr()
+        lib.call("bulletou_b200_i32_upload_pinned", c, in_bufs[0].as_ptr(), p[0].as_ptr(), p[0].length)
+        lib.call("bulletou_b200_i32_upload_pinned", c, in_bufs[1].as_ptr(), p[1].as_ptr(), p[1].length)
+        lib.call("bulletou_b200_f32_upload_pinned", c, in_bufs[2].as_ptr(), p[2].as_ptr(), p[2].length)
+        lib.call("bulletou_b200_f32_upload_pinned", c, in_bufs[3].as_ptr(), p[3].as_ptr(), p[3].length)
+        h2d = 4 * sum(x.length for x in p)
+        tr.step_device(bench.ranger(step), loss_kind, inv, finalize_loss=True)
+        lib.call("bulletou_b200_f32_download_pinned", c, ring[i].as_ptr(), tr.loss_workspace.mean.as_ptr(), 1)
+    e1.record(ctx)
+    e1.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1000.0
+    e2e_ms = bench.max_over_ranks(dist, max(e1.elapsed_ms_since(e0), wall_ms))
+    losses = [float(r.host()[0]) for r in ring]
+    assert all(np.isfinite(losses)), "non-finite loss"
+    return {"total_ms": total_ms, "phase_ms": phase_ms, "clocks": clocks.summary(),
+            "e2e": {"value": e2e_steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
+                    "path": "NnueDataParallelTrainer.step_device per rank (NCCL reduce-scatter / all-reduce / "
+                            "all-gather), inputs from pinned host memory, mean loss copied D2H every step"},
+            "gpu_launches": (bench.LAUNCHES_PER_STEP + 8) * args.steps,
+            "final_loss": losses[-1]}

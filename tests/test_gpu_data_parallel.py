@@ -1,0 +1,90 @@
+"""GPU (>= 2 devices, NCCL): two ranks of data-parallel HalfKP training on half
+batches reproduce one single-GPU fused step on the whole batch.  Skipped on a
+single GPU."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+BATCH = 2048  # per rank
+STEPS = 7
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _batches():
+    from bulletou_b200 import synthetic
+
+    return [synthetic.halfkp_batch(700 + i, 2 * BATCH) for i in range(STEPS)]
+
+
+def _params(step):
+    import bulletou_b200 as bo
+
+    return bo.RangerUpdateParams(radam=bo.RAdamUpdateParams(step=step, learning_rate=1e-3))
+
+
+def _rank_main(rank, world, port, out_path):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import bulletou_b200 as bo
+    from bulletou_b200 import synthetic
+    from bulletou_b200.data_parallel import B200Backend, NnueDataParallelTrainer
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        w = synthetic.halfkp_weights(synthetic.rng_for(17))
+        tr = NnueDataParallelTrainer(B200Backend(rank), dist,
+                                     bo.NnueForwardHostWeights(bo.NNUE_HALFKP_256X2_32_32, **w), BATCH, 38)
+        for step, b in enumerate(_batches(), start=1):
+            sl = slice(rank * BATCH * 38, (rank + 1) * BATCH * 38)
+            bs = slice(rank * BATCH, (rank + 1) * BATCH)
+            tr.upload_batch(b["stm"][sl], b["nstm"][sl], b["targets"][bs], b["entry_weights"][bs])
+            tr.step_device(_params(step), bo.ScalarLossKind.SigmoidPow(2.0), 1 / 600)
+        torch.cuda.synchronize()
+        got = tr.read_weights()
+        if rank == 0:
+            np.savez(out_path, **got)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+def test_two_gpu_data_parallel_matches_single_gpu_global_batch(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "rank0.npz"
+    mp.start_processes(_rank_main, args=(2, _free_port(), str(out)), nprocs=2, start_method="spawn")
+    got = np.load(out)
+
+    import bulletou_b200 as bo
+    from bulletou_b200 import synthetic
+
+    w = synthetic.halfkp_weights(synthetic.rng_for(17))
+    ctx = bo.Context(0)
+    runner = bo.NnueTrainStepRunner(ctx, bo.NnueForwardHostWeights(bo.NNUE_HALFKP_256X2_32_32, **w), 2 * BATCH, 38)
+    for step, b in enumerate(_batches(), start=1):
+        hb = bo.NnueTrainStepHostBatch(b["stm"], b["nstm"], b["targets"], b["entry_weights"], 2 * BATCH, 38)
+        runner.step_no_readback(ctx, _params(step), bo.ScalarLossKind.SigmoidPow(2.0), 1 / 600, hb)
+    ref = runner.read_weights(ctx)
+    for k, v in ref.items():
+        scale = max(float(np.abs(v).max()), 1e-30)
+        err = float(np.abs(got[k].astype(np.float64) - v).max())
+        assert err <= 1e-4 * scale, f"{k}: max |diff| {err:.3e} (scale {scale:.3e})"
