@@ -28,4 +28,13 @@ from .cuda_cpp import (  # noqa: F401
     scalar_loss_host,
 )
 
+from .sfnn import (  # noqa: F401
+    SFNN_HALFKA_HM2_1536_15_32_K3K3,
+    SfnnFactorizerAlpha,
+    SfnnForwardHostWeights,
+    SfnnForwardShape,
+    SfnnTrainStepHostBatch,
+    SfnnTrainStepRunner,
+)
+
 __version__ = "0.1.0"

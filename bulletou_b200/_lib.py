@@ -42,6 +42,13 @@ class RangerStep(ctypes.Structure):
     ]
 
 
+class SfnnShape(ctypes.Structure):
+    """BulletOuB200SfnnShape."""
+
+    _fields_ = [("input_size", Z), ("ft_size", Z), ("l1_hidden", Z), ("l1_skip", I), ("l2_size", Z),
+                ("num_stacks", Z), ("ft_factorizer_alpha", F), ("factorizer_shared_alpha", F)]
+
+
 class LossSpec(ctypes.Structure):
     """BulletOuB200LossSpec."""
 
@@ -121,6 +128,14 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_nnue_dense_gradient_len": [Z, Z, Z, P],
     "bulletou_b200_nnue_local_gradients_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P],
     "bulletou_b200_kppt_train_step_device": [P, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P],
+    # SFNN (cu:11329, cu:12882) and the fused SFNN step
+    "bulletou_cuda_cpp_sfnn_forward_device": (
+        [P, Z, Z, Z, I] + [Z] * 9 + [P] * 10 + [I] + [P] * 2 + [I] + [P] * 4 + [I] + [P] * 2 + [I] + [P] * 4 + [I]
+        + [P] * 2 + [I] + [I] * 6 + [F] * 6 + [P] * 2 + [P] * 7 + [P] * 2 + [I]),
+    "bulletou_cuda_cpp_sfnn_backward_train_device": (
+        [P, Z, Z, Z, I] + [Z] * 9 + [P] * 12 + [I] + [P] + [I] + [P] * 2 + [I] + [P] + [I] + [P] * 2 + [I] + [P]
+        + [I] + [I] * 6 + [F] * 6 + [P] * 2 + [P] + [P] * 8 + [P] * 20 + [I] + [P]),
+    "bulletou_b200_sfnn_train_step_device": [P, P, Z, Z] + [P] * 16,
 }
 
 

@@ -34,7 +34,7 @@ struct BulletOuCudaCppContext {
     bool owns_stream = true;
     int sm_count = 148;
     // Named scratch slots; see scratch_slot in runtime.cu.
-    bou::Scratch scratch[16];
+    bou::Scratch scratch[24];
     // Stage profiler (bulletou_b200_profile_*): events recorded on `stream`
     // at phase boundaries of the fused steps, read back after the run.
     bool prof_on = false;
@@ -97,6 +97,12 @@ enum ScratchSlot : int {
     kScratchHost = 11,
     kScratchActivations = 12,
     kScratchKingSort = 13,
+    kScratchSfnnFold = 14,      // folded FT table
+    kScratchSfnnStep = 15,      // SFNN per-step activations / gradients
+    kScratchSfnnSort = 16,      // SFNN king + bucket sort, tile table
+    kScratchSfnnPartials = 17,  // SFNN per-tile partial sums
+    kScratchSfnnGrads = 18,     // SFNN packed small-parameter gradients
+    kScratchSfnnEff = 19,       // SFNN effective (shared-factor folded) dense weights
 };
 
 int ok();

@@ -26,6 +26,7 @@
 #include <mutex>
 
 #include "halfkp_fast.cuh"
+#include "king_sort.cuh"
 
 namespace bou {
 
@@ -33,7 +34,7 @@ namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kKingKeys = 82;  // 81 kings + one bucket for perspectives without a valid feature
-constexpr int kPiecesPerKing = 1548;
+constexpr int kHalfkpPieces = 1548;
 constexpr int kGatherWarps = 8;
 template <int L1>
 __host__ __device__ constexpr int dense_warps() { return L1 == 256 ? 16 : 8; }  // l1w in smem: 74 KB (256) / 147 KB (512)
@@ -44,99 +45,6 @@ constexpr int kReduceChunk = 128;
 
 __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
 __device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f && a < 1.0f ? g : 0.0f; }
-
-// ------------------------------------------------------------------ king sort
-// Stable counting sort of half-positions h = 2*sample + perspective by king.
-// Three deterministic passes (no global atomics): per-block key histograms,
-// per-key bases over blocks, and an ordered scatter (within a bucket, h ascending).
-constexpr int kSortThreads = 256;
-constexpr int kSortWarps = kSortThreads / 32;
-
-__device__ __forceinline__ int half_position_key(const int* __restrict__ stm, const int* __restrict__ nstm, int h, int A,
-                                                 int input_size) {
-    const int* idx = ((h & 1) ? nstm : stm) + static_cast<size_t>(h >> 1) * A;
-    for (int s = 0; s < A; ++s) {
-        const int f = __ldg(idx + s);
-        if (f >= 0 && f < input_size) return min(f / kPiecesPerKing, kKingKeys - 1);
-    }
-    return kKingKeys - 1;
-}
-
-__global__ void __launch_bounds__(kSortThreads) king_hist_kernel(const int* __restrict__ stm,
-                                                                 const int* __restrict__ nstm, int n_half, int A,
-                                                                 int input_size, int* __restrict__ keys,
-                                                                 int* __restrict__ block_hist) {
-    __shared__ int hist[kKingKeys];
-    for (int i = threadIdx.x; i < kKingKeys; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
-    const int h = blockIdx.x * kSortThreads + threadIdx.x;
-    if (h < n_half) {
-        const int key = half_position_key(stm, nstm, h, A, input_size);
-        keys[h] = key;
-        atomicAdd(&hist[key], 1);  // counts only: order-independent
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < kKingKeys; i += blockDim.x) block_hist[blockIdx.x * kKingKeys + i] = hist[i];
-}
-
-// One CTA: king_off[k] = first slot of bucket k (king_off[82] = n_half); block_hist
-// becomes, per (block, key), the first slot of that block's items of that key.
-__global__ void __launch_bounds__(128) king_bases_kernel(int* __restrict__ block_hist, int nblocks,
-                                                         int* __restrict__ king_off) {
-    __shared__ int total[kKingKeys];
-    const int k = threadIdx.x;
-    if (k < kKingKeys) {
-        int s = 0;
-#pragma unroll 8
-        for (int b = 0; b < nblocks; ++b) s += block_hist[b * kKingKeys + k];
-        total[k] = s;
-    }
-    __syncthreads();
-    if (k == 0) {
-        int run = 0;
-        for (int i = 0; i < kKingKeys; ++i) {
-            const int t = total[i];
-            total[i] = run;
-            run += t;
-        }
-        king_off[kKingKeys] = run;
-    }
-    __syncthreads();
-    if (k < kKingKeys) {
-        int run = total[k];
-        king_off[k] = run;
-#pragma unroll 8
-        for (int b = 0; b < nblocks; ++b) {
-            const int c = block_hist[b * kKingKeys + k];
-            block_hist[b * kKingKeys + k] = run;
-            run += c;
-        }
-    }
-}
-
-__global__ void __launch_bounds__(kSortThreads) king_scatter_kernel(const int* __restrict__ keys, int n_half,
-                                                                    const int* __restrict__ block_base,
-                                                                    int* __restrict__ order, int* __restrict__ slot_of,
-                                                                    const int* __restrict__ king_off) {
-    __shared__ int wcount[kSortWarps][kKingKeys];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < kSortWarps * kKingKeys; i += blockDim.x) (&wcount[0][0])[i] = 0;
-    __syncthreads();
-    const int h = blockIdx.x * kSortThreads + threadIdx.x;
-    const bool valid = h < n_half;
-    const int key = valid ? keys[h] : -1;
-    const unsigned peers = __match_any_sync(0xffffffffu, key);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    if (valid && rank == 0) wcount[warp][key] = __popc(peers);
-    __syncthreads();
-    if (valid) {
-        int before = 0;
-        for (int w = 0; w < warp; ++w) before += wcount[w][key];
-        const int pos = block_base[blockIdx.x * kKingKeys + key] + before + rank;
-        order[pos] = h;
-        if (slot_of != nullptr) slot_of[h] = pos - king_off[key];
-    }
-}
 
 // ------------------------------------------------------------------ gather
 template <int Q>
@@ -657,21 +565,14 @@ int halfkp_fast_forward_backward(BulletOuCudaCppContext* ctx, const HalfkpDims& 
                                  const float* targets, const float* entry_weights, const LossArgs* loss,
                                  float* stm_l0, float* nstm_l0) {
     const int n_half = 2 * d.batch;
-    const int nblocks = (n_half + kSortThreads - 1) / kSortThreads;
-    // king sort scratch (fixed layout at the slot's start):
-    // king_off [83] | keys [2B] | order [2B] | block_hist [nblocks x 82]
     void* sort_mem = nullptr;
-    const size_t sort_ints = kKingKeys + 1 + 2 * static_cast<size_t>(n_half) + static_cast<size_t>(nblocks) * kKingKeys;
+    const size_t sort_ints = king_sort_scratch_ints<kKingKeys>(n_half);
     if (scratch_slot(ctx, kScratchKingSort, sort_ints * sizeof(int), &sort_mem, "cudaMalloc king sort") != 0) return -1;
-    int* king_off = static_cast<int*>(sort_mem);
-    int* keys = king_off + kKingKeys + 1;
-    int* order = keys + n_half;
-    int* block_hist = order + n_half;
-    king_hist_kernel<<<nblocks, kSortThreads, 0, ctx->stream>>>(stm, nstm, n_half, d.max_active, d.input_size, keys,
-                                                               block_hist);
-    king_bases_kernel<<<1, 128, 0, ctx->stream>>>(block_hist, nblocks, king_off);
-    king_scatter_kernel<<<nblocks, kSortThreads, 0, ctx->stream>>>(keys, n_half, block_hist, order, nullptr, king_off);
-    if (check_launch("king sort launch") != 0) return -1;
+    KingSortOut sorted{};
+    if (king_sort<kKingKeys>(ctx, stm, nstm, n_half, KingKey{kHalfkpPieces, d.input_size, d.max_active},
+                             static_cast<int*>(sort_mem), nullptr, &sorted) != 0)
+        return -1;
+    const int* order = sorted.order;
     prof_mark(ctx);
     const int rc = d.l1 == 256 ? launch_gather<1>(ctx, order, n_half, stm, nstm, d.max_active, map, w.l0w, w.l0b,
                                                   a.act, stm_l0, nstm_l0)
@@ -735,9 +636,7 @@ namespace {
 
 constexpr int kNoAllocMaxBatch = 65536;
 constexpr int kNoAllocMaxHalf = 2 * kNoAllocMaxBatch;
-constexpr int kNoAllocMaxBlocks = (kNoAllocMaxHalf + kSortThreads - 1) / kSortThreads;
-constexpr size_t kNoAllocInts =
-    (kKingKeys + 1) + 2 * static_cast<size_t>(kNoAllocMaxHalf) + static_cast<size_t>(kNoAllocMaxBlocks) * kKingKeys;
+constexpr size_t kNoAllocInts = king_sort_scratch_ints<kKingKeys>(kNoAllocMaxHalf);
 constexpr int kNoAllocMaxDevices = 64;
 
 __device__ __align__(256) int g_noalloc_king_scratch[kNoAllocInts];
@@ -800,16 +699,11 @@ extern "C" int bulletou_b200_nnue_forward_device_noalloc(
                        static_cast<int>(max_active)};
     const RowMap map = make_row_map(input_size);
     const int n_half = 2 * d.batch;
-    const int nblocks = (n_half + kSortThreads - 1) / kSortThreads;
-    int* king_off = scratch;
-    int* keys = king_off + kKingKeys + 1;
-    int* order = keys + n_half;
-    int* block_hist = order + n_half;
-    king_hist_kernel<<<nblocks, kSortThreads, 0, ctx->stream>>>(stm_indices->ptr, nstm_indices->ptr, n_half,
-                                                               d.max_active, d.input_size, keys, block_hist);
-    king_bases_kernel<<<1, 128, 0, ctx->stream>>>(block_hist, nblocks, king_off);
-    king_scatter_kernel<<<nblocks, kSortThreads, 0, ctx->stream>>>(keys, n_half, block_hist, order, nullptr, king_off);
-    if (check_launch("no-allocation king sort launch") != 0) return -1;
+    KingSortOut sorted{};
+    if (king_sort<kKingKeys>(ctx, stm_indices->ptr, nstm_indices->ptr, n_half,
+                             KingKey{kHalfkpPieces, d.input_size, d.max_active}, scratch, nullptr, &sorted) != 0)
+        return -1;
+    const int* order = sorted.order;
     const int rc = d.l1 == 256 ? launch_gather<1>(ctx, order, n_half, stm_indices->ptr, nstm_indices->ptr,
                                                   d.max_active, map, l0w->ptr, l0b->ptr, combined->ptr, stm_l0->ptr,
                                                   nstm_l0->ptr)

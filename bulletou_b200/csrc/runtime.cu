@@ -86,7 +86,8 @@ int validate_host(const void* ptr, size_t len, const char* name) {
 }
 
 int scratch_slot(BulletOuCudaCppContext* ctx, int slot, size_t bytes, void** out, const char* label) {
-    if (slot < 0 || slot >= 16) return fail_message("internal: scratch slot out of range");
+    if (slot < 0 || slot >= static_cast<int>(sizeof(ctx->scratch) / sizeof(ctx->scratch[0])))
+        return fail_message("internal: scratch slot out of range");
     Scratch& s = ctx->scratch[slot];
     if (bytes == 0) bytes = 256;
     if (s.bytes < bytes) {

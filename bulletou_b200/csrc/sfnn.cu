@@ -1,0 +1,1813 @@
+// SFNN LayerStack training and inference path for B200 (see sfnn.cuh for the
+// network and the reference lines each stage restates).
+//
+// One training step, every stage a kernel on the context stream:
+//   1. fold        -- factorized FT: folded[f] = l0w[f] + alpha * l0w[base + f % 1629]
+//                     (cu:1445-1456), so the gather reads one row per feature.
+//   2. sorts       -- the 2B half-positions (sample, perspective) by king
+//                     (a king's 1629 rows = 9.4 MB at width 1536, L2-resident while
+//                     its half-positions are gathered) and the B samples by
+//                     LayerStack bucket, cut into tiles of <= 128 samples of one bucket.
+//   3. FT forward  -- one warp per half-position in king order; 128-bit loads,
+//                     bias + rows in slot order (the reference's sum), ClippedReLU,
+//                     pairwise product * 127/128 (cu:1227-1320).
+//   4. L1 forward  -- per bucket tile; the tile's effective L1 weights
+//                     (bucket rows + alpha * shared factor, cu:2297-2303) in shared memory.
+//   5. head        -- per bucket tile, thread per sample: L2 input (SqrCReLU | CReLU),
+//                     L2 + CReLU, L3 + PSQT skip, the loss, and the backward through
+//                     L3 / L2 / L2 input to the L1 output gradient; per-tile partial
+//                     sums of the L2 / L3 / L1-bias gradients.
+//   6. L1 backward -- per (bucket tile, 256 columns): combined gradient, the FT
+//                     pre-activation gradients of both pair members, per-tile partial
+//                     sums of dL1w and of the FT bias gradient.  The pre-activation
+//                     gradients are written in king order.
+//   7. finalize    -- partial sums reduced in tile order (deterministic), shared-factor
+//                     gradients, loss sum; Ranger on the small groups.
+//   8. FT rows     -- one warp per (piece, column group): for the piece's row in every
+//                     king block, the row's gradient is summed from the inverse index
+//                     (ascending entry order) and Ranger updates the row in the same
+//                     pass; the virtual (factor) row of the piece receives
+//                     alpha * sum over kings (cu:4950-4985) and is updated last.
+//                     The FT gradient table is never written.
+#include <algorithm>
+#include <cfloat>
+#include <climits>
+#include <cstring>
+
+#include "king_sort.cuh"
+#include "sfnn.cuh"
+#include "sparse_rows.cuh"
+
+namespace bou {
+int launch_ranger(BulletOuCudaCppContext* ctx, size_t len, const RangerArgs& a, float* gradients, float* weights,
+                  float* momentum, float* velocity, float* slow);
+int loss_args(const BulletOuB200LossSpec* loss, size_t batch, LossArgs* out);
+}  // namespace bou
+
+namespace bou {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr float kPairScale = 127.0f / 128.0f;  // SFNN_PAIRWISE_SCALE, cu:1148
+constexpr int kBucketKeys = kSfnnMaxStacks + 1;
+constexpr int kPieceRowWarps = 8;
+constexpr int kPieceSortCap = 512;
+
+__device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
+__device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f && a < 1.0f ? g : 0.0f; }
+
+// ------------------------------------------------------------------ fold
+__global__ void fold_ft4_kernel(const float4* __restrict__ l0w, float4* __restrict__ folded, size_t total4, int w4,
+                                int base, float alpha) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= total4) return;
+    const size_t f = t / w4;
+    const size_t q = t - f * w4;
+    const float4 a = l0w[t];
+    const float4 v = l0w[(static_cast<size_t>(base) + f % kSfnnPieces) * w4 + q];
+    folded[t] = make_float4(fmaf(alpha, v.x, a.x), fmaf(alpha, v.y, a.y), fmaf(alpha, v.z, a.z), fmaf(alpha, v.w, a.w));
+}
+
+__global__ void fold_ft1_kernel(const float* __restrict__ l0w, float* __restrict__ folded, size_t total, int width,
+                                int base, float alpha) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= total) return;
+    const size_t f = t / width;
+    const size_t j = t - f * width;
+    folded[t] = fmaf(alpha, l0w[(static_cast<size_t>(base) + f % kSfnnPieces) * width + j], l0w[t]);
+}
+
+// ------------------------------------------------------------------ bucket sort + tiles
+__global__ void __launch_bounds__(kKingSortThreads) bucket_hist_kernel(const int* __restrict__ buckets, int n,
+                                                                       int stacks, int* __restrict__ keys,
+                                                                       int* __restrict__ block_hist) {
+    __shared__ int hist[kBucketKeys];
+    for (int i = threadIdx.x; i < kBucketKeys; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const int b = blockIdx.x * kKingSortThreads + threadIdx.x;
+    if (b < n) {
+        const int s = buckets[b];
+        const int key = (s >= 0 && s < stacks) ? s : stacks;
+        keys[b] = key;
+        atomicAdd(&hist[key], 1);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kBucketKeys; i += blockDim.x) block_hist[blockIdx.x * kBucketKeys + i] = hist[i];
+}
+
+// One CTA.  Keys 0..stacks (the last one holds samples with an invalid
+// bucket) are cut into tiles of at most kSfnnTile consecutive sorted samples.
+__global__ void __launch_bounds__(128) tile_table_kernel(const int* __restrict__ key_off, int keys,
+                                                         int* __restrict__ n_tiles, int* __restrict__ tile_key,
+                                                         int* __restrict__ tile_begin, int* __restrict__ tile_end,
+                                                         int* __restrict__ key_first) {
+    __shared__ int first[kBucketKeys + 1];
+    const int k = threadIdx.x;
+    int cnt = 0;
+    if (k < keys) cnt = (key_off[k + 1] - key_off[k] + kSfnnTile - 1) / kSfnnTile;
+    if (k < keys) first[k + 1] = cnt;
+    __syncthreads();
+    if (k == 0) {
+        first[0] = 0;
+        for (int i = 1; i <= keys; ++i) first[i] += first[i - 1];
+        *n_tiles = first[keys];
+    }
+    __syncthreads();
+    if (k <= keys) key_first[k] = first[k];
+    if (k < keys) {
+        const int b0 = key_off[k], b1 = key_off[k + 1];
+        for (int i = 0; i < cnt; ++i) {
+            const int t = first[k] + i;
+            tile_key[t] = k;
+            tile_begin[t] = b0 + i * kSfnnTile;
+            tile_end[t] = min(b1, b0 + (i + 1) * kSfnnTile);
+        }
+    }
+}
+
+struct Tiles {
+    const int* order;      // samples in bucket order
+    const int* n_tiles;    // device scalar
+    const int* key;        // bucket of each tile (== stacks: invalid-bucket samples)
+    const int* begin;
+    const int* end;
+    const int* key_first;  // first tile of each key, [stacks + 2]
+    int max_tiles;
+};
+
+// ------------------------------------------------------------------ FT forward
+struct FtArgs {
+    const int* order;  // king order of half-positions (null: h = position)
+    const int* stm;
+    const int* nstm;
+    const float* table;  // [n_features][width], folded when factorized
+    const float* bias;
+    float* l0[2];        // ClippedReLU output per perspective, [B][width]
+    float* combined;     // [B][width]
+    int n_half;
+    int max_active;
+    int n_features;
+    int width;
+};
+
+// One warp per half-position; lane owns float4 chunks lane + 32 i, so chunk i
+// and chunk i + NCH/2 are the two members of a pair (width / 2 apart).
+template <int NCH>
+__global__ void __launch_bounds__(256) ft_forward_kernel(FtArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int pos = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pos >= a.n_half) return;
+    const int h = a.order != nullptr ? a.order[pos] : pos;
+    const int b = h >> 1, v = h & 1;
+    const int* idx = (v ? a.nstm : a.stm) + static_cast<size_t>(b) * a.max_active;
+    const float4* bias4 = reinterpret_cast<const float4*>(a.bias);
+    float4 acc[NCH];
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) acc[i] = __ldg(bias4 + lane + 32 * i);
+    const size_t w4 = static_cast<size_t>(a.width) >> 2;
+    for (int s0 = 0; s0 < a.max_active; s0 += 32) {
+        const int mine = s0 + lane < a.max_active ? __ldg(idx + s0 + lane) : -1;
+        const int n = min(32, a.max_active - s0);
+        for (int u = 0; u < n; ++u) {
+            const int f = __shfl_sync(kFull, mine, u);
+            if (f < 0 || f >= a.n_features) continue;
+            const float4* row = reinterpret_cast<const float4*>(a.table) + static_cast<size_t>(f) * w4;
+            float4 r[NCH];
+#pragma unroll
+            for (int i = 0; i < NCH; ++i) r[i] = __ldg(row + lane + 32 * i);
+#pragma unroll
+            for (int i = 0; i < NCH; ++i) {
+                acc[i].x += r[i].x;
+                acc[i].y += r[i].y;
+                acc[i].z += r[i].z;
+                acc[i].w += r[i].w;
+            }
+        }
+    }
+    float4* out = reinterpret_cast<float4*>(a.l0[v]) + static_cast<size_t>(b) * w4;
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+        acc[i] = make_float4(crelu01(acc[i].x), crelu01(acc[i].y), crelu01(acc[i].z), crelu01(acc[i].w));
+        out[lane + 32 * i] = acc[i];
+    }
+    float4* comb = reinterpret_cast<float4*>(a.combined) + static_cast<size_t>(b) * w4 + v * (w4 >> 1);
+#pragma unroll
+    for (int i = 0; i < NCH / 2; ++i) {
+        const float4 x0 = acc[i], x1 = acc[i + NCH / 2];
+        comb[lane + 32 * i] = make_float4(x0.x * x1.x * kPairScale, x0.y * x1.y * kPairScale,
+                                          x0.z * x1.z * kPairScale, x0.w * x1.w * kPairScale);
+    }
+}
+
+// Any even width: one thread per (half-position, pair).
+__global__ void ft_forward_generic_kernel(FtArgs a) {
+    const int half = a.width / 2;
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= static_cast<size_t>(a.n_half) * half) return;
+    const int h = static_cast<int>(t / half);
+    const int j = static_cast<int>(t - static_cast<size_t>(h) * half);
+    const int b = h >> 1, v = h & 1;
+    const int* idx = (v ? a.nstm : a.stm) + static_cast<size_t>(b) * a.max_active;
+    float s0 = a.bias[j], s1 = a.bias[j + half];
+    for (int s = 0; s < a.max_active; ++s) {
+        const int f = idx[s];
+        if (f < 0 || f >= a.n_features) continue;
+        const float* row = a.table + static_cast<size_t>(f) * a.width;
+        s0 += row[j];
+        s1 += row[j + half];
+    }
+    const float x0 = crelu01(s0), x1 = crelu01(s1);
+    float* out = a.l0[v] + static_cast<size_t>(b) * a.width;
+    out[j] = x0;
+    out[j + half] = x1;
+    a.combined[static_cast<size_t>(b) * a.width + v * half + j] = x0 * x1 * kPairScale;
+}
+
+// ------------------------------------------------------------------ L1
+// Effective L1 weights, input-major [stacks][width][l1_out]:
+// l1w[s][o][i] + alpha * l1fw[i][o]  (cu:2297-2303).
+__global__ void l1_eff_kernel(const float* __restrict__ l1w, const float* __restrict__ l1fw, float alpha, int stacks,
+                              int out_dim, int width, float* __restrict__ w_eff) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const size_t per = static_cast<size_t>(width) * out_dim;
+    if (t >= per * stacks) return;
+    const size_t s = t / per;
+    const size_t r = t - s * per;
+    const size_t i = r / out_dim;
+    const size_t o = r - i * out_dim;
+    float w = l1w[(s * out_dim + o) * width + i];
+    if (l1fw != nullptr) w = fmaf(alpha, l1fw[i * out_dim + o], w);
+    w_eff[t] = w;
+}
+
+struct L1Args {
+    Tiles tiles;
+    const float* combined;
+    const float* w_eff;  // [stacks][width][O]
+    const float* l1b;
+    const float* l1fb;   // null without the shared factor
+    float alpha;
+    float* l1;           // [B][O]
+    int width;
+    int out_dim;
+    int stacks;
+};
+
+// Bias terms are added after the dot product, bucket bias first, as the
+// reference does (cu:2318-2322).
+__device__ __forceinline__ float l1_bias(const L1Args& a, int s, int o, float dot) {
+    float r = dot + a.l1b[s * a.out_dim + o];
+    if (a.l1fb != nullptr) r = fmaf(a.alpha, a.l1fb[o], r);
+    return r;
+}
+
+// O = 16: thread (sample lane, output quad); the tile's effective weights in
+// shared memory as [width][16], read as float4 (conflict-free).
+__global__ void __launch_bounds__(256) l1_forward16_kernel(L1Args a) {
+    extern __shared__ float4 ws4[];
+    const int t = blockIdx.x;
+    if (t >= *a.tiles.n_tiles) return;
+    const int s = a.tiles.key[t];
+    const int pb = a.tiles.begin[t], pe = a.tiles.end[t];
+    if (s >= a.stacks) {
+        for (int i = threadIdx.x; i < (pe - pb) * 16; i += blockDim.x)
+            a.l1[static_cast<size_t>(a.tiles.order[pb + i / 16]) * 16 + (i & 15)] = 0.0f;
+        return;
+    }
+    const float4* src = reinterpret_cast<const float4*>(a.w_eff + static_cast<size_t>(s) * a.width * 16);
+    for (int i = threadIdx.x; i < a.width * 4; i += blockDim.x) ws4[i] = src[i];
+    __syncthreads();
+    const int og = threadIdx.x & 3;
+    const int w4 = a.width >> 2;
+    for (int p = pb + (threadIdx.x >> 2); p < pe; p += 64) {
+        const int b = a.tiles.order[p];
+        const float4* c4 = reinterpret_cast<const float4*>(a.combined) + static_cast<size_t>(b) * w4;
+        float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+        for (int k4 = 0; k4 < w4; ++k4) {
+            const float4 c = __ldg(c4 + k4);
+            const float cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const float4 w = ws4[(4 * k4 + kk) * 4 + og];
+                acc0 = fmaf(cv[kk], w.x, acc0);
+                acc1 = fmaf(cv[kk], w.y, acc1);
+                acc2 = fmaf(cv[kk], w.z, acc2);
+                acc3 = fmaf(cv[kk], w.w, acc3);
+            }
+        }
+        float* out = a.l1 + static_cast<size_t>(b) * 16 + 4 * og;
+        out[0] = l1_bias(a, s, 4 * og + 0, acc0);
+        out[1] = l1_bias(a, s, 4 * og + 1, acc1);
+        out[2] = l1_bias(a, s, 4 * og + 2, acc2);
+        out[3] = l1_bias(a, s, 4 * og + 3, acc3);
+    }
+}
+
+// Any O / width: one thread per (sample, output) of the tile.
+__global__ void __launch_bounds__(256) l1_forward_generic_kernel(L1Args a) {
+    const int t = blockIdx.x;
+    if (t >= *a.tiles.n_tiles) return;
+    const int s = a.tiles.key[t];
+    const int pb = a.tiles.begin[t], pe = a.tiles.end[t];
+    const int O = a.out_dim;
+    for (int i = threadIdx.x; i < (pe - pb) * O; i += blockDim.x) {
+        const int b = a.tiles.order[pb + i / O];
+        const int o = i % O;
+        float* out = a.l1 + static_cast<size_t>(b) * O + o;
+        if (s >= a.stacks) {
+            *out = 0.0f;
+            continue;
+        }
+        const float* c = a.combined + static_cast<size_t>(b) * a.width;
+        const float* w = a.w_eff + static_cast<size_t>(s) * a.width * O + o;
+        float acc = 0.0f;
+        for (int k = 0; k < a.width; ++k) acc = fmaf(c[k], w[static_cast<size_t>(k) * O], acc);
+        *out = l1_bias(a, s, o, acc);
+    }
+}
+
+// ------------------------------------------------------------------ head
+enum HeadMode : int { kHeadForward = 0, kHeadTrain = 1, kHeadBackward = 2 };
+
+struct HeadArgs {
+    Tiles tiles;
+    const float* l1;
+    const float* l2w;
+    const float* l2b;   // null in the backward (biases are forward-only)
+    const float* l2fw;
+    const float* l2fb;
+    const float* l3w;
+    const float* l3b;
+    const float* l3fw;
+    const float* l3fb;
+    float alpha;
+    float* l2_input;  // [B][I2]   written (forward / train), read (backward)
+    float* l2;        // [B][L2]   written (forward / train), read (backward)
+    float* output;    // [B]
+    const float* targets;
+    const float* entry_weights;
+    LossArgs loss;
+    float* per_sample;
+    float* mog;       // written (train), read (backward)
+    float* g1;        // [B][O]
+    float* l2_gradients;        // optional [B][L2] (reference backward buffers)
+    float* l2_input_gradients;  // optional [B][I2]
+    float* partials;  // [max_tiles][head_partial_len]
+    int l1_hidden;
+    int l1_out;
+    int l1_skip;
+    int l2_size;
+    int stacks;
+    int mode;
+};
+
+__host__ __device__ inline int head_partial_len(int l2, int i2, int o) { return l2 * i2 + 2 * l2 + 1 + o + 1; }
+
+// Thread per sample (blockDim = kSfnnTile).  H / L2: compile-time dims, or 0
+// for runtime dims up to the kSfnnMax* bounds.
+template <int H, int L2>
+__global__ void __launch_bounds__(kSfnnTile) head_kernel(HeadArgs a) {
+    constexpr int kH = H > 0 ? H : (kSfnnMaxL1Out - 1);
+    constexpr int kL2 = L2 > 0 ? L2 : kSfnnMaxL2;
+    constexpr int kI2 = 2 * kH;
+    const int hdim = H > 0 ? H : a.l1_hidden;
+    const int l2n = L2 > 0 ? L2 : a.l2_size;
+    const int i2n = 2 * hdim;
+    const int O = a.l1_out;
+    extern __shared__ float sm[];
+    float* w2e = sm;                          // [l2n][i2n]
+    float* b2e = w2e + l2n * i2n;             // [l2n]
+    float* w3e = b2e + l2n;                   // [l2n]
+    float* b3e = w3e + l2n;                   // [1]
+    float* st_g2 = b3e + 1;                   // [T][l2n] masked L2 gradient
+    float* st_in = st_g2 + kSfnnTile * l2n;   // [T][i2n]
+    float* st_l2 = st_in + kSfnnTile * i2n;   // [T][l2n]
+    float* st_go = st_l2 + kSfnnTile * l2n;   // [T]
+    float* st_g1 = st_go + kSfnnTile;         // [T][O]
+    float* st_ls = st_g1 + kSfnnTile * O;     // [T]
+
+    const int t = blockIdx.x;
+    if (t >= *a.tiles.n_tiles) return;
+    const int s = a.tiles.key[t];
+    const bool valid = s < a.stacks;
+    const int pb = a.tiles.begin[t], pe = a.tiles.end[t];
+    if (valid) {
+        // Effective weights: bucket + alpha * shared (cu:2449-2552).
+        for (int i = threadIdx.x; i < l2n * i2n; i += blockDim.x) {
+            float w = a.l2w[static_cast<size_t>(s) * l2n * i2n + i];
+            if (a.l2fw != nullptr) w = fmaf(a.alpha, a.l2fw[i], w);
+            w2e[i] = w;
+        }
+        for (int o = threadIdx.x; o < l2n; o += blockDim.x) {
+            float b = a.l2b != nullptr ? a.l2b[s * l2n + o] : 0.0f;
+            if (a.l2fb != nullptr) b = fmaf(a.alpha, a.l2fb[o], b);
+            b2e[o] = b;
+            float w = a.l3w[s * l2n + o];
+            if (a.l3fw != nullptr) w = fmaf(a.alpha, a.l3fw[o], w);
+            w3e[o] = w;
+        }
+        if (threadIdx.x == 0) {
+            float b = a.l3b != nullptr ? a.l3b[s] : 0.0f;
+            if (a.l3fb != nullptr) b = fmaf(a.alpha, a.l3fb[0], b);
+            b3e[0] = b;
+        }
+    }
+    __syncthreads();
+
+    const int lt = threadIdx.x;
+    const int p = pb + lt;
+    if (p < pe) {
+        const int b = a.tiles.order[p];
+        float in[kI2], l2v[kL2], hid[kH];
+        float out = 0.0f;
+        const float* l1r = a.l1 + static_cast<size_t>(b) * O;
+#pragma unroll
+        for (int i = 0; i < kH; ++i) hid[i] = (H > 0 || i < hdim) ? l1r[i] : 0.0f;
+        if (a.mode != kHeadBackward) {
+            if (valid) {
+                // L2 input: [SqrCReLU | CReLU] of the hidden L1 outputs (cu:2428-2447).
+#pragma unroll
+                for (int i = 0; i < kH; ++i) {
+                    if (H > 0 || i < hdim) {
+                        const float av = fabsf(hid[i]);
+                        in[i] = crelu01(av * av * kPairScale);
+                        in[hdim + i] = crelu01(hid[i]);
+                    }
+                }
+#pragma unroll
+                for (int o = 0; o < kL2; ++o) {
+                    if (L2 > 0 || o < l2n) {
+                        float sum = b2e[o];
+                        const float* wr = w2e + o * i2n;
+#pragma unroll
+                        for (int i = 0; i < kI2; ++i)
+                            if (H > 0 || i < i2n) sum = fmaf(in[i], wr[i], sum);
+                        l2v[o] = crelu01(sum);
+                    }
+                }
+                out = b3e[0];
+#pragma unroll
+                for (int o = 0; o < kL2; ++o)
+                    if (L2 > 0 || o < l2n) out = fmaf(l2v[o], w3e[o], out);
+                if (a.l1_skip) out += l1r[hdim];
+            } else {
+#pragma unroll
+                for (int i = 0; i < kI2; ++i) in[i] = 0.0f;
+#pragma unroll
+                for (int o = 0; o < kL2; ++o) l2v[o] = 0.0f;
+            }
+            float* ir = a.l2_input + static_cast<size_t>(b) * i2n;
+            float* lr = a.l2 + static_cast<size_t>(b) * l2n;
+#pragma unroll
+            for (int i = 0; i < kI2; ++i)
+                if (H > 0 || i < i2n) ir[i] = in[i];
+#pragma unroll
+            for (int o = 0; o < kL2; ++o)
+                if (L2 > 0 || o < l2n) lr[o] = l2v[o];
+            a.output[b] = out;
+        } else {
+            const float* ir = a.l2_input + static_cast<size_t>(b) * i2n;
+            const float* lr = a.l2 + static_cast<size_t>(b) * l2n;
+#pragma unroll
+            for (int i = 0; i < kI2; ++i) in[i] = (H > 0 || i < i2n) ? ir[i] : 0.0f;
+#pragma unroll
+            for (int o = 0; o < kL2; ++o) l2v[o] = (L2 > 0 || o < l2n) ? lr[o] : 0.0f;
+        }
+        if (a.mode != kHeadForward) {
+            float gout = 0.0f, loss = 0.0f;
+            if (a.mode == kHeadTrain) {
+                loss = sample_loss(a.loss, out, a.targets[b], a.entry_weights[b], &gout);
+                a.per_sample[b] = loss;
+                a.mog[b] = gout;
+            } else {
+                gout = a.mog[b];
+            }
+            float* g1r = a.g1 + static_cast<size_t>(b) * O;
+            float g2m[kL2], gin[kI2];
+            if (valid) {
+                // L3 backward (cu:3324-3430): unmasked L2 gradient; CReLU mask in L2 backward.
+#pragma unroll
+                for (int o = 0; o < kL2; ++o) {
+                    if (L2 > 0 || o < l2n) {
+                        const float g = gout * w3e[o];
+                        if (a.l2_gradients != nullptr) a.l2_gradients[static_cast<size_t>(b) * l2n + o] = g;
+                        g2m[o] = crelu_grad(l2v[o], g);
+                    } else {
+                        g2m[o] = 0.0f;
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < kI2; ++i) {
+                    if (H > 0 || i < i2n) {
+                        float sum = 0.0f;
+#pragma unroll
+                        for (int o = 0; o < kL2; ++o)
+                            if (L2 > 0 || o < l2n) sum = fmaf(g2m[o], w2e[o * i2n + i], sum);
+                        gin[i] = sum;
+                        if (a.l2_input_gradients != nullptr)
+                            a.l2_input_gradients[static_cast<size_t>(b) * i2n + i] = sum;
+                    }
+                }
+                // cu:3709-3770: SqrCReLU branch d/dx (x^2 * 127/128) = 2x * 127/128
+                // while x^2 * 127/128 is inside (0, 1); CReLU branch while x is.
+#pragma unroll
+                for (int i = 0; i < kH; ++i) {
+                    if (H > 0 || i < hdim) {
+                        const float v = hid[i];
+                        const float cs = fabsf(v) * fabsf(v) * kPairScale;
+                        const float sg = (cs > 0.0f && cs < 1.0f) ? gin[i] * (2.0f * v * kPairScale) : 0.0f;
+                        const float lg = (v > 0.0f && v < 1.0f) ? gin[hdim + i] : 0.0f;
+                        g1r[i] = sg + lg;
+                        st_g1[lt * O + i] = sg + lg;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int o = 0; o < kL2; ++o) {
+                    g2m[o] = 0.0f;
+                    if ((L2 > 0 || o < l2n) && a.l2_gradients != nullptr)
+                        a.l2_gradients[static_cast<size_t>(b) * l2n + o] = 0.0f;
+                }
+#pragma unroll
+                for (int i = 0; i < kI2; ++i)
+                    if ((H > 0 || i < i2n) && a.l2_input_gradients != nullptr)
+                        a.l2_input_gradients[static_cast<size_t>(b) * i2n + i] = 0.0f;
+                for (int i = 0; i < hdim; ++i) {
+                    g1r[i] = 0.0f;
+                    st_g1[lt * O + i] = 0.0f;
+                }
+            }
+            if (a.l1_skip) {
+                g1r[hdim] = gout;  // PSQT skip: d out / d l1[hidden] = 1 (cu:3433-3437)
+                st_g1[lt * O + hdim] = valid ? gout : 0.0f;
+            }
+#pragma unroll
+            for (int o = 0; o < kL2; ++o)
+                if (L2 > 0 || o < l2n) {
+                    st_g2[lt * l2n + o] = g2m[o];
+                    st_l2[lt * l2n + o] = l2v[o];
+                }
+#pragma unroll
+            for (int i = 0; i < kI2; ++i)
+                if (H > 0 || i < i2n) st_in[lt * i2n + i] = in[i];
+            st_go[lt] = valid ? gout : 0.0f;
+            st_ls[lt] = loss;
+        }
+    }
+    if (a.mode == kHeadForward) return;
+    __syncthreads();
+    // Per-tile partial sums, samples in tile order.
+    const int n = pe - pb;
+    const int P = head_partial_len(l2n, i2n, O);
+    float* part = a.partials + static_cast<size_t>(t) * P;
+    for (int j = threadIdx.x; j < P; j += blockDim.x) {
+        float sum = 0.0f;
+        int r = j;
+        if (r < l2n * i2n) {
+            const int o = r / i2n, i = r - o * i2n;
+            for (int q = 0; q < n; ++q) sum = fmaf(st_g2[q * l2n + o], st_in[q * i2n + i], sum);
+        } else if ((r -= l2n * i2n) < l2n) {
+            for (int q = 0; q < n; ++q) sum += st_g2[q * l2n + r];
+        } else if ((r -= l2n) < l2n) {
+            for (int q = 0; q < n; ++q) sum = fmaf(st_go[q], st_l2[q * l2n + r], sum);
+        } else if ((r -= l2n) < 1) {
+            for (int q = 0; q < n; ++q) sum += st_go[q];
+        } else if ((r -= 1) < O) {
+            for (int q = 0; q < n; ++q) sum += st_g1[q * O + r];
+        } else {
+            for (int q = 0; q < n; ++q) sum += st_ls[q];
+        }
+        part[j] = sum;
+    }
+}
+
+// ------------------------------------------------------------------ L1 backward
+struct L1BackArgs {
+    Tiles tiles;
+    const float* g1;     // [B][O]
+    const float* w_eff;  // [stacks][width][O]
+    const float* l0[2];  // ClippedReLU FT output per perspective
+    // fused step: pre-activation gradients in king order, row rank[h]
+    float* pregrad_sorted;
+    const int* rank;
+    // reference backward buffers (null in the fused step)
+    float* combined_gradients;
+    float* l0_gradients[2];
+    float* pre_gradients[2];
+    float* dw1_partials;  // [max_tiles][O][width]
+    float* l0b_partials;  // [max_tiles][2][width]
+    int width;
+    int out_dim;
+    int stacks;
+};
+
+// Thread per combined column i of a 256-column chunk; column i belongs to
+// perspective v = i / (width/2) and pairs FT outputs j and j + width/2
+// (pairwise backward, cu:4376-4440).
+template <int O>
+__global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
+    constexpr int kO = O > 0 ? O : kSfnnMaxL1Out;
+    __shared__ float g1s[kSfnnTile * kSfnnMaxL1Out];
+    const int t = blockIdx.x;
+    if (t >= *a.tiles.n_tiles) return;
+    const int s = a.tiles.key[t];
+    const int pb = a.tiles.begin[t], pe = a.tiles.end[t];
+    const int od = O > 0 ? O : a.out_dim;
+    const int W = a.width, half = W / 2;
+    const int i = blockIdx.y * 256 + threadIdx.x;
+    const bool valid = s < a.stacks;
+    for (int q = threadIdx.x; q < (pe - pb) * od; q += blockDim.x)
+        g1s[q] = valid ? a.g1[static_cast<size_t>(a.tiles.order[pb + q / od]) * od + q % od] : 0.0f;
+    __syncthreads();
+    if (i >= W) return;
+    const int v = i >= half ? 1 : 0;
+    const int j = i - v * half;
+    float wcol[kO], dw[kO];
+#pragma unroll
+    for (int o = 0; o < kO; ++o) {
+        wcol[o] = (valid && (O > 0 || o < od)) ? a.w_eff[(static_cast<size_t>(s) * W + i) * od + o] : 0.0f;
+        dw[o] = 0.0f;
+    }
+    float p0sum = 0.0f, p1sum = 0.0f;
+    const float* x = a.l0[v];
+    for (int q = 0; q < pe - pb; ++q) {
+        const int b = a.tiles.order[pb + q];
+        const size_t row = static_cast<size_t>(b) * W;
+        const float x0 = x[row + j], x1 = x[row + j + half];
+        const float c = x0 * x1 * kPairScale;
+        float dc = 0.0f;
+#pragma unroll
+        for (int o = 0; o < kO; ++o) {
+            if (O > 0 || o < od) {
+                const float g = g1s[q * od + o];
+                dc = fmaf(g, wcol[o], dc);
+                dw[o] = fmaf(g, c, dw[o]);
+            }
+        }
+        const float pg = dc * kPairScale;
+        const float u0 = pg * x1, u1 = pg * x0;
+        const float p0 = crelu_grad(x0, u0), p1 = crelu_grad(x1, u1);
+        if (a.pregrad_sorted != nullptr) {
+            float* pr = a.pregrad_sorted + static_cast<size_t>(a.rank[2 * b + v]) * W;
+            pr[j] = p0;
+            pr[j + half] = p1;
+        }
+        if (a.combined_gradients != nullptr) {
+            a.combined_gradients[row + i] = dc;
+            a.l0_gradients[v][row + j] = u0;
+            a.l0_gradients[v][row + j + half] = u1;
+            a.pre_gradients[v][row + j] = p0;
+            a.pre_gradients[v][row + j + half] = p1;
+        }
+        p0sum += p0;
+        p1sum += p1;
+    }
+    float* dwp = a.dw1_partials + static_cast<size_t>(t) * od * W;
+#pragma unroll
+    for (int o = 0; o < kO; ++o)
+        if (O > 0 || o < od) dwp[static_cast<size_t>(o) * W + i] = dw[o];
+    float* bp = a.l0b_partials + (static_cast<size_t>(t) * 2 + v) * W;
+    bp[j] = p0sum;
+    bp[j + half] = p1sum;
+}
+
+// ------------------------------------------------------------------ finalize
+struct FinalArgs {
+    Tiles tiles;
+    const float* head_partials;
+    const float* dw1_partials;
+    const float* l0b_partials;
+    float* dst[kSfGroups];  // gradient destinations per small group (null: group absent)
+    int accumulate;         // dst += gradient (reference backward) or dst = gradient
+    float* weighted_sum;    // optional loss outputs
+    float* mean;
+    float alpha;
+    int width;
+    int out_dim;
+    int l2_size;
+    int l2_in;
+    int stacks;
+    int batch;
+};
+
+__device__ __forceinline__ void put(const FinalArgs& a, int g, size_t i, float v) {
+    float* d = a.dst[g];
+    if (d == nullptr) return;
+    d[i] = a.accumulate ? d[i] + v : v;
+}
+
+// Work items (flattened over blockIdx / threadIdx):
+//   [0, W)                   l0b[j]
+//   [W, W + S*O*W)           l1w[s][o][i]
+//   + W*O                    l1fw[i][o]   (alpha * sum over all valid tiles)
+//   + S*P                    head groups per bucket (l2w, l2b, l3w, l3b, l1b)
+//   + P                      shared head groups (l2fw, l2fb, l3fw, l3fb, l1fb) and the loss
+__global__ void finalize_kernel(FinalArgs a) {
+    const int W = a.width, O = a.out_dim, L2 = a.l2_size, I2 = a.l2_in, S = a.stacks;
+    const int P = head_partial_len(L2, I2, O);
+    const size_t n0 = W;
+    const size_t n1 = n0 + static_cast<size_t>(S) * O * W;
+    const size_t n2 = n1 + static_cast<size_t>(W) * O;
+    const size_t n3 = n2 + static_cast<size_t>(S) * P;
+    const size_t n4 = n3 + P;
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= n4) return;
+    const int n_tiles = *a.tiles.n_tiles;
+    const int valid_tiles = a.tiles.key_first[S];
+    if (t < n0) {
+        float sum = 0.0f;
+        for (int k = 0; k < n_tiles; ++k)
+            sum += a.l0b_partials[(static_cast<size_t>(k) * 2) * W + t] +
+                   a.l0b_partials[(static_cast<size_t>(k) * 2 + 1) * W + t];
+        put(a, kSfL0b, t, sum);
+    } else if (t < n1) {
+        const size_t r = t - n0;
+        const int s = static_cast<int>(r / (static_cast<size_t>(O) * W));
+        const size_t oi = r - static_cast<size_t>(s) * O * W;
+        float sum = 0.0f;
+        for (int k = a.tiles.key_first[s]; k < a.tiles.key_first[s + 1]; ++k)
+            sum += a.dw1_partials[static_cast<size_t>(k) * O * W + oi];
+        put(a, kSfL1w, r, sum);
+    } else if (t < n2) {
+        const size_t r = t - n1;  // [i][o]
+        const int i = static_cast<int>(r / O), o = static_cast<int>(r % O);
+        float sum = 0.0f;
+        for (int k = 0; k < valid_tiles; ++k) sum += a.dw1_partials[(static_cast<size_t>(k) * O + o) * W + i];
+        put(a, kSfL1fw, r, a.alpha * sum);
+    } else if (t < n3) {
+        const size_t r = t - n2;
+        const int s = static_cast<int>(r / P);
+        int j = static_cast<int>(r - static_cast<size_t>(s) * P);
+        float sum = 0.0f;
+        for (int k = a.tiles.key_first[s]; k < a.tiles.key_first[s + 1]; ++k)
+            sum += a.head_partials[static_cast<size_t>(k) * P + j];
+        if (j < L2 * I2) put(a, kSfL2w, static_cast<size_t>(s) * L2 * I2 + j, sum);
+        else if ((j -= L2 * I2) < L2) put(a, kSfL2b, static_cast<size_t>(s) * L2 + j, sum);
+        else if ((j -= L2) < L2) put(a, kSfL3w, static_cast<size_t>(s) * L2 + j, sum);
+        else if ((j -= L2) < 1) put(a, kSfL3b, s, sum);
+        else if ((j -= 1) < O) put(a, kSfL1b, static_cast<size_t>(s) * O + j, sum);
+    } else {
+        int j = static_cast<int>(t - n3);
+        const bool loss = j == P - 1;
+        const int tiles = loss ? n_tiles : valid_tiles;
+        float sum = 0.0f;
+        for (int k = 0; k < tiles; ++k) sum += a.head_partials[static_cast<size_t>(k) * P + j];
+        if (loss) {
+            if (a.weighted_sum != nullptr) {
+                *a.weighted_sum = sum;
+                *a.mean = sum / static_cast<float>(a.batch);
+            }
+            return;
+        }
+        sum *= a.alpha;
+        if (j < L2 * I2) put(a, kSfL2fw, j, sum);
+        else if ((j -= L2 * I2) < L2) put(a, kSfL2fb, j, sum);
+        else if ((j -= L2) < L2) put(a, kSfL3fw, j, sum);
+        else if ((j -= L2) < 1) put(a, kSfL3fb, 0, sum);
+        else if ((j -= 1) < O) put(a, kSfL1fb, j, sum);
+    }
+}
+
+// ------------------------------------------------------------------ FT rows
+struct PieceRowArgs {
+    const int* offsets;
+    const int* entries;
+    const float* src[2];  // gradient row of entry e: src[e & 1] + (e >> 1) * src_stride
+    size_t src_stride;
+    int pieces;           // P
+    int kings;            // rows per piece: row(k, p) = k * P + p
+    int virtual_base;     // virtual row of piece p = virtual_base + p; < 0: none
+    float alpha;
+    int width;
+    int col_groups;
+    int group_width;
+    float* weights;
+    float* momentum;
+    float* velocity;
+    float* slow;
+    float* gradients;     // kRowWrite / kRowAccumulate target
+    RangerArgs ranger;
+    int skip_quiet;
+};
+
+__device__ __forceinline__ int warp_sort_asc(int v, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const int other = __shfl_xor_sync(kFull, v, j);
+            const bool ascending = (lane & k) == 0;
+            const bool lower = (lane & j) == 0;
+            const int lo = min(v, other), hi = max(v, other);
+            v = (lower == ascending) ? lo : hi;
+        }
+    }
+    return v;
+}
+
+__device__ void smem_sort_asc(int* buf, int size, int lane) {
+    for (int k = 2; k <= size; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < size; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const int x = buf[i], y = buf[ixj];
+                    const bool ascending = (i & k) == 0;
+                    if ((x > y) == ascending) {
+                        buf[i] = y;
+                        buf[ixj] = x;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+template <int VEC>
+__device__ __forceinline__ void ldv(const float* p, float* o) {
+    if constexpr (VEC == 8) {
+        const float4 x = *reinterpret_cast<const float4*>(p);
+        const float4 y = *reinterpret_cast<const float4*>(p + 4);
+        o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w; o[4] = y.x; o[5] = y.y; o[6] = y.z; o[7] = y.w;
+    } else if constexpr (VEC == 4) {
+        const float4 x = *reinterpret_cast<const float4*>(p);
+        o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w;
+    } else {
+        o[0] = *p;
+    }
+}
+
+template <int VEC>
+__device__ __forceinline__ void stv(float* p, const float* v) {
+    if constexpr (VEC == 8) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    } else if constexpr (VEC == 4) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        *p = v[0];
+    }
+}
+
+// Applies the row update for one column chunk: Ranger / write / accumulate.
+// `seen` receives the row's gradient as the virtual row sees it (the
+// accumulated value in accumulate mode).
+template <int VEC, int MODE>
+__device__ __forceinline__ void row_update(const PieceRowArgs& a, size_t off, const float* g, bool quiet_row,
+                                           float* seen) {
+    if constexpr (MODE == kRowWrite) {
+        stv<VEC>(a.gradients + off, g);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) seen[e] = g[e];
+    } else if constexpr (MODE == kRowAccumulate) {
+        float x[VEC];
+        ldv<VEC>(a.gradients + off, x);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) x[e] += g[e];
+        stv<VEC>(a.gradients + off, x);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) seen[e] = x[e];
+    } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) seen[e] = g[e];
+        float w[VEC], m[VEC], v[VEC];
+        ldv<VEC>(a.weights + off, w);
+        ldv<VEC>(a.momentum + off, m);
+        ldv<VEC>(a.velocity + off, v);
+        if (quiet_row && a.skip_quiet && !a.ranger.do_lookahead) {
+            bool quiet = true;
+#pragma unroll
+            for (int e = 0; e < VEC; ++e)
+                quiet = quiet && (__float_as_uint(m[e]) | __float_as_uint(v[e])) == 0u && weight_is_quiet(w[e], a.ranger);
+            if (quiet) return;
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) radam_coordinate(a.ranger.gradient_factor * g[e], a.ranger, w[e], m[e], v[e]);
+        if (a.ranger.do_lookahead) {
+            float sl[VEC];
+            ldv<VEC>(a.slow + off, sl);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) w[e] = lookahead_coordinate(w[e], sl[e], a.ranger);
+            stv<VEC>(a.slow + off, w);
+        }
+        stv<VEC>(a.weights + off, w);
+        stv<VEC>(a.momentum + off, m);
+        stv<VEC>(a.velocity + off, v);
+    }
+}
+
+// One warp per (piece, column group).  The piece's rows are visited in king
+// order; every warp walks the kings at about the same pace, so the gradient
+// rows being read at any time belong to a few kings' half-positions (L2).
+template <int VEC, int ITERS, int MODE>
+__global__ void __launch_bounds__(kPieceRowWarps * 32) piece_row_kernel(PieceRowArgs a) {
+    __shared__ int sort_buf[kPieceRowWarps][kPieceSortCap];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gw = blockIdx.x * kPieceRowWarps + warp;
+    const int p = gw / a.col_groups;
+    if (p >= a.pieces) return;
+    const int c0 = (gw - p * a.col_groups) * a.group_width;
+    const int c_end = min(a.width, c0 + a.group_width);
+    float vacc[ITERS][VEC];
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) vacc[it][e] = 0.0f;
+    bool any = false;
+    for (int k = 0; k < a.kings; ++k) {
+        const int row = k * a.pieces + p;
+        const int beg = a.offsets[row];
+        const int n = a.offsets[row + 1] - beg;
+        const int* elist = a.entries + beg;
+        any = any || n > 0;
+        int mine = INT_MAX;
+        int mode = 0;
+        if (n <= 32) {
+            mine = lane < n ? elist[lane] : INT_MAX;
+            mine = warp_sort_asc(mine, lane);
+        } else if (n <= kPieceSortCap) {
+            int size = 64;
+            while (size < n) size <<= 1;
+            int* buf = sort_buf[warp];
+            for (int i = lane; i < size; i += 32) buf[i] = i < n ? elist[i] : INT_MAX;
+            __syncwarp();
+            smem_sort_asc(buf, size, lane);
+            mode = 1;
+        } else {
+            mode = 2;
+        }
+        const int* list = mode == 1 ? sort_buf[warp] : elist;
+        const size_t row_off = static_cast<size_t>(row) * a.width;
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+            const int c = c0 + (it * 32 + lane) * VEC;
+            const bool active = c < c_end;
+            float acc[VEC];
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
+            int q = 0;
+            for (; q + 4 <= n; q += 4) {
+                int en[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) en[u] = mode == 0 ? __shfl_sync(kFull, mine, q + u) : list[q + u];
+                if (active) {
+                    float x[4][VEC];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        ldv<VEC>(a.src[en[u] & 1] + static_cast<size_t>(en[u] >> 1) * a.src_stride + c, x[u]);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+#pragma unroll
+                        for (int e = 0; e < VEC; ++e) acc[e] += x[u][e];
+                }
+            }
+            for (; q < n; ++q) {
+                const int en = mode == 0 ? __shfl_sync(kFull, mine, q) : list[q];
+                if (active) {
+                    float x[VEC];
+                    ldv<VEC>(a.src[en & 1] + static_cast<size_t>(en >> 1) * a.src_stride + c, x);
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) acc[e] += x[e];
+                }
+            }
+            if (active) {
+                float seen[VEC];
+                row_update<VEC, MODE>(a, row_off + c, acc, n == 0, seen);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) vacc[it][e] += seen[e];
+            }
+        }
+        __syncwarp();
+    }
+    if (a.virtual_base < 0) return;
+    const size_t vrow = static_cast<size_t>(a.virtual_base + p) * a.width;
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+        const int c = c0 + (it * 32 + lane) * VEC;
+        if (c >= c_end) continue;
+        float g[VEC], seen[VEC];
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) g[e] = a.alpha * vacc[it][e];
+        if constexpr (MODE == kRowAccumulate) {
+            stv<VEC>(a.gradients + vrow + c, g);  // cu:4950-4985 overwrites the factor row's gradient
+        } else {
+            row_update<VEC, MODE>(a, vrow + c, g, !any, seen);
+        }
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <int MODE>
+int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec, int iters) {
+    const int warps = a.pieces * a.col_groups;
+    const int blocks = (warps + kPieceRowWarps - 1) / kPieceRowWarps;
+    if (vec == 8 && iters == 2) piece_row_kernel<8, 2, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
+    else if (vec == 8) piece_row_kernel<8, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
+    else if (vec == 4) piece_row_kernel<4, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
+    else piece_row_kernel<1, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
+    return check_launch("SFNN FT row kernel launch");
+}
+
+int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a) {
+    bool al = aligned16(a.src[0]) && aligned16(a.src[1]) && a.src_stride % 4 == 0;
+    if (mode == kRowRanger)
+        al = al && aligned16(a.weights) && aligned16(a.momentum) && aligned16(a.velocity) && aligned16(a.slow);
+    else
+        al = al && aligned16(a.gradients);
+    int vec = 1, iters = 1;
+    if (al && a.width % 512 == 0) {
+        vec = 8;
+        iters = 2;
+        a.group_width = 512;
+    } else if (al && a.width % 256 == 0) {
+        vec = 8;
+        a.group_width = 256;
+    } else if (al && a.width % 128 == 0) {
+        vec = 4;
+        a.group_width = 128;
+    } else {
+        a.group_width = 32;
+    }
+    a.col_groups = (a.width + a.group_width - 1) / a.group_width;
+    switch (mode) {
+        case kRowRanger: return launch_piece_rows_mode<kRowRanger>(ctx, a, vec, iters);
+        case kRowWrite: return launch_piece_rows_mode<kRowWrite>(ctx, a, vec, iters);
+        default: return launch_piece_rows_mode<kRowAccumulate>(ctx, a, vec, iters);
+    }
+}
+
+// ------------------------------------------------------------------ host plan
+struct SfnnPlan {
+    const float* table;  // what the FT gather reads
+    KingSortOut king;
+    int* king_rank;
+    Tiles tiles;
+    float* w1_eff;
+    float* head_partials;
+    float* dw1_partials;
+    float* l0b_partials;
+    float* g1;
+};
+
+size_t align_floats(size_t n) { return (n + 63) & ~static_cast<size_t>(63); }
+
+// Fold, sorts, tile table and effective L1 weights; every scratch the step needs.
+int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, const int* stm, const int* nstm,
+                 const int* buckets, float* fold_target, SfnnPlan* plan) {
+    const int threads = 256;
+    int blocks = 0;
+    // 1. fold
+    plan->table = w.l0w;
+    if (d.base > 0) {
+        float* folded = fold_target;
+        const size_t n = static_cast<size_t>(d.base) * d.width;
+        if (folded == nullptr) {
+            void* p = nullptr;
+            if (scratch_slot(ctx, kScratchSfnnFold, n * sizeof(float), &p, "cudaMalloc SFNN folded FT") != 0) return -1;
+            folded = static_cast<float*>(p);
+        }
+        if (d.width % 4 == 0 && aligned16(w.l0w) && aligned16(folded)) {
+            if (grid_1d(n / 4, threads, &blocks, "SFNN fold") != 0) return -1;
+            fold_ft4_kernel<<<blocks, threads, 0, ctx->stream>>>(reinterpret_cast<const float4*>(w.l0w),
+                                                                 reinterpret_cast<float4*>(folded), n / 4, d.width / 4,
+                                                                 d.base, d.ft_alpha);
+        } else {
+            if (grid_1d(n, threads, &blocks, "SFNN fold") != 0) return -1;
+            fold_ft1_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l0w, folded, n, d.width, d.base, d.ft_alpha);
+        }
+        if (check_launch("SFNN fold launch") != 0) return -1;
+        plan->table = folded;
+    }
+    prof_mark(ctx);
+    // 2. sorts + tiles
+    const int n_half = 2 * d.batch;
+    const int max_tiles = d.batch / kSfnnTile + d.stacks + 2;
+    const size_t king_ints = king_sort_scratch_ints<kSfnnKingKeys>(n_half);
+    const size_t bucket_ints = king_sort_scratch_ints<kBucketKeys>(d.batch);
+    const size_t tile_ints = 1 + 3 * static_cast<size_t>(max_tiles) + (kBucketKeys + 1);
+    const size_t sort_ints = king_ints + n_half + bucket_ints + tile_ints;
+    void* sp = nullptr;
+    if (scratch_slot(ctx, kScratchSfnnSort, sort_ints * sizeof(int), &sp, "cudaMalloc SFNN sort") != 0) return -1;
+    int* king_scratch = static_cast<int*>(sp);
+    int* rank = king_scratch + king_ints;
+    int* bucket_scratch = rank + n_half;
+    int* tt = bucket_scratch + bucket_ints;
+    const int piece = (d.n_features % kSfnnPieces == 0) ? kSfnnPieces : d.n_features;
+    if (king_sort<kSfnnKingKeys>(ctx, stm, nstm, n_half, KingKey{piece, d.n_features, d.max_active}, king_scratch, rank,
+                                 &plan->king) != 0)
+        return -1;
+    plan->king_rank = rank;
+    {
+        const int nblocks = (d.batch + kKingSortThreads - 1) / kKingSortThreads;
+        int* key_off = bucket_scratch;
+        int* keys = key_off + kBucketKeys + 1;
+        int* order = keys + d.batch;
+        int* block_hist = order + d.batch;
+        bucket_hist_kernel<<<nblocks, kKingSortThreads, 0, ctx->stream>>>(buckets, d.batch, d.stacks, keys, block_hist);
+        king_bases_kernel<kBucketKeys><<<1, 128, 0, ctx->stream>>>(block_hist, nblocks, key_off);
+        king_scatter_kernel<kBucketKeys><<<nblocks, kKingSortThreads, 0, ctx->stream>>>(keys, d.batch, block_hist, order,
+                                                                                         nullptr);
+        int* n_tiles = tt;
+        int* tile_key = n_tiles + 1;
+        int* tile_begin = tile_key + max_tiles;
+        int* tile_end = tile_begin + max_tiles;
+        int* key_first = tile_end + max_tiles;
+        tile_table_kernel<<<1, 128, 0, ctx->stream>>>(key_off, d.stacks + 1, n_tiles, tile_key, tile_begin, tile_end,
+                                                      key_first);
+        if (check_launch("SFNN bucket sort launch") != 0) return -1;
+        plan->tiles = Tiles{order, n_tiles, tile_key, tile_begin, tile_end, key_first, max_tiles};
+    }
+    // 3. effective L1 weights and per-tile partial buffers
+    const size_t eff = static_cast<size_t>(d.stacks) * d.width * d.l1_out;
+    void* ep = nullptr;
+    if (scratch_slot(ctx, kScratchSfnnEff, eff * sizeof(float), &ep, "cudaMalloc SFNN L1 weights") != 0) return -1;
+    plan->w1_eff = static_cast<float*>(ep);
+    if (grid_1d(eff, threads, &blocks, "SFNN L1 weights") != 0) return -1;
+    l1_eff_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l1w, d.has_l1f ? w.l1fw : nullptr, d.shared_alpha, d.stacks,
+                                                       d.l1_out, d.width, plan->w1_eff);
+    if (check_launch("SFNN L1 weights launch") != 0) return -1;
+    const size_t hp = align_floats(static_cast<size_t>(max_tiles) * head_partial_len(d.l2_size, d.l2_in, d.l1_out));
+    const size_t dp = align_floats(static_cast<size_t>(max_tiles) * d.l1_out * d.width);
+    const size_t bp = align_floats(static_cast<size_t>(max_tiles) * 2 * d.width);
+    const size_t gp = align_floats(static_cast<size_t>(d.batch) * d.l1_out);
+    void* pp = nullptr;
+    if (scratch_slot(ctx, kScratchSfnnPartials, (hp + dp + bp + gp) * sizeof(float), &pp,
+                     "cudaMalloc SFNN partials") != 0)
+        return -1;
+    plan->head_partials = static_cast<float*>(pp);
+    plan->dw1_partials = plan->head_partials + hp;
+    plan->l0b_partials = plan->dw1_partials + dp;
+    plan->g1 = plan->l0b_partials + bp;
+    prof_mark(ctx);
+    return 0;
+}
+
+int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnPlan& plan, const int* stm,
+                      const int* nstm, const float* l0b, const SfnnActivations& act) {
+    FtArgs fa{};
+    fa.order = plan.king.order;
+    fa.stm = stm;
+    fa.nstm = nstm;
+    fa.table = plan.table;
+    fa.bias = l0b;
+    fa.l0[0] = act.stm_l0;
+    fa.l0[1] = act.nstm_l0;
+    fa.combined = act.combined;
+    fa.n_half = 2 * d.batch;
+    fa.max_active = d.max_active;
+    fa.n_features = d.n_features;
+    fa.width = d.width;
+    const bool al = aligned16(plan.table) && aligned16(l0b) && aligned16(act.stm_l0) && aligned16(act.nstm_l0) &&
+                    aligned16(act.combined);
+    const int blocks = (fa.n_half + 7) / 8;
+    if (al && d.width == 1536) ft_forward_kernel<12><<<blocks, 256, 0, ctx->stream>>>(fa);
+    else if (al && d.width == 1024) ft_forward_kernel<8><<<blocks, 256, 0, ctx->stream>>>(fa);
+    else if (al && d.width == 2304) ft_forward_kernel<18><<<blocks, 256, 0, ctx->stream>>>(fa);
+    else if (al && d.width == 512) ft_forward_kernel<4><<<blocks, 256, 0, ctx->stream>>>(fa);
+    else if (al && d.width == 256) ft_forward_kernel<2><<<blocks, 256, 0, ctx->stream>>>(fa);
+    else {
+        fa.order = nullptr;
+        int gb = 0;
+        if (grid_1d(static_cast<size_t>(fa.n_half) * (d.width / 2), 256, &gb, "SFNN FT forward") != 0) return -1;
+        ft_forward_generic_kernel<<<gb, 256, 0, ctx->stream>>>(fa);
+    }
+    return check_launch("SFNN FT forward launch");
+}
+
+int launch_l1_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, const SfnnPlan& plan,
+                      const float* combined, float* l1) {
+    L1Args la{};
+    la.tiles = plan.tiles;
+    la.combined = combined;
+    la.w_eff = plan.w1_eff;
+    la.l1b = w.l1b;
+    la.l1fb = d.has_l1f ? w.l1fb : nullptr;
+    la.alpha = d.shared_alpha;
+    la.l1 = l1;
+    la.width = d.width;
+    la.out_dim = d.l1_out;
+    la.stacks = d.stacks;
+    const size_t smem = static_cast<size_t>(d.width) * 16 * sizeof(float);
+    if (d.l1_out == 16 && d.width % 4 == 0 && smem <= 200 * 1024 && aligned16(combined)) {
+        cudaError_t st = cudaFuncSetAttribute(l1_forward16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(smem));
+        if (st != cudaSuccess) return fail("cudaFuncSetAttribute SFNN L1", st);
+        l1_forward16_kernel<<<plan.tiles.max_tiles, 256, smem, ctx->stream>>>(la);
+    } else {
+        l1_forward_generic_kernel<<<plan.tiles.max_tiles, 256, 0, ctx->stream>>>(la);
+    }
+    return check_launch("SFNN L1 forward launch");
+}
+
+size_t head_smem_bytes(const SfnnDims& d) {
+    const size_t l2 = d.l2_size, i2 = d.l2_in, o = d.l1_out;
+    return (l2 * i2 + 2 * l2 + 1 + kSfnnTile * (2 * l2 + i2 + 1 + o + 1)) * sizeof(float);
+}
+
+int launch_head(BulletOuCudaCppContext* ctx, const SfnnDims& d, const HeadArgs& h) {
+    const size_t smem = head_smem_bytes(d);
+    auto kernel = (d.l1_hidden == 15 && d.l2_size == 32) ? head_kernel<15, 32> : head_kernel<0, 0>;
+    cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (st != cudaSuccess) return fail("cudaFuncSetAttribute SFNN head", st);
+    kernel<<<h.tiles.max_tiles, kSfnnTile, smem, ctx->stream>>>(h);
+    return check_launch("SFNN head launch");
+}
+
+HeadArgs head_args(const SfnnDims& d, const SfnnWeights& w, const SfnnPlan& plan, const SfnnActivations& act) {
+    HeadArgs h{};
+    h.tiles = plan.tiles;
+    h.l1 = act.l1;
+    h.l2w = w.l2w;
+    h.l2b = w.l2b;
+    h.l2fw = d.has_l2f ? w.l2fw : nullptr;
+    h.l2fb = d.has_l2f ? w.l2fb : nullptr;
+    h.l3w = w.l3w;
+    h.l3b = w.l3b;
+    h.l3fw = d.has_l3f ? w.l3fw : nullptr;
+    h.l3fb = d.has_l3f ? w.l3fb : nullptr;
+    h.alpha = d.shared_alpha;
+    h.l2_input = act.l2_input;
+    h.l2 = act.l2;
+    h.output = act.output;
+    h.g1 = plan.g1;
+    h.partials = plan.head_partials;
+    h.l1_hidden = d.l1_hidden;
+    h.l1_out = d.l1_out;
+    h.l1_skip = d.l1_skip;
+    h.l2_size = d.l2_size;
+    h.stacks = d.stacks;
+    return h;
+}
+
+int launch_l1_backward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnPlan& plan, L1BackArgs& b) {
+    b.tiles = plan.tiles;
+    b.g1 = plan.g1;
+    b.w_eff = plan.w1_eff;
+    b.dw1_partials = plan.dw1_partials;
+    b.l0b_partials = plan.l0b_partials;
+    b.width = d.width;
+    b.out_dim = d.l1_out;
+    b.stacks = d.stacks;
+    const dim3 grid(plan.tiles.max_tiles, (d.width + 255) / 256);
+    if (d.l1_out == 16) l1_backward_kernel<16><<<grid, 256, 0, ctx->stream>>>(b);
+    else l1_backward_kernel<0><<<grid, 256, 0, ctx->stream>>>(b);
+    return check_launch("SFNN L1 backward launch");
+}
+
+int launch_finalize(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnPlan& plan, FinalArgs& f) {
+    f.tiles = plan.tiles;
+    f.head_partials = plan.head_partials;
+    f.dw1_partials = plan.dw1_partials;
+    f.l0b_partials = plan.l0b_partials;
+    f.alpha = d.shared_alpha;
+    f.width = d.width;
+    f.out_dim = d.l1_out;
+    f.l2_size = d.l2_size;
+    f.l2_in = d.l2_in;
+    f.stacks = d.stacks;
+    f.batch = d.batch;
+    const int P = head_partial_len(d.l2_size, d.l2_in, d.l1_out);
+    const size_t n = static_cast<size_t>(d.width) + static_cast<size_t>(d.stacks) * d.l1_out * d.width +
+                     static_cast<size_t>(d.width) * d.l1_out + static_cast<size_t>(d.stacks) * P + P;
+    int blocks = 0;
+    if (grid_1d(n, 256, &blocks, "SFNN finalize") != 0) return -1;
+    finalize_kernel<<<blocks, 256, 0, ctx->stream>>>(f);
+    return check_launch("SFNN finalize launch");
+}
+
+PieceRowArgs piece_row_args(const SfnnDims& d, const InverseIndex& index) {
+    PieceRowArgs r{};
+    r.offsets = index.offsets;
+    r.entries = index.entries;
+    if (d.base > 0) {
+        r.pieces = kSfnnPieces;
+        r.kings = d.base / kSfnnPieces;
+        r.virtual_base = d.base;
+    } else {
+        r.pieces = d.n_features;
+        r.kings = 1;
+        r.virtual_base = -1;
+    }
+    r.alpha = d.ft_alpha;
+    r.width = d.width;
+    return r;
+}
+
+// ------------------------------------------------------------------ validation
+int sfnn_dims(size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip, size_t l2_size, size_t num_stacks,
+              size_t batch, size_t max_active, float ft_alpha, float shared_alpha, SfnnDims* d) {
+    if (input_size == 0 || ft_size == 0 || l1_hidden == 0 || l2_size == 0 || num_stacks == 0 || batch == 0 ||
+        max_active == 0)
+        return fail_message("SFNN shape, batch and max_active must be greater than zero");
+    if (ft_size % 2 != 0) return fail_messagef("SFNN ft_size must be even, got %zu", ft_size);
+    const size_t l1_out = l1_hidden + (l1_skip ? 1 : 0);
+    if (l1_out > static_cast<size_t>(kSfnnMaxL1Out))
+        return fail_messagef("SFNN l1_hidden + skip must be at most %d on this backend", kSfnnMaxL1Out);
+    if (l2_size > static_cast<size_t>(kSfnnMaxL2))
+        return fail_messagef("SFNN l2_size must be at most %d on this backend", kSfnnMaxL2);
+    if (num_stacks > static_cast<size_t>(kSfnnMaxStacks))
+        return fail_messagef("SFNN num_stacks must be at most %d on this backend", kSfnnMaxStacks);
+    if (batch > (1u << 26) || max_active > 4096 || input_size > static_cast<size_t>(INT_MAX) / 2 || ft_size > 8192 ||
+        input_size * ft_size > (static_cast<size_t>(1) << 40))
+        return fail_message("SFNN batch, max_active or table too large for this backend");
+    if (!(ft_alpha >= 0.0f && ft_alpha <= 100.0f) || !(shared_alpha >= 0.0f && shared_alpha <= 10.0f))
+        return fail_message("SFNN factorizer alpha out of range");
+    d->input_size = static_cast<int>(input_size);
+    d->base = sfnn_factorized_base(input_size);
+    d->n_features = d->base > 0 ? d->base : static_cast<int>(input_size);
+    d->width = static_cast<int>(ft_size);
+    d->l1_hidden = static_cast<int>(l1_hidden);
+    d->l1_out = static_cast<int>(l1_out);
+    d->l1_skip = l1_skip ? 1 : 0;
+    d->l2_in = static_cast<int>(2 * l1_hidden);
+    d->l2_size = static_cast<int>(l2_size);
+    d->stacks = static_cast<int>(num_stacks);
+    d->batch = static_cast<int>(batch);
+    d->max_active = static_cast<int>(max_active);
+    d->ft_alpha = ft_alpha;
+    d->shared_alpha = shared_alpha;
+    return 0;
+}
+
+int validate_sfnn_weights(BulletOuCudaCppContext* ctx, const SfnnDims& d, const BulletOuCudaCppF32Buffer* const* p,
+                          const char* what) {
+    const SfnnGroupLayout g = sfnn_group_layout(d);
+    static const char* names[14] = {"l0w", "l0b", "l1w", "l1b", "l1fw", "l1fb", "l2w",
+                                    "l2b", "l2fw", "l2fb", "l3w", "l3b", "l3fw", "l3fb"};
+    char name[64];
+    std::snprintf(name, sizeof(name), "%s l0w", what);
+    if (validate_f32(ctx, p[0], static_cast<size_t>(d.input_size) * d.width, name) != 0) return -1;
+    for (int k = 0; k < kSfGroups; ++k) {
+        std::snprintf(name, sizeof(name), "%s %s", what, names[k + 1]);
+        if (g.len[k] == 0) {
+            if (p[k + 1] != nullptr) return fail_messagef("%s must be null when its factorizer is inactive", name);
+            continue;
+        }
+        if (validate_f32(ctx, p[k + 1], g.len[k], name) != 0) return -1;
+    }
+    return 0;
+}
+
+SfnnWeights weights_from(const BulletOuCudaCppF32Buffer* const* p) {
+    auto ptr = [&](int i) -> const float* { return p[i] != nullptr ? p[i]->ptr : nullptr; };
+    return SfnnWeights{ptr(0), ptr(1), ptr(2),  ptr(3),  ptr(4),  ptr(5),  ptr(6),
+                       ptr(7), ptr(8), ptr(9), ptr(10), ptr(11), ptr(12), ptr(13)};
+}
+
+// Scratch activations of the fused step: stm_l0 | nstm_l0 | combined | l1 |
+// l2_input | l2 | pregrad (king order).
+struct StepBuffers {
+    SfnnActivations act;
+    float* pregrad;
+};
+
+int step_buffers(BulletOuCudaCppContext* ctx, const SfnnDims& d, float* output, StepBuffers* sb) {
+    const size_t BW = static_cast<size_t>(d.batch) * d.width;
+    const size_t sizes[7] = {align_floats(BW),
+                             align_floats(BW),
+                             align_floats(BW),
+                             align_floats(static_cast<size_t>(d.batch) * d.l1_out),
+                             align_floats(static_cast<size_t>(d.batch) * d.l2_in),
+                             align_floats(static_cast<size_t>(d.batch) * d.l2_size),
+                             align_floats(2 * BW)};
+    size_t total = 0;
+    for (size_t s : sizes) total += s;
+    void* p = nullptr;
+    if (scratch_slot(ctx, kScratchSfnnStep, total * sizeof(float), &p, "cudaMalloc SFNN step buffers") != 0) return -1;
+    float* f = static_cast<float*>(p);
+    float* ptrs[7];
+    for (int i = 0; i < 7; ++i) {
+        ptrs[i] = f;
+        f += sizes[i];
+    }
+    sb->act = SfnnActivations{ptrs[0], ptrs[1], ptrs[2], ptrs[3], ptrs[4], ptrs[5], output};
+    sb->pregrad = ptrs[6];
+    return 0;
+}
+
+// Bounds of the L1 shared factor refer to its contribution alpha * w
+// (factor_contribution_clip, lib.rs:8772-8788): divided by alpha, unbounded
+// when alpha is 0; infinite bounds stay infinite.
+RangerArgs shared_factor_clip(RangerArgs a, float alpha) {
+    auto scale = [&](float bound, float lim) -> float {
+        if (alpha == 0.0f) return lim;
+        if (bound == -FLT_MAX || bound == FLT_MAX) return bound;
+        const double x = static_cast<double>(bound) / static_cast<double>(alpha);
+        return static_cast<float>(std::min<double>(FLT_MAX, std::max<double>(-FLT_MAX, x)));
+    };
+    a.min_weight = scale(a.min_weight, -FLT_MAX);
+    a.max_weight = scale(a.max_weight, FLT_MAX);
+    if (a.lookahead_min != -FLT_MAX || a.lookahead_max != FLT_MAX) {
+        a.lookahead_min = a.min_weight;
+        a.lookahead_max = a.max_weight;
+    }
+    return a;
+}
+
+// The fused step: forward, loss, backward and Ranger (ranger != null), or the
+// local gradients (ranger == null: FT gradient rows written to ft_grad, small
+// groups packed into dense_grad in the sfnn_group_layout order).
+int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, const int* stm, const int* nstm,
+              const int* buckets, const float* targets, const float* entry_weights, const LossArgs& la, int finalize,
+              const BulletOuB200RangerStep* ranger, float* const* wm, float* const* mm, float* const* vm,
+              float* const* sm, float* output, float* per_sample, float* mog, float* weighted_sum, float* mean,
+              float* ft_grad, float* dense_grad) {
+    ctx->prof_marks_per_step = 9;
+    prof_mark(ctx);
+    SfnnPlan plan{};
+    if (sfnn_prepare(ctx, d, w, stm, nstm, buckets, nullptr, &plan) != 0) return -1;
+    InverseIndex index;
+    if (build_inverse_index_rows(ctx, stm, nstm, d.batch, d.max_active, d.n_features, &index, plan.king_rank) != 0)
+        return -1;
+    StepBuffers sb{};
+    if (step_buffers(ctx, d, output, &sb) != 0) return -1;
+    prof_mark(ctx);
+    if (launch_ft_forward(ctx, d, plan, stm, nstm, w.l0b, sb.act) != 0) return -1;
+    prof_mark(ctx);
+    if (launch_l1_forward(ctx, d, w, plan, sb.act.combined, sb.act.l1) != 0) return -1;
+    HeadArgs h = head_args(d, w, plan, sb.act);
+    h.mode = kHeadTrain;
+    h.targets = targets;
+    h.entry_weights = entry_weights;
+    h.loss = la;
+    h.per_sample = per_sample;
+    h.mog = mog;
+    if (launch_head(ctx, d, h) != 0) return -1;
+    prof_mark(ctx);
+    L1BackArgs lb{};
+    lb.l0[0] = sb.act.stm_l0;
+    lb.l0[1] = sb.act.nstm_l0;
+    lb.pregrad_sorted = sb.pregrad;
+    lb.rank = plan.king_rank;
+    if (launch_l1_backward(ctx, d, plan, lb) != 0) return -1;
+    prof_mark(ctx);
+    // small-parameter gradients (packed), loss sum, then Ranger per group
+    const SfnnGroupLayout g = sfnn_group_layout(d);
+    float* packed = dense_grad;
+    if (packed == nullptr) {
+        void* gp = nullptr;
+        if (scratch_slot(ctx, kScratchSfnnGrads, g.begin[kSfGroups] * sizeof(float), &gp, "cudaMalloc SFNN grads") != 0)
+            return -1;
+        packed = static_cast<float*>(gp);
+    }
+    FinalArgs f{};
+    for (int k = 0; k < kSfGroups; ++k) f.dst[k] = g.len[k] ? packed + g.begin[k] : nullptr;
+    f.accumulate = 0;
+    if (finalize) {
+        f.weighted_sum = weighted_sum;
+        f.mean = mean;
+    }
+    if (launch_finalize(ctx, d, plan, f) != 0) return -1;
+    RangerArgs ra{};
+    if (ranger != nullptr) {
+        ra = ranger_args_from(*ranger);
+        for (int k = 0; k < kSfGroups; ++k) {
+            if (!g.len[k]) continue;
+            const RangerArgs ga = (k == kSfL1fw || k == kSfL1fb) ? shared_factor_clip(ra, d.shared_alpha) : ra;
+            if (launch_ranger(ctx, g.len[k], ga, packed + g.begin[k], wm[k + 1], mm[k + 1], vm[k + 1], sm[k + 1]) != 0)
+                return -1;
+        }
+    }
+    prof_mark(ctx);
+    PieceRowArgs r = piece_row_args(d, index);
+    r.src[0] = sb.pregrad;
+    r.src[1] = sb.pregrad + d.width;
+    r.src_stride = 2 * static_cast<size_t>(d.width);
+    if (ranger != nullptr) {
+        r.weights = wm[0];
+        r.momentum = mm[0];
+        r.velocity = vm[0];
+        r.slow = sm[0];
+        r.ranger = ra;
+        r.skip_quiet = ranger_zero_step_is_identity(ra) ? 1 : 0;
+        if (launch_piece_rows(ctx, kRowRanger, r) != 0) return -1;
+    } else {
+        r.gradients = ft_grad;
+        if (launch_piece_rows(ctx, kRowWrite, r) != 0) return -1;
+    }
+    prof_mark(ctx);
+    return 0;
+}
+
+// Rejects the reference options this backend does not implement: grouped and
+// common+shard L1, bucket-axis factorizers, residual count gates.
+int reject_unsupported(size_t l1_group_count, size_t l1_common_size, size_t l1_shard_size, int has_l1ax, int has_l2ax,
+                       int has_l3ax, int use_king_axis, int use_hand_axis, int use_progress_axis,
+                       int use_king_hand_pair, int use_king_progress_pair, int use_hand_progress_pair,
+                       const BulletOuCudaCppF32Buffer* residual_count_gates,
+                       const BulletOuCudaCppF32Buffer* factorizer_axis_confidences) {
+    if (l1_group_count > 1 || l1_common_size != 0 || l1_shard_size != 0)
+        return fail_message("unsupported on this backend: grouped / common+shard SFNN L1");
+    if (has_l1ax || has_l2ax || has_l3ax || use_king_axis || use_hand_axis || use_progress_axis || use_king_hand_pair ||
+        use_king_progress_pair || use_hand_progress_pair)
+        return fail_message("unsupported on this backend: SFNN bucket-axis factorizers");
+    if (residual_count_gates != nullptr || factorizer_axis_confidences != nullptr)
+        return fail_message("unsupported on this backend: SFNN residual count gates / axis confidences");
+    return 0;
+}
+
+}  // namespace
+}  // namespace bou
+
+using namespace bou;
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+int bulletou_cuda_cpp_sfnn_forward_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip, size_t l2_size,
+    size_t num_stacks, size_t l1_group_count, size_t l1_common_size, size_t l1_shard_size,
+    size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* l0w, BulletOuCudaCppF32Buffer* folded_l0w,
+    const BulletOuCudaCppF32Buffer* l0b, const BulletOuCudaCppF32Buffer* l1w, const BulletOuCudaCppF32Buffer* l1b,
+    const BulletOuCudaCppF32Buffer* l1fw, const BulletOuCudaCppF32Buffer* l1fb, int has_l1f,
+    const BulletOuCudaCppF32Buffer* l1axw, const BulletOuCudaCppF32Buffer* l1axb, int has_l1ax,
+    const BulletOuCudaCppF32Buffer* l2w, const BulletOuCudaCppF32Buffer* l2b, const BulletOuCudaCppF32Buffer* l2fw,
+    const BulletOuCudaCppF32Buffer* l2fb, int has_l2f, const BulletOuCudaCppF32Buffer* l2axw,
+    const BulletOuCudaCppF32Buffer* l2axb, int has_l2ax, const BulletOuCudaCppF32Buffer* l3w,
+    const BulletOuCudaCppF32Buffer* l3b, const BulletOuCudaCppF32Buffer* l3fw, const BulletOuCudaCppF32Buffer* l3fb,
+    int has_l3f, const BulletOuCudaCppF32Buffer* l3axw, const BulletOuCudaCppF32Buffer* l3axb, int has_l3ax,
+    int use_king_axis, int use_hand_axis, int use_progress_axis, int use_king_hand_pair, int use_king_progress_pair,
+    int use_hand_progress_pair, float ft_factorizer_alpha, float factorizer_shared_alpha,
+    float factorizer_king_axis_alpha, float factorizer_hand_axis_alpha, float factorizer_progress_axis_alpha,
+    float factorizer_pair_alpha, const BulletOuCudaCppF32Buffer* residual_count_gates,
+    const BulletOuCudaCppF32Buffer* factorizer_axis_confidences, BulletOuCudaCppF32Buffer* stm_l0,
+    BulletOuCudaCppF32Buffer* nstm_l0, BulletOuCudaCppF32Buffer* combined, BulletOuCudaCppF32Buffer* l1,
+    BulletOuCudaCppF32Buffer* l2_input, BulletOuCudaCppF32Buffer* l2, BulletOuCudaCppF32Buffer* output,
+    BulletOuCudaCppF32Buffer* qat_l1w, BulletOuCudaCppF32Buffer* qat_l1b, int refresh_qat_l1) {
+    (void)factorizer_king_axis_dim;
+    (void)factorizer_hand_axis_dim;
+    (void)factorizer_king_axis_alpha;
+    (void)factorizer_hand_axis_alpha;
+    (void)factorizer_progress_axis_alpha;
+    (void)factorizer_pair_alpha;
+    (void)l1axw;
+    (void)l1axb;
+    (void)l2axw;
+    (void)l2axb;
+    (void)l3axw;
+    (void)l3axb;
+    (void)refresh_qat_l1;
+    if (reject_unsupported(l1_group_count, l1_common_size, l1_shard_size, has_l1ax, has_l2ax, has_l3ax, use_king_axis,
+                           use_hand_axis, use_progress_axis, use_king_hand_pair, use_king_progress_pair,
+                           use_hand_progress_pair, residual_count_gates, factorizer_axis_confidences) != 0)
+        return -1;
+    if (qat_l1w != nullptr || qat_l1b != nullptr)
+        return fail_message("unsupported on this backend: L1 QAT scratch in the reference forward entry");
+    SfnnDims d{};
+    if (sfnn_dims(input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks, batch, max_active, ft_factorizer_alpha,
+                  factorizer_shared_alpha, &d) != 0)
+        return -1;
+    d.has_l1f = has_l1f ? 1 : 0;
+    d.has_l2f = has_l2f ? 1 : 0;
+    d.has_l3f = has_l3f ? 1 : 0;
+    if ((!has_l1f && (l1fw || l1fb)) || (!has_l2f && (l2fw || l2fb)) || (!has_l3f && (l3fw || l3fb)))
+        return fail_message("sfnn shared factor buffers must be null when their has_* flag is false");
+    const BulletOuCudaCppF32Buffer* params[14] = {l0w, l0b, l1w, l1b, l1fw, l1fb, l2w,
+                                                  l2b, l2fw, l2fb, l3w, l3b, l3fw, l3fb};
+    const size_t BW = batch * ft_size;
+    if (validate_i32(ctx, stm_indices, batch * max_active, "stm_indices") != 0 ||
+        validate_i32(ctx, nstm_indices, batch * max_active, "nstm_indices") != 0 ||
+        validate_i32(ctx, buckets, batch, "buckets") != 0 || validate_sfnn_weights(ctx, d, params, "sfnn") != 0 ||
+        validate_f32(ctx, stm_l0, BW, "sfnn stm_l0") != 0 || validate_f32(ctx, nstm_l0, BW, "sfnn nstm_l0") != 0 ||
+        validate_f32(ctx, combined, BW, "sfnn combined") != 0 ||
+        validate_f32(ctx, l1, batch * d.l1_out, "sfnn l1") != 0 ||
+        validate_f32(ctx, l2_input, batch * d.l2_in, "sfnn l2_input") != 0 ||
+        validate_f32(ctx, l2, batch * l2_size, "sfnn l2") != 0 || validate_f32(ctx, output, batch, "sfnn output") != 0)
+        return -1;
+    if (folded_l0w != nullptr && validate_f32(ctx, folded_l0w, input_size * ft_size, "sfnn folded_l0w scratch") != 0)
+        return -1;
+    if (set_device(ctx) != 0) return -1;
+    const SfnnWeights w = weights_from(params);
+    SfnnPlan plan{};
+    if (sfnn_prepare(ctx, d, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr,
+                     folded_l0w != nullptr ? folded_l0w->ptr : nullptr, &plan) != 0)
+        return -1;
+    const SfnnActivations act{stm_l0->ptr, nstm_l0->ptr, combined->ptr, l1->ptr, l2_input->ptr, l2->ptr, output->ptr};
+    if (launch_ft_forward(ctx, d, plan, stm_indices->ptr, nstm_indices->ptr, w.l0b, act) != 0) return -1;
+    if (launch_l1_forward(ctx, d, w, plan, act.combined, act.l1) != 0) return -1;
+    HeadArgs h = head_args(d, w, plan, act);
+    h.mode = kHeadForward;
+    if (launch_head(ctx, d, h) != 0) return -1;
+    return ok();
+}
+
+int bulletou_cuda_cpp_sfnn_backward_train_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip, size_t l2_size,
+    size_t num_stacks, size_t l1_group_count, size_t l1_common_size, size_t l1_shard_size,
+    size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* stm_l0,
+    const BulletOuCudaCppF32Buffer* nstm_l0, const BulletOuCudaCppF32Buffer* combined,
+    const BulletOuCudaCppF32Buffer* l1, const BulletOuCudaCppF32Buffer* l2_input, const BulletOuCudaCppF32Buffer* l2,
+    const BulletOuCudaCppF32Buffer* l1w, const BulletOuCudaCppF32Buffer* qat_l1w, const BulletOuCudaCppF32Buffer* l1fw,
+    int has_l1f, const BulletOuCudaCppF32Buffer* l1axw, int has_l1ax, const BulletOuCudaCppF32Buffer* l2w,
+    const BulletOuCudaCppF32Buffer* l2fw, int has_l2f, const BulletOuCudaCppF32Buffer* l2axw, int has_l2ax,
+    const BulletOuCudaCppF32Buffer* l3w, const BulletOuCudaCppF32Buffer* l3fw, int has_l3f,
+    const BulletOuCudaCppF32Buffer* l3axw, int has_l3ax, int use_king_axis, int use_hand_axis, int use_progress_axis,
+    int use_king_hand_pair, int use_king_progress_pair, int use_hand_progress_pair, float ft_factorizer_alpha,
+    float factorizer_shared_alpha, float factorizer_king_axis_alpha, float factorizer_hand_axis_alpha,
+    float factorizer_progress_axis_alpha, float factorizer_pair_alpha,
+    const BulletOuCudaCppF32Buffer* residual_count_gates, const BulletOuCudaCppF32Buffer* factorizer_axis_confidences,
+    const BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* l2_gradients,
+    BulletOuCudaCppF32Buffer* l1_gradients, BulletOuCudaCppF32Buffer* l2_input_gradients,
+    BulletOuCudaCppF32Buffer* combined_gradients, BulletOuCudaCppF32Buffer* stm_l0_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_gradients, BulletOuCudaCppF32Buffer* stm_l0_pre_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_pre_gradients, BulletOuCudaCppF32Buffer* l0w_gradients,
+    BulletOuCudaCppF32Buffer* l0b_gradients, BulletOuCudaCppF32Buffer* l1w_gradients,
+    BulletOuCudaCppF32Buffer* l1b_gradients, BulletOuCudaCppF32Buffer* l1fw_gradients,
+    BulletOuCudaCppF32Buffer* l1fb_gradients, BulletOuCudaCppF32Buffer* l1axw_gradients,
+    BulletOuCudaCppF32Buffer* l1axb_gradients, BulletOuCudaCppF32Buffer* l2w_gradients,
+    BulletOuCudaCppF32Buffer* l2b_gradients, BulletOuCudaCppF32Buffer* l2fw_gradients,
+    BulletOuCudaCppF32Buffer* l2fb_gradients, BulletOuCudaCppF32Buffer* l2axw_gradients,
+    BulletOuCudaCppF32Buffer* l2axb_gradients, BulletOuCudaCppF32Buffer* l3w_gradients,
+    BulletOuCudaCppF32Buffer* l3b_gradients, BulletOuCudaCppF32Buffer* l3fw_gradients,
+    BulletOuCudaCppF32Buffer* l3fb_gradients, BulletOuCudaCppF32Buffer* l3axw_gradients,
+    BulletOuCudaCppF32Buffer* l3axb_gradients, int zero_parameter_gradients, BulletOuCudaCppF32Buffer* entry_weights) {
+    (void)factorizer_king_axis_dim;
+    (void)factorizer_hand_axis_dim;
+    (void)factorizer_king_axis_alpha;
+    (void)factorizer_hand_axis_alpha;
+    (void)factorizer_progress_axis_alpha;
+    (void)factorizer_pair_alpha;
+    (void)l1axw;
+    (void)l2axw;
+    (void)l3axw;
+    (void)l1axw_gradients;
+    (void)l1axb_gradients;
+    (void)l2axw_gradients;
+    (void)l2axb_gradients;
+    (void)l3axw_gradients;
+    (void)l3axb_gradients;
+    (void)combined;
+    if (reject_unsupported(l1_group_count, l1_common_size, l1_shard_size, has_l1ax, has_l2ax, has_l3ax, use_king_axis,
+                           use_hand_axis, use_progress_axis, use_king_hand_pair, use_king_progress_pair,
+                           use_hand_progress_pair, residual_count_gates, factorizer_axis_confidences) != 0)
+        return -1;
+    if (qat_l1w != nullptr)
+        return fail_message("unsupported on this backend: L1 QAT weights in the reference backward entry");
+    SfnnDims d{};
+    if (sfnn_dims(input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks, batch, max_active, ft_factorizer_alpha,
+                  factorizer_shared_alpha, &d) != 0)
+        return -1;
+    d.has_l1f = has_l1f ? 1 : 0;
+    d.has_l2f = has_l2f ? 1 : 0;
+    d.has_l3f = has_l3f ? 1 : 0;
+    const SfnnGroupLayout g = sfnn_group_layout(d);
+    const size_t BW = batch * ft_size;
+    BulletOuCudaCppF32Buffer* grads[kSfGroups] = {l0b_gradients,
+                                                  l1w_gradients,
+                                                  l1b_gradients,
+                                                  has_l1f ? l1fw_gradients : nullptr,
+                                                  has_l1f ? l1fb_gradients : nullptr,
+                                                  l2w_gradients,
+                                                  l2b_gradients,
+                                                  has_l2f ? l2fw_gradients : nullptr,
+                                                  has_l2f ? l2fb_gradients : nullptr,
+                                                  l3w_gradients,
+                                                  l3b_gradients,
+                                                  has_l3f ? l3fw_gradients : nullptr,
+                                                  has_l3f ? l3fb_gradients : nullptr};
+    static const char* gnames[kSfGroups] = {"l0b_gradients", "l1w_gradients", "l1b_gradients", "l1fw_gradients",
+                                            "l1fb_gradients", "l2w_gradients", "l2b_gradients", "l2fw_gradients",
+                                            "l2fb_gradients", "l3w_gradients", "l3b_gradients", "l3fw_gradients",
+                                            "l3fb_gradients"};
+    for (int k = 0; k < kSfGroups; ++k)
+        if (g.len[k] && validate_f32(ctx, grads[k], g.len[k], gnames[k]) != 0) return -1;
+    if (validate_i32(ctx, stm_indices, batch * max_active, "stm_indices") != 0 ||
+        validate_i32(ctx, nstm_indices, batch * max_active, "nstm_indices") != 0 ||
+        validate_i32(ctx, buckets, batch, "buckets") != 0 || validate_f32(ctx, stm_l0, BW, "sfnn stm_l0") != 0 ||
+        validate_f32(ctx, nstm_l0, BW, "sfnn nstm_l0") != 0 ||
+        validate_f32(ctx, l1, batch * d.l1_out, "sfnn l1") != 0 ||
+        validate_f32(ctx, l2_input, batch * d.l2_in, "sfnn l2_input") != 0 ||
+        validate_f32(ctx, l2, batch * l2_size, "sfnn l2") != 0 ||
+        validate_f32(ctx, l1w, g.len[kSfL1w], "sfnn l1w") != 0 || validate_f32(ctx, l2w, g.len[kSfL2w], "sfnn l2w") != 0 ||
+        validate_f32(ctx, l3w, g.len[kSfL3w], "sfnn l3w") != 0 ||
+        (has_l1f && validate_f32(ctx, l1fw, g.len[kSfL1fw], "sfnn l1fw") != 0) ||
+        (has_l2f && validate_f32(ctx, l2fw, g.len[kSfL2fw], "sfnn l2fw") != 0) ||
+        (has_l3f && validate_f32(ctx, l3fw, g.len[kSfL3fw], "sfnn l3fw") != 0) ||
+        validate_f32(ctx, mean_output_gradients, batch, "mean_output_gradients") != 0 ||
+        validate_f32(ctx, l2_gradients, batch * l2_size, "l2_gradients") != 0 ||
+        validate_f32(ctx, l1_gradients, batch * d.l1_out, "l1_gradients") != 0 ||
+        validate_f32(ctx, l2_input_gradients, batch * d.l2_in, "l2_input_gradients") != 0 ||
+        validate_f32(ctx, combined_gradients, BW, "combined_gradients") != 0 ||
+        validate_f32(ctx, stm_l0_gradients, BW, "stm_l0_gradients") != 0 ||
+        validate_f32(ctx, nstm_l0_gradients, BW, "nstm_l0_gradients") != 0 ||
+        validate_f32(ctx, stm_l0_pre_gradients, BW, "stm_l0_pre_gradients") != 0 ||
+        validate_f32(ctx, nstm_l0_pre_gradients, BW, "nstm_l0_pre_gradients") != 0 ||
+        validate_f32(ctx, l0w_gradients, input_size * ft_size, "l0w_gradients") != 0)
+        return -1;
+    if (entry_weights != nullptr && validate_f32(ctx, entry_weights, batch, "backward entry weights") != 0) return -1;
+    if (set_device(ctx) != 0) return -1;
+    if (zero_parameter_gradients) {
+        cudaError_t st = cudaMemsetAsync(l0w_gradients->ptr, 0, l0w_gradients->len * sizeof(float), ctx->stream);
+        for (int k = 0; k < kSfGroups && st == cudaSuccess; ++k)
+            if (g.len[k]) st = cudaMemsetAsync(grads[k]->ptr, 0, g.len[k] * sizeof(float), ctx->stream);
+        if (st != cudaSuccess) return fail("cudaMemsetAsync SFNN gradients", st);
+    }
+    // The backward reads only the L1 / L2 / L3 weights (and their shared
+    // factors); the FT table is not needed, so nothing is folded.
+    const SfnnWeights w{nullptr,  nullptr, l1w->ptr, nullptr, has_l1f ? l1fw->ptr : nullptr, nullptr,
+                        l2w->ptr, nullptr, has_l2f ? l2fw->ptr : nullptr, nullptr,
+                        l3w->ptr, nullptr, has_l3f ? l3fw->ptr : nullptr, nullptr};
+    SfnnPlan plan{};
+    SfnnDims dn = d;
+    dn.base = 0;
+    if (sfnn_prepare(ctx, dn, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr, nullptr, &plan) != 0) return -1;
+    SfnnActivations act{const_cast<float*>(stm_l0->ptr), const_cast<float*>(nstm_l0->ptr), nullptr,
+                        const_cast<float*>(l1->ptr),     const_cast<float*>(l2_input->ptr),
+                        const_cast<float*>(l2->ptr),     nullptr};
+    HeadArgs h = head_args(d, w, plan, act);
+    h.mode = kHeadBackward;
+    h.mog = const_cast<float*>(mean_output_gradients->ptr);
+    h.g1 = l1_gradients->ptr;
+    h.l2_gradients = l2_gradients->ptr;
+    h.l2_input_gradients = l2_input_gradients->ptr;
+    plan.g1 = l1_gradients->ptr;
+    if (launch_head(ctx, d, h) != 0) return -1;
+    L1BackArgs lb{};
+    lb.l0[0] = stm_l0->ptr;
+    lb.l0[1] = nstm_l0->ptr;
+    lb.combined_gradients = combined_gradients->ptr;
+    lb.l0_gradients[0] = stm_l0_gradients->ptr;
+    lb.l0_gradients[1] = nstm_l0_gradients->ptr;
+    lb.pre_gradients[0] = stm_l0_pre_gradients->ptr;
+    lb.pre_gradients[1] = nstm_l0_pre_gradients->ptr;
+    if (launch_l1_backward(ctx, d, plan, lb) != 0) return -1;
+    FinalArgs f{};
+    for (int k = 0; k < kSfGroups; ++k) f.dst[k] = g.len[k] ? grads[k]->ptr : nullptr;
+    f.accumulate = 1;
+    if (launch_finalize(ctx, d, plan, f) != 0) return -1;
+    InverseIndex index;
+    if (build_inverse_index_rows(ctx, stm_indices->ptr, nstm_indices->ptr, d.batch, d.max_active, d.n_features, &index,
+                                 nullptr) != 0)
+        return -1;
+    PieceRowArgs r = piece_row_args(d, index);
+    r.src[0] = stm_l0_pre_gradients->ptr;
+    r.src[1] = nstm_l0_pre_gradients->ptr;
+    r.src_stride = ft_size;
+    r.gradients = l0w_gradients->ptr;
+    if (launch_piece_rows(ctx, kRowAccumulate, r) != 0) return -1;
+    return ok();
+}
+
+int bulletou_b200_sfnn_train_step_device(
+    BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* targets,
+    const BulletOuCudaCppF32Buffer* entry_weights, const BulletOuB200LossSpec* loss,
+    const BulletOuB200RangerStep* ranger, BulletOuCudaCppF32Buffer* const* params,
+    BulletOuCudaCppF32Buffer* const* momentum, BulletOuCudaCppF32Buffer* const* velocity,
+    BulletOuCudaCppF32Buffer* const* slow_params, BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean) {
+    if (shape == nullptr) return fail_message("SFNN shape must not be null");
+    if (ranger == nullptr) return fail_message("ranger step must not be null");
+    if (params == nullptr || momentum == nullptr || velocity == nullptr || slow_params == nullptr)
+        return fail_message("SFNN parameter / optimizer-state arrays must not be null");
+    if (ranger->norm_loss_rate != 0.0f)
+        return fail_message("SFNN fused step: the SFNN runner applies no norm loss with default multipliers; pass 0");
+    SfnnDims d{};
+    LossArgs la{};
+    if (sfnn_dims(shape->input_size, shape->ft_size, shape->l1_hidden, shape->l1_skip, shape->l2_size,
+                  shape->num_stacks, batch, max_active, shape->ft_factorizer_alpha, shape->factorizer_shared_alpha,
+                  &d) != 0 ||
+        loss_args(loss, batch, &la) != 0)
+        return -1;
+    d.has_l1f = params[4] != nullptr;
+    d.has_l2f = params[8] != nullptr;
+    d.has_l3f = params[12] != nullptr;
+    if (validate_sfnn_weights(ctx, d, params, "params") != 0 || validate_sfnn_weights(ctx, d, momentum, "momentum") != 0 ||
+        validate_sfnn_weights(ctx, d, velocity, "velocity") != 0 ||
+        validate_sfnn_weights(ctx, d, slow_params, "slow_params") != 0 ||
+        validate_i32(ctx, stm_indices, batch * max_active, "stm_indices") != 0 ||
+        validate_i32(ctx, nstm_indices, batch * max_active, "nstm_indices") != 0 ||
+        validate_i32(ctx, buckets, batch, "buckets") != 0 || validate_f32(ctx, targets, batch, "targets") != 0 ||
+        validate_f32(ctx, entry_weights, batch, "entry_weights") != 0 ||
+        validate_f32(ctx, output, batch, "output") != 0 || validate_f32(ctx, per_sample, batch, "per_sample") != 0 ||
+        validate_f32(ctx, mean_output_gradients, batch, "mean_output_gradients") != 0 ||
+        validate_f32(ctx, weighted_sum, 1, "weighted_sum") != 0 || validate_f32(ctx, mean, 1, "mean") != 0)
+        return -1;
+    if (set_device(ctx) != 0) return -1;
+    float* wm[14];
+    float* mm[14];
+    float* vm[14];
+    float* smm[14];
+    for (int i = 0; i < 14; ++i) {
+        wm[i] = params[i] ? params[i]->ptr : nullptr;
+        mm[i] = momentum[i] ? momentum[i]->ptr : nullptr;
+        vm[i] = velocity[i] ? velocity[i]->ptr : nullptr;
+        smm[i] = slow_params[i] ? slow_params[i]->ptr : nullptr;
+    }
+    const SfnnWeights w = weights_from(params);
+    if (sfnn_step(ctx, d, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr, targets->ptr, entry_weights->ptr, la,
+                  loss->finalize_loss, ranger, wm, mm, vm, smm, output->ptr, per_sample->ptr,
+                  mean_output_gradients->ptr, weighted_sum->ptr, mean->ptr, nullptr, nullptr) != 0)
+        return -1;
+    return ok();
+}
+
+}  // extern "C"

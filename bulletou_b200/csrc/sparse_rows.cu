@@ -104,13 +104,15 @@ __global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const int* __r
 // count array needs no clearing between steps).
 __global__ void fill_rows_kernel(const int* __restrict__ stm, const int* __restrict__ nstm, size_t slots,
                                  size_t max_active, RowMap map, const int* __restrict__ offsets,
-                                 int* __restrict__ cursor, int* __restrict__ entries) {
+                                 int* __restrict__ cursor, int* __restrict__ entries,
+                                 const int* __restrict__ entry_rank) {
     const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t >= 2 * slots) return;
     const int persp = t < slots ? 0 : 1;
     const size_t s = persp == 0 ? t : t - slots;
     const int f = persp == 0 ? stm[s] : nstm[s];
-    const int entry = static_cast<int>((s / max_active) * 2 + persp);
+    const int h = static_cast<int>((s / max_active) * 2 + persp);
+    const int entry = entry_rank != nullptr ? entry_rank[h] : h;
     int r0, r1;
     const int n = map.rows(f, &r0, &r1);
     if (n >= 1) entries[offsets[r0] + atomicSub(&cursor[r0], 1) - 1] = entry;
@@ -322,9 +324,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
-                        size_t max_active, size_t input_size, size_t n_rows, InverseIndex* out) {
-    const RowMap map = make_row_map(input_size);
+namespace {
+
+int build_index_impl(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch, size_t max_active,
+                     const RowMap& map, size_t n_rows, InverseIndex* out, const int* entry_rank) {
     const size_t slots = batch * max_active;
     const size_t max_entries = 2 * slots * (map.factorized ? 2 : 1);
     if (n_rows >= static_cast<size_t>(INT_MAX) - kScanTile || max_entries >= static_cast<size_t>(INT_MAX) ||
@@ -360,7 +363,7 @@ int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* 
     if (check_launch("sparse scan launch") != 0) return -1;
     if (blocks > 0) {
         fill_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, max_active, map, o, c,
-                                                             static_cast<int*>(entries));
+                                                             static_cast<int*>(entries), entry_rank);
         if (check_launch("sparse fill launch") != 0) return -1;
     }
     out->offsets = o;
@@ -369,6 +372,22 @@ int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* 
     out->n_rows = n;
     out->capacity = max_entries;
     return 0;
+}
+
+}  // namespace
+
+int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
+                        size_t max_active, size_t input_size, size_t n_rows, InverseIndex* out,
+                        const int* entry_rank) {
+    return build_index_impl(ctx, stm, nstm, batch, max_active, make_row_map(input_size), n_rows, out, entry_rank);
+}
+
+int build_inverse_index_rows(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
+                             size_t max_active, size_t n_features, InverseIndex* out, const int* entry_rank) {
+    RowMap map;
+    map.input_size = static_cast<int>(n_features);
+    map.factorized = 0;
+    return build_index_impl(ctx, stm, nstm, batch, max_active, map, n_features, out, entry_rank);
 }
 
 int launch_row_kernel(BulletOuCudaCppContext* ctx, int mode, const RowKernelArgs& args, int rows_to_process) {

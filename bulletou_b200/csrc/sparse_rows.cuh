@@ -57,9 +57,16 @@ struct InverseIndex {
 };
 
 // Builds the index for `batch` samples x `max_active` slots x 2 perspectives
-// into context scratch.  Enqueued on ctx->stream.
+// into context scratch.  Enqueued on ctx->stream.  Entry ids are
+// h = 2*sample + perspective, or entry_rank[h] when entry_rank is given (the
+// position of h in a permuted layout of the gradient rows).
 int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
-                        size_t max_active, size_t input_size, size_t n_rows, InverseIndex* out);
+                        size_t max_active, size_t input_size, size_t n_rows, InverseIndex* out,
+                        const int* entry_rank = nullptr);
+
+// Same, for a plain table: every feature id in [0, n_features) is its own row.
+int build_inverse_index_rows(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
+                             size_t max_active, size_t n_features, InverseIndex* out, const int* entry_rank);
 
 // Parameters of the per-row consumer kernels.
 struct RowGradientSource {

@@ -1,0 +1,475 @@
+"""SFNN LayerStack part of the cuda-cpp crate mirror (crates/cuda_cpp/src/lib.rs).
+
+``SfnnForwardShape`` (lib.rs:928-1056), ``SfnnFactorizerAlpha`` (lib.rs:1280),
+``SfnnForwardHostWeights`` (lib.rs:1405), ``SfnnTrainStepHostBatch``
+(lib.rs:6027), the forward / backward entry points (lib.rs:2014-2253,
+3462-4090) and ``SfnnTrainStepRunner`` (lib.rs:6187-7960) with default layer
+multipliers and the FT / shared-L1 factorizers.
+
+Bound to the product library the runner issues one fused call per step
+(bulletou_b200_sfnn_train_step_device); bound to the reference backend it
+issues the reference runner's call sequence: forward with the gradient
+buffer as fold scratch (then cleared, lib.rs:2078-2084), loss, training
+backward, and Ranger over every group in update order (lib.rs:8425-8730).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, replace
+from typing import Optional
+
+import numpy as np
+
+from ._lib import CudaCppError, SfnnShape
+from .cuda_cpp import (FLT_MAX, Context, Event, F32Buffer, I32Buffer, PinnedF32Buffer, PinnedI32Buffer,
+                       RangerDeviceState, RangerParamState, RangerUpdateParams, ScalarLossKind, ScalarLossReadback,
+                       ScalarLossWorkspace, ranger_update_device, scalar_loss_device)
+
+HALFKA_HM2_DIMENSIONS = 73305
+HALFKA2_DIMENSIONS = 131949
+PIECE_INPUTS = 1629
+SFNN_WEIGHT_NAMES = ("l0w", "l0b", "l1w", "l1b", "l1fw", "l1fb", "l2w", "l2b", "l2fw", "l2fb", "l3w", "l3b", "l3fw",
+                     "l3fb")
+SHARED_NAMES = ("l1fw", "l1fb", "l2fw", "l2fb", "l3fw", "l3fb")
+
+
+@dataclass(frozen=True)
+class SfnnForwardShape:
+    """Dense-L1 SFNN shape (lib.rs:928-1056); grouped / common+shard L1 and the
+    bucket-axis factorizers are not supported by this backend."""
+
+    input_size: int
+    ft_size: int
+    l1_hidden: int
+    l1_skip: bool
+    l2_size: int
+    num_stacks: int
+
+    @property
+    def l1_out(self) -> int:
+        return self.l1_hidden + int(self.l1_skip)
+
+    @property
+    def l2_in(self) -> int:
+        return 2 * self.l1_hidden
+
+    @property
+    def pairwise_size(self) -> int:
+        return self.ft_size // 2
+
+    def factorized_base(self) -> int:
+        """cu:1180-1184: input_size = base + 1629 virtual piece rows."""
+        return {HALFKA_HM2_DIMENSIONS + PIECE_INPUTS: HALFKA_HM2_DIMENSIONS,
+                HALFKA2_DIMENSIONS + PIECE_INPUTS: HALFKA2_DIMENSIONS}.get(self.input_size, 0)
+
+    def weight_lengths(self) -> dict:
+        W, O, L2, I2, S = self.ft_size, self.l1_out, self.l2_size, self.l2_in, self.num_stacks
+        return {"l0w": self.input_size * W, "l0b": W, "l1w": S * O * W, "l1b": S * O, "l1fw": W * O, "l1fb": O,
+                "l2w": S * L2 * I2, "l2b": S * L2, "l2fw": L2 * I2, "l2fb": L2, "l3w": S * L2, "l3b": S,
+                "l3fw": L2, "l3fb": 1}
+
+    def as_tuple(self) -> tuple:
+        return (self.input_size, self.ft_size, self.l1_hidden, int(self.l1_skip), self.l2_size, self.num_stacks)
+
+    def validate(self) -> None:
+        if min(self.input_size, self.ft_size, self.l1_hidden, self.l2_size, self.num_stacks) <= 0:
+            raise CudaCppError("invalid SFNN shape: every dimension must be > 0")
+        if self.ft_size % 2 != 0:
+            raise CudaCppError(f"invalid SFNN shape: ft_size must be even, got {self.ft_size}")
+
+
+# SFNN_halfkahm2_1536_15_32_k3k3 with the FT factorizer (docs/en/shogi/sfnn-1536.md:27-57)
+SFNN_HALFKA_HM2_1536_15_32_K3K3 = SfnnForwardShape(HALFKA_HM2_DIMENSIONS + PIECE_INPUTS, 1536, 15, True, 32, 9)
+
+
+@dataclass(frozen=True)
+class SfnnFactorizerAlpha:
+    """lib.rs:1280-1312 (ft and shared coefficients; axis terms unsupported)."""
+
+    ft: float = 1.0
+    shared: float = 1.0
+
+    def validate(self) -> None:
+        if not (np.isfinite(self.ft) and 0.0 <= self.ft <= 100.0):
+            raise CudaCppError("SFNN FT factorizer alpha must be in [0, 100]")
+        if not (np.isfinite(self.shared) and 0.0 <= self.shared <= 10.0):
+            raise CudaCppError("SFNN shared factorizer alpha must be in [0, 10]")
+
+
+@dataclass
+class SfnnForwardHostWeights:
+    shape: SfnnForwardShape
+    l0w: np.ndarray
+    l0b: np.ndarray
+    l1w: np.ndarray
+    l1b: np.ndarray
+    l2w: np.ndarray
+    l2b: np.ndarray
+    l3w: np.ndarray
+    l3b: np.ndarray
+    l1fw: Optional[np.ndarray] = None
+    l1fb: Optional[np.ndarray] = None
+    l2fw: Optional[np.ndarray] = None
+    l2fb: Optional[np.ndarray] = None
+    l3fw: Optional[np.ndarray] = None
+    l3fb: Optional[np.ndarray] = None
+
+    def arrays(self) -> dict:
+        return {n: (None if getattr(self, n) is None else np.ascontiguousarray(getattr(self, n), np.float32).reshape(-1))
+                for n in SFNN_WEIGHT_NAMES}
+
+    def validate(self) -> None:
+        self.shape.validate()
+        lens = self.shape.weight_lengths()
+        for a, b in (("l1fw", "l1fb"), ("l2fw", "l2fb"), ("l3fw", "l3fb")):
+            if (getattr(self, a) is None) != (getattr(self, b) is None):
+                raise CudaCppError(f"SFNN factorized state is partial: {a}/{b}")
+        for n, a in self.arrays().items():
+            if a is not None and a.size != lens[n]:
+                raise CudaCppError(f"weight length mismatch for {n}: expected {lens[n]}, got {a.size}")
+
+
+@dataclass
+class SfnnTrainStepHostBatch:
+    stm_indices: np.ndarray
+    nstm_indices: np.ndarray
+    buckets: np.ndarray
+    targets: np.ndarray
+    entry_weights: np.ndarray
+    batch_size: int
+    max_active: int
+
+    def validate(self) -> None:
+        n = self.batch_size * self.max_active
+        if np.asarray(self.stm_indices).size != n or np.asarray(self.nstm_indices).size != n:
+            raise CudaCppError("SFNN batch: sparse index length mismatch")
+        for name in ("buckets", "targets", "entry_weights"):
+            if np.asarray(getattr(self, name)).size != self.batch_size:
+                raise CudaCppError(f"SFNN batch: {name} length mismatch")
+
+
+class SfnnForwardWorkspace:
+    """lib.rs:1936-2012."""
+
+    def __init__(self, ctx: Context, shape: SfnnForwardShape, batch_size: int):
+        W = shape.ft_size
+        self.layout = (shape, batch_size)
+        self.stm_l0 = F32Buffer(ctx, batch_size * W)
+        self.nstm_l0 = F32Buffer(ctx, batch_size * W)
+        self.combined = F32Buffer(ctx, batch_size * W)
+        self.l1 = F32Buffer(ctx, batch_size * shape.l1_out)
+        self.l2_input = F32Buffer(ctx, batch_size * shape.l2_in)
+        self.l2 = F32Buffer(ctx, batch_size * shape.l2_size)
+        self.output = F32Buffer(ctx, batch_size)
+
+    def download(self, ctx: Optional[Context] = None) -> dict:
+        return {k: getattr(self, k).download(ctx) for k in ("stm_l0", "nstm_l0", "combined", "l1", "l2_input", "l2",
+                                                              "output")}
+
+
+class SfnnBackwardWorkspace:
+    """Activation gradients plus one gradient buffer per present parameter group."""
+
+    INTERMEDIATE = ("l2_gradients", "l1_gradients", "l2_input_gradients", "combined_gradients", "stm_l0_gradients",
+                    "nstm_l0_gradients", "stm_l0_pre_gradients", "nstm_l0_pre_gradients")
+
+    def __init__(self, ctx: Context, shape: SfnnForwardShape, batch_size: int, present: dict):
+        W = shape.ft_size
+        sizes = {"l2_gradients": batch_size * shape.l2_size, "l1_gradients": batch_size * shape.l1_out,
+                 "l2_input_gradients": batch_size * shape.l2_in}
+        for k in self.INTERMEDIATE:
+            setattr(self, k, F32Buffer(ctx, sizes.get(k, batch_size * W)))
+        lens = shape.weight_lengths()
+        self.params = {}
+        for n in SFNN_WEIGHT_NAMES:
+            if present[n]:
+                b = F32Buffer(ctx, lens[n])
+                b.fill(0.0)
+                self.params[n] = b
+            else:
+                self.params[n] = None
+
+    def zero_parameter_gradients(self, ctx: Optional[Context] = None) -> None:
+        for b in self.params.values():
+            if b is not None:
+                b.fill(0.0, ctx)
+
+    def download(self, ctx: Optional[Context] = None) -> dict:
+        out = {k: getattr(self, k).download(ctx) for k in self.INTERMEDIATE}
+        out.update({f"{n}_gradients": b.download(ctx) for n, b in self.params.items() if b is not None})
+        return out
+
+
+def _p(b: Optional[F32Buffer]):
+    return None if b is None else b.as_ptr()
+
+
+def sfnn_forward_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int, stm: I32Buffer,
+                        nstm: I32Buffer, buckets: I32Buffer, weights: dict, ws: SfnnForwardWorkspace,
+                        alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
+                        folded_l0w: Optional[F32Buffer] = None) -> None:
+    """bulletou_cuda_cpp_sfnn_forward_device (lib.rs:2033-2253 argument order)."""
+    w = weights
+    has = [int(w[n] is not None) for n in ("l1fw", "l2fw", "l3fw")]
+    ctx.lib.call(
+        "bulletou_cuda_cpp_sfnn_forward_device", ctx.as_ptr(), shape.input_size, shape.ft_size, shape.l1_hidden,
+        int(shape.l1_skip), shape.l2_size, shape.num_stacks, 1, 0, 0, 0, 0, batch_size, max_active, stm.as_ptr(),
+        nstm.as_ptr(), buckets.as_ptr(), _p(w["l0w"]), _p(folded_l0w), _p(w["l0b"]), _p(w["l1w"]), _p(w["l1b"]),
+        _p(w["l1fw"]), _p(w["l1fb"]), has[0], None, None, 0, _p(w["l2w"]), _p(w["l2b"]), _p(w["l2fw"]),
+        _p(w["l2fb"]), has[1], None, None, 0, _p(w["l3w"]), _p(w["l3b"]), _p(w["l3fw"]), _p(w["l3fb"]), has[2], None,
+        None, 0, 0, 0, 0, 0, 0, 0, alpha.ft, alpha.shared, 1.0, 1.0, 1.0, 1.0, None, None, ws.stm_l0.as_ptr(),
+        ws.nstm_l0.as_ptr(), ws.combined.as_ptr(), ws.l1.as_ptr(), ws.l2_input.as_ptr(), ws.l2.as_ptr(),
+        ws.output.as_ptr(), None, None, 0)
+
+
+def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int,
+                               stm: I32Buffer, nstm: I32Buffer, buckets: I32Buffer, weights: dict,
+                               fws: SfnnForwardWorkspace, mean_output_gradients: F32Buffer,
+                               bws: SfnnBackwardWorkspace, alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
+                               zero_parameter_gradients: bool = False,
+                               entry_weights: Optional[F32Buffer] = None) -> None:
+    """bulletou_cuda_cpp_sfnn_backward_train_device (lib.rs:3529-4090 argument order)."""
+    w, g = weights, bws.params
+    has = [int(w[n] is not None) for n in ("l1fw", "l2fw", "l3fw")]
+    ctx.lib.call(
+        "bulletou_cuda_cpp_sfnn_backward_train_device", ctx.as_ptr(), shape.input_size, shape.ft_size,
+        shape.l1_hidden, int(shape.l1_skip), shape.l2_size, shape.num_stacks, 1, 0, 0, 0, 0, batch_size, max_active,
+        stm.as_ptr(), nstm.as_ptr(), buckets.as_ptr(), fws.stm_l0.as_ptr(), fws.nstm_l0.as_ptr(),
+        fws.combined.as_ptr(), fws.l1.as_ptr(), fws.l2_input.as_ptr(), fws.l2.as_ptr(), _p(w["l1w"]), None,
+        _p(w["l1fw"]), has[0], None, 0, _p(w["l2w"]), _p(w["l2fw"]), has[1], None, 0, _p(w["l3w"]), _p(w["l3fw"]),
+        has[2], None, 0, 0, 0, 0, 0, 0, 0, alpha.ft, alpha.shared, 1.0, 1.0, 1.0, 1.0, None, None,
+        mean_output_gradients.as_ptr(), *[getattr(bws, k).as_ptr() for k in bws.INTERMEDIATE], _p(g["l0w"]),
+        _p(g["l0b"]), _p(g["l1w"]), _p(g["l1b"]), _p(g["l1fw"]), _p(g["l1fb"]), None, None, _p(g["l2w"]),
+        _p(g["l2b"]), _p(g["l2fw"]), _p(g["l2fb"]), None, None, _p(g["l3w"]), _p(g["l3b"]), _p(g["l3fw"]),
+        _p(g["l3fb"]), None, None, int(zero_parameter_gradients), _p(entry_weights))
+
+
+def factor_contribution_clip(params: RangerUpdateParams, alpha: float) -> RangerUpdateParams:
+    """lib.rs:8772-8788: bounds of a shared factor refer to alpha * w."""
+    r = params.radam
+    if alpha == 0.0:
+        return replace(params, radam=replace(r, min_weight=-FLT_MAX, max_weight=FLT_MAX))
+
+    def scale(bound: float) -> float:
+        if bound in (-FLT_MAX, FLT_MAX):
+            return bound
+        return float(np.float32(min(FLT_MAX, max(-FLT_MAX, float(bound) / float(alpha)))))
+
+    return replace(params, radam=replace(r, min_weight=scale(r.min_weight), max_weight=scale(r.max_weight)))
+
+
+class SfnnTrainStepUploadSlot:
+    """SfnnTrainStepUploadSlot (lib.rs:6087-6186): device batch, pinned staging,
+    upload-ready and compute-done events."""
+
+    def __init__(self, ctx: Context, batch_size: int, max_active: int):
+        n = batch_size * max_active
+        self.stm_indices, self.nstm_indices = I32Buffer(ctx, n), I32Buffer(ctx, n)
+        self.buckets = I32Buffer(ctx, batch_size)
+        self.targets, self.entry_weights = F32Buffer(ctx, batch_size), F32Buffer(ctx, batch_size)
+        self.pinned = (PinnedI32Buffer(ctx, n), PinnedI32Buffer(ctx, n), PinnedI32Buffer(ctx, batch_size),
+                       PinnedF32Buffer(ctx, batch_size), PinnedF32Buffer(ctx, batch_size))
+        self.device = (self.stm_indices, self.nstm_indices, self.buckets, self.targets, self.entry_weights)
+        self.upload_ready = Event(ctx)
+        self.compute_done = Event(ctx)
+        self.in_use = False
+
+    def fill(self, batch: SfnnTrainStepHostBatch) -> None:
+        for dst, src in zip(self.pinned, (batch.stm_indices, batch.nstm_indices, batch.buckets, batch.targets,
+                                          batch.entry_weights)):
+            np.copyto(dst.host(), np.asarray(src).reshape(-1))
+
+    def upload(self, upload_ctx: Context, batch: Optional[SfnnTrainStepHostBatch],
+               pinned_source: Optional["SfnnTrainStepUploadSlot"] = None) -> int:
+        lib = upload_ctx.lib
+        if self.in_use:
+            self.upload_ready.synchronize()
+            self.compute_done.wait(upload_ctx)
+        if not lib.has("bulletou_b200_i32_upload_pinned"):
+            if batch is None:
+                raise CudaCppError("this backend needs host batch arrays for staged uploads")
+            srcs = (batch.stm_indices, batch.nstm_indices, batch.buckets, batch.targets, batch.entry_weights)
+            for pin, dst, src in zip(self.pinned, self.device, srcs):
+                pin.upload_to_device(upload_ctx, dst, src)
+            self.upload_ready.record(upload_ctx)
+            self.in_use = True
+            return 4 * sum(x.length for x in self.pinned)
+        src = pinned_source.pinned if pinned_source is not None else self.pinned
+        if pinned_source is None:
+            self.fill(batch)
+        c = upload_ctx.as_ptr()
+        for pin, dst in zip(src, self.device):
+            name = "bulletou_b200_i32_upload_pinned" if isinstance(dst, I32Buffer) else "bulletou_b200_f32_upload_pinned"
+            lib.call(name, c, dst.as_ptr(), pin.as_ptr(), pin.length)
+        self.upload_ready.record(upload_ctx)
+        self.in_use = True
+        return 4 * sum(x.length for x in src)
+
+
+class SfnnTrainStepRunner:
+    """SFNN train-step runner (lib.rs:6187-7960), default layer multipliers."""
+
+    def __init__(self, ctx: Context, initial_weights: SfnnForwardHostWeights, batch_size: int, max_active: int,
+                 factorizer_alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(), fused: Optional[bool] = None):
+        initial_weights.validate()
+        factorizer_alpha.validate()
+        if batch_size == 0 or max_active == 0:
+            raise CudaCppError("SFNN train-step batch_size and max_active must be greater than zero")
+        self.ctx = ctx
+        self.lib = ctx.lib
+        self.shape = initial_weights.shape
+        self.alpha = factorizer_alpha
+        self.batch_size, self.max_active = batch_size, max_active
+        self.fused = self.lib.has("bulletou_b200_sfnn_train_step_device") if fused is None else bool(fused)
+        arrays = initial_weights.arrays()
+        self.present = {n: arrays[n] is not None for n in SFNN_WEIGHT_NAMES}
+        self.weights = {n: (None if a is None else F32Buffer.from_host(ctx, a)) for n, a in arrays.items()}
+        self.optimizer_states = {n: (None if a is None else RangerParamState(ctx, a)) for n, a in arrays.items()}
+        n = batch_size * max_active
+        self.stm_indices, self.nstm_indices = I32Buffer(ctx, n), I32Buffer(ctx, n)
+        self.buckets = I32Buffer(ctx, batch_size)
+        self.targets, self.entry_weights = F32Buffer(ctx, batch_size), F32Buffer(ctx, batch_size)
+        self.loss_workspace = ScalarLossWorkspace(ctx, batch_size)
+        self.forward_workspace = None
+        self.backward_workspace = None
+        self.output = F32Buffer(ctx, batch_size) if self.fused else None
+        if not self.fused:
+            self._reference_workspaces(ctx)
+        self._handles_cache = None
+        self._slots = None
+        self._next_slot = 0
+
+    def _reference_workspaces(self, ctx: Context) -> None:
+        self.forward_workspace = SfnnForwardWorkspace(ctx, self.shape, self.batch_size)
+        self.output = self.forward_workspace.output
+        self.backward_workspace = SfnnBackwardWorkspace(ctx, self.shape, self.batch_size, self.present)
+
+    # -- batch upload ------------------------------------------------------
+    def upload_batch(self, batch: SfnnTrainStepHostBatch, ctx: Optional[Context] = None) -> None:
+        batch.validate()
+        if batch.batch_size != self.batch_size or batch.max_active != self.max_active:
+            raise CudaCppError(
+                f"SFNN train-step batch layout mismatch: got batch_size={batch.batch_size} "
+                f"max_active={batch.max_active}, expected batch_size={self.batch_size} max_active={self.max_active}")
+        c = ctx or self.ctx
+        self.stm_indices.upload(batch.stm_indices, c)
+        self.nstm_indices.upload(batch.nstm_indices, c)
+        self.buckets.upload(batch.buckets, c)
+        self.targets.upload(batch.targets, c)
+        self.entry_weights.upload(batch.entry_weights, c)
+
+    # -- steps -------------------------------------------------------------
+    def step(self, ctx: Context, params: RangerUpdateParams, loss_kind: ScalarLossKind, output_inv_scale: float,
+             batch: SfnnTrainStepHostBatch) -> ScalarLossReadback:
+        self.step_no_readback(ctx, params, loss_kind, output_inv_scale, batch)
+        return self.read_loss(ctx)
+
+    def step_no_readback(self, ctx, params, loss_kind, output_inv_scale, batch) -> None:
+        self.step_no_readback_with_loss_finalize(ctx, params, loss_kind, output_inv_scale, batch, True)
+
+    def step_no_readback_with_loss_finalize(self, ctx, params, loss_kind, output_inv_scale, batch,
+                                            finalize_loss: bool) -> None:
+        self.upload_batch(batch, ctx)
+        self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
+
+    def _handles(self):
+        if self._handles_cache is None:
+            arr = ctypes.c_void_p * 14
+
+            def pack(get):
+                return arr(*[(None if self.weights[n] is None else get(n).as_ptr().value) for n in SFNN_WEIGHT_NAMES])
+
+            self._handles_cache = (pack(lambda n: self.weights[n]),
+                                   pack(lambda n: self.optimizer_states[n].momentum),
+                                   pack(lambda n: self.optimizer_states[n].velocity),
+                                   pack(lambda n: self.optimizer_states[n].slow_params))
+        return self._handles_cache
+
+    def step_device(self, ctx: Context, params: RangerUpdateParams, loss_kind: ScalarLossKind,
+                    output_inv_scale: float, finalize_loss: bool = True) -> None:
+        """One step on the batch already resident in this runner's device buffers."""
+        # With default layer multipliers the SFNN update applies no norm loss
+        # (clip_params, lib.rs:6416-6420).
+        params = replace(params, norm_loss_strength=0.0, norm_loss_before=False)
+        lw = self.loss_workspace
+        if self.fused and params.sgd_momentum is None:
+            sh = self.shape
+            shape = SfnnShape(sh.input_size, sh.ft_size, sh.l1_hidden, int(sh.l1_skip), sh.l2_size, sh.num_stacks,
+                              self.alpha.ft, self.alpha.shared)
+            spec = loss_kind.spec(output_inv_scale, finalize_loss)
+            step = params.ffi_step()
+            w, m, v, s = self._handles()
+            self.lib.call("bulletou_b200_sfnn_train_step_device", ctx.as_ptr(), ctypes.byref(shape), self.batch_size,
+                          self.max_active, self.stm_indices.as_ptr(), self.nstm_indices.as_ptr(),
+                          self.buckets.as_ptr(), self.targets.as_ptr(), self.entry_weights.as_ptr(),
+                          ctypes.byref(spec), ctypes.byref(step), w, m, v, s, self.output.as_ptr(),
+                          lw.per_sample.as_ptr(), lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(),
+                          lw.mean.as_ptr())
+            return
+        if self.forward_workspace is None:
+            self._reference_workspaces(ctx)
+        fws, bws = self.forward_workspace, self.backward_workspace
+        fold = bws.params["l0w"] if self.shape.factorized_base() else None
+        sfnn_forward_device(ctx, self.shape, self.batch_size, self.max_active, self.stm_indices, self.nstm_indices,
+                            self.buckets, self.weights, fws, self.alpha, fold)
+        if fold is not None:
+            fold.fill(0.0, ctx)  # lib.rs:2078-2084: discard the folded weights before backward adds
+        scalar_loss_device(ctx, loss_kind, output_inv_scale, self.batch_size, fws.output, self.targets,
+                           self.entry_weights, lw, finalize_loss)
+        sfnn_backward_train_device(ctx, self.shape, self.batch_size, self.max_active, self.stm_indices,
+                                   self.nstm_indices, self.buckets, self.weights, fws, lw.mean_output_gradients, bws,
+                                   self.alpha, False, self.entry_weights)
+        for n in SFNN_WEIGHT_NAMES:
+            if self.weights[n] is None:
+                continue
+            p = factor_contribution_clip(params, self.alpha.shared) if n in ("l1fw", "l1fb") else params
+            st = self.optimizer_states[n]
+            ranger_update_device(ctx, p, RangerDeviceState(bws.params[n], self.weights[n], st.momentum, st.velocity,
+                                                           st.slow_params))
+
+    # -- pipelined steps (lib.rs:7535-7720) -------------------------------
+    def upload_slots(self, count: int = 2) -> list:
+        if self._slots is None or len(self._slots) != count:
+            self._slots = [SfnnTrainStepUploadSlot(self.ctx, self.batch_size, self.max_active) for _ in range(count)]
+            self._next_slot = 0
+        return self._slots
+
+    def step_pipelined_no_readback_with_loss_finalize(self, ctx: Context, upload_ctx: Context,
+                                                      params: RangerUpdateParams, loss_kind: ScalarLossKind,
+                                                      output_inv_scale: float,
+                                                      batch: Optional[SfnnTrainStepHostBatch],
+                                                      finalize_loss: bool = True,
+                                                      pinned_source: Optional[SfnnTrainStepUploadSlot] = None,
+                                                      loss_out: Optional[PinnedF32Buffer] = None) -> int:
+        """Upload on `upload_ctx` into the next slot, hand off with an event, run
+        the step on `ctx`, then (optionally) an async D2H of the mean loss into
+        `loss_out`.  Returns H2D bytes."""
+        slots = self.upload_slots()
+        slot = slots[self._next_slot]
+        self._next_slot = (self._next_slot + 1) % len(slots)
+        nbytes = slot.upload(upload_ctx, batch, pinned_source)
+        slot.upload_ready.wait(ctx)
+        self.stm_indices, self.nstm_indices, self.buckets = slot.stm_indices, slot.nstm_indices, slot.buckets
+        self.targets, self.entry_weights = slot.targets, slot.entry_weights
+        self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
+        if loss_out is not None:
+            if self.lib.has("bulletou_b200_f32_download_pinned"):
+                self.lib.call("bulletou_b200_f32_download_pinned", ctx.as_ptr(), loss_out.as_ptr(),
+                              self.loss_workspace.mean.as_ptr(), 1)
+            else:
+                loss_out.host()[0] = self.loss_workspace.mean.download(ctx)[0]
+        slot.compute_done.record(ctx)
+        return nbytes
+
+    # -- readback ----------------------------------------------------------
+    def read_loss(self, ctx: Optional[Context] = None) -> ScalarLossReadback:
+        return self.loss_workspace.download(ctx)
+
+    def read_output(self, ctx: Optional[Context] = None) -> np.ndarray:
+        return self.output.download(ctx)
+
+    def read_weights(self, ctx: Optional[Context] = None) -> dict:
+        return {n: w.download(ctx) for n, w in self.weights.items() if w is not None}
+
+    def read_optimizer_states(self, ctx: Optional[Context] = None) -> dict:
+        return {n: s.download(ctx) for n, s in self.optimizer_states.items() if s is not None}

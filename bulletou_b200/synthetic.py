@@ -10,6 +10,10 @@ and value distributions:
 * KPPT: 38 distinct BonaPieces per view; KPP = all 703 pairs a<b,
   k*1548^2 + a*1548 + b (shogi_kpp.rs:14); KKP = k*81*1548 + k'*1548 + p;
   KK = k*81 + k';
+* HalfKA_hm2 (73305 = 45 mirrored king buckets x 1629): per perspective a
+  king bucket k ~ U{0..44} and 40 distinct pieces p ~ U[0,1629); feature =
+  k*1629 + p (shogi_halfka_hm2.rs:106-260); LayerStack bucket ~ U{0..8}
+  (k3k3) or Zipf(1.1) over 81 buckets through a seeded permutation (k9k9);
 * weights ~ N(0, 0.01); targets t = 0.5*r + 0.5*sigmoid(score/600) with
   score = round(N(0,600)) clipped to +-3000 and r in {0, 1/2, 1}
   (teacher_batch.rs:1709-1746 blend with lambda = 0.5); entry weight 1.
@@ -107,3 +111,57 @@ def kppt_indices(rng: np.random.Generator, batch: int, component: str) -> tuple[
             views.append((k0 * HALFKP_KINGS + k1).astype(np.int32))
         return views[0], views[1], KK_INPUTS, 1
     raise ValueError(f"unknown KPPT component {component!r}")
+
+
+HM2_KINGS = 45
+HM2_PIECES = 1629
+HM2_INPUTS = HM2_KINGS * HM2_PIECES  # 73305
+HM2_ACTIVE = 40
+
+
+def hm2_indices(rng: np.random.Generator, batch: int) -> tuple[np.ndarray, np.ndarray]:
+    """(stm, nstm) int32 [batch*40] HalfKA_hm2 features, perspectives independent."""
+    views = []
+    for _ in range(2):
+        kings = rng.integers(0, HM2_KINGS, size=(batch, 1), dtype=np.int32)
+        pieces = distinct_pieces(rng, batch, HM2_ACTIVE, HM2_PIECES)
+        views.append((kings * HM2_PIECES + pieces).astype(np.int32).reshape(-1))
+    return views[0], views[1]
+
+
+def layerstack_buckets(rng: np.random.Generator, batch: int, stacks: int = 9, zipf: float = 0.0) -> np.ndarray:
+    """Uniform buckets, or Zipf(s) ranks mapped through a seeded permutation."""
+    if zipf <= 0.0:
+        return rng.integers(0, stacks, size=batch).astype(np.int32)
+    ranks = np.arange(1, stacks + 1, dtype=np.float64)
+    p = ranks ** -zipf
+    p /= p.sum()
+    perm = rng.permutation(stacks)
+    return perm[rng.choice(stacks, size=batch, p=p)].astype(np.int32)
+
+
+def sfnn_batch(seed: int, batch: int, rank: int = 0, stacks: int = 9, zipf: float = 0.0) -> dict:
+    rng = rng_for(seed, rank)
+    stm, nstm = hm2_indices(rng, batch)
+    buckets = layerstack_buckets(rng, batch, stacks, zipf)
+    t, w = targets(rng, batch)
+    return {"stm": stm, "nstm": nstm, "buckets": buckets, "targets": t, "entry_weights": w, "batch": batch,
+            "max_active": HM2_ACTIVE}
+
+
+def sfnn_weights(rng: np.random.Generator, input_size: int = HM2_INPUTS + HM2_PIECES, ft: int = 1536,
+                 l1_hidden: int = 15, l1_skip: bool = True, l2: int = 32, stacks: int = 9, shared_l1: bool = True,
+                 shared_l2_l3: bool = False, std: float = 0.01) -> dict:
+    """N(0, std) weights of an SFNN LayerStack net (absent shared factors are None)."""
+    o = l1_hidden + int(l1_skip)
+    i2 = 2 * l1_hidden
+    shapes = {"l0w": input_size * ft, "l0b": ft, "l1w": stacks * o * ft, "l1b": stacks * o,
+              "l2w": stacks * l2 * i2, "l2b": stacks * l2, "l3w": stacks * l2, "l3b": stacks}
+    if shared_l1:
+        shapes.update({"l1fw": ft * o, "l1fb": o})
+    if shared_l2_l3:
+        shapes.update({"l2fw": l2 * i2, "l2fb": l2, "l3fw": l2, "l3fb": 1})
+    out = {k: rng.normal(0.0, std, size=n).astype(np.float32) for k, n in shapes.items()}
+    for k in ("l1fw", "l1fb", "l2fw", "l2fb", "l3fw", "l3fb"):
+        out.setdefault(k, None)
+    return out

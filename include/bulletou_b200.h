@@ -188,6 +188,44 @@ int bulletou_b200_kppt_train_step_device(
     BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
     BulletOuCudaCppF32Buffer* mean);
 
+
+/* SFNN shape of the fused step (the reference's SfnnForwardShape,
+ * lib.rs:928-970, dense L1 only) plus the factorizer coefficients
+ * (SfnnFactorizerAlpha::ft / ::shared, lib.rs:1280-1312). */
+typedef struct BulletOuB200SfnnShape {
+    size_t input_size;  /* 73305 / 131949, or + 1629 with the FT factorizer */
+    size_t ft_size;
+    size_t l1_hidden;
+    int l1_skip;
+    size_t l2_size;
+    size_t num_stacks;
+    float ft_factorizer_alpha;
+    float factorizer_shared_alpha;
+} BulletOuB200SfnnShape;
+
+/* One complete SFNN train step.  Replaces
+ * SfnnTrainStepRunner::step_no_readback_with_loss_finalize (lib.rs:7448-7533)
+ * with default layer multipliers: sfnn_forward_device (cu:11329) -> scalar
+ * loss -> sfnn_backward_train_device (cu:12882) -> Ranger on every group
+ * (update_weights_with_lr_multipliers_and_dirty_buckets, lib.rs:8425-8730).
+ * params / momentum / velocity / slow_params: 14 handles each in the order
+ * l0w l0b l1w l1b l1fw l1fb l2w l2b l2fw l2fb l3w l3b l3fw l3fb; the shared
+ * factor handles (l1fw/l1fb, l2fw/l2fb, l3fw/l3fb) are null when that factor
+ * is absent.  The FT gradient is never materialised: each FT row (and each
+ * virtual factor row) is updated by the pass that sums its gradient.
+ * ranger->norm_loss_rate must be 0 (with default multipliers the SFNN runner
+ * applies no norm loss, lib.rs:6416-6420). */
+int bulletou_b200_sfnn_train_step_device(
+    BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* targets,
+    const BulletOuCudaCppF32Buffer* entry_weights, const BulletOuB200LossSpec* loss,
+    const BulletOuB200RangerStep* ranger, BulletOuCudaCppF32Buffer* const* params,
+    BulletOuCudaCppF32Buffer* const* momentum, BulletOuCudaCppF32Buffer* const* velocity,
+    BulletOuCudaCppF32Buffer* const* slow_params, BulletOuCudaCppF32Buffer* output,
+    BulletOuCudaCppF32Buffer* per_sample, BulletOuCudaCppF32Buffer* mean_output_gradients,
+    BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean);
+
 #ifdef __cplusplus
 }
 #endif

@@ -207,6 +207,84 @@ int bulletou_cuda_cpp_kppt_backward_device(
     BulletOuCudaCppF32Buffer* table_w_gradients, BulletOuCudaCppF32Buffer* table_b_gradients,
     BulletOuCudaCppF32Buffer* outw_gradients, BulletOuCudaCppF32Buffer* outb_gradients);      /* cu:11934 */
 
+/* SFNN LayerStack forward (HalfKA_hm2 / HalfKA2 FT, pairwise product, bucketed
+ * L1 -> SqrCReLU|CReLU -> L2 -> L3 + PSQT skip).  Same arguments as the
+ * reference (cu:11329).  Supported: dense L1 (l1_group_count <= 1, no
+ * common+shard), the shared L1/L2/L3 factors (has_l*f), the FT factorizer
+ * (input_size = base + 1629, virtual rows folded with ft_factorizer_alpha);
+ * bucket-axis factorizers, residual count gates and the L1 QAT scratch
+ * (qat_l1w / qat_l1b) return -1 with "unsupported on this backend".
+ * folded_l0w (optional, input_size*ft_size) is used as fold scratch. */
+int bulletou_cuda_cpp_sfnn_forward_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip,
+    size_t l2_size, size_t num_stacks, size_t l1_group_count, size_t l1_common_size,
+    size_t l1_shard_size, size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim,
+    size_t batch, size_t max_active, const BulletOuCudaCppI32Buffer* stm_indices,
+    const BulletOuCudaCppI32Buffer* nstm_indices, const BulletOuCudaCppI32Buffer* buckets,
+    const BulletOuCudaCppF32Buffer* l0w, BulletOuCudaCppF32Buffer* folded_l0w,
+    const BulletOuCudaCppF32Buffer* l0b, const BulletOuCudaCppF32Buffer* l1w,
+    const BulletOuCudaCppF32Buffer* l1b, const BulletOuCudaCppF32Buffer* l1fw,
+    const BulletOuCudaCppF32Buffer* l1fb, int has_l1f, const BulletOuCudaCppF32Buffer* l1axw,
+    const BulletOuCudaCppF32Buffer* l1axb, int has_l1ax, const BulletOuCudaCppF32Buffer* l2w,
+    const BulletOuCudaCppF32Buffer* l2b, const BulletOuCudaCppF32Buffer* l2fw,
+    const BulletOuCudaCppF32Buffer* l2fb, int has_l2f, const BulletOuCudaCppF32Buffer* l2axw,
+    const BulletOuCudaCppF32Buffer* l2axb, int has_l2ax, const BulletOuCudaCppF32Buffer* l3w,
+    const BulletOuCudaCppF32Buffer* l3b, const BulletOuCudaCppF32Buffer* l3fw,
+    const BulletOuCudaCppF32Buffer* l3fb, int has_l3f, const BulletOuCudaCppF32Buffer* l3axw,
+    const BulletOuCudaCppF32Buffer* l3axb, int has_l3ax, int use_king_axis, int use_hand_axis,
+    int use_progress_axis, int use_king_hand_pair, int use_king_progress_pair,
+    int use_hand_progress_pair, float ft_factorizer_alpha, float factorizer_shared_alpha,
+    float factorizer_king_axis_alpha, float factorizer_hand_axis_alpha,
+    float factorizer_progress_axis_alpha, float factorizer_pair_alpha,
+    const BulletOuCudaCppF32Buffer* residual_count_gates,
+    const BulletOuCudaCppF32Buffer* factorizer_axis_confidences, BulletOuCudaCppF32Buffer* stm_l0,
+    BulletOuCudaCppF32Buffer* nstm_l0, BulletOuCudaCppF32Buffer* combined, BulletOuCudaCppF32Buffer* l1,
+    BulletOuCudaCppF32Buffer* l2_input, BulletOuCudaCppF32Buffer* l2, BulletOuCudaCppF32Buffer* output,
+    BulletOuCudaCppF32Buffer* qat_l1w, BulletOuCudaCppF32Buffer* qat_l1b, int refresh_qat_l1); /* cu:11329 */
+
+/* SFNN training backward (cu:12882): parameter gradients are accumulated into
+ * the given buffers (cleared first when zero_parameter_gradients != 0); the
+ * FT gradient includes the virtual factor rows (alpha * sum over king blocks,
+ * overwritten as in cu:4950-4985); intermediate gradient buffers are written.
+ * Same support limits as the forward. */
+int bulletou_cuda_cpp_sfnn_backward_train_device(
+    BulletOuCudaCppContext* ctx, size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip,
+    size_t l2_size, size_t num_stacks, size_t l1_group_count, size_t l1_common_size,
+    size_t l1_shard_size, size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim,
+    size_t batch, size_t max_active, const BulletOuCudaCppI32Buffer* stm_indices,
+    const BulletOuCudaCppI32Buffer* nstm_indices, const BulletOuCudaCppI32Buffer* buckets,
+    const BulletOuCudaCppF32Buffer* stm_l0, const BulletOuCudaCppF32Buffer* nstm_l0,
+    const BulletOuCudaCppF32Buffer* combined, const BulletOuCudaCppF32Buffer* l1,
+    const BulletOuCudaCppF32Buffer* l2_input, const BulletOuCudaCppF32Buffer* l2,
+    const BulletOuCudaCppF32Buffer* l1w, const BulletOuCudaCppF32Buffer* qat_l1w,
+    const BulletOuCudaCppF32Buffer* l1fw, int has_l1f, const BulletOuCudaCppF32Buffer* l1axw,
+    int has_l1ax, const BulletOuCudaCppF32Buffer* l2w, const BulletOuCudaCppF32Buffer* l2fw,
+    int has_l2f, const BulletOuCudaCppF32Buffer* l2axw, int has_l2ax,
+    const BulletOuCudaCppF32Buffer* l3w, const BulletOuCudaCppF32Buffer* l3fw, int has_l3f,
+    const BulletOuCudaCppF32Buffer* l3axw, int has_l3ax, int use_king_axis, int use_hand_axis,
+    int use_progress_axis, int use_king_hand_pair, int use_king_progress_pair,
+    int use_hand_progress_pair, float ft_factorizer_alpha, float factorizer_shared_alpha,
+    float factorizer_king_axis_alpha, float factorizer_hand_axis_alpha,
+    float factorizer_progress_axis_alpha, float factorizer_pair_alpha,
+    const BulletOuCudaCppF32Buffer* residual_count_gates,
+    const BulletOuCudaCppF32Buffer* factorizer_axis_confidences,
+    const BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* l2_gradients,
+    BulletOuCudaCppF32Buffer* l1_gradients, BulletOuCudaCppF32Buffer* l2_input_gradients,
+    BulletOuCudaCppF32Buffer* combined_gradients, BulletOuCudaCppF32Buffer* stm_l0_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_gradients, BulletOuCudaCppF32Buffer* stm_l0_pre_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_pre_gradients, BulletOuCudaCppF32Buffer* l0w_gradients,
+    BulletOuCudaCppF32Buffer* l0b_gradients, BulletOuCudaCppF32Buffer* l1w_gradients,
+    BulletOuCudaCppF32Buffer* l1b_gradients, BulletOuCudaCppF32Buffer* l1fw_gradients,
+    BulletOuCudaCppF32Buffer* l1fb_gradients, BulletOuCudaCppF32Buffer* l1axw_gradients,
+    BulletOuCudaCppF32Buffer* l1axb_gradients, BulletOuCudaCppF32Buffer* l2w_gradients,
+    BulletOuCudaCppF32Buffer* l2b_gradients, BulletOuCudaCppF32Buffer* l2fw_gradients,
+    BulletOuCudaCppF32Buffer* l2fb_gradients, BulletOuCudaCppF32Buffer* l2axw_gradients,
+    BulletOuCudaCppF32Buffer* l2axb_gradients, BulletOuCudaCppF32Buffer* l3w_gradients,
+    BulletOuCudaCppF32Buffer* l3b_gradients, BulletOuCudaCppF32Buffer* l3fw_gradients,
+    BulletOuCudaCppF32Buffer* l3fb_gradients, BulletOuCudaCppF32Buffer* l3axw_gradients,
+    BulletOuCudaCppF32Buffer* l3axb_gradients, int zero_parameter_gradients,
+    BulletOuCudaCppF32Buffer* entry_weights);                                            /* cu:12882 */
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,6 +20,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 #include <float.h>
 
@@ -310,4 +311,257 @@ EXPORT void oracle_kppt_backward(int64_t input_size, int64_t batch, int64_t max_
     outw_g[0] = (float)w0;
     outw_g[1] = (float)w1;
     outb_g[0] = (float)ob;
+}
+
+/* ------------------------------------------------------------------ SFNN
+ * SFNN LayerStack network.  Follows the CPU statement
+ * crates/bulletou_lib/src/value/fast_sfnn.rs:325-452 (forward, factorized
+ * virtual feature) and the reference test oracle tiny_sfnn_forward_cpu /
+ * tiny_sfnn_backward_cpu (crates/cuda_cpp/src/lib.rs:14252-14710, shared
+ * L1/L2/L3 factors), with the factor coefficients of the GPU kernels
+ * (ft alpha: cu:1445-1456 fold; shared alpha: cu:2297-2322, 2449-2600).
+ * The FT row sum uses the folded row w[f] + alpha * w[virtual] like the
+ * reference's training forward; dense dots and every batch reduction
+ * accumulate in double.
+ * Weight pointers, in order: l0w l0b l1w l1b l1fw l1fb l2w l2b l2fw l2fb l3w
+ * l3b l3fw l3fb (shared factors may be NULL). */
+#define SFNN_PIECES 1629
+
+typedef struct {
+    int64_t input_size, width, hidden, skip, l2, stacks, batch, max_active;
+    float ft_alpha, shared_alpha;
+    int64_t base, n_features, l1_out, l2_in;
+} sfnn_dims;
+
+static sfnn_dims sfnn_make_dims(const int64_t* shape, const float* alphas) {
+    sfnn_dims d;
+    d.input_size = shape[0];
+    d.width = shape[1];
+    d.hidden = shape[2];
+    d.skip = shape[3];
+    d.l2 = shape[4];
+    d.stacks = shape[5];
+    d.batch = shape[6];
+    d.max_active = shape[7];
+    d.ft_alpha = alphas[0];
+    d.shared_alpha = alphas[1];
+    /* cu:1180-1184: the two HalfKA bases + 1629 virtual piece rows */
+    d.base = (d.input_size == 131949 + SFNN_PIECES) ? 131949 : (d.input_size == 73305 + SFNN_PIECES) ? 73305 : 0;
+    d.n_features = d.base ? d.base : d.input_size;
+    d.l1_out = d.hidden + (d.skip ? 1 : 0);
+    d.l2_in = 2 * d.hidden;
+    return d;
+}
+
+static void sfnn_ft_view(const sfnn_dims* d, const int* idx, const float* l0w, const float* l0b, float* x) {
+    for (int64_t j = 0; j < d->width; ++j) x[j] = l0b[j];
+    for (int64_t s = 0; s < d->max_active; ++s) {
+        int f = idx[s];
+        if (f < 0 || (int64_t)f >= d->n_features) continue;
+        const float* row = l0w + (int64_t)f * d->width;
+        if (d->base) {
+            const float* v = l0w + (d->base + (int64_t)f % SFNN_PIECES) * d->width;
+            for (int64_t j = 0; j < d->width; ++j) x[j] += fmaf(d->ft_alpha, v[j], row[j]);
+        } else {
+            for (int64_t j = 0; j < d->width; ++j) x[j] += row[j];
+        }
+    }
+    for (int64_t j = 0; j < d->width; ++j) x[j] = crelu(x[j]);
+}
+
+static float sfnn_w1(const sfnn_dims* d, const float* const* w, int64_t s, int64_t o, int64_t i) {
+    float v = w[2][(s * d->l1_out + o) * d->width + i];
+    if (w[4]) v = fmaf(d->shared_alpha, w[4][i * d->l1_out + o], v);
+    return v;
+}
+
+static float sfnn_w2(const sfnn_dims* d, const float* const* w, int64_t s, int64_t o, int64_t i) {
+    float v = w[6][(s * d->l2 + o) * d->l2_in + i];
+    if (w[8]) v = fmaf(d->shared_alpha, w[8][o * d->l2_in + i], v);
+    return v;
+}
+
+static float sfnn_w3(const sfnn_dims* d, const float* const* w, int64_t s, int64_t o) {
+    float v = w[10][s * d->l2 + o];
+    if (w[12]) v = fmaf(d->shared_alpha, w[12][o], v);
+    return v;
+}
+
+/* shape: input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks, batch, max_active;
+ * alphas: ft, shared.  Outputs (row-major per sample): stm_l0, nstm_l0,
+ * combined [B][W], l1 [B][l1_out], l2_input [B][2H], l2 [B][L2], output [B]. */
+EXPORT void oracle_sfnn_forward(const int64_t* shape, const float* alphas, const int* stm, const int* nstm,
+                                const int* buckets, const float* const* w, float* stm_l0, float* nstm_l0,
+                                float* combined, float* l1, float* l2_input, float* l2, float* output) {
+    sfnn_dims d = sfnn_make_dims(shape, alphas);
+    const float scale = 127.0f / 128.0f;
+    const int64_t W = d.width, half = W / 2;
+    for (int64_t b = 0; b < d.batch; ++b) {
+        float* xs = stm_l0 + b * W;
+        float* xn = nstm_l0 + b * W;
+        sfnn_ft_view(&d, stm + b * d.max_active, w[0], w[1], xs);
+        sfnn_ft_view(&d, nstm + b * d.max_active, w[0], w[1], xn);
+        float* c = combined + b * W;
+        for (int64_t j = 0; j < half; ++j) {
+            c[j] = xs[j] * xs[j + half] * scale;
+            c[half + j] = xn[j] * xn[j + half] * scale;
+        }
+        float* l1r = l1 + b * d.l1_out;
+        float* in = l2_input + b * d.l2_in;
+        float* l2r = l2 + b * d.l2;
+        int s = buckets[b];
+        if (s < 0 || s >= d.stacks) {  /* cu:2250-2256: invalid bucket -> zeros */
+            for (int64_t o = 0; o < d.l1_out; ++o) l1r[o] = 0.0f;
+            for (int64_t i = 0; i < d.l2_in; ++i) in[i] = 0.0f;
+            for (int64_t o = 0; o < d.l2; ++o) l2r[o] = 0.0f;
+            output[b] = 0.0f;
+            continue;
+        }
+        for (int64_t o = 0; o < d.l1_out; ++o) {
+            double acc = 0.0;
+            for (int64_t i = 0; i < W; ++i) acc += (double)c[i] * sfnn_w1(&d, w, s, o, i);
+            float r = (float)acc + w[3][s * d.l1_out + o];
+            if (w[5]) r = fmaf(d.shared_alpha, w[5][o], r);
+            l1r[o] = r;
+        }
+        for (int64_t i = 0; i < d.hidden; ++i) {
+            float a = fabsf(l1r[i]);
+            in[i] = crelu(a * a * scale);            /* SqrCReLU, cu:2428-2447 */
+            in[d.hidden + i] = crelu(l1r[i]);        /* CReLU */
+        }
+        for (int64_t o = 0; o < d.l2; ++o) {
+            float bias = w[7][s * d.l2 + o];
+            if (w[9]) bias = fmaf(d.shared_alpha, w[9][o], bias);
+            double acc = bias;
+            for (int64_t i = 0; i < d.l2_in; ++i) acc += (double)in[i] * sfnn_w2(&d, w, s, o, i);
+            l2r[o] = crelu((float)acc);
+        }
+        float b3 = w[11][s];
+        if (w[13]) b3 = fmaf(d.shared_alpha, w[13][0], b3);
+        double out = b3;
+        for (int64_t o = 0; o < d.l2; ++o) out += (double)l2r[o] * sfnn_w3(&d, w, s, o);
+        output[b] = (float)out + (d.skip ? l1r[d.hidden] : 0.0f);
+    }
+}
+
+/* Backward of oracle_sfnn_forward for output gradients mog (lib.rs:14516-14710
+ * with the alphas of the GPU kernels).  grads (same order as w, NULL where w
+ * is NULL) are overwritten; l0w's gradient includes the virtual rows
+ * (alpha * sum of the base rows' gradients, cu:4950-4985).  l1_gradients
+ * [B][l1_out] and combined_gradients [B][W] are written too. */
+EXPORT void oracle_sfnn_backward(const int64_t* shape, const float* alphas, const int* stm, const int* nstm,
+                                 const int* buckets, const float* const* w, const float* stm_l0, const float* nstm_l0,
+                                 const float* combined, const float* l1, const float* l2_input, const float* l2,
+                                 const float* mog, double* acc_l0w, float* const* grads, float* l1_gradients,
+                                 float* combined_gradients) {
+    sfnn_dims d = sfnn_make_dims(shape, alphas);
+    const float scale = 127.0f / 128.0f;
+    const int64_t W = d.width, half = W / 2, O = d.l1_out, L2 = d.l2, I2 = d.l2_in, S = d.stacks;
+    const int64_t lens[14] = {d.input_size * W, W, S * O * W, S * O, W * O, O, S * L2 * I2, S * L2, L2 * I2, L2,
+                              S * L2, S, L2, 1};
+    double* acc[14];
+    double* pool = 0;
+    int64_t total = 0;
+    for (int k = 1; k < 14; ++k) total += lens[k];
+    pool = (double*)calloc((size_t)total, sizeof(double));
+    int64_t off = 0;
+    acc[0] = acc_l0w;
+    for (int k = 1; k < 14; ++k) {
+        acc[k] = pool + off;
+        off += lens[k];
+    }
+    for (int64_t i = 0; i < lens[0]; ++i) acc_l0w[i] = 0.0;
+    float* g2 = (float*)malloc(sizeof(float) * (size_t)L2);
+    float* gin = (float*)malloc(sizeof(float) * (size_t)I2);
+    float* pre_s = (float*)malloc(sizeof(float) * (size_t)W);
+    float* pre_n = (float*)malloc(sizeof(float) * (size_t)W);
+    for (int64_t b = 0; b < d.batch; ++b) {
+        const float gout = mog[b];
+        float* g1 = l1_gradients + b * O;
+        float* dc = combined_gradients + b * W;
+        for (int64_t o = 0; o < O; ++o) g1[o] = 0.0f;
+        for (int64_t i = 0; i < W; ++i) dc[i] = 0.0f;
+        if (d.skip) g1[d.hidden] = gout;  /* PSQT skip, cu:3433-3437 */
+        int s = buckets[b];
+        if (s < 0 || s >= S) continue;
+        const float* l2r = l2 + b * L2;
+        const float* in = l2_input + b * I2;
+        const float* l1r = l1 + b * O;
+        /* L3 (cu:3324-3480) */
+        acc[11][s] += gout;
+        if (w[13]) acc[13][0] += (double)d.shared_alpha * gout;
+        for (int64_t o = 0; o < L2; ++o) {
+            acc[10][s * L2 + o] += (double)gout * l2r[o];
+            if (w[12]) acc[12][o] += (double)d.shared_alpha * gout * l2r[o];
+            g2[o] = crelu_grad(l2r[o], gout * sfnn_w3(&d, w, s, o));
+        }
+        /* L2 (cu:3489-3700) */
+        for (int64_t i = 0; i < I2; ++i) gin[i] = 0.0f;
+        for (int64_t o = 0; o < L2; ++o) {
+            acc[7][s * L2 + o] += g2[o];
+            if (w[9]) acc[9][o] += (double)d.shared_alpha * g2[o];
+            for (int64_t i = 0; i < I2; ++i) {
+                acc[6][(s * L2 + o) * I2 + i] += (double)g2[o] * in[i];
+                if (w[8]) acc[8][o * I2 + i] += (double)d.shared_alpha * g2[o] * in[i];
+                gin[i] += g2[o] * sfnn_w2(&d, w, s, o, i);
+            }
+        }
+        /* L2 input (cu:3709-3770) */
+        for (int64_t i = 0; i < d.hidden; ++i) {
+            float v = l1r[i];
+            float sq = crelu_grad(in[i], gin[i] * (2.0f * v * scale));
+            float lin = crelu_grad(in[d.hidden + i], gin[d.hidden + i]);
+            g1[i] = sq + lin;
+        }
+        /* L1 (cu:3778-4100) */
+        for (int64_t o = 0; o < O; ++o) {
+            acc[3][s * O + o] += g1[o];
+            if (w[5]) acc[5][o] += (double)d.shared_alpha * g1[o];
+            for (int64_t i = 0; i < W; ++i) {
+                acc[2][(s * O + o) * W + i] += (double)g1[o] * combined[b * W + i];
+                if (w[4]) acc[4][i * O + o] += (double)d.shared_alpha * g1[o] * combined[b * W + i];
+            }
+        }
+        for (int64_t i = 0; i < W; ++i) {
+            double t = 0.0;
+            for (int64_t o = 0; o < O; ++o) t += (double)g1[o] * sfnn_w1(&d, w, s, o, i);
+            dc[i] = (float)t;
+        }
+        /* pairwise + ClippedReLU (cu:4376-4440) */
+        for (int v = 0; v < 2; ++v) {
+            const float* x = (v ? nstm_l0 : stm_l0) + b * W;
+            float* pre = v ? pre_n : pre_s;
+            for (int64_t j = 0; j < half; ++j) {
+                float pg = dc[v * half + j] * scale;
+                pre[j] = crelu_grad(x[j], pg * x[j + half]);
+                pre[j + half] = crelu_grad(x[j + half], pg * x[j]);
+            }
+            for (int64_t j = 0; j < W; ++j) acc[1][j] += pre[j];
+            const int* idx = (v ? nstm : stm) + b * d.max_active;
+            for (int64_t k = 0; k < d.max_active; ++k) {
+                int f = idx[k];
+                if (f < 0 || (int64_t)f >= d.n_features) continue;
+                double* row = acc_l0w + (int64_t)f * W;
+                for (int64_t j = 0; j < W; ++j) row[j] += pre[j];
+            }
+        }
+    }
+    if (d.base) {
+        for (int64_t p = 0; p < SFNN_PIECES; ++p) {
+            double* vrow = acc_l0w + (d.base + p) * W;
+            for (int64_t j = 0; j < W; ++j) vrow[j] = 0.0;
+            for (int64_t f = p; f < d.base; f += SFNN_PIECES)
+                for (int64_t j = 0; j < W; ++j) vrow[j] += acc_l0w[f * W + j];
+            for (int64_t j = 0; j < W; ++j) vrow[j] *= d.ft_alpha;
+        }
+    }
+    for (int k = 0; k < 14; ++k) {
+        if (!grads[k]) continue;
+        for (int64_t i = 0; i < lens[k]; ++i) grads[k][i] = (float)acc[k][i];
+    }
+    free(pool);
+    free(g2);
+    free(gin);
+    free(pre_s);
+    free(pre_n);
 }

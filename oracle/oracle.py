@@ -43,9 +43,11 @@ def lib():
         _lib.oracle_ranger_update.argtypes = [i64, f, f, f, i, f, f, f, f, f, f, i, f, i] + [p] * 5
         _lib.oracle_kppt_forward.argtypes = [i64] * 3 + [p] * 9
         _lib.oracle_kppt_backward.argtypes = [i64] * 3 + [p] * 11
+        _lib.oracle_sfnn_forward.argtypes = [p] * 13
+        _lib.oracle_sfnn_backward.argtypes = [p] * 17
         for fn in (_lib.oracle_nnue_forward, _lib.oracle_scalar_loss, _lib.oracle_nnue_backward,
                    _lib.oracle_radam_step_scale, _lib.oracle_ranger_update, _lib.oracle_kppt_forward,
-                   _lib.oracle_kppt_backward):
+                   _lib.oracle_kppt_backward, _lib.oracle_sfnn_forward, _lib.oracle_sfnn_backward):
             fn.restype = None
     return _lib
 
@@ -176,3 +178,107 @@ def kppt_backward(input_size, stm, nstm, batch, max_active, fwd: dict, outw, mog
                                _p(ow), _p(mg), _p(acc), _p(g["table_w"]), _p(g["table_b"]), _p(g["outw"]),
                                _p(g["outb"]))
     return g
+
+
+# ---------------------------------------------------------------- SFNN
+SFNN_NAMES = ("l0w", "l0b", "l1w", "l1b", "l1fw", "l1fb", "l2w", "l2b", "l2fw", "l2fb", "l3w", "l3b", "l3fw", "l3fb")
+SFNN_FACTORIZED_BASES = {73305 + 1629: 73305, 131949 + 1629: 131949}
+
+
+def _sfnn_shape_arrays(shape, batch, max_active, ft_alpha, shared_alpha):
+    input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks = shape
+    sh = np.array([input_size, ft_size, l1_hidden, int(bool(l1_skip)), l2_size, num_stacks, batch, max_active],
+                  np.int64)
+    al = np.array([ft_alpha, shared_alpha], np.float32)
+    return sh, al
+
+
+def _ptr_array(arrays):
+    arr = (ctypes.c_void_p * len(arrays))()
+    for k, a in enumerate(arrays):
+        arr[k] = None if a is None else a.ctypes.data
+    return arr
+
+
+def sfnn_forward(shape, stm, nstm, buckets, batch, max_active, weights: dict, ft_alpha=1.0, shared_alpha=1.0) -> dict:
+    """Forward of the SFNN LayerStack net (oracle_sfnn_forward in the C file).
+    shape = (input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks)."""
+    _, W, H, skip, L2, _ = shape
+    O = H + (1 if skip else 0)
+    sh, al = _sfnn_shape_arrays(shape, batch, max_active, ft_alpha, shared_alpha)
+    ws = [None if weights.get(n) is None else _f(weights[n]) for n in SFNN_NAMES]
+    out = {"stm_l0": np.zeros(batch * W, np.float32), "nstm_l0": np.zeros(batch * W, np.float32),
+           "combined": np.zeros(batch * W, np.float32), "l1": np.zeros(batch * O, np.float32),
+           "l2_input": np.zeros(batch * 2 * H, np.float32), "l2": np.zeros(batch * L2, np.float32),
+           "output": np.zeros(batch, np.float32)}
+    s, n, b = _i(stm), _i(nstm), _i(buckets)
+    lib().oracle_sfnn_forward(_p(sh), _p(al), _p(s), _p(n), _p(b), _ptr_array(ws), *(_p(out[k]) for k in (
+        "stm_l0", "nstm_l0", "combined", "l1", "l2_input", "l2", "output")))
+    return out
+
+
+def sfnn_backward(shape, stm, nstm, buckets, batch, max_active, fwd: dict, weights: dict, mog, ft_alpha=1.0,
+                  shared_alpha=1.0) -> dict:
+    """Parameter gradients ("<name>_gradients", FT virtual rows included) plus
+    l1_gradients and combined_gradients (oracle_sfnn_backward)."""
+    input_size, W, H, skip, L2, S = shape
+    O = H + (1 if skip else 0)
+    sh, al = _sfnn_shape_arrays(shape, batch, max_active, ft_alpha, shared_alpha)
+    ws = [None if weights.get(n) is None else _f(weights[n]) for n in SFNN_NAMES]
+    grads = [None if a is None else np.zeros_like(a) for a in ws]
+    acc = np.zeros(input_size * W, np.float64)
+    l1g = np.zeros(batch * O, np.float32)
+    cg = np.zeros(batch * W, np.float32)
+    s, n, b = _i(stm), _i(nstm), _i(buckets)
+    lib().oracle_sfnn_backward(_p(sh), _p(al), _p(s), _p(n), _p(b), _ptr_array(ws),
+                               *(_p(_f(fwd[k])) for k in ("stm_l0", "nstm_l0", "combined", "l1", "l2_input", "l2")),
+                               _p(_f(mog)), _p(acc), _ptr_array(grads), _p(l1g), _p(cg))
+    out = {f"{name}_gradients": g for name, g in zip(SFNN_NAMES, grads) if g is not None}
+    out["l1_gradients"] = l1g
+    out["combined_gradients"] = cg
+    return out
+
+
+class SfnnTrainer:
+    """CPU reference runner for SFNN (SfnnTrainStepRunner with default layer
+    multipliers, lib.rs:7448-7533 / 8425-8730): forward -> loss -> backward ->
+    Ranger on every present group in the order of SFNN_NAMES."""
+
+    def __init__(self, shape, weights: dict, ft_alpha=1.0, shared_alpha=1.0):
+        self.shape = tuple(shape)
+        self.ft_alpha, self.shared_alpha = ft_alpha, shared_alpha
+        self.names = [n for n in SFNN_NAMES if weights.get(n) is not None]
+        self.w = {n: _f(weights[n]).copy() for n in self.names}
+        self.m = {n: np.zeros_like(self.w[n]) for n in self.names}
+        self.v = {n: np.zeros_like(self.w[n]) for n in self.names}
+        self.slow = {n: self.w[n].copy() for n in self.names}
+
+    def step(self, stm, nstm, buckets, batch, max_active, targets, entry_weights, *, loss_kind=0, inv_scale=1.0,
+             pow_exp=2.0, loss_param=0.0, **ranger) -> dict:
+        fwd = sfnn_forward(self.shape, stm, nstm, buckets, batch, max_active, self.w, self.ft_alpha, self.shared_alpha)
+        loss = scalar_loss(loss_kind, inv_scale, pow_exp, loss_param, fwd["output"], targets, entry_weights)
+        g = sfnn_backward(self.shape, stm, nstm, buckets, batch, max_active, fwd, self.w,
+                          loss["mean_output_gradients"], self.ft_alpha, self.shared_alpha)
+        for n in self.names:
+            r = dict(ranger)
+            if n in ("l1fw", "l1fb"):
+                r = shared_factor_clip(r, self.shared_alpha)
+            ranger_update(g[f"{n}_gradients"], self.w[n], self.m[n], self.v[n], self.slow[n], **r)
+        return {"forward": fwd, "loss": loss, "gradients": g}
+
+
+def shared_factor_clip(ranger: dict, alpha: float) -> dict:
+    """Bounds of a shared factor refer to alpha * w (factor_contribution_clip, lib.rs:8772-8788)."""
+    r = dict(ranger)
+    lo, hi = r.get("min_weight", -FLT_MAX), r.get("max_weight", FLT_MAX)
+    if alpha == 0.0:
+        r["min_weight"], r["max_weight"] = -FLT_MAX, FLT_MAX
+        return r
+
+    def scale(bound):
+        if bound in (-FLT_MAX, FLT_MAX):
+            return bound
+        return float(np.float32(min(FLT_MAX, max(-FLT_MAX, float(bound) / float(alpha)))))
+
+    r["min_weight"], r["max_weight"] = scale(lo), scale(hi)
+    return r

@@ -25,6 +25,64 @@ TINY_NNUE = {
     },
 }
 
+TINY_SFNN_FAST = {
+    "source": "crates/bulletou_lib/src/value/fast_sfnn.rs:663-705 (tiny_shape / tiny_batch / tiny_weights)",
+    "shape": [4, 4, 2, 1, 2, 2],
+    "batch": 2, "max_active": 3, "stm": [0, 1, -1, 3, -1, -1], "nstm": [2, -1, -1, 0, 2, -1], "buckets": [0, 1],
+    "weights": {
+        "l0w": [0.2, 0.1, -0.1, 0.0, -0.1, 0.2, 0.1, 0.2, 0.0, -0.2, 0.2, 0.1, 0.3, 0.0, -0.3, 0.2],
+        "l0b": [0.1, 0.2, 0.3, 0.4],
+        "l1w": [1.0, 0.0, 0.0, 0.0, 0.0, 1.0, 0.0, 1.0, 0.0, 0.0, 0.0, 0.0,
+                0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 0.0, 0.0, 1.0, 0.0, 1.0, 0.0],
+        "l1b": [0.0] * 6,
+        "l2w": [1.0, 0.0, 0.0, 0.0, 0.0, 1.0, 0.0, 0.0, 1.0, 0.0, 1.0, 0.0, 0.0, 1.0, 0.0, 1.0],
+        "l2b": [0.0] * 4,
+        "l3w": [2.0, -0.5, -1.0, 0.8],
+        "l3b": [0.1, -0.02],
+    },
+    "trace_source": "crates/bulletou_lib/src/value/fast_sfnn.rs:513-541 (scalar_trace_exposes_intermediate_activations)",
+    "stm_l0": [0.2, 0.5, 0.3, 0.6, 0.4, 0.2, 0.0, 0.6],
+    "nstm_l0": [0.1, 0.0, 0.5, 0.5, 0.3, 0.1, 0.4, 0.5],
+    "combined": [0.05953125, 0.29765625, 0.049609375, 0.0, 0.0, 0.1190625, 0.1190625, 0.049609375],
+    "l1": [0.05953125, 0.29765625, 0.0, 0.049609375, 0.0, 0.1190625],
+    "l2_input": [0.0035162825, 0.08790706, 0.05953125, 0.29765625, 0.0024418628, 0.0, 0.049609375, 0.0],
+    "l2": [0.0035162825, 0.08790706, 0.05205124, 0.0],
+    "outputs": [0.06307903, 0.04701126],
+    "tolerance": 1e-6,
+}
+
+TINY_SFNN_RUNNER = {
+    "source": "crates/cuda_cpp/src/lib.rs:14180-14250 (tiny_sfnn_shape / tiny_sfnn_weights, shared L1/L2/L3 factors)",
+    "shape": [4, 4, 2, 1, 2, 2],
+    "weights": {
+        "l0w": [0.2, 0.3, 0.4, 0.5, 0.1, -0.2, 0.3, -0.4, -0.3, 0.2, 0.6, 0.1, 0.7, 0.4, -0.5, 0.2],
+        "l0b": [0.05, 0.1, 0.15, 0.2],
+        "l1w": [0.4, -0.1, 0.2, 0.3, 0.1, 0.5, -0.2, 0.4, -0.3, 0.2, 0.6, -0.1,
+                0.2, 0.3, -0.4, 0.1, -0.2, 0.4, 0.1, 0.5, 0.3, -0.5, 0.2, 0.1],
+        "l1b": [0.01, 0.02, 0.03, -0.01, 0.04, -0.02],
+        "l1fw": [0.01, -0.02, 0.03, -0.01, 0.02, -0.03, 0.04, 0.01, -0.02, 0.02, -0.04, 0.01],
+        "l1fb": [0.005, -0.006, 0.007],
+        "l2w": [0.3, -0.1, 0.2, 0.4, -0.2, 0.5, 0.1, -0.3, 0.1, 0.2, -0.4, 0.3, 0.4, -0.2, 0.3, 0.1],
+        "l2b": [0.02, -0.03, 0.01, 0.04],
+        "l2fw": [0.01, -0.02, 0.03, -0.04, -0.03, 0.02, -0.01, 0.04],
+        "l2fb": [0.006, -0.008],
+        "l3w": [0.6, -0.4, 0.5, 0.2],
+        "l3b": [0.05, -0.02],
+        "l3fw": [0.03, -0.02],
+        "l3fb": [0.004],
+    },
+    "train_source": "crates/cuda_cpp/src/lib.rs:13929-13955 (sfnn_tiny_train_step_runner_smoke)",
+    "batch": 4, "max_active": 3,
+    "stm": [0, 1, -1, 2, -1, -1, 1, 3, -1, 3, 2, -1],
+    "nstm": [2, -1, -1, 0, 3, -1, 0, -1, -1, 1, -1, -1],
+    "buckets": [0, 1, 0, 1],
+    "targets": [0.25, 0.75, 0.6, 0.1],
+    "entry_weights": [1.0, 0.5, 0.75, 1.25],
+    "ranger": {"step": 1, "learning_rate": 0.01, "beta1": 0.9, "beta2": 0.999, "min_weight": -1.98,
+               "max_weight": 1.98, "lookahead_alpha": 0.5, "lookahead_period": 6},
+    "tolerance": 1e-6,
+}
+
 GOLDENS = {
     "tiny_nnue": TINY_NNUE,
     "tiny_nnue_trace": {
@@ -73,6 +131,8 @@ GOLDENS = {
         "grad_overrides": {"16": "-0.0", "20": 0.1}, "momentum_overrides": {"24": 0.2},
         "velocity_overrides": {"28": 0.3}, "steps": [1, 6, 12], "min_weight": -1.0, "max_weight": 1.0,
     },
+    "tiny_sfnn_fast": TINY_SFNN_FAST,
+    "tiny_sfnn_runner": TINY_SFNN_RUNNER,
 }
 
 if __name__ == "__main__":
