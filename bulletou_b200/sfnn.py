@@ -179,24 +179,25 @@ class SfnnBackwardWorkspace:
                  "l2_input_gradients": batch_size * shape.l2_in}
         for k in self.INTERMEDIATE:
             setattr(self, k, F32Buffer(ctx, sizes.get(k, batch_size * W)))
+        # Every gradient buffer exists, as in the reference workspace
+        # (lib.rs:3260-3300): shared-factor gradients at full size even when
+        # the factor is absent, bucket-axis gradients with length 0.
         lens = shape.weight_lengths()
+        self.present = dict(present)
         self.params = {}
         for n in SFNN_WEIGHT_NAMES:
-            if present[n]:
-                b = F32Buffer(ctx, lens[n])
-                b.fill(0.0)
-                self.params[n] = b
-            else:
-                self.params[n] = None
+            b = F32Buffer(ctx, lens[n])
+            b.fill(0.0)
+            self.params[n] = b
+        self.axis = {n: F32Buffer(ctx, 0) for n in ("l1axw", "l1axb", "l2axw", "l2axb", "l3axw", "l3axb")}
 
     def zero_parameter_gradients(self, ctx: Optional[Context] = None) -> None:
         for b in self.params.values():
-            if b is not None:
-                b.fill(0.0, ctx)
+            b.fill(0.0, ctx)
 
     def download(self, ctx: Optional[Context] = None) -> dict:
         out = {k: getattr(self, k).download(ctx) for k in self.INTERMEDIATE}
-        out.update({f"{n}_gradients": b.download(ctx) for n, b in self.params.items() if b is not None})
+        out.update({f"{n}_gradients": b.download(ctx) for n, b in self.params.items() if self.present[n]})
         return out
 
 
@@ -229,7 +230,7 @@ def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size
                                zero_parameter_gradients: bool = False,
                                entry_weights: Optional[F32Buffer] = None) -> None:
     """bulletou_cuda_cpp_sfnn_backward_train_device (lib.rs:3529-4090 argument order)."""
-    w, g = weights, bws.params
+    w, g, ax = weights, bws.params, bws.axis
     has = [int(w[n] is not None) for n in ("l1fw", "l2fw", "l3fw")]
     ctx.lib.call(
         "bulletou_cuda_cpp_sfnn_backward_train_device", ctx.as_ptr(), shape.input_size, shape.ft_size,
@@ -239,9 +240,10 @@ def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size
         _p(w["l1fw"]), has[0], None, 0, _p(w["l2w"]), _p(w["l2fw"]), has[1], None, 0, _p(w["l3w"]), _p(w["l3fw"]),
         has[2], None, 0, 0, 0, 0, 0, 0, 0, alpha.ft, alpha.shared, 1.0, 1.0, 1.0, 1.0, None, None,
         mean_output_gradients.as_ptr(), *[getattr(bws, k).as_ptr() for k in bws.INTERMEDIATE], _p(g["l0w"]),
-        _p(g["l0b"]), _p(g["l1w"]), _p(g["l1b"]), _p(g["l1fw"]), _p(g["l1fb"]), None, None, _p(g["l2w"]),
-        _p(g["l2b"]), _p(g["l2fw"]), _p(g["l2fb"]), None, None, _p(g["l3w"]), _p(g["l3b"]), _p(g["l3fw"]),
-        _p(g["l3fb"]), None, None, int(zero_parameter_gradients), _p(entry_weights))
+        _p(g["l0b"]), _p(g["l1w"]), _p(g["l1b"]), _p(g["l1fw"]), _p(g["l1fb"]), _p(ax["l1axw"]), _p(ax["l1axb"]),
+        _p(g["l2w"]), _p(g["l2b"]), _p(g["l2fw"]), _p(g["l2fb"]), _p(ax["l2axw"]), _p(ax["l2axb"]), _p(g["l3w"]),
+        _p(g["l3b"]), _p(g["l3fw"]), _p(g["l3fb"]), _p(ax["l3axw"]), _p(ax["l3axb"]), int(zero_parameter_gradients),
+        _p(entry_weights))
 
 
 def factor_contribution_clip(params: RangerUpdateParams, alpha: float) -> RangerUpdateParams:
