@@ -103,6 +103,7 @@ enum ScratchSlot : int {
     kScratchSfnnPartials = 17,  // SFNN per-tile partial sums
     kScratchSfnnGrads = 18,     // SFNN packed small-parameter gradients
     kScratchSfnnEff = 19,       // SFNN effective (shared-factor folded) dense weights
+    kScratchSfnnVirtual = 20,   // SFNN per-piece virtual-row gradient sums between row launches
 };
 
 int ok();

@@ -51,7 +51,7 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr float kPairScale = 127.0f / 128.0f;  // SFNN_PAIRWISE_SCALE, cu:1148
 constexpr int kBucketKeys = kSfnnMaxStacks + 1;
 constexpr int kPieceRowWarps = 8;
-constexpr int kPieceSortCap = 512;
+constexpr int kKingsPerLaunch = 3;  // FT row kernel: king blocks per launch (L2 working set)
 
 __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
 __device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f && a < 1.0f ? g : 0.0f; }
@@ -607,16 +607,28 @@ struct L1BackArgs {
 template <int O>
 __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
     constexpr int kO = O > 0 ? O : kSfnnMaxL1Out;
+    constexpr int kU = 4;  // samples in flight per thread
     __shared__ float g1s[kSfnnTile * kSfnnMaxL1Out];
+    __shared__ int bs[kSfnnTile];
+    __shared__ int rs[kSfnnTile * 2];
     const int t = blockIdx.x;
     if (t >= *a.tiles.n_tiles) return;
     const int s = a.tiles.key[t];
     const int pb = a.tiles.begin[t], pe = a.tiles.end[t];
+    const int n = pe - pb;
     const int od = O > 0 ? O : a.out_dim;
     const int W = a.width, half = W / 2;
     const int i = blockIdx.y * 256 + threadIdx.x;
     const bool valid = s < a.stacks;
-    for (int q = threadIdx.x; q < (pe - pb) * od; q += blockDim.x)
+    for (int q = threadIdx.x; q < n; q += blockDim.x) {
+        const int b = a.tiles.order[pb + q];
+        bs[q] = b;
+        if (a.rank != nullptr) {
+            rs[2 * q] = a.rank[2 * b];
+            rs[2 * q + 1] = a.rank[2 * b + 1];
+        }
+    }
+    for (int q = threadIdx.x; q < n * od; q += blockDim.x)
         g1s[q] = valid ? a.g1[static_cast<size_t>(a.tiles.order[pb + q / od]) * od + q % od] : 0.0f;
     __syncthreads();
     if (i >= W) return;
@@ -630,37 +642,52 @@ __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
     }
     float p0sum = 0.0f, p1sum = 0.0f;
     const float* x = a.l0[v];
-    for (int q = 0; q < pe - pb; ++q) {
-        const int b = a.tiles.order[pb + q];
-        const size_t row = static_cast<size_t>(b) * W;
-        const float x0 = x[row + j], x1 = x[row + j + half];
-        const float c = x0 * x1 * kPairScale;
-        float dc = 0.0f;
+    for (int q0 = 0; q0 < n; q0 += kU) {
+        // Issue the loads of kU samples before using any of them.
+        float xa[kU], xb[kU];
 #pragma unroll
-        for (int o = 0; o < kO; ++o) {
-            if (O > 0 || o < od) {
-                const float g = g1s[q * od + o];
-                dc = fmaf(g, wcol[o], dc);
-                dw[o] = fmaf(g, c, dw[o]);
+        for (int u = 0; u < kU; ++u) {
+            const int q = q0 + u;
+            if (q < n) {
+                const size_t row = static_cast<size_t>(bs[q]) * W;
+                xa[u] = x[row + j];
+                xb[u] = x[row + j + half];
             }
         }
-        const float pg = dc * kPairScale;
-        const float u0 = pg * x1, u1 = pg * x0;
-        const float p0 = crelu_grad(x0, u0), p1 = crelu_grad(x1, u1);
-        if (a.pregrad_sorted != nullptr) {
-            float* pr = a.pregrad_sorted + static_cast<size_t>(a.rank[2 * b + v]) * W;
-            pr[j] = p0;
-            pr[j + half] = p1;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int q = q0 + u;
+            if (q >= n) break;
+            const float x0 = xa[u], x1 = xb[u];
+            const float c = x0 * x1 * kPairScale;
+            float dc = 0.0f;
+#pragma unroll
+            for (int o = 0; o < kO; ++o) {
+                if (O > 0 || o < od) {
+                    const float g = g1s[q * od + o];
+                    dc = fmaf(g, wcol[o], dc);
+                    dw[o] = fmaf(g, c, dw[o]);
+                }
+            }
+            const float pg = dc * kPairScale;
+            const float u0 = pg * x1, u1 = pg * x0;
+            const float p0 = crelu_grad(x0, u0), p1 = crelu_grad(x1, u1);
+            if (a.pregrad_sorted != nullptr) {
+                float* pr = a.pregrad_sorted + static_cast<size_t>(rs[2 * q + v]) * W;
+                pr[j] = p0;
+                pr[j + half] = p1;
+            }
+            if (a.combined_gradients != nullptr) {
+                const size_t row = static_cast<size_t>(bs[q]) * W;
+                a.combined_gradients[row + i] = dc;
+                a.l0_gradients[v][row + j] = u0;
+                a.l0_gradients[v][row + j + half] = u1;
+                a.pre_gradients[v][row + j] = p0;
+                a.pre_gradients[v][row + j + half] = p1;
+            }
+            p0sum += p0;
+            p1sum += p1;
         }
-        if (a.combined_gradients != nullptr) {
-            a.combined_gradients[row + i] = dc;
-            a.l0_gradients[v][row + j] = u0;
-            a.l0_gradients[v][row + j + half] = u1;
-            a.pre_gradients[v][row + j] = p0;
-            a.pre_gradients[v][row + j + half] = p1;
-        }
-        p0sum += p0;
-        p1sum += p1;
     }
     float* dwp = a.dw1_partials + static_cast<size_t>(t) * od * W;
 #pragma unroll
@@ -788,41 +815,17 @@ struct PieceRowArgs {
     float* gradients;     // kRowWrite / kRowAccumulate target
     RangerArgs ranger;
     int skip_quiet;
+    // The kings are processed in launches of a few king blocks each, so the
+    // gradient rows read by one launch (those of its kings' half-positions)
+    // stay L2-resident.  The per-piece virtual-row sums carry over between
+    // launches in vacc / vany (owned by one warp each: deterministic).
+    int king_begin;
+    int king_end;
+    int first_launch;
+    int last_launch;
+    float* vacc;          // [pieces][width]
+    int* vany;            // [pieces * col_groups]
 };
-
-__device__ __forceinline__ int warp_sort_asc(int v, int lane) {
-#pragma unroll
-    for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            const int other = __shfl_xor_sync(kFull, v, j);
-            const bool ascending = (lane & k) == 0;
-            const bool lower = (lane & j) == 0;
-            const int lo = min(v, other), hi = max(v, other);
-            v = (lower == ascending) ? lo : hi;
-        }
-    }
-    return v;
-}
-
-__device__ void smem_sort_asc(int* buf, int size, int lane) {
-    for (int k = 2; k <= size; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = lane; i < size; i += 32) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const int x = buf[i], y = buf[ixj];
-                    const bool ascending = (i & k) == 0;
-                    if ((x > y) == ascending) {
-                        buf[i] = y;
-                        buf[ixj] = x;
-                    }
-                }
-            }
-            __syncwarp();
-        }
-    }
-}
 
 template <int VEC>
 __device__ __forceinline__ void ldv(const float* p, float* o) {
@@ -901,43 +904,31 @@ __device__ __forceinline__ void row_update(const PieceRowArgs& a, size_t off, co
 // order; every warp walks the kings at about the same pace, so the gradient
 // rows being read at any time belong to a few kings' half-positions (L2).
 template <int VEC, int ITERS, int MODE>
-__global__ void __launch_bounds__(kPieceRowWarps * 32) piece_row_kernel(PieceRowArgs a) {
-    __shared__ int sort_buf[kPieceRowWarps][kPieceSortCap];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gw = blockIdx.x * kPieceRowWarps + warp;
+__device__ __forceinline__ void piece_rows(const PieceRowArgs& a, int gw, int lane) {
     const int p = gw / a.col_groups;
-    if (p >= a.pieces) return;
     const int c0 = (gw - p * a.col_groups) * a.group_width;
     const int c_end = min(a.width, c0 + a.group_width);
+    const bool has_virtual = a.virtual_base >= 0;
     float vacc[ITERS][VEC];
-#pragma unroll
-    for (int it = 0; it < ITERS; ++it)
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) vacc[it][e] = 0.0f;
     bool any = false;
-    for (int k = 0; k < a.kings; ++k) {
+    float* vsave = a.vacc + static_cast<size_t>(p) * a.width;
+#pragma unroll
+    for (int it = 0; it < ITERS; ++it) {
+        const int c = c0 + (it * 32 + lane) * VEC;
+        if (has_virtual && !a.first_launch && c < c_end) {
+            ldv<VEC>(vsave + c, vacc[it]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) vacc[it][e] = 0.0f;
+        }
+    }
+    if (has_virtual && !a.first_launch) any = a.vany[gw] != 0;
+    for (int k = a.king_begin; k < a.king_end; ++k) {
         const int row = k * a.pieces + p;
         const int beg = a.offsets[row];
         const int n = a.offsets[row + 1] - beg;
-        const int* elist = a.entries + beg;
+        const int* elist = a.entries + beg;  // ascending (sort_inverse_index)
         any = any || n > 0;
-        int mine = INT_MAX;
-        int mode = 0;
-        if (n <= 32) {
-            mine = lane < n ? elist[lane] : INT_MAX;
-            mine = warp_sort_asc(mine, lane);
-        } else if (n <= kPieceSortCap) {
-            int size = 64;
-            while (size < n) size <<= 1;
-            int* buf = sort_buf[warp];
-            for (int i = lane; i < size; i += 32) buf[i] = i < n ? elist[i] : INT_MAX;
-            __syncwarp();
-            smem_sort_asc(buf, size, lane);
-            mode = 1;
-        } else {
-            mode = 2;
-        }
-        const int* list = mode == 1 ? sort_buf[warp] : elist;
         const size_t row_off = static_cast<size_t>(row) * a.width;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
@@ -946,29 +937,33 @@ __global__ void __launch_bounds__(kPieceRowWarps * 32) piece_row_kernel(PieceRow
             float acc[VEC];
 #pragma unroll
             for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
-            int q = 0;
-            for (; q + 4 <= n; q += 4) {
-                int en[4];
+            for (int q0 = 0; q0 < n; q0 += 32) {
+                const int m = min(32, n - q0);
+                const int mine = lane < m ? __ldg(elist + q0 + lane) : 0;
+                int q = 0;
+                for (; q + 4 <= m; q += 4) {
+                    int en[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) en[u] = mode == 0 ? __shfl_sync(kFull, mine, q + u) : list[q + u];
-                if (active) {
-                    float x[4][VEC];
+                    for (int u = 0; u < 4; ++u) en[u] = __shfl_sync(kFull, mine, q + u);
+                    if (active) {
+                        float x[4][VEC];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        ldv<VEC>(a.src[en[u] & 1] + static_cast<size_t>(en[u] >> 1) * a.src_stride + c, x[u]);
+                        for (int u = 0; u < 4; ++u)
+                            ldv<VEC>(a.src[en[u] & 1] + static_cast<size_t>(en[u] >> 1) * a.src_stride + c, x[u]);
 #pragma unroll
-                    for (int u = 0; u < 4; ++u)
+                        for (int u = 0; u < 4; ++u)
 #pragma unroll
-                        for (int e = 0; e < VEC; ++e) acc[e] += x[u][e];
+                            for (int e = 0; e < VEC; ++e) acc[e] += x[u][e];
+                    }
                 }
-            }
-            for (; q < n; ++q) {
-                const int en = mode == 0 ? __shfl_sync(kFull, mine, q) : list[q];
-                if (active) {
-                    float x[VEC];
-                    ldv<VEC>(a.src[en & 1] + static_cast<size_t>(en >> 1) * a.src_stride + c, x);
+                for (; q < m; ++q) {
+                    const int en = __shfl_sync(kFull, mine, q);
+                    if (active) {
+                        float x[VEC];
+                        ldv<VEC>(a.src[en & 1] + static_cast<size_t>(en >> 1) * a.src_stride + c, x);
 #pragma unroll
-                    for (int e = 0; e < VEC; ++e) acc[e] += x[e];
+                        for (int e = 0; e < VEC; ++e) acc[e] += x[e];
+                    }
                 }
             }
             if (active) {
@@ -980,7 +975,16 @@ __global__ void __launch_bounds__(kPieceRowWarps * 32) piece_row_kernel(PieceRow
         }
         __syncwarp();
     }
-    if (a.virtual_base < 0) return;
+    if (!has_virtual) return;
+    if (!a.last_launch) {
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+            const int c = c0 + (it * 32 + lane) * VEC;
+            if (c < c_end) stv<VEC>(vsave + c, vacc[it]);
+        }
+        if (lane == 0) a.vany[gw] = any ? 1 : 0;
+        return;
+    }
     const size_t vrow = static_cast<size_t>(a.virtual_base + p) * a.width;
 #pragma unroll
     for (int it = 0; it < ITERS; ++it) {
@@ -997,17 +1001,35 @@ __global__ void __launch_bounds__(kPieceRowWarps * 32) piece_row_kernel(PieceRow
     }
 }
 
+template <int VEC, int ITERS, int MODE>
+__global__ void __launch_bounds__(kPieceRowWarps * 32, 3) piece_row_kernel(PieceRowArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int items = a.pieces * a.col_groups;
+    for (int gw = blockIdx.x * kPieceRowWarps + (threadIdx.x >> 5); gw < items; gw += gridDim.x * kPieceRowWarps)
+        piece_rows<VEC, ITERS, MODE>(a, gw, lane);
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+size_t align_floats(size_t n) { return (n + 63) & ~static_cast<size_t>(63); }
+
 template <int MODE>
-int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec, int iters) {
+int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec) {
+    // Persistent grid: three CTAs per SM, each warp loops over (piece, column
+    // group) work items.
     const int warps = a.pieces * a.col_groups;
-    const int blocks = (warps + kPieceRowWarps - 1) / kPieceRowWarps;
-    if (vec == 8 && iters == 2) piece_row_kernel<8, 2, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
-    else if (vec == 8) piece_row_kernel<8, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
-    else if (vec == 4) piece_row_kernel<4, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
-    else piece_row_kernel<1, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
-    return check_launch("SFNN FT row kernel launch");
+    const int blocks = std::max(1, std::min((warps + kPieceRowWarps - 1) / kPieceRowWarps, 3 * ctx->sm_count));
+    for (int k0 = 0; k0 < a.kings; k0 += kKingsPerLaunch) {
+        a.king_begin = k0;
+        a.king_end = std::min(a.kings, k0 + kKingsPerLaunch);
+        a.first_launch = k0 == 0;
+        a.last_launch = a.king_end == a.kings;
+        if (vec == 8) piece_row_kernel<8, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
+        else if (vec == 4) piece_row_kernel<4, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
+        else piece_row_kernel<1, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
+        if (check_launch("SFNN FT row kernel launch") != 0) return -1;
+    }
+    return 0;
 }
 
 int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a) {
@@ -1016,12 +1038,8 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a) {
         al = al && aligned16(a.weights) && aligned16(a.momentum) && aligned16(a.velocity) && aligned16(a.slow);
     else
         al = al && aligned16(a.gradients);
-    int vec = 1, iters = 1;
-    if (al && a.width % 512 == 0) {
-        vec = 8;
-        iters = 2;
-        a.group_width = 512;
-    } else if (al && a.width % 256 == 0) {
+    int vec = 1;
+    if (al && a.width % 256 == 0) {
         vec = 8;
         a.group_width = 256;
     } else if (al && a.width % 128 == 0) {
@@ -1031,10 +1049,19 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a) {
         a.group_width = 32;
     }
     a.col_groups = (a.width + a.group_width - 1) / a.group_width;
+    if (a.virtual_base >= 0 && a.kings > kKingsPerLaunch) {
+        const size_t vf = align_floats(static_cast<size_t>(a.pieces) * a.width);
+        void* vp = nullptr;
+        if (scratch_slot(ctx, kScratchSfnnVirtual, (vf + static_cast<size_t>(a.pieces) * a.col_groups) * sizeof(float),
+                         &vp, "cudaMalloc SFNN virtual-row sums") != 0)
+            return -1;
+        a.vacc = static_cast<float*>(vp);
+        a.vany = reinterpret_cast<int*>(a.vacc + vf);
+    }
     switch (mode) {
-        case kRowRanger: return launch_piece_rows_mode<kRowRanger>(ctx, a, vec, iters);
-        case kRowWrite: return launch_piece_rows_mode<kRowWrite>(ctx, a, vec, iters);
-        default: return launch_piece_rows_mode<kRowAccumulate>(ctx, a, vec, iters);
+        case kRowRanger: return launch_piece_rows_mode<kRowRanger>(ctx, a, vec);
+        case kRowWrite: return launch_piece_rows_mode<kRowWrite>(ctx, a, vec);
+        default: return launch_piece_rows_mode<kRowAccumulate>(ctx, a, vec);
     }
 }
 
@@ -1050,8 +1077,6 @@ struct SfnnPlan {
     float* l0b_partials;
     float* g1;
 };
-
-size_t align_floats(size_t n) { return (n + 63) & ~static_cast<size_t>(63); }
 
 // Fold, sorts, tile table and effective L1 weights; every scratch the step needs.
 int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, const int* stm, const int* nstm,
@@ -1419,7 +1444,8 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
     SfnnPlan plan{};
     if (sfnn_prepare(ctx, d, w, stm, nstm, buckets, nullptr, &plan) != 0) return -1;
     InverseIndex index;
-    if (build_inverse_index_rows(ctx, stm, nstm, d.batch, d.max_active, d.n_features, &index, plan.king_rank) != 0)
+    if (build_inverse_index_rows(ctx, stm, nstm, d.batch, d.max_active, d.n_features, &index, plan.king_rank) != 0 ||
+        sort_inverse_index(ctx, index) != 0)
         return -1;
     StepBuffers sb{};
     if (step_buffers(ctx, d, output, &sb) != 0) return -1;
@@ -1743,7 +1769,8 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     if (launch_finalize(ctx, d, plan, f) != 0) return -1;
     InverseIndex index;
     if (build_inverse_index_rows(ctx, stm_indices->ptr, nstm_indices->ptr, d.batch, d.max_active, d.n_features, &index,
-                                 nullptr) != 0)
+                                 nullptr) != 0 ||
+        sort_inverse_index(ctx, index) != 0)
         return -1;
     PieceRowArgs r = piece_row_args(d, index);
     r.src[0] = stm_l0_pre_gradients->ptr;

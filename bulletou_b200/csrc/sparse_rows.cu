@@ -153,6 +153,32 @@ __device__ void smem_sort_ascending(int* buf, int size, int lane) {
     }
 }
 
+// Warp per row: ascending sort of the row's entry ids in place.
+__global__ void __launch_bounds__(kRowWarps * 32) sort_rows_kernel(const int* __restrict__ offsets,
+                                                                    int* __restrict__ entries, int n_rows) {
+    __shared__ int buf_s[kRowWarps][kSortCap];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = blockIdx.x * kRowWarps + warp;
+    if (row >= n_rows) return;
+    const int beg = offsets[row];
+    const int n = offsets[row + 1] - beg;
+    int* e = entries + beg;
+    if (n <= 1) return;
+    if (n <= 32) {
+        int v = lane < n ? e[lane] : INT_MAX;
+        v = warp_sort_ascending(v, lane);
+        if (lane < n) e[lane] = v;
+    } else if (n <= kSortCap) {
+        int size = 64;
+        while (size < n) size <<= 1;
+        int* buf = buf_s[warp];
+        for (int i = lane; i < size; i += 32) buf[i] = i < n ? e[i] : INT_MAX;
+        __syncwarp();
+        smem_sort_ascending(buf, size, lane);
+        for (int i = lane; i < n; i += 32) e[i] = buf[i];
+    }
+}
+
 template <int VEC>
 struct Vec {
     float v[VEC];
@@ -375,6 +401,13 @@ int build_index_impl(BulletOuCudaCppContext* ctx, const int* stm, const int* nst
 }
 
 }  // namespace
+
+int sort_inverse_index(BulletOuCudaCppContext* ctx, const InverseIndex& index) {
+    if (index.n_rows <= 0) return 0;
+    const int blocks = (index.n_rows + kRowWarps - 1) / kRowWarps;
+    sort_rows_kernel<<<blocks, kRowWarps * 32, 0, ctx->stream>>>(index.offsets, index.entries, index.n_rows);
+    return check_launch("inverse index row sort launch");
+}
 
 int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
                         size_t max_active, size_t input_size, size_t n_rows, InverseIndex* out,

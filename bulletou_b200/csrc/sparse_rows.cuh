@@ -64,6 +64,11 @@ int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* 
                         size_t max_active, size_t input_size, size_t n_rows, InverseIndex* out,
                         const int* entry_rank = nullptr);
 
+// Sorts every row's entry list ascending in place (rows with more than
+// kSortCap entries are left in fill order), so that consumers can sum a row in
+// a fixed order without sorting it themselves.
+int sort_inverse_index(BulletOuCudaCppContext* ctx, const InverseIndex& index);
+
 // Same, for a plain table: every feature id in [0, n_features) is its own row.
 int build_inverse_index_rows(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
                              size_t max_active, size_t n_features, InverseIndex* out, const int* entry_rank);
