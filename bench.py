@@ -1,12 +1,20 @@
 #!/usr/bin/env python3
-"""Benchmark: HalfKP 256x2-32-32-1 training step.
+"""Benchmark: BulletOu training step on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload sfnn|halfkp]
 
-One "step" = one Ranger train step (forward, sigmoid-WDL loss, backward,
-optimizer over every parameter) on a batch of 16384 synthetic positions
-(seeded, shapes and distributions of the reference's teacher data; see
-bulletou_b200/synthetic.py).  Prints one JSON line (rank 0).
+Workloads (one "step" = one Ranger train step: forward, sigmoid-WDL loss,
+backward, optimizer over every parameter):
+
+* sfnn (default, BASELINE configs[2], the north-star target): SFNN
+  HalfKA_hm2 1536x2 -> LayerStack k3k3 (9 buckets) 1536 -> 15+1 -> 32 -> 1
+  with the FT factorizer (+1629 virtual rows) and the shared L1 factor,
+  f32, 65536 positions per GPU;
+* halfkp: HalfKP 256x2-32-32-1, 16384 positions.
+
+Synthetic seeded batches with the reference teacher data's shapes and
+distributions (bulletou_b200/synthetic.py).  Prints one JSON line (rank 0):
 
 * value      positions/s with the batches already resident in HBM
              (CUDA events on the library's stream, max over ranks);
@@ -21,7 +29,9 @@ bulletou_b200/synthetic.py).  Prints one JSON line (rank 0).
 
 --impl reference times the reference's own cuda-cpp backend (built from its
 sources into oracle/_ref) through the reference runner's call sequence, on the
-same GPU, config and metric.
+same GPU, config and metric.  With N > 1 ranks the product arm trains data
+parallel (per-rank batch fixed: weak scaling) with NCCL reduce-scatter /
+all-reduce / all-gather.
 """
 from __future__ import annotations
 
@@ -49,6 +59,16 @@ PHASES = ("inverse_index", "king_sort", "ft_gather", "dense_fwd_loss_bwd", "batc
           "ft_row_grad_ranger")
 LAUNCHES_PER_STEP = 13  # index 5 + king sort 3 + gather, dense, reduce, finalize, rows
 
+SFNN_BATCH = 65536
+SFNN_ACTIVE = 40
+SFNN_N_BATCHES = 4
+SFNN_METRIC = "train positions/sec (SFNN HalfKA_hm2 1536x2 LayerStack k3k3 15+1-32-1, batch 65536 per GPU)"
+SFNN_PHASES = ("fold", "sorts_tiles", "inverse_index", "ft_forward", "l1_head", "l1_backward", "small_grads_ranger",
+               "ft_rows_ranger")
+# fold 1, king sort 3, bucket sort 3, tile table 1, L1 weights 1, index 5 + row sort 1, FT forward 1,
+# L1 forward 1, head 1, L1 backward 1, finalize 1, Ranger on 9 small groups, FT rows 45 kings / 3 per launch
+SFNN_LAUNCHES_PER_STEP = 1 + 3 + 3 + 1 + 1 + 6 + 1 + 1 + 1 + 1 + 1 + 9 + 15
+
 
 def parse_args():
     ap = argparse.ArgumentParser()
@@ -56,7 +76,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--workload", choices=("sfnn", "halfkp"), default="sfnn")
+    ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -385,25 +406,351 @@ def roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0):
             "phase_ms": {k: round(v, 4) for k, v in phase_ms.items()}}
 
 
+# --------------------------------------------------------------------------- SFNN workload
+def sfnn_shape():
+    from bulletou_b200 import sfnn as bs
+
+    return bs.SFNN_HALFKA_HM2_1536_15_32_K3K3
+
+
+def make_sfnn_batches(batch, rank=0):
+    from bulletou_b200 import synthetic
+
+    return [synthetic.sfnn_batch(2000 + i, batch, rank) for i in range(SFNN_N_BATCHES)]
+
+
+def sfnn_host_weights():
+    from bulletou_b200 import sfnn as bs
+    from bulletou_b200 import synthetic
+
+    return bs.SfnnForwardHostWeights(sfnn_shape(), **synthetic.sfnn_weights(synthetic.rng_for(7)))
+
+
+def sfnn_device_batches(ctx, batches):
+    import bulletou_b200 as bo
+
+    return [(bo.I32Buffer.from_host(ctx, b["stm"]), bo.I32Buffer.from_host(ctx, b["nstm"]),
+             bo.I32Buffer.from_host(ctx, b["buckets"]), bo.F32Buffer.from_host(ctx, b["targets"]),
+             bo.F32Buffer.from_host(ctx, b["entry_weights"])) for b in batches]
+
+
+def bind_sfnn(runner, dev):
+    runner.stm_indices, runner.nstm_indices, runner.buckets, runner.targets, runner.entry_weights = dev
+
+
+def sfnn_cpu_baseline(batch_cap=256, budget_s=8.0):
+    """CPU oracle SFNN forward (C restatement of the reference's CPU
+    evaluation path, fast_sfnn.rs:325-386), one thread, bounded sample."""
+    from bulletou_b200 import synthetic
+    from oracle import oracle
+
+    sh = sfnn_shape()
+    w = synthetic.sfnn_weights(synthetic.rng_for(7))
+    b = synthetic.sfnn_batch(4242, batch_cap)
+    args = (sh.as_tuple(), b["stm"], b["nstm"], b["buckets"])
+    oracle.sfnn_forward(sh.as_tuple(), b["stm"][:SFNN_ACTIVE * 8], b["nstm"][:SFNN_ACTIVE * 8], b["buckets"][:8], 8,
+                        SFNN_ACTIVE, w)  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.sfnn_forward(*args, batch_cap, SFNN_ACTIVE, w)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": reps * batch_cap / dt, "unit": "positions/s (forward only)", "cores": 1, "kind": "port",
+            "sample": f"oracle SFNN 1536 forward, {reps} x {batch_cap} positions in {dt:.1f} s "
+                      f"(the reference cannot train on CPU; its CPU path is evaluation only)"}
+
+
+def _profile(lib, ctx, marks):
+    import ctypes
+
+    ms = (ctypes.c_float * 16)()
+    nsteps, nphases = ctypes.c_size_t(), ctypes.c_size_t()
+    lib.call("bulletou_b200_profile_end", ctx.as_ptr(), ms, 16, ctypes.byref(nsteps), ctypes.byref(nphases))
+    return {SFNN_PHASES[p]: ms[p] / max(1, nsteps.value) for p in range(min(nphases.value, len(SFNN_PHASES)))}
+
+
+def run_sfnn_b200(args, rank, world, local, dist):
+    import bulletou_b200 as bo
+    from bulletou_b200 import sfnn as bs
+    from bulletou_b200.cuda_cpp import PinnedF32Buffer
+
+    if world > 1:
+        return run_sfnn_data_parallel(args, rank, world, local, dist)
+    ctx = bo.Context(local)
+    runner = bs.SfnnTrainStepRunner(ctx, sfnn_host_weights(), args.batch, SFNN_ACTIVE, fused=True)
+    batches = make_sfnn_batches(args.batch, rank)
+    devb = sfnn_device_batches(ctx, batches)
+    loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
+    inv = 1.0 / 600.0
+    step = 0
+    for i in range(args.warmup):
+        step += 1
+        bind_sfnn(runner, devb[i % len(devb)])
+        runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=False)
+    ctx.synchronize()
+    lib = ctx.lib
+    start, stop = bo.Event(ctx), bo.Event(ctx)
+    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 9 * args.steps + 9)
+    with ClockSampler(local) as clocks:
+        start.record(ctx)
+        for i in range(args.steps):
+            step += 1
+            bind_sfnn(runner, devb[i % len(devb)])
+            runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=False)
+        stop.record(ctx)
+        stop.synchronize()
+    phase_ms = _profile(lib, ctx, 9)
+    total_ms = stop.elapsed_ms_since(start)
+    clk = clocks.summary()
+    # ---- end to end through the public runner API (pipelined step, lib.rs:7627) ----
+    upload_ctx = bo.Context(local)
+    sources = []
+    for b in batches:  # the data loader's output: batches already in pinned host memory
+        slot = bs.SfnnTrainStepUploadSlot(ctx, args.batch, SFNN_ACTIVE)
+        slot.fill(bs.SfnnTrainStepHostBatch(b["stm"], b["nstm"], b["buckets"], b["targets"], b["entry_weights"],
+                                            args.batch, SFNN_ACTIVE))
+        sources.append(slot)
+    e2e_steps = max(8, args.steps)
+    loss_ring = [PinnedF32Buffer(ctx, 1) for _ in range(e2e_steps)]
+    for i in range(3):
+        step += 1
+        runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv, None, True,
+                                                             sources[i % len(sources)], loss_ring[i])
+    ctx.synchronize()
+    upload_ctx.synchronize()
+    h2d = 0
+    e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    t0 = time.perf_counter()
+    e0.record(ctx)
+    for i in range(e2e_steps):
+        step += 1
+        h2d = runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv, None,
+                                                                   True, sources[i % len(sources)], loss_ring[i])
+    e1.record(ctx)
+    e1.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1000.0
+    losses = [float(r.host()[0]) for r in loss_ring]
+    e2e_ms = max(e1.elapsed_ms_since(e0), wall_ms)
+    assert all(np.isfinite(losses)), "non-finite loss"
+    return {
+        "total_ms": total_ms, "phase_ms": phase_ms, "clocks": clk,
+        "e2e": {"value": e2e_steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
+                "path": "SfnnTrainStepRunner.step_pipelined_no_readback_with_loss_finalize (2 upload slots, "
+                        "second stream), inputs in pinned host memory, mean loss copied D2H every step"},
+        "gpu_launches": SFNN_LAUNCHES_PER_STEP * args.steps,
+        "final_loss": losses[-1],
+    }
+
+
+def run_sfnn_data_parallel(args, rank, world, local, dist):
+    """N > 1: weak scaling, args.batch positions per rank (NCCL exchange)."""
+    import torch
+
+    import bulletou_b200 as bo
+    from bulletou_b200.cuda_cpp import F32Buffer, I32Buffer, PinnedF32Buffer, PinnedI32Buffer
+    from bulletou_b200.data_parallel import B200Backend, SfnnDataParallelTrainer
+
+    backend = B200Backend(local)
+    ctx, lib = backend.ctx, backend.lib
+    tr = SfnnDataParallelTrainer(backend, dist, sfnn_host_weights(), args.batch, SFNN_ACTIVE)
+    batches = make_sfnn_batches(args.batch, rank)
+    devb = sfnn_device_batches(ctx, batches)
+    loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
+    inv = 1.0 / 600.0
+    step = 0
+
+    def bind(i):
+        tr.stm_indices, tr.nstm_indices, tr.buckets, tr.targets, tr.entry_weights = devb[i % len(devb)]
+
+    for i in range(args.warmup):
+        step += 1
+        bind(i)
+        tr.step_device(ranger(step), loss_kind, inv, finalize_loss=False)
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, stop = bo.Event(ctx), bo.Event(ctx)
+    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 9 * args.steps + 9)
+    with ClockSampler(local) as clocks:
+        start.record(ctx)
+        for i in range(args.steps):
+            step += 1
+            bind(i)
+            tr.step_device(ranger(step), loss_kind, inv, finalize_loss=False)
+        stop.record(ctx)
+        stop.synchronize()
+    phase_ms = _profile(lib, ctx, 9)
+    torch.cuda.synchronize()
+    dist.barrier()
+    total_ms = max_over_ranks(dist, stop.elapsed_ms_since(start))
+    # end to end: per step H2D from pinned host memory, step, D2H of the mean loss
+    pins = []
+    for b in batches:
+        p = (PinnedI32Buffer(ctx, b["stm"].size), PinnedI32Buffer(ctx, b["nstm"].size),
+             PinnedI32Buffer(ctx, args.batch), PinnedF32Buffer(ctx, args.batch), PinnedF32Buffer(ctx, args.batch))
+        for dst, src in zip(p, (b["stm"], b["nstm"], b["buckets"], b["targets"], b["entry_weights"])):
+            np.copyto(dst.host(), src)
+        pins.append(p)
+    n = args.batch * SFNN_ACTIVE
+    in_bufs = (I32Buffer(ctx, n), I32Buffer(ctx, n), I32Buffer(ctx, args.batch), F32Buffer(ctx, args.batch),
+               F32Buffer(ctx, args.batch))
+    tr.stm_indices, tr.nstm_indices, tr.buckets, tr.targets, tr.entry_weights = in_bufs
+    e2e_steps = max(8, args.steps)
+    ring = [PinnedF32Buffer(ctx, 1) for _ in range(e2e_steps)]
+    dist.barrier()
+    e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    t0 = time.perf_counter()
+    e0.record(ctx)
+    h2d = 0
+    for i in range(e2e_steps):
+        step += 1
+        p = pins[i % len(pins)]
+        c = ctx.as_ptr()
+        for dst, src in zip(in_bufs, p):
+            name = "bulletou_b200_i32_upload_pinned" if isinstance(dst, I32Buffer) else "bulletou_b200_f32_upload_pinned"
+            lib.call(name, c, dst.as_ptr(), src.as_ptr(), src.length)
+        h2d = 4 * sum(x.length for x in p)
+        tr.step_device(ranger(step), loss_kind, inv, finalize_loss=True)
+        lib.call("bulletou_b200_f32_download_pinned", c, ring[i].as_ptr(), tr.loss_workspace.mean.as_ptr(), 1)
+    e1.record(ctx)
+    e1.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1000.0
+    e2e_ms = max_over_ranks(dist, max(e1.elapsed_ms_since(e0), wall_ms))
+    losses = [float(r.host()[0]) for r in ring]
+    assert all(np.isfinite(losses)), "non-finite loss"
+    # the fused row kernel becomes a gradient-write pass; Ranger runs per group on the shard
+    return {"total_ms": total_ms, "phase_ms": phase_ms, "clocks": clocks.summary(),
+            "e2e": {"value": e2e_steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
+                    "path": "SfnnDataParallelTrainer.step_device per rank (NCCL reduce-scatter / all-reduce / "
+                            "all-gather), inputs from pinned host memory, mean loss copied D2H every step"},
+            "gpu_launches": (SFNN_LAUNCHES_PER_STEP + 1) * args.steps,
+            "final_loss": losses[-1]}
+
+
+def run_sfnn_reference(args, local):
+    import bulletou_b200 as bo
+    from bulletou_b200 import sfnn as bs
+
+    lib = bo.reference_library()
+    ctx = bo.Context(local, lib)
+    runner = bs.SfnnTrainStepRunner(ctx, sfnn_host_weights(), args.batch, SFNN_ACTIVE, fused=False)
+    batches = make_sfnn_batches(args.batch)
+    devb = sfnn_device_batches(ctx, batches)
+    loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
+    inv = 1.0 / 600.0
+    step = 0
+    for i in range(args.warmup):
+        step += 1
+        bind_sfnn(runner, devb[i % len(devb)])
+        runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=False)
+    ctx.synchronize()
+    start, stop = bo.Event(ctx), bo.Event(ctx)
+    with ClockSampler(local) as clocks:
+        start.record(ctx)
+        for i in range(args.steps):
+            step += 1
+            bind_sfnn(runner, devb[i % len(devb)])
+            runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=False)
+        stop.record(ctx)
+        stop.synchronize()
+    total_ms = stop.elapsed_ms_since(start)
+    clk = clocks.summary()
+    upload_ctx = bo.Context(local, lib)
+    hbs = [bs.SfnnTrainStepHostBatch(b["stm"], b["nstm"], b["buckets"], b["targets"], b["entry_weights"], args.batch,
+                                     SFNN_ACTIVE) for b in batches]
+    e2e_steps = max(4, args.steps // 2)
+    for i in range(2):
+        step += 1
+        runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv,
+                                                             hbs[i % len(hbs)], True)
+        runner.loss_workspace.mean.download(ctx)
+    ctx.synchronize()
+    e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    t0 = time.perf_counter()
+    e0.record(ctx)
+    h2d = 0
+    for i in range(e2e_steps):
+        step += 1
+        h2d = runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv,
+                                                                   hbs[i % len(hbs)], True)
+        runner.loss_workspace.mean.download(ctx)
+    e1.record(ctx)
+    e1.synchronize()
+    e2e_ms = max(e1.elapsed_ms_since(e0), (time.perf_counter() - t0) * 1000.0)
+    return {"total_ms": total_ms, "clocks": clk,
+            "e2e": {"value": e2e_steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": e2e_steps}}
+
+
+def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0):
+    """Algorithmic bytes per launch of each SFNN phase (the per-position
+    formulas of the hot-path table; gathers counted at their logical size, so
+    a fraction above 1 means L2 serves the repeated rows)."""
+    sh = sfnn_shape()
+    W, A = sh.ft_size, SFNN_ACTIVE
+    rows = sh.input_size
+    base = sh.factorized_base()
+    half_positions = 2 * batch
+    algo = {
+        "fold": base * W * 4 * 2 + 1629 * W * 4,
+        # logical rows gathered + indices + ClippedReLU outputs (2 views) and combined written
+        "ft_forward": half_positions * A * W * 4 + half_positions * A * 4 + 3 * batch * W * 4,
+        # every FT row's optimizer state (w, m, v read + written; slow on lookahead steps)
+        # + the pre-activation gradients gathered (logical) + the inverse index
+        "ft_rows_ranger": rows * W * 4 * (6 + 2 * lookahead_frac) + half_positions * A * W * 4
+                          + 4 * (half_positions * A + base + 1),
+        # both views' FT outputs read, pre-activation gradients written, L1 weight partials
+        "l1_backward": 2 * batch * W * 4 + 2 * batch * W * 4 + (batch // 128 + 11) * 16 * W * 4,
+        "l1_head": batch * W * 4 + batch * 4 * (16 + 30 + 32 + 16 + 4),
+        "inverse_index": 4 * (half_positions * A * 3 + base * 4),
+        "sorts_tiles": 4 * (half_positions * A + 4 * half_positions + 3 * batch),
+        "small_grads_ranger": 0.0,
+    }
+    dom = max(phase_ms, key=phase_ms.get)
+    t = phase_ms[dom] / 1000.0
+    achieved = algo.get(dom, 0.0) / t / 1e9 if t > 0 else 0.0
+    return {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind, "traffic": None,
+            "algorithmic_bytes_per_launch": int(algo.get(dom, 0.0)), "launch_ms": round(phase_ms[dom], 4),
+            "phase_ms": {k: round(v, 4) for k, v in phase_ms.items()}}
+
+
 def main():
     args = parse_args()
     rank, world, local, dist = dist_setup(args)
     if args.warmup < 3:
         args.warmup = 3
-    config = {"workload": "configs[1] HalfKP 256x2-32-32-1 train step", "model": "HalfKP 125388x256x2-32-32-1",
-              "global_batch": args.batch * world, "per_gpu_batch": args.batch, "seq_len": 1,
-              "max_active": ACTIVE, "optimizer": "Ranger (RAdam + Lookahead k=6, lr 1e-3)",
+    sfnn = args.workload == "sfnn"
+    if args.batch is None:
+        args.batch = SFNN_BATCH if sfnn else BATCH
+    common = {"global_batch": args.batch * world, "per_gpu_batch": args.batch, "seq_len": 1,
+              "optimizer": "Ranger (RAdam + Lookahead k=6, lr 1e-3)",
               "loss": "sigmoid-WDL MSE, scale 600, lambda 0.5",
-              "parallelism": f"dp{world}" if world > 1 else "single",
-              "l2": "no flush: each step streams 0.5 GB of optimizer state (> 126 MB L2)"}
-    base = {"metric": METRIC, "unit": "positions/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+              "parallelism": f"dp{world}" if world > 1 else "single"}
+    if sfnn:
+        metric = SFNN_METRIC
+        config = dict({"workload": "configs[2] SFNN HalfKA_hm2 1536x2 LayerStack k3k3 train step",
+                       "model": "SFNN_halfkahm2_1536_15_32_k3k3: (73305+1629 virtual) x 1536 FT, pairwise, "
+                                "9 x (1536 -> 15+1), shared L1 factor, 30 -> 32 -> 1",
+                       "max_active": SFNN_ACTIVE, "buckets": "uniform 0..8",
+                       "l2": "no flush: each step streams 1.8 GB of FT optimizer state (> 126 MB L2)"}, **common)
+    else:
+        metric = METRIC
+        config = dict({"workload": "configs[1] HalfKP 256x2-32-32-1 train step",
+                       "model": "HalfKP 125388x256x2-32-32-1", "max_active": ACTIVE,
+                       "l2": "no flush: each step streams 0.5 GB of optimizer state (> 126 MB L2)"}, **common)
+    base = {"metric": metric, "unit": "positions/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; reference teacher-data shapes and distributions)", "config": config}
     if args.impl == "reference":
         if rank != 0:
             return
         try:
-            r = run_reference(args, local)
+            r = run_sfnn_reference(args, local) if sfnn else run_reference(args, local)
         except (FileNotFoundError, OSError) as e:
             print(json.dumps({"impl": "reference", "unavailable": f"reference backend not built: {e}"}))
             return
@@ -414,19 +761,21 @@ def main():
                     arm="reference cuda-cpp backend built from its own sources (oracle/_ref), driven through its "
                         "C ABI in the reference runner's call order, same GPU/config/metric",
                     cpu_baseline={"value": round(value, 1), "unit": "positions/s", "cores": 0, "kind": "reference",
-                                  "sample": f"{args.steps} steps x {args.batch} positions on the GPU (not a CPU run)"})
+                                  "sample": f"{args.steps} steps x {args.batch} positions on the GPU: the reference's "
+                                            f"implementation of this path is its CUDA backend (not a CPU run)"})
         print(json.dumps(line))
         return
-    r = run_b200(args, rank, world, local, dist)
+    r = run_sfnn_b200(args, rank, world, local, dist) if sfnn else run_b200(args, rank, world, local, dist)
     value = args.steps * args.batch * world / (r["total_ms"] / 1000.0)
     if rank == 0:
         hbm, kind = measured_peaks()
+        rl = sfnn_roofline(r["phase_ms"], args.batch, hbm, kind) if sfnn else roofline(r["phase_ms"], args.batch, hbm,
+                                                                                          kind)
         line = dict(base, value=round(value, 1), ms_per_step=round(r["total_ms"] / args.steps, 4),
                     e2e={k: (round(v, 1) if isinstance(v, float) else v) for k, v in r["e2e"].items()},
-                    roofline=roofline(r["phase_ms"], args.batch, hbm, kind), clocks=r["clocks"],
-                    gpu_launches=r["gpu_launches"], final_loss=r["final_loss"])
+                    roofline=rl, clocks=r["clocks"], gpu_launches=r["gpu_launches"], final_loss=r["final_loss"])
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline()
+            line["cpu_baseline"] = sfnn_cpu_baseline() if sfnn else cpu_baseline()
         print(json.dumps(line))
     if dist is not None:
         dist.barrier()

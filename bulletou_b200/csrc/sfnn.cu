@@ -1781,6 +1781,62 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     return ok();
 }
 
+int bulletou_b200_sfnn_dense_gradient_len(const BulletOuB200SfnnShape* shape, int has_l1f, int has_l2f, int has_l3f,
+                                          size_t* out) {
+    if (shape == nullptr || out == nullptr) return fail_message("SFNN dense_gradient_len arguments must not be null");
+    SfnnDims d{};
+    if (sfnn_dims(shape->input_size, shape->ft_size, shape->l1_hidden, shape->l1_skip, shape->l2_size,
+                  shape->num_stacks, 1, 1, shape->ft_factorizer_alpha, shape->factorizer_shared_alpha, &d) != 0)
+        return -1;
+    d.has_l1f = has_l1f != 0;
+    d.has_l2f = has_l2f != 0;
+    d.has_l3f = has_l3f != 0;
+    *out = sfnn_group_layout(d).begin[kSfGroups];
+    return ok();
+}
+
+int bulletou_b200_sfnn_local_gradients_device(
+    BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* targets,
+    const BulletOuCudaCppF32Buffer* entry_weights, const BulletOuB200LossSpec* loss,
+    BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* ft_gradients,
+    BulletOuCudaCppF32Buffer* dense_gradients, BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean) {
+    if (shape == nullptr || params == nullptr) return fail_message("SFNN shape / parameter array must not be null");
+    SfnnDims d{};
+    LossArgs la{};
+    if (sfnn_dims(shape->input_size, shape->ft_size, shape->l1_hidden, shape->l1_skip, shape->l2_size,
+                  shape->num_stacks, batch, max_active, shape->ft_factorizer_alpha, shape->factorizer_shared_alpha,
+                  &d) != 0 ||
+        loss_args(loss, batch, &la) != 0)
+        return -1;
+    d.has_l1f = params[4] != nullptr;
+    d.has_l2f = params[8] != nullptr;
+    d.has_l3f = params[12] != nullptr;
+    const SfnnGroupLayout g = sfnn_group_layout(d);
+    if (validate_sfnn_weights(ctx, d, params, "params") != 0 ||
+        validate_i32(ctx, stm_indices, batch * max_active, "stm_indices") != 0 ||
+        validate_i32(ctx, nstm_indices, batch * max_active, "nstm_indices") != 0 ||
+        validate_i32(ctx, buckets, batch, "buckets") != 0 || validate_f32(ctx, targets, batch, "targets") != 0 ||
+        validate_f32(ctx, entry_weights, batch, "entry_weights") != 0 ||
+        validate_f32(ctx, ft_gradients, static_cast<size_t>(d.input_size) * d.width, "ft_gradients") != 0 ||
+        validate_f32(ctx, dense_gradients, g.begin[kSfGroups], "dense_gradients") != 0 ||
+        validate_f32(ctx, output, batch, "output") != 0 || validate_f32(ctx, per_sample, batch, "per_sample") != 0 ||
+        validate_f32(ctx, mean_output_gradients, batch, "mean_output_gradients") != 0 ||
+        validate_f32(ctx, weighted_sum, 1, "weighted_sum") != 0 || validate_f32(ctx, mean, 1, "mean") != 0)
+        return -1;
+    if (set_device(ctx) != 0) return -1;
+    const SfnnWeights w = weights_from(params);
+    if (sfnn_step(ctx, d, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr, targets->ptr, entry_weights->ptr, la,
+                  loss->finalize_loss, nullptr, nullptr, nullptr, nullptr, nullptr, output->ptr, per_sample->ptr,
+                  mean_output_gradients->ptr, weighted_sum->ptr, mean->ptr, ft_gradients->ptr,
+                  dense_gradients->ptr) != 0)
+        return -1;
+    return ok();
+}
+
 int bulletou_b200_sfnn_train_step_device(
     BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
     const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,

@@ -1,4 +1,4 @@
-"""Data-parallel HalfKP training over torch.distributed (NCCL on GPUs, gloo on CPU).
+"""Data-parallel HalfKP and SFNN training over torch.distributed (NCCL on GPUs, gloo on CPU).
 
 The reference trains on one GPU (no collectives, cu:9503-9545); this module is
 the additive multi-GPU layer.  Positions are independent, so the only
@@ -21,7 +21,10 @@ rows (padding rows are never referenced by a feature).  A step on N ranks of
 batch B equals one single-GPU step on the concatenated batch of N*B up to
 summation order.
 
-`NnueDataParallelTrainer` holds the orchestration; the arithmetic comes from a
+`NnueDataParallelTrainer` / `SfnnDataParallelTrainer` hold the orchestration
+(the SFNN one shards the FT table including its virtual factor rows, whose
+local gradients are already alpha * the king-row sums, so the reduce-scatter
+sums them like any other row); the arithmetic comes from a
 backend: `B200Backend` (the CUDA library, zero-copy torch views of its
 buffers, collectives ordered on the library's stream) for training, and, in
 tests, a CPU backend built on the oracle so the sharding and collective logic
@@ -113,6 +116,22 @@ class B200Backend:
                       tr.ft_grad.as_ptr(), tr.dense_grad.as_ptr(), tr.output.as_ptr(), lw.per_sample.as_ptr(),
                       lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(), lw.mean.as_ptr())
 
+    def sfnn_local_gradients(self, tr: "SfnnDataParallelTrainer", loss_spec) -> None:
+        from ._lib import SfnnShape
+
+        sh = tr.shape
+        shape = SfnnShape(sh.input_size, sh.ft_size, sh.l1_hidden, int(sh.l1_skip), sh.l2_size, sh.num_stacks,
+                          tr.alpha.ft, tr.alpha.shared)
+        arr = ctypes.c_void_p * 14
+        params = arr(*[(None if w is None else w.as_ptr().value) for w in tr.weight_list()])
+        lw = tr.loss_workspace
+        self.lib.call("bulletou_b200_sfnn_local_gradients_device", self.ctx.as_ptr(), ctypes.byref(shape),
+                      tr.batch_size, tr.max_active, tr.stm_indices.as_ptr(), tr.nstm_indices.as_ptr(),
+                      tr.buckets.as_ptr(), tr.targets.as_ptr(), tr.entry_weights.as_ptr(), ctypes.byref(loss_spec),
+                      params, tr.ft_grad.as_ptr(), tr.dense_grad.as_ptr(), tr.output.as_ptr(),
+                      lw.per_sample.as_ptr(), lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(),
+                      lw.mean.as_ptr())
+
     def ranger(self, params: RangerUpdateParams, grad, weights, m, v, slow) -> None:
         ranger_update_device(self.ctx, params, RangerDeviceState(grad, weights, m, v, slow))
 
@@ -194,6 +213,114 @@ class NnueDataParallelTrainer:
     def read_weights(self) -> dict:
         out = {n: self.backend.download(w) for n, w in zip(NNUE_WEIGHT_NAMES, self.weights)}
         out["l0w"] = out["l0w"][: self.shape.input_size * self.shape.l1]
+        return out
+
+
+def sfnn_dense_gradient_layout(shape, present: dict) -> list[tuple[str, int, int]]:
+    """(group, offset, length) of the packed SFNN small-parameter gradient:
+    the groups after l0w in update order, absent shared factors omitted."""
+    from .sfnn import SFNN_WEIGHT_NAMES
+
+    lens = shape.weight_lengths()
+    out, off = [], 0
+    for name in SFNN_WEIGHT_NAMES[1:]:
+        if present[name]:
+            out.append((name, off, lens[name]))
+            off += lens[name]
+    return out
+
+
+class SfnnDataParallelTrainer:
+    """One rank of data-parallel SFNN training (default layer multipliers)."""
+
+    def __init__(self, backend, dist, initial_weights, batch_size: int, max_active: int, alpha=None):
+        from .sfnn import SFNN_WEIGHT_NAMES, SfnnFactorizerAlpha
+
+        initial_weights.validate()
+        self.backend = backend
+        self.dist = dist
+        self.world = dist.get_world_size()
+        self.rank = dist.get_rank()
+        self.shape = initial_weights.shape
+        self.alpha = alpha or SfnnFactorizerAlpha()
+        self.batch_size, self.max_active = batch_size, max_active
+        sh = self.shape
+        W = sh.ft_size
+        self.layout = ShardLayout(sh.input_size, W, self.world, self.rank)
+        lay = self.layout
+        arrays = initial_weights.arrays()
+        self.present = {n: arrays[n] is not None for n in SFNN_WEIGHT_NAMES}
+        l0w = np.zeros(lay.rows_padded * W, np.float32)
+        l0w[: arrays["l0w"].size] = arrays["l0w"]
+        self.weights = {"l0w": backend.from_host(l0w)}
+        for n in SFNN_WEIGHT_NAMES[1:]:
+            self.weights[n] = None if arrays[n] is None else backend.from_host(arrays[n])
+        own = slice(lay.row_begin * W, (lay.row_begin + lay.real_rows) * W)
+        n_own = lay.real_rows * W
+        self.ft_state = (backend.zeros(n_own), backend.zeros(n_own), backend.from_host(l0w[own]))
+        self.dense_layout = sfnn_dense_gradient_layout(sh, self.present)
+        self.small_state = {n: (backend.zeros(arrays[n].size), backend.zeros(arrays[n].size), backend.from_host(arrays[n]))
+                            for n, _, _ in self.dense_layout}
+        self.ft_grad = backend.zeros(lay.rows_padded * W)
+        total = self.dense_layout[-1][1] + self.dense_layout[-1][2]
+        self.dense_grad = backend.zeros(total)
+        ctx = getattr(backend, "ctx", None)
+        n = batch_size * max_active
+        if ctx is not None:
+            self.stm_indices, self.nstm_indices = I32Buffer(ctx, n), I32Buffer(ctx, n)
+            self.buckets = I32Buffer(ctx, batch_size)
+            self.targets, self.entry_weights = F32Buffer(ctx, batch_size), F32Buffer(ctx, batch_size)
+            self.output = F32Buffer(ctx, batch_size)
+            self.loss_workspace = ScalarLossWorkspace(ctx, batch_size)
+        self.ft_grad_shard = backend.view(self.ft_grad, lay.row_begin * W, lay.real_rows * W)
+        self.l0w_shard = backend.view(self.weights["l0w"], lay.row_begin * W, lay.real_rows * W)
+        self.dense_views = {name: backend.view(self.dense_grad, off, k) for name, off, k in self.dense_layout}
+        self._t_ft_grad = backend.tensor(self.ft_grad)
+        self._t_l0w = backend.tensor(self.weights["l0w"])
+        self._t_dense = backend.tensor(self.dense_grad)
+
+    def weight_list(self) -> list:
+        from .sfnn import SFNN_WEIGHT_NAMES
+
+        return [self.weights[n] for n in SFNN_WEIGHT_NAMES]
+
+    def upload_batch(self, stm, nstm, buckets, targets, entry_weights) -> None:
+        self.stm_indices.upload(stm)
+        self.nstm_indices.upload(nstm)
+        self.buckets.upload(buckets)
+        self.targets.upload(targets)
+        self.entry_weights.upload(entry_weights)
+
+    def exchange_and_update(self, params: RangerUpdateParams) -> None:
+        from dataclasses import replace
+
+        from .sfnn import factor_contribution_clip
+
+        params = replace(params, norm_loss_strength=0.0, norm_loss_before=False)  # lib.rs:6416-6420
+        lay, W = self.layout, self.shape.ft_size
+        chunk = lay.shard_rows * W
+        shard_t = self._t_ft_grad[self.rank * chunk:(self.rank + 1) * chunk]
+        self.dist.reduce_scatter_tensor(shard_t, self._t_ft_grad)
+        self.dist.all_reduce(self._t_dense)
+        if lay.real_rows > 0:
+            m, v, slow = self.ft_state
+            self.backend.ranger(params, self.ft_grad_shard, self.l0w_shard, m, v, slow)
+        for name, _, _ in self.dense_layout:
+            p = factor_contribution_clip(params, self.alpha.shared) if name in ("l1fw", "l1fb") else params
+            m, v, slow = self.small_state[name]
+            self.backend.ranger(p, self.dense_views[name], self.weights[name], m, v, slow)
+        own_t = self._t_l0w[self.rank * chunk:(self.rank + 1) * chunk]
+        self.dist.all_gather_into_tensor(self._t_l0w, own_t)
+
+    def step_device(self, params: RangerUpdateParams, loss_kind: ScalarLossKind, output_inv_scale: float,
+                    finalize_loss: bool = True) -> None:
+        spec = loss_kind.spec(output_inv_scale, finalize_loss, normalizer=self.batch_size * self.world)
+        self.backend.sfnn_local_gradients(self, spec)
+        self.exchange_and_update(params)
+
+    def read_weights(self) -> dict:
+        out = {n: self.backend.download(w) for n, w in self.weights.items() if w is not None}
+        out["l0w"] = out["l0w"][: self.shape.input_size * self.shape.ft_size]
         return out
 
 

@@ -226,6 +226,29 @@ int bulletou_b200_sfnn_train_step_device(
     BulletOuCudaCppF32Buffer* per_sample, BulletOuCudaCppF32Buffer* mean_output_gradients,
     BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean);
 
+/* Length of the packed SFNN small-parameter gradient (groups l0b l1w l1b
+ * [l1fw l1fb] l2w l2b [l2fw l2fb] l3w l3b [l3fw l3fb], absent shared factors
+ * omitted) used by the data-parallel phases. */
+int bulletou_b200_sfnn_dense_gradient_len(const BulletOuB200SfnnShape* shape, int has_l1f, int has_l2f, int has_l3f,
+    size_t* out);
+
+/* SFNN data-parallel phase 1: forward + loss + backward of a rank's local
+ * batch (the loss normalizer in `loss` is the global batch).  Overwrites
+ * ft_gradients [input_size*ft_size, virtual factor rows included] with the
+ * batch's FT gradient and dense_gradients [sfnn_dense_gradient_len] with the
+ * packed small-parameter gradient; params as in sfnn_train_step_device.
+ * The exchange (reduce-scatter / all-reduce) and the update
+ * (ranger_update_device on views) are the caller's. */
+int bulletou_b200_sfnn_local_gradients_device(
+    BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* targets,
+    const BulletOuCudaCppF32Buffer* entry_weights, const BulletOuB200LossSpec* loss,
+    BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* ft_gradients,
+    BulletOuCudaCppF32Buffer* dense_gradients, BulletOuCudaCppF32Buffer* output,
+    BulletOuCudaCppF32Buffer* per_sample, BulletOuCudaCppF32Buffer* mean_output_gradients,
+    BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,20 @@ class CpuOracleBackend:
         for (name, off, n) in tr.dense_layout:
             tr.dense_grad[off:off + n] = torch.from_numpy(g[f"{name}_gradients"])
 
+    def sfnn_local_gradients(self, tr, spec):
+        sh = tr.shape
+        w = {n: (None if b is None else b.numpy()) for n, b in tr.weights.items()}
+        w["l0w"] = w["l0w"][: sh.input_size * sh.ft_size]
+        args = (sh.as_tuple(), tr.stm, tr.nstm, tr.buckets, tr.batch_size, tr.max_active)
+        fwd = oracle.sfnn_forward(*args, w, tr.alpha.ft, tr.alpha.shared)
+        loss = oracle.scalar_loss(spec.kind, spec.output_inv_scale, spec.loss_pow_exp, spec.loss_param,
+                                  fwd["output"], tr.targets, tr.entry_weights, normalizer=spec.normalizer)
+        g = oracle.sfnn_backward(*args, fwd, w, loss["mean_output_gradients"], tr.alpha.ft, tr.alpha.shared)
+        tr.ft_grad.zero_()
+        tr.ft_grad[: sh.input_size * sh.ft_size] = torch.from_numpy(g["l0w_gradients"])
+        for (name, off, n) in tr.dense_layout:
+            tr.dense_grad[off:off + n] = torch.from_numpy(g[f"{name}_gradients"])
+
     def ranger(self, params, grad, weights, m, v, slow):
         p = params.radam
         oracle.ranger_update(grad.numpy(), weights.numpy(), m.numpy(), v.numpy(), slow.numpy(), step=p.step,
@@ -131,4 +145,69 @@ def test_two_rank_step_equals_single_process_global_batch(tmp_path):
         ref.step(b["stm"], b["nstm"], 2 * BATCH, A, b["targets"], b["entry_weights"], step=step, learning_rate=0.01,
                  min_weight=-2.0, max_weight=2.0)
     for k in oracle.NAMES:
+        np.testing.assert_allclose(got[k], ref.w[k], rtol=1e-5, atol=1e-6, err_msg=k)
+
+
+# ---------------------------------------------------------------- SFNN
+from bulletou_b200 import sfnn as bs  # noqa: E402
+from bulletou_b200.data_parallel import SfnnDataParallelTrainer  # noqa: E402
+
+SF_SHAPE = bs.SfnnForwardShape(73305 + 1629, 4, 2, True, 3, 3)  # factorized HalfKA_hm2, tiny widths
+SF_ALPHA = bs.SfnnFactorizerAlpha(0.5, 2.0)
+SF_A = 6
+
+
+def _sf_weights():
+    rng = np.random.default_rng(15)
+    lens = SF_SHAPE.weight_lengths()
+    return {n: rng.normal(0, 0.3, lens[n]).astype(np.float32) for n in bs.SFNN_WEIGHT_NAMES}
+
+
+def _sf_batches(steps):
+    rng = np.random.default_rng(19)
+    out = []
+    for _ in range(steps):
+        n = 2 * BATCH * SF_A
+        kings = rng.integers(0, 45, (2 * BATCH * 2, 1))
+        feats = (kings * 1629 + rng.integers(0, 1629, (2 * BATCH * 2, SF_A))).reshape(2, -1).astype(np.int32)
+        out.append({"stm": feats[0][:n], "nstm": feats[1][:n],
+                    "buckets": rng.integers(0, SF_SHAPE.num_stacks, 2 * BATCH).astype(np.int32),
+                    "targets": rng.random(2 * BATCH).astype(np.float32),
+                    "entry_weights": np.ones(2 * BATCH, np.float32)})
+    return out
+
+
+def _sf_rank_main(rank, world, port, steps, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tr = SfnnDataParallelTrainer(CpuOracleBackend(), dist, bs.SfnnForwardHostWeights(SF_SHAPE, **_sf_weights()),
+                                     BATCH, SF_A, SF_ALPHA)
+        for step, b in enumerate(_sf_batches(steps), start=1):
+            sl = slice(rank * BATCH * SF_A, (rank + 1) * BATCH * SF_A)
+            bsl = slice(rank * BATCH, (rank + 1) * BATCH)
+            tr.stm, tr.nstm, tr.buckets = b["stm"][sl], b["nstm"][sl], b["buckets"][bsl]
+            tr.targets, tr.entry_weights = b["targets"][bsl], b["entry_weights"][bsl]
+            tr.step_device(_params(step), ScalarLossKind.SigmoidPow(2.0), 1.0)
+        got = tr.read_weights()
+        if rank == 0:
+            np.savez(out_path, **got)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_two_rank_sfnn_step_equals_single_process_global_batch(tmp_path):
+    """Factorized FT (virtual rows sharded like any row), shared L1 factor with
+    its scaled clip bounds, alpha != 1."""
+    steps = 7
+    out = tmp_path / "rank0.npz"
+    mp.start_processes(_sf_rank_main, args=(2, _free_port(), steps, str(out)), nprocs=2, start_method="spawn")
+    got = np.load(out)
+    ref = oracle.SfnnTrainer(SF_SHAPE.as_tuple(), _sf_weights(), SF_ALPHA.ft, SF_ALPHA.shared)
+    for step, b in enumerate(_sf_batches(steps), start=1):
+        ref.step(b["stm"], b["nstm"], b["buckets"], 2 * BATCH, SF_A, b["targets"], b["entry_weights"], step=step,
+                 learning_rate=0.01, min_weight=-2.0, max_weight=2.0)
+    for k in ref.names:
         np.testing.assert_allclose(got[k], ref.w[k], rtol=1e-5, atol=1e-6, err_msg=k)

@@ -88,3 +88,73 @@ def test_two_gpu_data_parallel_matches_single_gpu_global_batch(tmp_path):
         scale = max(float(np.abs(v).max()), 1e-30)
         err = float(np.abs(got[k].astype(np.float64) - v).max())
         assert err <= 1e-4 * scale, f"{k}: max |diff| {err:.3e} (scale {scale:.3e})"
+
+
+# ---------------------------------------------------------------- SFNN
+SF_BATCH = 1024  # per rank
+
+
+def _sf_batches():
+    return [synthetic.sfnn_batch(800 + i, 2 * SF_BATCH) for i in range(STEPS)]
+
+
+def _sf_rank_main(rank, world, port, out_path):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import bulletou_b200 as bo
+    from bulletou_b200 import sfnn as bs
+    from bulletou_b200.data_parallel import B200Backend, SfnnDataParallelTrainer
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        w = synthetic.sfnn_weights(synthetic.rng_for(23), ft=256)
+        shape = bs.SfnnForwardShape(73305 + 1629, 256, 15, True, 32, 9)
+        tr = SfnnDataParallelTrainer(B200Backend(rank), dist, bs.SfnnForwardHostWeights(shape, **w), SF_BATCH, 40)
+        for step, b in enumerate(_sf_batches(), start=1):
+            sl = slice(rank * SF_BATCH * 40, (rank + 1) * SF_BATCH * 40)
+            bsl = slice(rank * SF_BATCH, (rank + 1) * SF_BATCH)
+            tr.upload_batch(b["stm"][sl], b["nstm"][sl], b["buckets"][bsl], b["targets"][bsl],
+                            b["entry_weights"][bsl])
+            tr.step_device(_params(step), bo.ScalarLossKind.SigmoidPow(2.0), 1 / 600)
+        torch.cuda.synchronize()
+        got = tr.read_weights()
+        if rank == 0:
+            np.savez(out_path, **got)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+def test_two_gpu_sfnn_data_parallel_matches_single_gpu_global_batch(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = tmp_path / "rank0.npz"
+    mp.start_processes(_sf_rank_main, args=(2, _free_port(), str(out)), nprocs=2, start_method="spawn")
+    got = np.load(out)
+
+    import bulletou_b200 as bo
+    from bulletou_b200 import sfnn as bs
+
+    w = synthetic.sfnn_weights(synthetic.rng_for(23), ft=256)
+    shape = bs.SfnnForwardShape(73305 + 1629, 256, 15, True, 32, 9)
+    ctx = bo.Context(0)
+    runner = bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(shape, **w), 2 * SF_BATCH, 40)
+    for step, b in enumerate(_sf_batches(), start=1):
+        hb = bs.SfnnTrainStepHostBatch(b["stm"], b["nstm"], b["buckets"], b["targets"], b["entry_weights"],
+                                       2 * SF_BATCH, 40)
+        runner.step_no_readback(ctx, _params(step), bo.ScalarLossKind.SigmoidPow(2.0), 1 / 600, hb)
+    ref = runner.read_weights(ctx)
+    for k, v in ref.items():
+        scale = max(float(np.abs(v).max()), 1e-30)
+        err = float(np.abs(got[k].astype(np.float64) - v).max())
+        assert err <= 1e-4 * scale, f"{k}: max |diff| {err:.3e} (scale {scale:.3e})"
