@@ -95,6 +95,8 @@ SF_BATCH = 1024  # per rank
 
 
 def _sf_batches():
+    from bulletou_b200 import synthetic
+
     return [synthetic.sfnn_batch(800 + i, 2 * SF_BATCH) for i in range(STEPS)]
 
 
@@ -105,6 +107,7 @@ def _sf_rank_main(rank, world, port, out_path):
 
     import bulletou_b200 as bo
     from bulletou_b200 import sfnn as bs
+    from bulletou_b200 import synthetic
     from bulletou_b200.data_parallel import B200Backend, SfnnDataParallelTrainer
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -144,6 +147,7 @@ def test_two_gpu_sfnn_data_parallel_matches_single_gpu_global_batch(tmp_path):
 
     import bulletou_b200 as bo
     from bulletou_b200 import sfnn as bs
+    from bulletou_b200 import synthetic
 
     w = synthetic.sfnn_weights(synthetic.rng_for(23), ft=256)
     shape = bs.SfnnForwardShape(73305 + 1629, 256, 15, True, 32, 9)
