@@ -47,13 +47,16 @@ __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f),
 __device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f && a < 1.0f ? g : 0.0f; }
 
 // ------------------------------------------------------------------ gather
+// A lane owns columns [4*lane, 4*lane+4) and [128+4*lane, 128+4*lane+4) of
+// every 256-column block, so each warp-wide float4 load reads 512 contiguous
+// bytes (4 L1 wavefronts).
 template <int Q>
 __device__ __forceinline__ void add_row(float (&acc)[Q][8], const float* __restrict__ l0w, int row, int lane) {
-    const float* p = l0w + static_cast<size_t>(row) * (Q * 256) + lane * 8;
+    const float* p = l0w + static_cast<size_t>(row) * (Q * 256) + lane * 4;
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
         const float4 a = __ldg(reinterpret_cast<const float4*>(p + q * 256));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(p + q * 256 + 4));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p + q * 256 + 128));
         acc[q][0] += a.x; acc[q][1] += a.y; acc[q][2] += a.z; acc[q][3] += a.w;
         acc[q][4] += b.x; acc[q][5] += b.y; acc[q][6] += b.z; acc[q][7] += b.w;
     }
@@ -62,14 +65,14 @@ __device__ __forceinline__ void add_row(float (&acc)[Q][8], const float* __restr
 template <int Q>
 __device__ __forceinline__ void add_row_pair(float (&acc)[Q][8], const float* __restrict__ l0w, int r0, int r1,
                                              int lane) {
-    const float* p0 = l0w + static_cast<size_t>(r0) * (Q * 256) + lane * 8;
-    const float* p1 = l0w + static_cast<size_t>(r1) * (Q * 256) + lane * 8;
+    const float* p0 = l0w + static_cast<size_t>(r0) * (Q * 256) + lane * 4;
+    const float* p1 = l0w + static_cast<size_t>(r1) * (Q * 256) + lane * 4;
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
         const float4 a0 = __ldg(reinterpret_cast<const float4*>(p0 + q * 256));
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(p0 + q * 256 + 4));
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(p0 + q * 256 + 128));
         const float4 a1 = __ldg(reinterpret_cast<const float4*>(p1 + q * 256));
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(p1 + q * 256 + 4));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(p1 + q * 256 + 128));
         acc[q][0] += a0.x + a1.x; acc[q][1] += a0.y + a1.y; acc[q][2] += a0.z + a1.z; acc[q][3] += a0.w + a1.w;
         acc[q][4] += b0.x + b1.x; acc[q][5] += b0.y + b1.y; acc[q][6] += b0.z + b1.z; acc[q][7] += b0.w + b1.w;
     }
@@ -82,8 +85,8 @@ __device__ __forceinline__ void gather_perspective(float (&acc)[Q][8], const int
                                                    const float* __restrict__ l0b, int lane) {
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(l0b + q * 256 + lane * 8));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(l0b + q * 256 + lane * 8 + 4));
+        const float4 a = __ldg(reinterpret_cast<const float4*>(l0b + q * 256 + lane * 4));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(l0b + q * 256 + lane * 4 + 128));
         acc[q][0] = a.x; acc[q][1] = a.y; acc[q][2] = a.z; acc[q][3] = a.w;
         acc[q][4] = b.x; acc[q][5] = b.y; acc[q][6] = b.z; acc[q][7] = b.w;
     }
@@ -112,12 +115,12 @@ __device__ __forceinline__ void gather_perspective(float (&acc)[Q][8], const int
             float4 x[4][Q][2];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const float* p = l0w + static_cast<size_t>(ok[u] ? f[u] : 0) * (Q * 256) + lane * 8;
+                const float* p = l0w + static_cast<size_t>(ok[u] ? f[u] : 0) * (Q * 256) + lane * 4;
 #pragma unroll
                 for (int q = 0; q < Q; ++q) {
                     if (ok[u]) {
                         x[u][q][0] = __ldg(reinterpret_cast<const float4*>(p + q * 256));
-                        x[u][q][1] = __ldg(reinterpret_cast<const float4*>(p + q * 256 + 4));
+                        x[u][q][1] = __ldg(reinterpret_cast<const float4*>(p + q * 256 + 128));
                     }
                 }
             }
@@ -153,18 +156,18 @@ __global__ void __launch_bounds__(kGatherWarps * 32) ft_gather_kernel(
     const int b = h >> 1, persp = h & 1;
     float acc[Q][8];
     gather_perspective<Q>(acc, (persp ? nstm : stm) + static_cast<size_t>(b) * A, A, map, l0w, l0b, lane);
-    float* out = act + static_cast<size_t>(b) * (2 * L1) + persp * L1 + lane * 8;
+    float* out = act + static_cast<size_t>(b) * (2 * L1) + persp * L1 + lane * 4;
     float* side = persp ? nstm_l0 : stm_l0;
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
         const float4 lo = make_float4(crelu01(acc[q][0]), crelu01(acc[q][1]), crelu01(acc[q][2]), crelu01(acc[q][3]));
         const float4 hi = make_float4(crelu01(acc[q][4]), crelu01(acc[q][5]), crelu01(acc[q][6]), crelu01(acc[q][7]));
         *reinterpret_cast<float4*>(out + q * 256) = lo;
-        *reinterpret_cast<float4*>(out + q * 256 + 4) = hi;
+        *reinterpret_cast<float4*>(out + q * 256 + 128) = hi;
         if (side != nullptr) {
-            float* sp = side + static_cast<size_t>(b) * L1 + q * 256 + lane * 8;
+            float* sp = side + static_cast<size_t>(b) * L1 + q * 256 + lane * 4;
             *reinterpret_cast<float4*>(sp) = lo;
-            *reinterpret_cast<float4*>(sp + 4) = hi;
+            *reinterpret_cast<float4*>(sp + 128) = hi;
         }
     }
 }

@@ -186,9 +186,9 @@ struct Vec {
 
 template <int VEC>
 __device__ __forceinline__ void load_vec(const float* p, float* out) {
-    if constexpr (VEC == 8) {
+    if constexpr (VEC == 8) {  // columns [c, c+4) and [c+128, c+132): see lane_col
         const float4 a = *reinterpret_cast<const float4*>(p);
-        const float4 b = *reinterpret_cast<const float4*>(p + 4);
+        const float4 b = *reinterpret_cast<const float4*>(p + 128);
         out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
         out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
     } else if constexpr (VEC == 4) {
@@ -204,7 +204,7 @@ template <int VEC>
 __device__ __forceinline__ void store_vec(float* p, const float* in) {
     if constexpr (VEC == 8) {
         *reinterpret_cast<float4*>(p) = make_float4(in[0], in[1], in[2], in[3]);
-        *reinterpret_cast<float4*>(p + 4) = make_float4(in[4], in[5], in[6], in[7]);
+        *reinterpret_cast<float4*>(p + 128) = make_float4(in[4], in[5], in[6], in[7]);
     } else if constexpr (VEC == 4) {
         *reinterpret_cast<float4*>(p) = make_float4(in[0], in[1], in[2], in[3]);
     } else {
@@ -261,7 +261,9 @@ __global__ void __launch_bounds__(kRowWarps * 32, 3) row_kernel(RowKernelArgs a,
     const size_t row_off = static_cast<size_t>(row) * a.width;
     const size_t out_off = static_cast<size_t>(local) * a.width;
     for (int col0 = 0; col0 < a.width; col0 += 32 * VEC) {
-        const int c = col0 + lane * VEC;
+        // VEC = 8: a lane owns [c, c+4) and [c+128, c+132), so every warp-wide
+        // float4 access is 512 contiguous bytes (4 L1 wavefronts, not 8).
+        const int c = VEC == 8 ? col0 + lane * 4 : col0 + lane * VEC;
         const bool active = c < a.width;
         // Optimizer state (or the gradient row being accumulated) does not
         // depend on the entry list: issue those loads first so their HBM
