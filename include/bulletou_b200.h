@@ -88,9 +88,11 @@ int bulletou_b200_f32_buffer_view(const BulletOuCudaCppF32Buffer* buffer, size_t
  * profile_begin reserves room for `max_marks` events; profile_end waits for
  * the stream and returns in ms_out[i] the summed time between consecutive
  * marks i and i+1 of every step (phase i), in *steps_out the steps recorded
- * and in *phases_out the phases per step.  HalfKP phases: 0 inverse index,
- * 1 fused forward/loss/backward, 2 dense weight gradients, 3 small-parameter
- * Ranger + loss finalize, 4 feature-transformer row gradient + Ranger. */
+ * and in *phases_out the phases per step.  HalfKP step phases: inverse index,
+ * king sort, FT gather, dense forward/loss/backward, batch reduce,
+ * small-group Ranger + loss, FT rows.  SFNN step phases: fold, sorts + tiles,
+ * inverse index, FT forward, L1 forward + head, L1 backward, small-group
+ * Ranger + loss, FT rows. */
 int bulletou_b200_profile_begin(BulletOuCudaCppContext* ctx, size_t max_marks);
 int bulletou_b200_profile_end(BulletOuCudaCppContext* ctx, float* ms_out, size_t ms_len, size_t* steps_out,
     size_t* phases_out);
