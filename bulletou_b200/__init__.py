@@ -30,11 +30,16 @@ from .cuda_cpp import (  # noqa: F401
 
 from .sfnn import (  # noqa: F401
     SFNN_HALFKA_HM2_1536_15_32_K3K3,
+    QuantizedRounding,
+    QuantizedSfnnDeviceWeights,
+    SfnnIntegerForwardWorkspace,
     SfnnFactorizerAlpha,
     SfnnForwardHostWeights,
     SfnnForwardShape,
     SfnnTrainStepHostBatch,
     SfnnTrainStepRunner,
+    sfnn_integer_forward_device,
+    sfnn_quantize_device,
 )
 
 __version__ = "0.1.0"

@@ -49,6 +49,13 @@ class SfnnShape(ctypes.Structure):
                 ("num_stacks", Z), ("ft_factorizer_alpha", F), ("factorizer_shared_alpha", F)]
 
 
+class QuantRounding(ctypes.Structure):
+    """BulletOuB200QuantRounding."""
+
+    _fields_ = [("ft_shift", I), ("ft_round", I), ("crelu_round", I), ("sqr_clipped_relu_round", I),
+                ("final_div_round", I), ("fv_scale", I)]
+
+
 class LossSpec(ctypes.Structure):
     """BulletOuB200LossSpec."""
 
@@ -138,6 +145,8 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_sfnn_train_step_device": [P, P, Z, Z] + [P] * 16,
     "bulletou_b200_sfnn_dense_gradient_len": [P, I, I, I, P],
     "bulletou_b200_sfnn_local_gradients_device": [P, P, Z, Z] + [P] * 14,
+    "bulletou_b200_sfnn_quantize_device": [P, P, P, P],
+    "bulletou_b200_sfnn_integer_forward_device": [P, P, Z, Z] + [P] * 9,
 }
 
 

@@ -104,6 +104,7 @@ enum ScratchSlot : int {
     kScratchSfnnGrads = 18,     // SFNN packed small-parameter gradients
     kScratchSfnnEff = 19,       // SFNN effective (shared-factor folded) dense weights
     kScratchSfnnVirtual = 20,   // SFNN per-piece virtual-row gradient sums between row launches
+    kScratchSfnnQuant = 21,     // SFNN integer forward: FT pair values + king sort
 };
 
 int ok();

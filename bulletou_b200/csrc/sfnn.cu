@@ -1330,6 +1330,8 @@ PieceRowArgs piece_row_args(const SfnnDims& d, const InverseIndex& index) {
 }
 
 // ------------------------------------------------------------------ validation
+}  // namespace
+
 int sfnn_dims(size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip, size_t l2_size, size_t num_stacks,
               size_t batch, size_t max_active, float ft_alpha, float shared_alpha, SfnnDims* d) {
     if (input_size == 0 || ft_size == 0 || l1_hidden == 0 || l2_size == 0 || num_stacks == 0 || batch == 0 ||
@@ -1364,6 +1366,8 @@ int sfnn_dims(size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip, 
     d->shared_alpha = shared_alpha;
     return 0;
 }
+
+namespace {
 
 int validate_sfnn_weights(BulletOuCudaCppContext* ctx, const SfnnDims& d, const BulletOuCudaCppF32Buffer* const* p,
                           const char* what) {

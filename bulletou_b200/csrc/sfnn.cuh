@@ -115,4 +115,9 @@ inline SfnnGroupLayout sfnn_group_layout(const SfnnDims& d) {
     return g;
 }
 
+// Checks an SFNN shape against this backend's limits and fills `d`
+// (has_l*f are left zero).  0 or -1 with the error message set.
+int sfnn_dims(size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip, size_t l2_size, size_t num_stacks,
+              size_t batch, size_t max_active, float ft_alpha, float shared_alpha, SfnnDims* d);
+
 }  // namespace bou

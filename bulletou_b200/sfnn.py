@@ -20,7 +20,7 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import CudaCppError, SfnnShape
+from ._lib import CudaCppError, QuantRounding, SfnnShape
 from .cuda_cpp import (FLT_MAX, Context, Event, F32Buffer, I32Buffer, PinnedF32Buffer, PinnedI32Buffer,
                        RangerDeviceState, RangerParamState, RangerUpdateParams, ScalarLossKind, ScalarLossReadback,
                        ScalarLossWorkspace, ranger_update_device, scalar_loss_device)
@@ -475,3 +475,117 @@ class SfnnTrainStepRunner:
 
     def read_optimizer_states(self, ctx: Optional[Context] = None) -> dict:
         return {n: s.download(ctx) for n, s in self.optimizer_states.items() if s is not None}
+
+
+# ------------------------------------------------------------------ quantised SFNN
+SFNN_QUANT_NAMES = ("l0w", "l0b", "l1w", "l1b", "l2w", "l2b", "l3w", "l3b")
+_QUANT_DTYPES = {"l0w": np.int16, "l0b": np.int16, "l1w": np.int8, "l1b": np.int32, "l2w": np.int8,
+                 "l2b": np.int32, "l3w": np.int8, "l3b": np.int32}
+
+
+def _pad32(n: int) -> int:
+    return (n + 31) // 32 * 32
+
+
+@dataclass(frozen=True)
+class QuantizedRounding:
+    """The integer evaluator's rounding switches (examples/bulletou.rs:1254-1340
+    defaults: FV_SCALE 24, ft shift 7, every right shift floored)."""
+
+    ft_shift: int = 7
+    ft_round: bool = False
+    crelu_round: bool = False
+    sqr_clipped_relu_round: bool = False
+    final_div_round: bool = False
+    fv_scale: int = 24
+
+    def as_struct(self) -> QuantRounding:
+        return QuantRounding(int(self.ft_shift), int(self.ft_round), int(self.crelu_round),
+                             int(self.sqr_clipped_relu_round), int(self.final_div_round), int(self.fv_scale))
+
+
+class QuantizedSfnnDeviceWeights:
+    """Engine-format quantised SFNN weights on the device
+    (QuantizedSfnnWeights, examples/bulletou.rs:7355-7377): FT i16 rows with the
+    factorizer folded, dense i8 rows padded to 32 inputs, i32 biases.  Each
+    tensor lives in an I32 buffer holding the packed narrow integers."""
+
+    def __init__(self, ctx: Context, shape: SfnnForwardShape):
+        self.shape = shape
+        base = shape.factorized_base()
+        self.rows = base if base else shape.input_size
+        S, O, L2 = shape.num_stacks, shape.l1_out, shape.l2_size
+        self.counts = {"l0w": self.rows * shape.ft_size, "l0b": shape.ft_size,
+                       "l1w": S * O * _pad32(shape.ft_size), "l1b": S * O,
+                       "l2w": S * L2 * _pad32(shape.l2_in), "l2b": S * L2, "l3w": S * _pad32(L2), "l3b": S}
+        self.buffers = {}
+        for n in SFNN_QUANT_NAMES:
+            nbytes = self.counts[n] * np.dtype(_QUANT_DTYPES[n]).itemsize
+            self.buffers[n] = I32Buffer(ctx, (nbytes + 3) // 4)
+
+    def _array(self):
+        arr = (ctypes.c_void_p * len(SFNN_QUANT_NAMES))()
+        for k, n in enumerate(SFNN_QUANT_NAMES):
+            arr[k] = self.buffers[n].as_ptr().value
+        return arr
+
+    def download(self, ctx: Optional[Context] = None) -> dict:
+        out = {}
+        for n in SFNN_QUANT_NAMES:
+            words = self.buffers[n].download(ctx)
+            out[n] = words.view(_QUANT_DTYPES[n])[: self.counts[n]].copy()
+        return out
+
+    def upload(self, arrays: dict, ctx: Optional[Context] = None) -> None:
+        for n in SFNN_QUANT_NAMES:
+            a = np.ascontiguousarray(arrays[n], dtype=_QUANT_DTYPES[n]).reshape(-1)
+            if a.size != self.counts[n]:
+                raise ValueError(f"quantised {n}: expected {self.counts[n]} values, got {a.size}")
+            raw = np.zeros(self.buffers[n].length * 4, np.uint8)
+            raw[: a.nbytes] = a.view(np.uint8)
+            self.buffers[n].upload(raw.view(np.int32), ctx)
+
+
+def _shape_struct(shape: SfnnForwardShape, alpha: SfnnFactorizerAlpha) -> SfnnShape:
+    return SfnnShape(shape.input_size, shape.ft_size, shape.l1_hidden, int(shape.l1_skip), shape.l2_size,
+                     shape.num_stacks, alpha.ft, alpha.shared)
+
+
+def sfnn_quantize_device(ctx: Context, shape: SfnnForwardShape, weights: dict, out: QuantizedSfnnDeviceWeights,
+                         alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha()) -> None:
+    """Export quantisation on the device (bulletou_b200_sfnn_quantize_device;
+    quantized_sfnn_weights_from_cuda_cpp_readback, examples/bulletou.rs:10050-10300)."""
+    params = (ctypes.c_void_p * 14)()
+    for k, n in enumerate(SFNN_WEIGHT_NAMES):
+        params[k] = None if weights.get(n) is None else weights[n].as_ptr().value
+    sh = _shape_struct(shape, alpha)
+    ctx.lib.call("bulletou_b200_sfnn_quantize_device", ctx.as_ptr(), ctypes.byref(sh), params, out._array())
+
+
+class SfnnIntegerForwardWorkspace:
+    """Outputs of the integer forward: raw i32 evaluation, i32 L1 sums, the
+    engine score raw / FV_SCALE and the error counter."""
+
+    def __init__(self, ctx: Context, shape: SfnnForwardShape, batch_size: int):
+        self.raw = I32Buffer(ctx, batch_size)
+        self.l1 = I32Buffer(ctx, batch_size * shape.l1_out)
+        self.score = I32Buffer(ctx, batch_size)
+        self.errors = I32Buffer(ctx, 1)
+
+    def download(self, ctx: Optional[Context] = None) -> dict:
+        return {"raw": self.raw.download(ctx), "l1": self.l1.download(ctx), "score": self.score.download(ctx),
+                "errors": int(self.errors.download(ctx)[0])}
+
+
+def sfnn_integer_forward_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int,
+                                stm: I32Buffer, nstm: I32Buffer, buckets: I32Buffer,
+                                weights: QuantizedSfnnDeviceWeights, ws: SfnnIntegerForwardWorkspace,
+                                rounding: QuantizedRounding = QuantizedRounding()) -> None:
+    """Integer forward of a batch (bulletou_b200_sfnn_integer_forward_device;
+    quantized_sfnn_forward_sample + quantized_final_division,
+    examples/bulletou.rs:8001-8163)."""
+    sh = _shape_struct(shape, SfnnFactorizerAlpha())
+    r = rounding.as_struct()
+    ctx.lib.call("bulletou_b200_sfnn_integer_forward_device", ctx.as_ptr(), ctypes.byref(sh), batch_size,
+                 max_active, stm.as_ptr(), nstm.as_ptr(), buckets.as_ptr(), weights._array(), ctypes.byref(r),
+                 ws.l1.as_ptr(), ws.raw.as_ptr(), ws.score.as_ptr(), ws.errors.as_ptr())

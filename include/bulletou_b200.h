@@ -251,6 +251,56 @@ int bulletou_b200_sfnn_local_gradients_device(
     BulletOuCudaCppF32Buffer* per_sample, BulletOuCudaCppF32Buffer* mean_output_gradients,
     BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean);
 
+/* ---------------------------------------------------------------- quantised SFNN
+ * The reference evaluates a trained SFNN through the engine's integer network
+ * on the CPU (examples/bulletou.rs: export quantisation 10050-10300, integer
+ * forward quantized_sfnn_forward_sample 8001-8163, final division 8045-8054).
+ * These two entries run the same integer arithmetic on the device; they have
+ * no counterpart in the reference's C ABI.
+ *
+ * Quantised buffers (I32 handles holding packed narrow integers, lengths in
+ * 32-bit words rounded up), in this order:
+ *   0 l0w  i16 [rows][ft_size]     rows = the factorizer base (73305 / 131949)
+ *                                  when input_size carries the virtual rows,
+ *                                  else input_size; virtual rows folded in
+ *   1 l0b  i16 [ft_size]
+ *   2 l1w  i8  [stacks][l1_out][pad32(ft_size)]   shared L1 factor folded in
+ *   3 l1b  i32 [stacks][l1_out]
+ *   4 l2w  i8  [stacks][l2_size][pad32(2*l1_hidden)]
+ *   5 l2b  i32 [stacks][l2_size]
+ *   6 l3w  i8  [stacks][pad32(l2_size)]
+ *   7 l3b  i32 [stacks]
+ * Scales: FT 127 (i16), dense weights 64 (i8), dense biases 127*64 (i32);
+ * round half away from zero, saturating. */
+typedef struct BulletOuB200QuantRounding {
+    int ft_shift;               /* sfnn_ft_shift, 0..16 (reference default 7) */
+    int ft_round;               /* 0 floor, 1 nearest (quant_ft_round) */
+    int crelu_round;            /* quant_crelu_round */
+    int sqr_clipped_relu_round; /* quant_sqrcrelu_round */
+    int final_div_round;        /* quant_final_div_round */
+    int fv_scale;               /* > 0: score = raw / fv_scale */
+} BulletOuB200QuantRounding;
+
+/* Quantises f32 SFNN parameters (14 handles as in sfnn_train_step_device;
+ * absent shared factors null) into the 8 buffers above.  Replaces
+ * quantized_sfnn_weights_from_cuda_cpp_readback (bulletou.rs:10050-10300). */
+int bulletou_b200_sfnn_quantize_device(BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape,
+    BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppI32Buffer* const* quantized);
+
+/* Integer forward of a batch with quantised weights: raw_output[batch] (i32,
+ * the engine's raw evaluation), optional l1_out[batch][l1_out] (i32 L1 sums)
+ * and score_output[batch] (raw / fv_scale with final_div_round).  Features
+ * below 0 are padding; features at or above the table's rows are skipped and
+ * buckets out of range give raw 0, each counted in errors[0] when errors is
+ * given (the reference stops with an error for either).  shape is the
+ * training shape (input_size with or without the virtual rows). */
+int bulletou_b200_sfnn_integer_forward_device(BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape,
+    size_t batch, size_t max_active, const BulletOuCudaCppI32Buffer* stm_indices,
+    const BulletOuCudaCppI32Buffer* nstm_indices, const BulletOuCudaCppI32Buffer* buckets,
+    BulletOuCudaCppI32Buffer* const* quantized, const BulletOuB200QuantRounding* rounding,
+    BulletOuCudaCppI32Buffer* l1_out, BulletOuCudaCppI32Buffer* raw_output, BulletOuCudaCppI32Buffer* score_output,
+    BulletOuCudaCppI32Buffer* errors);
+
 #ifdef __cplusplus
 }
 #endif

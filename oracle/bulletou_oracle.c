@@ -565,3 +565,184 @@ EXPORT void oracle_sfnn_backward(const int64_t* shape, const float* alphas, cons
     free(pre_s);
     free(pre_n);
 }
+
+/* ------------------------------------------------------------------ quantised SFNN
+ * Export quantisation of a trained SFNN (examples/bulletou.rs:10050-10300,
+ * quantized_sfnn_weights_from_cuda_cpp_readback): fold the FT factorizer
+ * (bulletou.rs:26417-26444, f32 `w + alpha * w_virtual`, no fused multiply-add)
+ * and the shared L1 / L2 / L3 factors (bulletou.rs:21339-21520,
+ * `w += alpha * shared`), then round(x * scale) half away from zero in double
+ * and clamp (bulletou.rs:26481-26493): FT i16 at 127, dense i8 at 64, dense
+ * biases i32 at 127 * 64.  Dense rows are padded to a multiple of 32 inputs
+ * with zeros (nnue_save_sfnn1536.rs layout). */
+static int64_t pad32(int64_t n) { return (n + 31) / 32 * 32; }
+
+static int16_t q_i16(float v, float s) {
+    double q = round((double)v * (double)s);
+    if (q < -32768.0) q = -32768.0;
+    if (q > 32767.0) q = 32767.0;
+    return (int16_t)q;
+}
+static int8_t q_i8(float v, float s) {
+    double q = round((double)v * (double)s);
+    if (q < -128.0) q = -128.0;
+    if (q > 127.0) q = 127.0;
+    return (int8_t)q;
+}
+static int32_t q_i32(float v, float s) {
+    double q = round((double)v * (double)s);
+    if (q < -2147483648.0) q = -2147483648.0;
+    if (q > 2147483647.0) q = 2147483647.0;
+    return (int32_t)q;
+}
+
+EXPORT void oracle_sfnn_quantize(const int64_t* shape, const float* alphas, const float* const* w, int16_t* l0w_q,
+                                 int16_t* l0b_q, int8_t* l1w_q, int32_t* l1b_q, int8_t* l2w_q, int32_t* l2b_q,
+                                 int8_t* l3w_q, int32_t* l3b_q) {
+    sfnn_dims d = sfnn_make_dims(shape, alphas);
+    const int64_t W = d.width, O = d.l1_out, L2 = d.l2, I2 = d.l2_in, S = d.stacks;
+    const int64_t rows = d.base ? d.base : d.input_size;
+    const float a = d.shared_alpha;
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t j = 0; j < W; ++j) {
+            float v = w[0][r * W + j];
+            if (d.base) {
+                float t = d.ft_alpha * w[0][(d.base + r % SFNN_PIECES) * W + j];
+                v = v + t;
+            }
+            l0w_q[r * W + j] = q_i16(v, 127.0f);
+        }
+    for (int64_t j = 0; j < W; ++j) l0b_q[j] = q_i16(w[1][j], 127.0f);
+    const int64_t p1 = pad32(W), p2 = pad32(I2), p3 = pad32(L2);
+    for (int64_t s = 0; s < S; ++s) {
+        for (int64_t o = 0; o < O; ++o) {
+            float b = w[3][s * O + o];
+            if (w[5]) { float t = a * w[5][o]; b = b + t; }
+            l1b_q[s * O + o] = q_i32(b, 8128.0f);
+            for (int64_t i = 0; i < p1; ++i) {
+                int8_t q = 0;
+                if (i < W) {
+                    float v = w[2][(s * O + o) * W + i];
+                    if (w[4]) { float t = a * w[4][i * O + o]; v = v + t; }
+                    q = q_i8(v, 64.0f);
+                }
+                l1w_q[(s * O + o) * p1 + i] = q;
+            }
+        }
+        for (int64_t o = 0; o < L2; ++o) {
+            float b = w[7][s * L2 + o];
+            if (w[9]) { float t = a * w[9][o]; b = b + t; }
+            l2b_q[s * L2 + o] = q_i32(b, 8128.0f);
+            for (int64_t i = 0; i < p2; ++i) {
+                int8_t q = 0;
+                if (i < I2) {
+                    float v = w[6][(s * L2 + o) * I2 + i];
+                    if (w[8]) { float t = a * w[8][o * I2 + i]; v = v + t; }
+                    q = q_i8(v, 64.0f);
+                }
+                l2w_q[(s * L2 + o) * p2 + i] = q;
+            }
+        }
+        float b3 = w[11][s];
+        if (w[13]) { float t = a * w[13][0]; b3 = b3 + t; }
+        l3b_q[s] = q_i32(b3, 8128.0f);
+        for (int64_t i = 0; i < p3; ++i) {
+            int8_t q = 0;
+            if (i < L2) {
+                float v = w[10][s * L2 + i];
+                if (w[12]) { float t = a * w[12][i]; v = v + t; }
+                q = q_i8(v, 64.0f);
+            }
+            l3w_q[s * p3 + i] = q;
+        }
+    }
+}
+
+/* Integer SFNN forward of one batch (examples/bulletou.rs:8001-8163,
+ * quantized_sfnn_forward_sample): FT sums of doubled i16 weights and bias
+ * wrapped to i16, clamped to [0, 254], pair product (s0 << ft_shift) * s1 >> 16
+ * (floor or nearest) clamped to 255; L1 = bias + sum u8 * i8; L2 input
+ * SqrCReLU min(x^2 >> 19, 127) | CReLU clamp(x >> 6, 0, 127); L2 the same
+ * CReLU; raw output = l3 bias + sum + l1 skip.  round: 0 floor, 1 nearest
+ * (ft, crelu, sqrcrelu).  Features < 0 are padding; features >= the table's
+ * rows and buckets out of range are reported through *error (first sample,
+ * or -1 when none) like the reference's errors.  quantised weights as written
+ * by oracle_sfnn_quantize; table rows = base (factorized) or input_size. */
+static int64_t shr_round(int64_t v, int shift, int nearest) {
+    return nearest ? (v + ((int64_t)1 << (shift - 1))) >> shift : v >> shift;
+}
+
+EXPORT void oracle_sfnn_integer_forward(const int64_t* shape, const int* stm, const int* nstm, const int* buckets,
+                                        const int16_t* l0w_q, const int16_t* l0b_q, const int8_t* l1w_q,
+                                        const int32_t* l1b_q, const int8_t* l2w_q, const int32_t* l2b_q,
+                                        const int8_t* l3w_q, const int32_t* l3b_q, int ft_shift, int ft_round,
+                                        int crelu_round, int sqr_round, int32_t* l1_out, int32_t* raw_out,
+                                        int64_t* error) {
+    float alphas[2] = {1.0f, 1.0f};
+    sfnn_dims d = sfnn_make_dims(shape, alphas);
+    const int64_t W = d.width, half = W / 2, O = d.l1_out, L2 = d.l2, I2 = d.l2_in, H = d.hidden;
+    const int64_t rows = d.base ? d.base : d.input_size;
+    const int64_t p1 = pad32(W), p2 = pad32(I2), p3 = pad32(L2);
+    uint8_t* ft = (uint8_t*)malloc((size_t)W);
+    int32_t* l1 = (int32_t*)malloc(sizeof(int32_t) * (size_t)O);
+    uint8_t* in = (uint8_t*)malloc((size_t)I2 + 1);
+    uint8_t* l2 = (uint8_t*)malloc((size_t)L2);
+    *error = -1;
+    for (int64_t b = 0; b < d.batch; ++b) {
+        int s = buckets[b];
+        if (s < 0 || s >= d.stacks) {
+            if (*error < 0) *error = b;
+            raw_out[b] = 0;
+            continue;
+        }
+        for (int v = 0; v < 2; ++v) {
+            const int* idx = (v ? nstm : stm) + b * d.max_active;
+            for (int64_t j = 0; j < half; ++j) {
+                int32_t s0 = (int32_t)l0b_q[j] * 2, s1 = (int32_t)l0b_q[half + j] * 2;
+                for (int64_t k = 0; k < d.max_active; ++k) {
+                    int f = idx[k];
+                    if (f < 0) continue;
+                    if ((int64_t)f >= rows) {
+                        if (*error < 0) *error = b;
+                        continue;
+                    }
+                    s0 += (int32_t)l0w_q[(int64_t)f * W + j] * 2;
+                    s1 += (int32_t)l0w_q[(int64_t)f * W + half + j] * 2;
+                }
+                int32_t x0 = (int32_t)(int16_t)s0, x1 = (int32_t)(int16_t)s1;
+                x0 = x0 < 0 ? 0 : (x0 > 254 ? 254 : x0);
+                x1 = x1 < 0 ? 0 : (x1 > 254 ? 254 : x1);
+                int64_t p = shr_round(((int64_t)x0 << ft_shift) * x1, 16, ft_round);
+                ft[v * half + j] = (uint8_t)(p > 255 ? 255 : (p < 0 ? 0 : p));
+            }
+        }
+        for (int64_t o = 0; o < O; ++o) {
+            int32_t sum = l1b_q[s * O + o];
+            const int8_t* row = l1w_q + (s * O + o) * p1;
+            for (int64_t i = 0; i < W; ++i) sum += (int32_t)ft[i] * (int32_t)row[i];
+            l1[o] = sum;
+            l1_out[b * O + o] = sum;
+        }
+        for (int64_t i = 0; i < H; ++i) {
+            int64_t sq = shr_round((int64_t)l1[i] * l1[i], 19, sqr_round);
+            in[i] = (uint8_t)(sq > 127 ? 127 : sq);
+            int32_t c = (crelu_round && l1[i] > 0) ? (l1[i] + 32) >> 6 : l1[i] >> 6;
+            in[H + i] = (uint8_t)(c < 0 ? 0 : (c > 127 ? 127 : c));
+        }
+        for (int64_t o = 0; o < L2; ++o) {
+            int32_t sum = l2b_q[s * L2 + o];
+            const int8_t* row = l2w_q + (s * L2 + o) * p2;
+            for (int64_t i = 0; i < I2; ++i) sum += (int32_t)in[i] * (int32_t)row[i];
+            int32_t c = (crelu_round && sum > 0) ? (sum + 32) >> 6 : sum >> 6;
+            l2[o] = (uint8_t)(c < 0 ? 0 : (c > 127 ? 127 : c));
+        }
+        int32_t out = l3b_q[s];
+        for (int64_t i = 0; i < L2; ++i) out += (int32_t)l2[i] * (int32_t)l3w_q[s * p3 + i];
+        if (d.skip) out += l1[H];
+        raw_out[b] = out;
+    }
+    free(ft);
+    free(l1);
+    free(in);
+    free(l2);
+}

@@ -45,9 +45,12 @@ def lib():
         _lib.oracle_kppt_backward.argtypes = [i64] * 3 + [p] * 11
         _lib.oracle_sfnn_forward.argtypes = [p] * 13
         _lib.oracle_sfnn_backward.argtypes = [p] * 17
+        _lib.oracle_sfnn_quantize.argtypes = [p] * 11
+        _lib.oracle_sfnn_integer_forward.argtypes = [p] * 12 + [i] * 4 + [p] * 3
         for fn in (_lib.oracle_nnue_forward, _lib.oracle_scalar_loss, _lib.oracle_nnue_backward,
                    _lib.oracle_radam_step_scale, _lib.oracle_ranger_update, _lib.oracle_kppt_forward,
-                   _lib.oracle_kppt_backward, _lib.oracle_sfnn_forward, _lib.oracle_sfnn_backward):
+                   _lib.oracle_kppt_backward, _lib.oracle_sfnn_forward, _lib.oracle_sfnn_backward,
+                   _lib.oracle_sfnn_quantize, _lib.oracle_sfnn_integer_forward):
             fn.restype = None
     return _lib
 
@@ -282,3 +285,60 @@ def shared_factor_clip(ranger: dict, alpha: float) -> dict:
 
     r["min_weight"], r["max_weight"] = scale(lo), scale(hi)
     return r
+
+
+# ------------------------------------------------------------------ quantised SFNN
+SFNN_QUANT_NAMES = ("l0w", "l0b", "l1w", "l1b", "l2w", "l2b", "l3w", "l3b")
+
+
+def pad32(n: int) -> int:
+    return (n + 31) // 32 * 32
+
+
+def sfnn_quant_shapes(shape) -> dict:
+    """Element counts and dtypes of the quantised buffers (engine layout,
+    dense rows padded to 32 inputs)."""
+    input_size, W, H, skip, L2, S = shape
+    O = H + (1 if skip else 0)
+    base = 131949 if input_size == 131949 + 1629 else (73305 if input_size == 73305 + 1629 else 0)
+    rows = base or input_size
+    return {"l0w": (rows * W, np.int16), "l0b": (W, np.int16), "l1w": (S * O * pad32(W), np.int8),
+            "l1b": (S * O, np.int32), "l2w": (S * L2 * pad32(2 * H), np.int8), "l2b": (S * L2, np.int32),
+            "l3w": (S * pad32(L2), np.int8), "l3b": (S, np.int32)}
+
+
+def sfnn_quantize(shape, weights: dict, ft_alpha=1.0, shared_alpha=1.0) -> dict:
+    """Export quantisation (oracle_sfnn_quantize): FT and shared factors folded,
+    FT i16 at 127, dense i8 at 64 (rows padded to 32), biases i32 at 8128."""
+    sh, al = _sfnn_shape_arrays(shape, 1, 1, ft_alpha, shared_alpha)
+    ws = [None if weights.get(n) is None else _f(weights[n]) for n in SFNN_NAMES]
+    out = {n: np.zeros(c, dt) for n, (c, dt) in sfnn_quant_shapes(shape).items()}
+    lib().oracle_sfnn_quantize(_p(sh), _p(al), _ptr_array(ws), *(_p(out[n]) for n in SFNN_QUANT_NAMES))
+    return out
+
+
+def sfnn_integer_forward(shape, stm, nstm, buckets, batch, max_active, q: dict, *, ft_shift=7, ft_round=0,
+                         crelu_round=0, sqr_round=0) -> dict:
+    """Engine integer forward (oracle_sfnn_integer_forward): raw i32 output,
+    i32 L1 sums, and the first sample with an out-of-range feature or bucket
+    (-1 when none)."""
+    _, W, H, skip, L2, S = shape
+    O = H + (1 if skip else 0)
+    sh, al = _sfnn_shape_arrays(shape, batch, max_active, 1.0, 1.0)
+    qs = {n: np.ascontiguousarray(q[n], dtype=dt).reshape(-1) for n, (_, dt) in sfnn_quant_shapes(shape).items()}
+    l1 = np.zeros(batch * O, np.int32)
+    raw = np.zeros(batch, np.int32)
+    err = np.zeros(1, np.int64)
+    s, n, b = _i(stm), _i(nstm), _i(buckets)
+    lib().oracle_sfnn_integer_forward(_p(sh), _p(s), _p(n), _p(b), *(_p(qs[k]) for k in SFNN_QUANT_NAMES),
+                                      int(ft_shift), int(ft_round), int(crelu_round), int(sqr_round),
+                                      _p(l1), _p(raw), _p(err))
+    return {"raw": raw, "l1": l1, "error": int(err[0])}
+
+
+def final_division(raw, fv_scale: int, nearest: bool) -> np.ndarray:
+    """raw / fv_scale truncating toward zero; nearest adds half the scale away
+    from zero first (examples/bulletou.rs:8045-8054)."""
+    r = np.asarray(raw, np.int64)
+    mag = np.abs(r) + (fv_scale // 2 if nearest else 0)
+    return (np.sign(r) * (mag // fv_scale)).astype(np.int32)
