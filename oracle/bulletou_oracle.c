@@ -387,41 +387,254 @@ static float sfnn_w3(const sfnn_dims* d, const float* const* w, int64_t s, int64
     return v;
 }
 
+/* ------------------------------------------------------------------ SFNN QAT
+ * Quantisation-aware training modes of the reference runner (bitmask):
+ *   1 L1  fake-quantised folded L1 weights / bias (sfnn_qat_l1; cu:11514-11590,
+ *         sfnn_build_quantized_proxy_stacked_{weights,bias}_kernel cu:1735-1990)
+ *   2 FT  fake-quantised FT weights / bias, virtual rows folded in and zeroed
+ *         (layer QAT, layer_qat.rs:832-880, layer_qat_ft_fold_kernel cu:9302)
+ *   4 L2, 8 L3  fake-quantised L2 / L3 weights (scale 64) and biases (8128)
+ *         (layer_qat_vector_kernel cu:9294)
+ * L1 + L2 + L3 together select the dense integer QAT (layer_qat.rs:977-991):
+ * FT output floored to the 1/127 lattice (or the engine's integer FT when FT
+ * QAT is on, dense_qat_exact_ft_kernel cu:6344), integer L1 / L2 / L3 with
+ * the master L2 / L3 biases rounded to 8128 (cu:6282-6320), and continuous
+ * activation STEs in the backward (dense_qat_l2_ste_kernel cu:6322,
+ * sfnn_l2_input_backward_kernel cu:3709-3770).  Gradients always reach the
+ * f32 masters through an identity STE. */
+#define SFNN_QAT_L1 1
+#define SFNN_QAT_FT 2
+#define SFNN_QAT_L2 4
+#define SFNN_QAT_L3 8
+
+/* sfnn_quantize_dequant_clamped, cu:1644-1666 (training form): f32 product
+ * rounded half away from zero; ties and |x| >= 2^22 redone in double. */
+static float qat_qd(float v, float scale, float lo, float hi) {
+    const float scaled = v * scale;
+    float q = roundf(scaled);
+    if (fabsf(scaled) >= 4194304.0f || fabsf(scaled - truncf(scaled)) == 0.5f)
+        q = (float)round((double)v * (double)scale);
+    q = fminf(fmaxf(q, lo), hi);
+    return q / scale;
+}
+
+/* a + alpha * b with two roundings (the QAT folds use __fadd_rn/__fmul_rn). */
+static float fold_nf(float a, float alpha, float b) {
+    const float t = alpha * b;
+    return a + t;
+}
+
+static int32_t round_bias_8128(float v) {
+    double q = round((double)v * 8128.0);
+    q = fmin(2147483647.0, fmax(-2147483648.0, q));
+    return (int32_t)q;
+}
+
+/* floor(clamp(x, 0, 1) * 127), exact (dense_qat_lattice_integer, cu:5998). */
+static int qat_lattice(float x) {
+    const float c = fminf(1.0f, fmaxf(0.0f, x));
+    return (int)floor((double)c * 127.0);
+}
+
+typedef struct {
+    int l1, ft, l2, l3, dense;
+    float *l0w, *l0b;           /* FT copies (ft): [input_size][W], [W] */
+    float *w1, *b1;             /* Q(folded L1) [S][O][W], [S][O] (l1) */
+    float *b1_master;           /* folded master L1 bias [S][O] (l1) */
+    int32_t* b1_int;            /* round(folded master * 8128) [S][O] (l1) */
+    float *w2, *b2, *w3, *b3;   /* Q copies (l2, l3) */
+} sfnn_qat;
+
+static void sfnn_qat_prepare(const sfnn_dims* d, int mode, const float* const* w, sfnn_qat* q) {
+    memset(q, 0, sizeof(*q));
+    q->l1 = (mode & SFNN_QAT_L1) != 0;
+    q->ft = (mode & SFNN_QAT_FT) != 0;
+    q->l2 = (mode & SFNN_QAT_L2) != 0;
+    q->l3 = (mode & SFNN_QAT_L3) != 0;
+    q->dense = q->l1 && q->l2 && q->l3;
+    const int64_t W = d->width, O = d->l1_out, S = d->stacks, L2 = d->l2, I2 = d->l2_in;
+    if (q->ft) {
+        q->l0w = (float*)malloc(sizeof(float) * (size_t)(d->input_size * W));
+        q->l0b = (float*)malloc(sizeof(float) * (size_t)W);
+        for (int64_t f = 0; f < d->input_size; ++f)
+            for (int64_t j = 0; j < W; ++j) {
+                float v = 0.0f;
+                if (!d->base || f < d->base) {
+                    v = w[0][f * W + j];
+                    if (d->base) v = fold_nf(v, d->ft_alpha, w[0][(d->base + f % SFNN_PIECES) * W + j]);
+                    v = qat_qd(v, 127.0f, -32768.0f, 32767.0f);
+                }
+                q->l0w[f * W + j] = v;
+            }
+        for (int64_t j = 0; j < W; ++j) q->l0b[j] = qat_qd(w[1][j], 127.0f, -32768.0f, 32767.0f);
+    }
+    if (q->l1) {
+        q->w1 = (float*)malloc(sizeof(float) * (size_t)(S * O * W));
+        q->b1 = (float*)malloc(sizeof(float) * (size_t)(S * O));
+        q->b1_master = (float*)malloc(sizeof(float) * (size_t)(S * O));
+        q->b1_int = (int32_t*)malloc(sizeof(int32_t) * (size_t)(S * O));
+        for (int64_t s = 0; s < S; ++s)
+            for (int64_t o = 0; o < O; ++o) {
+                for (int64_t i = 0; i < W; ++i) {
+                    float v = w[2][(s * O + o) * W + i];
+                    if (w[4]) v = fold_nf(v, d->shared_alpha, w[4][i * O + o]);
+                    q->w1[(s * O + o) * W + i] = qat_qd(v, 64.0f, -128.0f, 127.0f);
+                }
+                float b = w[3][s * O + o];
+                if (w[5]) b = fold_nf(b, d->shared_alpha, w[5][o]);
+                q->b1_master[s * O + o] = b;
+                q->b1_int[s * O + o] = round_bias_8128(b);
+                q->b1[s * O + o] = qat_qd(b, 8128.0f, -2147483648.0f, 2147483647.0f);
+            }
+    }
+    if (q->l2) {
+        q->w2 = (float*)malloc(sizeof(float) * (size_t)(S * L2 * I2));
+        q->b2 = (float*)malloc(sizeof(float) * (size_t)(S * L2));
+        for (int64_t i = 0; i < S * L2 * I2; ++i) q->w2[i] = qat_qd(w[6][i], 64.0f, -128.0f, 127.0f);
+        for (int64_t i = 0; i < S * L2; ++i) q->b2[i] = qat_qd(w[7][i], 8128.0f, -2147483648.0f, 2147483647.0f);
+    }
+    if (q->l3) {
+        q->w3 = (float*)malloc(sizeof(float) * (size_t)(S * L2));
+        q->b3 = (float*)malloc(sizeof(float) * (size_t)S);
+        for (int64_t i = 0; i < S * L2; ++i) q->w3[i] = qat_qd(w[10][i], 64.0f, -128.0f, 127.0f);
+        for (int64_t i = 0; i < S; ++i) q->b3[i] = qat_qd(w[11][i], 8128.0f, -2147483648.0f, 2147483647.0f);
+    }
+}
+
+static void sfnn_qat_free(sfnn_qat* q) {
+    free(q->l0w); free(q->l0b); free(q->w1); free(q->b1); free(q->b1_master); free(q->b1_int);
+    free(q->w2); free(q->b2); free(q->w3); free(q->b3);
+}
+
+/* Weights the forward / backward use under QAT. */
+static float qat_w1(const sfnn_dims* d, const sfnn_qat* q, const float* const* w, int64_t s, int64_t o, int64_t i) {
+    return q->l1 ? q->w1[(s * d->l1_out + o) * d->width + i] : sfnn_w1(d, w, s, o, i);
+}
+static float qat_w2(const sfnn_dims* d, const sfnn_qat* q, const float* const* w, int64_t s, int64_t o, int64_t i) {
+    return q->l2 ? q->w2[(s * d->l2 + o) * d->l2_in + i] : sfnn_w2(d, w, s, o, i);
+}
+static float qat_w3(const sfnn_dims* d, const sfnn_qat* q, const float* const* w, int64_t s, int64_t o) {
+    return q->l3 ? q->w3[s * d->l2 + o] : sfnn_w3(d, w, s, o);
+}
+
+/* Engine integer FT of one view from FT QAT weights (q / 127 values):
+ * doubled i16 sums with wrap, clamp [0, 254], (s0 * s1) >> 9 (cu:6344-6390). */
+static void qat_exact_ft(const sfnn_dims* d, const sfnn_qat* q, const int* idx, int* pair) {
+    const int64_t W = d->width, half = W / 2;
+    for (int64_t j = 0; j < half; ++j) {
+        int32_t s0 = 2 * (int32_t)rintf(q->l0b[j] * 127.0f), s1 = 2 * (int32_t)rintf(q->l0b[half + j] * 127.0f);
+        for (int64_t k = 0; k < d->max_active; ++k) {
+            int f = idx[k];
+            if (f < 0 || (int64_t)f >= d->n_features) continue;
+            s0 += 2 * (int32_t)rintf(q->l0w[(int64_t)f * W + j] * 127.0f);
+            s1 += 2 * (int32_t)rintf(q->l0w[(int64_t)f * W + half + j] * 127.0f);
+        }
+        int32_t x0 = (int32_t)(int16_t)s0, x1 = (int32_t)(int16_t)s1;
+        x0 = x0 < 0 ? 0 : (x0 > 254 ? 254 : x0);
+        x1 = x1 < 0 ? 0 : (x1 > 254 ? 254 : x1);
+        pair[j] = (x0 * x1) >> 9;
+    }
+}
+
 /* shape: input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks, batch, max_active;
- * alphas: ft, shared.  Outputs (row-major per sample): stm_l0, nstm_l0,
- * combined [B][W], l1 [B][l1_out], l2_input [B][2H], l2 [B][L2], output [B]. */
-EXPORT void oracle_sfnn_forward(const int64_t* shape, const float* alphas, const int* stm, const int* nstm,
-                                const int* buckets, const float* const* w, float* stm_l0, float* nstm_l0,
-                                float* combined, float* l1, float* l2_input, float* l2, float* output) {
+ * alphas: ft, shared; qat: SFNN_QAT_* bitmask.  Outputs (row-major per
+ * sample): stm_l0, nstm_l0, combined [B][W], l1 [B][l1_out], l2_input [B][2H],
+ * l2 [B][L2], output [B]; under dense QAT also l1_raw [B][l1_out] and l2_raw
+ * [B][L2] (the integer sums; may be NULL otherwise). */
+EXPORT void oracle_sfnn_forward_qat(const int64_t* shape, const float* alphas, int qat, const int* stm,
+                                    const int* nstm, const int* buckets, const float* const* w, float* stm_l0,
+                                    float* nstm_l0, float* combined, float* l1, float* l2_input, float* l2,
+                                    float* output, int32_t* l1_raw, int32_t* l2_raw) {
     sfnn_dims d = sfnn_make_dims(shape, alphas);
+    sfnn_qat q;
+    sfnn_qat_prepare(&d, qat, w, &q);
+    const float* ftw = q.ft ? q.l0w : w[0];
+    const float* ftb = q.ft ? q.l0b : w[1];
     const float scale = 127.0f / 128.0f;
-    const int64_t W = d.width, half = W / 2;
+    const int64_t W = d.width, half = W / 2, O = d.l1_out;
+    int* pair = (int*)malloc(sizeof(int) * (size_t)half);
+    int* in_int = (int*)malloc(sizeof(int) * (size_t)d.l2_in);
     for (int64_t b = 0; b < d.batch; ++b) {
         float* xs = stm_l0 + b * W;
         float* xn = nstm_l0 + b * W;
-        sfnn_ft_view(&d, stm + b * d.max_active, w[0], w[1], xs);
-        sfnn_ft_view(&d, nstm + b * d.max_active, w[0], w[1], xn);
+        sfnn_ft_view(&d, stm + b * d.max_active, ftw, ftb, xs);
+        sfnn_ft_view(&d, nstm + b * d.max_active, ftw, ftb, xn);
         float* c = combined + b * W;
         for (int64_t j = 0; j < half; ++j) {
             c[j] = xs[j] * xs[j + half] * scale;
             c[half + j] = xn[j] * xn[j + half] * scale;
         }
-        float* l1r = l1 + b * d.l1_out;
+        if (q.dense) {
+            if (q.ft) {
+                for (int v = 0; v < 2; ++v) {
+                    qat_exact_ft(&d, &q, (v ? nstm : stm) + b * d.max_active, pair);
+                    for (int64_t j = 0; j < half; ++j) c[v * half + j] = (float)pair[j] / 127.0f;
+                }
+            } else {
+                for (int64_t j = 0; j < W; ++j) c[j] = (float)qat_lattice(c[j]) / 127.0f;
+            }
+        }
+        float* l1r = l1 + b * O;
         float* in = l2_input + b * d.l2_in;
         float* l2r = l2 + b * d.l2;
         int s = buckets[b];
         if (s < 0 || s >= d.stacks) {  /* cu:2250-2256: invalid bucket -> zeros */
-            for (int64_t o = 0; o < d.l1_out; ++o) l1r[o] = 0.0f;
+            for (int64_t o = 0; o < O; ++o) l1r[o] = 0.0f;
             for (int64_t i = 0; i < d.l2_in; ++i) in[i] = 0.0f;
             for (int64_t o = 0; o < d.l2; ++o) l2r[o] = 0.0f;
+            if (l1_raw) for (int64_t o = 0; o < O; ++o) l1_raw[b * O + o] = 0;
+            if (l2_raw) for (int64_t o = 0; o < d.l2; ++o) l2_raw[b * d.l2 + o] = 0;
             output[b] = 0.0f;
             continue;
         }
-        for (int64_t o = 0; o < d.l1_out; ++o) {
+        if (q.dense) {
+            /* integer L1 / L2 / L3 (cu:6223-6320) */
+            int32_t raw1[64];
+            for (int64_t o = 0; o < O; ++o) {
+                int64_t acc = q.b1_int[s * O + o];
+                for (int64_t i = 0; i < W; ++i)
+                    acc += (int64_t)rintf(c[i] * 127.0f) * (int64_t)rintf(qat_w1(&d, &q, w, s, o, i) * 64.0f);
+                raw1[o] = (int32_t)acc;
+                l1r[o] = (float)((double)raw1[o] / 8128.0);
+                if (l1_raw) l1_raw[b * O + o] = raw1[o];
+            }
+            for (int64_t i = 0; i < d.hidden; ++i) {
+                const int64_t x = raw1[i];
+                int64_t sq = (x * x) >> 19;
+                if (sq > 127) sq = 127;
+                int32_t lin = raw1[i] >> 6;
+                lin = lin < 0 ? 0 : (lin > 127 ? 127 : lin);
+                in[i] = (float)sq / 127.0f;
+                in[d.hidden + i] = (float)lin / 127.0f;
+                in_int[i] = (int)sq;
+                in_int[d.hidden + i] = lin;
+            }
+            int64_t out = round_bias_8128(w[11][s]);
+            for (int64_t o = 0; o < d.l2; ++o) {
+                int64_t acc = round_bias_8128(w[7][s * d.l2 + o]);
+                for (int64_t i = 0; i < d.l2_in; ++i)
+                    acc += (int64_t)in_int[i] * (int64_t)rintf(qat_w2(&d, &q, w, s, o, i) * 64.0f);
+                const int32_t r2 = (int32_t)acc;
+                if (l2_raw) l2_raw[b * d.l2 + o] = r2;
+                int32_t v = r2 >> 6;
+                v = v < 0 ? 0 : (v > 127 ? 127 : v);
+                l2r[o] = (float)v / 127.0f;
+                out += (int64_t)v * (int64_t)rintf(qat_w3(&d, &q, w, s, o) * 64.0f);
+            }
+            if (d.skip) out += raw1[d.hidden];
+            output[b] = (float)((double)(int32_t)out / 8128.0);
+            continue;
+        }
+        for (int64_t o = 0; o < O; ++o) {
             double acc = 0.0;
-            for (int64_t i = 0; i < W; ++i) acc += (double)c[i] * sfnn_w1(&d, w, s, o, i);
-            float r = (float)acc + w[3][s * d.l1_out + o];
-            if (w[5]) r = fmaf(d.shared_alpha, w[5][o], r);
+            for (int64_t i = 0; i < W; ++i) acc += (double)c[i] * qat_w1(&d, &q, w, s, o, i);
+            float r;
+            if (q.l1) {
+                r = (float)acc + q.b1[s * O + o];
+            } else {
+                r = (float)acc + w[3][s * O + o];
+                if (w[5]) r = fmaf(d.shared_alpha, w[5][o], r);
+            }
             l1r[o] = r;
         }
         for (int64_t i = 0; i < d.hidden; ++i) {
@@ -430,18 +643,38 @@ EXPORT void oracle_sfnn_forward(const int64_t* shape, const float* alphas, const
             in[d.hidden + i] = crelu(l1r[i]);        /* CReLU */
         }
         for (int64_t o = 0; o < d.l2; ++o) {
-            float bias = w[7][s * d.l2 + o];
-            if (w[9]) bias = fmaf(d.shared_alpha, w[9][o], bias);
+            float bias;
+            if (q.l2) {
+                bias = q.b2[s * d.l2 + o];
+            } else {
+                bias = w[7][s * d.l2 + o];
+                if (w[9]) bias = fmaf(d.shared_alpha, w[9][o], bias);
+            }
             double acc = bias;
-            for (int64_t i = 0; i < d.l2_in; ++i) acc += (double)in[i] * sfnn_w2(&d, w, s, o, i);
+            for (int64_t i = 0; i < d.l2_in; ++i) acc += (double)in[i] * qat_w2(&d, &q, w, s, o, i);
             l2r[o] = crelu((float)acc);
         }
-        float b3 = w[11][s];
-        if (w[13]) b3 = fmaf(d.shared_alpha, w[13][0], b3);
+        float b3;
+        if (q.l3) {
+            b3 = q.b3[s];
+        } else {
+            b3 = w[11][s];
+            if (w[13]) b3 = fmaf(d.shared_alpha, w[13][0], b3);
+        }
         double out = b3;
-        for (int64_t o = 0; o < d.l2; ++o) out += (double)l2r[o] * sfnn_w3(&d, w, s, o);
+        for (int64_t o = 0; o < d.l2; ++o) out += (double)l2r[o] * qat_w3(&d, &q, w, s, o);
         output[b] = (float)out + (d.skip ? l1r[d.hidden] : 0.0f);
     }
+    free(pair);
+    free(in_int);
+    sfnn_qat_free(&q);
+}
+
+EXPORT void oracle_sfnn_forward(const int64_t* shape, const float* alphas, const int* stm, const int* nstm,
+                                const int* buckets, const float* const* w, float* stm_l0, float* nstm_l0,
+                                float* combined, float* l1, float* l2_input, float* l2, float* output) {
+    oracle_sfnn_forward_qat(shape, alphas, 0, stm, nstm, buckets, w, stm_l0, nstm_l0, combined, l1, l2_input, l2,
+                            output, 0, 0);
 }
 
 /* Backward of oracle_sfnn_forward for output gradients mog (lib.rs:14516-14710
@@ -449,12 +682,15 @@ EXPORT void oracle_sfnn_forward(const int64_t* shape, const float* alphas, const
  * is NULL) are overwritten; l0w's gradient includes the virtual rows
  * (alpha * sum of the base rows' gradients, cu:4950-4985).  l1_gradients
  * [B][l1_out] and combined_gradients [B][W] are written too. */
-EXPORT void oracle_sfnn_backward(const int64_t* shape, const float* alphas, const int* stm, const int* nstm,
-                                 const int* buckets, const float* const* w, const float* stm_l0, const float* nstm_l0,
-                                 const float* combined, const float* l1, const float* l2_input, const float* l2,
-                                 const float* mog, double* acc_l0w, float* const* grads, float* l1_gradients,
-                                 float* combined_gradients) {
+EXPORT void oracle_sfnn_backward_qat(const int64_t* shape, const float* alphas, int qat, const int* stm,
+                                     const int* nstm, const int* buckets, const float* const* w,
+                                     const float* stm_l0, const float* nstm_l0, const float* combined,
+                                     const float* l1, const float* l2_input, const float* l2, const int32_t* l1_raw,
+                                     const int32_t* l2_raw, const float* mog, double* acc_l0w, float* const* grads,
+                                     float* l1_gradients, float* combined_gradients) {
     sfnn_dims d = sfnn_make_dims(shape, alphas);
+    sfnn_qat q;
+    sfnn_qat_prepare(&d, qat, w, &q);
     const float scale = 127.0f / 128.0f;
     const int64_t W = d.width, half = W / 2, O = d.l1_out, L2 = d.l2, I2 = d.l2_in, S = d.stacks;
     const int64_t lens[14] = {d.input_size * W, W, S * O * W, S * O, W * O, O, S * L2 * I2, S * L2, L2 * I2, L2,
@@ -493,7 +729,22 @@ EXPORT void oracle_sfnn_backward(const int64_t* shape, const float* alphas, cons
         for (int64_t o = 0; o < L2; ++o) {
             acc[10][s * L2 + o] += (double)gout * l2r[o];
             if (w[12]) acc[12][o] += (double)d.shared_alpha * gout * l2r[o];
-            g2[o] = crelu_grad(l2r[o], gout * sfnn_w3(&d, w, s, o));
+            const float g = gout * qat_w3(&d, &q, w, s, o);
+            if (q.dense) {
+                /* continuous STE of the integer L2 CReLU (cu:6322-6342) */
+                const int32_t x = l2_raw[b * L2 + o];
+                float gg = g;
+                if (x < 0 || x > 8128) {
+                    gg = 0.0f;
+                } else if (x == 0 || x == 8128) {
+                    const double bias = fmin(2147483647.0, fmax(-2147483648.0, (double)w[7][s * L2 + o] * 8128.0));
+                    const double fraction = bias - round(bias);
+                    if ((x == 0 && fraction <= 0.0) || (x == 8128 && fraction >= 0.0)) gg = 0.0f;
+                }
+                g2[o] = gg;
+            } else {
+                g2[o] = crelu_grad(l2r[o], g);
+            }
         }
         /* L2 (cu:3489-3700) */
         for (int64_t i = 0; i < I2; ++i) gin[i] = 0.0f;
@@ -503,12 +754,40 @@ EXPORT void oracle_sfnn_backward(const int64_t* shape, const float* alphas, cons
             for (int64_t i = 0; i < I2; ++i) {
                 acc[6][(s * L2 + o) * I2 + i] += (double)g2[o] * in[i];
                 if (w[8]) acc[8][o * I2 + i] += (double)d.shared_alpha * g2[o] * in[i];
-                gin[i] += g2[o] * sfnn_w2(&d, w, s, o, i);
+                gin[i] += g2[o] * qat_w2(&d, &q, w, s, o, i);
             }
         }
         /* L2 input (cu:3709-3770) */
         for (int64_t i = 0; i < d.hidden; ++i) {
             float v = l1r[i];
+            if (q.dense) {
+                /* STE from the pre-rounding L1 value: raw / 8128 plus the
+                 * rounded-off fraction of the master bias. */
+                const float master = q.b1_master[s * O + i];
+                const int32_t qi = q.b1_int[s * O + i];
+                float frac;
+                if (qi >= -16777216 && qi <= 16777216) {
+                    frac = fmaf(master, 8128.0f, -(float)qi);
+                } else {
+                    const double scaled = fmin(2147483647.0, fmax(-2147483648.0, (double)master * 8128.0));
+                    frac = (float)(scaled - (double)qi);
+                }
+                const float ste = fmaf(frac, 1.0f / 8128.0f, v);
+                const float cs = fabsf(ste) * fabsf(ste) * scale;
+                int sq_on = cs > 0.0f && cs < 1.0f;
+                int lin_on = ste > 0.0f && ste < 1.0f;
+                const int32_t raw = l1_raw[b * O + i];
+                if (raw == 0) lin_on = frac > 0.0f;
+                else if (raw == 8128) lin_on = frac < 0.0f;
+                if (raw == 8160 || raw == -8160) {
+                    const double x = (double)raw + (double)frac;
+                    sq_on = x * x * 127.0 < 128.0 * 8128.0 * 8128.0;
+                }
+                const float sg = sq_on ? gin[i] * (2.0f * ste * scale) : 0.0f;
+                const float lg = lin_on ? gin[d.hidden + i] : 0.0f;
+                g1[i] = sg + lg;
+                continue;
+            }
             float sq = crelu_grad(in[i], gin[i] * (2.0f * v * scale));
             float lin = crelu_grad(in[d.hidden + i], gin[d.hidden + i]);
             g1[i] = sq + lin;
@@ -524,7 +803,7 @@ EXPORT void oracle_sfnn_backward(const int64_t* shape, const float* alphas, cons
         }
         for (int64_t i = 0; i < W; ++i) {
             double t = 0.0;
-            for (int64_t o = 0; o < O; ++o) t += (double)g1[o] * sfnn_w1(&d, w, s, o, i);
+            for (int64_t o = 0; o < O; ++o) t += (double)g1[o] * qat_w1(&d, &q, w, s, o, i);
             dc[i] = (float)t;
         }
         /* pairwise + ClippedReLU (cu:4376-4440) */
@@ -559,11 +838,21 @@ EXPORT void oracle_sfnn_backward(const int64_t* shape, const float* alphas, cons
         if (!grads[k]) continue;
         for (int64_t i = 0; i < lens[k]; ++i) grads[k][i] = (float)acc[k][i];
     }
+    sfnn_qat_free(&q);
     free(pool);
     free(g2);
     free(gin);
     free(pre_s);
     free(pre_n);
+}
+
+EXPORT void oracle_sfnn_backward(const int64_t* shape, const float* alphas, const int* stm, const int* nstm,
+                                 const int* buckets, const float* const* w, const float* stm_l0, const float* nstm_l0,
+                                 const float* combined, const float* l1, const float* l2_input, const float* l2,
+                                 const float* mog, double* acc_l0w, float* const* grads, float* l1_gradients,
+                                 float* combined_gradients) {
+    oracle_sfnn_backward_qat(shape, alphas, 0, stm, nstm, buckets, w, stm_l0, nstm_l0, combined, l1, l2_input, l2, 0,
+                             0, mog, acc_l0w, grads, l1_gradients, combined_gradients);
 }
 
 /* ------------------------------------------------------------------ quantised SFNN

@@ -45,12 +45,14 @@ def lib():
         _lib.oracle_kppt_backward.argtypes = [i64] * 3 + [p] * 11
         _lib.oracle_sfnn_forward.argtypes = [p] * 13
         _lib.oracle_sfnn_backward.argtypes = [p] * 17
+        _lib.oracle_sfnn_forward_qat.argtypes = [p, p, i] + [p] * 13
+        _lib.oracle_sfnn_backward_qat.argtypes = [p, p, i] + [p] * 17
         _lib.oracle_sfnn_quantize.argtypes = [p] * 11
         _lib.oracle_sfnn_integer_forward.argtypes = [p] * 12 + [i] * 4 + [p] * 3
         for fn in (_lib.oracle_nnue_forward, _lib.oracle_scalar_loss, _lib.oracle_nnue_backward,
                    _lib.oracle_radam_step_scale, _lib.oracle_ranger_update, _lib.oracle_kppt_forward,
                    _lib.oracle_kppt_backward, _lib.oracle_sfnn_forward, _lib.oracle_sfnn_backward,
-                   _lib.oracle_sfnn_quantize, _lib.oracle_sfnn_integer_forward):
+                   _lib.oracle_sfnn_forward_qat, _lib.oracle_sfnn_backward_qat, _lib.oracle_sfnn_quantize, _lib.oracle_sfnn_integer_forward):
             fn.restype = None
     return _lib
 
@@ -203,9 +205,19 @@ def _ptr_array(arrays):
     return arr
 
 
-def sfnn_forward(shape, stm, nstm, buckets, batch, max_active, weights: dict, ft_alpha=1.0, shared_alpha=1.0) -> dict:
-    """Forward of the SFNN LayerStack net (oracle_sfnn_forward in the C file).
-    shape = (input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks)."""
+QAT_L1, QAT_FT, QAT_L2, QAT_L3 = 1, 2, 4, 8
+
+
+def qat_mask(l1=False, ft=False, l2=False, l3=False) -> int:
+    """SFNN_QAT_* bitmask of the C file (the runner's qat_l1 / qat_ft / qat_l2 / qat_l3)."""
+    return (QAT_L1 if l1 else 0) | (QAT_FT if ft else 0) | (QAT_L2 if l2 else 0) | (QAT_L3 if l3 else 0)
+
+
+def sfnn_forward(shape, stm, nstm, buckets, batch, max_active, weights: dict, ft_alpha=1.0, shared_alpha=1.0,
+                 qat: int = 0) -> dict:
+    """Forward of the SFNN LayerStack net (oracle_sfnn_forward_qat in the C file).
+    shape = (input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks);
+    qat = qat_mask(...).  Dense QAT also returns the integer l1_raw / l2_raw."""
     _, W, H, skip, L2, _ = shape
     O = H + (1 if skip else 0)
     sh, al = _sfnn_shape_arrays(shape, batch, max_active, ft_alpha, shared_alpha)
@@ -213,17 +225,18 @@ def sfnn_forward(shape, stm, nstm, buckets, batch, max_active, weights: dict, ft
     out = {"stm_l0": np.zeros(batch * W, np.float32), "nstm_l0": np.zeros(batch * W, np.float32),
            "combined": np.zeros(batch * W, np.float32), "l1": np.zeros(batch * O, np.float32),
            "l2_input": np.zeros(batch * 2 * H, np.float32), "l2": np.zeros(batch * L2, np.float32),
-           "output": np.zeros(batch, np.float32)}
+           "output": np.zeros(batch, np.float32), "l1_raw": np.zeros(batch * O, np.int32),
+           "l2_raw": np.zeros(batch * L2, np.int32)}
     s, n, b = _i(stm), _i(nstm), _i(buckets)
-    lib().oracle_sfnn_forward(_p(sh), _p(al), _p(s), _p(n), _p(b), _ptr_array(ws), *(_p(out[k]) for k in (
-        "stm_l0", "nstm_l0", "combined", "l1", "l2_input", "l2", "output")))
+    lib().oracle_sfnn_forward_qat(_p(sh), _p(al), int(qat), _p(s), _p(n), _p(b), _ptr_array(ws), *(_p(out[k]) for k in (
+        "stm_l0", "nstm_l0", "combined", "l1", "l2_input", "l2", "output", "l1_raw", "l2_raw")))
     return out
 
 
 def sfnn_backward(shape, stm, nstm, buckets, batch, max_active, fwd: dict, weights: dict, mog, ft_alpha=1.0,
-                  shared_alpha=1.0) -> dict:
+                  shared_alpha=1.0, qat: int = 0) -> dict:
     """Parameter gradients ("<name>_gradients", FT virtual rows included) plus
-    l1_gradients and combined_gradients (oracle_sfnn_backward)."""
+    l1_gradients and combined_gradients (oracle_sfnn_backward_qat)."""
     input_size, W, H, skip, L2, S = shape
     O = H + (1 if skip else 0)
     sh, al = _sfnn_shape_arrays(shape, batch, max_active, ft_alpha, shared_alpha)
@@ -233,9 +246,12 @@ def sfnn_backward(shape, stm, nstm, buckets, batch, max_active, fwd: dict, weigh
     l1g = np.zeros(batch * O, np.float32)
     cg = np.zeros(batch * W, np.float32)
     s, n, b = _i(stm), _i(nstm), _i(buckets)
-    lib().oracle_sfnn_backward(_p(sh), _p(al), _p(s), _p(n), _p(b), _ptr_array(ws),
-                               *(_p(_f(fwd[k])) for k in ("stm_l0", "nstm_l0", "combined", "l1", "l2_input", "l2")),
-                               _p(_f(mog)), _p(acc), _ptr_array(grads), _p(l1g), _p(cg))
+    l1_raw = np.ascontiguousarray(fwd.get("l1_raw", np.zeros(batch * O, np.int32)), np.int32)
+    l2_raw = np.ascontiguousarray(fwd.get("l2_raw", np.zeros(batch * L2, np.int32)), np.int32)
+    lib().oracle_sfnn_backward_qat(_p(sh), _p(al), int(qat), _p(s), _p(n), _p(b), _ptr_array(ws),
+                                   *(_p(_f(fwd[k])) for k in ("stm_l0", "nstm_l0", "combined", "l1", "l2_input",
+                                                             "l2")),
+                                   _p(l1_raw), _p(l2_raw), _p(_f(mog)), _p(acc), _ptr_array(grads), _p(l1g), _p(cg))
     out = {f"{name}_gradients": g for name, g in zip(SFNN_NAMES, grads) if g is not None}
     out["l1_gradients"] = l1g
     out["combined_gradients"] = cg
@@ -247,9 +263,10 @@ class SfnnTrainer:
     multipliers, lib.rs:7448-7533 / 8425-8730): forward -> loss -> backward ->
     Ranger on every present group in the order of SFNN_NAMES."""
 
-    def __init__(self, shape, weights: dict, ft_alpha=1.0, shared_alpha=1.0):
+    def __init__(self, shape, weights: dict, ft_alpha=1.0, shared_alpha=1.0, qat: int = 0):
         self.shape = tuple(shape)
         self.ft_alpha, self.shared_alpha = ft_alpha, shared_alpha
+        self.qat = int(qat)
         self.names = [n for n in SFNN_NAMES if weights.get(n) is not None]
         self.w = {n: _f(weights[n]).copy() for n in self.names}
         self.m = {n: np.zeros_like(self.w[n]) for n in self.names}
@@ -258,10 +275,11 @@ class SfnnTrainer:
 
     def step(self, stm, nstm, buckets, batch, max_active, targets, entry_weights, *, loss_kind=0, inv_scale=1.0,
              pow_exp=2.0, loss_param=0.0, **ranger) -> dict:
-        fwd = sfnn_forward(self.shape, stm, nstm, buckets, batch, max_active, self.w, self.ft_alpha, self.shared_alpha)
+        fwd = sfnn_forward(self.shape, stm, nstm, buckets, batch, max_active, self.w, self.ft_alpha, self.shared_alpha,
+                           self.qat)
         loss = scalar_loss(loss_kind, inv_scale, pow_exp, loss_param, fwd["output"], targets, entry_weights)
         g = sfnn_backward(self.shape, stm, nstm, buckets, batch, max_active, fwd, self.w,
-                          loss["mean_output_gradients"], self.ft_alpha, self.shared_alpha)
+                          loss["mean_output_gradients"], self.ft_alpha, self.shared_alpha, self.qat)
         for n in self.names:
             r = dict(ranger)
             if n in ("l1fw", "l1fb"):
