@@ -33,6 +33,7 @@ from .sfnn import (  # noqa: F401
     QuantizedRounding,
     QuantizedSfnnDeviceWeights,
     SfnnIntegerForwardWorkspace,
+    SfnnLayerLrMultipliers,
     SfnnFactorizerAlpha,
     SfnnForwardHostWeights,
     SfnnForwardShape,

@@ -56,6 +56,12 @@ class QuantRounding(ctypes.Structure):
                 ("final_div_round", I), ("fv_scale", I)]
 
 
+class SfnnQat(ctypes.Structure):
+    """BulletOuB200SfnnQat."""
+
+    _fields_ = [("l1", I), ("ft", I), ("l2", I), ("l3", I)]
+
+
 class LossSpec(ctypes.Structure):
     """BulletOuB200LossSpec."""
 
@@ -64,6 +70,8 @@ class LossSpec(ctypes.Structure):
 
 
 _BUF = P  # handle pointers are opaque
+# Entries returning void (no status code).
+VOID_RETURN = {"bulletou_dense_qat_end"}
 SIGNATURES: dict[str, list] = {
     # runtime
     "bulletou_cuda_cpp_last_error": [P, Z],
@@ -142,9 +150,14 @@ SIGNATURES: dict[str, list] = {
     "bulletou_cuda_cpp_sfnn_backward_train_device": (
         [P, Z, Z, Z, I] + [Z] * 9 + [P] * 12 + [I] + [P] + [I] + [P] * 2 + [I] + [P] + [I] + [P] * 2 + [I] + [P]
         + [I] + [I] * 6 + [F] * 6 + [P] * 2 + [P] + [P] * 8 + [P] * 20 + [I] + [P]),
-    "bulletou_b200_sfnn_train_step_device": [P, P, Z, Z] + [P] * 16,
+    "bulletou_b200_sfnn_train_step_device": [P, P, Z, Z] + [P] * 17,
     "bulletou_b200_sfnn_dense_gradient_len": [P, I, I, I, P],
-    "bulletou_b200_sfnn_local_gradients_device": [P, P, Z, Z] + [P] * 14,
+    "bulletou_b200_sfnn_local_gradients_device": [P, P, Z, Z] + [P] * 15,
+    # SFNN QAT (reference entries)
+    "bulletou_layer_qat": [P, P, P, F, F, F, Z, Z, Z, F],
+    "bulletou_layer_qat_nonzero": [P, P, P, P],
+    "bulletou_dense_qat_begin": [P, P, P, Z, Z, Z, Z, I],
+    "bulletou_dense_qat_end": [P],
     "bulletou_b200_sfnn_quantize_device": [P, P, P, P],
     "bulletou_b200_sfnn_integer_forward_device": [P, P, Z, Z] + [P] * 9,
 }
@@ -172,7 +185,7 @@ class Library:
         if f is None:
             f = getattr(self._cdll, self.prefix + name)
             f.argtypes = SIGNATURES[name]
-            f.restype = I
+            f.restype = None if name in VOID_RETURN else I
             self._fns[name] = f
         return f
 
@@ -183,6 +196,8 @@ class Library:
 
     def call(self, name: str, *args) -> None:
         rc = self.fn(name)(*args)
+        if name in VOID_RETURN:
+            return
         if rc != 0:
             raise CudaCppError(f"{name}: {self.last_error()}", rc)
 

@@ -35,6 +35,12 @@ struct BulletOuCudaCppContext {
     int sm_count = 148;
     // Named scratch slots; see scratch_slot in runtime.cu.
     bou::Scratch scratch[24];
+    // Dense QAT mode between bulletou_dense_qat_begin / _end (the reference's
+    // context flags, cu:9356-9382): integer L1 / L2 / L3 in the SFNN entries.
+    bool dense_qat = false;
+    bool dense_qat_integer_ft = false;
+    const float* dense_qat_l2_bias = nullptr;
+    const float* dense_qat_l3_bias = nullptr;
     // Stage profiler (bulletou_b200_profile_*): events recorded on `stream`
     // at phase boundaries of the fused steps, read back after the run.
     bool prof_on = false;
@@ -105,6 +111,8 @@ enum ScratchSlot : int {
     kScratchSfnnEff = 19,       // SFNN effective (shared-factor folded) dense weights
     kScratchSfnnVirtual = 20,   // SFNN per-piece virtual-row gradient sums between row launches
     kScratchSfnnQuant = 21,     // SFNN integer forward: FT pair values + king sort
+    kScratchSfnnQat = 22,       // SFNN QAT: quantised L1 bias, integer biases, raw L1 / L2 sums
+    kScratchSfnnQatFt = 23,     // SFNN QAT: fake-quantised FT bias
 };
 
 int ok();

@@ -56,6 +56,40 @@ constexpr int kKingsPerLaunch = 3;  // FT row kernel: king blocks per launch (L2
 __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
 __device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f && a < 1.0f ? g : 0.0f; }
 
+// ------------------------------------------------------------------ QAT arithmetic
+// Fake quantisation of the reference's training path (cu:1644-1666): the f32
+// product rounded half away from zero, ties and |x| >= 2^22 redone in double,
+// clamped, divided back (IEEE division: this file is built with fast math).
+__device__ __forceinline__ float qat_qd(float v, float scale, float lo, float hi) {
+    const float scaled = __fmul_rn(v, scale);
+    float q = roundf(scaled);
+    if (fabsf(scaled) >= 4194304.0f || fabsf(scaled - truncf(scaled)) == 0.5f)
+        q = static_cast<float>(round(static_cast<double>(v) * static_cast<double>(scale)));
+    q = fminf(fmaxf(q, lo), hi);
+    return __fdiv_rn(q, scale);
+}
+__device__ __forceinline__ float qat_q64(float v) { return qat_qd(v, 64.0f, -128.0f, 127.0f); }
+__device__ __forceinline__ float qat_q8128(float v) { return qat_qd(v, 8128.0f, -2147483648.0f, 2147483647.0f); }
+__device__ __forceinline__ float qat_q127(float v) { return qat_qd(v, 127.0f, -32768.0f, 32767.0f); }
+// a + alpha * b with two roundings (the QAT folds, cu:1790-1795, 9302-9310).
+__device__ __forceinline__ float fold_nf(float a, float alpha, float b) { return __fadd_rn(a, __fmul_rn(alpha, b)); }
+// round(v * 8128) in double, saturated to i32 (cu:1986-1988).
+__device__ __forceinline__ int qat_bias_int(float v) {
+    const double q = fmin(2147483647.0, fmax(-2147483648.0, round(static_cast<double>(v) * 8128.0)));
+    return static_cast<int>(q);
+}
+// floor(clamp(c, 0, 1) * 127), exact: the double product of a float and 127 is exact.
+__device__ __forceinline__ int qat_lattice(float c) {
+    return static_cast<int>(floor(static_cast<double>(fminf(1.0f, fmaxf(0.0f, c))) * 127.0));
+}
+__device__ __forceinline__ float qat_on_lattice(int n) { return __fdiv_rn(static_cast<float>(n), 127.0f); }
+// Integer of a value already on a lattice (q / 127 or q / 64): round to nearest.
+__device__ __forceinline__ int qat_int127(float v) { return __float2int_rn(__fmul_rn(v, 127.0f)); }
+__device__ __forceinline__ int qat_int64(float v) { return __float2int_rn(__fmul_rn(v, 64.0f)); }
+__device__ __forceinline__ float qat_raw_to_float(long long raw) {
+    return static_cast<float>(static_cast<double>(static_cast<int>(raw)) / 8128.0);
+}
+
 // ------------------------------------------------------------------ fold
 __global__ void fold_ft4_kernel(const float4* __restrict__ l0w, float4* __restrict__ folded, size_t total4, int w4,
                                 int base, float alpha) {
@@ -75,6 +109,81 @@ __global__ void fold_ft1_kernel(const float* __restrict__ l0w, float* __restrict
     const size_t f = t / width;
     const size_t j = t - f * width;
     folded[t] = fmaf(alpha, l0w[(static_cast<size_t>(base) + f % kSfnnPieces) * width + j], l0w[t]);
+}
+
+// FT QAT (layer_qat_ft_fold_kernel, cu:9302-9312): base rows folded with their
+// virtual row (two roundings), then fake-quantised to i16 at 127.
+__global__ void fold_ft_qat_kernel(const float* __restrict__ l0w, float* __restrict__ folded, size_t total, int width,
+                                   int base, float alpha) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= total) return;
+    float v = l0w[t];
+    if (base > 0) {
+        const size_t f = t / width;
+        const size_t j = t - f * width;
+        v = fold_nf(v, alpha, l0w[(static_cast<size_t>(base) + f % kSfnnPieces) * width + j]);
+    }
+    folded[t] = qat_q127(v);
+}
+
+// layer_qat_vector_kernel (cu:9294-9300): element-wise fake quantisation.
+__global__ void qat_vector_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t n, int kind) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    const float v = src[t];
+    dst[t] = kind == 0 ? qat_q127(v) : (kind == 1 ? qat_q64(v) : qat_q8128(v));
+}
+
+// Reference-layout L1 QAT weights [S][O][W] (sfnn_build_quantized_proxy_stacked_
+// weights_kernel, cu:1735-1810): bucket rows + alpha * shared (two roundings),
+// fake-quantised to i8 at 64 when quantize.
+__global__ void qat_l1_fold_kernel(const float* __restrict__ l1w, const float* __restrict__ l1fw, float alpha,
+                                   size_t total, int out_dim, int width, int quantize, float* __restrict__ dst) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= total) return;
+    float v = l1w[t];
+    if (l1fw != nullptr) {
+        const size_t i = t % width;
+        const size_t o = (t / width) % out_dim;
+        v = fold_nf(v, alpha, l1fw[i * out_dim + o]);
+    }
+    dst[t] = quantize ? qat_q64(v) : v;
+}
+
+// L1 QAT biases (sfnn_build_quantized_proxy_stacked_bias_kernel, cu:1921-1991):
+// folded master bias, its i32 at 8128 and its fake-quantised value.
+__global__ void qat_l1_bias_kernel(const float* __restrict__ l1b, const float* __restrict__ l1fb, float alpha, int n,
+                                   int out_dim, int quantize, float* __restrict__ b_eff, int* __restrict__ b_int,
+                                   float* __restrict__ b_master) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    float v = l1b[t];
+    if (l1fb != nullptr) v = fold_nf(v, alpha, l1fb[t % out_dim]);
+    if (b_master != nullptr) b_master[t] = v;
+    if (b_int != nullptr) b_int[t] = qat_bias_int(v);
+    if (b_eff != nullptr) b_eff[t] = quantize ? qat_q8128(v) : v;
+}
+
+// bulletou_layer_qat FT layout (layer_qat_ft_fold_kernel, cu:9302-9312): base
+// rows folded with virtual row base + f % vr and fake-quantised; virtual rows 0.
+__global__ void layer_qat_ft_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t base, size_t vr,
+                                    size_t width, float alpha, size_t total) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= total) return;
+    const size_t f = t / width;
+    const size_t u = t - f * width;
+    if (f >= base) {
+        dst[t] = 0.0f;
+        return;
+    }
+    dst[t] = qat_q127(fold_nf(src[t], alpha, src[(base + f % vr) * width + u]));
+}
+
+__global__ void nonzero_kernel(const float* __restrict__ w, size_t nw, const float* __restrict__ b, size_t nb,
+                               float* __restrict__ flag) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const bool nz = i < nw ? w[i] != 0.0f : (i < nw + nb && b[i - nw] != 0.0f);
+    if (__syncthreads_or(nz) && threadIdx.x == 0) atomicExch(flag, 1.0f);
 }
 
 // ------------------------------------------------------------------ bucket sort + tiles
@@ -148,7 +257,13 @@ struct FtArgs {
     int max_active;
     int n_features;
     int width;
+    int lattice;         // dense QAT: combined floored to the 1/127 lattice (cu:5993-6012)
 };
+
+__device__ __forceinline__ float pair_out(float x0, float x1, int lattice) {
+    const float c = x0 * x1 * kPairScale;
+    return lattice ? qat_on_lattice(qat_lattice(c)) : c;
+}
 
 // One warp per half-position; lane owns float4 chunks lane + 32 i, so chunk i
 // and chunk i + NCH/2 are the two members of a pair (width / 2 apart).
@@ -194,8 +309,8 @@ __global__ void __launch_bounds__(256) ft_forward_kernel(FtArgs a) {
 #pragma unroll
     for (int i = 0; i < NCH / 2; ++i) {
         const float4 x0 = acc[i], x1 = acc[i + NCH / 2];
-        comb[lane + 32 * i] = make_float4(x0.x * x1.x * kPairScale, x0.y * x1.y * kPairScale,
-                                          x0.z * x1.z * kPairScale, x0.w * x1.w * kPairScale);
+        comb[lane + 32 * i] = make_float4(pair_out(x0.x, x1.x, a.lattice), pair_out(x0.y, x1.y, a.lattice),
+                                          pair_out(x0.z, x1.z, a.lattice), pair_out(x0.w, x1.w, a.lattice));
     }
 }
 
@@ -220,14 +335,38 @@ __global__ void ft_forward_generic_kernel(FtArgs a) {
     float* out = a.l0[v] + static_cast<size_t>(b) * a.width;
     out[j] = x0;
     out[j + half] = x1;
-    a.combined[static_cast<size_t>(b) * a.width + v * half + j] = x0 * x1 * kPairScale;
+    a.combined[static_cast<size_t>(b) * a.width + v * half + j] = pair_out(x0, x1, a.lattice);
+}
+
+// Dense QAT with FT QAT: the engine's integer FT from the fake-quantised table
+// (q / 127): doubled i16 sums with wrap, clamp [0, 254], (s0 * s1) >> 9, over
+// 127 (dense_qat_exact_ft_kernel, cu:6344-6390).  Thread per (half-position, pair).
+__global__ void qat_exact_ft_kernel(FtArgs a) {
+    const int half = a.width / 2;
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= static_cast<size_t>(a.n_half) * half) return;
+    const int h = static_cast<int>(t / half);
+    const int j = static_cast<int>(t - static_cast<size_t>(h) * half);
+    const int b = h >> 1, v = h & 1;
+    const int* idx = (v ? a.nstm : a.stm) + static_cast<size_t>(b) * a.max_active;
+    int s0 = 2 * qat_int127(a.bias[j]), s1 = 2 * qat_int127(a.bias[j + half]);
+    for (int s = 0; s < a.max_active; ++s) {
+        const int f = idx[s];
+        if (f < 0 || f >= a.n_features) continue;
+        const float* row = a.table + static_cast<size_t>(f) * a.width;
+        s0 += 2 * qat_int127(row[j]);
+        s1 += 2 * qat_int127(row[j + half]);
+    }
+    const int x0 = min(254, max(0, static_cast<int>(static_cast<short>(s0))));
+    const int x1 = min(254, max(0, static_cast<int>(static_cast<short>(s1))));
+    a.combined[static_cast<size_t>(b) * a.width + v * half + j] = qat_on_lattice((x0 * x1) >> 9);
 }
 
 // ------------------------------------------------------------------ L1
 // Effective L1 weights, input-major [stacks][width][l1_out]:
 // l1w[s][o][i] + alpha * l1fw[i][o]  (cu:2297-2303).
 __global__ void l1_eff_kernel(const float* __restrict__ l1w, const float* __restrict__ l1fw, float alpha, int stacks,
-                              int out_dim, int width, float* __restrict__ w_eff) {
+                              int out_dim, int width, int quantize, float* __restrict__ w_eff) {
     const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const size_t per = static_cast<size_t>(width) * out_dim;
     if (t >= per * stacks) return;
@@ -236,7 +375,13 @@ __global__ void l1_eff_kernel(const float* __restrict__ l1w, const float* __rest
     const size_t i = r / out_dim;
     const size_t o = r - i * out_dim;
     float w = l1w[(s * out_dim + o) * width + i];
-    if (l1fw != nullptr) w = fmaf(alpha, l1fw[i * out_dim + o], w);
+    if (quantize) {
+        // L1 QAT: fold with two roundings, then fake-quantise (cu:11514-11570).
+        if (l1fw != nullptr) w = fold_nf(w, alpha, l1fw[i * out_dim + o]);
+        w = qat_q64(w);
+    } else if (l1fw != nullptr) {
+        w = fmaf(alpha, l1fw[i * out_dim + o], w);
+    }
     w_eff[t] = w;
 }
 
@@ -326,6 +471,99 @@ __global__ void __launch_bounds__(256) l1_forward_generic_kernel(L1Args a) {
     }
 }
 
+// Dense QAT L1 (dense_qat_l1_warp_kernel / _packed, cu:6056-6100, 6223-6280):
+// raw = round(b * 8128) + sum_i int(c_i * 127) * int(w_i * 64) over the lattice
+// FT output and the fake-quantised weights, exact in integers; l1 = raw / 8128.
+struct L1IntArgs {
+    Tiles tiles;
+    const float* combined;
+    const float* w_eff;  // [stacks][width][O] fake-quantised
+    const int* b_int;    // [stacks][O]
+    float* l1;
+    int* raw;
+    int width;
+    int out_dim;
+    int stacks;
+};
+
+// O = 16: thread (sample lane, output quad), the tile's integer weights in
+// shared memory as [width][16] (int4 reads).
+__global__ void __launch_bounds__(256) l1_forward16_int_kernel(L1IntArgs a) {
+    extern __shared__ int4 wi4[];
+    const int t = blockIdx.x;
+    if (t >= *a.tiles.n_tiles) return;
+    const int s = a.tiles.key[t];
+    const int pb = a.tiles.begin[t], pe = a.tiles.end[t];
+    if (s >= a.stacks) {
+        for (int i = threadIdx.x; i < (pe - pb) * 16; i += blockDim.x) {
+            const size_t k = static_cast<size_t>(a.tiles.order[pb + i / 16]) * 16 + (i & 15);
+            a.l1[k] = 0.0f;
+            a.raw[k] = 0;
+        }
+        return;
+    }
+    const float4* src = reinterpret_cast<const float4*>(a.w_eff + static_cast<size_t>(s) * a.width * 16);
+    for (int i = threadIdx.x; i < a.width * 4; i += blockDim.x) {
+        const float4 w = src[i];
+        wi4[i] = make_int4(qat_int64(w.x), qat_int64(w.y), qat_int64(w.z), qat_int64(w.w));
+    }
+    __syncthreads();
+    const int og = threadIdx.x & 3;
+    const int w4 = a.width >> 2;
+    for (int p = pb + (threadIdx.x >> 2); p < pe; p += 64) {
+        const int b = a.tiles.order[p];
+        const float4* c4 = reinterpret_cast<const float4*>(a.combined) + static_cast<size_t>(b) * w4;
+        // |sum| <= width * 127 * 128 < 2^31 for every width this backend accepts (<= 8192).
+        int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+        for (int k4 = 0; k4 < w4; ++k4) {
+            const float4 c = __ldg(c4 + k4);
+            const int cv[4] = {qat_int127(c.x), qat_int127(c.y), qat_int127(c.z), qat_int127(c.w)};
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const int4 w = wi4[(4 * k4 + kk) * 4 + og];
+                acc0 += cv[kk] * w.x;
+                acc1 += cv[kk] * w.y;
+                acc2 += cv[kk] * w.z;
+                acc3 += cv[kk] * w.w;
+            }
+        }
+        const int accs[4] = {acc0, acc1, acc2, acc3};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int o = 4 * og + q;
+            const long long r = static_cast<long long>(accs[q]) + a.b_int[s * 16 + o];
+            a.raw[static_cast<size_t>(b) * 16 + o] = static_cast<int>(r);
+            a.l1[static_cast<size_t>(b) * 16 + o] = qat_raw_to_float(r);
+        }
+    }
+}
+
+// Any O / width: one thread per (sample, output) of the tile.
+__global__ void __launch_bounds__(256) l1_forward_int_generic_kernel(L1IntArgs a) {
+    const int t = blockIdx.x;
+    if (t >= *a.tiles.n_tiles) return;
+    const int s = a.tiles.key[t];
+    const int pb = a.tiles.begin[t], pe = a.tiles.end[t];
+    const int O = a.out_dim;
+    for (int i = threadIdx.x; i < (pe - pb) * O; i += blockDim.x) {
+        const int b = a.tiles.order[pb + i / O];
+        const int o = i % O;
+        const size_t k = static_cast<size_t>(b) * O + o;
+        if (s >= a.stacks) {
+            a.l1[k] = 0.0f;
+            a.raw[k] = 0;
+            continue;
+        }
+        const float* c = a.combined + static_cast<size_t>(b) * a.width;
+        const float* w = a.w_eff + static_cast<size_t>(s) * a.width * O + o;
+        long long acc = a.b_int[s * O + o];
+        for (int j = 0; j < a.width; ++j)
+            acc += static_cast<long long>(qat_int127(c[j])) * qat_int64(w[static_cast<size_t>(j) * O]);
+        a.raw[k] = static_cast<int>(acc);
+        a.l1[k] = qat_raw_to_float(acc);
+    }
+}
+
 // ------------------------------------------------------------------ head
 enum HeadMode : int { kHeadForward = 0, kHeadTrain = 1, kHeadBackward = 2 };
 
@@ -359,13 +597,22 @@ struct HeadArgs {
     int l2_size;
     int stacks;
     int mode;
+    // QAT
+    int qat_l2;               // fake-quantise the staged L2 weights / biases
+    int qat_l3;
+    const int* l1_raw;        // dense: integer L1 sums [B][O]
+    int* l2_raw;              // dense: integer L2 sums [B][L2] (forward-only mode writes, backward mode reads)
+    const float* b1_master;   // dense: folded master L1 bias [S][O] and its i32 at 8128
+    const int* b1_int;
+    const float* l2b_master;  // dense: master L2 / L3 biases (rounded to 8128 for the integer layers)
+    const float* l3b_master;
 };
 
 __host__ __device__ inline int head_partial_len(int l2, int i2, int o) { return l2 * i2 + 2 * l2 + 1 + o + 1; }
 
 // Thread per sample (blockDim = kSfnnTile).  H / L2: compile-time dims, or 0
 // for runtime dims up to the kSfnnMax* bounds.
-template <int H, int L2>
+template <int H, int L2, bool DENSE>
 __global__ void __launch_bounds__(kSfnnTile) head_kernel(HeadArgs a) {
     constexpr int kH = H > 0 ? H : (kSfnnMaxL1Out - 1);
     constexpr int kL2 = L2 > 0 ? L2 : kSfnnMaxL2;
@@ -385,6 +632,10 @@ __global__ void __launch_bounds__(kSfnnTile) head_kernel(HeadArgs a) {
     float* st_go = st_l2 + kSfnnTile * l2n;   // [T]
     float* st_g1 = st_go + kSfnnTile;         // [T][O]
     float* st_ls = st_g1 + kSfnnTile * O;     // [T]
+    int* w2i = reinterpret_cast<int*>(st_ls + kSfnnTile);  // dense: integer weights / biases
+    int* b2i = w2i + l2n * i2n;
+    int* w3i = b2i + l2n;
+    int* b3i = w3i + l2n;
 
     const int t = blockIdx.x;
     if (t >= *a.tiles.n_tiles) return;
@@ -393,23 +644,34 @@ __global__ void __launch_bounds__(kSfnnTile) head_kernel(HeadArgs a) {
     const int pb = a.tiles.begin[t], pe = a.tiles.end[t];
     if (valid) {
         // Effective weights: bucket + alpha * shared (cu:2449-2552).
+        // Layer QAT fake-quantises the staged values (layer_qat_vector_kernel, cu:9294).
         for (int i = threadIdx.x; i < l2n * i2n; i += blockDim.x) {
             float w = a.l2w[static_cast<size_t>(s) * l2n * i2n + i];
             if (a.l2fw != nullptr) w = fmaf(a.alpha, a.l2fw[i], w);
+            if (a.qat_l2) w = qat_q64(w);
             w2e[i] = w;
+            if (DENSE) w2i[i] = qat_int64(w);
         }
         for (int o = threadIdx.x; o < l2n; o += blockDim.x) {
             float b = a.l2b != nullptr ? a.l2b[s * l2n + o] : 0.0f;
             if (a.l2fb != nullptr) b = fmaf(a.alpha, a.l2fb[o], b);
+            if (a.qat_l2) b = qat_q8128(b);
             b2e[o] = b;
             float w = a.l3w[s * l2n + o];
             if (a.l3fw != nullptr) w = fmaf(a.alpha, a.l3fw[o], w);
+            if (a.qat_l3) w = qat_q64(w);
             w3e[o] = w;
+            if (DENSE) {
+                w3i[o] = qat_int64(w);
+                b2i[o] = qat_bias_int(a.l2b_master[s * l2n + o]);
+            }
         }
         if (threadIdx.x == 0) {
             float b = a.l3b != nullptr ? a.l3b[s] : 0.0f;
             if (a.l3fb != nullptr) b = fmaf(a.alpha, a.l3fb[0], b);
+            if (a.qat_l3) b = qat_q8128(b);
             b3e[0] = b;
+            if (DENSE) b3i[0] = qat_bias_int(a.l3b_master[s]);
         }
     }
     __syncthreads();
@@ -419,11 +681,69 @@ __global__ void __launch_bounds__(kSfnnTile) head_kernel(HeadArgs a) {
     if (p < pe) {
         const int b = a.tiles.order[p];
         float in[kI2], l2v[kL2], hid[kH];
+        int r2[DENSE ? kL2 : 1];
         float out = 0.0f;
         const float* l1r = a.l1 + static_cast<size_t>(b) * O;
 #pragma unroll
         for (int i = 0; i < kH; ++i) hid[i] = (H > 0 || i < hdim) ? l1r[i] : 0.0f;
-        if (a.mode != kHeadBackward) {
+        if (DENSE && a.mode != kHeadBackward) {
+            // Integer L2 input / L2 / L3 + skip (cu:6282-6320).
+            if (valid) {
+                const int* r1 = a.l1_raw + static_cast<size_t>(b) * O;
+                int ii[kI2];
+#pragma unroll
+                for (int i = 0; i < kH; ++i) {
+                    if (H > 0 || i < hdim) {
+                        const long long x = r1[i];
+                        const int sq = static_cast<int>(min(127LL, (x * x) >> 19));
+                        const int lin = max(0, min(127, r1[i] >> 6));
+                        ii[i] = sq;
+                        ii[hdim + i] = lin;
+                        in[i] = qat_on_lattice(sq);
+                        in[hdim + i] = qat_on_lattice(lin);
+                    }
+                }
+                long long outr = b3i[0];
+#pragma unroll
+                for (int o = 0; o < kL2; ++o) {
+                    if (L2 > 0 || o < l2n) {
+                        long long sum = b2i[o];
+                        const int* wr = w2i + o * i2n;
+#pragma unroll
+                        for (int i = 0; i < kI2; ++i)
+                            if (H > 0 || i < i2n) sum += static_cast<long long>(ii[i]) * wr[i];
+                        r2[o] = static_cast<int>(sum);
+                        const int v = max(0, min(127, r2[o] >> 6));
+                        l2v[o] = qat_on_lattice(v);
+                        outr += static_cast<long long>(v) * w3i[o];
+                    }
+                }
+                if (a.l1_skip) outr += r1[hdim];
+                out = qat_raw_to_float(outr);
+            } else {
+#pragma unroll
+                for (int i = 0; i < kI2; ++i) in[i] = 0.0f;
+#pragma unroll
+                for (int o = 0; o < kL2; ++o) {
+                    l2v[o] = 0.0f;
+                    r2[o] = 0;
+                }
+            }
+            if (a.mode == kHeadForward && a.l2_raw != nullptr) {
+#pragma unroll
+                for (int o = 0; o < kL2; ++o)
+                    if (L2 > 0 || o < l2n) a.l2_raw[static_cast<size_t>(b) * l2n + o] = r2[o];
+            }
+            float* ir = a.l2_input + static_cast<size_t>(b) * i2n;
+            float* lr = a.l2 + static_cast<size_t>(b) * l2n;
+#pragma unroll
+            for (int i = 0; i < kI2; ++i)
+                if (H > 0 || i < i2n) ir[i] = in[i];
+#pragma unroll
+            for (int o = 0; o < kL2; ++o)
+                if (L2 > 0 || o < l2n) lr[o] = l2v[o];
+            a.output[b] = out;
+        } else if (a.mode != kHeadBackward) {
             if (valid) {
                 // L2 input: [SqrCReLU | CReLU] of the hidden L1 outputs (cu:2428-2447).
 #pragma unroll
@@ -472,6 +792,11 @@ __global__ void __launch_bounds__(kSfnnTile) head_kernel(HeadArgs a) {
             for (int i = 0; i < kI2; ++i) in[i] = (H > 0 || i < i2n) ? ir[i] : 0.0f;
 #pragma unroll
             for (int o = 0; o < kL2; ++o) l2v[o] = (L2 > 0 || o < l2n) ? lr[o] : 0.0f;
+            if (DENSE) {
+#pragma unroll
+                for (int o = 0; o < kL2; ++o)
+                    r2[o] = (valid && (L2 > 0 || o < l2n)) ? a.l2_raw[static_cast<size_t>(b) * l2n + o] : 0;
+            }
         }
         if (a.mode != kHeadForward) {
             float gout = 0.0f, loss = 0.0f;
@@ -490,8 +815,26 @@ __global__ void __launch_bounds__(kSfnnTile) head_kernel(HeadArgs a) {
                 for (int o = 0; o < kL2; ++o) {
                     if (L2 > 0 || o < l2n) {
                         const float g = gout * w3e[o];
-                        if (a.l2_gradients != nullptr) a.l2_gradients[static_cast<size_t>(b) * l2n + o] = g;
-                        g2m[o] = crelu_grad(l2v[o], g);
+                        if (DENSE) {
+                            // Continuous STE of the integer CReLU (cu:6322-6342): zero
+                            // outside [0, 8128]; at the edges the side of the rounded-off
+                            // master-bias fraction decides.
+                            const int x = r2[o];
+                            float gg = g;
+                            if (x < 0 || x > 8128) {
+                                gg = 0.0f;
+                            } else if (x == 0 || x == 8128) {
+                                const double bias = fmin(2147483647.0, fmax(-2147483648.0,
+                                    static_cast<double>(a.l2b_master[s * l2n + o]) * 8128.0));
+                                const double fraction = bias - round(bias);
+                                if ((x == 0 && fraction <= 0.0) || (x == 8128 && fraction >= 0.0)) gg = 0.0f;
+                            }
+                            g2m[o] = gg;
+                            if (a.l2_gradients != nullptr) a.l2_gradients[static_cast<size_t>(b) * l2n + o] = gg;
+                        } else {
+                            if (a.l2_gradients != nullptr) a.l2_gradients[static_cast<size_t>(b) * l2n + o] = g;
+                            g2m[o] = crelu_grad(l2v[o], g);
+                        }
                     } else {
                         g2m[o] = 0.0f;
                     }
@@ -513,10 +856,39 @@ __global__ void __launch_bounds__(kSfnnTile) head_kernel(HeadArgs a) {
 #pragma unroll
                 for (int i = 0; i < kH; ++i) {
                     if (H > 0 || i < hdim) {
-                        const float v = hid[i];
-                        const float cs = fabsf(v) * fabsf(v) * kPairScale;
-                        const float sg = (cs > 0.0f && cs < 1.0f) ? gin[i] * (2.0f * v * kPairScale) : 0.0f;
-                        const float lg = (v > 0.0f && v < 1.0f) ? gin[hdim + i] : 0.0f;
+                        float v = hid[i];
+                        bool sq_on, lin_on;
+                        if (DENSE) {
+                            // STE from the pre-rounding L1 value: raw / 8128 plus the
+                            // rounded-off part of the master bias (cu:3730-3766).
+                            const float master = a.b1_master[s * O + i];
+                            const int qi = a.b1_int[s * O + i];
+                            float frac;
+                            if (qi >= -16777216 && qi <= 16777216) {
+                                frac = __fmaf_rn(master, 8128.0f, -static_cast<float>(qi));
+                            } else {
+                                const double scaled = fmin(2147483647.0, fmax(-2147483648.0,
+                                                                              static_cast<double>(master) * 8128.0));
+                                frac = static_cast<float>(scaled - static_cast<double>(qi));
+                            }
+                            v = __fmaf_rn(frac, __fdiv_rn(1.0f, 8128.0f), v);
+                            const float cs = fabsf(v) * fabsf(v) * kPairScale;
+                            sq_on = cs > 0.0f && cs < 1.0f;
+                            lin_on = v > 0.0f && v < 1.0f;
+                            const int raw = a.l1_raw[static_cast<size_t>(b) * O + i];
+                            if (raw == 0) lin_on = frac > 0.0f;
+                            else if (raw == 8128) lin_on = frac < 0.0f;
+                            if (raw == 8160 || raw == -8160) {
+                                const double xd = static_cast<double>(raw) + static_cast<double>(frac);
+                                sq_on = xd * xd * 127.0 < 128.0 * 8128.0 * 8128.0;
+                            }
+                        } else {
+                            const float cs = fabsf(v) * fabsf(v) * kPairScale;
+                            sq_on = cs > 0.0f && cs < 1.0f;
+                            lin_on = v > 0.0f && v < 1.0f;
+                        }
+                        const float sg = sq_on ? gin[i] * (2.0f * v * kPairScale) : 0.0f;
+                        const float lg = lin_on ? gin[hdim + i] : 0.0f;
                         g1r[i] = sg + lg;
                         st_g1[lt * O + i] = sg + lg;
                     }
@@ -587,6 +959,7 @@ struct L1BackArgs {
     const float* g1;     // [B][O]
     const float* w_eff;  // [stacks][width][O]
     const float* l0[2];  // ClippedReLU FT output per perspective
+    const float* combined;  // dense QAT: the lattice FT output (dL1w uses it); null: recomputed
     // fused step: pre-activation gradients in king order, row rank[h]
     float* pregrad_sorted;
     const int* rank;
@@ -659,7 +1032,7 @@ __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
             const int q = q0 + u;
             if (q >= n) break;
             const float x0 = xa[u], x1 = xb[u];
-            const float c = x0 * x1 * kPairScale;
+            const float c = a.combined != nullptr ? a.combined[static_cast<size_t>(bs[q]) * W + i] : x0 * x1 * kPairScale;
             float dc = 0.0f;
 #pragma unroll
             for (int o = 0; o < kO; ++o) {
@@ -1076,7 +1449,8 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a) {
 
 // ------------------------------------------------------------------ host plan
 struct SfnnPlan {
-    const float* table;  // what the FT gather reads
+    const float* table;    // what the FT gather reads
+    const float* ft_bias;  // FT bias the gather starts from (fake-quantised under FT QAT)
     KingSortOut king;
     int* king_rank;
     Tiles tiles;
@@ -1085,7 +1459,31 @@ struct SfnnPlan {
     float* dw1_partials;
     float* l0b_partials;
     float* g1;
+    // QAT scratch (l1 or dense)
+    float* b1_eff;     // [S][O] fake-quantised folded L1 bias
+    int* b1_int;       // [S][O] its i32 at 8128
+    float* b1_master;  // [S][O] folded master L1 bias
+    int* l1_raw;       // [B][O] integer L1 sums
+    int* l2_raw;       // [B][L2] integer L2 sums
 };
+
+// QAT scratch: kept in one slot of fixed layout, so the reference forward and
+// backward entries see the integer sums of the forward in the backward.
+int qat_scratch(BulletOuCudaCppContext* ctx, const SfnnDims& d, SfnnPlan* plan) {
+    const size_t so = align_floats(static_cast<size_t>(d.stacks) * d.l1_out);
+    const size_t bo = align_floats(static_cast<size_t>(d.batch) * d.l1_out);
+    const size_t bl = align_floats(static_cast<size_t>(d.batch) * d.l2_size);
+    void* p = nullptr;
+    if (scratch_slot(ctx, kScratchSfnnQat, (3 * so + bo + bl) * sizeof(float), &p, "cudaMalloc SFNN QAT") != 0)
+        return -1;
+    float* f = static_cast<float*>(p);
+    plan->b1_eff = f;
+    plan->b1_int = reinterpret_cast<int*>(f + so);
+    plan->b1_master = f + 2 * so;
+    plan->l1_raw = reinterpret_cast<int*>(f + 3 * so);
+    plan->l2_raw = reinterpret_cast<int*>(f + 3 * so + bo);
+    return 0;
+}
 
 // Fold, sorts, tile table and effective L1 weights; every scratch the step needs.
 int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, const int* stm, const int* nstm,
@@ -1094,7 +1492,28 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
     int blocks = 0;
     // 1. fold
     plan->table = w.l0w;
-    if (d.base > 0) {
+    plan->ft_bias = w.l0b;
+    if (d.qat.ft && w.l0w != nullptr) {
+        // FT QAT: Q(row + alpha * virtual row) for the base rows (layer_qat.rs:832-880).
+        const size_t n = static_cast<size_t>(d.n_features) * d.width;
+        float* folded = fold_target;
+        if (folded == nullptr) {
+            void* p = nullptr;
+            if (scratch_slot(ctx, kScratchSfnnFold, n * sizeof(float), &p, "cudaMalloc SFNN folded FT") != 0) return -1;
+            folded = static_cast<float*>(p);
+        }
+        if (grid_1d(n, threads, &blocks, "SFNN FT QAT fold") != 0) return -1;
+        fold_ft_qat_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l0w, folded, n, d.width, d.base, d.ft_alpha);
+        void* bp = nullptr;
+        if (scratch_slot(ctx, kScratchSfnnQatFt, static_cast<size_t>(d.width) * sizeof(float), &bp,
+                         "cudaMalloc SFNN FT QAT bias") != 0)
+            return -1;
+        qat_vector_kernel<<<(d.width + threads - 1) / threads, threads, 0, ctx->stream>>>(
+            w.l0b, static_cast<float*>(bp), static_cast<size_t>(d.width), 0);
+        if (check_launch("SFNN FT QAT launch") != 0) return -1;
+        plan->table = folded;
+        plan->ft_bias = static_cast<float*>(bp);
+    } else if (d.base > 0) {
         float* folded = fold_target;
         const size_t n = static_cast<size_t>(d.base) * d.width;
         if (folded == nullptr) {
@@ -1160,8 +1579,18 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
     plan->w1_eff = static_cast<float*>(ep);
     if (grid_1d(eff, threads, &blocks, "SFNN L1 weights") != 0) return -1;
     l1_eff_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l1w, d.has_l1f ? w.l1fw : nullptr, d.shared_alpha, d.stacks,
-                                                       d.l1_out, d.width, plan->w1_eff);
+                                                       d.l1_out, d.width, d.qat.l1, plan->w1_eff);
     if (check_launch("SFNN L1 weights launch") != 0) return -1;
+    if (d.qat.l1 || d.qat.dense) {
+        if (qat_scratch(ctx, d, plan) != 0) return -1;
+        if (d.qat.l1 && w.l1b != nullptr) {
+            const int n = d.stacks * d.l1_out;
+            qat_l1_bias_kernel<<<(n + threads - 1) / threads, threads, 0, ctx->stream>>>(
+                w.l1b, d.has_l1f ? w.l1fb : nullptr, d.shared_alpha, n, d.l1_out, 1, plan->b1_eff, plan->b1_int,
+                plan->b1_master);
+            if (check_launch("SFNN L1 QAT bias launch") != 0) return -1;
+        }
+    }
     const size_t hp = align_floats(static_cast<size_t>(max_tiles) * head_partial_len(d.l2_size, d.l2_in, d.l1_out));
     const size_t dp = align_floats(static_cast<size_t>(max_tiles) * d.l1_out * d.width);
     const size_t bp = align_floats(static_cast<size_t>(max_tiles) * 2 * d.width);
@@ -1180,7 +1609,30 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
 
 int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnPlan& plan, const int* stm,
                       const int* nstm, const float* l0b, const SfnnActivations& act) {
+    if (d.qat.dense && d.qat.integer_ft) {
+        // The f32 FT pass keeps the activations the backward uses; combined is
+        // then overwritten by the engine's integer FT (cu:6654-6662).
+        SfnnDims df = d;
+        df.qat.integer_ft = 0;
+        df.qat.dense = 0;
+        if (launch_ft_forward(ctx, df, plan, stm, nstm, l0b, act) != 0) return -1;
+        FtArgs ea{};
+        ea.stm = stm;
+        ea.nstm = nstm;
+        ea.table = plan.table;
+        ea.bias = l0b;
+        ea.combined = act.combined;
+        ea.n_half = 2 * d.batch;
+        ea.max_active = d.max_active;
+        ea.n_features = d.n_features;
+        ea.width = d.width;
+        int gb = 0;
+        if (grid_1d(static_cast<size_t>(ea.n_half) * (d.width / 2), 256, &gb, "SFNN exact QAT FT") != 0) return -1;
+        qat_exact_ft_kernel<<<gb, 256, 0, ctx->stream>>>(ea);
+        return check_launch("SFNN exact QAT FT launch");
+    }
     FtArgs fa{};
+    fa.lattice = d.qat.dense ? 1 : 0;
     fa.order = plan.king.order;
     fa.stm = stm;
     fa.nstm = nstm;
@@ -1212,12 +1664,35 @@ int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const Sfnn
 
 int launch_l1_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, const SfnnPlan& plan,
                       const float* combined, float* l1) {
+    if (d.qat.dense) {
+        L1IntArgs ia{};
+        ia.tiles = plan.tiles;
+        ia.combined = combined;
+        ia.w_eff = plan.w1_eff;
+        ia.b_int = plan.b1_int;
+        ia.l1 = l1;
+        ia.raw = plan.l1_raw;
+        ia.width = d.width;
+        ia.out_dim = d.l1_out;
+        ia.stacks = d.stacks;
+        const size_t smem = static_cast<size_t>(d.width) * 16 * sizeof(int);
+        if (d.l1_out == 16 && d.width % 4 == 0 && smem <= 200 * 1024 && aligned16(combined)) {
+            cudaError_t st = cudaFuncSetAttribute(l1_forward16_int_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(smem));
+            if (st != cudaSuccess) return fail("cudaFuncSetAttribute SFNN QAT L1", st);
+            l1_forward16_int_kernel<<<plan.tiles.max_tiles, 256, smem, ctx->stream>>>(ia);
+        } else {
+            l1_forward_int_generic_kernel<<<plan.tiles.max_tiles, 256, 0, ctx->stream>>>(ia);
+        }
+        return check_launch("SFNN QAT L1 forward launch");
+    }
     L1Args la{};
     la.tiles = plan.tiles;
     la.combined = combined;
     la.w_eff = plan.w1_eff;
-    la.l1b = w.l1b;
-    la.l1fb = d.has_l1f ? w.l1fb : nullptr;
+    // L1 QAT: the fake-quantised folded bias replaces bias + shared factor.
+    la.l1b = d.qat.l1 ? plan.b1_eff : w.l1b;
+    la.l1fb = (d.has_l1f && !d.qat.l1) ? w.l1fb : nullptr;
     la.alpha = d.shared_alpha;
     la.l1 = l1;
     la.width = d.width;
@@ -1237,12 +1712,15 @@ int launch_l1_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const Sfnn
 
 size_t head_smem_bytes(const SfnnDims& d) {
     const size_t l2 = d.l2_size, i2 = d.l2_in, o = d.l1_out;
-    return (l2 * i2 + 2 * l2 + 1 + kSfnnTile * (2 * l2 + i2 + 1 + o + 1)) * sizeof(float);
+    const size_t ints = d.qat.dense ? l2 * i2 + 2 * l2 + 1 : 0;
+    return (l2 * i2 + 2 * l2 + 1 + kSfnnTile * (2 * l2 + i2 + 1 + o + 1)) * sizeof(float) + ints * sizeof(int);
 }
 
 int launch_head(BulletOuCudaCppContext* ctx, const SfnnDims& d, const HeadArgs& h) {
     const size_t smem = head_smem_bytes(d);
-    auto kernel = (d.l1_hidden == 15 && d.l2_size == 32) ? head_kernel<15, 32> : head_kernel<0, 0>;
+    const bool prod = d.l1_hidden == 15 && d.l2_size == 32;
+    auto kernel = d.qat.dense ? (prod ? head_kernel<15, 32, true> : head_kernel<0, 0, true>)
+                              : (prod ? head_kernel<15, 32, false> : head_kernel<0, 0, false>);
     cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (st != cudaSuccess) return fail("cudaFuncSetAttribute SFNN head", st);
     kernel<<<h.tiles.max_tiles, kSfnnTile, smem, ctx->stream>>>(h);
@@ -1272,6 +1750,16 @@ HeadArgs head_args(const SfnnDims& d, const SfnnWeights& w, const SfnnPlan& plan
     h.l1_skip = d.l1_skip;
     h.l2_size = d.l2_size;
     h.stacks = d.stacks;
+    h.qat_l2 = d.qat.l2;
+    h.qat_l3 = d.qat.l3;
+    if (d.qat.dense) {
+        h.l1_raw = plan.l1_raw;
+        h.l2_raw = plan.l2_raw;
+        h.b1_master = plan.b1_master;
+        h.b1_int = plan.b1_int;
+        h.l2b_master = d.qat.l2b_master;
+        h.l3b_master = d.qat.l3b_master;
+    }
     return h;
 }
 
@@ -1463,7 +1951,7 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
     StepBuffers sb{};
     if (step_buffers(ctx, d, output, &sb) != 0) return -1;
     prof_mark(ctx);
-    if (launch_ft_forward(ctx, d, plan, stm, nstm, w.l0b, sb.act) != 0) return -1;
+    if (launch_ft_forward(ctx, d, plan, stm, nstm, plan.ft_bias, sb.act) != 0) return -1;
     prof_mark(ctx);
     if (launch_l1_forward(ctx, d, w, plan, sb.act.combined, sb.act.l1) != 0) return -1;
     HeadArgs h = head_args(d, w, plan, sb.act);
@@ -1480,6 +1968,7 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
     lb.l0[1] = sb.act.nstm_l0;
     lb.pregrad_sorted = sb.pregrad;
     lb.rank = plan.king_rank;
+    lb.combined = d.qat.dense ? sb.act.combined : nullptr;
     if (launch_l1_backward(ctx, d, plan, lb) != 0) return -1;
     prof_mark(ctx);
     // small-parameter gradients (packed), loss sum, then Ranger per group
@@ -1527,6 +2016,25 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
         if (launch_piece_rows(ctx, kRowWrite, r) != 0) return -1;
     }
     prof_mark(ctx);
+    return 0;
+}
+
+// The fused step's QAT switches (null: none) into d->qat; the f32 masters in
+// `w` are what every QAT mode rounds.  Layer QAT of L2 / L3 takes no shared
+// factor (layer_qat.rs:937-943).
+int apply_qat(const BulletOuB200SfnnQat* q, const SfnnWeights& w, SfnnDims* d) {
+    d->qat = SfnnQat{};
+    if (q == nullptr) return 0;
+    if ((q->l2 && d->has_l2f) || (q->l3 && d->has_l3f))
+        return fail_message("SFNN layer QAT does not support L2/L3 shared factors; fold them first");
+    d->qat.l1 = q->l1 != 0;
+    d->qat.ft = q->ft != 0;
+    d->qat.l2 = q->l2 != 0;
+    d->qat.l3 = q->l3 != 0;
+    d->qat.dense = d->qat.l1 && d->qat.l2 && d->qat.l3;
+    d->qat.integer_ft = d->qat.dense && d->qat.ft;
+    d->qat.l2b_master = w.l2b;
+    d->qat.l3b_master = w.l3b;
     return 0;
 }
 
@@ -1589,13 +2097,12 @@ int bulletou_cuda_cpp_sfnn_forward_device(
     (void)l2axb;
     (void)l3axw;
     (void)l3axb;
-    (void)refresh_qat_l1;
     if (reject_unsupported(l1_group_count, l1_common_size, l1_shard_size, has_l1ax, has_l2ax, has_l3ax, use_king_axis,
                            use_hand_axis, use_progress_axis, use_king_hand_pair, use_king_progress_pair,
                            use_hand_progress_pair, residual_count_gates, factorizer_axis_confidences) != 0)
         return -1;
-    if (qat_l1w != nullptr || qat_l1b != nullptr)
-        return fail_message("unsupported on this backend: L1 QAT scratch in the reference forward entry");
+    if ((qat_l1w == nullptr) != (qat_l1b == nullptr))
+        return fail_message("L1 QAT requires both weight and bias scratch buffers");
     SfnnDims d{};
     if (sfnn_dims(input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks, batch, max_active, ft_factorizer_alpha,
                   factorizer_shared_alpha, &d) != 0)
@@ -1619,18 +2126,59 @@ int bulletou_cuda_cpp_sfnn_forward_device(
         return -1;
     if (folded_l0w != nullptr && validate_f32(ctx, folded_l0w, input_size * ft_size, "sfnn folded_l0w scratch") != 0)
         return -1;
+    const size_t l1w_len = static_cast<size_t>(d.stacks) * d.l1_out * d.width;
+    if (qat_l1w != nullptr && (validate_f32(ctx, qat_l1w, l1w_len, "QAT L1 weights") != 0 ||
+                               validate_f32(ctx, qat_l1b, static_cast<size_t>(d.stacks) * d.l1_out, "QAT L1 bias") != 0))
+        return -1;
+    // Dense QAT between bulletou_dense_qat_begin / _end (cu:6666-6668).
+    d.qat.dense = ctx->dense_qat ? 1 : 0;
+    d.qat.integer_ft = ctx->dense_qat && ctx->dense_qat_integer_ft ? 1 : 0;
+    d.qat.l2b_master = ctx->dense_qat_l2_bias;
+    d.qat.l3b_master = ctx->dense_qat_l3_bias;
+    if (d.qat.dense && ((has_l1f && qat_l1w == nullptr) || has_l2f || has_l3f))
+        return fail_message("dense QAT requires folded L1 and unfactorized L2/L3 without BN");
+    if (d.qat.dense && qat_l1w == nullptr)
+        return fail_message("dense QAT on this backend requires the L1 QAT scratch (qat_l1w / qat_l1b)");
     if (set_device(ctx) != 0) return -1;
-    const SfnnWeights w = weights_from(params);
+    SfnnWeights w = weights_from(params);
+    SfnnDims dk = d;
+    // L1 QAT: fold first, then fake-quantise; the f32 masters stay untouched.
+    // refresh_qat_l1: 1 rebuild quantised, 0 reuse quantised, -2 rebuild
+    // f32 fold, -1 reuse f32 fold (cu:11514-11590).
+    const bool quantize_l1 = refresh_qat_l1 >= 0;
+    const bool refresh_l1 = refresh_qat_l1 == 1 || refresh_qat_l1 == -2;
+    if (qat_l1w != nullptr) {
+        if (refresh_l1) {
+            int blocks = 0;
+            if (grid_1d(l1w_len, 256, &blocks, "QAT L1 weights") != 0) return -1;
+            qat_l1_fold_kernel<<<blocks, 256, 0, ctx->stream>>>(l1w->ptr, has_l1f ? l1fw->ptr : nullptr,
+                                                                factorizer_shared_alpha, l1w_len, d.l1_out, d.width,
+                                                                quantize_l1 ? 1 : 0, qat_l1w->ptr);
+            if (check_launch("QAT L1 weights launch") != 0) return -1;
+        }
+        w.l1w = qat_l1w->ptr;
+        w.l1b = qat_l1b->ptr;
+        w.l1fw = nullptr;
+        w.l1fb = nullptr;
+        dk.has_l1f = 0;
+    }
     SfnnPlan plan{};
-    if (sfnn_prepare(ctx, d, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr,
+    if (sfnn_prepare(ctx, dk, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr,
                      folded_l0w != nullptr ? folded_l0w->ptr : nullptr, &plan) != 0)
         return -1;
+    if (qat_l1w != nullptr && (refresh_l1 || d.qat.dense)) {
+        const int n = d.stacks * d.l1_out;
+        qat_l1_bias_kernel<<<(n + 255) / 256, 256, 0, ctx->stream>>>(
+            l1b->ptr, has_l1f ? l1fb->ptr : nullptr, factorizer_shared_alpha, n, d.l1_out, quantize_l1 ? 1 : 0,
+            qat_l1b->ptr, d.qat.dense ? plan.b1_int : nullptr, d.qat.dense ? plan.b1_master : nullptr);
+        if (check_launch("QAT L1 bias launch") != 0) return -1;
+    }
     const SfnnActivations act{stm_l0->ptr, nstm_l0->ptr, combined->ptr, l1->ptr, l2_input->ptr, l2->ptr, output->ptr};
-    if (launch_ft_forward(ctx, d, plan, stm_indices->ptr, nstm_indices->ptr, w.l0b, act) != 0) return -1;
-    if (launch_l1_forward(ctx, d, w, plan, act.combined, act.l1) != 0) return -1;
-    HeadArgs h = head_args(d, w, plan, act);
+    if (launch_ft_forward(ctx, dk, plan, stm_indices->ptr, nstm_indices->ptr, plan.ft_bias, act) != 0) return -1;
+    if (launch_l1_forward(ctx, dk, w, plan, act.combined, act.l1) != 0) return -1;
+    HeadArgs h = head_args(dk, w, plan, act);
     h.mode = kHeadForward;
-    if (launch_head(ctx, d, h) != 0) return -1;
+    if (launch_head(ctx, dk, h) != 0) return -1;
     return ok();
 }
 
@@ -1681,13 +2229,10 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     (void)l2axb_gradients;
     (void)l3axw_gradients;
     (void)l3axb_gradients;
-    (void)combined;
     if (reject_unsupported(l1_group_count, l1_common_size, l1_shard_size, has_l1ax, has_l2ax, has_l3ax, use_king_axis,
                            use_hand_axis, use_progress_axis, use_king_hand_pair, use_king_progress_pair,
                            use_hand_progress_pair, residual_count_gates, factorizer_axis_confidences) != 0)
         return -1;
-    if (qat_l1w != nullptr)
-        return fail_message("unsupported on this backend: L1 QAT weights in the reference backward entry");
     SfnnDims d{};
     if (sfnn_dims(input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks, batch, max_active, ft_factorizer_alpha,
                   factorizer_shared_alpha, &d) != 0)
@@ -1740,6 +2285,13 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
         validate_f32(ctx, l0w_gradients, input_size * ft_size, "l0w_gradients") != 0)
         return -1;
     if (entry_weights != nullptr && validate_f32(ctx, entry_weights, batch, "backward entry weights") != 0) return -1;
+    if (qat_l1w != nullptr && validate_f32(ctx, qat_l1w, g.len[kSfL1w], "QAT L1 weights") != 0) return -1;
+    d.qat.dense = ctx->dense_qat ? 1 : 0;
+    d.qat.l2b_master = ctx->dense_qat_l2_bias;
+    d.qat.l3b_master = ctx->dense_qat_l3_bias;
+    if (d.qat.dense && (qat_l1w == nullptr || has_l2f || has_l3f))
+        return fail_message("dense QAT requires the L1 QAT weights and unfactorized L2/L3");
+    if (d.qat.dense && validate_f32(ctx, combined, BW, "sfnn combined") != 0) return -1;
     if (set_device(ctx) != 0) return -1;
     if (zero_parameter_gradients) {
         cudaError_t st = cudaMemsetAsync(l0w_gradients->ptr, 0, l0w_gradients->len * sizeof(float), ctx->stream);
@@ -1749,7 +2301,10 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     }
     // The backward reads only the L1 / L2 / L3 weights (and their shared
     // factors); the FT table is not needed, so nothing is folded.
-    const SfnnWeights w{nullptr,  nullptr, l1w->ptr, nullptr, has_l1f ? l1fw->ptr : nullptr, nullptr,
+    // With L1 QAT the input gradient uses the folded, fake-quantised weights
+    // (identity STE; the shared factor still receives alpha * sum).
+    const SfnnWeights w{nullptr,  nullptr, qat_l1w != nullptr ? qat_l1w->ptr : l1w->ptr, nullptr,
+                        (has_l1f && qat_l1w == nullptr) ? l1fw->ptr : nullptr, nullptr,
                         l2w->ptr, nullptr, has_l2f ? l2fw->ptr : nullptr, nullptr,
                         l3w->ptr, nullptr, has_l3f ? l3fw->ptr : nullptr, nullptr};
     SfnnPlan plan{};
@@ -1775,6 +2330,7 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     lb.l0_gradients[1] = nstm_l0_gradients->ptr;
     lb.pre_gradients[0] = stm_l0_pre_gradients->ptr;
     lb.pre_gradients[1] = nstm_l0_pre_gradients->ptr;
+    lb.combined = d.qat.dense ? combined->ptr : nullptr;
     if (launch_l1_backward(ctx, d, plan, lb) != 0) return -1;
     FinalArgs f{};
     for (int k = 0; k < kSfGroups; ++k) f.dst[k] = g.len[k] ? grads[k]->ptr : nullptr;
@@ -1816,7 +2372,7 @@ int bulletou_b200_sfnn_local_gradients_device(
     BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* ft_gradients,
     BulletOuCudaCppF32Buffer* dense_gradients, BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
     BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
-    BulletOuCudaCppF32Buffer* mean) {
+    BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat) {
     if (shape == nullptr || params == nullptr) return fail_message("SFNN shape / parameter array must not be null");
     SfnnDims d{};
     LossArgs la{};
@@ -1842,6 +2398,7 @@ int bulletou_b200_sfnn_local_gradients_device(
         return -1;
     if (set_device(ctx) != 0) return -1;
     const SfnnWeights w = weights_from(params);
+    if (apply_qat(qat, w, &d) != 0) return -1;
     if (sfnn_step(ctx, d, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr, targets->ptr, entry_weights->ptr, la,
                   loss->finalize_loss, nullptr, nullptr, nullptr, nullptr, nullptr, output->ptr, per_sample->ptr,
                   mean_output_gradients->ptr, weighted_sum->ptr, mean->ptr, ft_gradients->ptr,
@@ -1859,7 +2416,7 @@ int bulletou_b200_sfnn_train_step_device(
     BulletOuCudaCppF32Buffer* const* momentum, BulletOuCudaCppF32Buffer* const* velocity,
     BulletOuCudaCppF32Buffer* const* slow_params, BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
     BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
-    BulletOuCudaCppF32Buffer* mean) {
+    BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat) {
     if (shape == nullptr) return fail_message("SFNN shape must not be null");
     if (ranger == nullptr) return fail_message("ranger step must not be null");
     if (params == nullptr || momentum == nullptr || velocity == nullptr || slow_params == nullptr)
@@ -1899,11 +2456,82 @@ int bulletou_b200_sfnn_train_step_device(
         smm[i] = slow_params[i] ? slow_params[i]->ptr : nullptr;
     }
     const SfnnWeights w = weights_from(params);
+    if (apply_qat(qat, w, &d) != 0) return -1;
     if (sfnn_step(ctx, d, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr, targets->ptr, entry_weights->ptr, la,
                   loss->finalize_loss, ranger, wm, mm, vm, smm, output->ptr, per_sample->ptr,
                   mean_output_gradients->ptr, weighted_sum->ptr, mean->ptr, nullptr, nullptr) != 0)
         return -1;
     return ok();
+}
+
+// Fake-quantised copy of one layer's tensor (layer_qat.rs:832-880): scale 127
+// (FT, i16; with vr > 0 the virtual rows are folded into the base rows and
+// zeroed), 64 (dense weights, i8) or 8128 (dense biases, i32).
+int bulletou_layer_qat(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* src, BulletOuCudaCppF32Buffer* dst,
+                       float scale, float lo, float hi, size_t base, size_t vr, size_t width, float alpha) {
+    (void)lo;
+    (void)hi;
+    if (ctx == nullptr || src == nullptr || dst == nullptr) return fail_message("layer QAT arguments must not be null");
+    if (validate_f32(ctx, src, src->len, "layer QAT input") != 0 ||
+        validate_f32(ctx, dst, src->len, "layer QAT output") != 0 || set_device(ctx) != 0)
+        return -1;
+    if (src->len == 0) return ok();
+    int blocks = 0;
+    if (grid_1d(src->len, 256, &blocks, "layer QAT") != 0) return -1;
+    if (vr != 0) {
+        if (width == 0 || src->len != (base + vr) * width) return fail_message("invalid layer QAT FT layout");
+        layer_qat_ft_kernel<<<blocks, 256, 0, ctx->stream>>>(src->ptr, dst->ptr, base, vr, width, alpha, src->len);
+    } else if (scale == 127.0f) {
+        qat_vector_kernel<<<blocks, 256, 0, ctx->stream>>>(src->ptr, dst->ptr, src->len, 0);
+    } else if (scale == 64.0f) {
+        qat_vector_kernel<<<blocks, 256, 0, ctx->stream>>>(src->ptr, dst->ptr, src->len, 1);
+    } else if (scale == 8128.0f) {
+        qat_vector_kernel<<<blocks, 256, 0, ctx->stream>>>(src->ptr, dst->ptr, src->len, 2);
+    } else {
+        return fail_message("unsupported layer QAT scale");
+    }
+    if (check_launch("layer QAT launch") != 0) return -1;
+    return ok();
+}
+
+// flag[0] = 1 when any element of w or b is nonzero (the FT QAT zero check).
+int bulletou_layer_qat_nonzero(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w, BulletOuCudaCppF32Buffer* b,
+                               BulletOuCudaCppF32Buffer* flag) {
+    if (ctx == nullptr || w == nullptr || b == nullptr || flag == nullptr)
+        return fail_message("FT QAT zero check arguments must not be null");
+    if (validate_f32(ctx, w, w->len, "FT QAT weights") != 0 || validate_f32(ctx, b, b->len, "FT QAT bias") != 0 ||
+        validate_f32(ctx, flag, 1, "FT QAT flag") != 0 || set_device(ctx) != 0)
+        return -1;
+    int blocks = 0;
+    if (grid_1d(w->len + b->len, 256, &blocks, "FT QAT zero check") != 0) return -1;
+    if (blocks > 0) nonzero_kernel<<<blocks, 256, 0, ctx->stream>>>(w->ptr, w->len, b->ptr, b->len, flag->ptr);
+    if (check_launch("FT QAT zero check launch") != 0) return -1;
+    return ok();
+}
+
+// Enters dense QAT: the SFNN forward / backward entries of this context run the
+// integer L1 / L2 / L3 with these master biases until bulletou_dense_qat_end.
+int bulletou_dense_qat_begin(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* l2_bias,
+                             BulletOuCudaCppF32Buffer* l3_bias, size_t batch, size_t l1_out, size_t l2_size,
+                             size_t stacks, int integer_ft) {
+    if (ctx == nullptr || batch == 0 || l1_out == 0 || l2_size == 0 || stacks == 0)
+        return fail_message("invalid dense QAT dimensions");
+    if (validate_f32(ctx, l2_bias, stacks * l2_size, "dense QAT master L2 bias") != 0 ||
+        validate_f32(ctx, l3_bias, stacks, "dense QAT master L3 bias") != 0 || set_device(ctx) != 0)
+        return -1;
+    ctx->dense_qat_l2_bias = l2_bias->ptr;
+    ctx->dense_qat_l3_bias = l3_bias->ptr;
+    ctx->dense_qat = true;
+    ctx->dense_qat_integer_ft = integer_ft != 0;
+    return ok();
+}
+
+void bulletou_dense_qat_end(BulletOuCudaCppContext* ctx) {
+    if (ctx == nullptr) return;
+    ctx->dense_qat = false;
+    ctx->dense_qat_integer_ft = false;
+    ctx->dense_qat_l2_bias = nullptr;
+    ctx->dense_qat_l3_bias = nullptr;
 }
 
 }  // extern "C"

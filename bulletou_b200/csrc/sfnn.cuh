@@ -26,6 +26,28 @@ constexpr int kSfnnMaxL2 = 64;
 constexpr int kSfnnMaxStacks = 127;        // bucket sort keys (stacks + "invalid bucket")
 constexpr int kSfnnTile = 128;             // samples per bucket tile
 
+// Quantisation-aware training (the reference runner's qat_l1 / qat_ft /
+// qat_l2 / qat_l3, lib.rs:6332-6336; layer_qat.rs; cu:5993-6400, 9294-9470).
+//   l1     L1 weights / bias folded with the shared factor, then fake-quantised
+//          (i8 at 64, i32 at 8128); backward input gradients use them.
+//   ft     fused step: FT rows folded with their virtual row, then fake-quantised
+//          (i16 at 127); FT bias too.
+//   l2/l3  fused step: L2 / L3 weights (64) and biases (8128) fake-quantised.
+//   dense  l1 && l2 && l3: integer L1 / L2 / L3 on the 1/127 lattice with the
+//          master L2 / L3 biases rounded to 8128, continuous activation STEs.
+//   integer_ft  dense with FT QAT: combined from the engine's integer FT.
+// Every gradient reaches the f32 masters through an identity STE.
+struct SfnnQat {
+    int l1;
+    int ft;
+    int l2;
+    int l3;
+    int dense;
+    int integer_ft;
+    const float* l2b_master;  // dense: master biases of the integer L2 / L3
+    const float* l3b_master;
+};
+
 struct SfnnDims {
     int input_size;   // l0w rows (virtual rows included when factorized)
     int base;         // factorized: first virtual row (73305 / 131949); 0 otherwise
@@ -44,6 +66,7 @@ struct SfnnDims {
     int has_l1f;
     int has_l2f;
     int has_l3f;
+    SfnnQat qat;
 };
 
 // Factorized FT layout: input_size == base + 1629 for the two HalfKA bases

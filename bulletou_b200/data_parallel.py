@@ -125,12 +125,13 @@ class B200Backend:
         arr = ctypes.c_void_p * 14
         params = arr(*[(None if w is None else w.as_ptr().value) for w in tr.weight_list()])
         lw = tr.loss_workspace
+        qat = tr.lr_multipliers.as_struct()
         self.lib.call("bulletou_b200_sfnn_local_gradients_device", self.ctx.as_ptr(), ctypes.byref(shape),
                       tr.batch_size, tr.max_active, tr.stm_indices.as_ptr(), tr.nstm_indices.as_ptr(),
                       tr.buckets.as_ptr(), tr.targets.as_ptr(), tr.entry_weights.as_ptr(), ctypes.byref(loss_spec),
                       params, tr.ft_grad.as_ptr(), tr.dense_grad.as_ptr(), tr.output.as_ptr(),
                       lw.per_sample.as_ptr(), lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(),
-                      lw.mean.as_ptr())
+                      lw.mean.as_ptr(), ctypes.byref(qat))
 
     def ranger(self, params: RangerUpdateParams, grad, weights, m, v, slow) -> None:
         ranger_update_device(self.ctx, params, RangerDeviceState(grad, weights, m, v, slow))
@@ -233,10 +234,12 @@ def sfnn_dense_gradient_layout(shape, present: dict) -> list[tuple[str, int, int
 class SfnnDataParallelTrainer:
     """One rank of data-parallel SFNN training (default layer multipliers)."""
 
-    def __init__(self, backend, dist, initial_weights, batch_size: int, max_active: int, alpha=None):
-        from .sfnn import SFNN_WEIGHT_NAMES, SfnnFactorizerAlpha
+    def __init__(self, backend, dist, initial_weights, batch_size: int, max_active: int, alpha=None,
+                 lr_multipliers=None):
+        from .sfnn import SFNN_WEIGHT_NAMES, SfnnFactorizerAlpha, SfnnLayerLrMultipliers
 
         initial_weights.validate()
+        self.lr_multipliers = lr_multipliers or SfnnLayerLrMultipliers()
         self.backend = backend
         self.dist = dist
         self.world = dist.get_world_size()

@@ -20,7 +20,7 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import CudaCppError, QuantRounding, SfnnShape
+from ._lib import CudaCppError, QuantRounding, SfnnQat, SfnnShape
 from .cuda_cpp import (FLT_MAX, Context, Event, F32Buffer, I32Buffer, PinnedF32Buffer, PinnedI32Buffer,
                        RangerDeviceState, RangerParamState, RangerUpdateParams, ScalarLossKind, ScalarLossReadback,
                        ScalarLossWorkspace, ranger_update_device, scalar_loss_device)
@@ -208,8 +208,11 @@ def _p(b: Optional[F32Buffer]):
 def sfnn_forward_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int, stm: I32Buffer,
                         nstm: I32Buffer, buckets: I32Buffer, weights: dict, ws: SfnnForwardWorkspace,
                         alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
-                        folded_l0w: Optional[F32Buffer] = None) -> None:
-    """bulletou_cuda_cpp_sfnn_forward_device (lib.rs:2033-2253 argument order)."""
+                        folded_l0w: Optional[F32Buffer] = None, qat_l1: Optional["SfnnL1Qat"] = None,
+                        refresh_qat_l1: int = 1) -> None:
+    """bulletou_cuda_cpp_sfnn_forward_device (lib.rs:2033-2253 argument order).
+    qat_l1: the L1 QAT scratch (weights, bias); refresh_qat_l1 as in the
+    reference (1 rebuild quantised, 0 reuse)."""
     w = weights
     has = [int(w[n] is not None) for n in ("l1fw", "l2fw", "l3fw")]
     ctx.lib.call(
@@ -220,7 +223,8 @@ def sfnn_forward_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, 
         _p(w["l2fb"]), has[1], None, None, 0, _p(w["l3w"]), _p(w["l3b"]), _p(w["l3fw"]), _p(w["l3fb"]), has[2], None,
         None, 0, 0, 0, 0, 0, 0, 0, alpha.ft, alpha.shared, 1.0, 1.0, 1.0, 1.0, None, None, ws.stm_l0.as_ptr(),
         ws.nstm_l0.as_ptr(), ws.combined.as_ptr(), ws.l1.as_ptr(), ws.l2_input.as_ptr(), ws.l2.as_ptr(),
-        ws.output.as_ptr(), None, None, 0)
+        ws.output.as_ptr(), None if qat_l1 is None else qat_l1.weights.as_ptr(),
+        None if qat_l1 is None else qat_l1.bias.as_ptr(), 0 if qat_l1 is None else int(refresh_qat_l1))
 
 
 def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int,
@@ -228,15 +232,18 @@ def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size
                                fws: SfnnForwardWorkspace, mean_output_gradients: F32Buffer,
                                bws: SfnnBackwardWorkspace, alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
                                zero_parameter_gradients: bool = False,
-                               entry_weights: Optional[F32Buffer] = None) -> None:
-    """bulletou_cuda_cpp_sfnn_backward_train_device (lib.rs:3529-4090 argument order)."""
+                               entry_weights: Optional[F32Buffer] = None,
+                               qat_l1_weights: Optional[F32Buffer] = None) -> None:
+    """bulletou_cuda_cpp_sfnn_backward_train_device (lib.rs:3529-4090 argument order);
+    qat_l1_weights: the forward's L1 QAT weights (input gradients use them)."""
     w, g, ax = weights, bws.params, bws.axis
     has = [int(w[n] is not None) for n in ("l1fw", "l2fw", "l3fw")]
     ctx.lib.call(
         "bulletou_cuda_cpp_sfnn_backward_train_device", ctx.as_ptr(), shape.input_size, shape.ft_size,
         shape.l1_hidden, int(shape.l1_skip), shape.l2_size, shape.num_stacks, 1, 0, 0, 0, 0, batch_size, max_active,
         stm.as_ptr(), nstm.as_ptr(), buckets.as_ptr(), fws.stm_l0.as_ptr(), fws.nstm_l0.as_ptr(),
-        fws.combined.as_ptr(), fws.l1.as_ptr(), fws.l2_input.as_ptr(), fws.l2.as_ptr(), _p(w["l1w"]), None,
+        fws.combined.as_ptr(), fws.l1.as_ptr(), fws.l2_input.as_ptr(), fws.l2.as_ptr(), _p(w["l1w"]),
+        _p(qat_l1_weights),
         _p(w["l1fw"]), has[0], None, 0, _p(w["l2w"]), _p(w["l2fw"]), has[1], None, 0, _p(w["l3w"]), _p(w["l3fw"]),
         has[2], None, 0, 0, 0, 0, 0, 0, 0, alpha.ft, alpha.shared, 1.0, 1.0, 1.0, 1.0, None, None,
         mean_output_gradients.as_ptr(), *[getattr(bws, k).as_ptr() for k in bws.INTERMEDIATE], _p(g["l0w"]),
@@ -244,6 +251,77 @@ def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size
         _p(g["l2w"]), _p(g["l2b"]), _p(g["l2fw"]), _p(g["l2fb"]), _p(ax["l2axw"]), _p(ax["l2axb"]), _p(g["l3w"]),
         _p(g["l3b"]), _p(g["l3fw"]), _p(g["l3fb"]), _p(ax["l3axw"]), _p(ax["l3axb"]), int(zero_parameter_gradients),
         _p(entry_weights))
+
+
+@dataclass(frozen=True)
+class SfnnLayerLrMultipliers:
+    """The QAT switches of the runner's layer multipliers (lib.rs:6320-6370);
+    the learning-rate multipliers themselves stay at their defaults here."""
+
+    qat_l1: bool = False
+    qat_ft: bool = False
+    qat_l2: bool = False
+    qat_l3: bool = False
+
+    @property
+    def layer_qat(self) -> bool:
+        return self.qat_ft or self.qat_l2 or self.qat_l3
+
+    @property
+    def dense_qat(self) -> bool:
+        return self.qat_l1 and self.qat_l2 and self.qat_l3
+
+    def as_struct(self) -> SfnnQat:
+        return SfnnQat(int(self.qat_l1), int(self.qat_ft), int(self.qat_l2), int(self.qat_l3))
+
+
+class SfnnL1Qat:
+    """Training-only fake-quantised L1 scratch (SfnnL1Qat, lib.rs:1946-1995)."""
+
+    def __init__(self, ctx: Context, shape: SfnnForwardShape):
+        self.weights = F32Buffer(ctx, shape.num_stacks * shape.l1_out * shape.ft_size)
+        self.bias = F32Buffer(ctx, shape.num_stacks * shape.l1_out)
+
+
+class SfnnLayerQatCopies:
+    """Fake-quantised copies of the FT / L2 / L3 tensors a layer-QAT step swaps
+    in for its forward and backward (layer_qat.rs:5-11, 832-923)."""
+
+    def __init__(self):
+        self.copies = {}
+        self.checked_ft = False
+
+    def prepare(self, ctx: Context, runner: "SfnnTrainStepRunner", lr: SfnnLayerLrMultipliers) -> dict:
+        lib = ctx.lib
+        base = runner.shape.factorized_base()
+        vr = PIECE_INPUTS if base else 0
+        swaps = {}
+        for on, w_name, b_name, ft in ((lr.qat_ft, "l0w", "l0b", True), (lr.qat_l2, "l2w", "l2b", False),
+                                       (lr.qat_l3, "l3w", "l3b", False)):
+            if not on:
+                continue
+            for name, is_bias in ((w_name, False), (b_name, True)):
+                src = runner.weights[name]
+                dst = self.copies.get(name)
+                if dst is None or dst.length != src.length:
+                    dst = F32Buffer(ctx, src.length)
+                    self.copies[name] = dst
+                scale = 127.0 if ft else (8128.0 if is_bias else 64.0)
+                lo, hi = ((-32768.0, 32767.0) if ft else ((-2147483648.0, 2147483647.0) if is_bias else (-128.0, 127.0)))
+                rows = vr if (ft and not is_bias) else 0
+                lib.call("bulletou_layer_qat", ctx.as_ptr(), src.as_ptr(), dst.as_ptr(), scale, lo, hi,
+                         base if rows else 0, rows, runner.shape.ft_size if rows else 0, runner.alpha.ft)
+                swaps[name] = dst
+        if lr.qat_ft and not self.checked_ft:
+            # One readback when FT QAT switches on (layer_qat.rs:968-972).
+            flag = F32Buffer.from_host(ctx, np.zeros(1, np.float32))
+            lib.call("bulletou_layer_qat_nonzero", ctx.as_ptr(), swaps["l0w"].as_ptr(), swaps["l0b"].as_ptr(),
+                     flag.as_ptr())
+            if flag.download(ctx)[0] == 0.0:
+                raise CudaCppError("FT QAT rounded every effective FT weight and bias to zero (scale=127); "
+                                   "pairwise FT gradients vanish")
+            self.checked_ft = True
+        return swaps
 
 
 def factor_contribution_clip(params: RangerUpdateParams, alpha: float) -> RangerUpdateParams:
@@ -312,7 +390,8 @@ class SfnnTrainStepRunner:
     """SFNN train-step runner (lib.rs:6187-7960), default layer multipliers."""
 
     def __init__(self, ctx: Context, initial_weights: SfnnForwardHostWeights, batch_size: int, max_active: int,
-                 factorizer_alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(), fused: Optional[bool] = None):
+                 factorizer_alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(), fused: Optional[bool] = None,
+                 lr_multipliers: SfnnLayerLrMultipliers = SfnnLayerLrMultipliers()):
         initial_weights.validate()
         factorizer_alpha.validate()
         if batch_size == 0 or max_active == 0:
@@ -340,6 +419,9 @@ class SfnnTrainStepRunner:
         self._handles_cache = None
         self._slots = None
         self._next_slot = 0
+        self.lr_multipliers = lr_multipliers
+        self.qat_l1 = None
+        self.layer_qat = SfnnLayerQatCopies()
 
     def _reference_workspaces(self, ctx: Context) -> None:
         self.forward_workspace = SfnnForwardWorkspace(ctx, self.shape, self.batch_size)
@@ -394,33 +476,57 @@ class SfnnTrainStepRunner:
         # (clip_params, lib.rs:6416-6420).
         params = replace(params, norm_loss_strength=0.0, norm_loss_before=False)
         lw = self.loss_workspace
+        lr = self.lr_multipliers
+        if (lr.qat_l2 and self.present["l2fw"]) or (lr.qat_l3 and self.present["l3fw"]):
+            raise CudaCppError("Layer QAT does not support legacy L2/L3 factorizer tensors; fold them first")
         if self.fused and params.sgd_momentum is None:
             sh = self.shape
             shape = SfnnShape(sh.input_size, sh.ft_size, sh.l1_hidden, int(sh.l1_skip), sh.l2_size, sh.num_stacks,
                               self.alpha.ft, self.alpha.shared)
             spec = loss_kind.spec(output_inv_scale, finalize_loss)
             step = params.ffi_step()
+            qat = lr.as_struct()
             w, m, v, s = self._handles()
             self.lib.call("bulletou_b200_sfnn_train_step_device", ctx.as_ptr(), ctypes.byref(shape), self.batch_size,
                           self.max_active, self.stm_indices.as_ptr(), self.nstm_indices.as_ptr(),
                           self.buckets.as_ptr(), self.targets.as_ptr(), self.entry_weights.as_ptr(),
                           ctypes.byref(spec), ctypes.byref(step), w, m, v, s, self.output.as_ptr(),
                           lw.per_sample.as_ptr(), lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(),
-                          lw.mean.as_ptr())
+                          lw.mean.as_ptr(), ctypes.byref(qat))
             return
         if self.forward_workspace is None:
             self._reference_workspaces(ctx)
         fws, bws = self.forward_workspace, self.backward_workspace
-        fold = bws.params["l0w"] if self.shape.factorized_base() else None
-        sfnn_forward_device(ctx, self.shape, self.batch_size, self.max_active, self.stm_indices, self.nstm_indices,
-                            self.buckets, self.weights, fws, self.alpha, fold)
-        if fold is not None:
-            fold.fill(0.0, ctx)  # lib.rs:2078-2084: discard the folded weights before backward adds
-        scalar_loss_device(ctx, loss_kind, output_inv_scale, self.batch_size, fws.output, self.targets,
-                           self.entry_weights, lw, finalize_loss)
-        sfnn_backward_train_device(ctx, self.shape, self.batch_size, self.max_active, self.stm_indices,
-                                   self.nstm_indices, self.buckets, self.weights, fws, lw.mean_output_gradients, bws,
-                                   self.alpha, False, self.entry_weights)
+        # L1 QAT scratch (prepare_l1_qat, lib.rs:6525-6550); every step follows
+        # an update, so the fake-quantised L1 is rebuilt each step.
+        if lr.qat_l1 and self.qat_l1 is None:
+            self.qat_l1 = SfnnL1Qat(ctx, self.shape)
+        qat_l1 = self.qat_l1 if lr.qat_l1 else None
+        # Layer QAT (layer_qat::step, layer_qat.rs:925-1004): fake-quantised
+        # copies stand in for the masters through forward and backward.
+        swaps = self.layer_qat.prepare(ctx, self, lr) if lr.layer_qat else {}
+        used = dict(self.weights)
+        used.update(swaps)
+        dense = lr.dense_qat
+        if dense:
+            self.lib.call("bulletou_dense_qat_begin", ctx.as_ptr(), self.weights["l2b"].as_ptr(),
+                          self.weights["l3b"].as_ptr(), self.batch_size, self.shape.l1_out, self.shape.l2_size,
+                          self.shape.num_stacks, int(lr.qat_ft))
+        try:
+            fold = bws.params["l0w"] if self.shape.factorized_base() else None
+            sfnn_forward_device(ctx, self.shape, self.batch_size, self.max_active, self.stm_indices,
+                                self.nstm_indices, self.buckets, used, fws, self.alpha, fold, qat_l1, 1)
+            if fold is not None:
+                fold.fill(0.0, ctx)  # lib.rs:2078-2084: discard the folded weights before backward adds
+            scalar_loss_device(ctx, loss_kind, output_inv_scale, self.batch_size, fws.output, self.targets,
+                               self.entry_weights, lw, finalize_loss)
+            sfnn_backward_train_device(ctx, self.shape, self.batch_size, self.max_active, self.stm_indices,
+                                       self.nstm_indices, self.buckets, used, fws, lw.mean_output_gradients, bws,
+                                       self.alpha, False, self.entry_weights,
+                                       None if qat_l1 is None else qat_l1.weights)
+        finally:
+            if dense:
+                self.lib.call("bulletou_dense_qat_end", ctx.as_ptr())
         for n in SFNN_WEIGHT_NAMES:
             if self.weights[n] is None:
                 continue

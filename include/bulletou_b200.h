@@ -205,6 +205,27 @@ typedef struct BulletOuB200SfnnShape {
     float factorizer_shared_alpha;
 } BulletOuB200SfnnShape;
 
+/* Quantisation-aware training switches of the SFNN runner
+ * (SfnnLayerLrMultipliers::qat_l1 / qat_ft / qat_l2 / qat_l3, lib.rs:6332-6336):
+ *   l1  L1 weights folded with the shared factor then fake-quantised to i8 at
+ *       64, bias to i32 at 127*64; backward input gradients use them
+ *       (cu:11514-11590; the runner's prepare_l1_qat, lib.rs:6525-6550);
+ *   ft  FT rows folded with their virtual row then fake-quantised to i16 at
+ *       127, FT bias too (layer_qat.rs:832-880);
+ *   l2, l3  L2 / L3 weights fake-quantised at 64, biases at 127*64; no L2/L3
+ *       shared factors allowed (layer_qat.rs:937-943).
+ * l1 && l2 && l3 selects the dense integer QAT (layer_qat.rs:977-991;
+ * cu:6654-6712, 6322, 3709-3770): FT output floored to the 1/127 lattice, or
+ * the engine's integer FT when ft is set; integer L1 / L2 / L3 with the master
+ * L2 / L3 biases rounded to 127*64; continuous activation STEs.  Gradients
+ * reach the f32 masters through an identity STE. */
+typedef struct BulletOuB200SfnnQat {
+    int l1;
+    int ft;
+    int l2;
+    int l3;
+} BulletOuB200SfnnQat;
+
 /* One complete SFNN train step.  Replaces
  * SfnnTrainStepRunner::step_no_readback_with_loss_finalize (lib.rs:7448-7533)
  * with default layer multipliers: sfnn_forward_device (cu:11329) -> scalar
@@ -216,7 +237,8 @@ typedef struct BulletOuB200SfnnShape {
  * is absent.  The FT gradient is never materialised: each FT row (and each
  * virtual factor row) is updated by the pass that sums its gradient.
  * ranger->norm_loss_rate must be 0 (with default multipliers the SFNN runner
- * applies no norm loss, lib.rs:6416-6420). */
+ * applies no norm loss, lib.rs:6416-6420).  qat: the QAT switches, or null
+ * for none. */
 int bulletou_b200_sfnn_train_step_device(
     BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
     const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
@@ -226,7 +248,7 @@ int bulletou_b200_sfnn_train_step_device(
     BulletOuCudaCppF32Buffer* const* momentum, BulletOuCudaCppF32Buffer* const* velocity,
     BulletOuCudaCppF32Buffer* const* slow_params, BulletOuCudaCppF32Buffer* output,
     BulletOuCudaCppF32Buffer* per_sample, BulletOuCudaCppF32Buffer* mean_output_gradients,
-    BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean);
+    BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat);
 
 /* Length of the packed SFNN small-parameter gradient (groups l0b l1w l1b
  * [l1fw l1fb] l2w l2b [l2fw l2fb] l3w l3b [l3fw l3fb], absent shared factors
@@ -249,7 +271,7 @@ int bulletou_b200_sfnn_local_gradients_device(
     BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* ft_gradients,
     BulletOuCudaCppF32Buffer* dense_gradients, BulletOuCudaCppF32Buffer* output,
     BulletOuCudaCppF32Buffer* per_sample, BulletOuCudaCppF32Buffer* mean_output_gradients,
-    BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean);
+    BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat);
 
 /* ---------------------------------------------------------------- quantised SFNN
  * The reference evaluates a trained SFNN through the engine's integer network

@@ -285,6 +285,25 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     BulletOuCudaCppF32Buffer* l3axb_gradients, int zero_parameter_gradients,
     BulletOuCudaCppF32Buffer* entry_weights);                                            /* cu:12882 */
 
+/* ---- SFNN quantisation-aware training (cu:9294-9470; driver layer_qat.rs) ----
+ * bulletou_layer_qat: dst = fake-quantised src.  scale 127 (FT weights or
+ * bias, i16 bounds; with vr > 0 the FT rows are folded with virtual row
+ * base + f % vr as src[f] + alpha * src[virtual] and the virtual rows zeroed),
+ * 64 (dense weights, i8) or 8128 (dense biases, i32); lo / hi are implied by
+ * the scale.  bulletou_layer_qat_nonzero sets flag[0] = 1 when any element of
+ * w or b is nonzero.  bulletou_dense_qat_begin / _end bracket a dense-QAT
+ * forward + backward: the SFNN entries of the context then run integer
+ * L1 / L2 / L3 with the given master L2 / L3 biases (and the engine's integer
+ * FT when integer_ft), using the L1 QAT scratch of the forward entry. */
+int bulletou_layer_qat(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* src, BulletOuCudaCppF32Buffer* dst,
+    float scale, float lo, float hi, size_t base, size_t vr, size_t width, float alpha);             /* cu:9441 */
+int bulletou_layer_qat_nonzero(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* flag);                                     /* cu:9462 */
+int bulletou_dense_qat_begin(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* l2_bias,
+    BulletOuCudaCppF32Buffer* l3_bias, size_t batch, size_t l1_out, size_t l2_size, size_t stacks,
+    int integer_ft);                                                                                  /* cu:9356 */
+void bulletou_dense_qat_end(BulletOuCudaCppContext* ctx);                                             /* cu:9375 */
+
 #ifdef __cplusplus
 }
 #endif

@@ -68,10 +68,13 @@ class CpuOracleBackend:
         w = {n: (None if b is None else b.numpy()) for n, b in tr.weights.items()}
         w["l0w"] = w["l0w"][: sh.input_size * sh.ft_size]
         args = (sh.as_tuple(), tr.stm, tr.nstm, tr.buckets, tr.batch_size, tr.max_active)
-        fwd = oracle.sfnn_forward(*args, w, tr.alpha.ft, tr.alpha.shared)
+        lr = tr.lr_multipliers
+        qat = oracle.qat_mask(lr.qat_l1, lr.qat_ft, lr.qat_l2, lr.qat_l3)
+        fwd = oracle.sfnn_forward(*args, w, tr.alpha.ft, tr.alpha.shared, qat=qat)
         loss = oracle.scalar_loss(spec.kind, spec.output_inv_scale, spec.loss_pow_exp, spec.loss_param,
                                   fwd["output"], tr.targets, tr.entry_weights, normalizer=spec.normalizer)
-        g = oracle.sfnn_backward(*args, fwd, w, loss["mean_output_gradients"], tr.alpha.ft, tr.alpha.shared)
+        g = oracle.sfnn_backward(*args, fwd, w, loss["mean_output_gradients"], tr.alpha.ft, tr.alpha.shared,
+                                 qat=qat)
         tr.ft_grad.zero_()
         tr.ft_grad[: sh.input_size * sh.ft_size] = torch.from_numpy(g["l0w_gradients"])
         for (name, off, n) in tr.dense_layout:
