@@ -68,6 +68,38 @@ SFNN_PHASES = ("fold", "sorts_tiles", "inverse_index", "ft_forward", "l1_head", 
 # fold 1, king sort 3, bucket sort 3, tile table 1, L1 weights 1, index 5 + row sort 1, FT forward 1,
 # L1 forward 1, head 1, L1 backward 1, finalize 1, Ranger on 9 small groups, FT rows 45 kings / 3 per launch
 SFNN_LAUNCHES_PER_STEP = 1 + 3 + 3 + 1 + 1 + 6 + 1 + 1 + 1 + 1 + 1 + 9 + 15
+# QAT modes (the runner's qat_l1 / qat_ft / qat_l2 / qat_l3).  configs[2] trains
+# "with QAT fake-quant": the default quantises every layer (FT, L1, L2, L3),
+# which selects the dense integer QAT with the engine's integer FT.
+SFNN_QAT_MODES = {
+    "none": (False, False, False, False),
+    "l1": (True, False, False, False),
+    "layers": (True, True, True, False),
+    "dense": (True, False, True, True),
+    "all": (True, True, True, True),
+}
+SFNN_QAT_LABELS = {
+    "none": "none (f32)",
+    "l1": "L1 fake-quant (fold then i8 / i32 rounding, identity STE)",
+    "layers": "FT + L1 + L2 fake-quant (identity STE, f32 activations)",
+    "dense": "L1 + L2 + L3: dense integer QAT on the 1/127 FT lattice, continuous STEs",
+    "all": "FT + L1 + L2 + L3: dense integer QAT with the engine's integer FT, continuous STEs",
+}
+
+
+def sfnn_lr_multipliers(mode):
+    from bulletou_b200 import sfnn as bs
+
+    l1, ft, l2, l3 = SFNN_QAT_MODES[mode]
+    return bs.SfnnLayerLrMultipliers(qat_l1=l1, qat_ft=ft, qat_l2=l2, qat_l3=l3)
+
+
+def sfnn_launches_per_step(mode):
+    """Kernels of one fused step: the QAT extras are the L1 bias fold (L1 QAT),
+    the FT bias rounding (FT QAT), and the integer FT (dense + FT QAT; its i16
+    table is written by the fold)."""
+    l1, ft, l2, l3 = SFNN_QAT_MODES[mode]
+    return SFNN_LAUNCHES_PER_STEP + int(l1) + int(ft) + (1 if (ft and l1 and l2 and l3) else 0)
 
 
 def parse_args():
@@ -78,6 +110,8 @@ def parse_args():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--workload", choices=("sfnn", "halfkp"), default="sfnn")
     ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--qat", choices=tuple(SFNN_QAT_MODES), default="all",
+                    help="SFNN quantisation-aware training mode (both arms)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -439,28 +473,32 @@ def bind_sfnn(runner, dev):
 
 
 def sfnn_cpu_baseline(batch_cap=256, budget_s=8.0):
-    """CPU oracle SFNN forward (C restatement of the reference's CPU
-    evaluation path, fast_sfnn.rs:325-386), one thread, bounded sample."""
+    """The reference's CPU evaluation path for SFNN -- the engine's integer
+    forward over the exported quantised network (examples/bulletou.rs:
+    8001-8163, rayon over positions there) -- as the C oracle's restatement,
+    one thread, on a bounded sample."""
     from bulletou_b200 import synthetic
     from oracle import oracle
 
     sh = sfnn_shape()
     w = synthetic.sfnn_weights(synthetic.rng_for(7))
+    q = oracle.sfnn_quantize(sh.as_tuple(), w)
     b = synthetic.sfnn_batch(4242, batch_cap)
     args = (sh.as_tuple(), b["stm"], b["nstm"], b["buckets"])
-    oracle.sfnn_forward(sh.as_tuple(), b["stm"][:SFNN_ACTIVE * 8], b["nstm"][:SFNN_ACTIVE * 8], b["buckets"][:8], 8,
-                        SFNN_ACTIVE, w)  # warm
+    oracle.sfnn_integer_forward(sh.as_tuple(), b["stm"][:SFNN_ACTIVE * 8], b["nstm"][:SFNN_ACTIVE * 8],
+                                b["buckets"][:8], 8, SFNN_ACTIVE, q)  # warm
     t0 = time.perf_counter()
     reps = 0
     while True:
-        oracle.sfnn_forward(*args, batch_cap, SFNN_ACTIVE, w)
+        oracle.sfnn_integer_forward(*args, batch_cap, SFNN_ACTIVE, q)
         reps += 1
         if time.perf_counter() - t0 >= budget_s:
             break
     dt = time.perf_counter() - t0
-    return {"value": reps * batch_cap / dt, "unit": "positions/s (forward only)", "cores": 1, "kind": "port",
-            "sample": f"oracle SFNN 1536 forward, {reps} x {batch_cap} positions in {dt:.1f} s "
-                      f"(the reference cannot train on CPU; its CPU path is evaluation only)"}
+    return {"value": reps * batch_cap / dt, "unit": "positions/s (integer forward evaluation only)", "cores": 1,
+            "kind": "port",
+            "sample": f"oracle quantised SFNN 1536 integer forward (the reference's CPU evaluator), {reps} x "
+                      f"{batch_cap} positions in {dt:.1f} s; the reference cannot train on CPU"}
 
 
 def _profile(lib, ctx, marks):
@@ -480,7 +518,8 @@ def run_sfnn_b200(args, rank, world, local, dist):
     if world > 1:
         return run_sfnn_data_parallel(args, rank, world, local, dist)
     ctx = bo.Context(local)
-    runner = bs.SfnnTrainStepRunner(ctx, sfnn_host_weights(), args.batch, SFNN_ACTIVE, fused=True)
+    runner = bs.SfnnTrainStepRunner(ctx, sfnn_host_weights(), args.batch, SFNN_ACTIVE, fused=True,
+                                    lr_multipliers=sfnn_lr_multipliers(args.qat))
     batches = make_sfnn_batches(args.batch, rank)
     devb = sfnn_device_batches(ctx, batches)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
@@ -541,7 +580,7 @@ def run_sfnn_b200(args, rank, world, local, dist):
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
                 "path": "SfnnTrainStepRunner.step_pipelined_no_readback_with_loss_finalize (2 upload slots, "
                         "second stream), inputs in pinned host memory, mean loss copied D2H every step"},
-        "gpu_launches": SFNN_LAUNCHES_PER_STEP * args.steps,
+        "gpu_launches": sfnn_launches_per_step(args.qat) * args.steps,
         "final_loss": losses[-1],
     }
 
@@ -556,7 +595,8 @@ def run_sfnn_data_parallel(args, rank, world, local, dist):
 
     backend = B200Backend(local)
     ctx, lib = backend.ctx, backend.lib
-    tr = SfnnDataParallelTrainer(backend, dist, sfnn_host_weights(), args.batch, SFNN_ACTIVE)
+    tr = SfnnDataParallelTrainer(backend, dist, sfnn_host_weights(), args.batch, SFNN_ACTIVE,
+                                 lr_multipliers=sfnn_lr_multipliers(args.qat))
     batches = make_sfnn_batches(args.batch, rank)
     devb = sfnn_device_batches(ctx, batches)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
@@ -627,7 +667,7 @@ def run_sfnn_data_parallel(args, rank, world, local, dist):
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
                     "path": "SfnnDataParallelTrainer.step_device per rank (NCCL reduce-scatter / all-reduce / "
                             "all-gather), inputs from pinned host memory, mean loss copied D2H every step"},
-            "gpu_launches": (SFNN_LAUNCHES_PER_STEP + 1) * args.steps,
+            "gpu_launches": (sfnn_launches_per_step(args.qat) + 1) * args.steps,
             "final_loss": losses[-1]}
 
 
@@ -637,7 +677,8 @@ def run_sfnn_reference(args, local):
 
     lib = bo.reference_library()
     ctx = bo.Context(local, lib)
-    runner = bs.SfnnTrainStepRunner(ctx, sfnn_host_weights(), args.batch, SFNN_ACTIVE, fused=False)
+    runner = bs.SfnnTrainStepRunner(ctx, sfnn_host_weights(), args.batch, SFNN_ACTIVE, fused=False,
+                                    lr_multipliers=sfnn_lr_multipliers(args.qat))
     batches = make_sfnn_batches(args.batch)
     devb = sfnn_device_batches(ctx, batches)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
@@ -686,7 +727,7 @@ def run_sfnn_reference(args, local):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": e2e_steps}}
 
 
-def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0):
+def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0, qat="none"):
     """Algorithmic bytes per launch of each SFNN phase (the per-position
     formulas of the hot-path table; gathers counted at their logical size, so
     a fraction above 1 means L2 serves the repeated rows)."""
@@ -710,6 +751,13 @@ def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0
         "sorts_tiles": 4 * (half_positions * A + 4 * half_positions + 3 * batch),
         "small_grads_ranger": 0.0,
     }
+    l1, ft, l2, l3 = SFNN_QAT_MODES[qat]
+    if ft and l1 and l2 and l3:
+        # the fold also writes the i16 table; the integer FT gathers it and rewrites combined
+        algo["fold"] += base * W * 2
+        algo["ft_forward"] += half_positions * A * W * 2 + batch * W * 4
+    if l1 and l2 and l3:
+        algo["l1_backward"] += batch * W * 4  # the lattice FT output read for dL1w
     dom = max(phase_ms, key=phase_ms.get)
     t = phase_ms[dom] / 1000.0
     achieved = algo.get(dom, 0.0) / t / 1e9 if t > 0 else 0.0
@@ -737,6 +785,7 @@ def main():
                        "model": "SFNN_halfkahm2_1536_15_32_k3k3: (73305+1629 virtual) x 1536 FT, pairwise, "
                                 "9 x (1536 -> 15+1), shared L1 factor, 30 -> 32 -> 1",
                        "max_active": SFNN_ACTIVE, "buckets": "uniform 0..8",
+                       "qat": f"{args.qat}: {SFNN_QAT_LABELS[args.qat]}",
                        "l2": "no flush: each step streams 1.8 GB of FT optimizer state (> 126 MB L2)"}, **common)
     else:
         metric = METRIC
@@ -769,8 +818,8 @@ def main():
     value = args.steps * args.batch * world / (r["total_ms"] / 1000.0)
     if rank == 0:
         hbm, kind = measured_peaks()
-        rl = sfnn_roofline(r["phase_ms"], args.batch, hbm, kind) if sfnn else roofline(r["phase_ms"], args.batch, hbm,
-                                                                                          kind)
+        rl = (sfnn_roofline(r["phase_ms"], args.batch, hbm, kind, qat=args.qat) if sfnn
+              else roofline(r["phase_ms"], args.batch, hbm, kind))
         line = dict(base, value=round(value, 1), ms_per_step=round(r["total_ms"] / args.steps, 4),
                     e2e={k: (round(v, 1) if isinstance(v, float) else v) for k, v in r["e2e"].items()},
                     roofline=rl, clocks=r["clocks"], gpu_launches=r["gpu_launches"], final_loss=r["final_loss"])

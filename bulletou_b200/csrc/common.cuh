@@ -34,7 +34,7 @@ struct BulletOuCudaCppContext {
     bool owns_stream = true;
     int sm_count = 148;
     // Named scratch slots; see scratch_slot in runtime.cu.
-    bou::Scratch scratch[24];
+    bou::Scratch scratch[32];
     // Dense QAT mode between bulletou_dense_qat_begin / _end (the reference's
     // context flags, cu:9356-9382): integer L1 / L2 / L3 in the SFNN entries.
     bool dense_qat = false;
@@ -113,6 +113,7 @@ enum ScratchSlot : int {
     kScratchSfnnQuant = 21,     // SFNN integer forward: FT pair values + king sort
     kScratchSfnnQat = 22,       // SFNN QAT: quantised L1 bias, integer biases, raw L1 / L2 sums
     kScratchSfnnQatFt = 23,     // SFNN QAT: fake-quantised FT bias
+    kScratchSfnnQatTable = 24,  // SFNN dense QAT with FT QAT: integer FT table (i16)
 };
 
 int ok();

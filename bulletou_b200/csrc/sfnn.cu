@@ -126,12 +126,41 @@ __global__ void fold_ft_qat_kernel(const float* __restrict__ l0w, float* __restr
     folded[t] = qat_q127(v);
 }
 
+// The same four columns at a time; optionally the integers q (the i16 table of
+// the engine's integer FT) are written alongside.
+__global__ void fold_ft_qat4_kernel(const float4* __restrict__ l0w, float4* __restrict__ folded,
+                                    short4* __restrict__ table16, size_t total4, int w4, int base, float alpha) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= total4) return;
+    float4 a = l0w[t];
+    if (base > 0) {
+        const size_t f = t / w4;
+        const float4 v = l0w[(static_cast<size_t>(base) + f % kSfnnPieces) * w4 + (t - f * w4)];
+        a = make_float4(fold_nf(a.x, alpha, v.x), fold_nf(a.y, alpha, v.y), fold_nf(a.z, alpha, v.z),
+                        fold_nf(a.w, alpha, v.w));
+    }
+    const float4 q = make_float4(qat_q127(a.x), qat_q127(a.y), qat_q127(a.z), qat_q127(a.w));
+    folded[t] = q;
+    if (table16 != nullptr)
+        table16[t] = make_short4(static_cast<short>(qat_int127(q.x)), static_cast<short>(qat_int127(q.y)),
+                                 static_cast<short>(qat_int127(q.z)), static_cast<short>(qat_int127(q.w)));
+}
+
 // layer_qat_vector_kernel (cu:9294-9300): element-wise fake quantisation.
 __global__ void qat_vector_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t n, int kind) {
     const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t >= n) return;
     const float v = src[t];
     dst[t] = kind == 0 ? qat_q127(v) : (kind == 1 ? qat_q64(v) : qat_q8128(v));
+}
+
+// The integers q of an FT table already on the 1/127 lattice (FT QAT), as i16.
+__global__ void qat_table16_kernel(const float4* __restrict__ table, short4* __restrict__ out, size_t n4) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= n4) return;
+    const float4 v = table[t];
+    out[t] = make_short4(static_cast<short>(qat_int127(v.x)), static_cast<short>(qat_int127(v.y)),
+                         static_cast<short>(qat_int127(v.z)), static_cast<short>(qat_int127(v.w)));
 }
 
 // Reference-layout L1 QAT weights [S][O][W] (sfnn_build_quantized_proxy_stacked_
@@ -267,7 +296,7 @@ __device__ __forceinline__ float pair_out(float x0, float x1, int lattice) {
 
 // One warp per half-position; lane owns float4 chunks lane + 32 i, so chunk i
 // and chunk i + NCH/2 are the two members of a pair (width / 2 apart).
-template <int NCH>
+template <int NCH, bool LATTICE>
 __global__ void __launch_bounds__(256) ft_forward_kernel(FtArgs a) {
     const int lane = threadIdx.x & 31;
     const int pos = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -309,8 +338,13 @@ __global__ void __launch_bounds__(256) ft_forward_kernel(FtArgs a) {
 #pragma unroll
     for (int i = 0; i < NCH / 2; ++i) {
         const float4 x0 = acc[i], x1 = acc[i + NCH / 2];
-        comb[lane + 32 * i] = make_float4(pair_out(x0.x, x1.x, a.lattice), pair_out(x0.y, x1.y, a.lattice),
-                                          pair_out(x0.z, x1.z, a.lattice), pair_out(x0.w, x1.w, a.lattice));
+        if (LATTICE) {
+            comb[lane + 32 * i] = make_float4(pair_out(x0.x, x1.x, 1), pair_out(x0.y, x1.y, 1),
+                                              pair_out(x0.z, x1.z, 1), pair_out(x0.w, x1.w, 1));
+        } else {
+            comb[lane + 32 * i] = make_float4(x0.x * x1.x * kPairScale, x0.y * x1.y * kPairScale,
+                                              x0.z * x1.z * kPairScale, x0.w * x1.w * kPairScale);
+        }
     }
 }
 
@@ -360,6 +394,56 @@ __global__ void qat_exact_ft_kernel(FtArgs a) {
     const int x0 = min(254, max(0, static_cast<int>(static_cast<short>(s0))));
     const int x1 = min(254, max(0, static_cast<int>(static_cast<short>(s1))));
     a.combined[static_cast<size_t>(b) * a.width + v * half + j] = qat_on_lattice((x0 * x1) >> 9);
+}
+
+// The same from the i16 table, one warp per half-position in king order
+// (W % 512 == 0): lane owns columns 256 k + 8 lane + e, 16-byte loads; chunk k
+// pairs with chunk k + NCH / 2.  All sums are exact integers.
+template <int NCH>
+__global__ void __launch_bounds__(256) qat_exact_ft16_kernel(FtArgs a, const short* __restrict__ table16) {
+    const int lane = threadIdx.x & 31;
+    const int pos = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pos >= a.n_half) return;
+    const int h = a.order[pos];
+    const int b = h >> 1, v = h & 1;
+    const int* idx = (v ? a.nstm : a.stm) + static_cast<size_t>(b) * a.max_active;
+    int acc[NCH][8];
+#pragma unroll
+    for (int k = 0; k < NCH; ++k)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[k][q] = 2 * qat_int127(a.bias[256 * k + 8 * lane + q]);
+    for (int s0 = 0; s0 < a.max_active; s0 += 32) {
+        const int mine = s0 + lane < a.max_active ? __ldg(idx + s0 + lane) : -1;
+        const int n = min(32, a.max_active - s0);
+        for (int u = 0; u < n; ++u) {
+            const int f = __shfl_sync(kFull, mine, u);
+            if (f < 0 || f >= a.n_features) continue;
+            const short* row = table16 + static_cast<size_t>(f) * a.width + 8 * lane;
+            int4 r[NCH];
+#pragma unroll
+            for (int k = 0; k < NCH; ++k) r[k] = __ldg(reinterpret_cast<const int4*>(row + 256 * k));
+#pragma unroll
+            for (int k = 0; k < NCH; ++k) {
+                const short* e = reinterpret_cast<const short*>(&r[k]);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc[k][q] += 2 * static_cast<int>(e[q]);
+            }
+        }
+    }
+    float* out = a.combined + static_cast<size_t>(b) * a.width + v * (a.width / 2) + 8 * lane;
+#pragma unroll
+    for (int k = 0; k < NCH / 2; ++k) {
+        float c[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int x0 = min(254, max(0, static_cast<int>(static_cast<short>(acc[k][q]))));
+            const int x1 = min(254, max(0, static_cast<int>(static_cast<short>(acc[k + NCH / 2][q]))));
+            c[q] = qat_on_lattice((x0 * x1) >> 9);
+        }
+        float4* o4 = reinterpret_cast<float4*>(out + 256 * k);
+        o4[0] = make_float4(c[0], c[1], c[2], c[3]);
+        o4[1] = make_float4(c[4], c[5], c[6], c[7]);
+    }
 }
 
 // ------------------------------------------------------------------ L1
@@ -1017,7 +1101,7 @@ __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
     const float* x = a.l0[v];
     for (int q0 = 0; q0 < n; q0 += kU) {
         // Issue the loads of kU samples before using any of them.
-        float xa[kU], xb[kU];
+        float xa[kU], xb[kU], cc[kU];
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const int q = q0 + u;
@@ -1025,6 +1109,7 @@ __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
                 const size_t row = static_cast<size_t>(bs[q]) * W;
                 xa[u] = x[row + j];
                 xb[u] = x[row + j + half];
+                if (a.combined != nullptr) cc[u] = a.combined[row + i];
             }
         }
 #pragma unroll
@@ -1032,7 +1117,7 @@ __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
             const int q = q0 + u;
             if (q >= n) break;
             const float x0 = xa[u], x1 = xb[u];
-            const float c = a.combined != nullptr ? a.combined[static_cast<size_t>(bs[q]) * W + i] : x0 * x1 * kPairScale;
+            const float c = a.combined != nullptr ? cc[u] : x0 * x1 * kPairScale;
             float dc = 0.0f;
 #pragma unroll
             for (int o = 0; o < kO; ++o) {
@@ -1450,6 +1535,7 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a) {
 // ------------------------------------------------------------------ host plan
 struct SfnnPlan {
     const float* table;    // what the FT gather reads
+    const short* table16;  // dense QAT with FT QAT: the table's integers, when the fold wrote them
     const float* ft_bias;  // FT bias the gather starts from (fake-quantised under FT QAT)
     KingSortOut king;
     int* king_rank;
@@ -1502,8 +1588,25 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
             if (scratch_slot(ctx, kScratchSfnnFold, n * sizeof(float), &p, "cudaMalloc SFNN folded FT") != 0) return -1;
             folded = static_cast<float*>(p);
         }
-        if (grid_1d(n, threads, &blocks, "SFNN FT QAT fold") != 0) return -1;
-        fold_ft_qat_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l0w, folded, n, d.width, d.base, d.ft_alpha);
+        plan->table16 = nullptr;
+        if (d.width % 4 == 0 && aligned16(w.l0w) && aligned16(folded)) {
+            short* t16 = nullptr;
+            if (d.qat.integer_ft && d.width % 512 == 0 && d.width <= 2560) {
+                void* tp = nullptr;
+                if (scratch_slot(ctx, kScratchSfnnQatTable, n * sizeof(short), &tp,
+                                 "cudaMalloc SFNN QAT i16 table") != 0)
+                    return -1;
+                t16 = static_cast<short*>(tp);
+                plan->table16 = t16;
+            }
+            if (grid_1d(n / 4, threads, &blocks, "SFNN FT QAT fold") != 0) return -1;
+            fold_ft_qat4_kernel<<<blocks, threads, 0, ctx->stream>>>(
+                reinterpret_cast<const float4*>(w.l0w), reinterpret_cast<float4*>(folded),
+                reinterpret_cast<short4*>(t16), n / 4, d.width / 4, d.base, d.ft_alpha);
+        } else {
+            if (grid_1d(n, threads, &blocks, "SFNN FT QAT fold") != 0) return -1;
+            fold_ft_qat_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l0w, folded, n, d.width, d.base, d.ft_alpha);
+        }
         void* bp = nullptr;
         if (scratch_slot(ctx, kScratchSfnnQatFt, static_cast<size_t>(d.width) * sizeof(float), &bp,
                          "cudaMalloc SFNN FT QAT bias") != 0)
@@ -1626,6 +1729,32 @@ int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const Sfnn
         ea.max_active = d.max_active;
         ea.n_features = d.n_features;
         ea.width = d.width;
+        ea.order = plan.king.order;
+        if (d.width % 512 == 0 && d.width <= 2560 && aligned16(plan.table) && aligned16(act.combined)) {
+            const short* t16 = plan.table16;
+            if (t16 == nullptr) {
+                // The table came from the caller (reference entry): take its integers.
+                const size_t n = static_cast<size_t>(d.n_features) * d.width;
+                void* tp = nullptr;
+                if (scratch_slot(ctx, kScratchSfnnQatTable, n * sizeof(short), &tp,
+                                 "cudaMalloc SFNN QAT i16 table") != 0)
+                    return -1;
+                int blocks = 0;
+                if (grid_1d(n / 4, 256, &blocks, "SFNN QAT i16 table") != 0) return -1;
+                qat_table16_kernel<<<blocks, 256, 0, ctx->stream>>>(reinterpret_cast<const float4*>(plan.table),
+                                                                      static_cast<short4*>(tp), n / 4);
+                t16 = static_cast<const short*>(tp);
+            }
+            const int hb = (ea.n_half + 7) / 8;
+            switch (d.width / 256) {
+                case 2: qat_exact_ft16_kernel<2><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
+                case 4: qat_exact_ft16_kernel<4><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
+                case 6: qat_exact_ft16_kernel<6><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
+                case 8: qat_exact_ft16_kernel<8><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
+                default: qat_exact_ft16_kernel<10><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
+            }
+            return check_launch("SFNN exact QAT FT launch");
+        }
         int gb = 0;
         if (grid_1d(static_cast<size_t>(ea.n_half) * (d.width / 2), 256, &gb, "SFNN exact QAT FT") != 0) return -1;
         qat_exact_ft_kernel<<<gb, 256, 0, ctx->stream>>>(ea);
@@ -1648,11 +1777,16 @@ int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const Sfnn
     const bool al = aligned16(plan.table) && aligned16(l0b) && aligned16(act.stm_l0) && aligned16(act.nstm_l0) &&
                     aligned16(act.combined);
     const int blocks = (fa.n_half + 7) / 8;
-    if (al && d.width == 1536) ft_forward_kernel<12><<<blocks, 256, 0, ctx->stream>>>(fa);
-    else if (al && d.width == 1024) ft_forward_kernel<8><<<blocks, 256, 0, ctx->stream>>>(fa);
-    else if (al && d.width == 2304) ft_forward_kernel<18><<<blocks, 256, 0, ctx->stream>>>(fa);
-    else if (al && d.width == 512) ft_forward_kernel<4><<<blocks, 256, 0, ctx->stream>>>(fa);
-    else if (al && d.width == 256) ft_forward_kernel<2><<<blocks, 256, 0, ctx->stream>>>(fa);
+    const bool lat = fa.lattice != 0;
+#define BOU_FT_FWD(N)                                                              \
+    (lat ? ft_forward_kernel<N, true><<<blocks, 256, 0, ctx->stream>>>(fa)        \
+         : ft_forward_kernel<N, false><<<blocks, 256, 0, ctx->stream>>>(fa))
+    if (al && d.width == 1536) BOU_FT_FWD(12);
+    else if (al && d.width == 1024) BOU_FT_FWD(8);
+    else if (al && d.width == 2304) BOU_FT_FWD(18);
+    else if (al && d.width == 512) BOU_FT_FWD(4);
+    else if (al && d.width == 256) BOU_FT_FWD(2);
+#undef BOU_FT_FWD
     else {
         fa.order = nullptr;
         int gb = 0;

@@ -18,6 +18,7 @@ pytestmark = pytest.mark.gpu
 HM2F = bs.HALFKA_HM2_DIMENSIONS + bs.PIECE_INPUTS
 PROD = bs.SFNN_HALFKA_HM2_1536_15_32_K3K3
 SMALL = bs.SfnnForwardShape(HM2F, 256, 15, True, 32, 9)
+MID = bs.SfnnForwardShape(HM2F, 512, 15, True, 32, 9)               # warp integer-FT kernel
 GENERIC = bs.SfnnForwardShape(HM2F, 12, 3, True, 5, 4)
 
 MODES = {
@@ -66,7 +67,7 @@ def _params(step, lr=1e-3):
 
 
 @pytest.mark.parametrize("mode", list(MODES))
-@pytest.mark.parametrize("shape", [SMALL, GENERIC], ids=["small", "generic"])
+@pytest.mark.parametrize("shape", [SMALL, MID, GENERIC], ids=["small", "mid", "generic"])
 def test_fused_qat_steps_vs_oracle(ctx, mode, shape):
     lr = MODES[mode]
     w = _weights(shape, 11)
@@ -136,7 +137,7 @@ def test_layer_qat_entry_vs_reference_backend(ctx, ref_ctx):
         np.testing.assert_array_equal(outs[0], outs[1], err_msg=f"scale {scale} rows {rows}")
 
 
-@pytest.mark.parametrize("mode", ["l1", "dense"])
+@pytest.mark.parametrize("mode", ["l1", "dense", "dense_ft"])
 def test_fused_qat_prod_vs_reference_backend(ctx, ref_ctx, mode):
     """Production shape, 20 steps: weights within 1e-3 of the reference backend."""
     lr = MODES[mode]
