@@ -100,7 +100,14 @@ def _sf_batches():
     return [synthetic.sfnn_batch(800 + i, 2 * SF_BATCH) for i in range(STEPS)]
 
 
-def _sf_rank_main(rank, world, port, out_path):
+def _sf_qat(mode):
+    from bulletou_b200 import sfnn as bs
+
+    return bs.SfnnLayerLrMultipliers() if mode == "none" else bs.SfnnLayerLrMultipliers(
+        qat_l1=True, qat_ft=True, qat_l2=True, qat_l3=True)
+
+
+def _sf_rank_main(rank, world, port, out_path, qat="none"):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -118,7 +125,8 @@ def _sf_rank_main(rank, world, port, out_path):
     try:
         w = synthetic.sfnn_weights(synthetic.rng_for(23), ft=256)
         shape = bs.SfnnForwardShape(73305 + 1629, 256, 15, True, 32, 9)
-        tr = SfnnDataParallelTrainer(B200Backend(rank), dist, bs.SfnnForwardHostWeights(shape, **w), SF_BATCH, 40)
+        tr = SfnnDataParallelTrainer(B200Backend(rank), dist, bs.SfnnForwardHostWeights(shape, **w), SF_BATCH, 40,
+                                     lr_multipliers=_sf_qat(qat))
         for step, b in enumerate(_sf_batches(), start=1):
             sl = slice(rank * SF_BATCH * 40, (rank + 1) * SF_BATCH * 40)
             bsl = slice(rank * SF_BATCH, (rank + 1) * SF_BATCH)
@@ -135,14 +143,15 @@ def _sf_rank_main(rank, world, port, out_path):
 
 
 @pytest.mark.timeout(600)
-def test_two_gpu_sfnn_data_parallel_matches_single_gpu_global_batch(tmp_path):
+@pytest.mark.parametrize("qat", ["none", "all"])
+def test_two_gpu_sfnn_data_parallel_matches_single_gpu_global_batch(tmp_path, qat):
     import torch
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     out = tmp_path / "rank0.npz"
-    mp.start_processes(_sf_rank_main, args=(2, _free_port(), str(out)), nprocs=2, start_method="spawn")
+    mp.start_processes(_sf_rank_main, args=(2, _free_port(), str(out), qat), nprocs=2, start_method="spawn")
     got = np.load(out)
 
     import bulletou_b200 as bo
@@ -152,7 +161,8 @@ def test_two_gpu_sfnn_data_parallel_matches_single_gpu_global_batch(tmp_path):
     w = synthetic.sfnn_weights(synthetic.rng_for(23), ft=256)
     shape = bs.SfnnForwardShape(73305 + 1629, 256, 15, True, 32, 9)
     ctx = bo.Context(0)
-    runner = bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(shape, **w), 2 * SF_BATCH, 40)
+    runner = bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(shape, **w), 2 * SF_BATCH, 40,
+                                    lr_multipliers=_sf_qat(qat))
     for step, b in enumerate(_sf_batches(), start=1):
         hb = bs.SfnnTrainStepHostBatch(b["stm"], b["nstm"], b["buckets"], b["targets"], b["entry_weights"],
                                        2 * SF_BATCH, 40)
