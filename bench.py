@@ -501,13 +501,22 @@ def sfnn_cpu_baseline(batch_cap=256, budget_s=8.0):
                       f"{batch_cap} positions in {dt:.1f} s; the reference cannot train on CPU"}
 
 
-def _profile(lib, ctx, marks):
+def sfnn_phases(qat):
+    """Stage-profiler phases of one fused step (the integer FT of the dense
+    QAT with FT QAT is a phase of its own)."""
+    l1, ft, l2, l3 = SFNN_QAT_MODES[qat]
+    if ft and l1 and l2 and l3:
+        return SFNN_PHASES[:4] + ("ft_integer",) + SFNN_PHASES[4:]
+    return SFNN_PHASES
+
+
+def _profile(lib, ctx, names):
     import ctypes
 
     ms = (ctypes.c_float * 16)()
     nsteps, nphases = ctypes.c_size_t(), ctypes.c_size_t()
     lib.call("bulletou_b200_profile_end", ctx.as_ptr(), ms, 16, ctypes.byref(nsteps), ctypes.byref(nphases))
-    return {SFNN_PHASES[p]: ms[p] / max(1, nsteps.value) for p in range(min(nphases.value, len(SFNN_PHASES)))}
+    return {names[p]: ms[p] / max(1, nsteps.value) for p in range(min(nphases.value, len(names)))}
 
 
 def run_sfnn_b200(args, rank, world, local, dist):
@@ -532,7 +541,7 @@ def run_sfnn_b200(args, rank, world, local, dist):
     ctx.synchronize()
     lib = ctx.lib
     start, stop = bo.Event(ctx), bo.Event(ctx)
-    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 9 * args.steps + 9)
+    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 10 * args.steps + 10)
     with ClockSampler(local) as clocks:
         start.record(ctx)
         for i in range(args.steps):
@@ -541,7 +550,7 @@ def run_sfnn_b200(args, rank, world, local, dist):
             runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=False)
         stop.record(ctx)
         stop.synchronize()
-    phase_ms = _profile(lib, ctx, 9)
+    phase_ms = _profile(lib, ctx, sfnn_phases(args.qat))
     total_ms = stop.elapsed_ms_since(start)
     clk = clocks.summary()
     # ---- end to end through the public runner API (pipelined step, lib.rs:7627) ----
@@ -613,7 +622,7 @@ def run_sfnn_data_parallel(args, rank, world, local, dist):
     torch.cuda.synchronize()
     dist.barrier()
     start, stop = bo.Event(ctx), bo.Event(ctx)
-    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 9 * args.steps + 9)
+    lib.call("bulletou_b200_profile_begin", ctx.as_ptr(), 10 * args.steps + 10)
     with ClockSampler(local) as clocks:
         start.record(ctx)
         for i in range(args.steps):
@@ -622,7 +631,7 @@ def run_sfnn_data_parallel(args, rank, world, local, dist):
             tr.step_device(ranger(step), loss_kind, inv, finalize_loss=False)
         stop.record(ctx)
         stop.synchronize()
-    phase_ms = _profile(lib, ctx, 9)
+    phase_ms = _profile(lib, ctx, sfnn_phases(args.qat))
     torch.cuda.synchronize()
     dist.barrier()
     total_ms = max_over_ranks(dist, stop.elapsed_ms_since(start))
@@ -753,9 +762,9 @@ def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0
     }
     l1, ft, l2, l3 = SFNN_QAT_MODES[qat]
     if ft and l1 and l2 and l3:
-        # the fold also writes the i16 table; the integer FT gathers it and rewrites combined
+        # the fold also writes the i16 table; the integer FT gathers it (logical) and rewrites combined
         algo["fold"] += base * W * 2
-        algo["ft_forward"] += half_positions * A * W * 2 + batch * W * 4
+        algo["ft_integer"] = half_positions * A * W * 2 + half_positions * A * 4 + batch * W * 4
     if l1 and l2 and l3:
         algo["l1_backward"] += batch * W * 4  # the lattice FT output read for dL1w
     dom = max(phase_ms, key=phase_ms.get)

@@ -43,4 +43,11 @@ from .sfnn import (  # noqa: F401
     sfnn_quantize_device,
 )
 
+from .nnue_quant import (  # noqa: F401
+    NnueIntegerForwardWorkspace,
+    QuantizedNnueDeviceWeights,
+    nnue_integer_forward_device,
+    nnue_quantize_device,
+)
+
 __version__ = "0.1.0"

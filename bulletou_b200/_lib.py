@@ -159,6 +159,8 @@ SIGNATURES: dict[str, list] = {
     "bulletou_dense_qat_begin": [P, P, P, Z, Z, Z, Z, I],
     "bulletou_dense_qat_end": [P],
     "bulletou_b200_sfnn_quantize_device": [P, P, P, P],
+    "bulletou_b200_nnue_quantize_device": [P, Z, Z, Z, Z, P, P, P],
+    "bulletou_b200_nnue_integer_forward_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, I, P, P, P],
     "bulletou_b200_sfnn_integer_forward_device": [P, P, Z, Z] + [P] * 9,
 }
 

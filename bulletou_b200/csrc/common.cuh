@@ -114,6 +114,7 @@ enum ScratchSlot : int {
     kScratchSfnnQat = 22,       // SFNN QAT: quantised L1 bias, integer biases, raw L1 / L2 sums
     kScratchSfnnQatFt = 23,     // SFNN QAT: fake-quantised FT bias
     kScratchSfnnQatTable = 24,  // SFNN dense QAT with FT QAT: integer FT table (i16)
+    kScratchNnueQuant = 25,     // integer HalfKP forward: transformed features (u8)
 };
 
 int ok();

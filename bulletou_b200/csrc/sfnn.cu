@@ -398,7 +398,10 @@ __global__ void qat_exact_ft_kernel(FtArgs a) {
 
 // The same from the i16 table, one warp per half-position in king order
 // (W % 512 == 0): lane owns columns 256 k + 8 lane + e, 16-byte loads; chunk k
-// pairs with chunk k + NCH / 2.  All sums are exact integers.
+// pairs with chunk k + NCH / 2.  Only the sums modulo 2^16 matter (the engine
+// wraps them to i16), so each 32-bit word of two columns is added whole into
+// `lo` (its low half is the even column's sum) and shifted into `hi` (the odd
+// column's): one shift and two adds per two columns.
 template <int NCH>
 __global__ void __launch_bounds__(256) qat_exact_ft16_kernel(FtArgs a, const short* __restrict__ table16) {
     const int lane = threadIdx.x & 31;
@@ -407,11 +410,14 @@ __global__ void __launch_bounds__(256) qat_exact_ft16_kernel(FtArgs a, const sho
     const int h = a.order[pos];
     const int b = h >> 1, v = h & 1;
     const int* idx = (v ? a.nstm : a.stm) + static_cast<size_t>(b) * a.max_active;
-    int acc[NCH][8];
+    unsigned lo[NCH][4], hi[NCH][4];
 #pragma unroll
     for (int k = 0; k < NCH; ++k)
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[k][q] = 2 * qat_int127(a.bias[256 * k + 8 * lane + q]);
+        for (int c = 0; c < 4; ++c) {
+            lo[k][c] = static_cast<unsigned>(qat_int127(a.bias[256 * k + 8 * lane + 2 * c]));
+            hi[k][c] = static_cast<unsigned>(qat_int127(a.bias[256 * k + 8 * lane + 2 * c + 1]));
+        }
     for (int s0 = 0; s0 < a.max_active; s0 += 32) {
         const int mine = s0 + lane < a.max_active ? __ldg(idx + s0 + lane) : -1;
         const int n = min(32, a.max_active - s0);
@@ -419,14 +425,19 @@ __global__ void __launch_bounds__(256) qat_exact_ft16_kernel(FtArgs a, const sho
             const int f = __shfl_sync(kFull, mine, u);
             if (f < 0 || f >= a.n_features) continue;
             const short* row = table16 + static_cast<size_t>(f) * a.width + 8 * lane;
-            int4 r[NCH];
+            uint4 r[NCH];
 #pragma unroll
-            for (int k = 0; k < NCH; ++k) r[k] = __ldg(reinterpret_cast<const int4*>(row + 256 * k));
+            for (int k = 0; k < NCH; ++k) r[k] = __ldg(reinterpret_cast<const uint4*>(row + 256 * k));
 #pragma unroll
             for (int k = 0; k < NCH; ++k) {
-                const short* e = reinterpret_cast<const short*>(&r[k]);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) acc[k][q] += 2 * static_cast<int>(e[q]);
+                lo[k][0] += r[k].x;
+                hi[k][0] += r[k].x >> 16;
+                lo[k][1] += r[k].y;
+                hi[k][1] += r[k].y >> 16;
+                lo[k][2] += r[k].z;
+                hi[k][2] += r[k].z >> 16;
+                lo[k][3] += r[k].w;
+                hi[k][3] += r[k].w >> 16;
             }
         }
     }
@@ -436,8 +447,11 @@ __global__ void __launch_bounds__(256) qat_exact_ft16_kernel(FtArgs a, const sho
         float c[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            const int x0 = min(254, max(0, static_cast<int>(static_cast<short>(acc[k][q]))));
-            const int x1 = min(254, max(0, static_cast<int>(static_cast<short>(acc[k + NCH / 2][q]))));
+            const unsigned s0w = (q & 1) ? hi[k][q >> 1] : lo[k][q >> 1];
+            const unsigned s1w = (q & 1) ? hi[k + NCH / 2][q >> 1] : lo[k + NCH / 2][q >> 1];
+            // doubled sums wrapped to i16, clamped to [0, 254]
+            const int x0 = min(254, max(0, static_cast<int>(static_cast<short>(s0w << 1))));
+            const int x1 = min(254, max(0, static_cast<int>(static_cast<short>(s1w << 1))));
             c[q] = qat_on_lattice((x0 * x1) >> 9);
         }
         float4* o4 = reinterpret_cast<float4*>(out + 256 * k);
@@ -1719,6 +1733,7 @@ int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const Sfnn
         df.qat.integer_ft = 0;
         df.qat.dense = 0;
         if (launch_ft_forward(ctx, df, plan, stm, nstm, l0b, act) != 0) return -1;
+        prof_mark(ctx);  // stage profiler: the integer FT is its own phase
         FtArgs ea{};
         ea.stm = stm;
         ea.nstm = nstm;
@@ -2074,7 +2089,7 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
               const BulletOuB200RangerStep* ranger, float* const* wm, float* const* mm, float* const* vm,
               float* const* sm, float* output, float* per_sample, float* mog, float* weighted_sum, float* mean,
               float* ft_grad, float* dense_grad) {
-    ctx->prof_marks_per_step = 9;
+    ctx->prof_marks_per_step = (d.qat.dense && d.qat.integer_ft) ? 10 : 9;
     prof_mark(ctx);
     SfnnPlan plan{};
     if (sfnn_prepare(ctx, d, w, stm, nstm, buckets, nullptr, &plan) != 0) return -1;

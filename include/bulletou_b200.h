@@ -273,6 +273,37 @@ int bulletou_b200_sfnn_local_gradients_device(
     BulletOuCudaCppF32Buffer* per_sample, BulletOuCudaCppF32Buffer* mean_output_gradients,
     BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat);
 
+/* ---------------------------------------------------------------- quantised HalfKP
+ * The reference exports a trained HalfKP 256x2-32-32 net to the engine's
+ * nn.bin (write_cuda_cpp_nnue_nn_bin, examples/bulletou.rs:26303-26413); the
+ * engine (YaneuraOu's halfkp_256x2-32-32 NNUE, outside the reference tree)
+ * evaluates it in integers.  No counterpart in the reference's C ABI.
+ * Quantised buffers (I32 handles holding packed narrow integers):
+ *   0 l0w  i16 [rows][l1]   rows = 125388 when input_size = 125388 + 1548
+ *                           (the 1548 leading virtual rows added to each base
+ *                           row), else input_size
+ *   1 l0b  i16 [l1]          2 l1w i8 [l2][pad32(2 l1)]   3 l1b i32 [l2]
+ *   4 l2w  i8 [l3][pad32(l2)] 5 l2b i32 [l3]   6 outw i8 [pad32(l3)]   7 outb i32 [1]
+ * Scales: FT 127, dense weights 64, biases 127 * 64; round half away from zero;
+ * values outside their integer range saturate and are counted in errors[0]
+ * (the reference's writer refuses them).  params: the 8 f32 handles
+ * l0w l0b l1w l1b l2w l2b outw outb in the training layout (dense weights
+ * input-major). */
+int bulletou_b200_nnue_quantize_device(BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2,
+    size_t l3, BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppI32Buffer* const* quantized,
+    BulletOuCudaCppI32Buffer* errors);
+
+/* Integer evaluation of a batch: per perspective (side to move first) an i16
+ * accumulator (bias + rows, wrapping) clamped to [0, 127]; each affine layer
+ * bias + sum u8 * i8 in i32 then clamp(x >> 6, 0, 127); raw_output = output
+ * bias + sum; score_output (optional) = raw / fv_scale (toward zero).
+ * Features below 0 are padding; features at or above rows are skipped and
+ * counted in errors[0] (optional). */
+int bulletou_b200_nnue_integer_forward_device(BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2,
+    size_t l3, size_t batch, size_t max_active, const BulletOuCudaCppI32Buffer* stm_indices,
+    const BulletOuCudaCppI32Buffer* nstm_indices, BulletOuCudaCppI32Buffer* const* quantized, int fv_scale,
+    BulletOuCudaCppI32Buffer* raw_output, BulletOuCudaCppI32Buffer* score_output, BulletOuCudaCppI32Buffer* errors);
+
 /* ---------------------------------------------------------------- quantised SFNN
  * The reference evaluates a trained SFNN through the engine's integer network
  * on the CPU (examples/bulletou.rs: export quantisation 10050-10300, integer

@@ -1035,3 +1035,111 @@ EXPORT void oracle_sfnn_integer_forward(const int64_t* shape, const int* stm, co
     free(in);
     free(l2);
 }
+
+/* ------------------------------------------------------------------ quantised HalfKP
+ * nn.bin quantisation of the HalfKP 256x2-32-32 net as the reference writes it
+ * (write_cuda_cpp_nnue_nn_bin, examples/bulletou.rs:26303-26386; scales
+ * qa = 127, qb = 64, L1 bias 127 * 64 = l1_bias_scale(CReLU, false, 127, 64),
+ * crates/bulletou_lib/src/value/nnue_save.rs:223-235): the factorized table's
+ * virtual rows (first 1548 rows) added to each base row (26390-26413), values
+ * round(scale * w) in double, half away from zero; dense weights transposed to
+ * output-major and padded to 32 inputs (pad_weights_for_simd, nnue_save.rs:
+ * 237-252).  Values outside the integer range are an error there: here they are
+ * saturated and counted in *errors.
+ * shape: input_size, l1, l2, l3.  Output rows = 125388 when input_size =
+ * 125388 + 1548 (factorized), else input_size. */
+static int64_t q_round_count(double v, double lo, double hi, int64_t* errors) {
+    double q = round(v);
+    if (q < lo) { q = lo; ++*errors; }
+    if (q > hi) { q = hi; ++*errors; }
+    return (int64_t)q;
+}
+
+EXPORT void oracle_nnue_quantize(const int64_t* shape, const float* const* w, int16_t* l0w_q, int16_t* l0b_q,
+                                 int8_t* l1w_q, int32_t* l1b_q, int8_t* l2w_q, int32_t* l2b_q, int8_t* outw_q,
+                                 int32_t* outb_q, int64_t* errors) {
+    const int64_t input_size = shape[0], L1 = shape[1], L2 = shape[2], L3 = shape[3];
+    const int factorized = input_size == 125388 + 1548;
+    const int64_t rows = factorized ? 125388 : input_size;
+    *errors = 0;
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t j = 0; j < L1; ++j) {
+            float v = factorized ? w[0][(1548 + r) * L1 + j] + w[0][(r % 1548) * L1 + j] : w[0][r * L1 + j];
+            l0w_q[r * L1 + j] = (int16_t)q_round_count(127.0 * (double)v, -32768.0, 32767.0, errors);
+        }
+    for (int64_t j = 0; j < L1; ++j) l0b_q[j] = (int16_t)q_round_count(127.0 * (double)w[1][j], -32768.0, 32767.0, errors);
+    const int64_t I1 = 2 * L1, p1 = pad32(I1), p2 = pad32(L2), p3 = pad32(L3);
+    for (int64_t o = 0; o < L2; ++o) {
+        l1b_q[o] = (int32_t)q_round_count(8128.0 * (double)w[3][o], -2147483648.0, 2147483647.0, errors);
+        for (int64_t i = 0; i < p1; ++i)
+            l1w_q[o * p1 + i] = i < I1 ? (int8_t)q_round_count(64.0 * (double)w[2][i * L2 + o], -128.0, 127.0, errors) : 0;
+    }
+    for (int64_t o = 0; o < L3; ++o) {
+        l2b_q[o] = (int32_t)q_round_count(8128.0 * (double)w[5][o], -2147483648.0, 2147483647.0, errors);
+        for (int64_t i = 0; i < p2; ++i)
+            l2w_q[o * p2 + i] = i < L2 ? (int8_t)q_round_count(64.0 * (double)w[4][i * L3 + o], -128.0, 127.0, errors) : 0;
+    }
+    outb_q[0] = (int32_t)q_round_count(8128.0 * (double)w[7][0], -2147483648.0, 2147483647.0, errors);
+    for (int64_t i = 0; i < p3; ++i)
+        outw_q[i] = i < L3 ? (int8_t)q_round_count(64.0 * (double)w[6][i], -128.0, 127.0, errors) : 0;
+}
+
+/* The engine's integer evaluation of that net (YaneuraOu's halfkp_256x2-32-32
+ * NNUE, the engine the reference exports to; not part of the reference tree):
+ * per perspective (side to move first) i16 accumulator = bias + sum of rows
+ * (i16 wrap), ClippedReLU clamp(acc, 0, 127) -> u8; each affine layer
+ * bias + sum u8 * i8 in i32, ClippedReLU clamp(x >> 6, 0, 127); output
+ * bias + sum; score = raw / fv_scale (C division, toward zero).  Features
+ * outside [0, rows) are skipped and counted in *errors. */
+EXPORT void oracle_nnue_integer_forward(const int64_t* shape, int64_t batch, int64_t max_active, const int* stm,
+                                        const int* nstm, const int16_t* l0w_q, const int16_t* l0b_q,
+                                        const int8_t* l1w_q, const int32_t* l1b_q, const int8_t* l2w_q,
+                                        const int32_t* l2b_q, const int8_t* outw_q, const int32_t* outb_q,
+                                        int fv_scale, int32_t* raw_out, int32_t* score_out, int64_t* errors) {
+    const int64_t input_size = shape[0], L1 = shape[1], L2 = shape[2], L3 = shape[3];
+    const int64_t rows = input_size == 125388 + 1548 ? 125388 : input_size;
+    const int64_t I1 = 2 * L1, p1 = pad32(I1), p2 = pad32(L2), p3 = pad32(L3);
+    uint8_t* x = (uint8_t*)malloc((size_t)I1);
+    int32_t* h1 = (int32_t*)malloc(sizeof(int32_t) * (size_t)L2);
+    int32_t* h2 = (int32_t*)malloc(sizeof(int32_t) * (size_t)L3);
+    *errors = 0;
+    for (int64_t b = 0; b < batch; ++b) {
+        for (int v = 0; v < 2; ++v) {
+            const int* idx = (v ? nstm : stm) + b * max_active;
+            for (int64_t j = 0; j < L1; ++j) {
+                int32_t acc = l0b_q[j];
+                for (int64_t k = 0; k < max_active; ++k) {
+                    int f = idx[k];
+                    if (f < 0) continue;
+                    if ((int64_t)f >= rows) {
+                        if (j == 0) ++*errors;
+                        continue;
+                    }
+                    acc += l0w_q[(int64_t)f * L1 + j];
+                }
+                int32_t a16 = (int32_t)(int16_t)acc;
+                x[v * L1 + j] = (uint8_t)(a16 < 0 ? 0 : (a16 > 127 ? 127 : a16));
+            }
+        }
+        for (int64_t o = 0; o < L2; ++o) {
+            int32_t s = l1b_q[o];
+            for (int64_t i = 0; i < I1; ++i) s += (int32_t)x[i] * (int32_t)l1w_q[o * p1 + i];
+            int32_t c = s >> 6;
+            h1[o] = c < 0 ? 0 : (c > 127 ? 127 : c);
+        }
+        for (int64_t o = 0; o < L3; ++o) {
+            int32_t s = l2b_q[o];
+            for (int64_t i = 0; i < L2; ++i) s += h1[i] * (int32_t)l2w_q[o * p2 + i];
+            int32_t c = s >> 6;
+            h2[o] = c < 0 ? 0 : (c > 127 ? 127 : c);
+        }
+        int32_t out = outb_q[0];
+        for (int64_t i = 0; i < L3; ++i) out += h2[i] * (int32_t)outw_q[i];
+        raw_out[b] = out;
+        if (score_out) score_out[b] = out / fv_scale;
+        (void)p3;
+    }
+    free(x);
+    free(h1);
+    free(h2);
+}

@@ -49,10 +49,13 @@ def lib():
         _lib.oracle_sfnn_backward_qat.argtypes = [p, p, i] + [p] * 17
         _lib.oracle_sfnn_quantize.argtypes = [p] * 11
         _lib.oracle_sfnn_integer_forward.argtypes = [p] * 12 + [i] * 4 + [p] * 3
+        _lib.oracle_nnue_quantize.argtypes = [p] * 11
+        _lib.oracle_nnue_integer_forward.argtypes = [p, i64, i64] + [p] * 10 + [i] + [p] * 3
         for fn in (_lib.oracle_nnue_forward, _lib.oracle_scalar_loss, _lib.oracle_nnue_backward,
                    _lib.oracle_radam_step_scale, _lib.oracle_ranger_update, _lib.oracle_kppt_forward,
                    _lib.oracle_kppt_backward, _lib.oracle_sfnn_forward, _lib.oracle_sfnn_backward,
-                   _lib.oracle_sfnn_forward_qat, _lib.oracle_sfnn_backward_qat, _lib.oracle_sfnn_quantize, _lib.oracle_sfnn_integer_forward):
+                   _lib.oracle_sfnn_forward_qat, _lib.oracle_sfnn_backward_qat, _lib.oracle_sfnn_quantize, _lib.oracle_sfnn_integer_forward, _lib.oracle_nnue_quantize,
+                   _lib.oracle_nnue_integer_forward):
             fn.restype = None
     return _lib
 
@@ -360,3 +363,41 @@ def final_division(raw, fv_scale: int, nearest: bool) -> np.ndarray:
     r = np.asarray(raw, np.int64)
     mag = np.abs(r) + (fv_scale // 2 if nearest else 0)
     return (np.sign(r) * (mag // fv_scale)).astype(np.int32)
+
+
+# ------------------------------------------------------------------ quantised HalfKP
+NNUE_QUANT_NAMES = ("l0w", "l0b", "l1w", "l1b", "l2w", "l2b", "outw", "outb")
+
+
+def nnue_quant_shapes(shape) -> dict:
+    input_size, L1, L2, L3 = shape
+    rows = 125388 if input_size == 125388 + 1548 else input_size
+    return {"l0w": (rows * L1, np.int16), "l0b": (L1, np.int16), "l1w": (L2 * pad32(2 * L1), np.int8),
+            "l1b": (L2, np.int32), "l2w": (L3 * pad32(L2), np.int8), "l2b": (L3, np.int32),
+            "outw": (pad32(L3), np.int8), "outb": (1, np.int32)}
+
+
+def nnue_quantize(shape, weights: dict) -> dict:
+    """nn.bin quantisation of a HalfKP net (oracle_nnue_quantize); "errors"
+    counts values outside their integer range (saturated)."""
+    sh = np.asarray(shape, np.int64)
+    ws = [_f(weights[n]) for n in NAMES]
+    out = {n: np.zeros(c, dt) for n, (c, dt) in nnue_quant_shapes(shape).items()}
+    err = np.zeros(1, np.int64)
+    lib().oracle_nnue_quantize(_p(sh), _ptr_array(ws), *(_p(out[n]) for n in NNUE_QUANT_NAMES), _p(err))
+    out["errors"] = int(err[0])
+    return out
+
+
+def nnue_integer_forward(shape, stm, nstm, batch, max_active, q: dict, fv_scale: int = 16) -> dict:
+    """The engine's integer HalfKP evaluation (oracle_nnue_integer_forward)."""
+    sh = np.asarray(shape, np.int64)
+    qs = {n: np.ascontiguousarray(q[n], dtype=dt).reshape(-1) for n, (_, dt) in nnue_quant_shapes(shape).items()}
+    raw = np.zeros(batch, np.int32)
+    score = np.zeros(batch, np.int32)
+    err = np.zeros(1, np.int64)
+    s, n = _i(stm), _i(nstm)
+    lib().oracle_nnue_integer_forward(_p(sh), int(batch), int(max_active), _p(s), _p(n),
+                                      *(_p(qs[k]) for k in NNUE_QUANT_NAMES), int(fv_scale), _p(raw), _p(score),
+                                      _p(err))
+    return {"raw": raw, "score": score, "errors": int(err[0])}
