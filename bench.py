@@ -736,6 +736,19 @@ def run_sfnn_reference(args, local):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": e2e_steps}}
 
 
+# DRAM bytes per step of each phase at B = 65536 (dram__bytes_read.sum +
+# dram__bytes_write.sum over the phase's launches), from the full-size capture
+# summarised in profiles/sfnn_train_step_b65536.md; keyed by the QAT modes
+# whose kernels they were measured on.
+SFNN_DRAM_BYTES_B65536 = {
+    "ft_rows_ranger": (4813480704, ("none", "l1", "layers", "dense", "all")),
+    "ft_forward": (1679058432, ("none", "l1", "dense", "all")),
+    "ft_integer": (613106176, ("all",)),
+    "l1_backward": (2076098304, ("dense", "all")),
+    "fold": (1124865536, ("all",)),
+}
+
+
 def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0, qat="none"):
     """Algorithmic bytes per launch of each SFNN phase (the per-position
     formulas of the hot-path table; gathers counted at their logical size, so
@@ -770,9 +783,17 @@ def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0
     dom = max(phase_ms, key=phase_ms.get)
     t = phase_ms[dom] / 1000.0
     achieved = algo.get(dom, 0.0) / t / 1e9 if t > 0 else 0.0
+    traffic = None
+    measured = SFNN_DRAM_BYTES_B65536.get(dom)
+    if measured is not None and batch == SFNN_BATCH and qat in measured[1]:
+        traffic = measured[0]
+    launches = 15 if dom == "ft_rows_ranger" else 1
     return {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind, "traffic": None,
-            "algorithmic_bytes_per_launch": int(algo.get(dom, 0.0)), "launch_ms": round(phase_ms[dom], 4),
+            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind, "traffic": traffic,
+            "traffic_note": "DRAM bytes of the phase per step (ncu, profiles/); algorithmic bytes count the "
+                            "logical row gathers, which L2 serves, so traffic is far below them",
+            "launches_per_step": launches,
+            "algorithmic_bytes_per_step": int(algo.get(dom, 0.0)), "kernel_ms_per_step": round(phase_ms[dom], 4),
             "phase_ms": {k: round(v, 4) for k, v in phase_ms.items()}}
 
 

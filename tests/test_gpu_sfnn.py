@@ -295,3 +295,25 @@ def test_train_step_rejects_norm_loss_and_bad_layout(ctx):
     runner = bs.SfnnTrainStepRunner(ctx, _host_weights(shape, w), 16, 40)
     with pytest.raises(bo.CudaCppError, match="layout mismatch"):
         runner.step(ctx, _params(1), bo.ScalarLossKind.SigmoidPow(2.0), 1.0, _host_batch(_batch(1, 8, 4)))
+
+
+def test_k9k9_zipf_fused_vs_reference_backend(ctx, ref_ctx):
+    """configs[4]'s LayerStack: 81 buckets, Zipf(1.1)-skewed bucket ids (a
+    seeded permutation of ranks), 20 steps of the fused step against the
+    reference backend, weights within 1e-3."""
+    shape = bs.SfnnForwardShape(HM2F, 1536, 15, True, 32, 81)
+    w = _weights(shape, 93, std=0.01)
+    B = 4096
+    ours = bs.SfnnTrainStepRunner(ctx, _host_weights(shape, w), B, 40)
+    ref = bs.SfnnTrainStepRunner(ref_ctx, _host_weights(shape, w), B, 40)
+    batches = [_host_batch(synthetic.sfnn_batch(500 + i, B, stacks=81, zipf=1.1)) for i in range(4)]
+    counts = np.bincount(np.concatenate([b.buckets for b in batches]), minlength=81)
+    assert counts.max() > 8 * max(1, counts[counts > 0].min())      # skewed
+    for step in range(1, 21):
+        hb = batches[step % len(batches)]
+        for r, c in ((ours, ctx), (ref, ref_ctx)):
+            r.step_no_readback(c, _params(step), bo.ScalarLossKind.SigmoidPow(2.0), 1 / 600, hb)
+    a, c = ours.read_weights(ctx), ref.read_weights(ref_ctx)
+    for nm in a:
+        err = float(np.abs(a[nm].astype(np.float64) - c[nm]).max())
+        assert err <= 1e-3, f"{nm}: max |diff| {err:.3e} after 20 steps"
