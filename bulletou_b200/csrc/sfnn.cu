@@ -584,10 +584,18 @@ struct L1IntArgs {
     int stacks;
 };
 
-// O = 16: thread (sample lane, output quad), the tile's integer weights in
-// shared memory as [width][16] (int4 reads).
+__device__ __forceinline__ int dp4a_u8s8(unsigned u8x4, int s8x4, int acc) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(u8x4), "r"(s8x4), "r"(acc));
+    return d;
+}
+
+// O = 16: thread (sample lane, output quad).  The tile's integer weights sit
+// in shared memory packed for dp4a: entry (k4, quad) is an int4 whose word j
+// holds the four i8 weights of inputs 4 k4 .. 4 k4 + 3 for output 4 quad + j;
+// the lattice FT outputs (0..127) are packed four to a word on the fly.
 __global__ void __launch_bounds__(256) l1_forward16_int_kernel(L1IntArgs a) {
-    extern __shared__ int4 wi4[];
+    extern __shared__ int4 wq4[];
     const int t = blockIdx.x;
     if (t >= *a.tiles.n_tiles) return;
     const int s = a.tiles.key[t];
@@ -600,30 +608,37 @@ __global__ void __launch_bounds__(256) l1_forward16_int_kernel(L1IntArgs a) {
         }
         return;
     }
-    const float4* src = reinterpret_cast<const float4*>(a.w_eff + static_cast<size_t>(s) * a.width * 16);
-    for (int i = threadIdx.x; i < a.width * 4; i += blockDim.x) {
-        const float4 w = src[i];
-        wi4[i] = make_int4(qat_int64(w.x), qat_int64(w.y), qat_int64(w.z), qat_int64(w.w));
+    const int w4 = a.width >> 2;
+    const float* src = a.w_eff + static_cast<size_t>(s) * a.width * 16;  // [width][16]
+    for (int i = threadIdx.x; i < w4 * 4; i += blockDim.x) {
+        const int k4 = i >> 2, quad = i & 3;
+        int word[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            unsigned packed = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                packed |= (static_cast<unsigned>(qat_int64(src[(4 * k4 + e) * 16 + 4 * quad + j])) & 0xffu) << (8 * e);
+            word[j] = static_cast<int>(packed);
+        }
+        wq4[i] = make_int4(word[0], word[1], word[2], word[3]);
     }
     __syncthreads();
     const int og = threadIdx.x & 3;
-    const int w4 = a.width >> 2;
     for (int p = pb + (threadIdx.x >> 2); p < pe; p += 64) {
         const int b = a.tiles.order[p];
         const float4* c4 = reinterpret_cast<const float4*>(a.combined) + static_cast<size_t>(b) * w4;
-        // |sum| <= width * 127 * 128 < 2^31 for every width this backend accepts (<= 8192).
         int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
         for (int k4 = 0; k4 < w4; ++k4) {
             const float4 c = __ldg(c4 + k4);
-            const int cv[4] = {qat_int127(c.x), qat_int127(c.y), qat_int127(c.z), qat_int127(c.w)};
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const int4 w = wi4[(4 * k4 + kk) * 4 + og];
-                acc0 += cv[kk] * w.x;
-                acc1 += cv[kk] * w.y;
-                acc2 += cv[kk] * w.z;
-                acc3 += cv[kk] * w.w;
-            }
+            const unsigned cv = static_cast<unsigned>(qat_int127(c.x)) | (static_cast<unsigned>(qat_int127(c.y)) << 8) |
+                                (static_cast<unsigned>(qat_int127(c.z)) << 16) |
+                                (static_cast<unsigned>(qat_int127(c.w)) << 24);
+            const int4 w = wq4[k4 * 4 + og];
+            acc0 = dp4a_u8s8(cv, w.x, acc0);
+            acc1 = dp4a_u8s8(cv, w.y, acc1);
+            acc2 = dp4a_u8s8(cv, w.z, acc2);
+            acc3 = dp4a_u8s8(cv, w.w, acc3);
         }
         const int accs[4] = {acc0, acc1, acc2, acc3};
 #pragma unroll
@@ -1824,7 +1839,7 @@ int launch_l1_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const Sfnn
         ia.width = d.width;
         ia.out_dim = d.l1_out;
         ia.stacks = d.stacks;
-        const size_t smem = static_cast<size_t>(d.width) * 16 * sizeof(int);
+        const size_t smem = static_cast<size_t>(d.width) * 4 * sizeof(int);
         if (d.l1_out == 16 && d.width % 4 == 0 && smem <= 200 * 1024 && aligned16(combined)) {
             cudaError_t st = cudaFuncSetAttribute(l1_forward16_int_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   static_cast<int>(smem));
