@@ -110,6 +110,8 @@ def parse_args():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--workload", choices=("sfnn", "halfkp"), default="sfnn")
     ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--dp-chunk-launches", type=int, default=3,
+                    help="N > 1: FT row launches per exchanged chunk (SFNN)")
     ap.add_argument("--qat", choices=tuple(SFNN_QAT_MODES), default="all",
                     help="SFNN quantisation-aware training mode (both arms)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -411,8 +413,8 @@ def run_reference(args, local):
 
 # --------------------------------------------------------------------------- roofline
 def roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0):
-    """Algorithmic bytes per launch of each phase (the formulas are written
-    out in DESIGN.md); the dominant phase is reported."""
+    """Algorithmic bytes per launch of each phase (formulas below); the
+    dominant phase is reported."""
     rows, width = SHAPE[0], SHAPE[1]
     entries = 2 * batch * ACTIVE
     algo = {
@@ -605,7 +607,8 @@ def run_sfnn_data_parallel(args, rank, world, local, dist):
     backend = B200Backend(local)
     ctx, lib = backend.ctx, backend.lib
     tr = SfnnDataParallelTrainer(backend, dist, sfnn_host_weights(), args.batch, SFNN_ACTIVE,
-                                 lr_multipliers=sfnn_lr_multipliers(args.qat))
+                                 lr_multipliers=sfnn_lr_multipliers(args.qat),
+                                 launches_per_chunk=args.dp_chunk_launches)
     batches = make_sfnn_batches(args.batch, rank)
     devb = sfnn_device_batches(ctx, batches)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
@@ -629,6 +632,7 @@ def run_sfnn_data_parallel(args, rank, world, local, dist):
             step += 1
             bind(i)
             tr.step_device(ranger(step), loss_kind, inv, finalize_loss=False)
+        tr.join()  # the last step's exchange runs on the comm stream
         stop.record(ctx)
         stop.synchronize()
     phase_ms = _profile(lib, ctx, sfnn_phases(args.qat))
@@ -664,6 +668,7 @@ def run_sfnn_data_parallel(args, rank, world, local, dist):
         h2d = 4 * sum(x.length for x in p)
         tr.step_device(ranger(step), loss_kind, inv, finalize_loss=True)
         lib.call("bulletou_b200_f32_download_pinned", c, ring[i].as_ptr(), tr.loss_workspace.mean.as_ptr(), 1)
+    tr.join()
     e1.record(ctx)
     e1.synchronize()
     wall_ms = (time.perf_counter() - t0) * 1000.0
@@ -737,9 +742,9 @@ def run_sfnn_reference(args, local):
 
 
 # DRAM bytes per step of each phase at B = 65536 (dram__bytes_read.sum +
-# dram__bytes_write.sum over the phase's launches), from the full-size capture
-# summarised in profiles/sfnn_train_step_b65536.md; keyed by the QAT modes
-# whose kernels they were measured on.
+# dram__bytes_write.sum over the phase's launches), from a full-size ncu
+# capture of `bench.py --steps 1 --warmup 3`; keyed by the QAT modes whose
+# kernels they were measured on.
 SFNN_DRAM_BYTES_B65536 = {
     "ft_rows_ranger": (4813480704, ("none", "l1", "layers", "dense", "all")),
     "ft_forward": (1679058432, ("none", "l1", "dense", "all")),
@@ -790,7 +795,7 @@ def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0
     launches = 15 if dom == "ft_rows_ranger" else 1
     return {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind, "traffic": traffic,
-            "traffic_note": "DRAM bytes of the phase per step (ncu, profiles/); algorithmic bytes count the "
+            "traffic_note": "DRAM bytes of the phase per step (ncu capture); algorithmic bytes count the "
                             "logical row gathers, which L2 serves, so traffic is far below them",
             "launches_per_step": launches,
             "algorithmic_bytes_per_step": int(algo.get(dom, 0.0)), "kernel_ms_per_step": round(phase_ms[dom], 4),

@@ -152,7 +152,8 @@ SIGNATURES: dict[str, list] = {
         + [I] + [I] * 6 + [F] * 6 + [P] * 2 + [P] + [P] * 8 + [P] * 20 + [I] + [P]),
     "bulletou_b200_sfnn_train_step_device": [P, P, Z, Z] + [P] * 17,
     "bulletou_b200_sfnn_dense_gradient_len": [P, I, I, I, P],
-    "bulletou_b200_sfnn_local_gradients_device": [P, P, Z, Z] + [P] * 15,
+    "bulletou_b200_sfnn_local_gradients_device": [P, P, Z, Z] + [P] * 17 + [Z],
+    "bulletou_b200_sfnn_row_launches": [P, P, P, Z],
     # SFNN QAT (reference entries)
     "bulletou_layer_qat": [P, P, P, F, F, F, Z, Z, Z, F],
     "bulletou_layer_qat_nonzero": [P, P, P, P],

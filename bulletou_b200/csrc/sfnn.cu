@@ -1509,26 +1509,48 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 size_t align_floats(size_t n) { return (n + 63) & ~static_cast<size_t>(63); }
 
+// Row ranges each launch of the FT row kernel completes: launch j writes the
+// rows of king blocks [3 j, 3 j + 3), the last one also the virtual rows.
+// Returns the launch count; row_end[j] = first row after launch j (if given).
+int piece_row_launches(const SfnnDims& d, size_t* row_end, size_t cap) {
+    const int kings = d.base > 0 ? d.base / kSfnnPieces : 1;
+    const int n = (kings + kKingsPerLaunch - 1) / kKingsPerLaunch;
+    for (int j = 0; j < n && row_end != nullptr && static_cast<size_t>(j) < cap; ++j)
+        row_end[j] = (j == n - 1) ? static_cast<size_t>(d.input_size)
+                                  : static_cast<size_t>(kKingsPerLaunch) * (j + 1) * kSfnnPieces;
+    return n;
+}
+
 template <int MODE>
-int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec) {
+int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec, const size_t* row_shift,
+                           const cudaEvent_t* events) {
     // Persistent grid: three CTAs per SM, each warp loops over (piece, column
     // group) work items.
     const int warps = a.pieces * a.col_groups;
     const int blocks = std::max(1, std::min((warps + kPieceRowWarps - 1) / kPieceRowWarps, 3 * ctx->sm_count));
-    for (int k0 = 0; k0 < a.kings; k0 += kKingsPerLaunch) {
+    float* const gradients = a.gradients;
+    for (int k0 = 0, j = 0; k0 < a.kings; k0 += kKingsPerLaunch, ++j) {
         a.king_begin = k0;
         a.king_end = std::min(a.kings, k0 + kKingsPerLaunch);
         a.first_launch = k0 == 0;
         a.last_launch = a.king_end == a.kings;
+        // Data-parallel layout: launch j's rows land row_shift[j] rows further,
+        // so each launch's range starts a chunk the collectives can split evenly.
+        if (row_shift != nullptr) a.gradients = gradients + row_shift[j] * static_cast<size_t>(a.width);
         if (vec == 8) piece_row_kernel<8, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
         else if (vec == 4) piece_row_kernel<4, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
         else piece_row_kernel<1, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
         if (check_launch("SFNN FT row kernel launch") != 0) return -1;
+        if (events != nullptr) {
+            cudaError_t st = cudaEventRecord(events[j], ctx->stream);
+            if (st != cudaSuccess) return fail("cudaEventRecord SFNN row launch", st);
+        }
     }
     return 0;
 }
 
-int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a) {
+int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, const size_t* row_shift = nullptr,
+                      const cudaEvent_t* events = nullptr) {
     bool al = aligned16(a.src[0]) && aligned16(a.src[1]) && a.src_stride % 4 == 0;
     if (mode == kRowRanger)
         al = al && aligned16(a.weights) && aligned16(a.momentum) && aligned16(a.velocity) && aligned16(a.slow);
@@ -1555,9 +1577,9 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a) {
         a.vany = reinterpret_cast<int*>(a.vacc + vf);
     }
     switch (mode) {
-        case kRowRanger: return launch_piece_rows_mode<kRowRanger>(ctx, a, vec);
-        case kRowWrite: return launch_piece_rows_mode<kRowWrite>(ctx, a, vec);
-        default: return launch_piece_rows_mode<kRowAccumulate>(ctx, a, vec);
+        case kRowRanger: return launch_piece_rows_mode<kRowRanger>(ctx, a, vec, row_shift, events);
+        case kRowWrite: return launch_piece_rows_mode<kRowWrite>(ctx, a, vec, row_shift, events);
+        default: return launch_piece_rows_mode<kRowAccumulate>(ctx, a, vec, row_shift, events);
     }
 }
 
@@ -2103,7 +2125,8 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
               const int* buckets, const float* targets, const float* entry_weights, const LossArgs& la, int finalize,
               const BulletOuB200RangerStep* ranger, float* const* wm, float* const* mm, float* const* vm,
               float* const* sm, float* output, float* per_sample, float* mog, float* weighted_sum, float* mean,
-              float* ft_grad, float* dense_grad) {
+              float* ft_grad, float* dense_grad, const size_t* row_shift = nullptr,
+              const cudaEvent_t* row_events = nullptr) {
     ctx->prof_marks_per_step = (d.qat.dense && d.qat.integer_ft) ? 10 : 9;
     prof_mark(ctx);
     SfnnPlan plan{};
@@ -2177,7 +2200,7 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
         if (launch_piece_rows(ctx, kRowRanger, r) != 0) return -1;
     } else {
         r.gradients = ft_grad;
-        if (launch_piece_rows(ctx, kRowWrite, r) != 0) return -1;
+        if (launch_piece_rows(ctx, kRowWrite, r, row_shift, row_events) != 0) return -1;
     }
     prof_mark(ctx);
     return 0;
@@ -2536,7 +2559,8 @@ int bulletou_b200_sfnn_local_gradients_device(
     BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* ft_gradients,
     BulletOuCudaCppF32Buffer* dense_gradients, BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
     BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
-    BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat) {
+    BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat, const size_t* row_shift,
+    BulletOuCudaCppEvent* const* row_events, size_t n_row_launches) {
     if (shape == nullptr || params == nullptr) return fail_message("SFNN shape / parameter array must not be null");
     SfnnDims d{};
     LossArgs la{};
@@ -2554,20 +2578,47 @@ int bulletou_b200_sfnn_local_gradients_device(
         validate_i32(ctx, nstm_indices, batch * max_active, "nstm_indices") != 0 ||
         validate_i32(ctx, buckets, batch, "buckets") != 0 || validate_f32(ctx, targets, batch, "targets") != 0 ||
         validate_f32(ctx, entry_weights, batch, "entry_weights") != 0 ||
-        validate_f32(ctx, ft_gradients, static_cast<size_t>(d.input_size) * d.width, "ft_gradients") != 0 ||
+        validate_f32(ctx, ft_gradients,
+                     (static_cast<size_t>(d.input_size) +
+                      (row_shift != nullptr ? row_shift[piece_row_launches(d, nullptr, 0) - 1] : 0)) * d.width,
+                     "ft_gradients") != 0 ||
         validate_f32(ctx, dense_gradients, g.begin[kSfGroups], "dense_gradients") != 0 ||
         validate_f32(ctx, output, batch, "output") != 0 || validate_f32(ctx, per_sample, batch, "per_sample") != 0 ||
         validate_f32(ctx, mean_output_gradients, batch, "mean_output_gradients") != 0 ||
         validate_f32(ctx, weighted_sum, 1, "weighted_sum") != 0 || validate_f32(ctx, mean, 1, "mean") != 0)
         return -1;
+    const int launches = piece_row_launches(d, nullptr, 0);
+    if ((row_shift != nullptr || row_events != nullptr) && n_row_launches != static_cast<size_t>(launches))
+        return fail_messagef("SFNN local gradients: %d row launches, got %zu shifts / events", launches,
+                             n_row_launches);
+    cudaEvent_t events[64];
+    if (row_events != nullptr) {
+        if (launches > 64) return fail_message("SFNN local gradients: too many row launches for events");
+        for (int j = 0; j < launches; ++j) {
+            if (row_events[j] == nullptr || row_events[j]->device != ctx->device)
+                return fail_message("SFNN local gradients: row event missing or on another device");
+            events[j] = row_events[j]->event;
+        }
+    }
     if (set_device(ctx) != 0) return -1;
     const SfnnWeights w = weights_from(params);
     if (apply_qat(qat, w, &d) != 0) return -1;
     if (sfnn_step(ctx, d, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr, targets->ptr, entry_weights->ptr, la,
                   loss->finalize_loss, nullptr, nullptr, nullptr, nullptr, nullptr, output->ptr, per_sample->ptr,
-                  mean_output_gradients->ptr, weighted_sum->ptr, mean->ptr, ft_gradients->ptr,
-                  dense_gradients->ptr) != 0)
+                  mean_output_gradients->ptr, weighted_sum->ptr, mean->ptr, ft_gradients->ptr, dense_gradients->ptr,
+                  row_shift, row_events != nullptr ? events : nullptr) != 0)
         return -1;
+    return ok();
+}
+
+int bulletou_b200_sfnn_row_launches(const BulletOuB200SfnnShape* shape, size_t* n_launches, size_t* row_end,
+                                    size_t cap) {
+    if (shape == nullptr || n_launches == nullptr) return fail_message("SFNN row launches: null argument");
+    SfnnDims d{};
+    if (sfnn_dims(shape->input_size, shape->ft_size, shape->l1_hidden, shape->l1_skip, shape->l2_size,
+                  shape->num_stacks, 1, 1, shape->ft_factorizer_alpha, shape->factorizer_shared_alpha, &d) != 0)
+        return -1;
+    *n_launches = static_cast<size_t>(piece_row_launches(d, row_end, cap));
     return ok();
 }
 

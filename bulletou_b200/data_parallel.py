@@ -2,7 +2,7 @@
 
 The reference trains on one GPU (no collectives, cu:9503-9545); this module is
 the additive multi-GPU layer.  Positions are independent, so the only
-exchange is the gradient sum (SURVEY 8e):
+exchange is the gradient sum:
 
     local step      forward + loss + backward of the rank's batch, the loss
                     gradient normalised by the *global* batch
@@ -34,6 +34,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass
+from typing import Optional
 
 import numpy as np
 
@@ -116,25 +117,68 @@ class B200Backend:
                       tr.ft_grad.as_ptr(), tr.dense_grad.as_ptr(), tr.output.as_ptr(), lw.per_sample.as_ptr(),
                       lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(), lw.mean.as_ptr())
 
-    def sfnn_local_gradients(self, tr: "SfnnDataParallelTrainer", loss_spec) -> None:
+    @staticmethod
+    def _sfnn_shape(sh, alpha):
         from ._lib import SfnnShape
 
-        sh = tr.shape
-        shape = SfnnShape(sh.input_size, sh.ft_size, sh.l1_hidden, int(sh.l1_skip), sh.l2_size, sh.num_stacks,
-                          tr.alpha.ft, tr.alpha.shared)
+        return SfnnShape(sh.input_size, sh.ft_size, sh.l1_hidden, int(sh.l1_skip), sh.l2_size, sh.num_stacks,
+                         alpha.ft, alpha.shared)
+
+    def sfnn_row_launches(self, sh, alpha) -> list:
+        shape = self._sfnn_shape(sh, alpha)
+        n = ctypes.c_size_t()
+        ends = (ctypes.c_size_t * 256)()
+        self.lib.call("bulletou_b200_sfnn_row_launches", ctypes.byref(shape), ctypes.byref(n), ends, 256)
+        return [int(ends[j]) for j in range(n.value)]
+
+    def sfnn_local_gradients(self, tr: "SfnnDataParallelTrainer", loss_spec, events=None) -> None:
+        shape = self._sfnn_shape(tr.shape, tr.alpha)
         arr = ctypes.c_void_p * 14
         params = arr(*[(None if w is None else w.as_ptr().value) for w in tr.weight_list()])
         lw = tr.loss_workspace
         qat = tr.lr_multipliers.as_struct()
+        n = len(tr.row_ends)
+        shifts = (ctypes.c_size_t * n)(*[tr.chunks[tr.launch_chunk[j]].shift for j in range(n)])
         self.lib.call("bulletou_b200_sfnn_local_gradients_device", self.ctx.as_ptr(), ctypes.byref(shape),
                       tr.batch_size, tr.max_active, tr.stm_indices.as_ptr(), tr.nstm_indices.as_ptr(),
                       tr.buckets.as_ptr(), tr.targets.as_ptr(), tr.entry_weights.as_ptr(), ctypes.byref(loss_spec),
                       params, tr.ft_grad.as_ptr(), tr.dense_grad.as_ptr(), tr.output.as_ptr(),
                       lw.per_sample.as_ptr(), lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(),
-                      lw.mean.as_ptr(), ctypes.byref(qat))
+                      lw.mean.as_ptr(), ctypes.byref(qat), shifts, events, n)
 
-    def ranger(self, params: RangerUpdateParams, grad, weights, m, v, slow) -> None:
-        ranger_update_device(self.ctx, params, RangerDeviceState(grad, weights, m, v, slow))
+    # -- overlapped exchange (SfnnDataParallelTrainer) --------------------------
+    supports_overlap = True
+
+    def prepare_overlap(self, tr: "SfnnDataParallelTrainer") -> None:
+        from . import cuda_cpp as cc
+
+        tr._comm = self.torch.cuda.Stream(device=self.device)
+        tr._comm_ctx = cc.Context(self.device, self.lib, stream=tr._comm.cuda_stream)
+        tr._events = [cc.Event(self.ctx) for _ in tr.row_ends]
+        tr._event_handles = (ctypes.c_void_p * len(tr.row_ends))(*[e._h.value for e in tr._events])
+
+    def sfnn_step_overlapped(self, tr: "SfnnDataParallelTrainer", loss_spec, params) -> None:
+        """Local step on the library's stream; per chunk, on the comm stream:
+        wait for the launch that completes it, reduce-scatter, Ranger on the
+        owned rows, all-gather.  The small groups' all-reduce and Ranger go
+        first (their gradients precede the row launches)."""
+        torch = self.torch
+        compute = torch.cuda.current_stream(self.device)
+        compute.wait_stream(tr._comm)  # the previous exchange wrote weights this step reads
+        self.sfnn_local_gradients(tr, loss_spec, tr._event_handles)
+        with torch.cuda.stream(tr._comm):
+            tr._events[0].wait(tr._comm_ctx)
+            tr._small_exchange(params, tr._comm_ctx)
+            for j in range(len(tr.chunks)):
+                last_launch = min(len(tr.row_ends), (j + 1) * tr.launches_per_chunk) - 1
+                tr._events[last_launch].wait(tr._comm_ctx)
+                tr._chunk_exchange(j, params, tr._comm_ctx)
+
+    def join_overlap(self, tr: "SfnnDataParallelTrainer") -> None:
+        self.torch.cuda.current_stream(self.device).wait_stream(tr._comm)
+
+    def ranger(self, params: RangerUpdateParams, grad, weights, m, v, slow, ctx=None) -> None:
+        ranger_update_device(ctx or self.ctx, params, RangerDeviceState(grad, weights, m, v, slow))
 
     def view(self, buf: F32Buffer, offset: int, length: int) -> F32Buffer:
         return buf.view(offset, length)
@@ -231,11 +275,50 @@ def sfnn_dense_gradient_layout(shape, present: dict) -> list[tuple[str, int, int
     return out
 
 
+@dataclass(frozen=True)
+class RowChunk:
+    """One launch's FT rows in the data-parallel layout: table rows
+    [start, start + length) sit at gradient rows start + shift ..., padded to
+    `padded` rows (a multiple of the world size); each rank owns padded / world
+    of them, stored from row `shard_off` of its compact shard."""
+
+    start: int
+    length: int
+    padded: int
+    shift: int
+    shard_off: int
+    shard_rows: int
+
+
+def sfnn_row_chunks(row_ends: list, world: int, launches_per_chunk: int = 1) -> list:
+    """Chunks of `launches_per_chunk` consecutive row launches (the last may
+    hold fewer)."""
+    chunks, shift, off, start = [], 0, 0, 0
+    ends = [row_ends[min(len(row_ends), i + launches_per_chunk) - 1]
+            for i in range(0, len(row_ends), launches_per_chunk)]
+    for end in ends:
+        length = end - start
+        padded = -(-length // world) * world
+        chunks.append(RowChunk(start, length, padded, shift, off, padded // world))
+        shift += padded - length
+        off += padded // world
+        start = end
+    return chunks
+
+
 class SfnnDataParallelTrainer:
-    """One rank of data-parallel SFNN training (default layer multipliers)."""
+    """One rank of data-parallel SFNN training (default layer multipliers).
+
+    The FT gradient rows come from a sequence of row-kernel launches, each
+    completing a contiguous range of rows (a few king blocks).  Each range is a
+    chunk of its own, padded to a multiple of the world size: the chunk is
+    reduce-scattered, the owned part updated by Ranger and all-gathered back,
+    chunk by chunk.  On the GPU the chunks' collectives and updates run on a
+    second stream, each starting when its launch has finished (an event the
+    library records), so the exchange overlaps the remaining launches."""
 
     def __init__(self, backend, dist, initial_weights, batch_size: int, max_active: int, alpha=None,
-                 lr_multipliers=None):
+                 lr_multipliers=None, overlap: Optional[bool] = None, launches_per_chunk: int = 3):
         from .sfnn import SFNN_WEIGHT_NAMES, SfnnFactorizerAlpha, SfnnLayerLrMultipliers
 
         initial_weights.validate()
@@ -249,22 +332,34 @@ class SfnnDataParallelTrainer:
         self.batch_size, self.max_active = batch_size, max_active
         sh = self.shape
         W = sh.ft_size
-        self.layout = ShardLayout(sh.input_size, W, self.world, self.rank)
-        lay = self.layout
+        self.row_ends = backend.sfnn_row_launches(sh, self.alpha)
+        self.launches_per_chunk = max(1, int(launches_per_chunk))
+        self.chunks = sfnn_row_chunks(self.row_ends, self.world, self.launches_per_chunk)
+        # launch j belongs to chunk j // launches_per_chunk
+        self.launch_chunk = [j // self.launches_per_chunk for j in range(len(self.row_ends))]
+        last = self.chunks[-1]
+        grad_rows = last.start + last.shift + last.padded
+        l0w_rows = last.start + last.padded  # a chunk's all-gather writes its padded length
+        shard_rows = last.shard_off + last.shard_rows
         arrays = initial_weights.arrays()
         self.present = {n: arrays[n] is not None for n in SFNN_WEIGHT_NAMES}
-        l0w = np.zeros(lay.rows_padded * W, np.float32)
+        l0w = np.zeros(l0w_rows * W, np.float32)
         l0w[: arrays["l0w"].size] = arrays["l0w"]
+        compact = np.zeros(shard_rows * W, np.float32)
+        for c in self.chunks:
+            r0 = c.start + self.rank * c.shard_rows
+            n_real = max(0, min(c.shard_rows, c.start + c.length - r0))
+            compact[c.shard_off * W:(c.shard_off + n_real) * W] = l0w[r0 * W:(r0 + n_real) * W]
         self.weights = {"l0w": backend.from_host(l0w)}
         for n in SFNN_WEIGHT_NAMES[1:]:
             self.weights[n] = None if arrays[n] is None else backend.from_host(arrays[n])
-        own = slice(lay.row_begin * W, (lay.row_begin + lay.real_rows) * W)
-        n_own = lay.real_rows * W
-        self.ft_state = (backend.zeros(n_own), backend.zeros(n_own), backend.from_host(l0w[own]))
+        self.l0w_compact = backend.from_host(compact)
+        self.ft_state = (backend.zeros(shard_rows * W), backend.zeros(shard_rows * W), backend.from_host(compact))
         self.dense_layout = sfnn_dense_gradient_layout(sh, self.present)
         self.small_state = {n: (backend.zeros(arrays[n].size), backend.zeros(arrays[n].size), backend.from_host(arrays[n]))
                             for n, _, _ in self.dense_layout}
-        self.ft_grad = backend.zeros(lay.rows_padded * W)
+        self.ft_grad = backend.zeros(grad_rows * W)
+        self.ft_grad_shard = backend.zeros(shard_rows * W)
         total = self.dense_layout[-1][1] + self.dense_layout[-1][2]
         self.dense_grad = backend.zeros(total)
         ctx = getattr(backend, "ctx", None)
@@ -275,12 +370,19 @@ class SfnnDataParallelTrainer:
             self.targets, self.entry_weights = F32Buffer(ctx, batch_size), F32Buffer(ctx, batch_size)
             self.output = F32Buffer(ctx, batch_size)
             self.loss_workspace = ScalarLossWorkspace(ctx, batch_size)
-        self.ft_grad_shard = backend.view(self.ft_grad, lay.row_begin * W, lay.real_rows * W)
-        self.l0w_shard = backend.view(self.weights["l0w"], lay.row_begin * W, lay.real_rows * W)
+        m, v, slow = self.ft_state
+        self.chunk_views = [tuple(backend.view(b, c.shard_off * W, c.shard_rows * W)
+                                  for b in (self.ft_grad_shard, self.l0w_compact, m, v, slow))
+                            for c in self.chunks]
         self.dense_views = {name: backend.view(self.dense_grad, off, k) for name, off, k in self.dense_layout}
         self._t_ft_grad = backend.tensor(self.ft_grad)
+        self._t_shard = backend.tensor(self.ft_grad_shard)
         self._t_l0w = backend.tensor(self.weights["l0w"])
+        self._t_compact = backend.tensor(self.l0w_compact)
         self._t_dense = backend.tensor(self.dense_grad)
+        self.overlap = bool(getattr(backend, "supports_overlap", False)) if overlap is None else bool(overlap)
+        if self.overlap:
+            backend.prepare_overlap(self)
 
     def weight_list(self) -> list:
         from .sfnn import SFNN_WEIGHT_NAMES
@@ -294,34 +396,54 @@ class SfnnDataParallelTrainer:
         self.targets.upload(targets)
         self.entry_weights.upload(entry_weights)
 
-    def exchange_and_update(self, params: RangerUpdateParams) -> None:
+    def _params(self, params: RangerUpdateParams) -> RangerUpdateParams:
         from dataclasses import replace
 
+        return replace(params, norm_loss_strength=0.0, norm_loss_before=False)  # lib.rs:6416-6420
+
+    def _chunk_exchange(self, j: int, params: RangerUpdateParams, ctx=None) -> None:
+        """Reduce-scatter chunk j, Ranger on the owned part, all-gather it back."""
+        c, W = self.chunks[j], self.shape.ft_size
+        g0 = (c.start + c.shift) * W
+        s0 = c.shard_off * W
+        self.dist.reduce_scatter_tensor(self._t_shard[s0:s0 + c.shard_rows * W],
+                                        self._t_ft_grad[g0:g0 + c.padded * W])
+        grad, w, m, v, slow = self.chunk_views[j]
+        self.backend.ranger(params, grad, w, m, v, slow, ctx)
+        self.dist.all_gather_into_tensor(self._t_l0w[c.start * W:(c.start + c.padded) * W],
+                                         self._t_compact[s0:s0 + c.shard_rows * W])
+
+    def _small_exchange(self, params: RangerUpdateParams, ctx=None) -> None:
         from .sfnn import factor_contribution_clip
 
-        params = replace(params, norm_loss_strength=0.0, norm_loss_before=False)  # lib.rs:6416-6420
-        lay, W = self.layout, self.shape.ft_size
-        chunk = lay.shard_rows * W
-        shard_t = self._t_ft_grad[self.rank * chunk:(self.rank + 1) * chunk]
-        self.dist.reduce_scatter_tensor(shard_t, self._t_ft_grad)
         self.dist.all_reduce(self._t_dense)
-        if lay.real_rows > 0:
-            m, v, slow = self.ft_state
-            self.backend.ranger(params, self.ft_grad_shard, self.l0w_shard, m, v, slow)
         for name, _, _ in self.dense_layout:
             p = factor_contribution_clip(params, self.alpha.shared) if name in ("l1fw", "l1fb") else params
             m, v, slow = self.small_state[name]
-            self.backend.ranger(p, self.dense_views[name], self.weights[name], m, v, slow)
-        own_t = self._t_l0w[self.rank * chunk:(self.rank + 1) * chunk]
-        self.dist.all_gather_into_tensor(self._t_l0w, own_t)
+            self.backend.ranger(p, self.dense_views[name], self.weights[name], m, v, slow, ctx)
+
+    def exchange_and_update(self, params: RangerUpdateParams) -> None:
+        params = self._params(params)
+        self._small_exchange(params)
+        for j in range(len(self.chunks)):
+            self._chunk_exchange(j, params)
 
     def step_device(self, params: RangerUpdateParams, loss_kind: ScalarLossKind, output_inv_scale: float,
                     finalize_loss: bool = True) -> None:
         spec = loss_kind.spec(output_inv_scale, finalize_loss, normalizer=self.batch_size * self.world)
+        if self.overlap:
+            self.backend.sfnn_step_overlapped(self, spec, self._params(params))
+            return
         self.backend.sfnn_local_gradients(self, spec)
         self.exchange_and_update(params)
 
+    def join(self) -> None:
+        """Makes the library's stream wait for this rank's outstanding exchange."""
+        if self.overlap:
+            self.backend.join_overlap(self)
+
     def read_weights(self) -> dict:
+        self.join()
         out = {n: self.backend.download(w) for n, w in self.weights.items() if w is not None}
         out["l0w"] = out["l0w"][: self.shape.input_size * self.shape.ft_size]
         return out

@@ -260,9 +260,16 @@ int bulletou_b200_sfnn_dense_gradient_len(const BulletOuB200SfnnShape* shape, in
  * batch (the loss normalizer in `loss` is the global batch).  Overwrites
  * ft_gradients [input_size*ft_size, virtual factor rows included] with the
  * batch's FT gradient and dense_gradients [sfnn_dense_gradient_len] with the
- * packed small-parameter gradient; params as in sfnn_train_step_device.
- * The exchange (reduce-scatter / all-reduce) and the update
- * (ranger_update_device on views) are the caller's. */
+ * packed small-parameter gradient; params and qat as in
+ * sfnn_train_step_device.  The exchange (reduce-scatter / all-reduce) and the
+ * update (ranger_update_device on views) are the caller's.
+ * The FT gradient rows are written by n_row_launches kernel launches, launch j
+ * completing rows [row_end[j-1], row_end[j]) (bulletou_b200_sfnn_row_launches).
+ * Optional row_shift[j]: launch j writes its rows row_shift[j] rows further
+ * into ft_gradients (so each range can start a padded chunk); optional
+ * row_events[j] is recorded on the context stream after launch j, so a
+ * collective on another stream can start on that range while later launches
+ * run.  Both null: rows at their own index, no events. */
 int bulletou_b200_sfnn_local_gradients_device(
     BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
     const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
@@ -271,7 +278,13 @@ int bulletou_b200_sfnn_local_gradients_device(
     BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* ft_gradients,
     BulletOuCudaCppF32Buffer* dense_gradients, BulletOuCudaCppF32Buffer* output,
     BulletOuCudaCppF32Buffer* per_sample, BulletOuCudaCppF32Buffer* mean_output_gradients,
-    BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat);
+    BulletOuCudaCppF32Buffer* weighted_sum, BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat,
+    const size_t* row_shift, BulletOuCudaCppEvent* const* row_events, size_t n_row_launches);
+
+/* The FT row kernel's launches for a shape: *n_launches, and row_end[j] (up
+ * to cap entries) = first row after launch j. */
+int bulletou_b200_sfnn_row_launches(const BulletOuB200SfnnShape* shape, size_t* n_launches, size_t* row_end,
+    size_t cap);
 
 /* ---------------------------------------------------------------- quantised HalfKP
  * The reference exports a trained HalfKP 256x2-32-32 net to the engine's

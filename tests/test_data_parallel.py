@@ -76,11 +76,20 @@ class CpuOracleBackend:
         g = oracle.sfnn_backward(*args, fwd, w, loss["mean_output_gradients"], tr.alpha.ft, tr.alpha.shared,
                                  qat=qat)
         tr.ft_grad.zero_()
-        tr.ft_grad[: sh.input_size * sh.ft_size] = torch.from_numpy(g["l0w_gradients"])
+        W = sh.ft_size
+        for c in tr.chunks:  # the padded chunk layout the row launches write (chunk-wise contiguous)
+            tr.ft_grad[(c.start + c.shift) * W:(c.start + c.shift + c.length) * W] = \
+                torch.from_numpy(g["l0w_gradients"][c.start * W:(c.start + c.length) * W])
         for (name, off, n) in tr.dense_layout:
             tr.dense_grad[off:off + n] = torch.from_numpy(g[f"{name}_gradients"])
 
-    def ranger(self, params, grad, weights, m, v, slow):
+    def sfnn_row_launches(self, sh, alpha):
+        base = 73305 if sh.input_size == 73305 + 1629 else (131949 if sh.input_size == 131949 + 1629 else 0)
+        kings = base // 1629 if base else 1
+        n = -(-kings // 3)
+        return [sh.input_size if j == n - 1 else 3 * (j + 1) * 1629 for j in range(n)]
+
+    def ranger(self, params, grad, weights, m, v, slow, ctx=None):
         p = params.radam
         oracle.ranger_update(grad.numpy(), weights.numpy(), m.numpy(), v.numpy(), slow.numpy(), step=p.step,
                              learning_rate=p.learning_rate, beta1=p.beta1, beta2=p.beta2, epsilon=p.epsilon,
