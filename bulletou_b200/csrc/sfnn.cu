@@ -294,6 +294,11 @@ __device__ __forceinline__ float pair_out(float x0, float x1, int lattice) {
     return lattice ? qat_on_lattice(qat_lattice(c)) : c;
 }
 
+// Widths with a warp FT kernel (NCH = width / 128 float4 chunks per row).
+__host__ __device__ inline bool ft_warp_width(int w) {
+    return w == 256 || w == 512 || w == 1024 || w == 1536 || w == 2304;
+}
+
 // One warp per half-position; lane owns float4 chunks lane + 32 i, so chunk i
 // and chunk i + NCH/2 are the two members of a pair (width / 2 apart).
 template <int NCH, bool LATTICE>
@@ -334,6 +339,7 @@ __global__ void __launch_bounds__(256) ft_forward_kernel(FtArgs a) {
         acc[i] = make_float4(crelu01(acc[i].x), crelu01(acc[i].y), crelu01(acc[i].z), crelu01(acc[i].w));
         out[lane + 32 * i] = acc[i];
     }
+    if (a.combined == nullptr) return;  // the engine's integer FT writes it instead
     float4* comb = reinterpret_cast<float4*>(a.combined) + static_cast<size_t>(b) * w4 + v * (w4 >> 1);
 #pragma unroll
     for (int i = 0; i < NCH / 2; ++i) {
@@ -369,7 +375,7 @@ __global__ void ft_forward_generic_kernel(FtArgs a) {
     float* out = a.l0[v] + static_cast<size_t>(b) * a.width;
     out[j] = x0;
     out[j + half] = x1;
-    a.combined[static_cast<size_t>(b) * a.width + v * half + j] = pair_out(x0, x1, a.lattice);
+    if (a.combined != nullptr) a.combined[static_cast<size_t>(b) * a.width + v * half + j] = pair_out(x0, x1, a.lattice);
 }
 
 // Dense QAT with FT QAT: the engine's integer FT from the fake-quantised table
@@ -1769,7 +1775,9 @@ int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const Sfnn
         SfnnDims df = d;
         df.qat.integer_ft = 0;
         df.qat.dense = 0;
-        if (launch_ft_forward(ctx, df, plan, stm, nstm, l0b, act) != 0) return -1;
+        SfnnActivations fact = act;
+        if (ft_warp_width(d.width)) fact.combined = nullptr;  // written by the integer FT below
+        if (launch_ft_forward(ctx, df, plan, stm, nstm, l0b, fact) != 0) return -1;
         prof_mark(ctx);  // stage profiler: the integer FT is its own phase
         FtArgs ea{};
         ea.stm = stm;
