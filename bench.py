@@ -108,7 +108,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    ap.add_argument("--workload", choices=("sfnn", "halfkp"), default="sfnn")
+    ap.add_argument("--workload", choices=("sfnn", "halfkp", "kppt"), default="sfnn")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--dp-chunk-launches", type=int, default=3,
                     help="N > 1: FT row launches per exchanged chunk (SFNN)")
@@ -409,6 +409,67 @@ def run_reference(args, local):
     return {"total_ms": total_ms, "clocks": clk,
             "e2e": {"value": e2e_steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4, "steps": e2e_steps}}
+
+
+# --------------------------------------------------------------------------- KPPT workload
+KPPT_BATCH = 32768
+KPPT_METRIC = "train positions/sec (KPPT KPP component table, 81 x 1548^2 entries, 703 pairs, batch 32768)"
+
+
+def run_kppt(args, local, reference=False):
+    """One KPP component-table train step per iteration (the reference trains
+    one component table per runner, lib.rs:4857-5066): device-resident
+    batches; the e2e leg uploads every step from pinned host memory."""
+    import bulletou_b200 as bo
+    from bulletou_b200 import synthetic
+
+    lib = bo.reference_library() if reference else None
+    ctx = bo.Context(local, lib) if lib else bo.Context(local)
+    rng = synthetic.rng_for(77)
+    n_inputs = synthetic.KPP_INPUTS
+    table = rng.normal(0.0, 0.01, n_inputs).astype(np.float32)
+    runner = bo.KpptTableTrainStepRunner(ctx, n_inputs, table, 0.0, [1.0, -1.0], 0.0, args.batch,
+                                         synthetic.KPP_PAIRS, fused=None if not reference else False)
+    batches = []
+    for i in range(2):
+        r = synthetic.rng_for(300 + i)
+        stm, nstm, _, A = synthetic.kppt_indices(r, args.batch, "kpp")
+        t, w = synthetic.targets(r, args.batch)
+        batches.append((stm, nstm, t, w))
+    loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
+    inv = 1.0 / 600.0
+    step = 0
+    runner.upload_batch(*batches[0], ctx)
+    for _ in range(args.warmup):
+        step += 1
+        runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=False)
+    ctx.synchronize()
+    start, stop = bo.Event(ctx), bo.Event(ctx)
+    with ClockSampler(local) as clocks:
+        start.record(ctx)
+        for _ in range(args.steps):
+            step += 1
+            runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=False)
+        stop.record(ctx)
+        stop.synchronize()
+    total_ms = stop.elapsed_ms_since(start)
+    e2e_steps = max(4, args.steps // 2)
+    e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    t0 = time.perf_counter()
+    e0.record(ctx)
+    for i in range(e2e_steps):
+        step += 1
+        runner.upload_batch(*batches[i % 2], ctx)
+        runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=True)
+        runner.read_loss(ctx)
+    e1.record(ctx)
+    e1.synchronize()
+    e2e_ms = max(e1.elapsed_ms_since(e0), (time.perf_counter() - t0) * 1000.0)
+    h2d = sum(a.nbytes for a in batches[0])
+    return {"total_ms": total_ms, "clocks": clocks.summary(),
+            "e2e": {"value": e2e_steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4 * (3 * args.batch + 2),
+                    "steps": e2e_steps}}
 
 
 # --------------------------------------------------------------------------- roofline
@@ -809,7 +870,26 @@ def main():
         args.warmup = 3
     sfnn = args.workload == "sfnn"
     if args.batch is None:
-        args.batch = SFNN_BATCH if sfnn else BATCH
+        args.batch = {"sfnn": SFNN_BATCH, "halfkp": BATCH, "kppt": KPPT_BATCH}[args.workload]
+    if args.workload == "kppt":
+        if rank == 0:
+            r = run_kppt(args, local, reference=args.impl == "reference")
+            line = {"metric": KPPT_METRIC, "unit": "positions/s", "n_gpus": 1, "steps": args.steps,
+                    "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                    "dtype": "f32", "data": "synthetic (seeded KPP pairs, reference shapes)",
+                    "config": {"workload": "configs[3] KPPT KPP component train step (Ranger, as the reference's "
+                                           "KPPT runner; the reference has no AdaGrad)",
+                               "global_batch": args.batch, "pairs": 703, "table": 194100624},
+                    "value": round(args.steps * args.batch / (r["total_ms"] / 1000.0), 1),
+                    "ms_per_step": round(r["total_ms"] / args.steps, 4), "clocks": r["clocks"],
+                    "e2e": {k: (round(v, 1) if isinstance(v, float) else v) for k, v in r["e2e"].items()}}
+            if args.impl == "reference":
+                line["impl"] = "reference"
+            print(json.dumps(line))
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     common = {"global_batch": args.batch * world, "per_gpu_batch": args.batch, "seq_len": 1,
               "optimizer": "Ranger (RAdam + Lookahead k=6, lr 1e-3)",
               "loss": "sigmoid-WDL MSE, scale 600, lambda 0.5",
