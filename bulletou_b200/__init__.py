@@ -50,4 +50,16 @@ from .nnue_quant import (  # noqa: F401
     nnue_quantize_device,
 )
 
+from .teacher import (  # noqa: F401
+    PSV_DTYPE,
+    LayerStackBucketKind,
+    TeacherBatch,
+    TeacherBatchConfig,
+    TeacherBatchProducer,
+    TeacherUploadSlot,
+    WinRateModelTargetParams,
+    teacher_prepare_device,
+    win_rate_model_score_table,
+)
+
 __version__ = "0.1.0"

@@ -62,6 +62,13 @@ class SfnnQat(ctypes.Structure):
     _fields_ = [("l1", I), ("ft", I), ("l2", I), ("l3", I)]
 
 
+class TeacherConfig(ctypes.Structure):
+    """BulletOuB200TeacherConfig."""
+
+    _fields_ = [("feature_set", I), ("max_active", I), ("hand_bucket", I), ("king_bucket", I),
+                ("result_blend", F), ("score_blend", F), ("rscale", F), ("score_drop_abs", I)]
+
+
 class LossSpec(ctypes.Structure):
     """BulletOuB200LossSpec."""
 
@@ -163,6 +170,7 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_nnue_quantize_device": [P, Z, Z, Z, Z, P, P, P],
     "bulletou_b200_nnue_integer_forward_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, I, P, P, P],
     "bulletou_b200_sfnn_integer_forward_device": [P, P, Z, Z] + [P] * 9,
+    "bulletou_b200_teacher_prepare_device": [P, P, P, Z] + [P] * 7,
 }
 
 

@@ -855,6 +855,26 @@ class NnueTrainStepRunner:
         self.upload_batch(batch, ctx)
         self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
 
+    def step_from_records(self, ctx: Context, params: RangerUpdateParams, loss_kind: ScalarLossKind,
+                          output_inv_scale: float, producer, records, finalize_loss: bool = True) -> None:
+        """Decode PackedSfenValue records into this runner's batch on the
+        device (HalfKP features, prepare_halfkp_direct_fast_batch,
+        teacher_batch.rs:1687-1750), then step."""
+        from .teacher import TeacherBatch
+
+        cfg = producer.config
+        base = self.shape.input_size - (1548 if self.shape.input_size == 125388 + 1548 else 0)
+        if (cfg.feature_set != "halfkp" or cfg.active != self.max_active or producer.batch_size != self.batch_size
+                or base != cfg.num_inputs):
+            raise CudaCppError(
+                f"teacher producer ({cfg.feature_set}, batch {producer.batch_size}, max_active {cfg.active}) does "
+                f"not match the HalfKP runner (batch {self.batch_size}, max_active {self.max_active}, "
+                f"input_size {self.shape.input_size})")
+        view = TeacherBatch.wrap(self.stm_indices, self.nstm_indices, None, self.targets, self.entry_weights,
+                                 self.batch_size, self.max_active)
+        producer.prepare(ctx, records, view)
+        self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
+
     def _handles(self):
         if self._handle_arrays is None:
             arr = ctypes.c_void_p * 8

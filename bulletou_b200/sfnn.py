@@ -569,6 +569,65 @@ class SfnnTrainStepRunner:
         slot.compute_done.record(ctx)
         return nbytes
 
+    # -- steps on PackedSfenValue records (device-side batch producer) -----
+    def _check_producer(self, producer) -> None:
+        cfg = producer.config
+        if cfg.feature_set != "halfka_hm2" or cfg.active != self.max_active or producer.batch_size != self.batch_size:
+            raise CudaCppError(
+                f"teacher producer ({cfg.feature_set}, batch {producer.batch_size}, max_active {cfg.active}) does "
+                f"not match the SFNN runner (batch {self.batch_size}, max_active {self.max_active})")
+        base = self.shape.factorized_base() or self.shape.input_size
+        if base != cfg.num_inputs:
+            raise CudaCppError(f"HalfKA_hm2 records feed {cfg.num_inputs} inputs, the runner has {base}")
+        if cfg.layerstack_bucket.num_stacks != self.shape.num_stacks:
+            raise CudaCppError(f"LayerStack bucket kind gives {cfg.layerstack_bucket.num_stacks} stacks, "
+                               f"the runner has {self.shape.num_stacks}")
+
+    def step_from_records(self, ctx: Context, params: RangerUpdateParams, loss_kind: ScalarLossKind,
+                          output_inv_scale: float, producer, records, finalize_loss: bool = True) -> None:
+        """Decode PackedSfenValue records into this runner's batch on the
+        device (bulletou_b200_teacher_prepare_device), then step."""
+        from .teacher import TeacherBatch
+
+        self._check_producer(producer)
+        view = TeacherBatch.wrap(self.stm_indices, self.nstm_indices, self.buckets, self.targets,
+                                 self.entry_weights, self.batch_size, self.max_active)
+        producer.prepare(ctx, records, view)
+        self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
+
+    def record_slots(self, producer, count: int = 2) -> list:
+        from .teacher import TeacherUploadSlot
+
+        if getattr(self, "_record_slots", None) is None or len(self._record_slots) != count:
+            self._check_producer(producer)
+            self._record_slots = [TeacherUploadSlot(self.ctx, producer) for _ in range(count)]
+            self._next_record_slot = 0
+        return self._record_slots
+
+    def step_pipelined_records(self, ctx: Context, upload_ctx: Context, producer, params: RangerUpdateParams,
+                               loss_kind: ScalarLossKind, output_inv_scale: float, records=None,
+                               finalize_loss: bool = True, pinned_source=None,
+                               loss_out: Optional[PinnedF32Buffer] = None) -> int:
+        """Pipelined step fed by PackedSfenValue records: the records (40 bytes
+        a position) go H2D on `upload_ctx` and are decoded there into the next
+        slot's batch while the previous step runs on `ctx`; an event hands the
+        batch over.  Optionally copies the mean loss D2H into `loss_out`.
+        Returns the H2D bytes."""
+        slots = self.record_slots(producer)
+        slot = slots[self._next_record_slot]
+        self._next_record_slot = (self._next_record_slot + 1) % len(slots)
+        nbytes = slot.upload(upload_ctx, producer, records, pinned_source)
+        slot.upload_ready.wait(ctx)
+        b = slot.batch
+        self.stm_indices, self.nstm_indices, self.buckets = b.stm_indices, b.nstm_indices, b.buckets
+        self.targets, self.entry_weights = b.targets, b.entry_weights
+        self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
+        if loss_out is not None:
+            self.lib.call("bulletou_b200_f32_download_pinned", ctx.as_ptr(), loss_out.as_ptr(),
+                          self.loss_workspace.mean.as_ptr(), 1)
+        slot.compute_done.record(ctx)
+        return nbytes
+
     # -- readback ----------------------------------------------------------
     def read_loss(self, ctx: Optional[Context] = None) -> ScalarLossReadback:
         return self.loss_workspace.download(ctx)

@@ -165,3 +165,166 @@ def sfnn_weights(rng: np.random.Generator, input_size: int = HM2_INPUTS + HM2_PI
     for k in ("l1fw", "l1fb", "l2fw", "l2fb", "l3fw", "l3fb"):
         out.setdefault(k, None)
     return out
+
+
+# ---------------------------------------------------------------- PackedSfenValue records
+# Piece types as in crates/bulletou_lib/src/shogi/types.rs:27-44.
+PAWN, LANCE, KNIGHT, SILVER, BISHOP, ROOK, GOLD, KING = 1, 2, 3, 4, 5, 6, 7, 8
+PRO_PAWN, PRO_LANCE, PRO_KNIGHT, PRO_SILVER, HORSE, DRAGON = 9, 10, 11, 12, 13, 14
+HAND_TYPES = (PAWN, LANCE, KNIGHT, SILVER, GOLD, BISHOP, ROOK)          # Hand slot order
+# Board Huffman code of each unpromoted type, LSB first (packed_sfen.rs:17-26).
+_BOARD_CODE = {PAWN: (0x01, 2), LANCE: (0x03, 4), KNIGHT: (0x0b, 4), SILVER: (0x07, 4), BISHOP: (0x1f, 6),
+               ROOK: (0x3f, 6), GOLD: (0x0f, 5)}
+_UNPROMOTE = {PRO_PAWN: PAWN, PRO_LANCE: LANCE, PRO_KNIGHT: KNIGHT, PRO_SILVER: SILVER, HORSE: BISHOP, DRAGON: ROOK}
+# 38 non-king pieces of a full set.
+FULL_SET = (PAWN,) * 18 + (LANCE,) * 4 + (KNIGHT,) * 4 + (SILVER,) * 4 + (GOLD,) * 4 + (BISHOP,) * 2 + (ROOK,) * 2
+PSV_DTYPE = np.dtype([("sfen", "u1", 32), ("score", "<i2"), ("move16", "<u2"), ("game_ply", "<u2"),
+                      ("game_result", "i1"), ("padding", "u1")])
+
+
+def _board_token(code: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """(value, length) of the board token for piece codes type | colour << 4."""
+    pt = code & 15
+    color = (code >> 4) & 1
+    value = np.zeros(code.shape, np.int64)
+    length = np.ones(code.shape, np.int64)                 # empty square: "0"
+    for t in range(1, 15):
+        m = pt == t
+        if not m.any():
+            continue
+        base = _UNPROMOTE.get(t, t)
+        pattern, n = _BOARD_CODE[base]
+        if base == GOLD:
+            value[m] = pattern | (color[m] << n)
+            length[m] = n + 1
+        else:
+            promoted = 1 if t in _UNPROMOTE else 0
+            value[m] = pattern | (promoted << n) | (color[m] << (n + 1))
+            length[m] = n + 2
+    return value, length
+
+
+def _hand_token(pt: int, color: np.ndarray, piecebox: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    pattern, n = _BOARD_CODE[pt]
+    hp, hn = pattern >> 1, n - 1
+    if pt == GOLD:
+        return hp | (color << hn), np.full(color.shape, hn + 1, np.int64)
+    return hp | (piecebox << hn) | (color << (hn + 1)), np.full(color.shape, hn + 2, np.int64)
+
+
+def psv_encode(stm, black_king, white_king, board, hands, score=0, result=0, game_ply=0, move16=0) -> np.ndarray:
+    """Encode positions into PackedSfenValue records (YaneuraOu's sfen packer
+    format, the inverse of ShogiBoard::from_packed_sfen, packed_sfen.rs:228-284).
+
+    stm, black_king, white_king: [n]; board: [n, 81] piece codes type | colour << 4
+    (0 empty; king squares are not read); hands: [n, 2, 7] counts in HAND_TYPES
+    order.  Positions with fewer than the full 38 pieces are padded to 256 bits
+    with piece-box pawns (a lance at a 4/5-bit tail); a position that leaves a
+    1-bit tail cannot be padded and raises."""
+    stm = np.atleast_1d(np.asarray(stm, np.int64))
+    n = stm.size
+    bk = np.broadcast_to(np.asarray(black_king, np.int64), (n,))
+    wk = np.broadcast_to(np.asarray(white_king, np.int64), (n,))
+    board = np.asarray(board, np.int64).reshape(n, 81)
+    hands = np.asarray(hands, np.int64).reshape(n, 2, 7)
+    bits = np.zeros((n, 256 + 16), np.uint8)
+    cursor = np.zeros(n, np.int64)
+    rows = np.arange(n)
+
+    def write(value, length, mask=None):
+        value = np.broadcast_to(np.asarray(value, np.int64), (n,))
+        length = np.broadcast_to(np.asarray(length, np.int64), (n,))
+        if mask is not None:
+            length = np.where(mask, length, 0)
+        for b in range(int(length.max(initial=0))):
+            m = b < length
+            if (cursor[m] + b >= 256).any():
+                raise ValueError("position needs more than 256 bits")
+            bits[rows[m], cursor[m] + b] = (value[m] >> b) & 1
+        cursor[:] += length
+
+    write(stm, 1)
+    write(bk, 7)
+    write(wk, 7)
+    for sq in range(81):
+        v, ln = _board_token(board[:, sq])
+        write(v, ln, (sq != bk) & (sq != wk))
+    for color in (0, 1):
+        for h, pt in enumerate(HAND_TYPES):
+            for i in range(int(hands[:, color, h].max(initial=0))):
+                v, ln = _hand_token(pt, np.full(n, color, np.int64))
+                write(v, ln, hands[:, color, h] > i)
+    # piece-box padding up to bit 256
+    while True:
+        r = 256 - cursor
+        if (r == 1).any():
+            raise ValueError("a 1-bit tail cannot be padded with piece-box pieces")
+        pawn = (r >= 3) & (r != 4) & (r != 5)
+        if not pawn.any():
+            break
+        write(0b010, 3, pawn)                                      # pawn code 0, box 1, black
+    r = 256 - cursor
+    write(0b10, 2, r == 2)                                         # pawn + box, colour bit past the end
+    write(0b1001, 4, r == 4)                                       # lance code + box, colour past the end
+    write(0b01001, 5, r == 5)                                      # lance code + box + black
+    assert (cursor == 256).all()
+    out = np.zeros(n, PSV_DTYPE)
+    out["sfen"] = np.packbits(bits[:, :256], axis=1, bitorder="little")
+    out["score"] = np.broadcast_to(np.asarray(score, np.int64), (n,)).astype(np.int16)
+    out["move16"] = np.broadcast_to(np.asarray(move16, np.int64), (n,)).astype(np.uint16)
+    out["game_ply"] = np.broadcast_to(np.asarray(game_ply, np.int64), (n,)).astype(np.uint16)
+    out["game_result"] = np.broadcast_to(np.asarray(result, np.int64), (n,)).astype(np.int8)
+    return out
+
+
+def psv_positions(rng: np.random.Generator, n: int, hand_fraction: float = 0.12,
+                  promote_fraction: float = 0.06) -> dict:
+    """Full-set positions: kings near their home ranks, each of the 38 other
+    pieces owned by either side, in hand with probability `hand_fraction`,
+    else on a random free square (promoted with probability
+    `promote_fraction` unless gold).  A full set packs into exactly 256 bits."""
+    def king(home):
+        rank = np.where(rng.random(n) < 0.85, home + np.where(home == 0, 1, -1) * rng.integers(0, 2, n),
+                        rng.integers(0, 9, n))
+        return rng.integers(0, 9, n) * 9 + rank
+
+    bk = king(np.full(n, 8))
+    wk = king(np.full(n, 0))
+    clash = bk == wk
+    wk[clash] = (wk[clash] + 9) % 81
+    stm = rng.integers(0, 2, n)
+    board = np.zeros((n, 81), np.int64)
+    hands = np.zeros((n, 2, 7), np.int64)
+    key = rng.random((n, 81))
+    key[np.arange(n), bk] = 2.0
+    key[np.arange(n), wk] = 2.0
+    order = np.argsort(key, axis=1)                                  # free squares first
+    slot = np.zeros(n, np.int64)
+    rows = np.arange(n)
+    for pt in FULL_SET:
+        color = rng.integers(0, 2, n)
+        in_hand = rng.random(n) < hand_fraction
+        h = HAND_TYPES.index(pt)
+        np.add.at(hands, (rows[in_hand], color[in_hand], h), 1)
+        on = ~in_hand
+        sq = order[rows[on], slot[on]]
+        code = np.full(on.sum(), pt, np.int64)
+        if pt != GOLD:
+            promo = rng.random(on.sum()) < promote_fraction
+            code[promo] = {PAWN: PRO_PAWN, LANCE: PRO_LANCE, KNIGHT: PRO_KNIGHT, SILVER: PRO_SILVER,
+                           BISHOP: HORSE, ROOK: DRAGON}[pt]
+        board[rows[on], sq] = code | (color[on] << 4)
+        slot[on] += 1
+    return {"stm": stm, "black_king": bk, "white_king": wk, "board": board, "hands": hands}
+
+
+def psv_records(seed: int, n: int, rank: int = 0, **kw) -> np.ndarray:
+    """`n` seeded PackedSfenValue records of full-set positions with teacher
+    scores round(N(0, 600)) clipped to +-3000, results in {-1, 0, 1}."""
+    rng = rng_for(seed, rank)
+    p = psv_positions(rng, n, **kw)
+    score = np.clip(np.rint(rng.normal(0.0, 600.0, n)), -3000, 3000).astype(np.int64)
+    result = rng.integers(-1, 2, n)
+    ply = rng.integers(1, 320, n)
+    move = rng.integers(0, 1 << 16, n)
+    return psv_encode(p["stm"], p["black_king"], p["white_king"], p["board"], p["hands"], score, result, ply, move)

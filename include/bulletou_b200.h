@@ -367,6 +367,44 @@ int bulletou_b200_sfnn_integer_forward_device(BulletOuCudaCppContext* ctx, const
     BulletOuCudaCppI32Buffer* l1_out, BulletOuCudaCppI32Buffer* raw_output, BulletOuCudaCppI32Buffer* score_output,
     BulletOuCudaCppI32Buffer* errors);
 
+
+/* ---- teacher-batch producer (PackedSfenValue records -> sparse batch) ----
+ * Replaces the host-side batch preparation of the reference's SFNN and HalfKP
+ * trainers: prepare_sfnn_fast_batch_from_board_features
+ * (crates/bulletou_lib/src/value/teacher_batch.rs:2869-3010) with the
+ * HalfKA_hm2 feature map (game/inputs/shogi_halfka_hm2.rs:195-258) and
+ * ShogiSfnnLayerStackBucketKind::bucket_from_board (game/outputs.rs:1227-1231),
+ * and prepare_halfkp_direct_fast_batch (teacher_batch.rs:1687-1750) with
+ * map_halfkp_features_from_packed (game/inputs/shogi_halfkp.rs:161-227). */
+#define BULLETOU_B200_FEATURES_HALFKA_HM2 0
+#define BULLETOU_B200_FEATURES_HALFKP 1
+
+typedef struct BulletOuB200TeacherConfig {
+    int32_t feature_set;    /* BULLETOU_B200_FEATURES_* */
+    int32_t max_active;     /* row stride of stm / nstm (40 HalfKA_hm2, 38 HalfKP); at most 48 */
+    int32_t hand_bucket;    /* ShogiSfnnHandBucketKind: 0 none, 1 hand4, 2 hand16, 3 hand64, 4 hand64z,
+                               5 hand256, 6 hand1024 */
+    int32_t king_bucket;    /* ShogiSfnnKingBucketKind: 0 none, 1 king rank 9, 2 king rank 81, 3 k9k9z,
+                               4 k13k13z, 5 k21k21, 6 k21k21z, 7 k29k29 */
+    float result_blend;     /* target = result_blend * result + score_blend * p(score) */
+    float score_blend;
+    float rscale;           /* 1 / scale for p(score) = sigmoid(rscale * score) */
+    int32_t score_drop_abs; /* entry weight 0 when |score| >= this; < 0 disables */
+} BulletOuB200TeacherConfig;
+
+/* records: n_records PackedSfenValue records (40 bytes = 10 words each) in an
+ * i32 buffer.  Writes stm / nstm [n_records][max_active] (-1 padded), buckets
+ * [n_records] (optional; 0 for HalfKP), targets and entry_weights [n_records].
+ * wrm_table (optional, 65536 floats indexed by score + 32768) replaces the
+ * sigmoid with the win-rate-model probability.  overflow[0] is increased by
+ * the number of records with more than max_active features (the reference
+ * aborts the batch on such a record); the caller zeroes it. */
+int bulletou_b200_teacher_prepare_device(BulletOuCudaCppContext* ctx, const BulletOuB200TeacherConfig* config,
+    const BulletOuCudaCppI32Buffer* records, size_t n_records, const BulletOuCudaCppF32Buffer* wrm_table,
+    BulletOuCudaCppI32Buffer* stm_indices, BulletOuCudaCppI32Buffer* nstm_indices,
+    BulletOuCudaCppI32Buffer* buckets, BulletOuCudaCppF32Buffer* targets, BulletOuCudaCppF32Buffer* entry_weights,
+    BulletOuCudaCppI32Buffer* overflow);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,7 +25,8 @@ _lib = None
 
 
 def build() -> Path:
-    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < (HERE / "bulletou_oracle.c").stat().st_mtime:
+    newest = max((HERE / f).stat().st_mtime for f in ("bulletou_oracle.c", "teacher_oracle.c", "Makefile"))
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < newest:
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB_PATH
 
