@@ -3,7 +3,7 @@
 the reference's host producer (teacher_batch.rs:1687-1750, 2869-3010 with the
 PackedSfenValue decode of packed_sfen.rs and the feature maps of
 shogi_halfka_hm2.rs / shogi_halfkp.rs): feature rows, buckets and entry
-weights bit-exact, targets bit-exact through the win-rate table and within 1
+weights bit-exact, targets bit-exact through the win-rate table and within 2
 ulp through the sigmoid; then train steps fed from records against steps fed
 from the oracle's batch."""
 import numpy as np
@@ -56,8 +56,9 @@ def _compare(got, want, cfg, exact_targets=None):
     if exact_targets if exact_targets is not None else cfg.win_rate_model:
         assert ulp.max() == 0
     else:
-        # exp in double rounded once vs the C library's expf
-        assert ulp.max() <= 1 and (ulp == 0).mean() > 0.999
+        # exp in double rounded once vs the C library's expf: 1 ulp of p(score),
+        # at most 2 after the blend's product and sum
+        assert ulp.max() <= 2 and (ulp == 0).mean() > 0.999
 
 
 @pytest.mark.parametrize("hand,king", BUCKET_KINDS)
