@@ -535,6 +535,84 @@ def bind_sfnn(runner, dev):
     runner.stm_indices, runner.nstm_indices, runner.buckets, runner.targets, runner.entry_weights = dev
 
 
+SFNN_RECORD_BATCHES = 2
+
+
+def sfnn_teacher_config():
+    """The reference's SFNN trainer defaults (examples/bulletou.rs:5050-5075,
+    18846-18866): lambda 1.0, win-rate-model targets (offset 270, scaling 380),
+    k3k3 = KingRank9 LayerStack buckets, no score drop."""
+    from bulletou_b200 import teacher as bt
+
+    return bt.TeacherBatchConfig(feature_set="halfka_hm2", lambda_=1.0, scale=600.0, win_rate_model=True)
+
+
+def sfnn_records_e2e(args, ctx, upload_ctx, runner, step, loss_kind, inv):
+    """End to end from teacher records: per step the batch's PackedSfenValue
+    records (40 bytes a position) go H2D from pinned memory and are decoded on
+    the device (HalfKA_hm2 rows, buckets, targets) on the upload stream while
+    the previous step trains; the mean loss comes back D2H every step.  Also
+    times the decode kernel alone on records resident in HBM."""
+    import bulletou_b200 as bo
+    from bulletou_b200 import synthetic
+    from bulletou_b200 import teacher as bt
+    from bulletou_b200.cuda_cpp import PinnedF32Buffer
+
+    producer = bt.TeacherBatchProducer(ctx, sfnn_teacher_config(), args.batch)
+    sources = []
+    for i in range(SFNN_RECORD_BATCHES):
+        slot = bt.TeacherUploadSlot(ctx, producer)
+        slot.fill(synthetic.psv_records(3000 + i, args.batch))
+        sources.append(slot)
+    # decode kernel alone, records resident
+    out = producer.new_batch()
+    ctx.lib.call("bulletou_b200_i32_upload_pinned", ctx.as_ptr(), producer.records.as_ptr(),
+                 sources[0].pinned.as_ptr(), sources[0].pinned.length)
+    for _ in range(3):
+        producer.decode(ctx, out)
+    d0, d1 = bo.Event(ctx), bo.Event(ctx)
+    reps = 20
+    d0.record(ctx)
+    for _ in range(reps):
+        producer.decode(ctx, out)
+    d1.record(ctx)
+    d1.synchronize()
+    decode_ms = d1.elapsed_ms_since(d0) / reps
+    e2e_steps = max(8, args.steps)
+    ring = [PinnedF32Buffer(ctx, 1) for _ in range(e2e_steps)]
+    for i in range(3):
+        step += 1
+        runner.step_pipelined_records(ctx, upload_ctx, producer, ranger(step), loss_kind, inv, None, True,
+                                      sources[i % len(sources)], ring[i])
+    ctx.synchronize()
+    upload_ctx.synchronize()
+    e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    h2d = 0
+    t0 = time.perf_counter()
+    e0.record(ctx)
+    for i in range(e2e_steps):
+        step += 1
+        h2d = runner.step_pipelined_records(ctx, upload_ctx, producer, ranger(step), loss_kind, inv, None, True,
+                                            sources[i % len(sources)], ring[i])
+    e1.record(ctx)
+    e1.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1000.0
+    e2e_ms = max(e1.elapsed_ms_since(e0), wall_ms)
+    producer.check(ctx)
+    losses = [float(r.host()[0]) for r in ring]
+    assert all(np.isfinite(losses)), "non-finite loss"
+    e2e = {"value": e2e_steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
+           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
+           "path": "SfnnTrainStepRunner.step_pipelined_records: PackedSfenValue records in pinned host memory -> "
+                   "H2D (40 B/position) -> device decode to HalfKA_hm2 rows / k3k3 buckets / win-rate targets "
+                   "(bulletou_b200_teacher_prepare_device) on the upload stream -> fused train step; mean loss "
+                   "copied D2H every step"}
+    producer_line = {"kernel": "teacher_psv_kernel", "ms_per_batch": round(decode_ms, 4),
+                     "positions_per_s": round(args.batch / (decode_ms / 1000.0), 1),
+                     "record_bytes_per_s": round(40 * args.batch / (decode_ms / 1000.0), 1)}
+    return e2e, producer_line, step
+
+
 def sfnn_cpu_baseline(batch_cap=256, budget_s=8.0):
     """The reference's CPU evaluation path for SFNN -- the engine's integer
     forward over the exported quantised network (examples/bulletou.rs:
@@ -562,6 +640,33 @@ def sfnn_cpu_baseline(batch_cap=256, budget_s=8.0):
             "kind": "port",
             "sample": f"oracle quantised SFNN 1536 integer forward (the reference's CPU evaluator), {reps} x "
                       f"{batch_cap} positions in {dt:.1f} s; the reference cannot train on CPU"}
+
+
+def teacher_cpu_baseline(n=16384, budget_s=6.0):
+    """The reference's teacher-batch producer for this workload
+    (prepare_sfnn_fast_batch_from_board_features, teacher_batch.rs:2869-3010)
+    as the C oracle's restatement, one thread, on a bounded sample."""
+    from bulletou_b200 import synthetic
+    from oracle import teacher as ot
+
+    recs = synthetic.psv_records(4343, n)
+    cfg = sfnn_teacher_config()
+    lb = cfg.layerstack_bucket
+    ocfg = ot.config("halfka_hm2", cfg.active, lb.hand, lb.king, cfg.lambda_, cfg.scale)
+    from bulletou_b200 import teacher as bt
+
+    table = bt.win_rate_model_score_table(cfg.wrm_target)
+    ot.prepare(recs[:64], ocfg, table)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        ot.prepare(recs, ocfg, table)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(reps * n / dt, 1), "unit": "positions/s", "cores": 1, "kind": "port",
+            "sample": f"oracle PackedSfenValue -> HalfKA_hm2 batch producer, {reps} x {n} records in {dt:.1f} s"}
 
 
 def sfnn_phases(qat):
@@ -646,12 +751,15 @@ def run_sfnn_b200(args, rank, world, local, dist):
     losses = [float(r.host()[0]) for r in loss_ring]
     e2e_ms = max(e1.elapsed_ms_since(e0), wall_ms)
     assert all(np.isfinite(losses)), "non-finite loss"
+    e2e_prepared = {"value": e2e_steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
+                    "path": "SfnnTrainStepRunner.step_pipelined_no_readback_with_loss_finalize (2 upload slots, "
+                            "second stream), prepared sparse batches in pinned host memory, mean loss copied D2H "
+                            "every step"}
+    e2e, producer_line, step = sfnn_records_e2e(args, ctx, upload_ctx, runner, step, loss_kind, inv)
     return {
         "total_ms": total_ms, "phase_ms": phase_ms, "clocks": clk,
-        "e2e": {"value": e2e_steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
-                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
-                "path": "SfnnTrainStepRunner.step_pipelined_no_readback_with_loss_finalize (2 upload slots, "
-                        "second stream), inputs in pinned host memory, mean loss copied D2H every step"},
+        "e2e": e2e, "e2e_prepared_batches": e2e_prepared, "producer": producer_line,
         "gpu_launches": sfnn_launches_per_step(args.qat) * args.steps,
         "final_loss": losses[-1],
     }
@@ -938,8 +1046,13 @@ def main():
         line = dict(base, value=round(value, 1), ms_per_step=round(r["total_ms"] / args.steps, 4),
                     e2e={k: (round(v, 1) if isinstance(v, float) else v) for k, v in r["e2e"].items()},
                     roofline=rl, clocks=r["clocks"], gpu_launches=r["gpu_launches"], final_loss=r["final_loss"])
+        for extra in ("e2e_prepared_batches", "producer"):
+            if extra in r:
+                line[extra] = {k: (round(v, 1) if isinstance(v, float) else v) for k, v in r[extra].items()}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = sfnn_cpu_baseline() if sfnn else cpu_baseline()
+            if "producer" in line:
+                line["producer"]["cpu_baseline"] = teacher_cpu_baseline()
         print(json.dumps(line))
     if dist is not None:
         dist.barrier()

@@ -115,6 +115,7 @@ enum ScratchSlot : int {
     kScratchSfnnQatFt = 23,     // SFNN QAT: fake-quantised FT bias
     kScratchSfnnQatTable = 24,  // SFNN dense QAT with FT QAT: integer FT table (i16)
     kScratchNnueQuant = 25,     // integer HalfKP forward: transformed features (u8)
+    kScratchSfnnHeavy = 26,     // SFNN FT rows: segment plan and partial sums of heavy rows
 };
 
 int ok();

@@ -1318,7 +1318,18 @@ struct PieceRowArgs {
     int last_launch;
     float* vacc;          // [pieces][width]
     int* vany;            // [pieces * col_groups]
+    // Heavy rows (more than kHeavyRow entries, e.g. the piece-squares of the
+    // common king squares in real teacher data) are summed beforehand in
+    // kHeavySeg-entry segments by every warp (heavy_segment_kernel); the row
+    // kernel then adds the row's segment partials in segment order.
+    size_t max_entries;          // entries of the index (bounds the segment plan)
+    const int* heavy_start;      // [kings * pieces] first segment of the row, -1: gather the entries
+    const float* heavy_partials; // [segments][width]
 };
+
+constexpr int kHeavyRow = 512;
+constexpr int kHeavySeg = 512;
+constexpr int kHeavyPlanThreads = 1024;
 
 // Column layout of a warp's chunk: with VEC = 8 a lane owns columns
 // [c, c+4) and [c+128, c+132) for c = 4 * lane, so each warp-wide float4 access
@@ -1402,6 +1413,42 @@ __device__ __forceinline__ void row_update(const PieceRowArgs& a, size_t off, co
     }
 }
 
+// Sum of the gradient rows of entries elist[0, n) over a lane's columns:
+// entry ids are broadcast 32 at a time, four loads in flight per lane.
+template <int VEC>
+__device__ __forceinline__ void gather_sum(const PieceRowArgs& a, const int* __restrict__ elist, int n, int c,
+                                           bool active, int lane, float* acc) {
+    for (int q0 = 0; q0 < n; q0 += 32) {
+        const int m = min(32, n - q0);
+        const int mine = lane < m ? __ldg(elist + q0 + lane) : 0;
+        int q = 0;
+        for (; q + 4 <= m; q += 4) {
+            int en[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) en[u] = __shfl_sync(kFull, mine, q + u);
+            if (active) {
+                float x[4][VEC];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    ldv<VEC>(a.src[en[u] & 1] + static_cast<size_t>(en[u] >> 1) * a.src_stride + c, x[u]);
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int e = 0; e < VEC; ++e) acc[e] += x[u][e];
+            }
+        }
+        for (; q < m; ++q) {
+            const int en = __shfl_sync(kFull, mine, q);
+            if (active) {
+                float x[VEC];
+                ldv<VEC>(a.src[en & 1] + static_cast<size_t>(en >> 1) * a.src_stride + c, x);
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) acc[e] += x[e];
+            }
+        }
+    }
+}
+
 // One warp per (piece, column group).  The piece's rows are visited in king
 // order; every warp walks the kings at about the same pace, so the gradient
 // rows being read at any time belong to a few kings' half-positions (L2).
@@ -1432,6 +1479,7 @@ __device__ __forceinline__ void piece_rows(const PieceRowArgs& a, int gw, int la
         const int* elist = a.entries + beg;  // ascending (sort_inverse_index)
         any = any || n > 0;
         const size_t row_off = static_cast<size_t>(row) * a.width;
+        const int hs = a.heavy_start != nullptr ? __ldg(a.heavy_start + row) : -1;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
             const int c = lane_col<VEC>(c0, it, lane);
@@ -1439,34 +1487,18 @@ __device__ __forceinline__ void piece_rows(const PieceRowArgs& a, int gw, int la
             float acc[VEC];
 #pragma unroll
             for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
-            for (int q0 = 0; q0 < n; q0 += 32) {
-                const int m = min(32, n - q0);
-                const int mine = lane < m ? __ldg(elist + q0 + lane) : 0;
-                int q = 0;
-                for (; q + 4 <= m; q += 4) {
-                    int en[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) en[u] = __shfl_sync(kFull, mine, q + u);
-                    if (active) {
-                        float x[4][VEC];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            ldv<VEC>(a.src[en[u] & 1] + static_cast<size_t>(en[u] >> 1) * a.src_stride + c, x[u]);
-#pragma unroll
-                        for (int u = 0; u < 4; ++u)
-#pragma unroll
-                            for (int e = 0; e < VEC; ++e) acc[e] += x[u][e];
-                    }
-                }
-                for (; q < m; ++q) {
-                    const int en = __shfl_sync(kFull, mine, q);
-                    if (active) {
+            if (hs >= 0) {
+                const int nseg = (n + kHeavySeg - 1) / kHeavySeg;
+                if (active) {
+                    for (int sg = 0; sg < nseg; ++sg) {
                         float x[VEC];
-                        ldv<VEC>(a.src[en & 1] + static_cast<size_t>(en >> 1) * a.src_stride + c, x);
+                        ldv<VEC>(a.heavy_partials + static_cast<size_t>(hs + sg) * a.width + c, x);
 #pragma unroll
                         for (int e = 0; e < VEC; ++e) acc[e] += x[e];
                     }
                 }
+            } else {
+                gather_sum<VEC>(a, elist, n, c, active, lane, acc);
             }
             if (active) {
                 float seen[VEC];
@@ -1509,6 +1541,89 @@ __global__ void __launch_bounds__(kPieceRowWarps * 32, 3) piece_row_kernel(Piece
     const int items = a.pieces * a.col_groups;
     for (int gw = blockIdx.x * kPieceRowWarps + (threadIdx.x >> 5); gw < items; gw += gridDim.x * kPieceRowWarps)
         piece_rows<VEC, ITERS, MODE>(a, gw, lane);
+}
+
+// Segment plan of the heavy rows (one CTA): per row its first segment (or -1),
+// per segment its row, and the segment count.  Rows are visited in order, so
+// the segments of a king block are contiguous.  If the plan would exceed the
+// scratch it keeps no heavy row (every row gathers its entries).
+__device__ __forceinline__ int plan_exclusive_scan(int v, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(kFull, incl, d);
+        if (lane >= d) incl += o;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < static_cast<int>(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int o = __shfl_up_sync(kFull, w, d);
+            if (lane >= d) w += o;
+        }
+        warp_sums[lane] = w;
+    }
+    __syncthreads();
+    *total = warp_sums[(blockDim.x >> 5) - 1];
+    return (warp > 0 ? warp_sums[warp - 1] : 0) + incl - v;
+}
+
+__global__ void __launch_bounds__(kHeavyPlanThreads) heavy_plan_kernel(const int* __restrict__ offsets, int rows,
+                                                                       int max_segments, int* __restrict__ seg_start,
+                                                                       int* __restrict__ seg_row,
+                                                                       int* __restrict__ total_out) {
+    __shared__ int warp_sums[32];
+    const int per = (rows + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+    const int r0 = static_cast<int>(threadIdx.x) * per, r1 = min(rows, r0 + per);
+    int mine = 0;
+    for (int r = r0; r < r1; ++r) {
+        const int n = offsets[r + 1] - offsets[r];
+        if (n > kHeavyRow) mine += (n + kHeavySeg - 1) / kHeavySeg;
+    }
+    int total = 0;
+    int s = plan_exclusive_scan(mine, warp_sums, &total);
+    const bool fits = total <= max_segments;
+    for (int r = r0; r < r1; ++r) {
+        const int n = offsets[r + 1] - offsets[r];
+        int start = -1;
+        if (fits && n > kHeavyRow) {
+            const int k = (n + kHeavySeg - 1) / kHeavySeg;
+            start = s;
+            for (int j = 0; j < k; ++j) seg_row[s + j] = r;
+            s += k;
+        }
+        seg_start[r] = start;
+    }
+    if (threadIdx.x == 0) *total_out = fits ? total : 0;
+}
+
+// Partial sums of the heavy rows' segments: warp per (segment, column group),
+// persistent over the plan's segment count.
+template <int VEC>
+__global__ void __launch_bounds__(kPieceRowWarps * 32, 3) heavy_segment_kernel(PieceRowArgs a,
+                                                                               const int* __restrict__ seg_row,
+                                                                               const int* __restrict__ total_p,
+                                                                               float* __restrict__ partials) {
+    const int lane = threadIdx.x & 31;
+    const int items = *total_p * a.col_groups;
+    for (int gw = blockIdx.x * kPieceRowWarps + (threadIdx.x >> 5); gw < items; gw += gridDim.x * kPieceRowWarps) {
+        const int seg = gw / a.col_groups;
+        const int c0 = (gw - seg * a.col_groups) * a.group_width;
+        const int c_end = min(a.width, c0 + a.group_width);
+        const int row = seg_row[seg];
+        const int beg = a.offsets[row] + (seg - a.heavy_start[row]) * kHeavySeg;
+        const int n = min(kHeavySeg, a.offsets[row + 1] - beg);
+        const int c = lane_col<VEC>(c0, 0, lane);
+        const bool active = c < c_end;
+        float acc[VEC];
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
+        gather_sum<VEC>(a, a.entries + beg, n, c, active, lane, acc);
+        if (active) stv<VEC>(partials + static_cast<size_t>(seg) * a.width + c, acc);
+    }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -1581,6 +1696,32 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, con
             return -1;
         a.vacc = static_cast<float*>(vp);
         a.vany = reinterpret_cast<int*>(a.vacc + vf);
+    }
+    {
+        // Heavy-row plan and segment sums.  Segments <= entries / kHeavySeg + heavy
+        // rows, and heavy rows < entries / kHeavyRow.
+        const int rows = a.kings * a.pieces;
+        const size_t entries = a.max_entries;
+        const size_t max_seg = entries / kHeavySeg + entries / kHeavyRow + 1;
+        const size_t ints = align_floats(static_cast<size_t>(rows) + max_seg + 1);
+        void* hp = nullptr;
+        if (scratch_slot(ctx, kScratchSfnnHeavy, (ints + max_seg * static_cast<size_t>(a.width)) * sizeof(float), &hp,
+                         "cudaMalloc SFNN heavy-row segments") != 0)
+            return -1;
+        int* seg_start = static_cast<int*>(hp);
+        int* seg_row = seg_start + rows;
+        int* total = seg_row + max_seg;
+        float* partials = reinterpret_cast<float*>(hp) + ints;
+        heavy_plan_kernel<<<1, kHeavyPlanThreads, 0, ctx->stream>>>(a.offsets, rows, static_cast<int>(max_seg),
+                                                                    seg_start, seg_row, total);
+        if (check_launch("SFNN heavy-row plan launch") != 0) return -1;
+        a.heavy_start = seg_start;
+        a.heavy_partials = partials;
+        const int blocks = 3 * ctx->sm_count;
+        if (vec == 8) heavy_segment_kernel<8><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, seg_row, total, partials);
+        else if (vec == 4) heavy_segment_kernel<4><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, seg_row, total, partials);
+        else heavy_segment_kernel<1><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, seg_row, total, partials);
+        if (check_launch("SFNN heavy-row segment launch") != 0) return -1;
     }
     switch (mode) {
         case kRowRanger: return launch_piece_rows_mode<kRowRanger>(ctx, a, vec, row_shift, events);
@@ -1997,6 +2138,7 @@ PieceRowArgs piece_row_args(const SfnnDims& d, const InverseIndex& index) {
     PieceRowArgs r{};
     r.offsets = index.offsets;
     r.entries = index.entries;
+    r.max_entries = 2 * static_cast<size_t>(d.batch) * static_cast<size_t>(d.max_active);
     if (d.base > 0) {
         r.pieces = kSfnnPieces;
         r.kings = d.base / kSfnnPieces;

@@ -13,7 +13,9 @@ import bulletou_b200 as bo
 from bulletou_b200 import sfnn as bs
 from bulletou_b200 import synthetic as syn
 from bulletou_b200 import teacher as bt
+from oracle import oracle
 from oracle import teacher as ot
+from tests.conftest import assert_close_scaled
 
 pytestmark = pytest.mark.gpu
 
@@ -240,3 +242,46 @@ def test_halfkp_steps_from_records_match_oracle_batches(ctx):
                            bo.NnueTrainStepHostBatch(o["stm"].reshape(-1), o["nstm"].reshape(-1), t,
                                                      o["entry_weights"], B, 38))
         assert a.read_loss(ctx).mean == b.read_loss(ctx).mean
+
+
+def oracle_sfnn_trainer(shape, w, qat):
+    return oracle.SfnnTrainer(shape.as_tuple(), w, qat=qat)
+
+
+def _heavy_rows(stm, nstm, threshold=512):
+    rows = np.concatenate([stm.reshape(-1), nstm.reshape(-1)])
+    counts = np.bincount(rows[rows >= 0])
+    return int((counts > threshold).sum()), int(counts.max())
+
+
+@pytest.mark.parametrize("qat", ["none", "dense_ft"])
+def test_fused_steps_on_record_batches_vs_oracle(ctx, qat):
+    """Real teacher data concentrates the kings near their home squares, so a
+    few FT rows collect thousands of entries (the heavy-row segment path of
+    the row kernel); the fused step still matches the oracle trainer."""
+    from tests.test_gpu_sfnn_qat import MODES, _mask, _weights
+
+    lr = bs.SfnnLayerLrMultipliers() if qat == "none" else MODES[qat]
+    shape = bs.SfnnForwardShape(bs.HALFKA_HM2_DIMENSIONS + bs.PIECE_INPUTS, 256, 15, True, 32, 9)
+    w = _weights(shape, 91)
+    B = 8192
+    cfg = _cfg("halfka_hm2", lam=0.6)
+    runner = bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(shape, **w), B, 40, lr_multipliers=lr)
+    assert runner.fused
+    trainer = oracle_sfnn_trainer(shape, w, _mask(lr))
+    prod = bt.TeacherBatchProducer(ctx, cfg, B, pinned=False)
+    loss = bo.ScalarLossKind.SigmoidPow(2.0)
+    for step in range(1, 4):
+        recs = syn.psv_records(100 + step, B)
+        o = _oracle(cfg, recs)
+        heavy, biggest = _heavy_rows(o["stm"], o["nstm"])
+        assert heavy > 0 and biggest > 2 * 512
+        runner.step_from_records(ctx, _ranger(step), loss, 1 / 600, prod, recs)
+        dev = prod.new_batch()
+        prod.prepare(ctx, recs, dev)
+        t = dev.targets.download(ctx)
+        trainer.step(o["stm"].reshape(-1), o["nstm"].reshape(-1), o["buckets"], B, 40, t, o["entry_weights"],
+                     step=step, learning_rate=1e-3, inv_scale=1 / 600)
+    got = runner.read_weights(ctx)
+    for nm in trainer.names:
+        assert_close_scaled(got[nm], trainer.w[nm], 1e-4, nm)
