@@ -115,6 +115,9 @@ def parse_args():
     ap.add_argument("--qat", choices=tuple(SFNN_QAT_MODES), default="all",
                     help="SFNN quantisation-aware training mode (both arms)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--data", choices=("psv", "uniform"), default="psv",
+                    help="SFNN batches: decoded PackedSfenValue records (kings near home, as in teacher data) or "
+                         "feature rows uniform over the king blocks")
     return ap.parse_args()
 
 
@@ -523,6 +526,49 @@ def sfnn_host_weights():
     return bs.SfnnForwardHostWeights(sfnn_shape(), **synthetic.sfnn_weights(synthetic.rng_for(7)))
 
 
+def sfnn_batches(args, ctx, rank=0, reference=False):
+    """(host batches, device batches) of the SFNN workload.  --data psv (the
+    default): seeded PackedSfenValue records of full-set positions, decoded to
+    HalfKA_hm2 rows, k3k3 buckets and win-rate targets -- on the device by the
+    product's producer, by the CPU oracle of the reference's producer on the
+    reference arm (the two agree bit for bit on these targets).  --data uniform:
+    rows drawn uniformly over the king blocks (synthetic.sfnn_batch)."""
+    if args.data == "uniform":
+        batches = make_sfnn_batches(args.batch, rank)
+        return batches, sfnn_device_batches(ctx, batches)
+    from bulletou_b200 import synthetic
+
+    records = [synthetic.psv_records(3000 + i, args.batch, rank) for i in range(SFNN_RECORD_BATCHES)]
+    cfg = sfnn_teacher_config()
+    if reference:
+        from bulletou_b200 import teacher as bt
+        from oracle import teacher as ot
+
+        lb = cfg.layerstack_bucket
+        ocfg = ot.config("halfka_hm2", cfg.active, lb.hand, lb.king, cfg.lambda_, cfg.scale)
+        table = bt.win_rate_model_score_table(cfg.wrm_target)
+        host = []
+        for r in records:
+            o = ot.prepare(r, ocfg, table)
+            assert (o["counts"] <= cfg.active).all()
+            host.append({"stm": o["stm"].reshape(-1), "nstm": o["nstm"].reshape(-1), "buckets": o["buckets"],
+                         "targets": o["targets"], "entry_weights": o["entry_weights"]})
+        return host, sfnn_device_batches(ctx, host)
+    from bulletou_b200 import teacher as bt
+
+    producer = bt.TeacherBatchProducer(ctx, cfg, args.batch, pinned=False)
+    host, dev = [], []
+    for r in records:
+        tb = producer.new_batch()
+        producer.prepare(ctx, r, tb)
+        dev.append((tb.stm_indices, tb.nstm_indices, tb.buckets, tb.targets, tb.entry_weights))
+        d = tb.download(ctx)
+        host.append({"stm": d["stm"].reshape(-1), "nstm": d["nstm"].reshape(-1), "buckets": d["buckets"],
+                     "targets": d["targets"], "entry_weights": d["entry_weights"]})
+    producer.check(ctx)
+    return host, dev
+
+
 def sfnn_device_batches(ctx, batches):
     import bulletou_b200 as bo
 
@@ -697,8 +743,7 @@ def run_sfnn_b200(args, rank, world, local, dist):
     ctx = bo.Context(local)
     runner = bs.SfnnTrainStepRunner(ctx, sfnn_host_weights(), args.batch, SFNN_ACTIVE, fused=True,
                                     lr_multipliers=sfnn_lr_multipliers(args.qat))
-    batches = make_sfnn_batches(args.batch, rank)
-    devb = sfnn_device_batches(ctx, batches)
+    batches, devb = sfnn_batches(args, ctx, rank)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
     inv = 1.0 / 600.0
     step = 0
@@ -778,8 +823,7 @@ def run_sfnn_data_parallel(args, rank, world, local, dist):
     tr = SfnnDataParallelTrainer(backend, dist, sfnn_host_weights(), args.batch, SFNN_ACTIVE,
                                  lr_multipliers=sfnn_lr_multipliers(args.qat),
                                  launches_per_chunk=args.dp_chunk_launches)
-    batches = make_sfnn_batches(args.batch, rank)
-    devb = sfnn_device_batches(ctx, batches)
+    batches, devb = sfnn_batches(args, ctx, rank)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
     inv = 1.0 / 600.0
     step = 0
@@ -862,8 +906,7 @@ def run_sfnn_reference(args, local):
     ctx = bo.Context(local, lib)
     runner = bs.SfnnTrainStepRunner(ctx, sfnn_host_weights(), args.batch, SFNN_ACTIVE, fused=False,
                                     lr_multipliers=sfnn_lr_multipliers(args.qat))
-    batches = make_sfnn_batches(args.batch)
-    devb = sfnn_device_batches(ctx, batches)
+    batches, devb = sfnn_batches(args, ctx, 0, reference=True)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
     inv = 1.0 / 600.0
     step = 0
@@ -912,8 +955,8 @@ def run_sfnn_reference(args, local):
 
 # DRAM bytes per step of each phase at B = 65536 (dram__bytes_read.sum +
 # dram__bytes_write.sum over the phase's launches), from a full-size ncu
-# capture of `bench.py --steps 1 --warmup 3`; keyed by the QAT modes whose
-# kernels they were measured on.
+# capture of `bench.py --steps 1 --warmup 3 --data uniform`; keyed by the QAT
+# modes whose kernels they were measured on.
 SFNN_DRAM_BYTES_B65536 = {
     "ft_rows_ranger": (4813480704, ("none", "l1", "layers", "dense", "all")),
     "ft_forward": (1679058432, ("none", "l1", "dense", "all")),
@@ -922,8 +965,11 @@ SFNN_DRAM_BYTES_B65536 = {
     "fold": (1124865536, ("all",)),
 }
 
+# The same on the default --data psv batches (decoded PackedSfenValue records).
+SFNN_DRAM_BYTES_PSV_B65536 = {}
 
-def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0, qat="none"):
+
+def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0, qat="none", data="psv"):
     """Algorithmic bytes per launch of each SFNN phase (the per-position
     formulas of the hot-path table; gathers counted at their logical size, so
     a fraction above 1 means L2 serves the repeated rows)."""
@@ -958,7 +1004,7 @@ def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0
     t = phase_ms[dom] / 1000.0
     achieved = algo.get(dom, 0.0) / t / 1e9 if t > 0 else 0.0
     traffic = None
-    measured = SFNN_DRAM_BYTES_B65536.get(dom)
+    measured = (SFNN_DRAM_BYTES_B65536 if data == "uniform" else SFNN_DRAM_BYTES_PSV_B65536).get(dom)
     if measured is not None and batch == SFNN_BATCH and qat in measured[1]:
         traffic = measured[0]
     launches = 15 if dom == "ft_rows_ranger" else 1
@@ -1007,7 +1053,11 @@ def main():
         config = dict({"workload": "configs[2] SFNN HalfKA_hm2 1536x2 LayerStack k3k3 train step",
                        "model": "SFNN_halfkahm2_1536_15_32_k3k3: (73305+1629 virtual) x 1536 FT, pairwise, "
                                 "9 x (1536 -> 15+1), shared L1 factor, 30 -> 32 -> 1",
-                       "max_active": SFNN_ACTIVE, "buckets": "uniform 0..8",
+                       "max_active": SFNN_ACTIVE,
+                       "data": ("seeded PackedSfenValue records (full-set positions, kings near their home ranks) "
+                                "decoded to HalfKA_hm2 rows / k3k3 buckets / win-rate targets"
+                                if args.data == "psv" else "feature rows uniform over the 45 king blocks, "
+                                                           "buckets uniform 0..8"),
                        "qat": f"{args.qat}: {SFNN_QAT_LABELS[args.qat]}",
                        "l2": "no flush: each step streams 1.8 GB of FT optimizer state (> 126 MB L2)"}, **common)
     else:
@@ -1041,7 +1091,7 @@ def main():
     value = args.steps * args.batch * world / (r["total_ms"] / 1000.0)
     if rank == 0:
         hbm, kind = measured_peaks()
-        rl = (sfnn_roofline(r["phase_ms"], args.batch, hbm, kind, qat=args.qat) if sfnn
+        rl = (sfnn_roofline(r["phase_ms"], args.batch, hbm, kind, qat=args.qat, data=args.data) if sfnn
               else roofline(r["phase_ms"], args.batch, hbm, kind))
         line = dict(base, value=round(value, 1), ms_per_step=round(r["total_ms"] / args.steps, 4),
                     e2e={k: (round(v, 1) if isinstance(v, float) else v) for k, v in r["e2e"].items()},

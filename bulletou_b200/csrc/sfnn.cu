@@ -52,6 +52,7 @@ constexpr float kPairScale = 127.0f / 128.0f;  // SFNN_PAIRWISE_SCALE, cu:1148
 constexpr int kBucketKeys = kSfnnMaxStacks + 1;
 constexpr int kPieceRowWarps = 8;
 constexpr int kKingsPerLaunch = 3;  // FT row kernel: king blocks per launch (L2 working set)
+constexpr int kTileRanks = 4096;    // half-positions per rank tile of the FT row index (24 MB of gradient rows)
 
 __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
 __device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f && a < 1.0f ? g : 0.0f; }
@@ -235,6 +236,22 @@ __global__ void __launch_bounds__(kKingSortThreads) bucket_hist_kernel(const int
 
 // One CTA.  Keys 0..stacks (the last one holds samples with an invalid
 // bucket) are cut into tiles of at most kSfnnTile consecutive sorted samples.
+// tile_base[k] = first rank tile of king block k, max(1, ceil(N_k / tile_ranks))
+// tiles each (one thread; kings <= kSfnnKingKeys).  With a single row block
+// (no factorized king blocks) every sorted rank belongs to it.
+__global__ void king_tiles_kernel(const int* __restrict__ key_off, int kings, int tile_ranks,
+                                  int* __restrict__ tile_base) {
+    if (threadIdx.x != 0) return;
+    int run = 0;
+    for (int k = 0; k < kings; ++k) {
+        tile_base[k] = run;
+        const int end = kings == 1 ? key_off[kSfnnKingKeys] : key_off[k + 1];
+        const int n = end - key_off[k];
+        run += max(1, (n + tile_ranks - 1) / tile_ranks);
+    }
+    tile_base[kings] = run;
+}
+
 __global__ void __launch_bounds__(128) tile_table_kernel(const int* __restrict__ key_off, int keys,
                                                          int* __restrict__ n_tiles, int* __restrict__ tile_key,
                                                          int* __restrict__ tile_begin, int* __restrict__ tile_end,
@@ -1318,18 +1335,23 @@ struct PieceRowArgs {
     int last_launch;
     float* vacc;          // [pieces][width]
     int* vany;            // [pieces * col_groups]
-    // Heavy rows (more than kHeavyRow entries, e.g. the piece-squares of the
-    // common king squares in real teacher data) are summed beforehand in
-    // kHeavySeg-entry segments by every warp (heavy_segment_kernel); the row
-    // kernel then adds the row's segment partials in segment order.
+    // Heavy rows (more than kHeavyRow entries over all their keys, e.g. the
+    // piece-squares of the common king squares in real teacher data) are summed
+    // beforehand in kHeavySeg-entry segments, each inside one rank tile, by every
+    // warp (heavy_segment_kernel); the row kernel then adds the row's segment
+    // partials in (tile, segment) order.
+    const int* tile_base;        // [kings + 1] rank tiles of each king (tile-keyed index), null: key = row
+    int n_keys;                  // keys of the index
     size_t max_entries;          // entries of the index (bounds the segment plan)
-    const int* heavy_start;      // [kings * pieces] first segment of the row, -1: gather the entries
+    const int* heavy_off;        // [n_keys + 1] exclusive scan of the keys' segment counts
     const float* heavy_partials; // [segments][width]
+    int heavy_row;               // rows with more entries are heavy
+    int heavy_seg;               // entries per segment
+    int heavy_ok;                // the plan fit the scratch (read on the device as well)
 };
 
-constexpr int kHeavyRow = 512;
-constexpr int kHeavySeg = 512;
-constexpr int kHeavyPlanThreads = 1024;
+constexpr int kHeavyRow = 128;  // FT row phase on king-concentrated batches: 512 -> 3.75 ms, 128 -> 3.03 ms
+constexpr int kHeavySeg = 128;
 
 // Column layout of a warp's chunk: with VEC = 8 a lane owns columns
 // [c, c+4) and [c+128, c+132) for c = 4 * lane, so each warp-wide float4 access
@@ -1414,7 +1436,8 @@ __device__ __forceinline__ void row_update(const PieceRowArgs& a, size_t off, co
 }
 
 // Sum of the gradient rows of entries elist[0, n) over a lane's columns:
-// entry ids are broadcast 32 at a time, four loads in flight per lane.
+// entry ids are broadcast 32 at a time, kGatherDepth rows in flight per lane.
+constexpr int kGatherDepth = 4;
 template <int VEC>
 __device__ __forceinline__ void gather_sum(const PieceRowArgs& a, const int* __restrict__ elist, int n, int c,
                                            bool active, int lane, float* acc) {
@@ -1422,17 +1445,17 @@ __device__ __forceinline__ void gather_sum(const PieceRowArgs& a, const int* __r
         const int m = min(32, n - q0);
         const int mine = lane < m ? __ldg(elist + q0 + lane) : 0;
         int q = 0;
-        for (; q + 4 <= m; q += 4) {
-            int en[4];
+        for (; q + kGatherDepth <= m; q += kGatherDepth) {
+            int en[kGatherDepth];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) en[u] = __shfl_sync(kFull, mine, q + u);
+            for (int u = 0; u < kGatherDepth; ++u) en[u] = __shfl_sync(kFull, mine, q + u);
             if (active) {
-                float x[4][VEC];
+                float x[kGatherDepth][VEC];
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
+                for (int u = 0; u < kGatherDepth; ++u)
                     ldv<VEC>(a.src[en[u] & 1] + static_cast<size_t>(en[u] >> 1) * a.src_stride + c, x[u]);
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
+                for (int u = 0; u < kGatherDepth; ++u)
 #pragma unroll
                     for (int e = 0; e < VEC; ++e) acc[e] += x[u][e];
             }
@@ -1474,35 +1497,54 @@ __device__ __forceinline__ void piece_rows(const PieceRowArgs& a, int gw, int la
     if (has_virtual && !a.first_launch) any = a.vany[gw] != 0;
     for (int k = a.king_begin; k < a.king_end; ++k) {
         const int row = k * a.pieces + p;
-        const int beg = a.offsets[row];
-        const int n = a.offsets[row + 1] - beg;
-        const int* elist = a.entries + beg;  // ascending (sort_inverse_index)
-        any = any || n > 0;
         const size_t row_off = static_cast<size_t>(row) * a.width;
-        const int hs = a.heavy_start != nullptr ? __ldg(a.heavy_start + row) : -1;
+        // the row's keys: one per rank tile of king k (or the row itself)
+        const int t0 = a.tile_base != nullptr ? __ldg(a.tile_base + k) : k;
+        const int t1 = a.tile_base != nullptr ? __ldg(a.tile_base + k + 1) : k + 1;
+        float acc[ITERS][VEC];
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it)
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[it][e] = 0.0f;
+        int total = 0;
+        for (int t = t0; t < t1; ++t) {
+            const int key = t * a.pieces + p;
+            const int beg = a.offsets[key];
+            const int n = a.offsets[key + 1] - beg;
+            if (n == 0) continue;
+            total += n;
+            const int* elist = a.entries + beg;  // ascending up to kSortCap entries (sort_inverse_index)
+            int hs = -1;
+            if (a.heavy_off != nullptr) {
+                const int s0 = __ldg(a.heavy_off + key), s1 = __ldg(a.heavy_off + key + 1);
+                if (s1 > s0 && __ldg(a.heavy_off + a.n_keys) <= a.heavy_ok) hs = s0;
+            }
+#pragma unroll
+            for (int it = 0; it < ITERS; ++it) {
+                const int c = lane_col<VEC>(c0, it, lane);
+                const bool active = c < c_end;
+                if (hs >= 0) {
+                    const int nseg = (n + a.heavy_seg - 1) / a.heavy_seg;
+                    if (active) {
+                        for (int sg = 0; sg < nseg; ++sg) {
+                            float x[VEC];
+                            ldv<VEC>(a.heavy_partials + static_cast<size_t>(hs + sg) * a.width + c, x);
+#pragma unroll
+                            for (int e = 0; e < VEC; ++e) acc[it][e] += x[e];
+                        }
+                    }
+                } else {
+                    gather_sum<VEC>(a, elist, n, c, active, lane, acc[it]);
+                }
+            }
+        }
+        any = any || total > 0;
 #pragma unroll
         for (int it = 0; it < ITERS; ++it) {
             const int c = lane_col<VEC>(c0, it, lane);
-            const bool active = c < c_end;
-            float acc[VEC];
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
-            if (hs >= 0) {
-                const int nseg = (n + kHeavySeg - 1) / kHeavySeg;
-                if (active) {
-                    for (int sg = 0; sg < nseg; ++sg) {
-                        float x[VEC];
-                        ldv<VEC>(a.heavy_partials + static_cast<size_t>(hs + sg) * a.width + c, x);
-#pragma unroll
-                        for (int e = 0; e < VEC; ++e) acc[e] += x[e];
-                    }
-                }
-            } else {
-                gather_sum<VEC>(a, elist, n, c, active, lane, acc);
-            }
-            if (active) {
+            if (c < c_end) {
                 float seen[VEC];
-                row_update<VEC, MODE>(a, row_off + c, acc, n == 0, seen);
+                row_update<VEC, MODE>(a, row_off + c, acc[it], total == 0, seen);
 #pragma unroll
                 for (int e = 0; e < VEC; ++e) vacc[it][e] += seen[e];
             }
@@ -1543,79 +1585,59 @@ __global__ void __launch_bounds__(kPieceRowWarps * 32, 3) piece_row_kernel(Piece
         piece_rows<VEC, ITERS, MODE>(a, gw, lane);
 }
 
-// Segment plan of the heavy rows (one CTA): per row its first segment (or -1),
-// per segment its row, and the segment count.  Rows are visited in order, so
-// the segments of a king block are contiguous.  If the plan would exceed the
-// scratch it keeps no heavy row (every row gathers its entries).
-__device__ __forceinline__ int plan_exclusive_scan(int v, int* warp_sums, int* total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int incl = v;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-        const int o = __shfl_up_sync(kFull, incl, d);
-        if (lane >= d) incl += o;
+// Segments per key: a row (k, p) is heavy when its entries over all its keys
+// (the rank tiles of king k) exceed heavy_row; each key of a heavy row is cut
+// into ceil(n / heavy_seg) segments, so a segment never crosses a rank tile.
+// Keys of unused tiles get 0.  Thread i covers row i and key i.
+__global__ void heavy_count_kernel(const int* __restrict__ offsets, const int* __restrict__ tile_base, int kings,
+                                   int pieces, int rows, int keys, int heavy_row, int heavy_seg,
+                                   int* __restrict__ seg_count) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int used_keys = tile_base != nullptr ? tile_base[kings] * pieces : rows;
+    if (i < keys && i >= used_keys) seg_count[i] = 0;
+    if (i >= rows) return;
+    const int k = i / pieces, p = i - k * pieces;
+    const int t0 = tile_base != nullptr ? tile_base[k] : i;
+    const int t1 = tile_base != nullptr ? tile_base[k + 1] : i + 1;
+    const int stride = tile_base != nullptr ? pieces : 1;
+    const int base = tile_base != nullptr ? p : 0;
+    int total = 0;
+    for (int t = t0; t < t1; ++t) total += offsets[t * stride + base + 1] - offsets[t * stride + base];
+    const bool heavy = total > heavy_row;
+    for (int t = t0; t < t1; ++t) {
+        const int key = t * stride + base;
+        const int n = offsets[key + 1] - offsets[key];
+        seg_count[key] = heavy ? (n + heavy_seg - 1) / heavy_seg : 0;
     }
-    if (lane == 31) warp_sums[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-        int w = lane < static_cast<int>(blockDim.x >> 5) ? warp_sums[lane] : 0;
-#pragma unroll
-        for (int d = 1; d < 32; d <<= 1) {
-            const int o = __shfl_up_sync(kFull, w, d);
-            if (lane >= d) w += o;
-        }
-        warp_sums[lane] = w;
-    }
-    __syncthreads();
-    *total = warp_sums[(blockDim.x >> 5) - 1];
-    return (warp > 0 ? warp_sums[warp - 1] : 0) + incl - v;
 }
 
-__global__ void __launch_bounds__(kHeavyPlanThreads) heavy_plan_kernel(const int* __restrict__ offsets, int rows,
-                                                                       int max_segments, int* __restrict__ seg_start,
-                                                                       int* __restrict__ seg_row,
-                                                                       int* __restrict__ total_out) {
-    __shared__ int warp_sums[32];
-    const int per = (rows + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
-    const int r0 = static_cast<int>(threadIdx.x) * per, r1 = min(rows, r0 + per);
-    int mine = 0;
-    for (int r = r0; r < r1; ++r) {
-        const int n = offsets[r + 1] - offsets[r];
-        if (n > kHeavyRow) mine += (n + kHeavySeg - 1) / kHeavySeg;
-    }
-    int total = 0;
-    int s = plan_exclusive_scan(mine, warp_sums, &total);
-    const bool fits = total <= max_segments;
-    for (int r = r0; r < r1; ++r) {
-        const int n = offsets[r + 1] - offsets[r];
-        int start = -1;
-        if (fits && n > kHeavyRow) {
-            const int k = (n + kHeavySeg - 1) / kHeavySeg;
-            start = s;
-            for (int j = 0; j < k; ++j) seg_row[s + j] = r;
-            s += k;
-        }
-        seg_start[r] = start;
-    }
-    if (threadIdx.x == 0) *total_out = fits ? total : 0;
+// seg_key[s] = key of segment s (thread per key).
+__global__ void heavy_fill_kernel(const int* __restrict__ seg_off, int keys, int max_segments,
+                                  int* __restrict__ seg_key) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= keys || seg_off[keys] > max_segments) return;
+    for (int s = seg_off[i]; s < seg_off[i + 1]; ++s) seg_key[s] = i;
 }
 
 // Partial sums of the heavy rows' segments: warp per (segment, column group),
-// persistent over the plan's segment count.
+// persistent over the segment count (segments in key order: tile-major, so the
+// warps in flight read the gradient rows of one or two rank tiles).  With more segments than the scratch holds no
+// row is heavy (heavy_off reads as empty, see piece_rows).
 template <int VEC>
-__global__ void __launch_bounds__(kPieceRowWarps * 32, 3) heavy_segment_kernel(PieceRowArgs a,
-                                                                               const int* __restrict__ seg_row,
-                                                                               const int* __restrict__ total_p,
+__global__ void __launch_bounds__(kPieceRowWarps * 32, 4) heavy_segment_kernel(PieceRowArgs a, int rows,
+                                                                               int max_segments,
+                                                                               const int* __restrict__ seg_key,
                                                                                float* __restrict__ partials) {
     const int lane = threadIdx.x & 31;
-    const int items = *total_p * a.col_groups;
+    const int total = a.heavy_off[rows];
+    const int items = total <= max_segments ? total * a.col_groups : 0;
     for (int gw = blockIdx.x * kPieceRowWarps + (threadIdx.x >> 5); gw < items; gw += gridDim.x * kPieceRowWarps) {
         const int seg = gw / a.col_groups;
         const int c0 = (gw - seg * a.col_groups) * a.group_width;
         const int c_end = min(a.width, c0 + a.group_width);
-        const int row = seg_row[seg];
-        const int beg = a.offsets[row] + (seg - a.heavy_start[row]) * kHeavySeg;
-        const int n = min(kHeavySeg, a.offsets[row + 1] - beg);
+        const int row = __ldg(seg_key + seg);
+        const int beg = a.offsets[row] + (seg - a.heavy_off[row]) * a.heavy_seg;
+        const int n = min(a.heavy_seg, a.offsets[row + 1] - beg);
         const int c = lane_col<VEC>(c0, 0, lane);
         const bool active = c < c_end;
         float acc[VEC];
@@ -1698,29 +1720,43 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, con
         a.vany = reinterpret_cast<int*>(a.vacc + vf);
     }
     {
-        // Heavy-row plan and segment sums.  Segments <= entries / kHeavySeg + heavy
-        // rows, and heavy rows < entries / kHeavyRow.
-        const int rows = a.kings * a.pieces;
-        const size_t entries = a.max_entries;
-        const size_t max_seg = entries / kHeavySeg + entries / kHeavyRow + 1;
-        const size_t ints = align_floats(static_cast<size_t>(rows) + max_seg + 1);
+        // Heavy-row segments: counts, their exclusive scan, the segment sums.
+        // Segments <= entries / heavy_seg + heavy rows < entries / heavy_seg + entries / heavy_row.
+        a.heavy_row = kHeavyRow;
+        a.heavy_seg = kHeavySeg;
+        const int rows = a.n_keys;
+        const size_t max_seg = a.max_entries / a.heavy_seg + a.max_entries / a.heavy_row + 1;
+        const size_t tiles = static_cast<size_t>(scan_tiles(rows)) + 1;
+        const size_t ints = align_floats(2 * static_cast<size_t>(rows) + 1 + tiles + max_seg);
         void* hp = nullptr;
         if (scratch_slot(ctx, kScratchSfnnHeavy, (ints + max_seg * static_cast<size_t>(a.width)) * sizeof(float), &hp,
                          "cudaMalloc SFNN heavy-row segments") != 0)
             return -1;
-        int* seg_start = static_cast<int*>(hp);
-        int* seg_row = seg_start + rows;
-        int* total = seg_row + max_seg;
+        int* seg_count = static_cast<int*>(hp);
+        int* seg_off = seg_count + rows;
+        int* tile_sums = seg_off + rows + 1;
+        int* seg_key = tile_sums + tiles;
         float* partials = reinterpret_cast<float*>(hp) + ints;
-        heavy_plan_kernel<<<1, kHeavyPlanThreads, 0, ctx->stream>>>(a.offsets, rows, static_cast<int>(max_seg),
-                                                                    seg_start, seg_row, total);
-        if (check_launch("SFNN heavy-row plan launch") != 0) return -1;
-        a.heavy_start = seg_start;
+        const int base_rows = a.kings * a.pieces;
+        const int threads = std::max(rows, base_rows);
+        heavy_count_kernel<<<(threads + 255) / 256, 256, 0, ctx->stream>>>(
+            a.offsets, a.tile_base, a.kings, a.pieces, base_rows, rows, a.heavy_row, a.heavy_seg, seg_count);
+        if (check_launch("SFNN heavy-row count launch") != 0) return -1;
+        if (exclusive_scan_counts(ctx, seg_count, rows, seg_off, tile_sums) != 0) return -1;
+        heavy_fill_kernel<<<(rows + 255) / 256, 256, 0, ctx->stream>>>(seg_off, rows, static_cast<int>(
+            std::min<size_t>(max_seg, INT_MAX)), seg_key);
+        if (check_launch("SFNN heavy-row segment map launch") != 0) return -1;
+        a.heavy_off = seg_off;
         a.heavy_partials = partials;
-        const int blocks = 3 * ctx->sm_count;
-        if (vec == 8) heavy_segment_kernel<8><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, seg_row, total, partials);
-        else if (vec == 4) heavy_segment_kernel<4><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, seg_row, total, partials);
-        else heavy_segment_kernel<1><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, seg_row, total, partials);
+        a.heavy_ok = static_cast<int>(std::min<size_t>(max_seg, INT_MAX));
+        const int blocks = 4 * ctx->sm_count;
+        const int ms = a.heavy_ok;
+        if (vec == 8)
+            heavy_segment_kernel<8><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, rows, ms, seg_key, partials);
+        else if (vec == 4)
+            heavy_segment_kernel<4><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, rows, ms, seg_key, partials);
+        else
+            heavy_segment_kernel<1><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a, rows, ms, seg_key, partials);
         if (check_launch("SFNN heavy-row segment launch") != 0) return -1;
     }
     switch (mode) {
@@ -1737,6 +1773,9 @@ struct SfnnPlan {
     const float* ft_bias;  // FT bias the gather starts from (fake-quantised under FT QAT)
     KingSortOut king;
     int* king_rank;
+    int* king_tiles;      // [kings + 1] first rank tile of each king block (tile-keyed FT row index)
+    int kings;
+    int max_king_tiles;
     Tiles tiles;
     float* w1_eff;
     float* head_partials;
@@ -1841,7 +1880,7 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
     const size_t king_ints = king_sort_scratch_ints<kSfnnKingKeys>(n_half);
     const size_t bucket_ints = king_sort_scratch_ints<kBucketKeys>(d.batch);
     const size_t tile_ints = 1 + 3 * static_cast<size_t>(max_tiles) + (kBucketKeys + 1);
-    const size_t sort_ints = king_ints + n_half + bucket_ints + tile_ints;
+    const size_t sort_ints = king_ints + n_half + bucket_ints + tile_ints + kSfnnKingKeys + 1;
     void* sp = nullptr;
     if (scratch_slot(ctx, kScratchSfnnSort, sort_ints * sizeof(int), &sp, "cudaMalloc SFNN sort") != 0) return -1;
     int* king_scratch = static_cast<int*>(sp);
@@ -1853,6 +1892,14 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
                                  &plan->king) != 0)
         return -1;
     plan->king_rank = rank;
+    {
+        // rank tiles of the king blocks (see RowTiles)
+        plan->kings = d.base > 0 ? d.base / kSfnnPieces : 1;
+        plan->king_tiles = tt + tile_ints;
+        plan->max_king_tiles = plan->kings + (n_half + kTileRanks - 1) / kTileRanks;
+        king_tiles_kernel<<<1, 32, 0, ctx->stream>>>(plan->king.key_off, plan->kings, kTileRanks, plan->king_tiles);
+        if (check_launch("SFNN king tile launch") != 0) return -1;
+    }
     {
         const int nblocks = (d.batch + kKingSortThreads - 1) / kKingSortThreads;
         int* key_off = bucket_scratch;
@@ -2139,6 +2186,7 @@ PieceRowArgs piece_row_args(const SfnnDims& d, const InverseIndex& index) {
     r.offsets = index.offsets;
     r.entries = index.entries;
     r.max_entries = 2 * static_cast<size_t>(d.batch) * static_cast<size_t>(d.max_active);
+    r.n_keys = index.n_rows;
     if (d.base > 0) {
         r.pieces = kSfnnPieces;
         r.kings = d.base / kSfnnPieces;
@@ -2282,7 +2330,9 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
     SfnnPlan plan{};
     if (sfnn_prepare(ctx, d, w, stm, nstm, buckets, nullptr, &plan) != 0) return -1;
     InverseIndex index;
-    if (build_inverse_index_rows(ctx, stm, nstm, d.batch, d.max_active, d.n_features, &index, plan.king_rank) != 0 ||
+    const RowTiles row_tiles{plan.king_tiles, plan.king.key_off, d.base > 0 ? kSfnnPieces : d.n_features, plan.kings,
+                             kTileRanks, plan.max_king_tiles};
+    if (build_inverse_index_tiled(ctx, stm, nstm, d.batch, d.max_active, row_tiles, &index, plan.king_rank) != 0 ||
         sort_inverse_index(ctx, index) != 0)
         return -1;
     StepBuffers sb{};
@@ -2337,6 +2387,7 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
     }
     prof_mark(ctx);
     PieceRowArgs r = piece_row_args(d, index);
+    r.tile_base = plan.king_tiles;
     r.src[0] = sb.pregrad;
     r.src[1] = sb.pregrad + d.width;
     r.src_stride = 2 * static_cast<size_t>(d.width);

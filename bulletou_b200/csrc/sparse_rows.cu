@@ -354,8 +354,51 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 namespace {
 
+// Tile-keyed map (RowTiles): one key per valid feature.
+struct TiledMap {
+    RowTiles t;
+    const int* entry_rank;
+    size_t max_active;
+    __device__ __forceinline__ int key(int f, size_t s, int persp, int* entry) const {
+        const int h = static_cast<int>((s / max_active) * 2 + persp);
+        const int e = entry_rank[h];
+        *entry = e;
+        if (f < 0 || f >= t.kings * t.pieces) return -1;
+        const int k = f / t.pieces;
+        const int p = f - k * t.pieces;
+        const int t0 = t.tile_base[k], nt = t.tile_base[k + 1] - t0;
+        const int off = e - t.rank_base[k];
+        const int tile = off <= 0 ? 0 : min(off / t.tile_ranks, nt - 1);
+        return (t0 + tile) * t.pieces + p;
+    }
+};
+
+__global__ void count_tiled_kernel(const int* __restrict__ stm, const int* __restrict__ nstm, size_t slots,
+                                   TiledMap map, int* __restrict__ counts) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= 2 * slots) return;
+    const int persp = t < slots ? 0 : 1;
+    const size_t s = persp == 0 ? t : t - slots;
+    int e;
+    const int key = map.key(persp == 0 ? stm[s] : nstm[s], s, persp, &e);
+    if (key >= 0) atomicAdd(&counts[key], 1);
+}
+
+__global__ void fill_tiled_kernel(const int* __restrict__ stm, const int* __restrict__ nstm, size_t slots,
+                                  TiledMap map, const int* __restrict__ offsets, int* __restrict__ cursor,
+                                  int* __restrict__ entries) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= 2 * slots) return;
+    const int persp = t < slots ? 0 : 1;
+    const size_t s = persp == 0 ? t : t - slots;
+    int e;
+    const int key = map.key(persp == 0 ? stm[s] : nstm[s], s, persp, &e);
+    if (key >= 0) entries[offsets[key] + atomicSub(&cursor[key], 1) - 1] = e;
+}
+
 int build_index_impl(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch, size_t max_active,
-                     const RowMap& map, size_t n_rows, InverseIndex* out, const int* entry_rank) {
+                     const RowMap& map, size_t n_rows, InverseIndex* out, const int* entry_rank,
+                     const TiledMap* tiled = nullptr) {
     const size_t slots = batch * max_active;
     const size_t max_entries = 2 * slots * (map.factorized ? 2 : 1);
     if (n_rows >= static_cast<size_t>(INT_MAX) - kScanTile || max_entries >= static_cast<size_t>(INT_MAX) ||
@@ -381,7 +424,8 @@ int build_index_impl(BulletOuCudaCppContext* ctx, const int* stm, const int* nst
     int* o = static_cast<int*>(offsets);
     int* t = static_cast<int*>(tile_sums);
     if (blocks > 0) {
-        count_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, map, c);
+        if (tiled != nullptr) count_tiled_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, *tiled, c);
+        else count_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, map, c);
         if (check_launch("sparse count launch") != 0) return -1;
     }
     const int n = static_cast<int>(n_rows);
@@ -390,8 +434,12 @@ int build_index_impl(BulletOuCudaCppContext* ctx, const int* stm, const int* nst
     scan_apply_kernel<<<tiles, kScanThreads, 0, ctx->stream>>>(c, n, t, tiles, o);
     if (check_launch("sparse scan launch") != 0) return -1;
     if (blocks > 0) {
-        fill_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, max_active, map, o, c,
-                                                             static_cast<int*>(entries), entry_rank);
+        if (tiled != nullptr)
+            fill_tiled_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, *tiled, o, c,
+                                                                  static_cast<int*>(entries));
+        else
+            fill_rows_kernel<<<blocks, threads, 0, ctx->stream>>>(stm, nstm, slots, max_active, map, o, c,
+                                                                 static_cast<int*>(entries), entry_rank);
         if (check_launch("sparse fill launch") != 0) return -1;
     }
     out->offsets = o;
@@ -403,6 +451,14 @@ int build_index_impl(BulletOuCudaCppContext* ctx, const int* stm, const int* nst
 }
 
 }  // namespace
+
+int exclusive_scan_counts(BulletOuCudaCppContext* ctx, const int* counts, int n, int* offsets, int* tile_sums) {
+    const int tiles = scan_tiles(n);
+    scan_tile_sums_kernel<<<tiles, kScanThreads, 0, ctx->stream>>>(counts, n, tile_sums);
+    scan_tile_offsets_kernel<<<1, kScanThreads, 0, ctx->stream>>>(tile_sums, tiles);
+    scan_apply_kernel<<<tiles, kScanThreads, 0, ctx->stream>>>(counts, n, tile_sums, tiles, offsets);
+    return check_launch("exclusive scan launch");
+}
 
 int sort_inverse_index(BulletOuCudaCppContext* ctx, const InverseIndex& index) {
     if (index.n_rows <= 0) return 0;
@@ -423,6 +479,16 @@ int build_inverse_index_rows(BulletOuCudaCppContext* ctx, const int* stm, const 
     map.input_size = static_cast<int>(n_features);
     map.factorized = 0;
     return build_index_impl(ctx, stm, nstm, batch, max_active, map, n_features, out, entry_rank);
+}
+
+int build_inverse_index_tiled(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
+                              size_t max_active, const RowTiles& tiles, InverseIndex* out, const int* entry_rank) {
+    if (entry_rank == nullptr) return fail_message("internal: the tiled index needs entry ranks");
+    TiledMap tm{tiles, entry_rank, max_active};
+    RowMap unused{};
+    return build_index_impl(ctx, stm, nstm, batch, max_active, unused,
+                            static_cast<size_t>(tiles.max_tiles) * static_cast<size_t>(tiles.pieces), out, entry_rank,
+                            &tm);
 }
 
 int launch_row_kernel(BulletOuCudaCppContext* ctx, int mode, const RowKernelArgs& args, int rows_to_process) {

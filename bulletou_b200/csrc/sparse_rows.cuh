@@ -64,6 +64,31 @@ int build_inverse_index(BulletOuCudaCppContext* ctx, const int* stm, const int* 
                         size_t max_active, size_t input_size, size_t n_rows, InverseIndex* out,
                         const int* entry_rank = nullptr);
 
+// Tile-keyed index of a king-ordered layout (SFNN): the entry ids are ranks in
+// the king-sorted half-position order, king block k owning the ranks
+// [rank_base[k], rank_base[k + 1]).  A king block's ranks are cut into tiles
+// of tile_ranks; key = tile * pieces + piece, where tile = tile_base[k] + the
+// tile of the entry's rank (clamped into the king's tiles).  A row (k, p) is
+// the union of the keys t * pieces + p for t in [tile_base[k], tile_base[k+1]).
+struct RowTiles {
+    const int* tile_base;  // [kings + 1], device
+    const int* rank_base;  // [kings + 1], device
+    int pieces;
+    int kings;
+    int tile_ranks;
+    int max_tiles;         // host bound of tile_base[kings]
+};
+
+// Builds the tile-keyed index (n_rows = max_tiles * pieces keys); features
+// outside [0, kings * pieces) are skipped.  entry_rank must be given.
+int build_inverse_index_tiled(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,
+                              size_t max_active, const RowTiles& tiles, InverseIndex* out, const int* entry_rank);
+
+// Deterministic exclusive scan of counts[0, n) into offsets[0, n] (offsets[n]
+// = total) on ctx->stream; tile_sums needs scan_tiles(n) + 1 ints.
+inline int scan_tiles(int n) { return (n + 4 * 1024 - 1) / (4 * 1024); }
+int exclusive_scan_counts(BulletOuCudaCppContext* ctx, const int* counts, int n, int* offsets, int* tile_sums);
+
 // Sorts every row's entry list ascending in place (rows with more than
 // kSortCap entries are left in fill order), so that consumers can sum a row in
 // a fixed order without sorting it themselves.
