@@ -965,8 +965,15 @@ SFNN_DRAM_BYTES_B65536 = {
     "fold": (1124865536, ("all",)),
 }
 
-# The same on the default --data psv batches (decoded PackedSfenValue records).
-SFNN_DRAM_BYTES_PSV_B65536 = {}
+# The same on the default --data psv batches (decoded PackedSfenValue records;
+# capture of `bench.py --steps 1 --warmup 3 --no-cpu-baseline`).
+SFNN_DRAM_BYTES_PSV_B65536 = {
+    "ft_rows_ranger": (11025470720, ("all",)),
+    "ft_forward": (1181280768, ("all",)),
+    "ft_integer": (569521408, ("all",)),
+    "l1_backward": (2068910848, ("all",)),
+    "fold": (1124453632, ("all",)),
+}
 
 
 def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 6.0, qat="none", data="psv"):

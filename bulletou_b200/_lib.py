@@ -171,6 +171,7 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_nnue_integer_forward_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, I, P, P, P],
     "bulletou_b200_sfnn_integer_forward_device": [P, P, Z, Z] + [P] * 9,
     "bulletou_b200_teacher_prepare_device": [P, P, P, Z] + [P] * 7,
+    "bulletou_b200_hcpe_to_psv_device": [P, P, Z, P, P, P],
 }
 
 

@@ -116,6 +116,7 @@ enum ScratchSlot : int {
     kScratchSfnnQatTable = 24,  // SFNN dense QAT with FT QAT: integer FT table (i16)
     kScratchNnueQuant = 25,     // integer HalfKP forward: transformed features (u8)
     kScratchSfnnHeavy = 26,     // SFNN FT rows: segment plan and partial sums of heavy rows
+    kScratchHcpe = 27,          // HCPE -> PackedSfenValue: uncompacted records, valid flags, scan
 };
 
 int ok();

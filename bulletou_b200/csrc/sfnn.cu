@@ -1721,11 +1721,12 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, con
     }
     {
         // Heavy-row segments: counts, their exclusive scan, the segment sums.
-        // Segments <= entries / heavy_seg + heavy rows < entries / heavy_seg + entries / heavy_row.
+        // Segments <= entries / heavy_seg + the keys of heavy rows (each key adds
+        // at most one partial segment) <= entries / heavy_seg + n_keys.
         a.heavy_row = kHeavyRow;
         a.heavy_seg = kHeavySeg;
         const int rows = a.n_keys;
-        const size_t max_seg = a.max_entries / a.heavy_seg + a.max_entries / a.heavy_row + 1;
+        const size_t max_seg = a.max_entries / a.heavy_seg + static_cast<size_t>(a.n_keys) + 1;
         const size_t tiles = static_cast<size_t>(scan_tiles(rows)) + 1;
         const size_t ints = align_floats(2 * static_cast<size_t>(rows) + 1 + tiles + max_seg);
         void* hp = nullptr;

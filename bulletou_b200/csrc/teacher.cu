@@ -26,9 +26,11 @@
 // counted in `overflow` (the reference aborts on it).
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstdint>
 
 #include "common.cuh"
+#include "sparse_rows.cuh"
 
 namespace bou {
 namespace {
@@ -57,6 +59,8 @@ __constant__ int16_t kHandBase[7][2] = {{20, 1}, {44, 39}, {54, 49}, {64, 59}, {
 __constant__ int8_t kBoardOrder[15] = {-1, 0, 1, 2, 3, 5, 6, 4, -1, 7, 8, 9, 10, 11, 12};
 // Hand slot of an unpromoted type (Hand::piece_index, types.rs:256-267).
 __constant__ int8_t kHandSlot[8] = {-1, 0, 1, 2, 3, 5, 6, 4};
+// Unpromoted type of each hand slot (HAND_PIECE_TYPES, types.rs:371-379).
+__constant__ int8_t kHandType[7] = {PAWN, LANCE, KNIGHT, SILVER, GOLD, BISHOP, ROOK};
 __constant__ int16_t kKingCount[8] = {1, 9, 81, 81, 169, 441, 441, 841};
 __constant__ int8_t kHandAxis[7] = {1, 2, 4, 8, 8, 16, 32};
 
@@ -129,6 +133,18 @@ __device__ __forceinline__ int promote_type(int pt) {
         case SILVER: return PRO_SILVER;
         case BISHOP: return HORSE;
         case ROOK: return DRAGON;
+        default: return pt;
+    }
+}
+
+__device__ __forceinline__ int unpromote_type(int pt) {
+    switch (pt) {
+        case PRO_PAWN: return PAWN;
+        case PRO_LANCE: return LANCE;
+        case PRO_KNIGHT: return KNIGHT;
+        case PRO_SILVER: return SILVER;
+        case HORSE: return BISHOP;
+        case DRAGON: return ROOK;
         default: return pt;
     }
 }
@@ -468,6 +484,215 @@ __global__ void __launch_bounds__(kTeacherThreads) teacher_psv_kernel(TeacherArg
     }
 }
 
+
+// ------------------------------------------------------------------ HCPE records
+// decode_hcpe_record (crates/bulletou_lib/src/value/loader/hcpe.rs:65-76):
+// Apery / cshogi HuffmanCodedPos (MiniPosition::from_hcp, loader/shogipack.rs:
+// 353-408: knight / silver codes swapped against the PackedSfen table, colour
+// bit before the promotion bit, hands and piece box in one 3/5/7-bit prefix
+// code) re-packed as a PackedSfenValue (pack_to_psfen, :477-554; game_ply 0;
+// the game result turned to the side to move, convert_game_result :679-697).
+// A record with a king square >= 81 or an unknown hand code is invalid: the
+// reference's loader skips it, here it is dropped from the compacted output.
+constexpr int kHcpeBytes = 38;
+constexpr int kHcpeStride = 11;   // words per staged record (44 bytes, odd stride)
+
+__constant__ uint8_t kHcpPattern[8] = {0x00, 0x01, 0x03, 0x07, 0x0b, 0x1f, 0x3f, 0x0f};
+// {code, bits, piece type, colour (2: piece box)} (shogipack.rs:81-105)
+__constant__ uint8_t kHcpHand[21][4] = {
+    {0x00, 3, PAWN, 0},   {0x01, 5, LANCE, 0},  {0x03, 5, KNIGHT, 0}, {0x05, 5, SILVER, 0}, {0x07, 5, GOLD, 0},
+    {0x1f, 7, BISHOP, 0}, {0x3f, 7, ROOK, 0},   {0x04, 3, PAWN, 1},   {0x11, 5, LANCE, 1},  {0x13, 5, KNIGHT, 1},
+    {0x15, 5, SILVER, 1}, {0x17, 5, GOLD, 1},   {0x5f, 7, BISHOP, 1}, {0x7f, 7, ROOK, 1},   {0x02, 3, PAWN, 2},
+    {0x09, 5, LANCE, 2},  {0x0b, 5, KNIGHT, 2}, {0x0d, 5, SILVER, 2}, {0x1d, 5, GOLD, 2},   {0x0f, 7, BISHOP, 2},
+    {0x2f, 7, ROOK, 2}};
+// PackedSfen table index of an unpromoted type (piece_type_to_index, shogipack.rs:212-224)
+__constant__ int8_t kPsvIndex[8] = {0, 1, 2, 3, 4, 5, 6, 7};
+
+struct HcpeShared {
+    uint32_t rec[kTeacherThreads * kHcpeStride];
+    uint32_t out[kTeacherThreads * kRecordStride];
+    uint8_t board[81][kTeacherThreads];
+    uint8_t board_code[256];   // idx | len << 4 of the HCP board code the next 8 bits start with
+    uint8_t hand_code[256];    // entry of kHcpHand, 0xff: no code within 7 bits
+};
+
+// LSB-first writer that drops bits past 256 (BitWriter, shogipack.rs:150-185).
+struct BitWriter32 {
+    uint32_t* words;
+    uint64_t buf;
+    int n;
+    int cursor;
+    __device__ void put(uint32_t v, int k) {
+        if (cursor >= 256) return;
+        k = min(k, 256 - cursor);
+        buf |= static_cast<uint64_t>(v & ((1u << k) - 1u)) << n;
+        n += k;
+        cursor += k;
+        if (n >= 32) {
+            words[(cursor - n) >> 5] = static_cast<uint32_t>(buf);
+            buf >>= 32;
+            n -= 32;
+        }
+    }
+    __device__ void flush() {
+        if (n > 0) words[(cursor - n) >> 5] = static_cast<uint32_t>(buf);
+    }
+};
+
+__global__ void __launch_bounds__(kTeacherThreads) hcpe_psv_kernel(const uint8_t* __restrict__ hcpe, int64_t n,
+                                                                   uint32_t* __restrict__ psv, int* __restrict__ valid) {
+    __shared__ HcpeShared sh;
+    const int t = threadIdx.x;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * kTeacherThreads;
+    const int here = static_cast<int>(n - first < kTeacherThreads ? n - first : kTeacherThreads);
+    for (int v = t; v < 256; v += kTeacherThreads) {
+        uint8_t board = 0xff, hand = 0xff;
+        for (int idx = 0; idx < 8; ++idx) {
+            const int len = kHuffLen[idx];   // the HCP board lengths equal the PackedSfen ones
+            if ((v & ((1 << len) - 1)) == kHcpPattern[idx]) board = static_cast<uint8_t>(idx | (len << 4));
+        }
+        for (int e = 0; e < 21; ++e) {
+            const int len = kHcpHand[e][1];
+            if ((v & ((1 << len) - 1)) == kHcpHand[e][0]) hand = static_cast<uint8_t>(e);
+        }
+        sh.board_code[v] = board;
+        sh.hand_code[v] = hand;
+    }
+    uint8_t* rb = reinterpret_cast<uint8_t*>(sh.rec);
+    const uint8_t* src = hcpe + first * kHcpeBytes;
+    for (int b = t; b < here * kHcpeBytes; b += kTeacherThreads) {
+        const int r = b / kHcpeBytes;
+        rb[r * kHcpeStride * 4 + (b - r * kHcpeBytes)] = src[b];
+    }
+    __syncthreads();
+    int ok = 0;
+    uint32_t* out = sh.out + t * kRecordStride;
+    if (t < here) {
+        const uint32_t* rec = sh.rec + t * kHcpeStride;
+        BitReader r{rec, 0ull, 0, 0, 0};
+        const int stm = static_cast<int>(r.peek8() & 1u);
+        r.consume(1);
+        const int bk = static_cast<int>(r.peek8() & 127u);
+        r.consume(7);
+        const int wk = static_cast<int>(r.peek8() & 127u);
+        r.consume(7);
+        int hands[14];
+#pragma unroll
+        for (int i = 0; i < 14; ++i) hands[i] = 0;
+        ok = bk < 81 && wk < 81;
+        if (ok) {
+            for (int sq = 0; sq < 81; ++sq) {
+                int code = 0;
+                if (sq != bk && sq != wk) {
+                    const uint32_t bits = r.peek8();
+                    const int e = sh.board_code[bits];
+                    const int idx = e & 15, len = e >> 4;
+                    if (idx == 0) {
+                        r.consume(len);
+                    } else {
+                        const uint32_t rest = bits >> len;
+                        const int color = rest & 1u;
+                        int promoted = 0;
+                        if (idx != 7) {
+                            promoted = (rest >> 1) & 1u;
+                            r.consume(len + 2);
+                        } else {
+                            r.consume(len + 1);
+                        }
+                        const int base = kHuffType[idx];
+                        code = (promoted ? promote_type(base) : base) | (color << 4);
+                    }
+                }
+                sh.board[sq][t] = static_cast<uint8_t>(code);
+            }
+            while (ok && r.cursor < 256) {
+                const int e = sh.hand_code[r.peek8()];
+                if (e == 0xff) {
+                    ok = 0;
+                    break;
+                }
+                r.consume(kHcpHand[e][1]);
+                const int owner = kHcpHand[e][3];
+                if (owner < 2) {
+                    const int i = owner * 7 + kHandSlot[kHcpHand[e][2] == GOLD ? 7 : kHcpHand[e][2]];
+                    hands[i] = (hands[i] + 1) & 0xff;
+                }
+            }
+        }
+        if (ok) {
+            // pack_to_psfen: a king square is the first square holding that king
+            const int kb = bk != wk ? bk : 81, kw = wk;
+            BitWriter32 w{out, 0ull, 0, 0};
+            w.put(static_cast<uint32_t>(stm), 1);
+            w.put(static_cast<uint32_t>(kb), 7);
+            w.put(static_cast<uint32_t>(kw), 7);
+            for (int sq = 0; sq < 81; ++sq) {
+                if (sq == kb || sq == kw) continue;
+                const int code = sh.board[sq][t];
+                if (code == 0) {
+                    w.put(0u, 1);
+                    continue;
+                }
+                const int pt = code & 15, color = code >> 4;
+                const int raw = unpromote_type(pt);
+                const int idx = kPsvIndex[raw == GOLD ? 7 : raw];
+                const int len = kHuffLen[idx];
+                uint32_t v = kHuffPattern[idx];
+                if (raw != GOLD) {
+                    v |= static_cast<uint32_t>(pt != raw) << len;
+                    v |= static_cast<uint32_t>(color) << (len + 1);
+                    w.put(v, len + 2);
+                } else {
+                    v |= static_cast<uint32_t>(color) << len;
+                    w.put(v, len + 1);
+                }
+            }
+            for (int color = 0; color < 2; ++color) {
+                for (int h = 0; h < 7; ++h) {
+                    const int pt = kHandType[h];
+                    const int idx = kPsvIndex[pt];
+                    const int len = kHuffLen[idx] - 1;
+                    const uint32_t code = kHuffPattern[idx] >> 1;
+                    const uint32_t v = pt != GOLD ? (code | (static_cast<uint32_t>(color) << (len + 1)))
+                                                  : (code | (static_cast<uint32_t>(color) << len));
+                    const int k = pt != GOLD ? len + 2 : len + 1;
+                    for (int c = 0; c < hands[color * 7 + h]; ++c) w.put(v, k);
+                }
+            }
+            while (w.cursor < 256) w.put(0b010u, 3);          // piece-box pawns
+            w.flush();
+            const uint32_t* rw = rec;
+            out[8] = rw[8];                                    // eval, bestMove16
+            const int res = static_cast<int>((rw[9] >> 0) & 0xffu);   // byte 36: 0 draw, 1 black, 2 white
+            const int r8 = res == 1 ? (stm == 0 ? 1 : -1) : (res == 2 ? (stm == 1 ? 1 : -1) : 0);
+            out[9] = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(r8))) << 16;  // ply 0
+        }
+        if (!ok) {
+#pragma unroll
+            for (int i = 0; i < kRecordWords; ++i) out[i] = 0u;
+        }
+        valid[first + t] = ok;
+    }
+    __syncthreads();
+    uint32_t* dst = psv + first * kRecordWords;
+    for (int e = t; e < here * kRecordWords; e += kTeacherThreads) {
+        const int row = e / kRecordWords;
+        dst[e] = sh.out[row * kRecordStride + (e - row * kRecordWords)];
+    }
+}
+
+// Copies the valid records to their compacted positions (offsets: exclusive
+// scan of the valid flags, offsets[n] = the count).
+__global__ void hcpe_compact_kernel(const uint32_t* __restrict__ psv_all, const int* __restrict__ valid,
+                                    const int* __restrict__ offsets, int64_t n, uint32_t* __restrict__ psv,
+                                    int* __restrict__ count) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i == 0) *count = offsets[n];
+    if (i >= n * kRecordWords) return;
+    const int64_t r = i / kRecordWords;
+    if (valid[r]) psv[static_cast<int64_t>(offsets[r]) * kRecordWords + (i - r * kRecordWords)] = psv_all[i];
+}
+
 }  // namespace
 }  // namespace bou
 
@@ -524,6 +749,47 @@ int bulletou_b200_teacher_prepare_device(BulletOuCudaCppContext* ctx, const Bull
     a.score_drop_abs = c.score_drop_abs;
     teacher_psv_kernel<<<blocks, kTeacherThreads, 0, ctx->stream>>>(a);
     if (check_launch("teacher prepare launch") != 0) return -1;
+    return ok();
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int bulletou_b200_hcpe_to_psv_device(BulletOuCudaCppContext* ctx, const BulletOuCudaCppI32Buffer* hcpe,
+                                     size_t n_records, BulletOuCudaCppI32Buffer* psv, BulletOuCudaCppI32Buffer* count,
+                                     BulletOuCudaCppI32Buffer* valid) {
+    const size_t in_words = (n_records * kHcpeBytes + 3) / 4;
+    if (validate_i32(ctx, hcpe, in_words, "hcpe records") != 0 ||
+        validate_i32(ctx, psv, n_records * kRecordWords, "hcpe psv output") != 0 ||
+        validate_i32(ctx, count, 1, "hcpe count") != 0)
+        return -1;
+    if (valid != nullptr && validate_i32(ctx, valid, n_records, "hcpe valid flags") != 0) return -1;
+    if (n_records >= static_cast<size_t>(INT_MAX) / kRecordWords) return fail_message("hcpe: too many records");
+    if (set_device(ctx) != 0) return -1;
+    const int n = static_cast<int>(n_records);
+    const size_t tiles = static_cast<size_t>(scan_tiles(n)) + 1;
+    const size_t ints = n_records * kRecordWords + 2 * n_records + 1 + tiles + (valid == nullptr ? n_records : 0);
+    void* sp = nullptr;
+    if (scratch_slot(ctx, kScratchHcpe, ints * sizeof(int), &sp, "cudaMalloc HCPE scratch") != 0) return -1;
+    uint32_t* psv_all = static_cast<uint32_t*>(sp);
+    int* offsets = reinterpret_cast<int*>(psv_all + n_records * kRecordWords);
+    int* tile_sums = offsets + n_records + 1;
+    int* flags = valid != nullptr ? valid->ptr : tile_sums + tiles;
+    if (n_records == 0) {
+        cudaError_t st = cudaMemsetAsync(count->ptr, 0, sizeof(int), ctx->stream);
+        return st == cudaSuccess ? ok() : fail("cudaMemsetAsync hcpe count", st);
+    }
+    int blocks = 0;
+    if (grid_1d(n_records, kTeacherThreads, &blocks, "hcpe decode") != 0) return -1;
+    hcpe_psv_kernel<<<blocks, kTeacherThreads, 0, ctx->stream>>>(reinterpret_cast<const uint8_t*>(hcpe->ptr),
+                                                                 static_cast<int64_t>(n_records), psv_all, flags);
+    if (check_launch("hcpe decode launch") != 0) return -1;
+    if (exclusive_scan_counts(ctx, flags, n, offsets, tile_sums) != 0) return -1;
+    if (grid_1d(n_records * kRecordWords, 256, &blocks, "hcpe compact") != 0) return -1;
+    hcpe_compact_kernel<<<blocks, 256, 0, ctx->stream>>>(psv_all, flags, offsets, static_cast<int64_t>(n_records),
+                                                         reinterpret_cast<uint32_t*>(psv->ptr), count->ptr);
+    if (check_launch("hcpe compact launch") != 0) return -1;
     return ok();
 }
 

@@ -328,3 +328,101 @@ def psv_records(seed: int, n: int, rank: int = 0, **kw) -> np.ndarray:
     ply = rng.integers(1, 320, n)
     move = rng.integers(0, 1 << 16, n)
     return psv_encode(p["stm"], p["black_king"], p["white_king"], p["board"], p["hands"], score, result, ply, move)
+
+
+# ---------------------------------------------------------------- HCPE records
+# Apery / cshogi HuffmanCodedPos codes (the reference's HCP tables,
+# crates/bulletou_lib/src/value/loader/shogipack.rs:60-105): knight and silver
+# swapped against the PackedSfen table, the colour bit before the promotion
+# bit, hand pieces and piece box in one prefix code.
+_HCP_BOARD_CODE = {PAWN: (0x01, 2), LANCE: (0x03, 4), KNIGHT: (0x07, 4), SILVER: (0x0b, 4), BISHOP: (0x1f, 6),
+                   ROOK: (0x3f, 6), GOLD: (0x0f, 5)}
+_HCP_HAND_CODE = {(PAWN, 0): (0x00, 3), (LANCE, 0): (0x01, 5), (KNIGHT, 0): (0x03, 5), (SILVER, 0): (0x05, 5),
+                  (GOLD, 0): (0x07, 5), (BISHOP, 0): (0x1f, 7), (ROOK, 0): (0x3f, 7),
+                  (PAWN, 1): (0x04, 3), (LANCE, 1): (0x11, 5), (KNIGHT, 1): (0x13, 5), (SILVER, 1): (0x15, 5),
+                  (GOLD, 1): (0x17, 5), (BISHOP, 1): (0x5f, 7), (ROOK, 1): (0x7f, 7)}
+HCPE_DTYPE = np.dtype([("hcp", "u1", 32), ("eval", "<i2"), ("best_move16", "<u2"), ("game_result", "u1"),
+                       ("dummy", "u1")])
+
+
+def hcpe_encode(stm, black_king, white_king, board, hands, eval_=0, game_result=0, best_move16=0) -> np.ndarray:
+    """Encode positions as HCPE records (38 bytes: HCP, eval, bestMove16,
+    gameResult 0 draw / 1 black win / 2 white win, padding) -- the inverse of
+    MiniPosition::from_hcp.  Same inputs as psv_encode; short positions are
+    padded with piece-box pawns (a piece-box lance at a 4/5-bit tail)."""
+    stm = np.atleast_1d(np.asarray(stm, np.int64))
+    n = stm.size
+    bk = np.broadcast_to(np.asarray(black_king, np.int64), (n,))
+    wk = np.broadcast_to(np.asarray(white_king, np.int64), (n,))
+    board = np.asarray(board, np.int64).reshape(n, 81)
+    hands = np.asarray(hands, np.int64).reshape(n, 2, 7)
+    bits = np.zeros((n, 256 + 16), np.uint8)
+    cursor = np.zeros(n, np.int64)
+    rows = np.arange(n)
+
+    def write(value, length, mask=None):
+        value = np.broadcast_to(np.asarray(value, np.int64), (n,))
+        length = np.broadcast_to(np.asarray(length, np.int64), (n,))
+        if mask is not None:
+            length = np.where(mask, length, 0)
+        for b in range(int(length.max(initial=0))):
+            m = b < length
+            if (cursor[m] + b >= 256).any():
+                raise ValueError("position needs more than 256 bits")
+            bits[rows[m], cursor[m] + b] = (value[m] >> b) & 1
+        cursor[:] += length
+
+    write(stm, 1)
+    write(bk, 7)
+    write(wk, 7)
+    for sq in range(81):
+        code = board[:, sq]
+        pt, color = code & 15, (code >> 4) & 1
+        value = np.zeros(n, np.int64)
+        length = np.ones(n, np.int64)
+        for t in range(1, 15):
+            m = pt == t
+            if not m.any():
+                continue
+            base = _UNPROMOTE.get(t, t)
+            pattern, k = _HCP_BOARD_CODE[base]
+            if base == GOLD:
+                value[m] = pattern | (color[m] << k)
+                length[m] = k + 1
+            else:
+                value[m] = pattern | (color[m] << k) | ((1 if t in _UNPROMOTE else 0) << (k + 1))
+                length[m] = k + 2
+        write(value, length, (sq != bk) & (sq != wk))
+    for color in (0, 1):
+        for h, pt in enumerate(HAND_TYPES):
+            code, k = _HCP_HAND_CODE[(pt, color)]
+            for i in range(int(hands[:, color, h].max(initial=0))):
+                write(code, k, hands[:, color, h] > i)
+    while True:
+        r = 256 - cursor
+        if (r == 1).any():
+            raise ValueError("a 1-bit tail cannot be padded with piece-box pieces")
+        pawn = (r >= 3) & (r != 4) & (r != 5)
+        if not pawn.any():
+            break
+        write(0b010, 3, pawn)                                      # piece-box pawn (0x02, 3 bits)
+    r = 256 - cursor
+    write(0b10, 2, r == 2)                                         # its first two bits; the third reads as 0
+    write(0b1001, 4, r == 4)                                       # piece-box lance (0x09, 5 bits), 4 written
+    write(0b01001, 5, r == 5)
+    assert (cursor == 256).all()
+    out = np.zeros(n, HCPE_DTYPE)
+    out["hcp"] = np.packbits(bits[:, :256], axis=1, bitorder="little")
+    out["eval"] = np.broadcast_to(np.asarray(eval_, np.int64), (n,)).astype(np.int16)
+    out["best_move16"] = np.broadcast_to(np.asarray(best_move16, np.int64), (n,)).astype(np.uint16)
+    out["game_result"] = np.broadcast_to(np.asarray(game_result, np.int64), (n,)).astype(np.uint8)
+    return out
+
+
+def hcpe_records(seed: int, n: int, rank: int = 0, **kw) -> np.ndarray:
+    """`n` seeded HCPE records of full-set positions (as psv_records)."""
+    rng = rng_for(seed, rank)
+    p = psv_positions(rng, n, **kw)
+    ev = np.clip(np.rint(rng.normal(0.0, 600.0, n)), -3000, 3000).astype(np.int64)
+    return hcpe_encode(p["stm"], p["black_king"], p["white_king"], p["board"], p["hands"], ev,
+                       rng.integers(0, 3, n), rng.integers(0, 1 << 16, n))

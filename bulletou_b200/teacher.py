@@ -330,3 +330,51 @@ class TeacherUploadSlot:
         self.upload_ready.record(upload_ctx)
         self.in_use = True
         return src.length * 4
+
+
+# ------------------------------------------------------------------ HCPE records
+HCPE_RECORD_BYTES = 38
+
+
+def hcpe_to_psv_device(ctx: Context, hcpe: I32Buffer, n_records: int, psv: I32Buffer, count: I32Buffer,
+                       valid: Optional[I32Buffer] = None) -> None:
+    """HCPE records (38 bytes each, back to back in `hcpe`) -> PackedSfenValue
+    records, the valid ones compacted in input order into `psv`, their number
+    into count[0] (decode_hcpe_record, value/loader/hcpe.rs:65-76)."""
+    ctx.lib.call("bulletou_b200_hcpe_to_psv_device", ctx.as_ptr(), hcpe.as_ptr(), int(n_records), psv.as_ptr(),
+                 count.as_ptr(), None if valid is None else valid.as_ptr())
+
+
+class HcpeConverter:
+    """Uploads up to `capacity` HCPE records and converts them on the device
+    into PackedSfenValue records that TeacherBatchProducer decodes; invalid
+    records are dropped like the reference's loader drops them."""
+
+    def __init__(self, ctx: Context, capacity: int):
+        self.ctx = ctx
+        self.capacity = int(capacity)
+        self.hcpe = I32Buffer(ctx, (self.capacity * HCPE_RECORD_BYTES + 3) // 4)
+        self.psv = I32Buffer(ctx, self.capacity * PSV_RECORD_WORDS)
+        self.count = I32Buffer(ctx, 1)
+        self.valid = I32Buffer(ctx, self.capacity)
+
+    def convert(self, ctx: Context, records) -> int:
+        """Converts `records` (HCPE_DTYPE array, uint8 [n, 38] or bytes);
+        returns how many were valid (a device-to-host read)."""
+        if isinstance(records, (bytes, bytearray, memoryview)):
+            a = np.frombuffer(records, dtype=np.uint8)
+        else:
+            a = np.asarray(records)
+            if a.dtype.fields is not None:
+                a = np.atleast_1d(a).view(np.uint8)
+        a = np.ascontiguousarray(a, dtype=np.uint8).reshape(-1)
+        if a.size % HCPE_RECORD_BYTES:
+            raise CudaCppError(f"HCPE records must be {HCPE_RECORD_BYTES}-byte records (got {a.size} bytes)")
+        n = a.size // HCPE_RECORD_BYTES
+        if n > self.capacity:
+            raise CudaCppError(f"{n} HCPE records exceed the converter capacity {self.capacity}")
+        words = np.zeros(self.hcpe.length * 4, np.uint8)
+        words[:a.size] = a
+        self.hcpe.upload(words.view(np.int32), ctx)
+        hcpe_to_psv_device(ctx, self.hcpe, n, self.psv, self.count, self.valid)
+        return int(self.count.download(ctx)[0])

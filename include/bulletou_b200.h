@@ -405,6 +405,19 @@ int bulletou_b200_teacher_prepare_device(BulletOuCudaCppContext* ctx, const Bull
     BulletOuCudaCppI32Buffer* buckets, BulletOuCudaCppF32Buffer* targets, BulletOuCudaCppF32Buffer* entry_weights,
     BulletOuCudaCppI32Buffer* overflow);
 
+/* HCPE records (38 bytes each: Apery / cshogi HuffmanCodedPos, eval i16,
+ * bestMove16, gameResult 0 draw / 1 black win / 2 white win, padding), packed
+ * back to back in an i32 buffer of ceil(38 n / 4) words, converted to
+ * PackedSfenValue records as the reference's decode_hcpe_record does
+ * (crates/bulletou_lib/src/value/loader/hcpe.rs:65-76: from_hcp, then
+ * pack_to_psfen, game_ply 0, the result turned to the side to move).  The
+ * records that decode are written compacted, in input order, to psv (n x 10
+ * words) and their number to count[0]; a record with a king square >= 81 or
+ * an unknown hand code is dropped, as the reference's loader skips it.
+ * valid (optional) receives the per-record flags. */
+int bulletou_b200_hcpe_to_psv_device(BulletOuCudaCppContext* ctx, const BulletOuCudaCppI32Buffer* hcpe,
+    size_t n_records, BulletOuCudaCppI32Buffer* psv, BulletOuCudaCppI32Buffer* count, BulletOuCudaCppI32Buffer* valid);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,8 @@ def lib():
         L.oracle_teacher_bucket_count.restype = i
         L.oracle_wrm_table.argtypes = [f, f, f, p]
         L.oracle_wrm_table.restype = None
+        L.oracle_hcpe_to_psv.argtypes = [p, p]
+        L.oracle_hcpe_to_psv.restype = i
         _ready = True
     return L
 
@@ -150,3 +152,17 @@ def wrm_table(offset=270.0, scaling=380.0, epsilon=0.0) -> np.ndarray:
     t = np.empty(65536, np.float32)
     lib().oracle_wrm_table(offset, scaling, epsilon, _p(t))
     return t
+
+
+def hcpe_to_psv(records) -> tuple:
+    """(PackedSfenValue records of the valid HCPE records in input order,
+    per-record valid flags) -- decode_hcpe_record on each 38-byte record."""
+    data = _u8(records)
+    n = data.size // 38
+    out = np.zeros((n, 40), np.uint8)
+    valid = np.zeros(n, np.int32)
+    L = lib()
+    for i in range(n):
+        rec = np.ascontiguousarray(data[38 * i:38 * (i + 1)])
+        valid[i] = L.oracle_hcpe_to_psv(_p(rec), _p(out[i]))
+    return out[valid == 1].copy(), valid

@@ -539,3 +539,168 @@ void oracle_wrm_table(float offset, float scaling, float epsilon, float* table) 
         table[raw + 32768] = epsilon == 0.0f ? prob : epsilon + (1.0f - 2.0f * epsilon) * prob;
     }
 }
+
+/* ------------------------------------------------------------ HCPE records */
+/* decode_hcpe_record (crates/bulletou_lib/src/value/loader/hcpe.rs:65-76):
+ * MiniPosition::from_hcp (loader/shogipack.rs:353-408) with the Apery / cshogi
+ * tables (shogipack.rs:60-105: knight and silver codes swapped against the
+ * PackedSfen table, colour bit before the promotion bit, hands and piece box
+ * in one prefix code), then pack_to_psfen (:477-554: board in square order,
+ * hands by colour and type, piece-box pawns up to bit 256, writes past bit 256
+ * dropped), to_packed_sfen_value (:557-569: game_ply 0) and
+ * convert_game_result (:679-697).  Returns 1 and writes the 40-byte record, or
+ * 0 for a record the reference skips (a king square >= 81, an unknown hand
+ * code). */
+static const uint32_t HCP_PATTERN[8] = {0x00, 0x01, 0x03, 0x07, 0x0b, 0x1f, 0x3f, 0x0f};
+static const int HCP_LEN[8] = {1, 2, 4, 4, 4, 6, 6, 5};
+static const int HCP_TYPE[8] = {PT_NONE, PAWN, LANCE, KNIGHT, SILVER, BISHOP, ROOK, GOLD};
+/* {code, bits, piece type, colour (-1: piece box)} in the reference's table order */
+static const int HCP_HAND[21][4] = {
+    {0x00, 3, PAWN, BLACK},   {0x01, 5, LANCE, BLACK},  {0x03, 5, KNIGHT, BLACK}, {0x05, 5, SILVER, BLACK},
+    {0x07, 5, GOLD, BLACK},   {0x1f, 7, BISHOP, BLACK}, {0x3f, 7, ROOK, BLACK},   {0x04, 3, PAWN, WHITE},
+    {0x11, 5, LANCE, WHITE},  {0x13, 5, KNIGHT, WHITE}, {0x15, 5, SILVER, WHITE}, {0x17, 5, GOLD, WHITE},
+    {0x5f, 7, BISHOP, WHITE}, {0x7f, 7, ROOK, WHITE},   {0x02, 3, PAWN, -1},      {0x09, 5, LANCE, -1},
+    {0x0b, 5, KNIGHT, -1},    {0x0d, 5, SILVER, -1},    {0x1d, 5, GOLD, -1},      {0x0f, 7, BISHOP, -1},
+    {0x2f, 7, ROOK, -1}};
+
+static int unpromote(int pt) {
+    switch (pt) {
+        case PRO_PAWN: return PAWN;
+        case PRO_LANCE: return LANCE;
+        case PRO_KNIGHT: return KNIGHT;
+        case PRO_SILVER: return SILVER;
+        case HORSE: return BISHOP;
+        case DRAGON: return ROOK;
+        default: return pt;
+    }
+}
+
+typedef struct {
+    uint8_t data[32];
+    int cursor;
+} bitwriter;
+
+static void bw_bit(bitwriter* w, int b) {
+    if (w->cursor < 256) {
+        if (b) w->data[w->cursor / 8] |= (uint8_t)(1u << (w->cursor % 8));
+        w->cursor++;
+    }
+}
+
+static void bw_bits(bitwriter* w, uint32_t v, int n) {
+    for (int i = 0; i < n; ++i) bw_bit(w, (v >> i) & 1u);
+}
+
+static int psv_index_of(int pt) {       /* piece_type_to_index, shogipack.rs:212-224 */
+    switch (unpromote(pt)) {
+        case PAWN: return 1;
+        case LANCE: return 2;
+        case KNIGHT: return 3;
+        case SILVER: return 4;
+        case BISHOP: return 5;
+        case ROOK: return 6;
+        case GOLD: return 7;
+        default: return 0;
+    }
+}
+
+static int is_promoted(int pt) { return pt >= PRO_PAWN && pt <= DRAGON; }
+
+int oracle_hcpe_to_psv(const uint8_t* rec, uint8_t* psv) {
+    piece board[81];
+    uint8_t hands[2][7];
+    memset(board, 0, sizeof(board));
+    memset(hands, 0, sizeof(hands));
+    bitstream s = {rec, 0, 256};
+    int stm = bs_read_bit(&s) ? WHITE : BLACK;
+    int bk = (int)bs_read_bits(&s, 7);
+    if (bk >= 81) return 0;
+    board[bk] = (piece){KING, BLACK};
+    int wk = (int)bs_read_bits(&s, 7);
+    if (wk >= 81) return 0;
+    board[wk] = (piece){KING, WHITE};
+    for (int sq = 0; sq < 81; ++sq) {
+        if (sq == bk || sq == wk) continue;
+        uint32_t code = 0;
+        int bits = 0, idx = -1;
+        for (;;) {
+            code |= (uint32_t)bs_read_bit(&s) << bits;
+            bits++;
+            if (bits > 6) return 0;
+            for (int i = 0; i < 8 && idx < 0; ++i)
+                if (HCP_PATTERN[i] == code && HCP_LEN[i] == bits) idx = i;
+            if (idx >= 0) break;
+        }
+        if (idx == 0) continue;
+        int base = HCP_TYPE[idx];
+        int color = bs_read_bit(&s) ? WHITE : BLACK;
+        int promoted = base != GOLD ? bs_read_bit(&s) : 0;
+        board[sq] = (piece){promoted ? promote(base) : base, color};
+    }
+    while (s.cursor < 256) {
+        uint32_t code = 0;
+        int bits = 0, e = -1;
+        for (;;) {
+            code |= (uint32_t)bs_read_bit(&s) << bits;
+            bits++;
+            if (bits > 7) return 0;
+            for (int i = 0; i < 21 && e < 0; ++i)
+                if ((uint32_t)HCP_HAND[i][0] == code && HCP_HAND[i][1] == bits) e = i;
+            if (e >= 0) break;
+        }
+        if (HCP_HAND[e][3] < 0) continue;               /* piece box */
+        int h = hand_index(HCP_HAND[e][2]);
+        hands[HCP_HAND[e][3]][h] = (uint8_t)(hands[HCP_HAND[e][3]][h] + 1);
+    }
+    /* pack_to_psfen */
+    int kb = 81, kw = 81;
+    for (int sq = 80; sq >= 0; --sq) {
+        if (board[sq].pt == KING && board[sq].color == BLACK) kb = sq;
+        if (board[sq].pt == KING && board[sq].color == WHITE) kw = sq;
+    }
+    bitwriter w;
+    memset(&w, 0, sizeof(w));
+    bw_bit(&w, stm == WHITE);
+    bw_bits(&w, (uint32_t)kb, 7);
+    bw_bits(&w, (uint32_t)kw, 7);
+    for (int sq = 0; sq < 81; ++sq) {
+        if (sq == kb || sq == kw) continue;
+        piece p = board[sq];
+        if (p.pt == PT_NONE) {
+            bw_bit(&w, 0);
+            continue;
+        }
+        int idx = psv_index_of(p.pt);
+        bw_bits(&w, HUFF_PATTERN[idx], HUFF_LEN[idx]);
+        if (unpromote(p.pt) != GOLD) bw_bit(&w, is_promoted(p.pt));
+        bw_bit(&w, p.color == WHITE);
+    }
+    static const int HAND_ORDER[7] = {PAWN, LANCE, KNIGHT, SILVER, GOLD, BISHOP, ROOK};
+    for (int color = BLACK; color <= WHITE; ++color) {
+        for (int t = 0; t < 7; ++t) {
+            int pt = HAND_ORDER[t];
+            int idx = psv_index_of(pt);
+            for (int c = 0; c < hands[color][hand_index(pt)]; ++c) {
+                bw_bits(&w, HUFF_PATTERN[idx] >> 1, HUFF_LEN[idx] - 1);
+                if (pt != GOLD) bw_bit(&w, 0);
+                bw_bit(&w, color == WHITE);
+            }
+        }
+    }
+    while (w.cursor < 256) {
+        bw_bit(&w, 0);
+        bw_bit(&w, 1);
+        bw_bit(&w, 0);
+    }
+    memcpy(psv, w.data, 32);
+    psv[32] = rec[32];                                   /* eval (i16 LE) */
+    psv[33] = rec[33];
+    psv[34] = rec[34];                                   /* bestMove16 */
+    psv[35] = rec[35];
+    psv[36] = 0;                                         /* game_ply */
+    psv[37] = 0;
+    int r = rec[36] == 1 ? (stm == BLACK ? 1 : -1) : (rec[36] == 2 ? (stm == WHITE ? 1 : -1) : 0);
+    psv[38] = (uint8_t)(int8_t)r;
+    psv[39] = 0;
+    return 1;
+}

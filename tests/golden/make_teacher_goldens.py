@@ -225,11 +225,47 @@ STACK_COUNTS = {
 }
 
 
+HCPE_SRC = "crates/bulletou_lib/src/value/loader"
+
+
+def hirate():
+    """MiniPosition::hirate (shogipack.rs:292-336) in file * 9 + rank squares."""
+    back = [LANCE, KNIGHT, SILVER, GOLD, KING, GOLD, SILVER, KNIGHT, LANCE]
+    board = {}
+    for i, pt in enumerate(back):
+        f = 8 - i
+        if pt != KING:
+            board[sq(f, 0)] = [pt, 1]
+            board[sq(f, 8)] = [pt, 0]
+    board[sq(7, 1)] = [BISHOP, 1]
+    board[sq(1, 1)] = [ROOK, 1]
+    board[sq(7, 7)] = [ROOK, 0]
+    board[sq(1, 7)] = [BISHOP, 0]
+    for f in range(9):
+        board[sq(f, 2)] = [PAWN, 1]
+        board[sq(f, 6)] = [PAWN, 0]
+    return {"black_king": sq(4, 8), "white_king": sq(4, 0), "board": board}
+
+
+HCPE = {
+    "record_bytes": {"source": f"{HCPE_SRC}/hcpe.rs:571-574 (hcpe_record_size_is_38)", "value": 38},
+    "convert_game_result": {
+        "source": f"{HCPE_SRC}/shogipack.rs:1356-1363 (test_convert_game_result)",
+        "cases": [[0, 0, 0], [1, 0, 1], [1, 1, -1], [2, 1, 1], [2, 0, -1]]},
+    "hirate_results": {
+        "source": f"{HCPE_SRC}/hcpe.rs:581-622 (decode_converts_game_result_to_stm_perspective): the hirate "
+                  "position packed in the PackedSfen encoding (pack_to_hcp is pack_to_psfen there), read as HCP",
+        "position": hirate(),
+        "stm0": [[1, 1], [2, -1], [0, 0]], "stm1": [[1, -1], [2, 1]]},
+    "all_zero": {"source": f"{HCPE_SRC}/hcpe.rs:625-633 (decode_invalid_record_returns_none): must not fail"},
+}
+
+
 def main():
     data = {"bitstream": BITSTREAM, "accessors": ACCESSORS, "pieces": PIECES, "bona": BONA,
             "hm2_index": HM2_INDEX, "positions": POSITIONS, "mirror": MIRROR,
             "halfkp_packed": [halfkp_packed_test_position(0), halfkp_packed_test_position(1)],
-            "buckets": BUCKETS, "hand_single": HAND_SINGLE, "stack_counts": STACK_COUNTS}
+            "buckets": BUCKETS, "hand_single": HAND_SINGLE, "stack_counts": STACK_COUNTS, "hcpe": HCPE}
     path = Path(__file__).with_name("teacher_goldens.json")
     path.write_text(json.dumps(data, indent=1) + "\n")
     print(f"wrote {path}")

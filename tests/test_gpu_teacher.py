@@ -285,3 +285,62 @@ def test_fused_steps_on_record_batches_vs_oracle(ctx, qat):
     got = runner.read_weights(ctx)
     for nm in trainer.names:
         assert_close_scaled(got[nm], trainer.w[nm], 1e-4, nm)
+
+
+# ------------------------------------------------------------------ HCPE records
+def _hcpe_device(ctx, recs):
+    n = np.asarray(recs).view(np.uint8).size // 38
+    conv = bt.HcpeConverter(ctx, max(n, 1))
+    count = conv.convert(ctx, recs)
+    psv = conv.psv.download(ctx).view(np.uint8).reshape(-1, 40)[:count]
+    return psv, conv.valid.download(ctx)[:n], count
+
+
+@pytest.mark.parametrize("n", [1, 63, 65, 4096])
+def test_hcpe_full_set_records_vs_oracle(ctx, n):
+    recs = syn.hcpe_records(50 + n, n, hand_fraction=0.25, promote_fraction=0.2)
+    want, wvalid = ot.hcpe_to_psv(recs)
+    got, valid, count = _hcpe_device(ctx, recs)
+    assert count == n == wvalid.sum()
+    np.testing.assert_array_equal(valid, wvalid)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_hcpe_random_and_short_records_vs_oracle(ctx):
+    """Random bytes (kings out of range, unknown hand codes: dropped and the
+    rest compacted in order) and short-material positions padded with piece-box
+    entries."""
+    rng = np.random.default_rng(61)
+    rand = rng.integers(0, 256, (20000, 38), dtype=np.uint8)
+    p = syn.psv_positions(syn.rng_for(62), 2000, hand_fraction=0.3)
+    p["board"][syn.rng_for(63).random(p["board"].shape) < 0.3] = 0
+    short = []
+    for i in range(2000):
+        try:
+            short.append(syn.hcpe_encode(p["stm"][i], p["black_king"][i], p["white_king"][i], p["board"][i][None],
+                                         p["hands"][i][None], 5, 2).view(np.uint8).reshape(-1, 38))
+        except ValueError:
+            continue
+    recs = np.concatenate([rand, np.concatenate(short)])
+    want, wvalid = ot.hcpe_to_psv(recs)
+    got, valid, count = _hcpe_device(ctx, recs)
+    assert count == wvalid.sum() and 0 < count < len(recs)
+    np.testing.assert_array_equal(valid, wvalid)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_hcpe_to_training_batch(ctx):
+    """HCPE records -> device PackedSfenValue -> device HalfKA_hm2 batch equals
+    the oracle's decode_hcpe_record -> prepare chain."""
+    recs = syn.hcpe_records(70, 8192)
+    cfg = _cfg("halfka_hm2", lam=1.0, wrm=True)
+    conv = bt.HcpeConverter(ctx, 8192)
+    count = conv.convert(ctx, recs)
+    prod = bt.TeacherBatchProducer(ctx, cfg, count, pinned=False)
+    out = prod.new_batch()
+    bt.teacher_prepare_device(ctx, cfg, conv.psv, count, out.stm_indices, out.nstm_indices, out.buckets,
+                              out.targets, out.entry_weights, prod.overflow, prod.wrm_table)
+    want_psv, _ = ot.hcpe_to_psv(recs)
+    got = out.download(ctx)
+    got["overflow"] = int(prod.overflow.download(ctx)[0])
+    _compare(got, _oracle(cfg, want_psv), cfg)

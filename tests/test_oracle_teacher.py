@@ -305,3 +305,64 @@ def test_fuzz_records_never_index_out_of_range():
         assert (out["stm"][valid] < n).all() and (out["nstm"][out["nstm"] >= 0] < n).all()
         np.testing.assert_array_equal(valid.sum(axis=1), np.minimum(out["counts"], A))
         assert (out["counts"] > A).any() and ((out["counts"] > 0) & (out["counts"] <= A)).any()
+
+
+# ------------------------------------------------------------------ HCPE records
+def _hirate_psv_bytes(stm):
+    h = G["hcpe"]["hirate_results"]["position"]
+    return _encode({"stm": stm, "black_king": h["black_king"], "white_king": h["white_king"], "board": h["board"]})
+
+
+def test_hcpe_known_answers():
+    """decode_converts_game_result_to_stm_perspective (hcpe.rs:581-622): the
+    PackedSfen-encoded hirate read as HCP decodes, and the absolute game result
+    turns into the side to move's; convert_game_result (shogipack.rs:1356-1363)."""
+    g = G["hcpe"]
+    assert g["record_bytes"]["value"] == syn.HCPE_DTYPE.itemsize == 38
+    for stm, cases in ((0, g["hirate_results"]["stm0"]), (1, g["hirate_results"]["stm1"])):
+        sfen = _hirate_psv_bytes(stm).view(np.uint8)[:32]
+        for abs_result, want in cases:
+            rec = np.zeros(38, np.uint8)
+            rec[:32] = sfen
+            rec[36] = abs_result
+            psv, valid = ot.hcpe_to_psv(rec)
+            assert valid[0] == 1
+            assert np.int8(psv[0, 38]) == want
+            assert psv[0, 36] == 0 and psv[0, 37] == 0                  # game_ply 0
+    for abs_result, stm, want in g["convert_game_result"]["cases"]:
+        rec = np.zeros(38, np.uint8)
+        rec[:32] = _hirate_psv_bytes(stm).view(np.uint8)[:32]
+        rec[36] = abs_result
+        psv, _ = ot.hcpe_to_psv(rec)
+        assert np.int8(psv[0, 38]) == want
+    ot.hcpe_to_psv(np.zeros(38, np.uint8))                            # hcpe.rs:625-633: no failure
+
+
+def test_hcpe_full_set_records_repack_to_the_psv_encoding():
+    """A full-set position encoded as HCP repacks to exactly the PackedSfenValue
+    bytes of the same position (pack_to_psfen order: board by square, hands by
+    colour and type; no padding needed), with eval, bestMove16, game_ply 0 and
+    the side to move's result."""
+    p = syn.psv_positions(syn.rng_for(44), 400, hand_fraction=0.3, promote_fraction=0.3)
+    res = syn.rng_for(45).integers(0, 3, 400)
+    h = syn.hcpe_encode(p["stm"], p["black_king"], p["white_king"], p["board"], p["hands"], -321, res, 777)
+    psv, valid = ot.hcpe_to_psv(h)
+    assert valid.all()
+    stm_result = np.where(res == 0, 0, np.where((res == 1) == (p["stm"] == 0), 1, -1))
+    want = syn.psv_encode(p["stm"], p["black_king"], p["white_king"], p["board"], p["hands"], -321, stm_result, 0,
+                          777)
+    np.testing.assert_array_equal(psv, want.view(np.uint8).reshape(-1, 40))
+
+
+def test_hcpe_invalid_records_are_dropped():
+    rng = np.random.default_rng(3)
+    recs = rng.integers(0, 256, (3000, 38), dtype=np.uint8)
+    psv, valid = ot.hcpe_to_psv(recs)
+    kings_ok = []
+    for r in recs:
+        bits = int.from_bytes(r[:2].tobytes(), "little")
+        kings_ok.append(((bits >> 1) & 127) < 81 and ((bits >> 8) & 127) < 81)
+    kings_ok = np.array(kings_ok)
+    assert not valid[~kings_ok].any()                                  # a king square >= 81: skipped
+    assert 0 < valid.sum() < kings_ok.sum()                           # some fail on unknown hand codes
+    assert psv.shape == (valid.sum(), 40)
