@@ -1053,7 +1053,7 @@ def main():
         return
     common = {"global_batch": args.batch * world, "per_gpu_batch": args.batch, "seq_len": 1,
               "optimizer": "Ranger (RAdam + Lookahead k=6, lr 1e-3)",
-              "loss": "sigmoid-WDL MSE, scale 600, lambda 0.5",
+              "loss": "sigmoid-pow(2) MSE of the output, scale 600",
               "parallelism": f"dp{world}" if world > 1 else "single"}
     if sfnn:
         metric = SFNN_METRIC
@@ -1061,6 +1061,8 @@ def main():
                        "model": "SFNN_halfkahm2_1536_15_32_k3k3: (73305+1629 virtual) x 1536 FT, pairwise, "
                                 "9 x (1536 -> 15+1), shared L1 factor, 30 -> 32 -> 1",
                        "max_active": SFNN_ACTIVE,
+                       "targets": ("win-rate-model probability of the teacher score (offset 270, scaling 380), "
+                                   "lambda 1" if args.data == "psv" else "0.5 result + 0.5 sigmoid(score / 600)"),
                        "data": ("seeded PackedSfenValue records (full-set positions, kings near their home ranks) "
                                 "decoded to HalfKA_hm2 rows / k3k3 buckets / win-rate targets"
                                 if args.data == "psv" else "feature rows uniform over the 45 king blocks, "
