@@ -62,4 +62,6 @@ from .teacher import (  # noqa: F401
     win_rate_model_score_table,
 )
 
+from .validate import AccuracyReport, ValidationLossKind, ValidationMetrics, sfnn_validation_stats  # noqa: F401
+
 __version__ = "0.1.0"

@@ -62,6 +62,13 @@ class SfnnQat(ctypes.Structure):
     _fields_ = [("l1", I), ("ft", I), ("l2", I), ("l3", I)]
 
 
+class ValidationConfig(ctypes.Structure):
+    """BulletOuB200ValidationConfig."""
+
+    _fields_ = [("have_results", I), ("score_drop_abs", I), ("loss_kind", I), ("lambda_", F), ("eval_scale", F),
+                ("model_output_scale", F), ("pow_exp", F), ("nnue2score", F), ("in_offset", F), ("in_scaling", F)]
+
+
 class TeacherConfig(ctypes.Structure):
     """BulletOuB200TeacherConfig."""
 
@@ -172,6 +179,9 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_sfnn_integer_forward_device": [P, P, Z, Z] + [P] * 9,
     "bulletou_b200_teacher_prepare_device": [P, P, P, Z] + [P] * 7,
     "bulletou_b200_hcpe_to_psv_device": [P, P, Z, P, P, P],
+    "bulletou_b200_validation_metrics_device": [P, P, P, P, Z, P, P],
+    "bulletou_cuda_cpp_sfnn_validation_stats": [P] * 7 + [Z] * 4,
+    "bulletou_cuda_cpp_sfnn_unit_stats": [P] * 7 + [Z] * 5,
 }
 
 

@@ -117,6 +117,7 @@ enum ScratchSlot : int {
     kScratchNnueQuant = 25,     // integer HalfKP forward: transformed features (u8)
     kScratchSfnnHeavy = 26,     // SFNN FT rows: segment plan and partial sums of heavy rows
     kScratchHcpe = 27,          // HCPE -> PackedSfenValue: uncompacted records, valid flags, scan
+    kScratchValidation = 28,    // validation metrics: per-CTA partials
 };
 
 int ok();

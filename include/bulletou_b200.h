@@ -415,6 +415,33 @@ int bulletou_b200_teacher_prepare_device(BulletOuCudaCppContext* ctx, const Bull
  * words) and their number to count[0]; a record with a king square >= 81 or
  * an unknown hand code is dropped, as the reference's loader skips it.
  * valid (optional) receives the per-record flags. */
+/* ---- validation metrics ----
+ * Replaces compute_sign_accuracy_with_loss_masked
+ * (crates/bulletou_lib/src/validate.rs:353-470) on the host: model outputs [n]
+ * and the positions' PackedSfenValue records [n][10 words] (teacher score and
+ * game result read from them) -> report[0..7] = compared, sign_matches,
+ * predicted_nonnegative, predicted_negative, predicted_zero, drawn_games,
+ * filtered_by_score_cap, loss_sampled; report[8..9] = the loss sum as a
+ * double (test loss = sum / loss_sampled).  wrm_table (65536 floats, the
+ * target's probability per score) is needed by the win-rate-model and BCE
+ * losses. */
+typedef struct BulletOuB200ValidationConfig {
+    int32_t have_results;       /* 0: the legacy score-sign path, no loss */
+    int32_t score_drop_abs;     /* < 0: none */
+    int32_t loss_kind;          /* 0 sigmoid-pow, 1 win-rate model, 2 BCE with logits */
+    float lambda;
+    float eval_scale;           /* <= 0: 1/400 */
+    float model_output_scale;   /* <= 0: 1 */
+    float pow_exp;
+    float nnue2score;
+    float in_offset;
+    float in_scaling;
+} BulletOuB200ValidationConfig;
+
+int bulletou_b200_validation_metrics_device(BulletOuCudaCppContext* ctx, const BulletOuB200ValidationConfig* config,
+    const BulletOuCudaCppF32Buffer* outputs, const BulletOuCudaCppI32Buffer* records, size_t n,
+    const BulletOuCudaCppF32Buffer* wrm_table, BulletOuCudaCppI32Buffer* report);
+
 int bulletou_b200_hcpe_to_psv_device(BulletOuCudaCppContext* ctx, const BulletOuCudaCppI32Buffer* hcpe,
     size_t n_records, BulletOuCudaCppI32Buffer* psv, BulletOuCudaCppI32Buffer* count, BulletOuCudaCppI32Buffer* valid);
 

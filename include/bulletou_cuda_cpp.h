@@ -304,6 +304,20 @@ int bulletou_dense_qat_begin(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buff
     int integer_ft);                                                                                  /* cu:9356 */
 void bulletou_dense_qat_end(BulletOuCudaCppContext* ctx);                                             /* cu:9375 */
 
+/* cu:13485-13504: activation statistics of a forward workspace, 5 x 256
+ * partials (FT outputs at 1, L2-input square / normal branches at 1, L2 at 1,
+ * output squared). */
+int bulletou_cuda_cpp_sfnn_validation_stats(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* stm,
+    BulletOuCudaCppF32Buffer* nstm, BulletOuCudaCppF32Buffer* l2_input, BulletOuCudaCppF32Buffer* l2,
+    BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* partials, size_t batch, size_t ft, size_t hidden,
+    size_t l2_size);
+
+/* cu:13506-13531: per-unit saturation counts [ft + stacks * (1 + 2 hidden + width)]. */
+int bulletou_cuda_cpp_sfnn_unit_stats(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* stm,
+    BulletOuCudaCppF32Buffer* nstm, BulletOuCudaCppF32Buffer* input, BulletOuCudaCppF32Buffer* l2,
+    BulletOuCudaCppI32Buffer* buckets, BulletOuCudaCppI32Buffer* counts, size_t batch, size_t ft, size_t hidden,
+    size_t width, size_t stacks);
+
 #ifdef __cplusplus
 }
 #endif

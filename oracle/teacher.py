@@ -55,6 +55,8 @@ def lib():
         L.oracle_wrm_table.restype = None
         L.oracle_hcpe_to_psv.argtypes = [p, p]
         L.oracle_hcpe_to_psv.restype = i
+        L.oracle_validation_metrics.argtypes = [p, p, p, i64, p, p, p, p]
+        L.oracle_validation_metrics.restype = None
         _ready = True
     return L
 
@@ -152,6 +154,41 @@ def wrm_table(offset=270.0, scaling=380.0, epsilon=0.0) -> np.ndarray:
     t = np.empty(65536, np.float32)
     lib().oracle_wrm_table(offset, scaling, epsilon, _p(t))
     return t
+
+
+class ValidationConfig(ctypes.Structure):
+    """oracle_validation_config (same field order as the product's ABI struct)."""
+
+    _fields_ = [("have_results", ctypes.c_int32), ("score_drop_abs", ctypes.c_int32), ("loss_kind", ctypes.c_int32),
+                ("lambda_", ctypes.c_float), ("eval_scale", ctypes.c_float), ("model_output_scale", ctypes.c_float),
+                ("pow_exp", ctypes.c_float), ("nnue2score", ctypes.c_float), ("in_offset", ctypes.c_float),
+                ("in_scaling", ctypes.c_float)]
+
+
+VALIDATION_COUNTS = ("compared", "sign_matches", "predicted_nonnegative", "predicted_negative", "predicted_zero",
+                     "drawn_games", "filtered_by_score_cap", "loss_sampled")
+
+
+def validation_metrics(outputs, scores, results=None, score_drop_abs=None, lambda_=1.0, eval_scale=400.0,
+                       model_output_scale=1.0, loss_kind=0, pow_exp=2.0, nnue2score=600.0, in_offset=270.0,
+                       in_scaling=380.0, wrm_table=None) -> dict:
+    """compute_sign_accuracy_with_loss_masked; returns the counts, loss_sum and
+    test_loss (None without results or samples)."""
+    o = np.ascontiguousarray(outputs, np.float32).reshape(-1)
+    s = np.ascontiguousarray(scores, np.int16).reshape(-1)
+    r = None if results is None or len(results) == 0 else np.ascontiguousarray(results, np.int8).reshape(-1)
+    cfg = ValidationConfig(int(r is not None), -1 if score_drop_abs is None else int(score_drop_abs), int(loss_kind),
+                           float(lambda_), float(eval_scale), float(model_output_scale), float(pow_exp),
+                           float(nnue2score), float(in_offset), float(in_scaling))
+    table = None if wrm_table is None else np.ascontiguousarray(wrm_table, np.float32)
+    counts = np.zeros(8, np.int64)
+    loss = ctypes.c_double()
+    lib().oracle_validation_metrics(_p(o), _p(s), None if r is None else _p(r), o.size, ctypes.byref(cfg),
+                                    None if table is None else _p(table), _p(counts), ctypes.byref(loss))
+    out = dict(zip(VALIDATION_COUNTS, counts.tolist()))
+    out["loss_sum"] = loss.value
+    out["test_loss"] = float(np.float32(loss.value / out["loss_sampled"])) if out["loss_sampled"] else None
+    return out
 
 
 def hcpe_to_psv(records) -> tuple:

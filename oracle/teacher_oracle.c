@@ -704,3 +704,83 @@ int oracle_hcpe_to_psv(const uint8_t* rec, uint8_t* psv) {
     psv[39] = 0;
     return 1;
 }
+
+/* ------------------------------------------------------------ validation metrics */
+/* build_validation_sample_mask + compute_sign_accuracy_with_loss_masked
+ * (crates/bulletou_lib/src/validate.rs:353-470), the per-sample loss in f32
+ * with the C library's expf / powf / log1pf and the sum in double in index
+ * order.  results may be NULL (the score-sign path, no loss).  counts: compared,
+ * sign_matches, predicted_nonnegative, predicted_negative, predicted_zero,
+ * drawn_games, filtered_by_score_cap, loss_sampled. */
+typedef struct {
+    int32_t have_results;
+    int32_t score_drop_abs;
+    int32_t loss_kind;     /* 0 sigmoid-pow, 1 win-rate model, 2 BCE with logits */
+    float lambda;
+    float eval_scale;
+    float model_output_scale;
+    float pow_exp;
+    float nnue2score;
+    float in_offset;
+    float in_scaling;
+} oracle_validation_config;
+
+static float sig(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+static float bce_logits(float z, float t) {
+    float lin = z >= 0.0f ? (1.0f - t) * z : -t * z;
+    return lin + log1pf(expf(-fabsf(z)));
+}
+
+void oracle_validation_metrics(const float* outputs, const int16_t* scores, const int8_t* results, int64_t n,
+                               const oracle_validation_config* c, const float* wrm_table, int64_t* counts,
+                               double* loss_sum) {
+    for (int k = 0; k < 8; ++k) counts[k] = 0;
+    double sum = 0.0;
+    int have = results != NULL && c->have_results;
+    for (int64_t i = 0; i < n; ++i) {
+        int s = scores[i];
+        if (c->score_drop_abs >= 0 && (s < 0 ? -s : s) >= c->score_drop_abs) {
+            counts[6]++;
+            continue;
+        }
+        int draw = have ? results[i] == 0 : s == 0;
+        float m = outputs[i];
+        if (draw) {
+            counts[5]++;
+        } else {
+            counts[0]++;
+            int pred = m >= 0.0f;
+            counts[pred ? 2 : 3]++;
+            if (m == 0.0f) counts[4]++;
+            int truth = have ? results[i] > 0 : s > 0;
+            if (pred == truth) counts[1]++;
+        }
+        if (!have) continue;
+        counts[7]++;
+        float blend = 1.0f - c->lambda;
+        float inv_scale = c->eval_scale > 0.0f ? 1.0f / c->eval_scale : 0.0025f;
+        float model_inv = c->model_output_scale > 0.0f ? 1.0f / c->model_output_scale : 1.0f;
+        int r = results[i];
+        float result_norm = r > 0 ? 1.0f : (r < 0 ? 0.0f : 0.5f);
+        float score_norm = c->loss_kind == 0 ? sig(inv_scale * (float)s) : wrm_table[s + 32768];
+        float target = blend * result_norm + (1.0f - blend) * score_norm;
+        float l;
+        if (c->loss_kind == 2) {
+            l = bce_logits(m * c->nnue2score / c->in_scaling, target);
+        } else {
+            float p;
+            if (c->loss_kind == 0) {
+                p = sig(m * model_inv);
+            } else {
+                float sc = m * c->nnue2score;
+                float q = (sc - c->in_offset) / c->in_scaling;
+                float qm = (-sc - c->in_offset) / c->in_scaling;
+                p = 0.5f * (1.0f + sig(q) - sig(qm));
+            }
+            l = powf(fabsf(p - target), c->pow_exp);
+        }
+        sum += (double)l;
+    }
+    *loss_sum = sum;
+}
