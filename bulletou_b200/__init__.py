@@ -63,5 +63,6 @@ from .teacher import (  # noqa: F401
 )
 
 from .validate import AccuracyReport, ValidationLossKind, ValidationMetrics, sfnn_validation_stats  # noqa: F401
+from .nn_bin import nnue_nn_bin_bytes, sfnn_nn_bin_bytes, write_nnue_nn_bin, write_sfnn_nn_bin  # noqa: F401
 
 __version__ = "0.1.0"
