@@ -65,4 +65,10 @@ from .teacher import (  # noqa: F401
 from .validate import AccuracyReport, ValidationLossKind, ValidationMetrics, sfnn_validation_stats  # noqa: F401
 from .nn_bin import nnue_nn_bin_bytes, sfnn_nn_bin_bytes, write_nnue_nn_bin, write_sfnn_nn_bin  # noqa: F401
 
+from .state_bin import (  # noqa: F401
+    CheckpointLog, SfnnTrainState, latest_complete_checkpoint_dir, load_halfkp_state, load_sfnn_state,
+    parse_model_weights_bin, restore_halfkp_runner, restore_sfnn_runner, write_checkpoint_dir, write_halfkp_state_bin,
+    write_sfnn_checkpoint, write_sfnn_state_bin,
+)
+
 __version__ = "0.1.0"
