@@ -70,5 +70,8 @@ from .state_bin import (  # noqa: F401
     parse_model_weights_bin, restore_halfkp_runner, restore_sfnn_runner, write_checkpoint_dir, write_halfkp_state_bin,
     write_sfnn_checkpoint, write_sfnn_state_bin,
 )
+from .revive import (  # noqa: F401
+    FtCalibration, begin_revival_epoch, compensate_ft_revival_mean, revive_ft, revive_ft_units, saturated_units,
+)
 
 __version__ = "0.1.0"

@@ -153,6 +153,18 @@ class RevivalRng:
         self.state = s
         return float(np.float32(2.0) * (np.float32(s >> 40) / np.float32(16777216.0)) - np.float32(1.0))
 
+    def signed_uniform_array(self, n: int) -> np.ndarray:
+        """n consecutive draws (the same values as n calls of signed_uniform)."""
+        s, m = self.state, 0xFFFFFFFFFFFFFFFF
+        top = np.empty(n, np.float32)
+        for i in range(n):
+            s ^= (s << 13) & m
+            s ^= s >> 7
+            s ^= (s << 17) & m
+            top[i] = s >> 40
+        self.state = s
+        return np.float32(2.0) * (top / np.float32(16777216.0)) - np.float32(1.0)
+
     def encode(self) -> np.ndarray:
         return encode_exact_step(self.state)
 
@@ -489,8 +501,12 @@ def _upload_group(ctx, st, host: dict) -> None:
 def sfnn_runner_state(ctx, runner, completed_steps: int, optimizer_steps: int) -> SfnnTrainState:
     """Download an SfnnTrainStepRunner's weights and Ranger states."""
     a = runner.alpha
+    rng = getattr(runner, "revival_rng", None)
     return SfnnTrainState(runner.read_weights(ctx), runner.read_optimizer_states(ctx), int(completed_steps),
-                          int(optimizer_steps), (a.ft, a.shared if runner.present.get("l1fw") else 0.0))
+                          int(optimizer_steps), (a.ft, a.shared if runner.present.get("l1fw") else 0.0),
+                          l1_revival_flags=getattr(runner, "l1_revival_flags", 0),
+                          l2_revival_flags=getattr(runner, "l2_revival_flags", 0),
+                          revival_rng=None if rng is None else RevivalRng(rng.state))
 
 
 def sfnn_runner_sizes(runner) -> Dict[str, int]:
@@ -513,6 +529,9 @@ def restore_sfnn_runner(ctx, runner, state: SfnnTrainState) -> None:
             st.slow_params.upload(state.weights[n], ctx)
         else:
             _upload_group(ctx, st, state.optimizer[n])
+    runner.revival_rng = RevivalRng(state.revival_rng.state)
+    runner.l1_revival_flags = state.l1_revival_flags
+    runner.l2_revival_flags = state.l2_revival_flags
 
 
 def write_sfnn_state_bin(path, ctx, runner, completed_steps: int, optimizer_steps: int) -> SfnnTrainState:

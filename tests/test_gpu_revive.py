@@ -1,0 +1,128 @@
+"""FT revival on the device tensors of an SfnnTrainStepRunner, the reference's
+GPU tests of crates/cuda_cpp/src/ft_revive.rs:171-258 on this backend."""
+import numpy as np
+import pytest
+
+import bulletou_b200 as bo
+from bulletou_b200 import revive as rv
+from bulletou_b200 import sfnn as bs
+from bulletou_b200 import state_bin as sb
+from bulletou_b200 import synthetic as syn
+from bulletou_b200.state_bin import RevivalRng
+
+pytestmark = pytest.mark.gpu
+
+SHAPE = bs.SfnnForwardShape(bs.HALFKA_HM2_DIMENSIONS + bs.PIECE_INPUTS, 12, 3, True, 5, 4)
+
+
+def _runner(ctx, shared, alpha=bs.SfnnFactorizerAlpha()):
+    w = syn.sfnn_weights(syn.rng_for(12), SHAPE.input_size, SHAPE.ft_size, SHAPE.l1_hidden, SHAPE.l1_skip,
+                         SHAPE.l2_size, SHAPE.num_stacks, shared, False, 0.1)
+    return bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(SHAPE, **w), 1024, 1, alpha)
+
+
+def _cal(mean=0.25):
+    c = rv.FtCalibration(SHAPE.ft_size, SHAPE.num_stacks)
+    c.counts[:] = 1024
+    c.means[:] = mean
+    return c
+
+
+def test_reset_and_mean_compensation_preserve_other_columns(ctx):
+    s = SHAPE
+    r = _runner(ctx, False)
+    old = r.read_weights(ctx)
+    rv.revive_ft(ctx, r, _cal(), [0], s.input_size)
+    ch = r.read_weights(ctx)
+    ft, half = s.ft_size, s.ft_size // 2
+    l0o, l0n = old["l0w"].reshape(-1, ft), ch["l0w"].reshape(-1, ft)
+    keep = [j for j in range(ft) if j not in (0, half)]
+    np.testing.assert_array_equal(l0n[:, keep], l0o[:, keep])
+    assert ch["l0b"][0] == 0.5 and ch["l0b"][half] == 0.5
+    # the revived rows are the revival stream, in unit order
+    rng = RevivalRng()
+    bound = max(np.float32(np.sqrt(np.float32(6.0) / np.float32(s.input_size + ft))), np.float32(1 / 127))
+    for col in (0, half):
+        want = rv._round_half_away(rng.signed_uniform_array(s.input_size) * bound * np.float32(127.0)) / np.float32(127.0)
+        np.testing.assert_array_equal(l0n[:, col], want)
+    l1o, l1n = old["l1w"].reshape(-1, ft), ch["l1w"].reshape(-1, ft)
+    exp = old["l1b"] + np.float32(0.25) * l1o[:, 0] + np.float32(0.25) * l1o[:, half]
+    np.testing.assert_allclose(ch["l1b"], exp, atol=1e-6)
+    assert np.all(np.abs(np.abs(l1n[:, [0, half]]) - 1 / 64) < 1e-7)
+    rv.compensate_ft_revival_mean(ctx, r, [0], _cal(0.5))
+    after = r.read_weights(ctx)
+    exp = ch["l1b"] - np.float32(0.5) * (l1n[:, 0] + l1n[:, half])
+    np.testing.assert_allclose(after["l1b"], exp, atol=1e-6)
+    np.testing.assert_array_equal(old["l2w"], after["l2w"])
+    np.testing.assert_array_equal(old["l3w"], after["l3w"])
+    st = r.read_optimizer_states(ctx)
+    assert np.all(st["l0w"]["momentum"].reshape(-1, ft)[:, [0, half]] == 0.0)
+    assert np.all(st["l1b"]["momentum"] == 0.0) and np.all(st["l1b"]["velocity"] == 0.0)
+    # no units: the stream does not move; a second revival draws new rows,
+    # and restoring the state repeats them exactly
+    snap = sb.sfnn_runner_state(ctx, r, 0, 0)
+    state_before = r.revival_rng.state
+    rv.revive_ft(ctx, r, _cal(), [], s.input_size)
+    assert r.revival_rng.state == state_before
+    rv.begin_revival_epoch(r)
+    rv.revive_ft(ctx, r, _cal(), [0], s.input_size)
+    second = r.read_weights(ctx)
+    assert not np.array_equal(second["l0w"], after["l0w"])
+    sb.restore_sfnn_runner(ctx, r, snap)
+    rv.begin_revival_epoch(r)
+    rv.revive_ft(ctx, r, _cal(), [0], s.input_size)
+    again = r.read_weights(ctx)
+    for k in second:
+        np.testing.assert_array_equal(again[k], second[k], err_msg=k)
+
+
+def test_revive_one_saturated_unit_preserves_partner(ctx):
+    s = SHAPE
+    r = _runner(ctx, False)
+    c = _cal()
+    c.counts[:] = 0
+    c.counts[0] = 1
+    old = r.read_weights(ctx)
+    rv.revive_ft_units(ctx, r, c, [0], s.input_size)
+    new = r.read_weights(ctx)
+    np.testing.assert_array_equal(old["l0w"].reshape(-1, s.ft_size)[:, 1:], new["l0w"].reshape(-1, s.ft_size)[:, 1:])
+    np.testing.assert_array_equal(old["l0b"][1:], new["l0b"][1:])
+    assert new["l0b"][0] == 0.5
+
+
+def test_shared_and_virtual_columns(ctx):
+    s = SHAPE
+    r = _runner(ctx, True, bs.SfnnFactorizerAlpha(1.0, 0.7))
+    old = r.read_weights(ctx)
+    rv.revive_ft(ctx, r, _cal(), [0], s.input_size - 1)
+    new = r.read_weights(ctx)
+    np.testing.assert_array_equal(old["l1fw"], new["l1fw"])
+    np.testing.assert_array_equal(old["l1fb"], new["l1fb"])
+    ft, n = s.ft_size, s.l1_out
+    l1 = new["l1w"].reshape(s.num_stacks, n, ft)
+    fw = new["l1fw"].reshape(ft, n)
+    for col in (0, ft // 2):
+        assert new["l0w"][(s.input_size - 1) * ft + col] == 0.0
+        eff = l1[:, :, col] + np.float32(0.7) * fw[col][None, :]
+        assert np.all(np.abs(np.abs(eff) - 1 / 64) < 1e-6)
+    st = r.read_optimizer_states(ctx)
+    np.testing.assert_array_equal(st["l0w"]["slow_params"].reshape(-1, ft)[:, [0, ft // 2]],
+                                  new["l0w"].reshape(-1, ft)[:, [0, ft // 2]])
+    assert np.all(st["l0w"]["momentum"].reshape(-1, ft)[:, [0, ft // 2]] == 0.0)
+    # the revived net trains on
+    b = syn.sfnn_batch(5, 1024, stacks=s.num_stacks)
+    k = b["max_active"]
+    hb = bs.SfnnTrainStepHostBatch(b["stm"].reshape(-1, k)[:, 0].copy(), b["nstm"].reshape(-1, k)[:, 0].copy(),
+                                   b["buckets"], b["targets"], b["entry_weights"], 1024, 1)
+    loss = r.step(ctx, bo.RangerUpdateParams(radam=bo.RAdamUpdateParams(step=1)), bo.ScalarLossKind.SigmoidPow(2.0),
+                  1 / 600, hb)
+    assert np.isfinite(loss.mean)
+
+
+def test_revival_rejects_legacy_factorizers(ctx):
+    s = SHAPE
+    w = syn.sfnn_weights(syn.rng_for(13), s.input_size, s.ft_size, s.l1_hidden, s.l1_skip, s.l2_size,
+                         s.num_stacks, True, True, 0.1)
+    r = bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(s, **w), 1024, 1)
+    with pytest.raises(bo.CudaCppError, match="FT revival requires"):
+        rv.revive_ft(ctx, r, _cal(), [0], s.input_size)

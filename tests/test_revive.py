@@ -1,0 +1,55 @@
+"""FT unit revival (crates/cuda_cpp/src/ft_revive.rs): the host-side selection
+and calibration on CPU (the reference's tests saturation_is_per_unit_and_
+includes_threshold and unobserved_bucket_mean_uses_global_mean), and the
+device-state edits on the GPU (gpu_reset_and_mean_compensation_preserve_other_
+columns, revive_one_saturated_unit_preserves_partner, gpu_shared_and_virtual_
+columns), with the random rows checked against the revival stream."""
+import numpy as np
+import pytest
+
+from bulletou_b200 import revive as rv
+from bulletou_b200._lib import CudaCppError
+from bulletou_b200.state_bin import RevivalRng
+
+
+def test_saturation_is_per_unit_and_includes_threshold():
+    assert rv.saturated_units([99, 100, 98, 0], 100, 0.99) == [0, 1]
+    with pytest.raises(CudaCppError):
+        rv.saturated_units([0], 0, 0.99)
+    with pytest.raises(CudaCppError):
+        rv.saturated_units([101], 100, 0.99)
+    with pytest.raises(CudaCppError):
+        rv.saturated_units([1], 100, 0.0)
+
+
+def test_unobserved_bucket_mean_uses_global_mean():
+    c = rv.FtCalibration(2, 2)
+    c.add([0, 0], [0.2, 0.4, 0.6, 0.8], [1.0, 1.0])
+    c.finish_means()
+    assert abs(c.means[2] - 0.4) < 1e-6 and abs(c.means[3] - 0.6) < 1e-6
+    assert abs(c.means[0] - 0.4) < 1e-6 and c.counts.tolist() == [2, 0]
+
+
+def test_calibration_mask_and_errors():
+    c = rv.FtCalibration(2, 3)
+    c.add([1, 2, 1], [1, 2, 3, 4, 5, 6], [1.0, 0.0, 2.0])
+    c.finish_means()
+    assert c.counts.tolist() == [0, 2, 0]
+    assert c.means[2:4].tolist() == [3.0, 4.0]
+    for args in (([0], [1.0, np.nan], [1.0]), ([3], [1.0, 2.0], [1.0]), ([0], [1.0, 2.0], [-1.0]),
+                 ([0], [1.0], [1.0])):
+        with pytest.raises(CudaCppError):
+            rv.FtCalibration(2, 3).add(*args)
+
+
+def test_revival_draws_are_the_xorshift_stream():
+    """The FT row values: round(u * bound * 127) / 127 in f32 with u the
+    stream's signed uniforms (revive_ft_units, ft_revive.rs:78-83)."""
+    r = RevivalRng()
+    u = r.signed_uniform_array(5)
+    s = RevivalRng()
+    assert u.tolist() == [s.signed_uniform() for _ in range(5)]
+    bound = max(np.float32(np.sqrt(np.float32(6.0) / np.float32(100 + 12))), np.float32(1 / 127))
+    v = rv._round_half_away(u * bound * np.float32(127.0)) / np.float32(127.0)
+    assert np.all(np.abs(v) <= bound + 1 / 127) and v.dtype == np.float32
+    assert rv._round_half_away(np.array([0.5, -0.5, 1.5, -2.5, 0.49999997], np.float32)).tolist() == [1, -1, 2, -3, 0]
