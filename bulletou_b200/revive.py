@@ -1,7 +1,8 @@
-"""FT unit revival at an epoch boundary: saturated feature-transformer units
+"""Unit revival at an epoch boundary: saturated feature-transformer units
 get fresh random rows, the L1 columns that read them are reset to +-1/64 with
 the change absorbed into the L1 biases, and the optimizer state of everything
-touched restarts.
+touched restarts; dead or saturated L1 units get fresh rows the same way, with
+the L2 weights that read them reset (crates/cuda_cpp/src/l1_revive.rs).
 
 Restates crates/cuda_cpp/src/ft_revive.rs (saturated_units :5-10,
 Calibration :12-52, revive_ft / revive_ft_units :57-117,
@@ -111,6 +112,18 @@ def _shared_terms(ctx, runner):
         sw = runner.optimizer_states["l1fw"].slow_params.download(ctx).reshape(ft, n)
         return (a * w).T + F32(0.0), (a * sw).T + F32(0.0)     # [u][col]
     z = np.zeros((n, ft), F32)
+    return z, z
+
+
+def _shared_bias(ctx, runner):
+    """Common::bias of the shared factorizer: alpha * l1fb[u] (fast, slow)."""
+    n = runner.shape.l1_out
+    if runner.present.get("l1fb"):
+        a = F32(runner.alpha.shared)
+        b = runner.weights["l1fb"].download(ctx)
+        sb = runner.optimizer_states["l1fb"].slow_params.download(ctx)
+        return a * b + F32(0.0), a * sb + F32(0.0)
+    z = np.zeros(n, F32)
     return z, z
 
 
@@ -233,4 +246,249 @@ def _invalidate_qat(runner) -> None:
     from .sfnn import SfnnLayerQatCopies
 
     runner.qat_l1 = None
+    runner.layer_qat = SfnnLayerQatCopies()
+
+
+# ------------------------------------------------------------------ L1 revival
+class Contribution:
+    """Exact mean-absolute-deviation utility of each unit's branches times the
+    magnitude of its outgoing weights (crates/cuda_cpp/src/l1_revive.rs
+    Contribution, :5-58); units whose utility relative to the bucket's best
+    is below the threshold are selected."""
+
+    def __init__(self, width: int, groups: int):
+        self.width = int(width)
+        self.values = [[] for _ in range(groups)]
+        self.means = np.zeros(groups * width, np.float64)
+        self.utility = np.zeros(0)
+        self.relative = np.zeros(0)
+        self.threshold = 0.01
+
+    def add(self, bucket: int, y) -> None:
+        self.values[bucket].append(np.asarray(y, np.float32).reshape(-1, self.width))
+
+    def finish(self, w, out: int, branches: int, threshold: float) -> None:
+        if not np.isfinite(threshold) or threshold <= 0.0 or threshold > 1.0:
+            raise CudaCppError("revive contribution threshold must be finite and in (0, 1]")
+        w = np.asarray(w, np.float32).reshape(-1)
+        if w.size != len(self.values) * out * self.width:
+            raise CudaCppError(f"revive outgoing weights length mismatch: expected "
+                               f"{len(self.values) * out * self.width}, got {w.size}")
+        if not np.all(np.isfinite(w)) or branches == 0 or self.width % branches != 0:
+            raise CudaCppError("invalid contribution weights or branch layout")
+        units = self.width // branches
+        G = len(self.values)
+        self.utility = np.zeros(G * units)
+        self.relative = np.zeros(G * units)
+        self.threshold = threshold
+        wb = np.abs(w.reshape(G, out, self.width).astype(np.float64))
+        for b, chunks in enumerate(self.values):
+            ys = np.concatenate(chunks).astype(np.float64) if chunks else np.zeros((0, self.width))
+            n = ys.shape[0]
+            if n == 0:
+                continue
+            mean = np.zeros(self.width)
+            for row in ys:
+                mean += row
+            mean /= n
+            self.means[b * self.width:(b + 1) * self.width] = mean
+            dev = np.zeros(self.width)
+            for row in ys:
+                dev += np.abs(row - mean)
+            mad = dev / n
+            norm = np.zeros(self.width)
+            for j in range(out):
+                norm += wb[b, j]
+            for col in range(self.width):
+                self.utility[b * units + col % units] += mad[col] * norm[col]
+            mx = max(0.0, float(self.utility[b * units:(b + 1) * units].max()))
+            if mx > 0.0:
+                self.relative[b * units:(b + 1) * units] = self.utility[b * units:(b + 1) * units] / mx
+        if not (np.all(np.isfinite(self.utility)) and np.all(np.isfinite(self.relative))):
+            raise CudaCppError("non-finite revival contribution")
+        self.values = [[] for _ in range(G)]
+
+    def selected(self, counts, units: int) -> List[int]:
+        return [i for i in range(self.relative.size) if counts[i // units] >= 1024 and self.relative[i] < self.threshold]
+
+
+class L1Calibration:
+    """Per-bucket statistics of the L1 branches over calibration positions
+    (l1_revive.rs Calibration, :60-146): input sums, branch sums, the upper /
+    zero saturation counts and the contribution samples."""
+
+    def __init__(self, input_size: int, width: int, groups: int):
+        self.input, self.width = int(input_size), int(width)
+        self.counts = np.zeros(groups, np.int64)
+        self.upper = np.zeros(groups * width, np.int64)
+        self.lower = np.zeros(groups * width, np.int64)
+        self.upper_threshold = 0.99
+        self.zero_threshold = 0.99
+        self.sums = np.zeros(groups * input_size, np.float64)
+        self.branch_sums = np.zeros(groups * 2 * width, np.float64)
+        self.contribution = Contribution(2 * width, groups)
+
+    def set_thresholds(self, upper: float, zero: float) -> None:
+        if any(not np.isfinite(v) or v <= 0.0 or v > 1.0 for v in (upper, zero)):
+            raise CudaCppError("revival thresholds must be finite and in (0, 1]")
+        self.upper_threshold, self.zero_threshold = upper, zero
+
+    def is_upper(self, i: int, enabled: bool) -> bool:
+        n = self.counts[i // self.width]
+        return bool(enabled and n >= 1024 and self.upper[i] / n >= self.upper_threshold)
+
+    def is_zero(self, i: int, enabled: bool) -> bool:
+        n = self.counts[i // self.width]
+        return bool(enabled and n >= 1024 and self.lower[i] / n >= self.zero_threshold)
+
+    def add(self, buckets, x, y, weights=None) -> None:
+        """x: combined FT input [n][input]; y: [n][square branches, normal branches]."""
+        b = np.asarray(buckets, np.int64).reshape(-1)
+        x = np.asarray(x, np.float32).reshape(-1)
+        y = np.asarray(y, np.float32).reshape(-1)
+        if x.size != b.size * self.input:
+            raise CudaCppError(f"L1 revival inputs length mismatch: expected {b.size * self.input}, got {x.size}")
+        if y.size != b.size * 2 * self.width:
+            raise CudaCppError(f"L1 revival branches length mismatch: expected {b.size * 2 * self.width}, got {y.size}")
+        if weights is not None:
+            weights = np.asarray(weights, np.float32).reshape(-1)
+            if weights.size != b.size:
+                raise CudaCppError(f"L1 revival sample weights length mismatch: expected {b.size}, got {weights.size}")
+            if not np.all(np.isfinite(weights)) or np.any(weights < 0):
+                raise CudaCppError("invalid L1 revival sample weight")
+        if not (np.all(np.isfinite(x)) and np.all(np.isfinite(y))) or np.any(b < 0) or np.any(b >= self.counts.size):
+            raise CudaCppError("invalid L1 revival calibration")
+        X = x.reshape(b.size, self.input)
+        Y = y.reshape(b.size, 2 * self.width)
+        W, I = self.width, self.input
+        for row in range(b.size):
+            if weights is not None and weights[row] == 0.0:
+                continue
+            k = int(b[row])
+            self.counts[k] += 1
+            self.contribution.add(k, Y[row])
+            self.sums[k * I:(k + 1) * I] += X[row].astype(np.float64)
+            sq, nm = Y[row, :W], Y[row, W:]
+            self.branch_sums[2 * k * W:(2 * k + 1) * W] += sq.astype(np.float64)
+            self.branch_sums[(2 * k + 1) * W:(2 * k + 2) * W] += nm.astype(np.float64)
+            self.upper[k * W:(k + 1) * W] += ((sq >= 1.0) & (nm >= 1.0))
+            self.lower[k * W:(k + 1) * W] += ((sq <= 0.0) & (nm <= 0.0))
+
+    def candidates_for(self, upper: bool, zero: bool) -> List[int]:
+        if self.contribution.relative.size:
+            return self.contribution.selected(self.counts, self.width) if (upper or zero) else []
+        return [i for i in range(self.upper.size) if self.is_upper(i, upper) or self.is_zero(i, zero)]
+
+
+def _flags(runner, name: str) -> int:
+    return int(getattr(runner, name, 0))
+
+
+def revive_l1_selected(ctx, runner, c: L1Calibration, upper: bool, zero: bool) -> List[int]:
+    """Reinitialise the selected L1 units (bucket * l1_hidden + unit) from the
+    revival stream with the bias that puts their calibration mean at 0.5, and
+    point the L2 weights reading their two branches at +-1/64 with the old
+    branch constants absorbed into the L2 biases (revive_l1_selected,
+    l1_revive.rs:150-225).  Once per revival epoch for each kind."""
+    flags = _flags(runner, "l1_revival_flags")
+    upper = upper and not (flags & 1)
+    zero = zero and not (flags & 2)
+    if not upper and not zero:
+        return []
+    if runner.present.get("l2fw") or runner.present.get("l3fw"):
+        raise CudaCppError("L1 revival requires non-BN L1 (none/shared/axis/pair), no residual count gates or legacy "
+                           "L2/L3 factorizers, and no pending gradients")
+    sh = runner.shape
+    H, n, ft, S, L2 = sh.l1_hidden, sh.l1_out, sh.ft_size, sh.num_stacks, sh.l2_size
+    l2_in = sh.l2_in
+    if c.input != ft or c.width != H or c.counts.size != S or int(c.counts.sum()) == 0:
+        raise CudaCppError("empty or incompatible L1 calibration")
+    ids = c.candidates_for(upper, zero)
+    w1 = runner.weights["l1w"].download(ctx).reshape(S * n, ft)
+    b1 = runner.weights["l1b"].download(ctx)
+    w2 = runner.weights["l2w"].download(ctx).reshape(S * L2, l2_in)
+    b2 = runner.weights["l2b"].download(ctx)
+    ws = runner.optimizer_states["l1w"].download(ctx)
+    bs_ = runner.optimizer_states["l1b"].download(ctx)
+    os_ = runner.optimizer_states["l2w"].download(ctx)
+    obs = runner.optimizer_states["l2b"].download(ctx)
+    wsm, wsv, wss = (ws[k].reshape(S * n, ft) for k in ("momentum", "velocity", "slow_params"))
+    osm, osv, oss = (os_[k].reshape(S * L2, l2_in) for k in ("momentum", "velocity", "slow_params"))
+    cw, cws = _shared_terms(ctx, runner)
+    cb, cbs = _shared_bias(ctx, runner)
+    rng = _runner_rng(runner)
+    bound = F32(np.sqrt(F32(6.0) / F32(ft + H)))
+    for i in ids:
+        bucket, u = divmod(i, H)
+        out = bucket * n + u
+        value = rng.signed_uniform_array(ft) * bound
+        mean = 0.0
+        sums = c.sums[bucket * ft:(bucket + 1) * ft]
+        cnt = float(c.counts[bucket])
+        terms = value.astype(np.float64) * sums / cnt
+        for t in terms:
+            mean += t
+        w1[out] = value - cw[u]
+        wsm[out] = 0.0
+        wsv[out] = 0.0
+        wss[out] = value - cws[u]
+        bias = F32(0.5) - F32(mean)
+        b1[out] = bias - cb[u]
+        bs_["momentum"][out] = 0.0
+        bs_["velocity"][out] = 0.0
+        bs_["slow_params"][out] = bias - cbs[u]
+        for j in range(L2):
+            row = bucket * L2 + j
+            for col in (u, H + u):
+                constant = F32(c.branch_sums[bucket * 2 * H + col] / cnt)
+                b2[row] += constant * w2[row, col]
+                obs["slow_params"][row] += constant * oss[row, col]
+                v = F32(-1.0 / 64.0) if w2[row, col] < 0.0 else F32(1.0 / 64.0)
+                w2[row, col] = v
+                osm[row, col] = 0.0
+                osv[row, col] = 0.0
+                oss[row, col] = v
+            obs["momentum"][row] = 0.0
+            obs["velocity"][row] = 0.0
+    if not all(np.all(np.isfinite(a)) for a in (w1, b1, w2, b2, wss, bs_["slow_params"], obs["slow_params"])):
+        raise CudaCppError("non-finite L1 revival result")
+    runner.weights["l1w"].upload(w1, ctx)
+    _upload_state(ctx, runner.optimizer_states["l1w"], {"momentum": wsm, "velocity": wsv, "slow_params": wss})
+    runner.weights["l1b"].upload(b1, ctx)
+    _upload_state(ctx, runner.optimizer_states["l1b"], bs_)
+    runner.weights["l2w"].upload(w2, ctx)
+    _upload_state(ctx, runner.optimizer_states["l2w"], {"momentum": osm, "velocity": osv, "slow_params": oss})
+    runner.weights["l2b"].upload(b2, ctx)
+    _upload_state(ctx, runner.optimizer_states["l2b"], obs)
+    _invalidate_qat(runner)
+    runner.l1_revival_flags = flags | int(upper) | (int(zero) << 1)
+    return ids
+
+
+def compensate_l1_revival_mean(ctx, runner, ids: Sequence[int], c: L1Calibration) -> None:
+    """Subtract the revived branches' measured means at each L2 preactivation
+    (compensate_l1_revival_mean, l1_revive.rs:227-258)."""
+    if not ids:
+        return
+    sh = runner.shape
+    H, S, L2, l2_in = sh.l1_hidden, sh.num_stacks, sh.l2_size, sh.l2_in
+    if c.width != H or c.counts.size != S or any(i >= S * H or c.counts[i // H] == 0 for i in ids):
+        raise CudaCppError("invalid L1 revival mean calibration")
+    w = runner.weights["l2w"].download(ctx).reshape(S * L2, l2_in)
+    sw = runner.optimizer_states["l2w"].slow_params.download(ctx).reshape(S * L2, l2_in)
+    b = runner.weights["l2b"].download(ctx)
+    sb_ = runner.optimizer_states["l2b"].slow_params.download(ctx)
+    for i in ids:
+        bucket, u = divmod(int(i), H)
+        for col in (u, H + u):
+            mean = F32(c.branch_sums[bucket * 2 * H + col] / float(c.counts[bucket]))
+            rows = slice(bucket * L2, (bucket + 1) * L2)
+            b[rows] -= w[rows, col] * mean
+            sb_[rows] -= sw[rows, col] * mean
+    if not (np.all(np.isfinite(b)) and np.all(np.isfinite(sb_))):
+        raise CudaCppError("non-finite L1 revival mean compensation")
+    runner.weights["l2b"].upload(b, ctx)
+    runner.optimizer_states["l2b"].slow_params.upload(sb_, ctx)
+    from .sfnn import SfnnLayerQatCopies
+
     runner.layer_qat = SfnnLayerQatCopies()

@@ -126,3 +126,62 @@ def test_revival_rejects_legacy_factorizers(ctx):
     r = bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(s, **w), 1024, 1)
     with pytest.raises(bo.CudaCppError, match="FT revival requires"):
         rv.revive_ft(ctx, r, _cal(), [0], s.input_size)
+
+
+def test_l1_contribution_mixed_constant_transfers_only_square_mean(ctx):
+    """gpu_contribution_mixed_constant_transfers_only_square_mean
+    (l1_revive.rs:290-320): unit 0 of bucket 0 has a constant square branch of
+    1 and a constant normal branch of 0; reviving it moves exactly the L2
+    weight of the square branch into the L2 bias."""
+    s = bs.SfnnForwardShape(bs.HALFKA_HM2_DIMENSIONS + bs.PIECE_INPUTS, 12, 2, True, 5, 4)
+    w = syn.sfnn_weights(syn.rng_for(14), s.input_size, s.ft_size, s.l1_hidden, s.l1_skip, s.l2_size,
+                         s.num_stacks, False, False, 0.1)
+    r = bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(s, **w), 1024, 1)
+    c = rv.L1Calibration(s.ft_size, s.l1_hidden, s.num_stacks)
+    for i in range(1024):
+        c.add([0], np.zeros(s.ft_size, np.float32), [1.0, float(i % 2), 0.0, float(i % 2)])
+    old = r.read_weights(ctx)
+    c.contribution.finish(old["l2w"], s.l2_size, 2, 0.01)
+    assert c.candidates_for(True, False) == [0]
+    assert rv.revive_l1_selected(ctx, r, c, True, False) == [0]
+    new = r.read_weights(ctx)
+    l2w = old["l2w"].reshape(-1, s.l2_in)
+    for j in range(s.l2_size):
+        assert abs(new["l2b"][j] - old["l2b"][j] - l2w[j, 0]) < 1e-6
+    np.testing.assert_array_equal(old["l0w"], new["l0w"])
+    np.testing.assert_array_equal(old["l3w"], new["l3w"])
+    # the revived unit: fresh row from the stream, bias 0.5 at a zero input mean
+    rng = RevivalRng()
+    bound = np.float32(np.sqrt(np.float32(6.0) / np.float32(s.ft_size + s.l1_hidden)))
+    np.testing.assert_array_equal(new["l1w"][:s.ft_size], rng.signed_uniform_array(s.ft_size) * bound)
+    assert new["l1b"][0] == np.float32(0.5)
+    np.testing.assert_array_equal(new["l1w"][s.ft_size:], old["l1w"][s.ft_size:])
+    np.testing.assert_array_equal(new["l1b"][1:], old["l1b"][1:])
+    assert set(np.abs(new["l2w"].reshape(-1, s.l2_in)[:s.l2_size, [0, 2]]).ravel().tolist()) == {1 / 64}
+    # once per epoch; a no-op leaves the stream alone
+    state = r.revival_rng.state
+    assert rv.revive_l1_selected(ctx, r, c, True, False) == []
+    assert r.revival_rng.state == state
+    snap = sb.sfnn_runner_state(ctx, r, 0, 0)
+    rv.begin_revival_epoch(r)
+    assert r.revival_rng.state == state
+    rv.revive_l1_selected(ctx, r, c, True, False)
+    second = r.read_weights(ctx)
+    assert not np.array_equal(new["l1w"], second["l1w"])
+    sb.restore_sfnn_runner(ctx, r, snap)
+    rv.begin_revival_epoch(r)
+    rv.revive_l1_selected(ctx, r, c, True, False)
+    again = r.read_weights(ctx)
+    for k in second:
+        np.testing.assert_array_equal(again[k], second[k], err_msg=k)
+    # mean compensation removes the measured branch means from the L2 biases
+    m = rv.L1Calibration(s.ft_size, s.l1_hidden, s.num_stacks)
+    for i in range(8):
+        m.add([0], np.zeros(s.ft_size, np.float32), [0.5, 0.0, 0.25, 0.0])
+    before = r.read_weights(ctx)
+    rv.compensate_l1_revival_mean(ctx, r, [0], m)
+    after = r.read_weights(ctx)
+    w2 = before["l2w"].reshape(-1, s.l2_in)
+    for j in range(s.l2_size):
+        exp = np.float32(np.float32(before["l2b"][j] - w2[j, 0] * np.float32(0.5)) - w2[j, 2] * np.float32(0.25))
+        assert after["l2b"][j] == exp
