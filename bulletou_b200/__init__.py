@@ -71,8 +71,9 @@ from .state_bin import (  # noqa: F401
     write_sfnn_checkpoint, write_sfnn_state_bin,
 )
 from .revive import (  # noqa: F401
-    Contribution, FtCalibration, L1Calibration, begin_revival_epoch, compensate_ft_revival_mean,
-    compensate_l1_revival_mean, revive_ft, revive_ft_units, revive_l1_selected, saturated_units,
+    Contribution, FtCalibration, L1Calibration, L2Calibration, begin_revival_epoch, compensate_ft_revival_mean,
+    compensate_l1_revival_mean, revive_ft, revive_ft_units, revive_l1_selected, revive_l2, revive_l2_selected,
+    saturated_units,
 )
 
 __version__ = "0.1.0"

@@ -2,7 +2,9 @@
 get fresh random rows, the L1 columns that read them are reset to +-1/64 with
 the change absorbed into the L1 biases, and the optimizer state of everything
 touched restarts; dead or saturated L1 units get fresh rows the same way, with
-the L2 weights that read them reset (crates/cuda_cpp/src/l1_revive.rs).
+the L2 weights that read them reset (crates/cuda_cpp/src/l1_revive.rs), and so
+do L2 units, with the output weight reset (crates/cuda_cpp/src/l2_revive.rs,
+the path without BatchNorm).
 
 Restates crates/cuda_cpp/src/ft_revive.rs (saturated_units :5-10,
 Calibration :12-52, revive_ft / revive_ft_units :57-117,
@@ -492,3 +494,150 @@ def compensate_l1_revival_mean(ctx, runner, ids: Sequence[int], c: L1Calibration
     from .sfnn import SfnnLayerQatCopies
 
     runner.layer_qat = SfnnLayerQatCopies()
+
+
+# ------------------------------------------------------------------ L2 revival
+class L2Calibration:
+    """Per-bucket L2 statistics (crates/cuda_cpp/src/l2_revive.rs Calibration,
+    :4-74): the L2 inputs of every calibration position, activation sums,
+    upper / zero saturation counts and the contribution samples."""
+
+    def __init__(self, input_size: int, width: int, groups: int):
+        self.input, self.width = int(input_size), int(width)
+        self.counts = np.zeros(groups, np.int64)
+        self.upper = np.zeros(groups * width, np.int64)
+        self.lower = np.zeros(groups * width, np.int64)
+        self.upper_threshold = 0.99
+        self.zero_threshold = 0.99
+        self.inputs = [[] for _ in range(groups)]
+        self.contribution = Contribution(width, groups)
+        self.sums = np.zeros(groups * width, np.float64)
+
+    set_thresholds = L1Calibration.set_thresholds
+    is_upper = L1Calibration.is_upper
+    is_zero = L1Calibration.is_zero
+
+    def add(self, buckets, x, y, weights=None) -> None:
+        b = np.asarray(buckets, np.int64).reshape(-1)
+        x = np.asarray(x, np.float32).reshape(-1)
+        y = np.asarray(y, np.float32).reshape(-1)
+        if x.size != b.size * self.input:
+            raise CudaCppError(f"revive inputs length mismatch: expected {b.size * self.input}, got {x.size}")
+        if y.size != b.size * self.width:
+            raise CudaCppError(f"revive outputs length mismatch: expected {b.size * self.width}, got {y.size}")
+        if weights is not None:
+            weights = np.asarray(weights, np.float32).reshape(-1)
+            if weights.size != b.size:
+                raise CudaCppError(f"L2 revival sample weights length mismatch: expected {b.size}, got {weights.size}")
+            if not np.all(np.isfinite(weights)) or np.any(weights < 0):
+                raise CudaCppError("invalid L2 revival sample weight")
+        if not (np.all(np.isfinite(x)) and np.all(np.isfinite(y))) or np.any(b < 0) or np.any(b >= self.counts.size):
+            raise CudaCppError("invalid L2 revival calibration")
+        X = x.reshape(b.size, self.input)
+        Y = y.reshape(b.size, self.width)
+        W = self.width
+        for row in range(b.size):
+            if weights is not None and weights[row] == 0.0:
+                continue
+            k = int(b[row])
+            self.counts[k] += 1
+            self.contribution.add(k, Y[row])
+            self.inputs[k].append(X[row].copy())
+            self.sums[k * W:(k + 1) * W] += Y[row].astype(np.float64)
+            self.upper[k * W:(k + 1) * W] += Y[row] >= 1.0
+            self.lower[k * W:(k + 1) * W] += Y[row] <= 0.0
+
+    def candidates(self) -> List[int]:
+        return self.candidates_for(True, False)
+
+    candidates_for = L1Calibration.candidates_for
+
+
+def _seq_sum(values) -> float:
+    acc = 0.0
+    for v in values:
+        acc += float(v)
+    return acc
+
+
+def revive_l2_selected(ctx, runner, c: L2Calibration, upper: bool, zero: bool) -> List[int]:
+    """Reinitialise the selected L2 units from the revival stream with the bias
+    that centres their calibration pre-activation at 0.5, point their output
+    weight at +-1/64 and move the old mean contribution (and the new unit's
+    quantised mean) into the output bias (revive_l2_selected,
+    l2_revive.rs:96-175, the path without BatchNorm)."""
+    flags = _flags(runner, "l2_revival_flags")
+    upper = upper and not (flags & 1)
+    zero = zero and not (flags & 2)
+    if not upper and not zero:
+        return []
+    if runner.present.get("l2fw") or runner.present.get("l3fw"):
+        raise CudaCppError("L2 revival requires SFNN L1 (none/shared/axis/pair), no legacy L2/L3 factorizer or "
+                           "residual gates, and no pending gradients")
+    sh = runner.shape
+    I, L2, S = sh.l2_in, sh.l2_size, sh.num_stacks
+    if c.input != I or c.width != L2 or c.counts.size != S or int(c.counts.sum()) == 0:
+        raise CudaCppError("empty or incompatible L2 calibration")
+    ids = c.candidates_for(upper, zero)
+    w = runner.weights["l2w"].download(ctx).reshape(S * L2, I)
+    b = runner.weights["l2b"].download(ctx)
+    out = runner.weights["l3w"].download(ctx)
+    ob = runner.weights["l3b"].download(ctx)
+    ws = runner.optimizer_states["l2w"].download(ctx)
+    bs_ = runner.optimizer_states["l2b"].download(ctx)
+    os_ = runner.optimizer_states["l3w"].download(ctx)
+    obs = runner.optimizer_states["l3b"].download(ctx)
+    wsm, wsv, wss = (ws[k].reshape(S * L2, I) for k in ("momentum", "velocity", "slow_params"))
+    rng = _runner_rng(runner)
+    bound = F32(np.sqrt(F32(6.0) / F32(I + L2)))
+    for i in ids:
+        g = i // L2
+        w[i] = rng.signed_uniform_array(I) * bound
+        wsm[i] = 0.0
+        wsv[i] = 0.0
+        wss[i] = w[i]
+        rows = np.array(c.inputs[g], np.float64).reshape(-1, I)
+        count = float(c.counts[g])
+        wq = (_round_half_away(w[i] * F32(64.0)) / F32(64.0)).astype(np.float64)
+        wd = w[i].astype(np.float64)
+        dot = np.zeros(rows.shape[0])
+        dq = np.zeros(rows.shape[0])
+        for k in range(I):
+            dot += rows[:, k] * wd[k]
+            dq += rows[:, k] * wq[k]
+        mean_dot = _seq_sum(dot) / count
+        beta = F32(0.5) - F32(mean_dot)
+        bq = float(_round_half_away(np.array([beta * F32(8128.0)], F32))[0] / F32(8128.0))
+        mean_y = _seq_sum(np.clip(dq + bq, 0.0, 1.0)) / count
+        v = F32(-1.0 / 64.0) if out[i] < 0.0 else F32(1.0 / 64.0)
+        old_activation = F32(c.sums[i] / count)
+        my = F32(mean_y)
+        ob[g] += old_activation * out[i] - v * my
+        obs["slow_params"][g] += old_activation * os_["slow_params"][i] - v * my
+        out[i] = v
+        os_["slow_params"][i] = v
+        os_["momentum"][i] = 0.0
+        os_["velocity"][i] = 0.0
+        b[i] = beta
+        bs_["slow_params"][i] = beta
+        bs_["momentum"][i] = 0.0
+        bs_["velocity"][i] = 0.0
+    if not all(np.all(np.isfinite(a)) for a in (w, b, out, ob)):
+        raise CudaCppError("non-finite L2 revival result")
+    runner.weights["l2w"].upload(w, ctx)
+    runner.weights["l2b"].upload(b, ctx)
+    runner.weights["l3w"].upload(out, ctx)
+    runner.weights["l3b"].upload(ob, ctx)
+    _upload_state(ctx, runner.optimizer_states["l2w"], {"momentum": wsm, "velocity": wsv, "slow_params": wss})
+    _upload_state(ctx, runner.optimizer_states["l2b"], bs_)
+    _upload_state(ctx, runner.optimizer_states["l3w"], os_)
+    _upload_state(ctx, runner.optimizer_states["l3b"], obs)
+    runner.l2_revival_flags = flags | int(upper) | (int(zero) << 1)
+    from .sfnn import SfnnLayerQatCopies
+
+    runner.layer_qat = SfnnLayerQatCopies()
+    return ids
+
+
+def revive_l2(ctx, runner, c: L2Calibration) -> List[int]:
+    return revive_l2_selected(ctx, runner, c, True, False)

@@ -185,3 +185,33 @@ def test_l1_contribution_mixed_constant_transfers_only_square_mean(ctx):
     for j in range(s.l2_size):
         exp = np.float32(np.float32(before["l2b"][j] - w2[j, 0] * np.float32(0.5)) - w2[j, 2] * np.float32(0.25))
         assert after["l2b"][j] == exp
+
+
+def test_l2_contribution_preserves_empirical_mean(ctx):
+    """gpu_contribution_preserves_empirical_mean_not_upper_or_zero
+    (l2_revive.rs:181-202): unit 0 is constant at 0.75; its revival moves
+    0.75 * w_old into the output bias and takes out the new unit's mean 0.5
+    times its new weight."""
+    s = SHAPE
+    w = syn.sfnn_weights(syn.rng_for(15), s.input_size, s.ft_size, s.l1_hidden, s.l1_skip, s.l2_size,
+                         s.num_stacks, False, False, 0.1)
+    r = bs.SfnnTrainStepRunner(ctx, bs.SfnnForwardHostWeights(s, **w), 1024, 1)
+    c = rv.L2Calibration(s.l2_in, s.l2_size, s.num_stacks)
+    for i in range(1024):
+        y = np.full(s.l2_size, float(i % 2), np.float32)
+        y[0] = 0.75
+        c.add([0], np.zeros(s.l2_in, np.float32), y)
+    old = r.read_weights(ctx)
+    c.contribution.finish(old["l3w"], 1, 1, 0.01)
+    assert c.candidates_for(True, False) == [0]
+    assert rv.revive_l2_selected(ctx, r, c, True, False) == [0]
+    new = r.read_weights(ctx)
+    assert abs(new["l3b"][0] - old["l3b"][0] - 0.75 * old["l3w"][0] + 0.5 * new["l3w"][0]) < 1e-6
+    np.testing.assert_array_equal(old["l0w"], new["l0w"])
+    np.testing.assert_array_equal(old["l1w"], new["l1w"])
+    rng = RevivalRng()
+    bound = np.float32(np.sqrt(np.float32(6.0) / np.float32(s.l2_in + s.l2_size)))
+    np.testing.assert_array_equal(new["l2w"][:s.l2_in], rng.signed_uniform_array(s.l2_in) * bound)
+    assert new["l2b"][0] == np.float32(0.5) and abs(new["l3w"][0]) == np.float32(1 / 64)
+    np.testing.assert_array_equal(new["l2w"][s.l2_in:], old["l2w"][s.l2_in:])
+    assert rv.revive_l2_selected(ctx, r, c, True, False) == []

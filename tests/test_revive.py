@@ -117,3 +117,20 @@ def test_l1_calibration_statistics():
     assert c.upper.tolist() == [1, 0, 0, 0] and c.lower.tolist() == [0, 1, 1, 1]
     with pytest.raises(CudaCppError):
         c.add([2], x[:1], y[:1])
+
+
+def test_l2_calibration_thresholds_and_statistics():
+    c = rv.L2Calibration(1, 4, 1)
+    c.counts[0] = 10000
+    c.upper[:] = [9900, 9899, 0, 0]
+    c.lower[:] = [0, 0, 9900, 9899]
+    assert c.candidates_for(True, True) == [0, 2] and c.candidates() == [0]
+    c.set_thresholds(0.98, 0.995)
+    assert c.candidates_for(True, True) == [0, 1]
+    d = rv.L2Calibration(2, 2, 2)
+    d.add([1, 1, 0], [[1, 2], [3, 4], [5, 6]], [[1.0, 0.0], [0.5, 0.0], [2.0, -1.0]], [1.0, 1.0, 0.0])
+    assert d.counts.tolist() == [0, 2] and d.sums.tolist() == [0, 0, 1.5, 0]
+    assert d.upper.tolist() == [0, 0, 1, 0] and d.lower.tolist() == [0, 0, 0, 2]
+    assert len(d.inputs[1]) == 2 and d.inputs[1][1].tolist() == [3, 4]
+    with pytest.raises(CudaCppError):
+        d.add([0], [1, 2], [1.0])
