@@ -968,11 +968,11 @@ SFNN_DRAM_BYTES_B65536 = {
 # The same on the default --data psv batches (decoded PackedSfenValue records;
 # capture of `bench.py --steps 1 --warmup 3 --no-cpu-baseline`).
 SFNN_DRAM_BYTES_PSV_B65536 = {
-    "ft_rows_ranger": (11025470720, ("all",)),
-    "ft_forward": (1181280768, ("all",)),
-    "ft_integer": (569521408, ("all",)),
-    "l1_backward": (2068910848, ("all",)),
-    "fold": (1124453632, ("all",)),
+    "ft_rows_ranger": (4668284928, ("all",)),
+    "ft_forward": (1181817600, ("all",)),
+    "ft_integer": (570697728, ("all",)),
+    "l1_backward": (2068230656, ("all",)),
+    "fold": (1125304832, ("all",)),
 }
 
 
