@@ -67,8 +67,8 @@ from .nn_bin import nnue_nn_bin_bytes, sfnn_nn_bin_bytes, write_nnue_nn_bin, wri
 
 from .state_bin import (  # noqa: F401
     CheckpointLog, SfnnTrainState, latest_complete_checkpoint_dir, load_halfkp_state, load_sfnn_state,
-    parse_model_weights_bin, restore_halfkp_runner, restore_sfnn_runner, write_checkpoint_dir, write_halfkp_state_bin,
-    write_sfnn_checkpoint, write_sfnn_state_bin,
+    parse_model_weights_bin, restore_halfkp_runner, restore_sfnn_runner, write_checkpoint_dir, write_halfkp_checkpoint,
+    write_halfkp_state_bin, write_sfnn_checkpoint, write_sfnn_state_bin,
 )
 from .revive import (  # noqa: F401
     Contribution, FtCalibration, L1Calibration, L2Calibration, begin_revival_epoch, compensate_ft_revival_mean,

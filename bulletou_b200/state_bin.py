@@ -575,3 +575,21 @@ def write_sfnn_checkpoint(output_dir, ctx, runner, log: CheckpointLog, completed
         write_sfnn_state_bin(tmp / "state.bin", ctx, runner, completed_steps, optimizer_steps)
 
     return write_checkpoint_dir(output_dir, log, payload)
+
+
+def write_halfkp_checkpoint(output_dir, ctx, runner, log: CheckpointLog, completed_steps: int, quantized=None,
+                            feature_set: str = "halfkp") -> Path:
+    """A numbered HalfKP checkpoint (write_cuda_cpp_nnue_numbered_checkpoint,
+    examples/bulletou.rs:20925-20948): nn.bin from the device quantisation of
+    the runner's weights (when ``quantized``, a QuantizedNnueDeviceWeights, is
+    given), state.bin, dataloader_pos.txt and learn.log."""
+    from .nn_bin import write_nnue_nn_bin
+    from .nnue_quant import nnue_quantize_device
+
+    def payload(tmp: Path) -> None:
+        if quantized is not None:
+            nnue_quantize_device(ctx, dict(zip(HALFKP_NAMES, runner.weights)), quantized)
+            write_nnue_nn_bin(tmp / "nn.bin", ctx, quantized, feature_set)
+        write_halfkp_state_bin(tmp / "state.bin", ctx, runner, completed_steps)
+
+    return write_checkpoint_dir(output_dir, log, payload)

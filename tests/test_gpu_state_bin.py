@@ -78,8 +78,15 @@ def test_halfkp_state_resume(ctx, tmp_path):
         full.step_no_readback(ctx, _ranger(step), loss, 1 / 600, hb(b))
     for step, b in enumerate(batches[:4], 1):
         part.step_no_readback(ctx, _ranger(step), loss, 1 / 600, hb(b))
-    sb.write_halfkp_state_bin(tmp_path / "state.bin", ctx, part, 4)
-    weights, opt, done = sb.load_halfkp_state(tmp_path / "state.bin", sb.halfkp_runner_sizes(resumed))
+    hs = bo.NNUE_HALFKP_256X2_32_32
+    shape = (hs.input_size, hs.l1, hs.l2, hs.l3)
+    dq = bo.QuantizedNnueDeviceWeights(ctx, *shape)
+    log = sb.CheckpointLog(1, 4, 4, 4 * B, 1e-3, 1e-3, 0.5, eval_name="halfkp_256x2-32-32")
+    d = sb.write_halfkp_checkpoint(tmp_path, ctx, part, log, 4, dq)
+    assert sb.is_complete_checkpoint_dir(d) and sb.latest_complete_checkpoint_dir(tmp_path) == d
+    saved = part.read_weights(ctx)
+    assert (d / "nn.bin").read_bytes() == nb.nnue_nn_bin_bytes(oracle.nnue_quantize(shape, saved), *shape[1:])
+    weights, opt, done = sb.load_halfkp_state(d / "state.bin", sb.halfkp_runner_sizes(resumed))
     assert done == 4
     sb.restore_halfkp_runner(ctx, resumed, weights, opt)
     for step, b in enumerate(batches[4:], done + 1):
