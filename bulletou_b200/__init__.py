@@ -63,7 +63,10 @@ from .teacher import (  # noqa: F401
 )
 
 from .validate import AccuracyReport, ValidationLossKind, ValidationMetrics, sfnn_validation_stats  # noqa: F401
-from .nn_bin import nnue_nn_bin_bytes, sfnn_nn_bin_bytes, write_nnue_nn_bin, write_sfnn_nn_bin  # noqa: F401
+from .nn_bin import (  # noqa: F401
+    nnue_nn_bin_bytes, parse_nnue_nn_bin, parse_sfnn_nn_bin, read_nnue_nn_bin, read_sfnn_nn_bin, sfnn_nn_bin_bytes,
+    write_nnue_nn_bin, write_sfnn_nn_bin,
+)
 
 from .state_bin import (  # noqa: F401
     CheckpointLog, SfnnTrainState, latest_complete_checkpoint_dir, load_halfkp_state, load_sfnn_state,

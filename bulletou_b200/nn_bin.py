@@ -167,3 +167,138 @@ def write_sfnn_nn_bin(path, ctx: Context, q, feature_set: str = "halfka_hm2", da
     blob = sfnn_nn_bin_bytes(arrays, sh.ft_size, sh.l1_out, sh.l2_size, sh.l2_in, sh.num_stacks, feature_set)
     Path(path).write_bytes(blob)
     return len(blob)
+
+
+# ------------------------------------------------------------------ readers
+def _pad32(n: int) -> int:
+    return (n + 31) // 32 * 32
+
+
+class _Reader:
+    def __init__(self, blob: bytes, what: str):
+        self.b, self.off, self.what = blob, 0, what
+
+    def u32(self) -> int:
+        if self.off + 4 > len(self.b):
+            raise CudaCppError(f"{self.what}: truncated file")
+        v = struct.unpack_from("<I", self.b, self.off)[0]
+        self.off += 4
+        return v
+
+    def array(self, dtype, n: int) -> np.ndarray:
+        nbytes = np.dtype(dtype).itemsize * n
+        if self.off + nbytes > len(self.b):
+            raise CudaCppError(f"{self.what}: truncated file")
+        a = np.frombuffer(self.b, dtype, n, self.off).copy()
+        self.off += nbytes
+        return a
+
+    def bytes(self, n: int) -> bytes:
+        if self.off + n > len(self.b):
+            raise CudaCppError(f"{self.what}: truncated file")
+        v = self.b[self.off:self.off + n]
+        self.off += n
+        return v
+
+    def expect(self, value: int, label: str) -> None:
+        got = self.u32()
+        if got != value:
+            raise CudaCppError(f"{self.what}: {label} mismatch: expected 0x{value:08X}, got 0x{got:08X}")
+
+    def end(self) -> None:
+        if self.off != len(self.b):
+            raise CudaCppError(f"{self.what}: {len(self.b) - self.off} trailing bytes")
+
+
+def parse_nnue_nn_bin(blob: bytes, rows: int, l1: int = 256, l2: int = 32, l3: int = 32,
+                      feature_set: str = "halfkp") -> dict:
+    """The quantised tensors of a HalfKP nn.bin (the engine's layout, as
+    written by nnue_nn_bin_bytes); header, hashes and sizes are checked."""
+    r = _Reader(bytes(blob), "nn.bin")
+    r.expect(NNUE_VERSION, "version")
+    r.expect(network_hash(feature_set, l1, l2, l3), "network hash")
+    desc = r.bytes(r.u32())
+    if desc != description(feature_set, l1, l2, l3).encode():
+        raise CudaCppError("nn.bin: architecture description mismatch")
+    r.expect(ft_hash(feature_set, l1), "feature transformer hash")
+    out = {"l0b": r.array("<i2", l1), "l0w": r.array("<i2", rows * l1)}
+    r.expect(compute_fc_hash(l1, l2, l3), "network hash of the dense layers")
+    for b, w, n_out, n_in in (("l1b", "l1w", l2, 2 * l1), ("l2b", "l2w", l3, l2), ("outb", "outw", 1, l3)):
+        out[b] = r.array("<i4", n_out)
+        out[w] = r.array("i1", n_out * _pad32(n_in))
+    r.end()
+    return out
+
+
+def read_signed_leb128_i16(data: bytes, count: int) -> tuple:
+    """count signed-LEB128 values from the start of data; returns (values,
+    bytes consumed)."""
+    b = np.frombuffer(data, np.uint8)
+    ends = np.flatnonzero((b & 0x80) == 0)
+    if ends.size < count:
+        raise CudaCppError("nn.bin: truncated COMPRESSED_LEB128 block")
+    if count == 0:
+        return np.zeros(0, np.int16), 0
+    ends = ends[:count]
+    starts = np.concatenate(([0], ends[:-1] + 1))
+    lengths = ends - starts + 1
+    if lengths.max() > 3:
+        raise CudaCppError("nn.bin: LEB128 value longer than an i16")
+    val = np.zeros(count, np.int64)
+    for k in range(3):
+        has = lengths > k
+        val[has] |= (b[starts[has] + k].astype(np.int64) & 0x7F) << (7 * k)
+    neg = (b[ends] & 0x40) != 0
+    val[neg] -= np.left_shift(np.int64(1), 7 * lengths[neg])
+    if val.min() < -32768 or val.max() > 32767:
+        raise CudaCppError("nn.bin: LEB128 value outside i16")
+    return val.astype(np.int16), int(ends[-1] + 1)
+
+
+def parse_sfnn_nn_bin(blob: bytes, rows: int, ft: int, l1_out: int, l2: int, l2_in: int, stacks: int,
+                      feature_set: str = "halfka_hm2") -> dict:
+    """The quantised tensors of an SFNN nn.bin (as written by
+    sfnn_nn_bin_bytes), in the engine layout QuantizedSfnnDeviceWeights holds."""
+    r = _Reader(bytes(blob), "SFNN nn.bin")
+    r.expect(NNUE_VERSION, "version")
+    r.expect(SFNN_KHASH, "kHash")
+    arch = r.bytes(r.u32())
+    if arch != sfnn_architecture(feature_set, ft, stacks).encode():
+        raise CudaCppError(f"SFNN nn.bin: architecture mismatch: {arch!r}")
+    r.expect(SFNN_FT_HASH, "feature transformer hash")
+    out = {}
+    for name, n in (("l0b", ft), ("l0w", rows * ft)):
+        if r.bytes(len(LEB128_MAGIC)) != LEB128_MAGIC:
+            raise CudaCppError(f"SFNN nn.bin: {name} is not a COMPRESSED_LEB128 block")
+        size = r.u32()
+        payload = r.bytes(size)
+        vals, used = read_signed_leb128_i16(payload, n)
+        if used != size:
+            raise CudaCppError(f"SFNN nn.bin: {name} block holds {size - used} extra bytes")
+        out[name] = vals
+    parts = {k: [] for k in ("l1b", "l1w", "l2b", "l2w", "l3b", "l3w")}
+    for _ in range(stacks):
+        r.expect(SFNN_NETWORK_HASH, "stack network hash")
+        parts["l1b"].append(r.array("<i4", l1_out))
+        parts["l1w"].append(r.array("i1", l1_out * _pad32(ft)))
+        parts["l2b"].append(r.array("<i4", l2))
+        parts["l2w"].append(r.array("i1", l2 * _pad32(l2_in)))
+        parts["l3b"].append(r.array("<i4", 1))
+        parts["l3w"].append(r.array("i1", _pad32(l2)))
+    r.end()
+    out.update({k: np.concatenate(v) for k, v in parts.items()})
+    return out
+
+
+def read_nnue_nn_bin(path, ctx: Context, q: QuantizedNnueDeviceWeights, feature_set: str = "halfkp") -> None:
+    """Loads a HalfKP nn.bin into the device tensors of ``q`` (its dims give
+    the expected layout)."""
+    _, l1, l2, l3 = q.dims
+    q.upload(parse_nnue_nn_bin(Path(path).read_bytes(), q.rows, l1, l2, l3, feature_set), ctx)
+
+
+def read_sfnn_nn_bin(path, ctx: Context, q, feature_set: str = "halfka_hm2") -> None:
+    """Loads an SFNN nn.bin into a QuantizedSfnnDeviceWeights."""
+    sh = q.shape
+    q.upload(parse_sfnn_nn_bin(Path(path).read_bytes(), q.rows, sh.ft_size, sh.l1_out, sh.l2_size, sh.l2_in,
+                               sh.num_stacks, feature_set), ctx)

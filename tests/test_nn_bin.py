@@ -165,3 +165,82 @@ def test_sfnn_device_quantised_file_matches_the_oracle_bytes(ctx, tmp_path):
                                 sh.l2_in, sh.num_stacks)
     got = (tmp_path / "nn.bin").read_bytes()
     assert n == len(want) and got == want
+
+
+# ------------------------------------------------------------------ readers
+def test_halfkp_read_round_trip_and_checks():
+    shape = (SHAPE[0] + 1548,) + SHAPE[1:]
+    w = synthetic.halfkp_weights(synthetic.rng_for(7), input_size=shape[0], std=0.05)
+    q = oracle.nnue_quantize(shape, w)
+    blob = nb.nnue_nn_bin_bytes(q, 256, 32, 32)
+    got = nb.parse_nnue_nn_bin(blob, SHAPE[0])
+    for k in oracle.NNUE_QUANT_NAMES:
+        np.testing.assert_array_equal(got[k], np.asarray(q[k]).reshape(-1), err_msg=k)
+    assert nb.nnue_nn_bin_bytes(got, 256, 32, 32) == blob
+    bad = bytearray(blob)
+    bad[4] ^= 1
+    with pytest.raises(bo.CudaCppError, match="network hash mismatch"):
+        nb.parse_nnue_nn_bin(bytes(bad), SHAPE[0])
+    with pytest.raises(bo.CudaCppError, match="truncated"):
+        nb.parse_nnue_nn_bin(blob[:-1], SHAPE[0])
+    with pytest.raises(bo.CudaCppError, match="trailing"):
+        nb.parse_nnue_nn_bin(blob + b"\0", SHAPE[0])
+
+
+def test_leb128_reader():
+    vals = np.random.default_rng(2).integers(-32768, 32768, 10000).astype(np.int16)
+    vals[:4] = [0, -1, 32767, -32768]
+    data = nb.signed_leb128_i16(vals)
+    got, used = nb.read_signed_leb128_i16(data + b"\x05", vals.size)
+    assert used == len(data)
+    np.testing.assert_array_equal(got, vals)
+    with pytest.raises(bo.CudaCppError, match="truncated"):
+        nb.read_signed_leb128_i16(data[:-1], vals.size)
+
+
+def test_sfnn_read_round_trip_and_checks():
+    sh = _sfnn_shape()
+    w = synthetic.sfnn_weights(synthetic.rng_for(8), sh.input_size, sh.ft_size, sh.l1_hidden, sh.l1_skip,
+                               sh.l2_size, sh.num_stacks, True, True, 0.05)
+    q = oracle.sfnn_quantize(sh.as_tuple(), w)
+    args = (sh.ft_size, sh.l1_out, sh.l2_size, sh.l2_in, sh.num_stacks)
+    blob = nb.sfnn_nn_bin_bytes(q, *args)
+    rows = sh.factorized_base()
+    got = nb.parse_sfnn_nn_bin(blob, rows, *args)
+    for k in q:
+        np.testing.assert_array_equal(got[k], np.asarray(q[k]).reshape(-1), err_msg=k)
+    assert nb.sfnn_nn_bin_bytes(got, *args) == blob
+    with pytest.raises(bo.CudaCppError, match="architecture mismatch"):
+        nb.parse_sfnn_nn_bin(blob, rows, 512, *args[1:])
+    with pytest.raises(bo.CudaCppError):
+        nb.parse_sfnn_nn_bin(blob[:-3], rows, *args)
+
+
+@pytest.mark.gpu
+def test_read_files_into_device_weights(ctx, tmp_path):
+    """A file written from the device quantisation loads back into fresh
+    device tensors unchanged (HalfKP and SFNN)."""
+    from bulletou_b200 import sfnn as bs
+
+    shape = (SHAPE[0] + 1548,) + SHAPE[1:]
+    w = synthetic.halfkp_weights(synthetic.rng_for(9), input_size=shape[0], std=0.05)
+    dq = bo.QuantizedNnueDeviceWeights(ctx, *shape)
+    bo.nnue_quantize_device(ctx, {n: bo.F32Buffer.from_host(ctx, w[n]) for n in oracle.NNUE_QUANT_NAMES}, dq)
+    nb.write_nnue_nn_bin(tmp_path / "a.bin", ctx, dq)
+    back = bo.QuantizedNnueDeviceWeights(ctx, *shape)
+    nb.read_nnue_nn_bin(tmp_path / "a.bin", ctx, back)
+    a, b = dq.download(ctx), back.download(ctx)
+    for k in oracle.NNUE_QUANT_NAMES:
+        np.testing.assert_array_equal(a[k], b[k], err_msg=k)
+    sh = _sfnn_shape()
+    sw = synthetic.sfnn_weights(synthetic.rng_for(10), sh.input_size, sh.ft_size, sh.l1_hidden, sh.l1_skip,
+                                sh.l2_size, sh.num_stacks, True, False, 0.05)
+    sq = bs.QuantizedSfnnDeviceWeights(ctx, sh)
+    bs.sfnn_quantize_device(ctx, sh, {n: (None if sw.get(n) is None else bo.F32Buffer.from_host(ctx, sw[n]))
+                                      for n in bs.SFNN_WEIGHT_NAMES}, sq)
+    nb.write_sfnn_nn_bin(tmp_path / "s.bin", ctx, sq)
+    sback = bs.QuantizedSfnnDeviceWeights(ctx, sh)
+    nb.read_sfnn_nn_bin(tmp_path / "s.bin", ctx, sback)
+    a, b = sq.download(ctx), sback.download(ctx)
+    for k in a:
+        np.testing.assert_array_equal(a[k], b[k], err_msg=k)
