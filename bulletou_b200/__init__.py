@@ -25,6 +25,7 @@ from .cuda_cpp import (  # noqa: F401
     nnue_forward_host,
     ranger_update_device,
     ranger_update_host,
+    ranger_update_stacked_dirty_device,
     scalar_loss_host,
 )
 
@@ -39,6 +40,9 @@ from .sfnn import (  # noqa: F401
     SfnnForwardShape,
     SfnnTrainStepHostBatch,
     SfnnTrainStepRunner,
+    sfnn_backward_device,
+    sfnn_backward_train_profile_device,
+    sfnn_build_quantized_proxy_device,
     sfnn_integer_forward_device,
     sfnn_quantize_device,
 )

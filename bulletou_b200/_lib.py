@@ -85,7 +85,7 @@ class LossSpec(ctypes.Structure):
 
 _BUF = P  # handle pointers are opaque
 # Entries returning void (no status code).
-VOID_RETURN = {"bulletou_dense_qat_end"}
+VOID_RETURN = {"bulletou_dense_qat_end", "bulletou_bn_reference_mode"}
 SIGNATURES: dict[str, list] = {
     # runtime
     "bulletou_cuda_cpp_last_error": [P, Z],
@@ -152,6 +152,7 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_f32_buffer_view": [P, Z, Z, P],
     "bulletou_b200_profile_begin": [P, Z],
     "bulletou_b200_profile_end": [P, P, Z, P, P],
+    "bulletou_b200_l2_read_probe": [P, P, Z, I, P],
     "bulletou_b200_nnue_forward_device_noalloc": [P, Z, Z, Z, Z, Z, Z] + [P] * 16,
     "bulletou_b200_nnue_train_step_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P],
     "bulletou_b200_nnue_dense_gradient_len": [Z, Z, Z, P],
@@ -182,6 +183,69 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_validation_metrics_device": [P, P, P, P, Z, P, P],
     "bulletou_cuda_cpp_sfnn_validation_stats": [P] * 7 + [Z] * 4,
     "bulletou_cuda_cpp_sfnn_unit_stats": [P] * 7 + [Z] * 5,
+    # the rest of the reference ABI (lib.rs mod ffi, batch_norm.rs, bn_qat.rs): implemented or
+    # "unsupported on this backend" (include/bulletou_cuda_cpp.h)
+    "bulletou_bind_ft_saturation_guard": [P] * 4 + [Z, Z, F, F, I],
+    "bulletou_bn_backward": [P] * 9 + [Z] * 4,
+    "bulletou_bn_bind": [P, I] + [P] * 6 + [Z] * 4 + [F, F, I],
+    "bulletou_bn_forward": [P] * 9 + [Z] * 4 + [F, F, I],
+    "bulletou_bn_qat_ft": [P, P, P, Z, Z, Z, F],
+    "bulletou_bn_qat_ft_training": [P] * 5 + [Z, Z, Z, F],
+    "bulletou_bn_qat_project_l2": [P, P, P, Z, Z],
+    "bulletou_bn_qat_pullback": [P] * 9 + [Z, Z, Z, I, Z, F],
+    "bulletou_bn_qat_unfold_training": [P] * 7 + [Z, Z, Z, I, Z, F],
+    "bulletou_bn_reference_mode": [I],
+    "bulletou_center_affine_layout": [P] * 8 + [Z, Z, I, I],
+    "bulletou_center_l1_groups": [P] * 14 + [Z, I],
+    "bulletou_center_mean_reference": [P, P, P, Z, Z],
+    "bulletou_center_scale": [P, P, P, Z, F],
+    "bulletou_clip_effective_l1": [P] * 6 + [Z, Z, F],
+    "bulletou_clip_effective_l1_axis": [P] * 8 + [Z] * 5 + [I] * 6 + [F] * 5,
+    "bulletou_cuda_cpp_context_release_sfnn_ft_fp16_scratch": [P, I, I, I],
+    "bulletou_cuda_cpp_context_set_sfnn_ft_fp16": [P, I],
+    "bulletou_cuda_cpp_context_set_sfnn_ft_fp16_act": [P, I],
+    "bulletou_cuda_cpp_context_set_sfnn_ft_fp16_grad": [P, I],
+    "bulletou_cuda_cpp_context_take_ft_half_grad_clipped": [P, P],
+    "bulletou_cuda_cpp_ft_half_moments_create": [P, P, P, Z, I, P],
+    "bulletou_cuda_cpp_ft_half_moments_decode": [P] * 4,
+    "bulletou_cuda_cpp_ft_half_moments_destroy": [P],
+    "bulletou_cuda_cpp_ft_half_moments_take_clipped": [P, P, P],
+    "bulletou_cuda_cpp_ranger_update_stacked_dirty_device": [P, F, I, Z, Z, Z, F, F, F, I] + [F] * 6 + [I, F, I] + [P] * 6,
+    "bulletou_cuda_cpp_rebase_shared_device": [P] * 10 + [Z] * 5 + [F, F],
+    "bulletou_cuda_cpp_scale_axis_rows_f32_device": [P, P, Z, P, Z, Z],
+    "bulletou_cuda_cpp_sfnn_add_residual_count_decay_gradients_device": [P] * 5 + [Z, Z, Z],
+    "bulletou_cuda_cpp_sfnn_add_saturation_penalty_gradients_device": [P, P, P, I, P, I] + [P] * 4 + [Z] * 6 + [I] * 6 + [F] * 6 + [P, P, I, F, F, F],
+    "bulletou_cuda_cpp_sfnn_apply_residual_count_gates_to_gradients_device": [P] * 4 + [Z, Z, Z],
+    "bulletou_cuda_cpp_sfnn_backward_device": [P, Z, Z, Z, I] + [Z] * 9 + [P] * 12 + [I, P, I, P, P, I, P, I, P, P, I, P] + [I] * 7 + [F] * 6 + [P] * 31,
+    "bulletou_cuda_cpp_sfnn_backward_train_profile_device": [P, Z, Z, Z, I] + [Z] * 9 + [P] * 12 + [I, P, I, P, P, I, P, I, P, P, I, P] + [I] * 7 + [F] * 6 + [P] * 31 + [I, P, Z],
+    "bulletou_cuda_cpp_sfnn_build_quantized_proxy_device": [P] + [Z] * 5 + [I] + [Z] * 7 + [P] * 6 + [I, P, P, I] + [P] * 4 + [I, P, P, I] + [P] * 4 + [I, P, P] + [I] * 7 + [F] * 6 + [P] * 10 + [I],
+    "bulletou_dense_qat_activation_reference": [P] * 7 + [Z],
+    "bulletou_dense_qat_integer_reference": [P] * 6 + [Z] * 4,
+    "bulletou_dense_qat_l1_backward_reference": [P] * 5 + [Z, Z, I],
+    "bulletou_experiment_bucket_centers": [P, P, P, Z, Z],
+    "bulletou_experiment_bucket_mean": [P] * 4 + [Z, Z, Z],
+    "bulletou_experiment_center_affine": [P] * 8 + [Z, Z, I],
+    "bulletou_experiment_center_affine_bucket": [P] * 8 + [Z, Z, Z, I],
+    "bulletou_experiment_column_mean": [P, P, P, Z, Z],
+    "bulletou_experiment_mean_penalty_test": [P] * 5 + [Z] * 4 + [F],
+    "bulletou_factor_axis_update_device": [P] + [Z] * 5 + [F] * 4 + [P] + [F] * 7 + [I, I, F, F, F, I, I, F, I] + [P] * 5,
+    "bulletou_ft_saturation_guard": [P] * 10 + [Z] * 4 + [F, F, F, I],
+    "bulletou_test_dense_l1_16": [P] * 6 + [Z, Z, Z, I],
+    "bulletou_test_dense_qat_exact_ft": [P] * 7 + [Z] * 4,
+    "bulletou_test_factorized_ft_half_fold": [P, P, P, Z, Z, F, I],
+    "bulletou_test_l1_bucket_fold": [P] * 8 + [I],
+    "bulletou_test_l1_gather2": [P] * 9 + [Z] * 4 + [F],
+    "bulletou_test_l1_gather2_king_progress": [P] * 12 + [Z] * 5 + [F] * 4,
+    "bulletou_test_l1_to_ft_f32_gradient": [P] * 7 + [Z, Z, Z, I],
+    "bulletou_test_l1_to_ft_half_gradient": [P] * 7 + [Z, Z, Z, I],
+    "bulletou_test_qat_ft_lattice": [P, P, Z, I],
+    "bulletou_test_qat_packed_l1": [P] * 7 + [Z] * 4 + [I],
+    "bulletou_test_sfnn_ft_fp16_scratch_sizes": [P] * 4,
+    "bulletou_test_sfnn_ft_gather": [P] * 5 + [Z, Z, I, I],
+    "bulletou_test_sfnn_ft_sort": [P] * 10 + [Z] * 4 + [I],
+    "bulletou_test_sfnn_half_grad": [P] * 7 + [Z, Z, I],
+    "bulletou_test_sfnn_half_grad_gather": [P] * 5 + [Z] * 4 + [I],
+    "bulletou_test_stream_delay": [P],
 }
 
 

@@ -209,6 +209,35 @@ __global__ void layer_qat_ft_kernel(const float* __restrict__ src, float* __rest
     dst[t] = qat_q127(fold_nf(src[t], alpha, src[(base + f % vr) * width + u]));
 }
 
+// Quantised-proxy FT rows (sfnn_build_quantized_proxy_l0w_kernel,
+// cu:1682-1705): row f < dst_rows folded with virtual row dst_rows + f % vr
+// when vr > 0 (two roundings), then rounded to 1/127 in i16 range.
+__global__ void proxy_ft_kernel(const float* __restrict__ src, float* __restrict__ dst, size_t dst_rows, size_t vr,
+                                size_t width, float alpha) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= dst_rows * width) return;
+    float v = src[t];
+    if (vr > 0) {
+        const size_t f = t / width;
+        v = fold_nf(v, alpha, src[(dst_rows + f % vr) * width + (t - f * width)]);
+    }
+    dst[t] = qat_q127(v);
+}
+
+// Quantised-proxy dense tensors laid out [stacks][cells] whose shared factor
+// has the same cell order (sfnn_build_quantized_proxy_stacked_weights_kernel /
+// _bias_kernel with an output-major factor, cu:1735-1830, 1921-1991): value
+// (+ alpha * shared[t % cells], two roundings) rounded to 1/64 in i8 range
+// (kind 1) or to 1/8128 in i32 range (kind 2).
+__global__ void proxy_stacked_kernel(const float* __restrict__ src, const float* __restrict__ shared, size_t cells,
+                                     size_t total, float alpha, int kind, float* __restrict__ dst) {
+    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= total) return;
+    float v = src[t];
+    if (shared != nullptr) v = fold_nf(v, alpha, shared[t % cells]);
+    dst[t] = kind == 1 ? qat_q64(v) : qat_q8128(v);
+}
+
 __global__ void nonzero_kernel(const float* __restrict__ w, size_t nw, const float* __restrict__ b, size_t nb,
                                float* __restrict__ flag) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -2575,7 +2604,50 @@ int bulletou_cuda_cpp_sfnn_forward_device(
     return ok();
 }
 
-int bulletou_cuda_cpp_sfnn_backward_train_device(
+}  // extern "C"
+
+namespace bou {
+namespace {
+
+// Stage events of the reference's backward profile (SfnnBackwardProfileEvents,
+// cu:5679-5750): zeroing, L3, L2, L2 input, L1, pairwise + FT, total.  The head
+// kernel does the L3 / L2 / L2-input backward at once: its time is reported as
+// L3, with L2 and L2 input 0.
+struct BackwardProfile {
+    float* out = nullptr;
+    cudaEvent_t ev[5] = {};
+    int n = 0;
+    ~BackwardProfile() {
+        for (cudaEvent_t e : ev)
+            if (e != nullptr) cudaEventDestroy(e);
+    }
+    int init(BulletOuCudaCppContext* ctx, float* ms, size_t len) {
+        if (ms == nullptr) return 0;
+        if (len < 7) return fail_message("SFNN backward profile output must have at least 7 floats");
+        out = ms;
+        for (int i = 0; i < 7; ++i) out[i] = 0.0f;
+        for (cudaEvent_t& e : ev) {
+            const cudaError_t st = cudaEventCreate(&e);
+            if (st != cudaSuccess) return fail("cudaEventCreate SFNN backward profile", st);
+        }
+        return mark(ctx);
+    }
+    int mark(BulletOuCudaCppContext* ctx) {
+        if (out == nullptr) return 0;
+        const cudaError_t st = cudaEventRecord(ev[n++], ctx->stream);
+        return st == cudaSuccess ? 0 : fail("cudaEventRecord SFNN backward profile", st);
+    }
+    int finish() {
+        if (out == nullptr) return 0;
+        cudaError_t st = cudaEventSynchronize(ev[4]);
+        if (st != cudaSuccess) return fail("cudaEventSynchronize SFNN backward profile", st);
+        const int from[5] = {0, 1, 2, 3, 0}, to[5] = {1, 2, 3, 4, 4}, slot[5] = {0, 1, 4, 5, 6};
+        for (int k = 0; k < 5 && st == cudaSuccess; ++k) st = cudaEventElapsedTime(&out[slot[k]], ev[from[k]], ev[to[k]]);
+        return st == cudaSuccess ? 0 : fail("cudaEventElapsedTime SFNN backward profile", st);
+    }
+};
+
+int sfnn_backward_impl(
     BulletOuCudaCppContext* ctx, size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip, size_t l2_size,
     size_t num_stacks, size_t l1_group_count, size_t l1_common_size, size_t l1_shard_size,
     size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim, size_t batch, size_t max_active,
@@ -2606,7 +2678,7 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     BulletOuCudaCppF32Buffer* l2axb_gradients, BulletOuCudaCppF32Buffer* l3w_gradients,
     BulletOuCudaCppF32Buffer* l3b_gradients, BulletOuCudaCppF32Buffer* l3fw_gradients,
     BulletOuCudaCppF32Buffer* l3fb_gradients, BulletOuCudaCppF32Buffer* l3axw_gradients,
-    BulletOuCudaCppF32Buffer* l3axb_gradients, int zero_parameter_gradients, BulletOuCudaCppF32Buffer* entry_weights) {
+    BulletOuCudaCppF32Buffer* l3axb_gradients, int zero_parameter_gradients, BulletOuCudaCppF32Buffer* entry_weights, float* profile_ms, size_t profile_ms_len) {
     (void)factorizer_king_axis_dim;
     (void)factorizer_hand_axis_dim;
     (void)factorizer_king_axis_alpha;
@@ -2686,12 +2758,15 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
         return fail_message("dense QAT requires the L1 QAT weights and unfactorized L2/L3");
     if (d.qat.dense && validate_f32(ctx, combined, BW, "sfnn combined") != 0) return -1;
     if (set_device(ctx) != 0) return -1;
+    BackwardProfile prof;
+    if (prof.init(ctx, profile_ms, profile_ms_len) != 0) return -1;
     if (zero_parameter_gradients) {
         cudaError_t st = cudaMemsetAsync(l0w_gradients->ptr, 0, l0w_gradients->len * sizeof(float), ctx->stream);
         for (int k = 0; k < kSfGroups && st == cudaSuccess; ++k)
             if (g.len[k]) st = cudaMemsetAsync(grads[k]->ptr, 0, g.len[k] * sizeof(float), ctx->stream);
         if (st != cudaSuccess) return fail("cudaMemsetAsync SFNN gradients", st);
     }
+    if (prof.mark(ctx) != 0) return -1;
     // The backward reads only the L1 / L2 / L3 weights (and their shared
     // factors); the FT table is not needed, so nothing is folded.
     // With L1 QAT the input gradient uses the folded, fake-quantised weights
@@ -2714,7 +2789,7 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     h.l2_gradients = l2_gradients->ptr;
     h.l2_input_gradients = l2_input_gradients->ptr;
     plan.g1 = l1_gradients->ptr;
-    if (launch_head(ctx, d, h) != 0) return -1;
+    if (launch_head(ctx, d, h) != 0 || prof.mark(ctx) != 0) return -1;
     L1BackArgs lb{};
     lb.l0[0] = stm_l0->ptr;
     lb.l0[1] = nstm_l0->ptr;
@@ -2728,7 +2803,7 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     FinalArgs f{};
     for (int k = 0; k < kSfGroups; ++k) f.dst[k] = g.len[k] ? grads[k]->ptr : nullptr;
     f.accumulate = 1;
-    if (launch_finalize(ctx, d, plan, f) != 0) return -1;
+    if (launch_finalize(ctx, d, plan, f) != 0 || prof.mark(ctx) != 0) return -1;
     InverseIndex index;
     if (build_inverse_index_rows(ctx, stm_indices->ptr, nstm_indices->ptr, d.batch, d.max_active, d.n_features, &index,
                                  nullptr) != 0 ||
@@ -2739,8 +2814,195 @@ int bulletou_cuda_cpp_sfnn_backward_train_device(
     r.src[1] = nstm_l0_pre_gradients->ptr;
     r.src_stride = ft_size;
     r.gradients = l0w_gradients->ptr;
-    if (launch_piece_rows(ctx, kRowAccumulate, r) != 0) return -1;
+    if (launch_piece_rows(ctx, kRowAccumulate, r) != 0 || prof.mark(ctx) != 0 || prof.finish() != 0) return -1;
     return ok();
+}
+
+}  // namespace
+}  // namespace bou
+
+extern "C" {
+
+#define BOU_SFNN_BACKWARD_PARAMS                                                                                       \
+    BulletOuCudaCppContext *ctx, size_t input_size, size_t ft_size, size_t l1_hidden, int l1_skip, size_t l2_size,     \
+        size_t num_stacks, size_t l1_group_count, size_t l1_common_size, size_t l1_shard_size,                         \
+        size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim, size_t batch, size_t max_active,             \
+        const BulletOuCudaCppI32Buffer *stm_indices, const BulletOuCudaCppI32Buffer *nstm_indices,                     \
+        const BulletOuCudaCppI32Buffer *buckets, const BulletOuCudaCppF32Buffer *stm_l0,                               \
+        const BulletOuCudaCppF32Buffer *nstm_l0, const BulletOuCudaCppF32Buffer *combined,                             \
+        const BulletOuCudaCppF32Buffer *l1, const BulletOuCudaCppF32Buffer *l2_input,                                  \
+        const BulletOuCudaCppF32Buffer *l2, const BulletOuCudaCppF32Buffer *l1w,                                       \
+        const BulletOuCudaCppF32Buffer *qat_l1w, const BulletOuCudaCppF32Buffer *l1fw, int has_l1f,                    \
+        const BulletOuCudaCppF32Buffer *l1axw, int has_l1ax, const BulletOuCudaCppF32Buffer *l2w,                      \
+        const BulletOuCudaCppF32Buffer *l2fw, int has_l2f, const BulletOuCudaCppF32Buffer *l2axw, int has_l2ax,        \
+        const BulletOuCudaCppF32Buffer *l3w, const BulletOuCudaCppF32Buffer *l3fw, int has_l3f,                        \
+        const BulletOuCudaCppF32Buffer *l3axw, int has_l3ax, int use_king_axis, int use_hand_axis,                     \
+        int use_progress_axis, int use_king_hand_pair, int use_king_progress_pair, int use_hand_progress_pair,         \
+        float ft_factorizer_alpha, float factorizer_shared_alpha, float factorizer_king_axis_alpha,                    \
+        float factorizer_hand_axis_alpha, float factorizer_progress_axis_alpha, float factorizer_pair_alpha,           \
+        const BulletOuCudaCppF32Buffer *residual_count_gates,                                                          \
+        const BulletOuCudaCppF32Buffer *factorizer_axis_confidences,                                                   \
+        const BulletOuCudaCppF32Buffer *mean_output_gradients, BulletOuCudaCppF32Buffer *l2_gradients,                 \
+        BulletOuCudaCppF32Buffer *l1_gradients, BulletOuCudaCppF32Buffer *l2_input_gradients,                          \
+        BulletOuCudaCppF32Buffer *combined_gradients, BulletOuCudaCppF32Buffer *stm_l0_gradients,                      \
+        BulletOuCudaCppF32Buffer *nstm_l0_gradients, BulletOuCudaCppF32Buffer *stm_l0_pre_gradients,                   \
+        BulletOuCudaCppF32Buffer *nstm_l0_pre_gradients, BulletOuCudaCppF32Buffer *l0w_gradients,                      \
+        BulletOuCudaCppF32Buffer *l0b_gradients, BulletOuCudaCppF32Buffer *l1w_gradients,                              \
+        BulletOuCudaCppF32Buffer *l1b_gradients, BulletOuCudaCppF32Buffer *l1fw_gradients,                             \
+        BulletOuCudaCppF32Buffer *l1fb_gradients, BulletOuCudaCppF32Buffer *l1axw_gradients,                           \
+        BulletOuCudaCppF32Buffer *l1axb_gradients, BulletOuCudaCppF32Buffer *l2w_gradients,                            \
+        BulletOuCudaCppF32Buffer *l2b_gradients, BulletOuCudaCppF32Buffer *l2fw_gradients,                             \
+        BulletOuCudaCppF32Buffer *l2fb_gradients, BulletOuCudaCppF32Buffer *l2axw_gradients,                           \
+        BulletOuCudaCppF32Buffer *l2axb_gradients, BulletOuCudaCppF32Buffer *l3w_gradients,                            \
+        BulletOuCudaCppF32Buffer *l3b_gradients, BulletOuCudaCppF32Buffer *l3fw_gradients,                             \
+        BulletOuCudaCppF32Buffer *l3fb_gradients, BulletOuCudaCppF32Buffer *l3axw_gradients,                           \
+        BulletOuCudaCppF32Buffer *l3axb_gradients
+#define BOU_SFNN_BACKWARD_ARGS                                                                                         \
+    ctx, input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks, l1_group_count, l1_common_size, l1_shard_size, \
+        factorizer_king_axis_dim, factorizer_hand_axis_dim, batch, max_active, stm_indices, nstm_indices, buckets,     \
+        stm_l0, nstm_l0, combined, l1, l2_input, l2, l1w, qat_l1w, l1fw, has_l1f, l1axw, has_l1ax, l2w, l2fw, has_l2f, \
+        l2axw, has_l2ax, l3w, l3fw, has_l3f, l3axw, has_l3ax, use_king_axis, use_hand_axis, use_progress_axis,         \
+        use_king_hand_pair, use_king_progress_pair, use_hand_progress_pair, ft_factorizer_alpha,                       \
+        factorizer_shared_alpha, factorizer_king_axis_alpha, factorizer_hand_axis_alpha,                               \
+        factorizer_progress_axis_alpha, factorizer_pair_alpha, residual_count_gates, factorizer_axis_confidences,      \
+        mean_output_gradients, l2_gradients, l1_gradients, l2_input_gradients, combined_gradients, stm_l0_gradients,   \
+        nstm_l0_gradients, stm_l0_pre_gradients, nstm_l0_pre_gradients, l0w_gradients, l0b_gradients, l1w_gradients,  \
+        l1b_gradients, l1fw_gradients, l1fb_gradients, l1axw_gradients, l1axb_gradients, l2w_gradients, l2b_gradients, \
+        l2fw_gradients, l2fb_gradients, l2axw_gradients, l2axb_gradients, l3w_gradients, l3b_gradients, l3fw_gradients,\
+        l3fb_gradients, l3axw_gradients, l3axb_gradients
+
+// cu:12882 -- the training backward.
+int bulletou_cuda_cpp_sfnn_backward_train_device(BOU_SFNN_BACKWARD_PARAMS, int zero_parameter_gradients,
+                                                 BulletOuCudaCppF32Buffer* entry_weights) {
+    return sfnn_backward_impl(BOU_SFNN_BACKWARD_ARGS, zero_parameter_gradients, entry_weights, nullptr, 0);
+}
+
+// cu:12274 -- the same with every parameter gradient cleared first.
+int bulletou_cuda_cpp_sfnn_backward_device(BOU_SFNN_BACKWARD_PARAMS) {
+    return sfnn_backward_impl(BOU_SFNN_BACKWARD_ARGS, 1, nullptr, nullptr, 0);
+}
+
+// cu:13080 -- the training backward with the stage times in profile_ms[0..7).
+int bulletou_cuda_cpp_sfnn_backward_train_profile_device(BOU_SFNN_BACKWARD_PARAMS, int zero_parameter_gradients,
+                                                         float* profile_ms, size_t profile_ms_len) {
+    return sfnn_backward_impl(BOU_SFNN_BACKWARD_ARGS, zero_parameter_gradients, nullptr, profile_ms, profile_ms_len);
+}
+#undef BOU_SFNN_BACKWARD_PARAMS
+#undef BOU_SFNN_BACKWARD_ARGS
+
+// cu:10937 -- the engine-lattice proxy of the f32 masters (see the header).
+int bulletou_cuda_cpp_sfnn_build_quantized_proxy_device(
+    BulletOuCudaCppContext* ctx, size_t src_input_size, size_t dst_input_size, size_t virtual_rows, size_t ft_size,
+    size_t l1_hidden, int l1_skip, size_t l2_size, size_t num_stacks, size_t l1_group_count, size_t l1_common_size,
+    size_t l1_shard_size, size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim,
+    const BulletOuCudaCppF32Buffer* src_l0w, const BulletOuCudaCppF32Buffer* src_l0b,
+    const BulletOuCudaCppF32Buffer* src_l1w, const BulletOuCudaCppF32Buffer* src_l1b,
+    const BulletOuCudaCppF32Buffer* src_l1fw, const BulletOuCudaCppF32Buffer* src_l1fb, int has_l1f,
+    const BulletOuCudaCppF32Buffer* src_l1axw, const BulletOuCudaCppF32Buffer* src_l1axb, int has_l1ax,
+    const BulletOuCudaCppF32Buffer* src_l2w, const BulletOuCudaCppF32Buffer* src_l2b,
+    const BulletOuCudaCppF32Buffer* src_l2fw, const BulletOuCudaCppF32Buffer* src_l2fb, int has_l2f,
+    const BulletOuCudaCppF32Buffer* src_l2axw, const BulletOuCudaCppF32Buffer* src_l2axb, int has_l2ax,
+    const BulletOuCudaCppF32Buffer* src_l3w, const BulletOuCudaCppF32Buffer* src_l3b,
+    const BulletOuCudaCppF32Buffer* src_l3fw, const BulletOuCudaCppF32Buffer* src_l3fb, int has_l3f,
+    const BulletOuCudaCppF32Buffer* src_l3axw, const BulletOuCudaCppF32Buffer* src_l3axb, int has_l3ax,
+    int use_king_axis, int use_hand_axis, int use_progress_axis, int use_king_hand_pair, int use_king_progress_pair,
+    int use_hand_progress_pair, float ft_factorizer_alpha, float factorizer_shared_alpha,
+    float factorizer_king_axis_alpha, float factorizer_hand_axis_alpha, float factorizer_progress_axis_alpha,
+    float factorizer_pair_alpha, const BulletOuCudaCppF32Buffer* residual_count_gates,
+    const BulletOuCudaCppF32Buffer* factorizer_axis_confidences, BulletOuCudaCppF32Buffer* dst_l0w,
+    BulletOuCudaCppF32Buffer* dst_l0b, BulletOuCudaCppF32Buffer* dst_l1w, BulletOuCudaCppF32Buffer* dst_l1b,
+    BulletOuCudaCppF32Buffer* dst_l2w, BulletOuCudaCppF32Buffer* dst_l2b, BulletOuCudaCppF32Buffer* dst_l3w,
+    BulletOuCudaCppF32Buffer* dst_l3b, int skip_ft_weights) {
+    (void)factorizer_king_axis_dim;
+    (void)factorizer_hand_axis_dim;
+    (void)factorizer_king_axis_alpha;
+    (void)factorizer_hand_axis_alpha;
+    (void)factorizer_progress_axis_alpha;
+    (void)factorizer_pair_alpha;
+    (void)src_l1axw;
+    (void)src_l1axb;
+    (void)src_l2axw;
+    (void)src_l2axb;
+    (void)src_l3axw;
+    (void)src_l3axb;
+    if (set_device(ctx) != 0) return -1;
+    if (src_input_size == 0 || dst_input_size == 0 || ft_size == 0 || l2_size == 0 || num_stacks == 0)
+        return fail_message("sfnn quantized GPU proxy dimensions must be non-zero");
+    if (!(src_input_size == dst_input_size || (virtual_rows != 0 && src_input_size == dst_input_size + virtual_rows)))
+        return fail_message("sfnn quantized GPU proxy input sizes do not match base/factorized layout");
+    if (reject_unsupported(l1_group_count, l1_common_size, l1_shard_size, has_l1ax, has_l2ax, has_l3ax, use_king_axis,
+                           use_hand_axis, use_progress_axis, use_king_hand_pair, use_king_progress_pair,
+                           use_hand_progress_pair, residual_count_gates, factorizer_axis_confidences) != 0)
+        return -1;
+    SfnnDims d{};
+    if (sfnn_dims(src_input_size, ft_size, l1_hidden, l1_skip, l2_size, num_stacks, 1, 1, ft_factorizer_alpha,
+                  factorizer_shared_alpha, &d) != 0)
+        return -1;
+    const size_t O = d.l1_out, I2 = d.l2_in, S = num_stacks;
+    const size_t vr = src_input_size == dst_input_size ? 0 : virtual_rows;
+    if (validate_f32(ctx, src_l0w, src_input_size * ft_size, "sfnn proxy src l0w") != 0 ||
+        validate_f32(ctx, src_l0b, ft_size, "sfnn proxy src l0b") != 0 ||
+        validate_f32(ctx, src_l1w, S * O * ft_size, "sfnn proxy src l1w") != 0 ||
+        validate_f32(ctx, src_l1b, S * O, "sfnn proxy src l1b") != 0 ||
+        validate_f32(ctx, src_l2w, S * l2_size * I2, "sfnn proxy src l2w") != 0 ||
+        validate_f32(ctx, src_l2b, S * l2_size, "sfnn proxy src l2b") != 0 ||
+        validate_f32(ctx, src_l3w, S * l2_size, "sfnn proxy src l3w") != 0 ||
+        validate_f32(ctx, src_l3b, S, "sfnn proxy src l3b") != 0 ||
+        validate_f32(ctx, dst_l0w, dst_input_size * ft_size, "sfnn proxy dst l0w") != 0 ||
+        validate_f32(ctx, dst_l0b, ft_size, "sfnn proxy dst l0b") != 0 ||
+        validate_f32(ctx, dst_l1w, S * O * ft_size, "sfnn proxy dst l1w") != 0 ||
+        validate_f32(ctx, dst_l1b, S * O, "sfnn proxy dst l1b") != 0 ||
+        validate_f32(ctx, dst_l2w, S * l2_size * I2, "sfnn proxy dst l2w") != 0 ||
+        validate_f32(ctx, dst_l2b, S * l2_size, "sfnn proxy dst l2b") != 0 ||
+        validate_f32(ctx, dst_l3w, S * l2_size, "sfnn proxy dst l3w") != 0 ||
+        validate_f32(ctx, dst_l3b, S, "sfnn proxy dst l3b") != 0)
+        return -1;
+    if (has_l1f && (validate_f32(ctx, src_l1fw, ft_size * O, "sfnn proxy src l1fw") != 0 ||
+                    validate_f32(ctx, src_l1fb, O, "sfnn proxy src l1fb") != 0))
+        return -1;
+    if (has_l2f && (validate_f32(ctx, src_l2fw, l2_size * I2, "sfnn proxy src l2fw") != 0 ||
+                    validate_f32(ctx, src_l2fb, l2_size, "sfnn proxy src l2fb") != 0))
+        return -1;
+    if (has_l3f && (validate_f32(ctx, src_l3fw, l2_size, "sfnn proxy src l3fw") != 0 ||
+                    validate_f32(ctx, src_l3fb, 1, "sfnn proxy src l3fb") != 0))
+        return -1;
+    const int threads = 256;
+    int blocks = 0;
+    const float alpha = factorizer_shared_alpha;
+    if (!skip_ft_weights) {
+        if (grid_1d(dst_input_size * ft_size, threads, &blocks, "sfnn proxy l0w") != 0) return -1;
+        proxy_ft_kernel<<<blocks, threads, 0, ctx->stream>>>(src_l0w->ptr, dst_l0w->ptr, dst_input_size, vr, ft_size,
+                                                             ft_factorizer_alpha);
+    }
+    qat_vector_kernel<<<(ft_size + threads - 1) / threads, threads, 0, ctx->stream>>>(src_l0b->ptr, dst_l0b->ptr,
+                                                                                      ft_size, 0);
+    // L1: input-major shared factor [W][O] (cu:11153 passes shared_weight_input_major = 1)
+    if (grid_1d(S * O * ft_size, threads, &blocks, "sfnn proxy l1w") != 0) return -1;
+    qat_l1_fold_kernel<<<blocks, threads, 0, ctx->stream>>>(src_l1w->ptr, has_l1f ? src_l1fw->ptr : nullptr, alpha,
+                                                            S * O * ft_size, static_cast<int>(O),
+                                                            static_cast<int>(ft_size), 1, dst_l1w->ptr);
+    qat_l1_bias_kernel<<<(S * O + threads - 1) / threads, threads, 0, ctx->stream>>>(
+        src_l1b->ptr, has_l1f ? src_l1fb->ptr : nullptr, alpha, static_cast<int>(S * O), static_cast<int>(O), 1,
+        dst_l1b->ptr, nullptr, nullptr);
+    struct Part {
+        const float* src;
+        const float* shared;
+        size_t cells;
+        size_t total;
+        int kind;
+        float* dst;
+    } parts[4] = {
+        {src_l2w->ptr, has_l2f ? src_l2fw->ptr : nullptr, l2_size * I2, S * l2_size * I2, 1, dst_l2w->ptr},
+        {src_l2b->ptr, has_l2f ? src_l2fb->ptr : nullptr, l2_size, S * l2_size, 2, dst_l2b->ptr},
+        {src_l3w->ptr, has_l3f ? src_l3fw->ptr : nullptr, l2_size, S * l2_size, 1, dst_l3w->ptr},
+        {src_l3b->ptr, has_l3f ? src_l3fb->ptr : nullptr, 1, S, 2, dst_l3b->ptr},
+    };
+    for (const Part& q : parts) {
+        if (grid_1d(q.total, threads, &blocks, "sfnn proxy dense") != 0) return -1;
+        proxy_stacked_kernel<<<blocks, threads, 0, ctx->stream>>>(q.src, q.shared, q.cells, q.total, alpha, q.kind,
+                                                                  q.dst);
+    }
+    return check_launch("sfnn quantized proxy launch");
 }
 
 int bulletou_b200_sfnn_dense_gradient_len(const BulletOuB200SfnnShape* shape, int has_l1f, int has_l2f, int has_l3f,

@@ -23,7 +23,7 @@ import numpy as np
 from ._lib import CudaCppError, QuantRounding, SfnnQat, SfnnShape
 from .cuda_cpp import (FLT_MAX, Context, Event, F32Buffer, I32Buffer, PinnedF32Buffer, PinnedI32Buffer,
                        RangerDeviceState, RangerParamState, RangerUpdateParams, ScalarLossKind, ScalarLossReadback,
-                       ScalarLossWorkspace, ranger_update_device, scalar_loss_device)
+                       ScalarLossWorkspace, ranger_update_device, scalar_loss_device, upload_from_pinned)
 
 HALFKA_HM2_DIMENSIONS = 73305
 HALFKA2_DIMENSIONS = 131949
@@ -227,19 +227,12 @@ def sfnn_forward_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, 
         None if qat_l1 is None else qat_l1.bias.as_ptr(), 0 if qat_l1 is None else int(refresh_qat_l1))
 
 
-def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int,
-                               stm: I32Buffer, nstm: I32Buffer, buckets: I32Buffer, weights: dict,
-                               fws: SfnnForwardWorkspace, mean_output_gradients: F32Buffer,
-                               bws: SfnnBackwardWorkspace, alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
-                               zero_parameter_gradients: bool = False,
-                               entry_weights: Optional[F32Buffer] = None,
-                               qat_l1_weights: Optional[F32Buffer] = None) -> None:
-    """bulletou_cuda_cpp_sfnn_backward_train_device (lib.rs:3529-4090 argument order);
-    qat_l1_weights: the forward's L1 QAT weights (input gradients use them)."""
+def _backward_args(ctx, shape, batch_size, max_active, stm, nstm, buckets, weights, fws, mean_output_gradients, bws,
+                   alpha, qat_l1_weights):
     w, g, ax = weights, bws.params, bws.axis
     has = [int(w[n] is not None) for n in ("l1fw", "l2fw", "l3fw")]
-    ctx.lib.call(
-        "bulletou_cuda_cpp_sfnn_backward_train_device", ctx.as_ptr(), shape.input_size, shape.ft_size,
+    return [
+        ctx.as_ptr(), shape.input_size, shape.ft_size,
         shape.l1_hidden, int(shape.l1_skip), shape.l2_size, shape.num_stacks, 1, 0, 0, 0, 0, batch_size, max_active,
         stm.as_ptr(), nstm.as_ptr(), buckets.as_ptr(), fws.stm_l0.as_ptr(), fws.nstm_l0.as_ptr(),
         fws.combined.as_ptr(), fws.l1.as_ptr(), fws.l2_input.as_ptr(), fws.l2.as_ptr(), _p(w["l1w"]),
@@ -249,8 +242,79 @@ def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size
         mean_output_gradients.as_ptr(), *[getattr(bws, k).as_ptr() for k in bws.INTERMEDIATE], _p(g["l0w"]),
         _p(g["l0b"]), _p(g["l1w"]), _p(g["l1b"]), _p(g["l1fw"]), _p(g["l1fb"]), _p(ax["l1axw"]), _p(ax["l1axb"]),
         _p(g["l2w"]), _p(g["l2b"]), _p(g["l2fw"]), _p(g["l2fb"]), _p(ax["l2axw"]), _p(ax["l2axb"]), _p(g["l3w"]),
-        _p(g["l3b"]), _p(g["l3fw"]), _p(g["l3fb"]), _p(ax["l3axw"]), _p(ax["l3axb"]), int(zero_parameter_gradients),
-        _p(entry_weights))
+        _p(g["l3b"]), _p(g["l3fw"]), _p(g["l3fb"]), _p(ax["l3axw"]), _p(ax["l3axb"])]
+
+
+def sfnn_backward_train_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int,
+                               stm: I32Buffer, nstm: I32Buffer, buckets: I32Buffer, weights: dict,
+                               fws: SfnnForwardWorkspace, mean_output_gradients: F32Buffer,
+                               bws: SfnnBackwardWorkspace, alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
+                               zero_parameter_gradients: bool = False,
+                               entry_weights: Optional[F32Buffer] = None,
+                               qat_l1_weights: Optional[F32Buffer] = None) -> None:
+    """bulletou_cuda_cpp_sfnn_backward_train_device (lib.rs:3529-4090 argument order);
+    qat_l1_weights: the forward's L1 QAT weights (input gradients use them)."""
+    args = _backward_args(ctx, shape, batch_size, max_active, stm, nstm, buckets, weights, fws,
+                          mean_output_gradients, bws, alpha, qat_l1_weights)
+    ctx.lib.call("bulletou_cuda_cpp_sfnn_backward_train_device", *args, int(zero_parameter_gradients),
+                 _p(entry_weights))
+
+
+def sfnn_backward_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int, stm: I32Buffer,
+                         nstm: I32Buffer, buckets: I32Buffer, weights: dict, fws: SfnnForwardWorkspace,
+                         mean_output_gradients: F32Buffer, bws: SfnnBackwardWorkspace,
+                         alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
+                         qat_l1_weights: Optional[F32Buffer] = None) -> None:
+    """bulletou_cuda_cpp_sfnn_backward_device (lib.rs:4002): the backward with
+    every parameter gradient cleared first."""
+    ctx.lib.call("bulletou_cuda_cpp_sfnn_backward_device",
+                 *_backward_args(ctx, shape, batch_size, max_active, stm, nstm, buckets, weights, fws,
+                                 mean_output_gradients, bws, alpha, qat_l1_weights))
+
+
+SFNN_BACKWARD_PROFILE_STAGES = ("zero", "l3", "l2", "l2_input", "l1", "l0", "total")
+
+
+def sfnn_backward_train_profile_device(ctx: Context, shape: SfnnForwardShape, batch_size: int, max_active: int,
+                                       stm: I32Buffer, nstm: I32Buffer, buckets: I32Buffer, weights: dict,
+                                       fws: SfnnForwardWorkspace, mean_output_gradients: F32Buffer,
+                                       bws: SfnnBackwardWorkspace,
+                                       alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
+                                       zero_parameter_gradients: bool = False,
+                                       qat_l1_weights: Optional[F32Buffer] = None) -> dict:
+    """bulletou_cuda_cpp_sfnn_backward_train_profile_device (lib.rs:3719): the
+    training backward and its stage times in ms (SFNN_BACKWARD_PROFILE_STAGES;
+    blocks until the backward is done)."""
+    import ctypes
+
+    ms = (ctypes.c_float * 7)()
+    ctx.lib.call("bulletou_cuda_cpp_sfnn_backward_train_profile_device",
+                 *_backward_args(ctx, shape, batch_size, max_active, stm, nstm, buckets, weights, fws,
+                                 mean_output_gradients, bws, alpha, qat_l1_weights),
+                 int(zero_parameter_gradients), ms, 7)
+    return dict(zip(SFNN_BACKWARD_PROFILE_STAGES, list(ms)))
+
+
+def sfnn_build_quantized_proxy_device(ctx: Context, shape: SfnnForwardShape, weights: dict, dst: dict,
+                                      alpha: SfnnFactorizerAlpha = SfnnFactorizerAlpha(),
+                                      skip_ft_weights: bool = False) -> None:
+    """bulletou_cuda_cpp_sfnn_build_quantized_proxy_device (lib.rs:2378, 6520):
+    the engine-lattice proxy of the f32 masters `weights` into `dst` (keys
+    l0w l0b l1w l1b l2w l2b l3w l3b; dst l0w has the base rows only when the
+    FT is factorized)."""
+    w = weights
+    base = shape.factorized_base()
+    vr = shape.input_size - base if base else 0
+    dst_rows = base if base else shape.input_size
+    has = [int(w[n] is not None) for n in ("l1fw", "l2fw", "l3fw")]
+    ctx.lib.call(
+        "bulletou_cuda_cpp_sfnn_build_quantized_proxy_device", ctx.as_ptr(), shape.input_size, dst_rows, vr,
+        shape.ft_size, shape.l1_hidden, int(shape.l1_skip), shape.l2_size, shape.num_stacks, 1, 0, 0, 0, 0,
+        _p(w["l0w"]), _p(w["l0b"]), _p(w["l1w"]), _p(w["l1b"]), _p(w["l1fw"]), _p(w["l1fb"]), has[0], None, None, 0,
+        _p(w["l2w"]), _p(w["l2b"]), _p(w["l2fw"]), _p(w["l2fb"]), has[1], None, None, 0,
+        _p(w["l3w"]), _p(w["l3b"]), _p(w["l3fw"]), _p(w["l3fb"]), has[2], None, None, 0,
+        0, 0, 0, 0, 0, 0, alpha.ft, alpha.shared, 1.0, 1.0, 1.0, 1.0, None, None,
+        *[_p(dst[k]) for k in ("l0w", "l0b", "l1w", "l1b", "l2w", "l2b", "l3w", "l3b")], int(skip_ft_weights))
 
 
 @dataclass(frozen=True)
@@ -365,7 +429,7 @@ class SfnnTrainStepUploadSlot:
         if self.in_use:
             self.upload_ready.synchronize()
             self.compute_done.wait(upload_ctx)
-        if not lib.has("bulletou_b200_i32_upload_pinned"):
+        if pinned_source is None and not lib.has("bulletou_b200_i32_upload_pinned"):
             if batch is None:
                 raise CudaCppError("this backend needs host batch arrays for staged uploads")
             srcs = (batch.stm_indices, batch.nstm_indices, batch.buckets, batch.targets, batch.entry_weights)
@@ -377,13 +441,11 @@ class SfnnTrainStepUploadSlot:
         src = pinned_source.pinned if pinned_source is not None else self.pinned
         if pinned_source is None:
             self.fill(batch)
-        c = upload_ctx.as_ptr()
         for pin, dst in zip(src, self.device):
-            name = "bulletou_b200_i32_upload_pinned" if isinstance(dst, I32Buffer) else "bulletou_b200_f32_upload_pinned"
-            lib.call(name, c, dst.as_ptr(), pin.as_ptr(), pin.length)
+            upload_from_pinned(upload_ctx, dst, pin)
         self.upload_ready.record(upload_ctx)
         self.in_use = True
-        return 4 * sum(x.length for x in src)
+        return sum(int(x.nbytes) if isinstance(x, np.ndarray) else 4 * x.length for x in src)
 
 
 class SfnnTrainStepRunner:

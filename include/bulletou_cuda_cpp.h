@@ -318,6 +318,355 @@ int bulletou_cuda_cpp_sfnn_unit_stats(BulletOuCudaCppContext* ctx, BulletOuCudaC
     BulletOuCudaCppI32Buffer* buckets, BulletOuCudaCppI32Buffer* counts, size_t batch, size_t ft, size_t hidden,
     size_t width, size_t stacks);
 
+/* ---- FP16 feature-transformer options (cu:9598-9665) ----
+ * This backend keeps the FT weights, gradients and activations in f32.
+ * Turning an option off (enabled = 0) succeeds; turning one on returns -1
+ * with "unsupported on this backend".  There is no FP16 scratch, so the
+ * release entry only checks its context and the clipped-gradient counter
+ * always reads 0. */
+int bulletou_cuda_cpp_context_set_sfnn_ft_fp16(BulletOuCudaCppContext* ctx, int enabled);  /* cu:9624 */
+int bulletou_cuda_cpp_context_set_sfnn_ft_fp16_grad(BulletOuCudaCppContext* ctx, int enabled);  /* cu:9604 */
+int bulletou_cuda_cpp_context_set_sfnn_ft_fp16_act(BulletOuCudaCppContext* ctx, int enabled);  /* cu:9598 */
+int bulletou_cuda_cpp_context_release_sfnn_ft_fp16_scratch(BulletOuCudaCppContext* ctx, int release_weights,
+    int release_gradients, int release_activations);  /* cu:9633 */
+int bulletou_cuda_cpp_context_take_ft_half_grad_clipped(BulletOuCudaCppContext* ctx, unsigned long long* out);  /* cu:9610 */
+int bulletou_test_sfnn_ft_fp16_scratch_sizes(BulletOuCudaCppContext* ctx, size_t* weights, size_t* gradients,
+    size_t* activations);  /* cu:9658 */
+
+/* ---- FP16 optimizer moments (cu:10366-10420) ----
+ * Not supported: create returns -1 with "unsupported on this backend" and
+ * leaves *out NULL; decode / take_clipped on a NULL state fail; destroy(NULL)
+ * is a no-op returning 0. */
+int bulletou_cuda_cpp_ft_half_moments_create(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* momentum,
+    BulletOuCudaCppF32Buffer* velocity, size_t len, int sgd, BulletOuCudaCppHalfMoments** out);  /* cu:10366 */
+int bulletou_cuda_cpp_ft_half_moments_decode(BulletOuCudaCppContext* ctx, BulletOuCudaCppHalfMoments* state,
+    BulletOuCudaCppF32Buffer* momentum, BulletOuCudaCppF32Buffer* velocity);  /* cu:10396 */
+int bulletou_cuda_cpp_ft_half_moments_take_clipped(BulletOuCudaCppContext* ctx,
+    BulletOuCudaCppHalfMoments* state, unsigned long long* out);  /* cu:10407 */
+int bulletou_cuda_cpp_ft_half_moments_destroy(BulletOuCudaCppHalfMoments* state);  /* cu:10420 */
+
+/* ---- per-bucket ("dirty") Ranger over a stacked parameter group (cu:10700) ----
+ * The group is [stacks][stride]; only the strides of the buckets listed in
+ * dirty_buckets (negative ids and rows past len skipped) are stepped and
+ * their gradients reset.  learning_rate == 0 only clears those gradients.
+ * Norm loss applies to the whole group, before or after the step as
+ * norm_loss_before says; the lookahead follows the step. */
+int bulletou_cuda_cpp_ranger_update_stacked_dirty_device(BulletOuCudaCppContext* ctx, float norm_loss_rate,
+    int norm_loss_before, size_t len, size_t stride, size_t dirty_count, float gradient_factor,
+    float learning_rate, float step_size, int use_denom, float decay, float beta1, float beta2,
+    float epsilon, float min_weight, float max_weight, int do_lookahead, float lookahead_alpha,
+    int clip_after_lookahead, const BulletOuCudaCppI32Buffer* dirty_buckets,
+    BulletOuCudaCppF32Buffer* gradients, BulletOuCudaCppF32Buffer* weights,
+    BulletOuCudaCppF32Buffer* momentum, BulletOuCudaCppF32Buffer* velocity,
+    BulletOuCudaCppF32Buffer* slow_params);  /* cu:10700 */
+
+/* ---- SFNN backward variants and the quantised proxy ----
+ * sfnn_backward_device (cu:12274): the training backward with every parameter
+ * gradient cleared first.  sfnn_backward_train_profile_device (cu:13080): the
+ * training backward with stage times written to profile_ms[0..7): zeroing,
+ * L3, L2, L2 input, L1, pairwise + FT, total (ms).  Here the L3 / L2 / L2-input
+ * backward is one kernel, so its time is reported under L3 and the L2 and
+ * L2-input entries read 0.  profile_ms may be NULL; otherwise
+ * profile_ms_len >= 7.  sfnn_build_quantized_proxy_device (cu:10937): the
+ * engine-lattice proxy of the f32 masters (FT rows folded with their virtual
+ * row and rounded to 1/127 in i16 range, FT bias likewise, dense weights
+ * folded with their shared factor and rounded to 1/64 in i8 range, dense
+ * biases to 1/8128 in i32 range); skip_ft_weights leaves dst_l0w untouched.
+ * Same support limits as the forward (no axis factorizers, residual gates or
+ * grouped L1; no BatchNorm on this backend). */
+int bulletou_cuda_cpp_sfnn_backward_device(BulletOuCudaCppContext* ctx, size_t input_size, size_t ft_size,
+    size_t l1_hidden, int l1_skip, size_t l2_size, size_t num_stacks, size_t l1_group_count,
+    size_t l1_common_size, size_t l1_shard_size, size_t factorizer_king_axis_dim,
+    size_t factorizer_hand_axis_dim, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* stm_l0,
+    const BulletOuCudaCppF32Buffer* nstm_l0, const BulletOuCudaCppF32Buffer* combined,
+    const BulletOuCudaCppF32Buffer* l1, const BulletOuCudaCppF32Buffer* l2_input,
+    const BulletOuCudaCppF32Buffer* l2, const BulletOuCudaCppF32Buffer* l1w,
+    const BulletOuCudaCppF32Buffer* qat_l1w, const BulletOuCudaCppF32Buffer* l1fw, int has_l1f,
+    const BulletOuCudaCppF32Buffer* l1axw, int has_l1ax, const BulletOuCudaCppF32Buffer* l2w,
+    const BulletOuCudaCppF32Buffer* l2fw, int has_l2f, const BulletOuCudaCppF32Buffer* l2axw, int has_l2ax,
+    const BulletOuCudaCppF32Buffer* l3w, const BulletOuCudaCppF32Buffer* l3fw, int has_l3f,
+    const BulletOuCudaCppF32Buffer* l3axw, int has_l3ax, int use_king_axis, int use_hand_axis,
+    int use_progress_axis, int use_king_hand_pair, int use_king_progress_pair, int use_hand_progress_pair,
+    float ft_factorizer_alpha, float factorizer_shared_alpha, float factorizer_king_axis_alpha,
+    float factorizer_hand_axis_alpha, float factorizer_progress_axis_alpha, float factorizer_pair_alpha,
+    const BulletOuCudaCppF32Buffer* residual_count_gates,
+    const BulletOuCudaCppF32Buffer* factorizer_axis_confidences,
+    const BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* l2_gradients,
+    BulletOuCudaCppF32Buffer* l1_gradients, BulletOuCudaCppF32Buffer* l2_input_gradients,
+    BulletOuCudaCppF32Buffer* combined_gradients, BulletOuCudaCppF32Buffer* stm_l0_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_gradients, BulletOuCudaCppF32Buffer* stm_l0_pre_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_pre_gradients, BulletOuCudaCppF32Buffer* l0w_gradients,
+    BulletOuCudaCppF32Buffer* l0b_gradients, BulletOuCudaCppF32Buffer* l1w_gradients,
+    BulletOuCudaCppF32Buffer* l1b_gradients, BulletOuCudaCppF32Buffer* l1fw_gradients,
+    BulletOuCudaCppF32Buffer* l1fb_gradients, BulletOuCudaCppF32Buffer* l1axw_gradients,
+    BulletOuCudaCppF32Buffer* l1axb_gradients, BulletOuCudaCppF32Buffer* l2w_gradients,
+    BulletOuCudaCppF32Buffer* l2b_gradients, BulletOuCudaCppF32Buffer* l2fw_gradients,
+    BulletOuCudaCppF32Buffer* l2fb_gradients, BulletOuCudaCppF32Buffer* l2axw_gradients,
+    BulletOuCudaCppF32Buffer* l2axb_gradients, BulletOuCudaCppF32Buffer* l3w_gradients,
+    BulletOuCudaCppF32Buffer* l3b_gradients, BulletOuCudaCppF32Buffer* l3fw_gradients,
+    BulletOuCudaCppF32Buffer* l3fb_gradients, BulletOuCudaCppF32Buffer* l3axw_gradients,
+    BulletOuCudaCppF32Buffer* l3axb_gradients);  /* cu:12274 */
+int bulletou_cuda_cpp_sfnn_backward_train_profile_device(BulletOuCudaCppContext* ctx, size_t input_size,
+    size_t ft_size, size_t l1_hidden, int l1_skip, size_t l2_size, size_t num_stacks, size_t l1_group_count,
+    size_t l1_common_size, size_t l1_shard_size, size_t factorizer_king_axis_dim,
+    size_t factorizer_hand_axis_dim, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* stm_l0,
+    const BulletOuCudaCppF32Buffer* nstm_l0, const BulletOuCudaCppF32Buffer* combined,
+    const BulletOuCudaCppF32Buffer* l1, const BulletOuCudaCppF32Buffer* l2_input,
+    const BulletOuCudaCppF32Buffer* l2, const BulletOuCudaCppF32Buffer* l1w,
+    const BulletOuCudaCppF32Buffer* qat_l1w, const BulletOuCudaCppF32Buffer* l1fw, int has_l1f,
+    const BulletOuCudaCppF32Buffer* l1axw, int has_l1ax, const BulletOuCudaCppF32Buffer* l2w,
+    const BulletOuCudaCppF32Buffer* l2fw, int has_l2f, const BulletOuCudaCppF32Buffer* l2axw, int has_l2ax,
+    const BulletOuCudaCppF32Buffer* l3w, const BulletOuCudaCppF32Buffer* l3fw, int has_l3f,
+    const BulletOuCudaCppF32Buffer* l3axw, int has_l3ax, int use_king_axis, int use_hand_axis,
+    int use_progress_axis, int use_king_hand_pair, int use_king_progress_pair, int use_hand_progress_pair,
+    float ft_factorizer_alpha, float factorizer_shared_alpha, float factorizer_king_axis_alpha,
+    float factorizer_hand_axis_alpha, float factorizer_progress_axis_alpha, float factorizer_pair_alpha,
+    const BulletOuCudaCppF32Buffer* residual_count_gates,
+    const BulletOuCudaCppF32Buffer* factorizer_axis_confidences,
+    const BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* l2_gradients,
+    BulletOuCudaCppF32Buffer* l1_gradients, BulletOuCudaCppF32Buffer* l2_input_gradients,
+    BulletOuCudaCppF32Buffer* combined_gradients, BulletOuCudaCppF32Buffer* stm_l0_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_gradients, BulletOuCudaCppF32Buffer* stm_l0_pre_gradients,
+    BulletOuCudaCppF32Buffer* nstm_l0_pre_gradients, BulletOuCudaCppF32Buffer* l0w_gradients,
+    BulletOuCudaCppF32Buffer* l0b_gradients, BulletOuCudaCppF32Buffer* l1w_gradients,
+    BulletOuCudaCppF32Buffer* l1b_gradients, BulletOuCudaCppF32Buffer* l1fw_gradients,
+    BulletOuCudaCppF32Buffer* l1fb_gradients, BulletOuCudaCppF32Buffer* l1axw_gradients,
+    BulletOuCudaCppF32Buffer* l1axb_gradients, BulletOuCudaCppF32Buffer* l2w_gradients,
+    BulletOuCudaCppF32Buffer* l2b_gradients, BulletOuCudaCppF32Buffer* l2fw_gradients,
+    BulletOuCudaCppF32Buffer* l2fb_gradients, BulletOuCudaCppF32Buffer* l2axw_gradients,
+    BulletOuCudaCppF32Buffer* l2axb_gradients, BulletOuCudaCppF32Buffer* l3w_gradients,
+    BulletOuCudaCppF32Buffer* l3b_gradients, BulletOuCudaCppF32Buffer* l3fw_gradients,
+    BulletOuCudaCppF32Buffer* l3fb_gradients, BulletOuCudaCppF32Buffer* l3axw_gradients,
+    BulletOuCudaCppF32Buffer* l3axb_gradients, int zero_parameter_gradients, float* profile_ms,
+    size_t profile_ms_len);  /* cu:13080 */
+int bulletou_cuda_cpp_sfnn_build_quantized_proxy_device(BulletOuCudaCppContext* ctx, size_t src_input_size,
+    size_t dst_input_size, size_t virtual_rows, size_t ft_size, size_t l1_hidden, int l1_skip,
+    size_t l2_size, size_t num_stacks, size_t l1_group_count, size_t l1_common_size, size_t l1_shard_size,
+    size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim,
+    const BulletOuCudaCppF32Buffer* src_l0w, const BulletOuCudaCppF32Buffer* src_l0b,
+    const BulletOuCudaCppF32Buffer* src_l1w, const BulletOuCudaCppF32Buffer* src_l1b,
+    const BulletOuCudaCppF32Buffer* src_l1fw, const BulletOuCudaCppF32Buffer* src_l1fb, int has_l1f,
+    const BulletOuCudaCppF32Buffer* src_l1axw, const BulletOuCudaCppF32Buffer* src_l1axb, int has_l1ax,
+    const BulletOuCudaCppF32Buffer* src_l2w, const BulletOuCudaCppF32Buffer* src_l2b,
+    const BulletOuCudaCppF32Buffer* src_l2fw, const BulletOuCudaCppF32Buffer* src_l2fb, int has_l2f,
+    const BulletOuCudaCppF32Buffer* src_l2axw, const BulletOuCudaCppF32Buffer* src_l2axb, int has_l2ax,
+    const BulletOuCudaCppF32Buffer* src_l3w, const BulletOuCudaCppF32Buffer* src_l3b,
+    const BulletOuCudaCppF32Buffer* src_l3fw, const BulletOuCudaCppF32Buffer* src_l3fb, int has_l3f,
+    const BulletOuCudaCppF32Buffer* src_l3axw, const BulletOuCudaCppF32Buffer* src_l3axb, int has_l3ax,
+    int use_king_axis, int use_hand_axis, int use_progress_axis, int use_king_hand_pair,
+    int use_king_progress_pair, int use_hand_progress_pair, float ft_factorizer_alpha,
+    float factorizer_shared_alpha, float factorizer_king_axis_alpha, float factorizer_hand_axis_alpha,
+    float factorizer_progress_axis_alpha, float factorizer_pair_alpha,
+    const BulletOuCudaCppF32Buffer* residual_count_gates,
+    const BulletOuCudaCppF32Buffer* factorizer_axis_confidences, BulletOuCudaCppF32Buffer* dst_l0w,
+    BulletOuCudaCppF32Buffer* dst_l0b, BulletOuCudaCppF32Buffer* dst_l1w, BulletOuCudaCppF32Buffer* dst_l1b,
+    BulletOuCudaCppF32Buffer* dst_l2w, BulletOuCudaCppF32Buffer* dst_l2b, BulletOuCudaCppF32Buffer* dst_l3w,
+    BulletOuCudaCppF32Buffer* dst_l3b, int skip_ft_weights);  /* cu:10937 */
+
+/* ---- small per-row / per-bucket utilities ----
+ * scale_axis_rows (cu:10245): values[r * row_len + j] *= row_scales[r].
+ * residual_count_decay (cu:13411): gradients[s][j] += 2 * decay[s] * weights[s][j]
+ * over the dirty buckets (all buckets when dirty_count == 0).
+ * residual_count_gates (cu:13451): gradients[s][j] *= gates[s] over the same set.
+ * center_scale (cu:13993): dst[i] = src[i] * scale. */
+int bulletou_cuda_cpp_scale_axis_rows_f32_device(BulletOuCudaCppContext* ctx,
+    BulletOuCudaCppF32Buffer* values, size_t value_len, const BulletOuCudaCppF32Buffer* row_scales,
+    size_t row_count, size_t row_len);  /* cu:10245 */
+int bulletou_cuda_cpp_sfnn_add_residual_count_decay_gradients_device(BulletOuCudaCppContext* ctx,
+    BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppF32Buffer* gradients,
+    BulletOuCudaCppF32Buffer* decay_by_stack, BulletOuCudaCppI32Buffer* dirty_buckets, size_t dirty_count,
+    size_t stride, size_t num_stacks);  /* cu:13411 */
+int bulletou_cuda_cpp_sfnn_apply_residual_count_gates_to_gradients_device(BulletOuCudaCppContext* ctx,
+    BulletOuCudaCppF32Buffer* gradients, const BulletOuCudaCppF32Buffer* gates,
+    const BulletOuCudaCppI32Buffer* dirty_buckets, size_t dirty_count, size_t stride, size_t num_stacks);  /* cu:13451 */
+int bulletou_center_scale(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* src,
+    BulletOuCudaCppF32Buffer* dst, size_t n, float scale);  /* cu:13993 */
+
+/* ---- research features outside this backend's scope ----
+ * Exported so that a Rust build of crates/cuda_cpp links against this
+ * library unchanged; each returns -1 with "unsupported on this backend: <name>"
+ * after checking nothing else.  BatchNorm (batch_norm.cuh, bn_qat.cuh),
+ * FT / L1 centering and its experiments, the FT saturation guard, effective
+ * L1 clipping, bucket-axis factorizer updates, the shared-factor rebase and
+ * the saturation penalty.  bulletou_bn_reference_mode (void) ignores its
+ * argument: there is no BatchNorm to switch. */
+int bulletou_bn_bind(BulletOuCudaCppContext* ctx, int layer, BulletOuCudaCppF32Buffer* params,
+    BulletOuCudaCppF32Buffer* running, BulletOuCudaCppF32Buffer* stats, BulletOuCudaCppF32Buffer* grads,
+    BulletOuCudaCppF32Buffer* xa, BulletOuCudaCppF32Buffer* xb, size_t rows, size_t stride, size_t width,
+    size_t groups, float epsilon, float momentum, int training);  /* batch_norm.cuh:365 */
+int bulletou_bn_forward(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* a,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* xa, BulletOuCudaCppF32Buffer* xb,
+    BulletOuCudaCppI32Buffer* ids, BulletOuCudaCppF32Buffer* params, BulletOuCudaCppF32Buffer* running,
+    BulletOuCudaCppF32Buffer* stats, size_t rows, size_t stride, size_t width, size_t groups, float epsilon,
+    float momentum, int training);  /* batch_norm.cuh:294 */
+int bulletou_bn_backward(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* da,
+    BulletOuCudaCppF32Buffer* db, BulletOuCudaCppF32Buffer* xa, BulletOuCudaCppF32Buffer* xb,
+    BulletOuCudaCppI32Buffer* ids, BulletOuCudaCppF32Buffer* params, BulletOuCudaCppF32Buffer* stats,
+    BulletOuCudaCppF32Buffer* grads, size_t rows, size_t stride, size_t width, size_t groups);  /* batch_norm.cuh:316 */
+int bulletou_bn_qat_project_l2(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* slow, size_t input, size_t channels);  /* bn_qat.cuh:20 */
+int bulletou_bn_qat_unfold_training(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* sw, BulletOuCudaCppF32Buffer* sb,
+    BulletOuCudaCppF32Buffer* qw, BulletOuCudaCppF32Buffer* qb, size_t input, size_t output, size_t groups,
+    int layer, size_t vr, float alpha);  /* bn_qat.cuh:78 */
+int bulletou_bn_qat_ft(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* src,
+    BulletOuCudaCppF32Buffer* dst, size_t base, size_t vr, size_t width, float alpha);  /* bn_qat.cuh:162 */
+int bulletou_bn_qat_ft_training(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* src,
+    BulletOuCudaCppF32Buffer* dst, BulletOuCudaCppF32Buffer* bias, BulletOuCudaCppF32Buffer* out_bias,
+    size_t base, size_t vr, size_t width, float alpha);  /* bn_qat.cuh:169 */
+int bulletou_bn_qat_pullback(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* sw, BulletOuCudaCppF32Buffer* sb,
+    BulletOuCudaCppF32Buffer* gw, BulletOuCudaCppF32Buffer* gb, BulletOuCudaCppF32Buffer* gs,
+    BulletOuCudaCppF32Buffer* gsb, size_t input, size_t output, size_t groups, int layer, size_t vr,
+    float alpha);  /* bn_qat.cuh:178 */
+void bulletou_bn_reference_mode(int enabled);  /* batch_norm.cuh:229 */
+int bulletou_center_l1_groups(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* sw, BulletOuCudaCppF32Buffer* sb,
+    BulletOuCudaCppF32Buffer* gw, BulletOuCudaCppF32Buffer* gb, BulletOuCudaCppF32Buffer* fw,
+    BulletOuCudaCppF32Buffer* fb, BulletOuCudaCppF32Buffer* fsw, BulletOuCudaCppF32Buffer* fsb,
+    BulletOuCudaCppF32Buffer* fgw, BulletOuCudaCppF32Buffer* fgb, BulletOuCudaCppF32Buffer* c, size_t cols,
+    int before);  /* cu:13936 */
+int bulletou_center_affine_layout(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* sw, BulletOuCudaCppF32Buffer* sb,
+    BulletOuCudaCppF32Buffer* gw, BulletOuCudaCppF32Buffer* gb, BulletOuCudaCppF32Buffer* c, size_t rows,
+    size_t cols, int before, int column_major);  /* cu:13974 */
+int bulletou_center_mean_reference(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* input,
+    BulletOuCudaCppF32Buffer* scratch, size_t rows, size_t cols);  /* cu:14013 */
+int bulletou_experiment_center_affine(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* sw, BulletOuCudaCppF32Buffer* sb,
+    BulletOuCudaCppF32Buffer* gw, BulletOuCudaCppF32Buffer* gb, BulletOuCudaCppF32Buffer* c, size_t rows,
+    size_t cols, int before);  /* cu:13959 */
+int bulletou_experiment_column_mean(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* input,
+    BulletOuCudaCppF32Buffer* scratch, size_t rows, size_t cols);  /* cu:14001 */
+int bulletou_experiment_bucket_mean(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* input,
+    BulletOuCudaCppI32Buffer* buckets, BulletOuCudaCppF32Buffer* scratch, size_t n, size_t d, size_t stacks);  /* cu:14043 */
+int bulletou_experiment_bucket_centers(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* sums,
+    BulletOuCudaCppF32Buffer* centers, size_t d, size_t stacks);  /* cu:14055 */
+int bulletou_experiment_center_affine_bucket(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* sw, BulletOuCudaCppF32Buffer* sb,
+    BulletOuCudaCppF32Buffer* gw, BulletOuCudaCppF32Buffer* gb, BulletOuCudaCppF32Buffer* c, size_t rows,
+    size_t cols, size_t group_rows, int before);  /* cu:14062 */
+int bulletou_experiment_mean_penalty_test(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* z,
+    BulletOuCudaCppI32Buffer* buckets, BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppF32Buffer* grad,
+    size_t batch, size_t hidden, size_t stride, size_t stacks, float strength);  /* cu:14075 */
+int bulletou_bind_ft_saturation_guard(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* weights,
+    BulletOuCudaCppI32Buffer* counts, BulletOuCudaCppI32Buffer* streaks, size_t batch, size_t ft,
+    float strength, float rate, int patience);  /* cu:13764 */
+int bulletou_ft_saturation_guard(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* a,
+    BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppI32Buffer* ai,
+    BulletOuCudaCppI32Buffer* bi, BulletOuCudaCppI32Buffer* counts, BulletOuCudaCppI32Buffer* streaks,
+    BulletOuCudaCppF32Buffer* gw, BulletOuCudaCppF32Buffer* gb, size_t batch, size_t ft, size_t active,
+    size_t inputs, float ft_alpha, float strength, float rate, int patience);  /* cu:13780 */
+int bulletou_clip_effective_l1(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* slow, BulletOuCudaCppF32Buffer* shared, BulletOuCudaCppF32Buffer* shared_slow,
+    BulletOuCudaCppF32Buffer* remainder, size_t cols, size_t outputs, float alpha);  /* cu:13831 */
+int bulletou_clip_effective_l1_axis(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* slow, BulletOuCudaCppF32Buffer* shared, BulletOuCudaCppF32Buffer* shared_slow,
+    BulletOuCudaCppF32Buffer* axis, BulletOuCudaCppF32Buffer* axis_slow, BulletOuCudaCppF32Buffer* remainder,
+    size_t cols, size_t outputs, size_t stacks, size_t king_dim, size_t hand_dim, int king, int hand,
+    int progress, int kh, int kp, int hp, float shared_alpha, float king_alpha, float hand_alpha,
+    float progress_alpha, float pair_alpha);  /* cu:13880 */
+int bulletou_factor_axis_update_device(BulletOuCudaCppContext* ctx, size_t len, size_t stride,
+    size_t king_end, size_t hand_end, size_t pair_end, float king_alpha, float hand_alpha, float pair_alpha,
+    float progress_alpha, BulletOuCudaCppF32Buffer* confidence, float gradient_factor, float lr, float decay,
+    float beta1, float beta2, float epsilon, float step_size, int use_denom, int sgd, float min_weight,
+    float max_weight, float norm_rate, int norm_before, int do_lookahead, float lookahead_alpha,
+    int clip_after, BulletOuCudaCppF32Buffer* gradients, BulletOuCudaCppF32Buffer* weights,
+    BulletOuCudaCppF32Buffer* momentum, BulletOuCudaCppF32Buffer* velocity, BulletOuCudaCppF32Buffer* slow);  /* cu:10522 */
+int bulletou_cuda_cpp_rebase_shared_device(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* base,
+    BulletOuCudaCppF32Buffer* base_slow, BulletOuCudaCppF32Buffer* base_m, BulletOuCudaCppF32Buffer* base_v,
+    BulletOuCudaCppF32Buffer* shared, BulletOuCudaCppF32Buffer* shared_slow,
+    BulletOuCudaCppF32Buffer* shared_m, BulletOuCudaCppF32Buffer* shared_v, BulletOuCudaCppF32Buffer* gates,
+    size_t base_count, size_t shared_count, size_t shared_offset, size_t input_dim, size_t output_dim,
+    float old_alpha, float new_alpha);  /* cu:13609 */
+int bulletou_cuda_cpp_sfnn_add_saturation_penalty_gradients_device(BulletOuCudaCppContext* ctx,
+    BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppF32Buffer* shared_weights, int has_shared,
+    BulletOuCudaCppF32Buffer* axis_weights, int has_axis, BulletOuCudaCppF32Buffer* gradients,
+    BulletOuCudaCppF32Buffer* shared_gradients, BulletOuCudaCppF32Buffer* axis_gradients,
+    BulletOuCudaCppI32Buffer* dirty_buckets, size_t dirty_count, size_t input_dim, size_t output_dim,
+    size_t num_stacks, size_t factorizer_king_axis_dim, size_t factorizer_hand_axis_dim, int use_king_axis,
+    int use_hand_axis, int use_progress_axis, int use_king_hand_pair, int use_king_progress_pair,
+    int use_hand_progress_pair, float ft_factorizer_alpha, float factorizer_shared_alpha,
+    float factorizer_king_axis_alpha, float factorizer_hand_axis_alpha, float factorizer_progress_axis_alpha,
+    float factorizer_pair_alpha, const BulletOuCudaCppF32Buffer* residual_count_gates,
+    const BulletOuCudaCppF32Buffer* factorizer_axis_confidences, int shared_weight_input_major,
+    float weight_scale, float threshold, float penalty);  /* cu:13277 */
+
+/* ---- the reference's kernel test hooks (crates/cuda_cpp/src tests) ----
+ * Entry points that exist so the reference's own tests can drive single
+ * internal kernels of its implementation (its FP16 gather variants, packed
+ * L1, sort kernels, the dense-QAT integer references).  They have no
+ * counterpart among this backend's kernels: each returns -1 with
+ * "unsupported on this backend: <name>".  bulletou_test_stream_delay returns 0
+ * (it only delays the stream in the reference). */
+int bulletou_test_dense_l1_16(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* input,
+    BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppF32Buffer* bias, BulletOuCudaCppI32Buffer* buckets,
+    BulletOuCudaCppF32Buffer* output, size_t batch, size_t input_dim, size_t stacks, int optimized);  /* cu:4595 */
+int bulletou_test_factorized_ft_half_fold(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* weights,
+    BulletOuCudaCppF32Buffer* output, size_t base, size_t ft, float alpha, int fused);  /* cu:4620 */
+int bulletou_test_sfnn_ft_sort(BulletOuCudaCppContext* ctx, BulletOuCudaCppI32Buffer* stm,
+    BulletOuCudaCppI32Buffer* nstm, BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppF32Buffer* bias,
+    BulletOuCudaCppF32Buffer* a, BulletOuCudaCppF32Buffer* b, BulletOuCudaCppF32Buffer* combined,
+    BulletOuCudaCppI32Buffer* counts, BulletOuCudaCppI32Buffer* order, size_t batch, size_t active,
+    size_t input, size_t ft, int sorted);  /* cu:4647 */
+int bulletou_test_sfnn_ft_gather(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* pre,
+    BulletOuCudaCppI32Buffer* positions, BulletOuCudaCppI32Buffer* offsets,
+    BulletOuCudaCppF32Buffer* gradients, size_t features, size_t ft, int tiled, int add);  /* cu:4762 */
+int bulletou_test_sfnn_half_grad_gather(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* pre,
+    BulletOuCudaCppI32Buffer* positions, BulletOuCudaCppI32Buffer* offsets, BulletOuCudaCppF32Buffer* out,
+    size_t batch, size_t features, size_t ft, size_t occurrences, int vector_width);  /* cu:4838 */
+int bulletou_test_sfnn_half_grad(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* stm,
+    BulletOuCudaCppF32Buffer* nstm, BulletOuCudaCppF32Buffer* combined, BulletOuCudaCppF32Buffer* out_stm,
+    BulletOuCudaCppF32Buffer* out_nstm, BulletOuCudaCppF32Buffer* bias_grad, size_t batch, size_t ft,
+    int fused);  /* cu:4866 */
+int bulletou_test_stream_delay(BulletOuCudaCppContext* ctx);  /* cu:5639 */
+int bulletou_test_l1_bucket_fold(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* w,
+    BulletOuCudaCppF32Buffer* shared, BulletOuCudaCppF32Buffer* axis, BulletOuCudaCppF32Buffer* gates,
+    BulletOuCudaCppF32Buffer* confidence, BulletOuCudaCppF32Buffer* out, BulletOuCudaCppI32Buffer* packed,
+    int fast);  /* cu:5646 */
+int bulletou_test_qat_ft_lattice(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* values, size_t n,
+    int fast);  /* cu:6013 */
+int bulletou_test_qat_packed_l1(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* input,
+    BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppI32Buffer* bias, BulletOuCudaCppI32Buffer* buckets,
+    BulletOuCudaCppF32Buffer* output, BulletOuCudaCppI32Buffer* raw, size_t batch, size_t inputs,
+    size_t outputs, size_t stacks, int packed);  /* cu:6247 */
+int bulletou_test_dense_qat_exact_ft(BulletOuCudaCppContext* ctx, BulletOuCudaCppI32Buffer* stm,
+    BulletOuCudaCppI32Buffer* nstm, BulletOuCudaCppF32Buffer* w, BulletOuCudaCppF32Buffer* bias,
+    BulletOuCudaCppF32Buffer* output, BulletOuCudaCppI32Buffer* packed, size_t batch, size_t active,
+    size_t inputs, size_t width);  /* cu:6384 */
+int bulletou_test_l1_to_ft_f32_gradient(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* dy,
+    BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppI32Buffer* buckets,
+    BulletOuCudaCppF32Buffer* activations, BulletOuCudaCppF32Buffer* result, BulletOuCudaCppF32Buffer* bias,
+    size_t batch, size_t width, size_t stacks, int fused);  /* cu:7123 */
+int bulletou_test_l1_to_ft_half_gradient(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* dy,
+    BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppI32Buffer* buckets,
+    BulletOuCudaCppF32Buffer* activations, BulletOuCudaCppF32Buffer* result, BulletOuCudaCppF32Buffer* bias,
+    size_t batch, size_t width, size_t stacks, int fused);  /* cu:7152 */
+int bulletou_test_l1_gather2(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* inputs,
+    BulletOuCudaCppF32Buffer* dy, BulletOuCudaCppI32Buffer* offsets, BulletOuCudaCppI32Buffer* positions,
+    BulletOuCudaCppF32Buffer* dw, BulletOuCudaCppF32Buffer* db, BulletOuCudaCppF32Buffer* dfw,
+    BulletOuCudaCppF32Buffer* dfb, size_t batch, size_t width, size_t outputs, size_t stacks, float alpha);  /* cu:7314 */
+int bulletou_test_l1_gather2_king_progress(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* inputs,
+    BulletOuCudaCppF32Buffer* dy, BulletOuCudaCppI32Buffer* offsets, BulletOuCudaCppI32Buffer* positions,
+    BulletOuCudaCppF32Buffer* dw, BulletOuCudaCppF32Buffer* db, BulletOuCudaCppF32Buffer* dfw,
+    BulletOuCudaCppF32Buffer* dfb, BulletOuCudaCppF32Buffer* daw, BulletOuCudaCppF32Buffer* dab,
+    BulletOuCudaCppF32Buffer* confidence, size_t batch, size_t width, size_t outputs, size_t stacks,
+    size_t king_dim, float shared_alpha, float king_alpha, float progress_alpha, float pair_alpha);  /* cu:7338 */
+int bulletou_dense_qat_integer_reference(BulletOuCudaCppContext* ctx, BulletOuCudaCppI32Buffer* input,
+    BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppF32Buffer* bias, BulletOuCudaCppI32Buffer* buckets,
+    BulletOuCudaCppI32Buffer* output, size_t batch, size_t inputs, size_t outputs, size_t stacks);  /* cu:9336 */
+int bulletou_dense_qat_activation_reference(BulletOuCudaCppContext* ctx, BulletOuCudaCppI32Buffer* raw,
+    BulletOuCudaCppF32Buffer* square_gradient, BulletOuCudaCppF32Buffer* linear_gradient,
+    BulletOuCudaCppI32Buffer* square_output, BulletOuCudaCppI32Buffer* linear_output,
+    BulletOuCudaCppF32Buffer* gradient, size_t n);  /* cu:9403 */
+int bulletou_dense_qat_l1_backward_reference(BulletOuCudaCppContext* ctx, BulletOuCudaCppF32Buffer* l1,
+    BulletOuCudaCppF32Buffer* l2_input, BulletOuCudaCppF32Buffer* l2_input_gradients,
+    BulletOuCudaCppF32Buffer* l1_gradients, size_t batch, size_t hidden, int skip);  /* cu:9422 */
+
 #ifdef __cplusplus
 }
 #endif
