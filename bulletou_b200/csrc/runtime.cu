@@ -365,6 +365,28 @@ int bulletou_cuda_cpp_context_destroy(BulletOuCudaCppContext* ctx) {
     return rc == 0 ? ok() : rc;
 }
 
+// Read bandwidth of a buffer that stays resident in L2: every pass reads the
+// whole buffer as 16-byte loads cached in L2 only (ld.global.cg), so after the
+// first pass the bytes come from L2.  One partial per thread keeps the loads
+// alive.  Used to measure the L2 peak the gather kernels are compared with.
+__global__ void l2_read_probe_kernel(const float4* __restrict__ buf, size_t n4, int passes, float* __restrict__ sink) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const size_t t0 = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    float acc = 0.0f;
+    for (int p = 0; p < passes; ++p) {
+        // a pass-dependent start keeps each thread's addresses moving across
+        // the L2 slices from pass to pass
+        const size_t shift = (static_cast<size_t>(p) * 7919u * blockDim.x) % n4;
+        for (size_t i = t0; i < n4; i += stride) {
+            size_t j = i + shift;
+            if (j >= n4) j -= n4;
+            const float4 v = __ldcg(buf + j);
+            acc += (v.x + v.y) + (v.z + v.w);
+        }
+    }
+    sink[t0] = acc;
+}
+
 int bulletou_b200_profile_begin(BulletOuCudaCppContext* ctx, size_t max_marks) {
     if (set_device(ctx) != 0) return -1;
     while (ctx->prof_events.size() < max_marks) {
@@ -400,6 +422,19 @@ int bulletou_b200_profile_end(BulletOuCudaCppContext* ctx, float* ms_out, size_t
     if (phases_out) *phases_out = phases;
     ctx->prof_used = 0;
     return ok();
+}
+
+int bulletou_b200_l2_read_probe(BulletOuCudaCppContext* ctx, const BulletOuCudaCppF32Buffer* buffer, size_t len,
+                                int passes, BulletOuCudaCppF32Buffer* sink) {
+    if (validate_f32(ctx, buffer, len, "L2 probe buffer") != 0) return -1;
+    if (len % 4 != 0 || len == 0 || passes <= 0) return fail_message("L2 probe: len must be a positive multiple of 4");
+    if (set_device(ctx) != 0) return -1;
+    const int threads = 512;
+    const int blocks = 4 * ctx->sm_count;
+    if (validate_f32(ctx, sink, static_cast<size_t>(threads) * blocks, "L2 probe sink") != 0) return -1;
+    l2_read_probe_kernel<<<blocks, threads, 0, ctx->stream>>>(reinterpret_cast<const float4*>(buffer->ptr), len / 4,
+                                                              passes, sink->ptr);
+    return check_launch("L2 read probe");
 }
 
 int bulletou_cuda_cpp_context_synchronize(BulletOuCudaCppContext* ctx) {

@@ -551,6 +551,21 @@ def ranger_update_device(ctx: Context, params: RangerUpdateParams, state: Ranger
                  state.slow_params.as_ptr(), None)
 
 
+def ranger_update_stacked_dirty_device(ctx: Context, params: RangerUpdateParams, state: RangerDeviceState,
+                                       stride: int, dirty_buckets: I32Buffer, dirty_count: int,
+                                       lr_multiplier: float = 1.0) -> None:
+    """Ranger on the listed buckets of a [stacks][stride] group
+    (update_param_group's dirty-bucket branch, lib.rs:8761-8890)."""
+    params.validate()
+    n = len(state.weights)
+    s = params.ffi_step(lr_multiplier)
+    ctx.lib.call("bulletou_cuda_cpp_ranger_update_stacked_dirty_device", ctx.as_ptr(), s.norm_loss_rate,
+                 s.norm_loss_before, n, stride, dirty_count, s.gradient_factor, s.learning_rate, s.step_size,
+                 s.use_denom, s.decay, s.beta1, s.beta2, s.epsilon, s.min_weight, s.max_weight, s.do_lookahead,
+                 s.lookahead_alpha, s.clip_after_lookahead, dirty_buckets.as_ptr(), state.gradients.as_ptr(),
+                 state.weights.as_ptr(), state.momentum.as_ptr(), state.velocity.as_ptr(), state.slow_params.as_ptr())
+
+
 def ranger_update_host(device: int, params: RangerUpdateParams, gradients: np.ndarray, weights: np.ndarray,
                        momentum: np.ndarray, velocity: np.ndarray, slow_params: np.ndarray,
                        lib: Optional[Library] = None) -> None:
@@ -714,6 +729,26 @@ class RangerParamState:
                 "slow_params": self.slow_params.download(ctx)}
 
 
+def upload_from_pinned(ctx: Context, dst: "_DeviceBuffer", pinned) -> None:
+    """Asynchronous H2D copy of a whole page-locked host buffer on ctx's stream,
+    with no host copy.  `pinned` is a _PinnedBuffer of this library (its
+    *_upload_pinned entries) or a page-locked numpy array (e.g. a view of
+    pinned torch memory), which goes through the drop-in ABI's plain *_upload
+    entries (cu:10084, 10153: one cudaMemcpyAsync, asynchronous from
+    page-locked memory) -- on either backend library."""
+    i32 = isinstance(dst, I32Buffer)
+    if isinstance(pinned, np.ndarray):
+        name = "bulletou_cuda_cpp_i32_upload" if i32 else "bulletou_cuda_cpp_f32_upload"
+        ctx.lib.call(name, ctx.as_ptr(), dst.as_ptr(), ctypes.c_void_p(pinned.ctypes.data), pinned.size)
+        return
+    name = "bulletou_b200_i32_upload_pinned" if i32 else "bulletou_b200_f32_upload_pinned"
+    ctx.lib.call(name, ctx.as_ptr(), dst.as_ptr(), pinned.as_ptr(), pinned.length)
+
+
+def _nbytes(buf) -> int:
+    return int(buf.nbytes) if isinstance(buf, np.ndarray) else 4 * buf.length
+
+
 class NnueTrainStepUploadSlot:
     """Device batch buffers + pinned staging + upload/compute events
     (NnueTrainStepUploadSlot, lib.rs:5509-5600).  Before a slot is refilled,
@@ -739,29 +774,26 @@ class NnueTrainStepUploadSlot:
         if self.in_use:
             self.upload_ready.synchronize()
             self.compute_done.wait(upload_ctx)
-        if not lib.has("bulletou_b200_i32_upload_pinned"):
+        dsts = (self.stm_indices, self.nstm_indices, self.targets, self.entry_weights)
+        if pinned_source is None and not lib.has("bulletou_b200_i32_upload_pinned"):
             # the reference ABI: staged uploads (host memcpy into the pinned
             # staging buffer, then an async copy), lib.rs:5552-5575
             if batch is None:
                 raise CudaCppError("this backend needs host batch arrays for staged uploads")
-            self.pinned[0].upload_to_device(upload_ctx, self.stm_indices, batch.stm_indices)
-            self.pinned[1].upload_to_device(upload_ctx, self.nstm_indices, batch.nstm_indices)
-            self.pinned[2].upload_to_device(upload_ctx, self.targets, batch.targets)
-            self.pinned[3].upload_to_device(upload_ctx, self.entry_weights, batch.entry_weights)
+            srcs = (batch.stm_indices, batch.nstm_indices, batch.targets, batch.entry_weights)
+            for pin, dst, a in zip(self.pinned, dsts, srcs):
+                pin.upload_to_device(upload_ctx, dst, a)
             self.upload_ready.record(upload_ctx)
             self.in_use = True
             return 4 * sum(x.length for x in self.pinned)
         src = pinned_source.pinned if pinned_source is not None else self.pinned
         if pinned_source is None:
             self.fill(batch)
-        c = upload_ctx.as_ptr()
-        lib.call("bulletou_b200_i32_upload_pinned", c, self.stm_indices.as_ptr(), src[0].as_ptr(), src[0].length)
-        lib.call("bulletou_b200_i32_upload_pinned", c, self.nstm_indices.as_ptr(), src[1].as_ptr(), src[1].length)
-        lib.call("bulletou_b200_f32_upload_pinned", c, self.targets.as_ptr(), src[2].as_ptr(), src[2].length)
-        lib.call("bulletou_b200_f32_upload_pinned", c, self.entry_weights.as_ptr(), src[3].as_ptr(), src[3].length)
+        for dst, pin in zip(dsts, src):
+            upload_from_pinned(upload_ctx, dst, pin)
         self.upload_ready.record(upload_ctx)
         self.in_use = True
-        return 4 * sum(x.length for x in src)
+        return sum(_nbytes(x) for x in src)
 
 
 class NnueTrainStepRunner:

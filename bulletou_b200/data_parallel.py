@@ -458,7 +458,6 @@ def run_data_parallel_bench(args, rank: int, world: int, local: int, dist):
     import bench
     import bulletou_b200 as bo
     from bulletou_b200 import synthetic
-    from bulletou_b200.cuda_cpp import PinnedF32Buffer, PinnedI32Buffer
 
     backend = B200Backend(local)
     w = synthetic.halfkp_weights(synthetic.rng_for(7))
@@ -497,45 +496,34 @@ def run_data_parallel_bench(args, rank: int, world: int, local: int, dist):
     dist.barrier()
     total_ms = bench.max_over_ranks(dist, stop.elapsed_ms_since(start))
     phase_ms = {bench.PHASES[p]: ms[p] / max(1, nsteps.value) for p in range(nphases.value)}
-    # end to end: per step H2D from pinned host memory, step, D2H of the mean loss
-    pins = []
-    for b in batches:
-        p = (PinnedI32Buffer(ctx, b["stm"].size), PinnedI32Buffer(ctx, b["nstm"].size),
-             PinnedF32Buffer(ctx, args.batch), PinnedF32Buffer(ctx, args.batch))
-        for dst, src in zip(p, (b["stm"], b["nstm"], b["targets"], b["entry_weights"])):
-            np.copyto(dst.host(), src)
-        pins.append(p)
+    # end to end: per step the batch H2D from page-locked host memory through
+    # the ABI's *_upload entries, the step, a synchronous read of the mean loss
+    from bulletou_b200.cuda_cpp import upload_from_pinned
+
+    sources = [bench.PinnedHostBatch((b["stm"], b["nstm"], b["targets"], b["entry_weights"])) for b in batches]
     in_bufs = (I32Buffer(ctx, args.batch * bench.ACTIVE), I32Buffer(ctx, args.batch * bench.ACTIVE),
                F32Buffer(ctx, args.batch), F32Buffer(ctx, args.batch))
     tr.stm_indices, tr.nstm_indices, tr.targets, tr.entry_weights = in_bufs
-    e2e_steps = max(8, args.steps)
-    ring = [PinnedF32Buffer(ctx, 1) for _ in range(e2e_steps)]
     dist.barrier()
     e0, e1 = bo.Event(ctx), bo.Event(ctx)
+    losses = []
     t0 = time.perf_counter()
     e0.record(ctx)
-    h2d = 0
-    for i in range(e2e_steps):
+    for i in range(args.steps):
         step += 1
-        p = pins[i % len(pins)]
-        c = ctx.as_ptr()
-        lib.call("bulletou_b200_i32_upload_pinned", c, in_bufs[0].as_ptr(), p[0].as_ptr(), p[0].length)
-        lib.call("bulletou_b200_i32_upload_pinned", c, in_bufs[1].as_ptr(), p[1].as_ptr(), p[1].length)
-        lib.call("bulletou_b200_f32_upload_pinned", c, in_bufs[2].as_ptr(), p[2].as_ptr(), p[2].length)
-        lib.call("bulletou_b200_f32_upload_pinned", c, in_bufs[3].as_ptr(), p[3].as_ptr(), p[3].length)
-        h2d = 4 * sum(x.length for x in p)
+        for dst, src in zip(in_bufs, sources[i % len(sources)].pinned):
+            upload_from_pinned(ctx, dst, src)
         tr.step_device(bench.ranger(step), loss_kind, inv, finalize_loss=True)
-        lib.call("bulletou_b200_f32_download_pinned", c, ring[i].as_ptr(), tr.loss_workspace.mean.as_ptr(), 1)
+        losses.append(float(tr.loss_workspace.mean.download(ctx)[0]))
     e1.record(ctx)
     e1.synchronize()
     wall_ms = (time.perf_counter() - t0) * 1000.0
     e2e_ms = bench.max_over_ranks(dist, max(e1.elapsed_ms_since(e0), wall_ms))
-    losses = [float(r.host()[0]) for r in ring]
     assert all(np.isfinite(losses)), "non-finite loss"
     return {"total_ms": total_ms, "phase_ms": phase_ms, "clocks": clocks.summary(),
-            "e2e": {"value": e2e_steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4, "steps": e2e_steps,
+            "e2e": {"value": args.steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
+                    "h2d_bytes_per_step": int(sources[0].nbytes), "d2h_bytes_per_step": 4, "steps": args.steps,
                     "path": "NnueDataParallelTrainer.step_device per rank (NCCL reduce-scatter / all-reduce / "
-                            "all-gather), inputs from pinned host memory, mean loss copied D2H every step"},
+                            "all-gather), inputs from page-locked host memory, mean loss read back every step"},
             "gpu_launches": (bench.LAUNCHES_PER_STEP + 8) * args.steps,
             "final_loss": losses[-1]}

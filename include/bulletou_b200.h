@@ -97,6 +97,15 @@ int bulletou_b200_profile_begin(BulletOuCudaCppContext* ctx, size_t max_marks);
 int bulletou_b200_profile_end(BulletOuCudaCppContext* ctx, float* ms_out, size_t ms_len, size_t* steps_out,
     size_t* phases_out);
 
+/* L2 read-bandwidth probe (no counterpart in the reference; measurement
+ * only): `passes` reads of buffer[0, len) with 16-byte loads cached in L2
+ * only, by 4 * SMs CTAs of 512 threads; sink receives one float per thread
+ * (len of sink >= 2048 * SMs).  With a buffer well inside L2 (126 MB on B200)
+ * every pass after the first is served by L2; time it with events on the
+ * context stream to get the L2 peak the row-gather kernels are judged by. */
+int bulletou_b200_l2_read_probe(BulletOuCudaCppContext* ctx, const BulletOuCudaCppF32Buffer* buffer, size_t len,
+    int passes, BulletOuCudaCppF32Buffer* sink);
+
 /* One complete HalfKP train step on device-resident batch buffers.
  *
  * Replaces NnueTrainStepRunner::step_no_readback_with_loss_finalize
