@@ -148,10 +148,11 @@ def sfnn_lr_multipliers(mode):
 
 
 def sfnn_launches_per_step(mode):
-    """Kernels of one fused step: the QAT extras are the L1 bias fold (L1 QAT),
-    the FT bias rounding (FT QAT), and the integer FT (dense + FT QAT)."""
+    """Kernels of one fused step: the QAT extras are the L1 bias fold (L1 QAT)
+    and the FT bias rounding (FT QAT); the engine's integer FT of the dense QAT
+    with FT QAT comes out of the FT forward's own gather."""
     l1, ft, l2, l3 = SFNN_QAT_MODES[mode]
-    return SFNN_LAUNCHES_PER_STEP + int(l1) + int(ft) + (1 if (ft and l1 and l2 and l3) else 0)
+    return SFNN_LAUNCHES_PER_STEP + int(l1) + int(ft)
 
 
 def parse_args():
@@ -977,11 +978,7 @@ def sfnn_records_e2e(args, ctx, upload_ctx, runner, step, loss_kind, inv):
 
 
 def sfnn_phases(qat):
-    """Stage-profiler phases of one fused step (the integer FT of the dense
-    QAT with FT QAT is a phase of its own)."""
-    l1, ft, l2, l3 = SFNN_QAT_MODES[qat]
-    if ft and l1 and l2 and l3:
-        return SFNN_PHASES[:4] + ("ft_integer",) + SFNN_PHASES[4:]
+    """Stage-profiler phases of one fused step (every QAT mode)."""
     return SFNN_PHASES
 
 
@@ -1176,23 +1173,15 @@ def run_sfnn_reference(args, wl, local):
 # dram__bytes_write.sum over the phase's launches, ncu), keyed by the QAT modes
 # whose kernels they were measured on; profiles/ holds the captures.
 SFNN_DRAM_BYTES_B65536 = {
-    "ft_rows_ranger": (4813480704, ("none", "l1", "layers", "dense", "all")),
-    "ft_forward": (1679058432, ("none", "l1", "dense", "all")),
-    "ft_integer": (613106176, ("all",)),
+    "ft_forward": (1679058432, ("none", "l1", "dense")),
     "l1_backward": (2076098304, ("dense", "all")),
-    "fold": (1124865536, ("all",)),
 }
 SFNN_DRAM_BYTES_PSV_B65536 = {
-    "ft_rows_ranger": (4668284928, ("all",)),
-    "ft_forward": (1181817600, ("all",)),
-    "ft_integer": (570697728, ("all",)),
     "l1_backward": (2068230656, ("all",)),
-    "fold": (1125304832, ("all",)),
 }
 SFNN_PHASE_KERNELS = {
     "ft_rows_ranger": "heavy_segment_kernel + 15 piece_row_kernel launches (FT gradient rows + fused Ranger)",
-    "ft_forward": "ft_forward_kernel<12>",
-    "ft_integer": "qat_exact_ft16_kernel<6>",
+    "ft_forward": "ft_forward_kernel<12> (ft_forward_int_kernel<12, 2> with all-layer QAT)",
     "l1_backward": "l1_backward_kernel<16>",
     "fold": "fold_ft_qat4_kernel",
 }
@@ -1210,16 +1199,15 @@ def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, l2_peak=None, lookahead_
     base = sh.factorized_base()
     H = 2 * batch
     l1, ft, l2, l3 = SFNN_QAT_MODES[qat]
-    integer_ft = ft and l1 and l2 and l3
     dense = l1 and l2 and l3
     keys = (45 + H // 4096 + 1) * 1629
     comp = {
-        # the table (+ virtual rows) read, the folded table written (+ its i16 integers)
-        "fold": rows * W * 4 + base * W * 4 + (base * W * 2 if integer_ft else 0),
+        # the table (+ virtual rows) read, the folded table written
+        "fold": rows * W * 4 + base * W * 4,
         "sorts_tiles": 4 * (H * A + 4 * H + 3 * batch),
         "inverse_index": 4 * (H * A * 3 + keys * 4),
-        # the folded table once + indices + the FT outputs written
-        "ft_forward": base * W * 4 + H * A * 4 + (2 if integer_ft else 3) * batch * W * 4,
+        # the folded table once + indices + the FT outputs written (both views' ClippedReLU, combined)
+        "ft_forward": base * W * 4 + H * A * 4 + 3 * batch * W * 4,
         "l1_head": batch * W * 4 + batch * 4 * (16 + 30 + 32 + 16 + 4),
         # both views' FT outputs (+ the lattice input) read, king-ordered pre-activation gradients written
         "l1_backward": 2 * batch * W * 4 + (batch * W * 4 if dense else 0) + H * W * 4
@@ -1230,9 +1218,6 @@ def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, l2_peak=None, lookahead_
         "ft_rows_ranger": rows * W * 4 * (6 + 2 * lookahead_frac) + H * W * 4 + 4 * (H * A + keys + 1),
     }
     logical = {"ft_forward": H * A * W * 4, "ft_rows_ranger": H * A * W * 4}
-    if integer_ft:
-        comp["ft_integer"] = base * W * 2 + H * A * 4 + batch * W * 4
-        logical["ft_integer"] = H * A * W * 2
     traffic = {}
     table = SFNN_DRAM_BYTES_B65536 if data == "uniform" else SFNN_DRAM_BYTES_PSV_B65536
     if batch == SFNN_BATCH and sh.num_stacks == 9:

@@ -52,6 +52,7 @@ constexpr float kPairScale = 127.0f / 128.0f;  // SFNN_PAIRWISE_SCALE, cu:1148
 constexpr int kBucketKeys = kSfnnMaxStacks + 1;
 constexpr int kPieceRowWarps = 8;
 constexpr int kKingsPerLaunch = 3;  // FT row kernel: king blocks per launch (L2 working set)
+constexpr int kPieceRowCtas = 3;    // FT row kernel: resident CTAs per SM (persistent grid)
 constexpr int kTileRanks = 4096;    // half-positions per rank tile of the FT row index (24 MB of gradient rows)
 
 __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
@@ -127,10 +128,9 @@ __global__ void fold_ft_qat_kernel(const float* __restrict__ l0w, float* __restr
     folded[t] = qat_q127(v);
 }
 
-// The same four columns at a time; optionally the integers q (the i16 table of
-// the engine's integer FT) are written alongside.
-__global__ void fold_ft_qat4_kernel(const float4* __restrict__ l0w, float4* __restrict__ folded,
-                                    short4* __restrict__ table16, size_t total4, int w4, int base, float alpha) {
+// The same four columns at a time.
+__global__ void fold_ft_qat4_kernel(const float4* __restrict__ l0w, float4* __restrict__ folded, size_t total4,
+                                    int w4, int base, float alpha) {
     const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t >= total4) return;
     float4 a = l0w[t];
@@ -142,9 +142,6 @@ __global__ void fold_ft_qat4_kernel(const float4* __restrict__ l0w, float4* __re
     }
     const float4 q = make_float4(qat_q127(a.x), qat_q127(a.y), qat_q127(a.z), qat_q127(a.w));
     folded[t] = q;
-    if (table16 != nullptr)
-        table16[t] = make_short4(static_cast<short>(qat_int127(q.x)), static_cast<short>(qat_int127(q.y)),
-                                 static_cast<short>(qat_int127(q.z)), static_cast<short>(qat_int127(q.w)));
 }
 
 // layer_qat_vector_kernel (cu:9294-9300): element-wise fake quantisation.
@@ -153,15 +150,6 @@ __global__ void qat_vector_kernel(const float* __restrict__ src, float* __restri
     if (t >= n) return;
     const float v = src[t];
     dst[t] = kind == 0 ? qat_q127(v) : (kind == 1 ? qat_q64(v) : qat_q8128(v));
-}
-
-// The integers q of an FT table already on the 1/127 lattice (FT QAT), as i16.
-__global__ void qat_table16_kernel(const float4* __restrict__ table, short4* __restrict__ out, size_t n4) {
-    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= n4) return;
-    const float4 v = table[t];
-    out[t] = make_short4(static_cast<short>(qat_int127(v.x)), static_cast<short>(qat_int127(v.y)),
-                         static_cast<short>(qat_int127(v.z)), static_cast<short>(qat_int127(v.w)));
 }
 
 // Reference-layout L1 QAT weights [S][O][W] (sfnn_build_quantized_proxy_stacked_
@@ -379,7 +367,7 @@ __global__ void __launch_bounds__(256) ft_forward_kernel(FtArgs a) {
             }
         }
     }
-    float4* out = reinterpret_cast<float4*>(a.l0[v]) + static_cast<size_t>(b) * w4;
+    float4* out = reinterpret_cast<float4*>(v ? a.l0[1] : a.l0[0]) + static_cast<size_t>(b) * w4;
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
         acc[i] = make_float4(crelu01(acc[i].x), crelu01(acc[i].y), crelu01(acc[i].z), crelu01(acc[i].w));
@@ -397,6 +385,107 @@ __global__ void __launch_bounds__(256) ft_forward_kernel(FtArgs a) {
             comb[lane + 32 * i] = make_float4(x0.x * x1.x * kPairScale, x0.y * x1.y * kPairScale,
                                               x0.z * x1.z * kPairScale, x0.w * x1.w * kPairScale);
         }
+    }
+}
+
+// Dense QAT with FT QAT in one gather: the f32 sums of the fake-quantised
+// folded rows (v = q / 127) give the ClippedReLU outputs the backward reads,
+// and the same loaded rows give the engine's integer FT (doubled i16 sums with
+// wrap, clamp [0, 254], (s0 s1) >> 9, over 127; dense_qat_exact_ft_kernel,
+// cu:6344-6390).  q comes back from v exactly without a conversion:
+// fma(v, 127, 1.5 * 2^23) lands in [2^23, 2^24), where the float spacing is 1,
+// on 1.5 * 2^23 + q (|v * 127 - q| <= 0.002), so the low 16 bits of its bit
+// pattern are q's two's complement.  The engine keeps only the sums modulo
+// 2^16: two columns' low halves are packed in one word (byte permute) and
+// summed with a per-half-word add (add.u16x2: no carry between the halves).
+//
+// G warps share a half-position; warp g owns, for every lane, the float4
+// chunks g*C .. g*C+C-1 of the first half of the row and their pair partners
+// H chunks further (H = NCH / 2, C = H / G).  Each row is loaded in R rounds
+// (fewer registers for loads in flight).
+constexpr float kQMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr int kFtIntWarps = 2;          // width 1536: warps per half-position
+constexpr int kFtIntRounds = 1;         // width 1536: load rounds per row
+
+__device__ __forceinline__ unsigned add_u16x2(unsigned a, unsigned b) {
+    unsigned d;
+    asm("add.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned q_pair(float x, float y) {
+    return __byte_perm(__float_as_uint(fmaf(x, 127.0f, kQMagic)), __float_as_uint(fmaf(y, 127.0f, kQMagic)),
+                       0x5410);
+}
+__device__ __forceinline__ unsigned q_pack(int lo, int hi) {
+    return (static_cast<unsigned>(lo) & 0xffffu) | (static_cast<unsigned>(hi) << 16);
+}
+
+template <int NCH, int G, int R>
+__global__ void __launch_bounds__(32 * G * (8 / G)) ft_forward_int_kernel(FtArgs a) {
+    constexpr int H = NCH / 2;
+    constexpr int C = H / G;
+    constexpr int S = 2 * C;   // chunks per warp
+    constexpr int SR = S / R;  // chunks per load round
+    constexpr int P = 8 / G;   // half-positions per CTA
+    static_assert(H % G == 0 && S % R == 0, "chunks must split evenly over warps and rounds");
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int pos = blockIdx.x * P + warp / G;
+    const int g = warp - (warp / G) * G;
+    if (pos >= a.n_half) return;
+    const int h = a.order[pos];
+    const int b = h >> 1, v = h & 1;
+    const int* idx = (v ? a.nstm : a.stm) + static_cast<size_t>(b) * a.max_active;
+    const float4* bias4 = reinterpret_cast<const float4*>(a.bias);
+    auto chunk_of = [&](int s) { return (s < C ? 0 : H) + g * C + (s < C ? s : s - C); };
+    float4 acc[S];
+    uint2 qs[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        acc[s] = __ldg(bias4 + lane + 32 * chunk_of(s));
+        qs[s] = make_uint2(q_pack(qat_int127(acc[s].x), qat_int127(acc[s].y)),
+                           q_pack(qat_int127(acc[s].z), qat_int127(acc[s].w)));
+    }
+    const size_t w4 = static_cast<size_t>(a.width) >> 2;
+    for (int s0 = 0; s0 < a.max_active; s0 += 32) {
+        const int mine = s0 + lane < a.max_active ? __ldg(idx + s0 + lane) : -1;
+        const int n = min(32, a.max_active - s0);
+        for (int u = 0; u < n; ++u) {
+            const int f = __shfl_sync(kFull, mine, u);
+            if (f < 0 || f >= a.n_features) continue;
+            const float4* row = reinterpret_cast<const float4*>(a.table) + static_cast<size_t>(f) * w4;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float4 t[SR];
+#pragma unroll
+                for (int k = 0; k < SR; ++k) t[k] = __ldg(row + lane + 32 * chunk_of(r * SR + k));
+#pragma unroll
+                for (int k = 0; k < SR; ++k) {
+                    const int s = r * SR + k;
+                    acc[s].x += t[k].x;
+                    acc[s].y += t[k].y;
+                    acc[s].z += t[k].z;
+                    acc[s].w += t[k].w;
+                    qs[s].x = add_u16x2(qs[s].x, q_pair(t[k].x, t[k].y));
+                    qs[s].y = add_u16x2(qs[s].y, q_pair(t[k].z, t[k].w));
+                }
+            }
+        }
+    }
+    float4* out = reinterpret_cast<float4*>(v ? a.l0[1] : a.l0[0]) + static_cast<size_t>(b) * w4;
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+        out[lane + 32 * chunk_of(s)] = make_float4(crelu01(acc[s].x), crelu01(acc[s].y), crelu01(acc[s].z),
+                                                   crelu01(acc[s].w));
+    float4* comb = reinterpret_cast<float4*>(a.combined) + static_cast<size_t>(b) * w4 + v * (w4 >> 1);
+    // a 16-bit sum q -> the doubled sum wrapped to i16, clamped to [0, 254]
+    auto clip = [](unsigned q) { return min(254, max(0, static_cast<int>(static_cast<short>(q << 1)))); };
+    auto pair = [&](unsigned q0, unsigned q1) { return qat_on_lattice((clip(q0) * clip(q1)) >> 9); };
+#pragma unroll
+    for (int s = 0; s < C; ++s) {
+        const uint2 q0 = qs[s], q1 = qs[s + C];
+        comb[lane + 32 * (g * C + s)] = make_float4(pair(q0.x & 0xffffu, q1.x & 0xffffu), pair(q0.x >> 16, q1.x >> 16),
+                                                    pair(q0.y & 0xffffu, q1.y & 0xffffu), pair(q0.y >> 16, q1.y >> 16));
     }
 }
 
@@ -418,7 +507,7 @@ __global__ void ft_forward_generic_kernel(FtArgs a) {
         s1 += row[j + half];
     }
     const float x0 = crelu01(s0), x1 = crelu01(s1);
-    float* out = a.l0[v] + static_cast<size_t>(b) * a.width;
+    float* out = (v ? a.l0[1] : a.l0[0]) + static_cast<size_t>(b) * a.width;
     out[j] = x0;
     out[j + half] = x1;
     if (a.combined != nullptr) a.combined[static_cast<size_t>(b) * a.width + v * half + j] = pair_out(x0, x1, a.lattice);
@@ -446,70 +535,6 @@ __global__ void qat_exact_ft_kernel(FtArgs a) {
     const int x0 = min(254, max(0, static_cast<int>(static_cast<short>(s0))));
     const int x1 = min(254, max(0, static_cast<int>(static_cast<short>(s1))));
     a.combined[static_cast<size_t>(b) * a.width + v * half + j] = qat_on_lattice((x0 * x1) >> 9);
-}
-
-// The same from the i16 table, one warp per half-position in king order
-// (W % 512 == 0): lane owns columns 256 k + 8 lane + e, 16-byte loads; chunk k
-// pairs with chunk k + NCH / 2.  Only the sums modulo 2^16 matter (the engine
-// wraps them to i16), so each 32-bit word of two columns is added whole into
-// `lo` (its low half is the even column's sum) and shifted into `hi` (the odd
-// column's): one shift and two adds per two columns.
-template <int NCH>
-__global__ void __launch_bounds__(256) qat_exact_ft16_kernel(FtArgs a, const short* __restrict__ table16) {
-    const int lane = threadIdx.x & 31;
-    const int pos = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (pos >= a.n_half) return;
-    const int h = a.order[pos];
-    const int b = h >> 1, v = h & 1;
-    const int* idx = (v ? a.nstm : a.stm) + static_cast<size_t>(b) * a.max_active;
-    unsigned lo[NCH][4], hi[NCH][4];
-#pragma unroll
-    for (int k = 0; k < NCH; ++k)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            lo[k][c] = static_cast<unsigned>(qat_int127(a.bias[256 * k + 8 * lane + 2 * c]));
-            hi[k][c] = static_cast<unsigned>(qat_int127(a.bias[256 * k + 8 * lane + 2 * c + 1]));
-        }
-    for (int s0 = 0; s0 < a.max_active; s0 += 32) {
-        const int mine = s0 + lane < a.max_active ? __ldg(idx + s0 + lane) : -1;
-        const int n = min(32, a.max_active - s0);
-        for (int u = 0; u < n; ++u) {
-            const int f = __shfl_sync(kFull, mine, u);
-            if (f < 0 || f >= a.n_features) continue;
-            const short* row = table16 + static_cast<size_t>(f) * a.width + 8 * lane;
-            uint4 r[NCH];
-#pragma unroll
-            for (int k = 0; k < NCH; ++k) r[k] = __ldg(reinterpret_cast<const uint4*>(row + 256 * k));
-#pragma unroll
-            for (int k = 0; k < NCH; ++k) {
-                lo[k][0] += r[k].x;
-                hi[k][0] += r[k].x >> 16;
-                lo[k][1] += r[k].y;
-                hi[k][1] += r[k].y >> 16;
-                lo[k][2] += r[k].z;
-                hi[k][2] += r[k].z >> 16;
-                lo[k][3] += r[k].w;
-                hi[k][3] += r[k].w >> 16;
-            }
-        }
-    }
-    float* out = a.combined + static_cast<size_t>(b) * a.width + v * (a.width / 2) + 8 * lane;
-#pragma unroll
-    for (int k = 0; k < NCH / 2; ++k) {
-        float c[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const unsigned s0w = (q & 1) ? hi[k][q >> 1] : lo[k][q >> 1];
-            const unsigned s1w = (q & 1) ? hi[k + NCH / 2][q >> 1] : lo[k + NCH / 2][q >> 1];
-            // doubled sums wrapped to i16, clamped to [0, 254]
-            const int x0 = min(254, max(0, static_cast<int>(static_cast<short>(s0w << 1))));
-            const int x1 = min(254, max(0, static_cast<int>(static_cast<short>(s1w << 1))));
-            c[q] = qat_on_lattice((x0 * x1) >> 9);
-        }
-        float4* o4 = reinterpret_cast<float4*>(out + 256 * k);
-        o4[0] = make_float4(c[0], c[1], c[2], c[3]);
-        o4[1] = make_float4(c[4], c[5], c[6], c[7]);
-    }
 }
 
 // ------------------------------------------------------------------ L1
@@ -1179,7 +1204,7 @@ __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
         dw[o] = 0.0f;
     }
     float p0sum = 0.0f, p1sum = 0.0f;
-    const float* x = a.l0[v];
+    const float* x = v ? a.l0[1] : a.l0[0];
     for (int q0 = 0; q0 < n; q0 += kU) {
         // Issue the loads of kU samples before using any of them.
         float xa[kU], xb[kU], cc[kU];
@@ -1219,10 +1244,12 @@ __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
             if (a.combined_gradients != nullptr) {
                 const size_t row = static_cast<size_t>(bs[q]) * W;
                 a.combined_gradients[row + i] = dc;
-                a.l0_gradients[v][row + j] = u0;
-                a.l0_gradients[v][row + j + half] = u1;
-                a.pre_gradients[v][row + j] = p0;
-                a.pre_gradients[v][row + j + half] = p1;
+                float* lg = v ? a.l0_gradients[1] : a.l0_gradients[0];
+                float* pg = v ? a.pre_gradients[1] : a.pre_gradients[0];
+                lg[row + j] = u0;
+                lg[row + j + half] = u1;
+                pg[row + j] = p0;
+                pg[row + j + half] = p1;
             }
             p0sum += p0;
             p1sum += p1;
@@ -1703,7 +1730,7 @@ int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec,
     // Persistent grid: three CTAs per SM, each warp loops over (piece, column
     // group) work items.
     const int warps = a.pieces * a.col_groups;
-    const int blocks = std::max(1, std::min((warps + kPieceRowWarps - 1) / kPieceRowWarps, 3 * ctx->sm_count));
+    const int blocks = std::max(1, std::min((warps + kPieceRowWarps - 1) / kPieceRowWarps, kPieceRowCtas * ctx->sm_count));
     float* const gradients = a.gradients;
     for (int k0 = 0, j = 0; k0 < a.kings; k0 += kKingsPerLaunch, ++j) {
         a.king_begin = k0;
@@ -1803,7 +1830,6 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, con
 // ------------------------------------------------------------------ host plan
 struct SfnnPlan {
     const float* table;    // what the FT gather reads
-    const short* table16;  // dense QAT with FT QAT: the table's integers, when the fold wrote them
     const float* ft_bias;  // FT bias the gather starts from (fake-quantised under FT QAT)
     KingSortOut king;
     int* king_rank;
@@ -1859,21 +1885,11 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
             if (scratch_slot(ctx, kScratchSfnnFold, n * sizeof(float), &p, "cudaMalloc SFNN folded FT") != 0) return -1;
             folded = static_cast<float*>(p);
         }
-        plan->table16 = nullptr;
         if (d.width % 4 == 0 && aligned16(w.l0w) && aligned16(folded)) {
-            short* t16 = nullptr;
-            if (d.qat.integer_ft && d.width % 512 == 0 && d.width <= 2560) {
-                void* tp = nullptr;
-                if (scratch_slot(ctx, kScratchSfnnQatTable, n * sizeof(short), &tp,
-                                 "cudaMalloc SFNN QAT i16 table") != 0)
-                    return -1;
-                t16 = static_cast<short*>(tp);
-                plan->table16 = t16;
-            }
             if (grid_1d(n / 4, threads, &blocks, "SFNN FT QAT fold") != 0) return -1;
             fold_ft_qat4_kernel<<<blocks, threads, 0, ctx->stream>>>(
-                reinterpret_cast<const float4*>(w.l0w), reinterpret_cast<float4*>(folded),
-                reinterpret_cast<short4*>(t16), n / 4, d.width / 4, d.base, d.ft_alpha);
+                reinterpret_cast<const float4*>(w.l0w), reinterpret_cast<float4*>(folded), n / 4, d.width / 4,
+                d.base, d.ft_alpha);
         } else {
             if (grid_1d(n, threads, &blocks, "SFNN FT QAT fold") != 0) return -1;
             fold_ft_qat_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l0w, folded, n, d.width, d.base, d.ft_alpha);
@@ -1992,15 +2008,44 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
 int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnPlan& plan, const int* stm,
                       const int* nstm, const float* l0b, const SfnnActivations& act) {
     if (d.qat.dense && d.qat.integer_ft) {
-        // The f32 FT pass keeps the activations the backward uses; combined is
-        // then overwritten by the engine's integer FT (cu:6654-6662).
+        // One gather for both outputs where the width has a warp kernel: the
+        // f32 ClippedReLU activations (kept for the backward) and the engine's
+        // integer FT into combined (cu:6654-6662).
+        const bool fused_al = aligned16(plan.table) && aligned16(l0b) && aligned16(act.stm_l0) &&
+                              aligned16(act.nstm_l0) && aligned16(act.combined);
+        if (fused_al && ft_warp_width(d.width)) {
+            FtArgs fa{};
+            fa.order = plan.king.order;
+            fa.stm = stm;
+            fa.nstm = nstm;
+            fa.table = plan.table;
+            fa.bias = l0b;
+            fa.l0[0] = act.stm_l0;
+            fa.l0[1] = act.nstm_l0;
+            fa.combined = act.combined;
+            fa.n_half = 2 * d.batch;
+            fa.max_active = d.max_active;
+            fa.n_features = d.n_features;
+            fa.width = d.width;
+            constexpr int G = kFtIntWarps, P = 8 / kFtIntWarps;
+            switch (d.width) {
+                case 256: ft_forward_int_kernel<2, 1, 1><<<(fa.n_half + 7) / 8, 256, 0, ctx->stream>>>(fa); break;
+                case 512: ft_forward_int_kernel<4, 1, 1><<<(fa.n_half + 7) / 8, 256, 0, ctx->stream>>>(fa); break;
+                case 1024: ft_forward_int_kernel<8, 2, 1><<<(fa.n_half + 3) / 4, 256, 0, ctx->stream>>>(fa); break;
+                case 1536:
+                    ft_forward_int_kernel<12, G, kFtIntRounds><<<(fa.n_half + P - 1) / P, 32 * G * P, 0, ctx->stream>>>(
+                        fa);
+                    break;
+                default: ft_forward_int_kernel<18, 3, 1><<<(fa.n_half + 1) / 2, 192, 0, ctx->stream>>>(fa); break;
+            }
+            return check_launch("SFNN dense QAT FT launch");
+        }
+        // Other widths: the f32 pass keeps the activations the backward uses,
+        // then combined is overwritten by the engine's integer FT.
         SfnnDims df = d;
         df.qat.integer_ft = 0;
         df.qat.dense = 0;
-        SfnnActivations fact = act;
-        if (ft_warp_width(d.width)) fact.combined = nullptr;  // written by the integer FT below
-        if (launch_ft_forward(ctx, df, plan, stm, nstm, l0b, fact) != 0) return -1;
-        prof_mark(ctx);  // stage profiler: the integer FT is its own phase
+        if (launch_ft_forward(ctx, df, plan, stm, nstm, l0b, act) != 0) return -1;
         FtArgs ea{};
         ea.stm = stm;
         ea.nstm = nstm;
@@ -2012,31 +2057,6 @@ int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const Sfnn
         ea.n_features = d.n_features;
         ea.width = d.width;
         ea.order = plan.king.order;
-        if (d.width % 512 == 0 && d.width <= 2560 && aligned16(plan.table) && aligned16(act.combined)) {
-            const short* t16 = plan.table16;
-            if (t16 == nullptr) {
-                // The table came from the caller (reference entry): take its integers.
-                const size_t n = static_cast<size_t>(d.n_features) * d.width;
-                void* tp = nullptr;
-                if (scratch_slot(ctx, kScratchSfnnQatTable, n * sizeof(short), &tp,
-                                 "cudaMalloc SFNN QAT i16 table") != 0)
-                    return -1;
-                int blocks = 0;
-                if (grid_1d(n / 4, 256, &blocks, "SFNN QAT i16 table") != 0) return -1;
-                qat_table16_kernel<<<blocks, 256, 0, ctx->stream>>>(reinterpret_cast<const float4*>(plan.table),
-                                                                      static_cast<short4*>(tp), n / 4);
-                t16 = static_cast<const short*>(tp);
-            }
-            const int hb = (ea.n_half + 7) / 8;
-            switch (d.width / 256) {
-                case 2: qat_exact_ft16_kernel<2><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
-                case 4: qat_exact_ft16_kernel<4><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
-                case 6: qat_exact_ft16_kernel<6><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
-                case 8: qat_exact_ft16_kernel<8><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
-                default: qat_exact_ft16_kernel<10><<<hb, 256, 0, ctx->stream>>>(ea, t16); break;
-            }
-            return check_launch("SFNN exact QAT FT launch");
-        }
         int gb = 0;
         if (grid_1d(static_cast<size_t>(ea.n_half) * (d.width / 2), 256, &gb, "SFNN exact QAT FT") != 0) return -1;
         qat_exact_ft_kernel<<<gb, 256, 0, ctx->stream>>>(ea);
@@ -2359,7 +2379,7 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
               float* const* sm, float* output, float* per_sample, float* mog, float* weighted_sum, float* mean,
               float* ft_grad, float* dense_grad, const size_t* row_shift = nullptr,
               const cudaEvent_t* row_events = nullptr) {
-    ctx->prof_marks_per_step = (d.qat.dense && d.qat.integer_ft) ? 10 : 9;
+    ctx->prof_marks_per_step = 9;
     prof_mark(ctx);
     SfnnPlan plan{};
     if (sfnn_prepare(ctx, d, w, stm, nstm, buckets, nullptr, &plan) != 0) return -1;
