@@ -945,7 +945,7 @@ def sfnn_records_e2e(args, ctx, upload_ctx, runner, step, loss_kind, inv):
     d1.synchronize()
     decode_ms = d1.elapsed_ms_since(d0) / reps
     steps = args.steps
-    ring = [PinnedF32Buffer(ctx, 1) for _ in range(steps)]
+    ring = [PinnedF32Buffer(ctx, 1) for _ in range(max(steps, 3))]
     for i in range(3):
         step += 1
         runner.step_pipelined_records(ctx, upload_ctx, producer, ranger(step), loss_kind, inv, None, True,

@@ -113,7 +113,7 @@ enum ScratchSlot : int {
     kScratchSfnnQuant = 21,     // SFNN integer forward: FT pair values + king sort
     kScratchSfnnQat = 22,       // SFNN QAT: quantised L1 bias, integer biases, raw L1 / L2 sums
     kScratchSfnnQatFt = 23,     // SFNN QAT: fake-quantised FT bias
-    kScratchSfnnQatTable = 24,  // (unused)
+    kScratchSfnnHeavyMma = 24,  // SFNN FT rows: tensor-core heavy-key plan and sums
     kScratchNnueQuant = 25,     // integer HalfKP forward: transformed features (u8)
     kScratchSfnnHeavy = 26,     // SFNN FT rows: segment plan and partial sums of heavy rows
     kScratchHcpe = 27,          // HCPE -> PackedSfenValue: uncompacted records, valid flags, scan

@@ -34,6 +34,7 @@
 #include <climits>
 #include <cstring>
 
+#include "ft_rows_mma.cuh"
 #include "king_sort.cuh"
 #include "sfnn.cuh"
 #include "sparse_rows.cuh"
@@ -1152,6 +1153,8 @@ struct L1BackArgs {
     const float* combined;  // dense QAT: the lattice FT output (dL1w uses it); null: recomputed
     // fused step: pre-activation gradients in king order, row rank[h]
     float* pregrad_sorted;
+    __nv_bfloat16* pregrad_hi;  // optional: the same rows as bf16 planes G = hi + lo (tensor-core heavy keys)
+    __nv_bfloat16* pregrad_lo;
     const int* rank;
     // reference backward buffers (null in the fused step)
     float* combined_gradients;
@@ -1237,9 +1240,17 @@ __global__ void __launch_bounds__(256) l1_backward_kernel(L1BackArgs a) {
             const float u0 = pg * x1, u1 = pg * x0;
             const float p0 = crelu_grad(x0, u0), p1 = crelu_grad(x1, u1);
             if (a.pregrad_sorted != nullptr) {
-                float* pr = a.pregrad_sorted + static_cast<size_t>(rs[2 * q + v]) * W;
+                const size_t ro = static_cast<size_t>(rs[2 * q + v]) * W;
+                float* pr = a.pregrad_sorted + ro;
                 pr[j] = p0;
                 pr[j + half] = p1;
+                if (a.pregrad_hi != nullptr) {
+                    const __nv_bfloat16 h0 = __float2bfloat16_rn(p0), h1 = __float2bfloat16_rn(p1);
+                    a.pregrad_hi[ro + j] = h0;
+                    a.pregrad_hi[ro + j + half] = h1;
+                    a.pregrad_lo[ro + j] = __float2bfloat16_rn(p0 - __bfloat162float(h0));
+                    a.pregrad_lo[ro + j + half] = __float2bfloat16_rn(p1 - __bfloat162float(h1));
+                }
             }
             if (a.combined_gradients != nullptr) {
                 const size_t row = static_cast<size_t>(bs[q]) * W;
@@ -1404,6 +1415,10 @@ struct PieceRowArgs {
     int heavy_row;               // rows with more entries are heavy
     int heavy_seg;               // entries per segment
     int heavy_ok;                // the plan fit the scratch (read on the device as well)
+    // Heavy keys summed on the tensor cores (ft_rows_mma.cu): slot of each key
+    // (-1: light) and the sums [slot][width]; null: the segment plan above.
+    const int* key_slot;
+    const float* key_partials;
 };
 
 constexpr int kHeavyRow = 128;  // FT row phase on king-concentrated batches: 512 -> 3.75 ms, 128 -> 3.03 ms
@@ -1570,6 +1585,7 @@ __device__ __forceinline__ void piece_rows(const PieceRowArgs& a, int gw, int la
             if (n == 0) continue;
             total += n;
             const int* elist = a.entries + beg;  // ascending up to kSortCap entries (sort_inverse_index)
+            const int slot = a.key_slot != nullptr ? __ldg(a.key_slot + key) : -1;
             int hs = -1;
             if (a.heavy_off != nullptr) {
                 const int s0 = __ldg(a.heavy_off + key), s1 = __ldg(a.heavy_off + key + 1);
@@ -1579,7 +1595,14 @@ __device__ __forceinline__ void piece_rows(const PieceRowArgs& a, int gw, int la
             for (int it = 0; it < ITERS; ++it) {
                 const int c = lane_col<VEC>(c0, it, lane);
                 const bool active = c < c_end;
-                if (hs >= 0) {
+                if (slot >= 0) {
+                    if (active) {
+                        float x[VEC];
+                        ldv<VEC>(a.key_partials + static_cast<size_t>(slot) * a.width + c, x);
+#pragma unroll
+                        for (int e = 0; e < VEC; ++e) acc[it][e] += x[e];
+                    }
+                } else if (hs >= 0) {
                     const int nseg = (n + a.heavy_seg - 1) / a.heavy_seg;
                     if (active) {
                         for (int sg = 0; sg < nseg; ++sg) {
@@ -1752,8 +1775,78 @@ int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec,
     return 0;
 }
 
+// Inputs of the tensor-core heavy-key sums (fused step only): the batch, the
+// king sort and the gradient rows as bf16 planes.
+struct HeavyMmaInputs {
+    const int* rank_base;  // king sort key offsets
+    const int* order;      // rank -> half-position
+    const int* stm;
+    const int* nstm;
+    int max_active;
+    int max_tiles;
+    int rows;
+    const __nv_bfloat16* hi;
+    const __nv_bfloat16* lo;
+};
+
+// The tensor-core plan in its scratch slot; false when it does not apply.
+int plan_heavy_mma(BulletOuCudaCppContext* ctx, const PieceRowArgs& a, const HeavyMmaInputs& in, HeavyMmaArgs* m) {
+    const size_t keys = static_cast<size_t>(in.max_tiles) * a.pieces;
+    const size_t max_slots = heavy_mma_max_slots(a.max_entries, kHeavyMmaThreshold);
+    const size_t max_work = heavy_mma_max_work(in.max_tiles, max_slots, a.width);
+    const size_t max_mblocks = heavy_mma_max_mblocks(in.max_tiles, max_slots);
+    const size_t ints = align_floats(2 * keys + 5 * static_cast<size_t>(in.max_tiles) + 2 + 2 * max_work + 3);
+    const size_t part = align_floats(max_slots * static_cast<size_t>(a.width));
+    const size_t inc = heavy_mma_incidence_bytes(max_mblocks);
+    void* p = nullptr;
+    const bool fresh = ctx->scratch[kScratchSfnnHeavyMma].bytes == 0;
+    if (scratch_slot(ctx, kScratchSfnnHeavyMma, (ints + part) * sizeof(float) + inc, &p,
+                     "cudaMalloc SFNN heavy-key tensor-core plan") != 0)
+        return -1;
+    int* q = static_cast<int*>(p);
+    HeavyMmaPlan& pl = m->plan;
+    pl.key_local = q;
+    pl.key_slot = q + keys;
+    pl.tile_heavy = q + 2 * keys;
+    pl.tile_slot = pl.tile_heavy + in.max_tiles;
+    pl.tile_r0 = pl.tile_slot + in.max_tiles + 1;
+    pl.tile_r1 = pl.tile_r0 + in.max_tiles;
+    pl.tile_mb = pl.tile_r1 + in.max_tiles;
+    pl.work = pl.tile_mb + in.max_tiles + 1;
+    pl.n_work = pl.work + 2 * max_work;
+    pl.n_slots = pl.n_work + 1;
+    pl.error = pl.n_slots + 1;
+    pl.partials = reinterpret_cast<float*>(q) + ints;
+    pl.incidence = reinterpret_cast<float*>(q) + ints + part;
+    pl.max_slots = static_cast<int>(std::min<size_t>(max_slots, INT_MAX));
+    pl.max_mblocks = static_cast<int>(std::min<size_t>(max_mblocks, INT_MAX));
+    pl.max_work = static_cast<int>(std::min<size_t>(max_work, INT_MAX));
+    if (fresh) {
+        const cudaError_t st = cudaMemsetAsync(pl.error, 0, sizeof(int), ctx->stream);
+        if (st != cudaSuccess) return fail("cudaMemsetAsync heavy-key error word", st);
+    }
+    m->offsets = a.offsets;
+    m->tile_base = a.tile_base;
+    m->rank_base = in.rank_base;
+    m->rank_base_end = 0;
+    m->kings = a.kings;
+    m->pieces = a.pieces;
+    m->tile_ranks = kTileRanks;
+    m->max_tiles = in.max_tiles;
+    m->threshold = kHeavyMmaThreshold;
+    m->order = in.order;
+    m->stm = in.stm;
+    m->nstm = in.nstm;
+    m->max_active = in.max_active;
+    m->hi = in.hi;
+    m->lo = in.lo;
+    m->rows = in.rows;
+    m->width = a.width;
+    return 0;
+}
+
 int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, const size_t* row_shift = nullptr,
-                      const cudaEvent_t* events = nullptr) {
+                      const cudaEvent_t* events = nullptr, const HeavyMmaInputs* mma = nullptr) {
     bool al = aligned16(a.src[0]) && aligned16(a.src[1]) && a.src_stride % 4 == 0;
     if (mode == kRowRanger)
         al = al && aligned16(a.weights) && aligned16(a.momentum) && aligned16(a.velocity) && aligned16(a.slow);
@@ -1779,7 +1872,16 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, con
         a.vacc = static_cast<float*>(vp);
         a.vany = reinterpret_cast<int*>(a.vacc + vf);
     }
-    {
+    const bool use_mma = mma != nullptr && vec == 8 && a.tile_base != nullptr && a.kings > 1 &&
+                         heavy_mma_supported(a.width) && a.pieces <= 2048;
+    if (use_mma) {
+        // heavy keys on the tensor cores; the row kernel adds their sums
+        HeavyMmaArgs m{};
+        if (plan_heavy_mma(ctx, a, *mma, &m) != 0 || launch_heavy_key_mma(ctx, m) != 0) return -1;
+        a.key_slot = m.plan.key_slot;
+        a.key_partials = m.plan.partials;
+        a.heavy_off = nullptr;
+    } else {
         // Heavy-row segments: counts, their exclusive scan, the segment sums.
         // Segments <= entries / heavy_seg + the keys of heavy rows (each key adds
         // at most one partial segment) <= entries / heavy_seg + n_keys.
@@ -2325,29 +2427,35 @@ SfnnWeights weights_from(const BulletOuCudaCppF32Buffer* const* p) {
 struct StepBuffers {
     SfnnActivations act;
     float* pregrad;
+    __nv_bfloat16* pregrad_hi;  // null unless the heavy keys go to the tensor cores
+    __nv_bfloat16* pregrad_lo;
 };
 
 int step_buffers(BulletOuCudaCppContext* ctx, const SfnnDims& d, float* output, StepBuffers* sb) {
     const size_t BW = static_cast<size_t>(d.batch) * d.width;
-    const size_t sizes[7] = {align_floats(BW),
+    const bool planes = heavy_mma_supported(d.width) && d.base > 0;
+    const size_t sizes[8] = {align_floats(BW),
                              align_floats(BW),
                              align_floats(BW),
                              align_floats(static_cast<size_t>(d.batch) * d.l1_out),
                              align_floats(static_cast<size_t>(d.batch) * d.l2_in),
                              align_floats(static_cast<size_t>(d.batch) * d.l2_size),
-                             align_floats(2 * BW)};
+                             align_floats(2 * BW),
+                             planes ? align_floats(2 * BW) : 0};  // bf16 hi and lo planes of the pregrad rows
     size_t total = 0;
     for (size_t s : sizes) total += s;
     void* p = nullptr;
     if (scratch_slot(ctx, kScratchSfnnStep, total * sizeof(float), &p, "cudaMalloc SFNN step buffers") != 0) return -1;
     float* f = static_cast<float*>(p);
-    float* ptrs[7];
-    for (int i = 0; i < 7; ++i) {
+    float* ptrs[8];
+    for (int i = 0; i < 8; ++i) {
         ptrs[i] = f;
         f += sizes[i];
     }
     sb->act = SfnnActivations{ptrs[0], ptrs[1], ptrs[2], ptrs[3], ptrs[4], ptrs[5], output};
     sb->pregrad = ptrs[6];
+    sb->pregrad_hi = planes ? reinterpret_cast<__nv_bfloat16*>(ptrs[7]) : nullptr;
+    sb->pregrad_lo = planes ? sb->pregrad_hi + 2 * BW : nullptr;
     return 0;
 }
 
@@ -2408,6 +2516,8 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
     lb.l0[0] = sb.act.stm_l0;
     lb.l0[1] = sb.act.nstm_l0;
     lb.pregrad_sorted = sb.pregrad;
+    lb.pregrad_hi = sb.pregrad_hi;
+    lb.pregrad_lo = sb.pregrad_lo;
     lb.rank = plan.king_rank;
     lb.combined = d.qat.dense ? sb.act.combined : nullptr;
     if (launch_l1_backward(ctx, d, plan, lb) != 0) return -1;
@@ -2445,6 +2555,9 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
     r.src[0] = sb.pregrad;
     r.src[1] = sb.pregrad + d.width;
     r.src_stride = 2 * static_cast<size_t>(d.width);
+    const HeavyMmaInputs mma{plan.king.key_off, plan.king.order, stm, nstm, d.max_active, plan.max_king_tiles,
+                             2 * d.batch, sb.pregrad_hi, sb.pregrad_lo};
+    const HeavyMmaInputs* mp = sb.pregrad_hi != nullptr ? &mma : nullptr;
     if (ranger != nullptr) {
         r.weights = wm[0];
         r.momentum = mm[0];
@@ -2452,10 +2565,10 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
         r.slow = sm[0];
         r.ranger = ra;
         r.skip_quiet = ranger_zero_step_is_identity(ra) ? 1 : 0;
-        if (launch_piece_rows(ctx, kRowRanger, r) != 0) return -1;
+        if (launch_piece_rows(ctx, kRowRanger, r, nullptr, nullptr, mp) != 0) return -1;
     } else {
         r.gradients = ft_grad;
-        if (launch_piece_rows(ctx, kRowWrite, r, row_shift, row_events) != 0) return -1;
+        if (launch_piece_rows(ctx, kRowWrite, r, row_shift, row_events, mp) != 0) return -1;
     }
     prof_mark(ctx);
     return 0;
