@@ -224,6 +224,7 @@ __global__ void heavy_plan_scan_kernel(HeavyMmaArgs a) {
     a.plan.tile_mb[a.max_tiles] = mbs;
     a.plan.n_work[0] = work;
     a.plan.n_slots[0] = slots;
+    a.plan.next_work[0] = 0;
 }
 
 // Global slot of every key (-1: light).
@@ -334,7 +335,13 @@ __global__ void __launch_bounds__(kThreads, 1) heavy_key_mma_kernel(const __grid
     int loads = 0;                            // bit s: loads issued on stage s not yet waited for
     const uint8_t* const inc = reinterpret_cast<const uint8_t*>(a.plan.incidence);
 
-    for (int w = blockIdx.x; w < n_work; w += gridDim.x) {
+    int* const next = abort_flag + 1;  // the work item this CTA takes next
+    if (tid == 0) *next = atomicAdd(a.plan.next_work, 1);
+    __syncthreads();
+    for (;;) {
+        const int w = *next;
+        __syncthreads();  // every thread has read `next` before thread 0 fetches the following item
+        if (w >= n_work) break;
         const int t = a.plan.work[2 * w];
         const int packed = a.plan.work[2 * w + 1];
         const int m0 = packed >> 16, nmb = (packed >> 8) & 0xff, grp = packed & 0xff;
@@ -402,6 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) heavy_key_mma_kernel(const __grid
             ok = ok && retire(0) && retire(1);  // accumulators complete
             if (!ok) *abort_flag = 1;
         }
+        if (tid == 0) *next = atomicAdd(a.plan.next_work, 1);  // read after the barrier below
         __syncthreads();
         if (*abort_flag) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");

@@ -19,6 +19,7 @@ struct HeavyMmaPlan {
     int* work;         // [2 * max_work] tile, (first M-block << 16) | (M-blocks << 8) | column group
     int* n_work;       // device scalar
     int* n_slots;      // device scalar
+    int* next_work;    // device scalar: dynamic work counter of the MMA kernel
     int* error;        // sticky: a bounded wait timed out
     float* partials;   // [max_slots][width] sums of the heavy keys
     void* incidence;   // [max_mblocks][64 chunks][16 KB] 0/1 key x rank operand, bf16, MMA layout

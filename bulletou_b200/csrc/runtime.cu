@@ -424,6 +424,15 @@ int bulletou_b200_profile_end(BulletOuCudaCppContext* ctx, float* ms_out, size_t
     return ok();
 }
 
+int bulletou_b200_context_scratch_bytes(const BulletOuCudaCppContext* ctx, size_t* out) {
+    if (validate_context(ctx) != 0) return -1;
+    if (out == nullptr) return fail_message("context_scratch_bytes: output must not be null");
+    size_t total = 0;
+    for (const Scratch& s : ctx->scratch) total += s.bytes;
+    *out = total;
+    return ok();
+}
+
 int bulletou_b200_l2_read_probe(BulletOuCudaCppContext* ctx, const BulletOuCudaCppF32Buffer* buffer, size_t len,
                                 int passes, BulletOuCudaCppF32Buffer* sink) {
     if (validate_f32(ctx, buffer, len, "L2 probe buffer") != 0) return -1;

@@ -1795,7 +1795,7 @@ int plan_heavy_mma(BulletOuCudaCppContext* ctx, const PieceRowArgs& a, const Hea
     const size_t max_slots = heavy_mma_max_slots(a.max_entries, kHeavyMmaThreshold);
     const size_t max_work = heavy_mma_max_work(in.max_tiles, max_slots, a.width);
     const size_t max_mblocks = heavy_mma_max_mblocks(in.max_tiles, max_slots);
-    const size_t ints = align_floats(2 * keys + 5 * static_cast<size_t>(in.max_tiles) + 2 + 2 * max_work + 3);
+    const size_t ints = align_floats(2 * keys + 5 * static_cast<size_t>(in.max_tiles) + 2 + 2 * max_work + 4);
     const size_t part = align_floats(max_slots * static_cast<size_t>(a.width));
     const size_t inc = heavy_mma_incidence_bytes(max_mblocks);
     void* p = nullptr;
@@ -1815,7 +1815,8 @@ int plan_heavy_mma(BulletOuCudaCppContext* ctx, const PieceRowArgs& a, const Hea
     pl.work = pl.tile_mb + in.max_tiles + 1;
     pl.n_work = pl.work + 2 * max_work;
     pl.n_slots = pl.n_work + 1;
-    pl.error = pl.n_slots + 1;
+    pl.next_work = pl.n_slots + 1;
+    pl.error = pl.next_work + 1;
     pl.partials = reinterpret_cast<float*>(q) + ints;
     pl.incidence = reinterpret_cast<float*>(q) + ints + part;
     pl.max_slots = static_cast<int>(std::min<size_t>(max_slots, INT_MAX));

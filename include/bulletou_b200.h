@@ -97,6 +97,11 @@ int bulletou_b200_profile_begin(BulletOuCudaCppContext* ctx, size_t max_marks);
 int bulletou_b200_profile_end(BulletOuCudaCppContext* ctx, float* ms_out, size_t ms_len, size_t* steps_out,
     size_t* phases_out);
 
+/* Device bytes the context currently holds in its grow-only scratch slots
+ * (no counterpart in the reference; diagnostics).  The slots are allocated on
+ * first use by the entries that need scratch and freed at context destroy. */
+int bulletou_b200_context_scratch_bytes(const BulletOuCudaCppContext* ctx, size_t* out);
+
 /* L2 read-bandwidth probe (no counterpart in the reference; measurement
  * only): `passes` reads of buffer[0, len) with 16-byte loads cached in L2
  * only, by 4 * SMs CTAs of 512 threads; sink receives one float per thread
@@ -141,10 +146,13 @@ int bulletou_b200_nnue_train_step_device(
  * positions are accepted (anything larger is rejected with an error).  Its
  * scratch is one static device array of 1.2 MB that every GPU loading the
  * library holds until exit; the first call on a device looks up that array's
- * device address (make that first call before any stream capture).  Nothing
- * in the array needs clearing between calls, but all calls on a device share
- * it: calls whose work overlaps on the GPU (other streams, other threads)
- * race and must be serialized by the caller. */
+ * device address (make that first call before any stream capture); the
+ * address is kept for the life of the process, so it is stale once the
+ * device's primary context is destroyed (cudaDeviceReset): do not call this
+ * entry after a device reset in the same process.  Nothing in the array needs
+ * clearing between calls, but all calls on a device share it: calls whose work
+ * overlaps on the GPU (other streams, other threads) race and must be
+ * serialized by the caller. */
 int bulletou_b200_nnue_forward_device_noalloc(
     BulletOuCudaCppContext* ctx, size_t input_size, size_t l1, size_t l2, size_t l3,
     size_t batch, size_t max_active,

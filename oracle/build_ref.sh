@@ -14,10 +14,14 @@
 # tests/ (GPU parity against the reference kernels) and by
 # `bench.py --impl reference` (the reference backend timed on the same GPU).
 #
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]
+# Usage: oracle/build_ref.sh REFERENCE_ROOT   (or BULLETOU_REFERENCE_ROOT set)
 set -euo pipefail
 here="$(cd "$(dirname "$0")" && pwd)"
-ref_root="${1:-${BULLETOU_REFERENCE_ROOT:-/root/reference}}"
+ref_root="${1:-${BULLETOU_REFERENCE_ROOT:-}}"
+if [[ -z "$ref_root" ]]; then
+    echo "usage: oracle/build_ref.sh REFERENCE_ROOT (or set BULLETOU_REFERENCE_ROOT)" >&2
+    exit 2
+fi
 src="$ref_root/crates/cuda_cpp/cpp/bulletou_cuda_backend.cu"
 out_dir="$here/_ref"
 out="$out_dir/libref_cudacpp.so"

@@ -49,6 +49,39 @@ def test_no_alloc_forward_matches_regular_forward_twice():
     ctx.close()
 
 
+def _scratch_bytes(lib, ctx):
+    import ctypes
+
+    n = ctypes.c_size_t(0)
+    lib.call("bulletou_b200_context_scratch_bytes", ctx.as_ptr(), ctypes.byref(n))
+    return n.value
+
+
+def test_no_alloc_forward_allocates_nothing_on_a_fresh_context():
+    """On a context no other entry point has used, the allocation-free forward
+    leaves the context's scratch empty, while the regular forward then has to
+    allocate its king-sort scratch."""
+    lib = bo.library()
+    ctx = bo.Context(0, lib)
+    w = synthetic.halfkp_weights(synthetic.rng_for(33))
+    wb = [bo.F32Buffer.from_host(ctx, a) for a in bo.NnueForwardHostWeights(SHAPE, **w).arrays()]
+    b = synthetic.halfkp_batch(43, 2048)
+    s, n = bo.I32Buffer.from_host(ctx, b["stm"]), bo.I32Buffer.from_host(ctx, b["nstm"])
+    ws = NnueForwardWorkspace(ctx, SHAPE, 2048)
+    assert _scratch_bytes(lib, ctx) == 0
+    for _ in range(2):
+        _call(lib, "bulletou_b200_nnue_forward_device_noalloc", ctx, 2048, 38, s, n, wb, ws)
+        ctx.synchronize()
+        assert _scratch_bytes(lib, ctx) == 0
+    first = _outputs(ws)
+    _call(lib, "bulletou_cuda_cpp_nnue_forward_device", ctx, 2048, 38, s, n, wb, ws)
+    assert _scratch_bytes(lib, ctx) > 0
+    again = _outputs(ws)
+    for k in first:
+        assert np.array_equal(first[k], again[k]), k
+    ctx.close()
+
+
 def test_no_alloc_forward_rejects_oversized_batch():
     lib = bo.library()
     ctx = bo.Context(0, lib)
