@@ -78,11 +78,12 @@ K9K9_GLOBAL_BATCH = 262144
 SFNN_N_BATCHES = 4
 SFNN_METRIC = "train positions/sec (SFNN HalfKA_hm2 1536x2 LayerStack k3k3 15+1-32-1, batch 65536 per GPU)"
 K9K9_METRIC = "train positions/sec (SFNN HalfKA_hm2 1536x2 LayerStack k9k9 15+1-32-1, global batch 262144)"
-SFNN_PHASES = ("fold", "sorts_tiles", "inverse_index", "ft_forward", "l1_head", "l1_backward", "small_grads_ranger",
+SFNN_PHASES = ("sorts_tiles", "inverse_index", "fold", "ft_forward", "l1_head", "l1_backward", "small_grads_ranger",
                "ft_rows_ranger")
-# fold 1, king sort 3, bucket sort 3, tile table 1, L1 weights 1, index 5 + row sort 1, FT forward 1,
-# L1 forward 1, head 1, L1 backward 1, finalize 1, Ranger on 9 small groups, heavy rows 4, FT rows 45 kings / 3
-SFNN_LAUNCHES_PER_STEP = 1 + 3 + 3 + 1 + 1 + 6 + 1 + 1 + 1 + 1 + 1 + 9 + 4 + 15
+# fold 1, king sort 3, bucket sort 3, king tiles + tile table 2, L1 weights 1, index 5 + row sort 1, FT forward 1,
+# L1 forward 1, head 1, L1 backward 1, finalize 1, Ranger on 9 small groups, heavy keys 5 (plan 3, incidence,
+# tensor-core sums), FT rows 45 kings / 3
+SFNN_LAUNCHES_PER_STEP = 1 + 3 + 3 + 2 + 1 + 6 + 1 + 1 + 1 + 1 + 1 + 9 + 5 + 15
 # QAT modes (the runner's qat_l1 / qat_ft / qat_l2 / qat_l3).  configs[2] trains
 # "with QAT fake-quant": the default quantises every layer (FT, L1, L2, L3),
 # which selects the dense integer QAT with the engine's integer FT.
@@ -166,6 +167,8 @@ def parse_args():
                     help="per-GPU batch (sfnn, halfkp, kppt) or global batch (sfnn_k9k9)")
     ap.add_argument("--dp-chunk-launches", type=int, default=3,
                     help="N > 1: FT row launches per exchanged chunk (SFNN)")
+    ap.add_argument("--dp-last-chunk-launches", type=int, default=1,
+                    help="N > 1: FT row launches of the last exchanged chunk (SFNN; 0: no separate last chunk)")
     ap.add_argument("--qat", choices=tuple(SFNN_QAT_MODES), default="all",
                     help="SFNN quantisation-aware training mode (both arms)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1067,7 +1070,8 @@ def run_sfnn_data_parallel(args, wl, rank, world, local, dist):
     ctx, lib = backend.ctx, backend.lib
     tr = SfnnDataParallelTrainer(backend, dist, sfnn_host_weights(wl.stacks), args.batch, SFNN_ACTIVE,
                                  lr_multipliers=sfnn_lr_multipliers(args.qat),
-                                 launches_per_chunk=args.dp_chunk_launches)
+                                 launches_per_chunk=args.dp_chunk_launches,
+                                 last_chunk_launches=args.dp_last_chunk_launches or None)
     host, devb = sfnn_batches(args, ctx, rank, workload=wl)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
     inv = 1.0 / 600.0
@@ -1123,12 +1127,27 @@ def run_sfnn_data_parallel(args, wl, rank, world, local, dist):
     wall_ms = (time.perf_counter() - t0) * 1000.0
     e2e_ms = max_over_ranks(dist, max(e1.elapsed_ms_since(e0), wall_ms))
     assert all(np.isfinite(losses)), "non-finite loss"
+    # after the timed regions: a few steps with events around each collective
+    # on the comm stream (the exchange breakdown; not part of any timed number)
+    tr.timing = True
+    for i in range(min(args.steps, 8)):
+        step += 1
+        bind(i)
+        tr.step_device(ranger(step), loss_kind, inv, finalize_loss=False)
+    tr.timing = False
+    tr.join()
+    exchange = backend.exchange_timing(tr)
+    exchange["exchange_tail_after_rows_ms_max_over_ranks"] = max_over_ranks(
+        dist, exchange.get("exchange_tail_after_rows_ms", 0.0))
+    torch.cuda.synchronize()
+    dist.barrier()
     return {"total_ms": total_ms, "phase_ms": phase_ms, "clocks": clocks.summary(),
             "e2e": {"value": args.steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
                     "h2d_bytes_per_step": int(sources[0].nbytes), "d2h_bytes_per_step": 4, "steps": args.steps,
                     "path": "SfnnDataParallelTrainer.step_device per rank (NCCL reduce-scatter / all-reduce / "
                             "all-gather), inputs from page-locked host memory, mean loss read back every step"},
-            "gpu_launches": (sfnn_launches_per_step(args.qat) + 1) * args.steps, "final_loss": losses[-1]}
+            "gpu_launches": (sfnn_launches_per_step(args.qat) + 1) * args.steps, "final_loss": losses[-1],
+            "exchange": exchange}
 
 
 def run_sfnn_reference(args, wl, local):
@@ -1180,10 +1199,11 @@ SFNN_DRAM_BYTES_PSV_B65536 = {
     "l1_backward": (2068230656, ("all",)),
 }
 SFNN_PHASE_KERNELS = {
-    "ft_rows_ranger": "heavy_segment_kernel + 15 piece_row_kernel launches (FT gradient rows + fused Ranger)",
+    "ft_rows_ranger": ("heavy-key plan (3 kernels) + heavy_incidence_kernel + heavy_key_mma_kernel (tcgen05) + 15 "
+                       "piece_row_kernel launches (FT gradient rows + fused Ranger)"),
     "ft_forward": "ft_forward_kernel<12> (ft_forward_int_kernel<12, 2> with all-layer QAT)",
     "l1_backward": "l1_backward_kernel<16>",
-    "fold": "fold_ft_qat4_kernel",
+    "fold": "fold_rows_kernel<true> (FT QAT fold)",
 }
 
 
@@ -1225,7 +1245,7 @@ def sfnn_roofline(phase_ms, batch, hbm_peak, peak_kind, l2_peak=None, lookahead_
             if qat in modes:
                 traffic[k] = b
     out = phase_roofline(phase_ms, comp, logical, hbm_peak, peak_kind, l2_peak, traffic, None, SFNN_PHASE_KERNELS)
-    out["launches_per_step"] = 16 if out["phase"] == "ft_rows_ranger" else 1
+    out["launches_per_step"] = 20 if out["phase"] == "ft_rows_ranger" else 1
     out["traffic_note"] = ("DRAM bytes of the phase per step from an ncu capture at B = 65536 (profiles/); "
                            "null where none was taken for this configuration")
     return out
@@ -1366,9 +1386,9 @@ def main():
             emit(line)
             return
         line.update(roofline=rl, gpu_launches=r["gpu_launches"], final_loss=r["final_loss"])
-        for extra in ("e2e_async_loss", "e2e_records", "producer", "l2_peak"):
+        for extra in ("e2e_async_loss", "e2e_records", "producer", "l2_peak", "exchange"):
             if extra in r:
-                line[extra] = rounded(r[extra])
+                line[extra] = r[extra] if extra == "exchange" else rounded(r[extra])
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             if args.workload == "halfkp":
                 line["cpu_baseline"] = halfkp_cpu_baseline()

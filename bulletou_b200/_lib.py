@@ -154,6 +154,7 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_profile_end": [P, P, Z, P, P],
     "bulletou_b200_l2_read_probe": [P, P, Z, I, P],
     "bulletou_b200_context_scratch_bytes": [P, P],
+    "bulletou_b200_context_wait_before_weights": [P, P],
     "bulletou_b200_nnue_forward_device_noalloc": [P, Z, Z, Z, Z, Z, Z] + [P] * 16,
     "bulletou_b200_nnue_train_step_device": [P, Z, Z, Z, Z, Z, Z, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P],
     "bulletou_b200_nnue_dense_gradient_len": [Z, Z, Z, P],

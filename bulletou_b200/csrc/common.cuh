@@ -41,6 +41,9 @@ struct BulletOuCudaCppContext {
     bool dense_qat_integer_ft = false;
     const float* dense_qat_l2_bias = nullptr;
     const float* dense_qat_l3_bias = nullptr;
+    // Event the next SFNN fused step waits for before reading a weight
+    // (bulletou_b200_context_wait_before_weights); cleared by that step.
+    cudaEvent_t weights_ready = nullptr;
     // Stage profiler (bulletou_b200_profile_*): events recorded on `stream`
     // at phase boundaries of the fused steps, read back after the run.
     bool prof_on = false;

@@ -433,6 +433,14 @@ int bulletou_b200_context_scratch_bytes(const BulletOuCudaCppContext* ctx, size_
     return ok();
 }
 
+int bulletou_b200_context_wait_before_weights(BulletOuCudaCppContext* ctx, const BulletOuCudaCppEvent* event) {
+    if (validate_context(ctx) != 0) return -1;
+    if (event != nullptr && (event->event == nullptr || event->device != ctx->device))
+        return fail_message("context_wait_before_weights: event missing or on another device");
+    ctx->weights_ready = event != nullptr ? event->event : nullptr;
+    return ok();
+}
+
 int bulletou_b200_l2_read_probe(BulletOuCudaCppContext* ctx, const BulletOuCudaCppF32Buffer* buffer, size_t len,
                                 int passes, BulletOuCudaCppF32Buffer* sink) {
     if (validate_f32(ctx, buffer, len, "L2 probe buffer") != 0) return -1;

@@ -63,17 +63,29 @@ __device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f 
 // Fake quantisation of the reference's training path (cu:1644-1666): the f32
 // product rounded half away from zero, ties and |x| >= 2^22 redone in double,
 // clamped, divided back (IEEE division: this file is built with fast math).
-__device__ __forceinline__ float qat_qd(float v, float scale, float lo, float hi) {
+__device__ __forceinline__ float qat_round(float v, float scale, float lo, float hi) {
     const float scaled = __fmul_rn(v, scale);
     float q = roundf(scaled);
     if (fabsf(scaled) >= 4194304.0f || fabsf(scaled - truncf(scaled)) == 0.5f)
         q = static_cast<float>(round(static_cast<double>(v) * static_cast<double>(scale)));
-    q = fminf(fmaxf(q, lo), hi);
-    return __fdiv_rn(q, scale);
+    return fminf(fmaxf(q, lo), hi);
 }
+__device__ __forceinline__ float qat_qd(float v, float scale, float lo, float hi) {
+    return __fdiv_rn(qat_round(v, scale, lo, hi), scale);
+}
+// The IEEE quotient q / 127 of an integer |q| <= 32768 without a division:
+// q * rh + RN(q * rl) rounded once (fma), rh = RN(1/127) = 0x1.020408p-7,
+// rl = RN(1/127 - rh) = 0x1.020408p-35 -- division by a constant through a
+// double-word reciprocal (Brisebarre, Muller and Raina, IEEE Trans. Computers
+// 53(8), 2004).  Before the final rounding the error is below 2^-46 |q / 127|,
+// and q / 127 lies at least ulp / 254 away from every rounding midpoint (127
+// is odd and prime, so q / 127 is an integer or not dyadic), so the result is
+// the correctly rounded quotient; checked with exact rationals for every q in
+// [-32768, 32767].
+__device__ __forceinline__ float div127(float q) { return __fmaf_rn(q, 0x1.020408p-7f, __fmul_rn(q, 0x1.020408p-35f)); }
 __device__ __forceinline__ float qat_q64(float v) { return qat_qd(v, 64.0f, -128.0f, 127.0f); }
 __device__ __forceinline__ float qat_q8128(float v) { return qat_qd(v, 8128.0f, -2147483648.0f, 2147483647.0f); }
-__device__ __forceinline__ float qat_q127(float v) { return qat_qd(v, 127.0f, -32768.0f, 32767.0f); }
+__device__ __forceinline__ float qat_q127(float v) { return div127(qat_round(v, 127.0f, -32768.0f, 32767.0f)); }
 // a + alpha * b with two roundings (the QAT folds, cu:1790-1795, 9302-9310).
 __device__ __forceinline__ float fold_nf(float a, float alpha, float b) { return __fadd_rn(a, __fmul_rn(alpha, b)); }
 // round(v * 8128) in double, saturated to i32 (cu:1986-1988).
@@ -85,7 +97,7 @@ __device__ __forceinline__ int qat_bias_int(float v) {
 __device__ __forceinline__ int qat_lattice(float c) {
     return static_cast<int>(floor(static_cast<double>(fminf(1.0f, fmaxf(0.0f, c))) * 127.0));
 }
-__device__ __forceinline__ float qat_on_lattice(int n) { return __fdiv_rn(static_cast<float>(n), 127.0f); }
+__device__ __forceinline__ float qat_on_lattice(int n) { return div127(static_cast<float>(n)); }
 // Integer of a value already on a lattice (q / 127 or q / 64): round to nearest.
 __device__ __forceinline__ int qat_int127(float v) { return __float2int_rn(__fmul_rn(v, 127.0f)); }
 __device__ __forceinline__ int qat_int64(float v) { return __float2int_rn(__fmul_rn(v, 64.0f)); }
@@ -94,17 +106,6 @@ __device__ __forceinline__ float qat_raw_to_float(long long raw) {
 }
 
 // ------------------------------------------------------------------ fold
-__global__ void fold_ft4_kernel(const float4* __restrict__ l0w, float4* __restrict__ folded, size_t total4, int w4,
-                                int base, float alpha) {
-    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= total4) return;
-    const size_t f = t / w4;
-    const size_t q = t - f * w4;
-    const float4 a = l0w[t];
-    const float4 v = l0w[(static_cast<size_t>(base) + f % kSfnnPieces) * w4 + q];
-    folded[t] = make_float4(fmaf(alpha, v.x, a.x), fmaf(alpha, v.y, a.y), fmaf(alpha, v.z, a.z), fmaf(alpha, v.w, a.w));
-}
-
 __global__ void fold_ft1_kernel(const float* __restrict__ l0w, float* __restrict__ folded, size_t total, int width,
                                 int base, float alpha) {
     const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -129,20 +130,47 @@ __global__ void fold_ft_qat_kernel(const float* __restrict__ l0w, float* __restr
     folded[t] = qat_q127(v);
 }
 
-// The same four columns at a time.
-__global__ void fold_ft_qat4_kernel(const float4* __restrict__ l0w, float4* __restrict__ folded, size_t total4,
-                                    int w4, int base, float alpha) {
-    const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= total4) return;
-    float4 a = l0w[t];
-    if (base > 0) {
-        const size_t f = t / w4;
-        const float4 v = l0w[(static_cast<size_t>(base) + f % kSfnnPieces) * w4 + (t - f * w4)];
-        a = make_float4(fold_nf(a.x, alpha, v.x), fold_nf(a.y, alpha, v.y), fold_nf(a.z, alpha, v.z),
-                        fold_nf(a.w, alpha, v.w));
+// Both folds row by row: one CTA per table row (the virtual row's index once
+// per CTA), each thread up to four float4 columns with every load issued
+// before the first store.  QAT: the fake-quantised fold, base == 0 quantises
+// the row alone.
+constexpr int kFoldThreads = 128;
+template <bool QAT>
+__global__ void __launch_bounds__(kFoldThreads) fold_rows_kernel(const float4* __restrict__ l0w,
+                                                                 float4* __restrict__ folded, int w4, int base,
+                                                                 float alpha) {
+    const size_t f = blockIdx.x;
+    const float4* src = l0w + f * w4;
+    const float4* vsrc = l0w + (static_cast<size_t>(base) + f % kSfnnPieces) * w4;
+    float4* dst = folded + f * w4;
+    for (int j0 = 0; j0 < w4; j0 += 4 * kFoldThreads) {
+        float4 a[4], v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = j0 + i * kFoldThreads + static_cast<int>(threadIdx.x);
+            if (j < w4) {
+                a[i] = src[j];
+                if (!QAT || base > 0) v[i] = vsrc[j];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = j0 + i * kFoldThreads + static_cast<int>(threadIdx.x);
+            if (j >= w4) continue;
+            float4 o;
+            if (QAT) {
+                float4 x = a[i];
+                if (base > 0)
+                    x = make_float4(fold_nf(x.x, alpha, v[i].x), fold_nf(x.y, alpha, v[i].y),
+                                    fold_nf(x.z, alpha, v[i].z), fold_nf(x.w, alpha, v[i].w));
+                o = make_float4(qat_q127(x.x), qat_q127(x.y), qat_q127(x.z), qat_q127(x.w));
+            } else {
+                o = make_float4(fmaf(alpha, v[i].x, a[i].x), fmaf(alpha, v[i].y, a[i].y), fmaf(alpha, v[i].z, a[i].z),
+                                fmaf(alpha, v[i].w, a[i].w));
+            }
+            dst[j] = o;
+        }
     }
-    const float4 q = make_float4(qat_q127(a.x), qat_q127(a.y), qat_q127(a.z), qat_q127(a.w));
-    folded[t] = q;
 }
 
 // layer_qat_vector_kernel (cu:9294-9300): element-wise fake quantisation.
@@ -1846,23 +1874,29 @@ int plan_heavy_mma(BulletOuCudaCppContext* ctx, const PieceRowArgs& a, const Hea
     return 0;
 }
 
-int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, const size_t* row_shift = nullptr,
-                      const cudaEvent_t* events = nullptr, const HeavyMmaInputs* mma = nullptr) {
+// Columns per lane of the FT row kernel for these buffers: 8, 4 or 1.
+int piece_row_vec(int mode, const PieceRowArgs& a) {
     bool al = aligned16(a.src[0]) && aligned16(a.src[1]) && a.src_stride % 4 == 0;
     if (mode == kRowRanger)
         al = al && aligned16(a.weights) && aligned16(a.momentum) && aligned16(a.velocity) && aligned16(a.slow);
     else
         al = al && aligned16(a.gradients);
-    int vec = 1;
-    if (al && a.width % 256 == 0) {
-        vec = 8;
-        a.group_width = 256;
-    } else if (al && a.width % 128 == 0) {
-        vec = 4;
-        a.group_width = 128;
-    } else {
-        a.group_width = 32;
-    }
+    if (al && a.width % 256 == 0) return 8;
+    if (al && a.width % 128 == 0) return 4;
+    return 1;
+}
+
+// Whether launch_piece_rows sums the heavy keys on the tensor cores (then
+// their entry lists are not read).
+bool piece_rows_use_mma(int mode, const PieceRowArgs& a, const HeavyMmaInputs* mma) {
+    return mma != nullptr && piece_row_vec(mode, a) == 8 && a.tile_base != nullptr && a.kings > 1 &&
+           heavy_mma_supported(a.width) && a.pieces <= 2048;
+}
+
+int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, const size_t* row_shift = nullptr,
+                      const cudaEvent_t* events = nullptr, const HeavyMmaInputs* mma = nullptr) {
+    const int vec = piece_row_vec(mode, a);
+    a.group_width = vec == 8 ? 256 : (vec == 4 ? 128 : 32);
     a.col_groups = (a.width + a.group_width - 1) / a.group_width;
     if (a.virtual_base >= 0 && a.kings > kKingsPerLaunch) {
         const size_t vf = align_floats(static_cast<size_t>(a.pieces) * a.width);
@@ -1873,9 +1907,7 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, con
         a.vacc = static_cast<float*>(vp);
         a.vany = reinterpret_cast<int*>(a.vacc + vf);
     }
-    const bool use_mma = mma != nullptr && vec == 8 && a.tile_base != nullptr && a.kings > 1 &&
-                         heavy_mma_supported(a.width) && a.pieces <= 2048;
-    if (use_mma) {
+    if (piece_rows_use_mma(mode, a, mma)) {
         // heavy keys on the tensor cores; the row kernel adds their sums
         HeavyMmaArgs m{};
         if (plan_heavy_mma(ctx, a, *mma, &m) != 0 || launch_heavy_key_mma(ctx, m) != 0) return -1;
@@ -1972,11 +2004,12 @@ int qat_scratch(BulletOuCudaCppContext* ctx, const SfnnDims& d, SfnnPlan* plan) 
 }
 
 // Fold, sorts, tile table and effective L1 weights; every scratch the step needs.
-int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, const int* stm, const int* nstm,
-                 const int* buckets, float* fold_target, SfnnPlan* plan) {
+// The weight-dependent preparation: the fold (FT QAT: fake-quantised fold and
+// bias), the effective L1 weights and the L1 QAT biases.
+int sfnn_prepare_weights(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, float* fold_target,
+                         SfnnPlan* plan) {
     const int threads = 256;
     int blocks = 0;
-    // 1. fold
     plan->table = w.l0w;
     plan->ft_bias = w.l0b;
     if (d.qat.ft && w.l0w != nullptr) {
@@ -1989,10 +2022,9 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
             folded = static_cast<float*>(p);
         }
         if (d.width % 4 == 0 && aligned16(w.l0w) && aligned16(folded)) {
-            if (grid_1d(n / 4, threads, &blocks, "SFNN FT QAT fold") != 0) return -1;
-            fold_ft_qat4_kernel<<<blocks, threads, 0, ctx->stream>>>(
-                reinterpret_cast<const float4*>(w.l0w), reinterpret_cast<float4*>(folded), n / 4, d.width / 4,
-                d.base, d.ft_alpha);
+            fold_rows_kernel<true><<<d.n_features, kFoldThreads, 0, ctx->stream>>>(
+                reinterpret_cast<const float4*>(w.l0w), reinterpret_cast<float4*>(folded), d.width / 4, d.base,
+                d.ft_alpha);
         } else {
             if (grid_1d(n, threads, &blocks, "SFNN FT QAT fold") != 0) return -1;
             fold_ft_qat_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l0w, folded, n, d.width, d.base, d.ft_alpha);
@@ -2015,10 +2047,9 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
             folded = static_cast<float*>(p);
         }
         if (d.width % 4 == 0 && aligned16(w.l0w) && aligned16(folded)) {
-            if (grid_1d(n / 4, threads, &blocks, "SFNN fold") != 0) return -1;
-            fold_ft4_kernel<<<blocks, threads, 0, ctx->stream>>>(reinterpret_cast<const float4*>(w.l0w),
-                                                                 reinterpret_cast<float4*>(folded), n / 4, d.width / 4,
-                                                                 d.base, d.ft_alpha);
+            fold_rows_kernel<false><<<d.base, kFoldThreads, 0, ctx->stream>>>(
+                reinterpret_cast<const float4*>(w.l0w), reinterpret_cast<float4*>(folded), d.width / 4, d.base,
+                d.ft_alpha);
         } else {
             if (grid_1d(n, threads, &blocks, "SFNN fold") != 0) return -1;
             fold_ft1_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l0w, folded, n, d.width, d.base, d.ft_alpha);
@@ -2026,8 +2057,32 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
         if (check_launch("SFNN fold launch") != 0) return -1;
         plan->table = folded;
     }
-    prof_mark(ctx);
-    // 2. sorts + tiles
+    const size_t eff = static_cast<size_t>(d.stacks) * d.width * d.l1_out;
+    void* ep = nullptr;
+    if (scratch_slot(ctx, kScratchSfnnEff, eff * sizeof(float), &ep, "cudaMalloc SFNN L1 weights") != 0) return -1;
+    plan->w1_eff = static_cast<float*>(ep);
+    if (grid_1d(eff, threads, &blocks, "SFNN L1 weights") != 0) return -1;
+    l1_eff_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l1w, d.has_l1f ? w.l1fw : nullptr, d.shared_alpha, d.stacks,
+                                                       d.l1_out, d.width, d.qat.l1, plan->w1_eff);
+    if (check_launch("SFNN L1 weights launch") != 0) return -1;
+    if (d.qat.l1 || d.qat.dense) {
+        if (qat_scratch(ctx, d, plan) != 0) return -1;
+        if (d.qat.l1 && w.l1b != nullptr) {
+            const int n = d.stacks * d.l1_out;
+            qat_l1_bias_kernel<<<(n + threads - 1) / threads, threads, 0, ctx->stream>>>(
+                w.l1b, d.has_l1f ? w.l1fb : nullptr, d.shared_alpha, n, d.l1_out, 1, plan->b1_eff, plan->b1_int,
+                plan->b1_master);
+            if (check_launch("SFNN L1 QAT bias launch") != 0) return -1;
+        }
+    }
+    return 0;
+}
+
+// The batch-only preparation: king sort of the half-positions, their rank
+// tiles, bucket sort of the samples and its tile table, per-tile partial
+// buffers.  Reads no weight.
+int sfnn_prepare_batch(BulletOuCudaCppContext* ctx, const SfnnDims& d, const int* stm, const int* nstm,
+                       const int* buckets, SfnnPlan* plan) {
     const int n_half = 2 * d.batch;
     const int max_tiles = d.batch / kSfnnTile + d.stacks + 2;
     const size_t king_ints = king_sort_scratch_ints<kSfnnKingKeys>(n_half);
@@ -2073,25 +2128,7 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
         if (check_launch("SFNN bucket sort launch") != 0) return -1;
         plan->tiles = Tiles{order, n_tiles, tile_key, tile_begin, tile_end, key_first, max_tiles};
     }
-    // 3. effective L1 weights and per-tile partial buffers
-    const size_t eff = static_cast<size_t>(d.stacks) * d.width * d.l1_out;
-    void* ep = nullptr;
-    if (scratch_slot(ctx, kScratchSfnnEff, eff * sizeof(float), &ep, "cudaMalloc SFNN L1 weights") != 0) return -1;
-    plan->w1_eff = static_cast<float*>(ep);
-    if (grid_1d(eff, threads, &blocks, "SFNN L1 weights") != 0) return -1;
-    l1_eff_kernel<<<blocks, threads, 0, ctx->stream>>>(w.l1w, d.has_l1f ? w.l1fw : nullptr, d.shared_alpha, d.stacks,
-                                                       d.l1_out, d.width, d.qat.l1, plan->w1_eff);
-    if (check_launch("SFNN L1 weights launch") != 0) return -1;
-    if (d.qat.l1 || d.qat.dense) {
-        if (qat_scratch(ctx, d, plan) != 0) return -1;
-        if (d.qat.l1 && w.l1b != nullptr) {
-            const int n = d.stacks * d.l1_out;
-            qat_l1_bias_kernel<<<(n + threads - 1) / threads, threads, 0, ctx->stream>>>(
-                w.l1b, d.has_l1f ? w.l1fb : nullptr, d.shared_alpha, n, d.l1_out, 1, plan->b1_eff, plan->b1_int,
-                plan->b1_master);
-            if (check_launch("SFNN L1 QAT bias launch") != 0) return -1;
-        }
-    }
+    // per-tile partial buffers
     const size_t hp = align_floats(static_cast<size_t>(max_tiles) * head_partial_len(d.l2_size, d.l2_in, d.l1_out));
     const size_t dp = align_floats(static_cast<size_t>(max_tiles) * d.l1_out * d.width);
     const size_t bp = align_floats(static_cast<size_t>(max_tiles) * 2 * d.width);
@@ -2104,8 +2141,13 @@ int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeigh
     plan->dw1_partials = plan->head_partials + hp;
     plan->l0b_partials = plan->dw1_partials + dp;
     plan->g1 = plan->l0b_partials + bp;
-    prof_mark(ctx);
     return 0;
+}
+
+int sfnn_prepare(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights& w, const int* stm, const int* nstm,
+                 const int* buckets, float* fold_target, SfnnPlan* plan) {
+    if (sfnn_prepare_weights(ctx, d, w, fold_target, plan) != 0) return -1;
+    return sfnn_prepare_batch(ctx, d, stm, nstm, buckets, plan);
 }
 
 int launch_ft_forward(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnPlan& plan, const int* stm,
@@ -2488,18 +2530,51 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
               float* const* sm, float* output, float* per_sample, float* mog, float* weighted_sum, float* mean,
               float* ft_grad, float* dense_grad, const size_t* row_shift = nullptr,
               const cudaEvent_t* row_events = nullptr) {
+    // phases: batch sorts and tiles, inverse index, [weights wait] fold and L1
+    // weights, FT forward, L1 + head, L1 backward, small groups, FT rows
     ctx->prof_marks_per_step = 9;
     prof_mark(ctx);
     SfnnPlan plan{};
-    if (sfnn_prepare(ctx, d, w, stm, nstm, buckets, nullptr, &plan) != 0) return -1;
+    if (sfnn_prepare_batch(ctx, d, stm, nstm, buckets, &plan) != 0) return -1;
+    prof_mark(ctx);
     InverseIndex index;
     const RowTiles row_tiles{plan.king_tiles, plan.king.key_off, d.base > 0 ? kSfnnPieces : d.n_features, plan.kings,
                              kTileRanks, plan.max_king_tiles};
-    if (build_inverse_index_tiled(ctx, stm, nstm, d.batch, d.max_active, row_tiles, &index, plan.king_rank) != 0 ||
-        sort_inverse_index(ctx, index) != 0)
+    if (build_inverse_index_tiled(ctx, stm, nstm, d.batch, d.max_active, row_tiles, &index, plan.king_rank) != 0)
         return -1;
     StepBuffers sb{};
     if (step_buffers(ctx, d, output, &sb) != 0) return -1;
+    // the FT rows' arguments (their Ranger step is filled in below)
+    PieceRowArgs r = piece_row_args(d, index);
+    r.tile_base = plan.king_tiles;
+    r.src[0] = sb.pregrad;
+    r.src[1] = sb.pregrad + d.width;
+    r.src_stride = 2 * static_cast<size_t>(d.width);
+    const int row_mode = ranger != nullptr ? kRowRanger : kRowWrite;
+    if (ranger != nullptr) {
+        r.weights = wm[0];
+        r.momentum = mm[0];
+        r.velocity = vm[0];
+        r.slow = sm[0];
+    } else {
+        r.gradients = ft_grad;
+    }
+    const HeavyMmaInputs mma{plan.king.key_off, plan.king.order, stm, nstm, d.max_active, plan.max_king_tiles,
+                             2 * d.batch, sb.pregrad_hi, sb.pregrad_lo};
+    const HeavyMmaInputs* mp = sb.pregrad_hi != nullptr ? &mma : nullptr;
+    // the tensor cores sum the heavy keys without their entry lists: only the
+    // light keys are sorted
+    if (sort_inverse_index(ctx, index, piece_rows_use_mma(row_mode, r, mp) ? kHeavyMmaThreshold : 0x7fffffff) != 0)
+        return -1;
+    prof_mark(ctx);
+    // everything above reads only the batch; from here on the step reads the
+    // weights, so it waits for the event a caller set to mark their update
+    if (ctx->weights_ready != nullptr) {
+        const cudaError_t st = cudaStreamWaitEvent(ctx->stream, ctx->weights_ready, 0);
+        ctx->weights_ready = nullptr;
+        if (st != cudaSuccess) return fail("cudaStreamWaitEvent weights-ready event", st);
+    }
+    if (sfnn_prepare_weights(ctx, d, w, nullptr, &plan) != 0) return -1;
     prof_mark(ctx);
     if (launch_ft_forward(ctx, d, plan, stm, nstm, plan.ft_bias, sb.act) != 0) return -1;
     prof_mark(ctx);
@@ -2551,24 +2626,11 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
         }
     }
     prof_mark(ctx);
-    PieceRowArgs r = piece_row_args(d, index);
-    r.tile_base = plan.king_tiles;
-    r.src[0] = sb.pregrad;
-    r.src[1] = sb.pregrad + d.width;
-    r.src_stride = 2 * static_cast<size_t>(d.width);
-    const HeavyMmaInputs mma{plan.king.key_off, plan.king.order, stm, nstm, d.max_active, plan.max_king_tiles,
-                             2 * d.batch, sb.pregrad_hi, sb.pregrad_lo};
-    const HeavyMmaInputs* mp = sb.pregrad_hi != nullptr ? &mma : nullptr;
     if (ranger != nullptr) {
-        r.weights = wm[0];
-        r.momentum = mm[0];
-        r.velocity = vm[0];
-        r.slow = sm[0];
         r.ranger = ra;
         r.skip_quiet = ranger_zero_step_is_identity(ra) ? 1 : 0;
         if (launch_piece_rows(ctx, kRowRanger, r, nullptr, nullptr, mp) != 0) return -1;
     } else {
-        r.gradients = ft_grad;
         if (launch_piece_rows(ctx, kRowWrite, r, row_shift, row_events, mp) != 0) return -1;
     }
     prof_mark(ctx);

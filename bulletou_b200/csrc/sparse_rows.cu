@@ -155,7 +155,8 @@ __device__ void smem_sort_ascending(int* buf, int size, int lane) {
 
 // Warp per row: ascending sort of the row's entry ids in place.
 __global__ void __launch_bounds__(kRowWarps * 32) sort_rows_kernel(const int* __restrict__ offsets,
-                                                                    int* __restrict__ entries, int n_rows) {
+                                                                    int* __restrict__ entries, int n_rows,
+                                                                    int skip_above) {
     __shared__ int buf_s[kRowWarps][kSortCap];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row = blockIdx.x * kRowWarps + warp;
@@ -163,7 +164,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) sort_rows_kernel(const int* __
     const int beg = offsets[row];
     const int n = offsets[row + 1] - beg;
     int* e = entries + beg;
-    if (n <= 1) return;
+    if (n <= 1 || n > skip_above) return;
     if (n <= 32) {
         int v = lane < n ? e[lane] : INT_MAX;
         v = warp_sort_ascending(v, lane);
@@ -460,10 +461,11 @@ int exclusive_scan_counts(BulletOuCudaCppContext* ctx, const int* counts, int n,
     return check_launch("exclusive scan launch");
 }
 
-int sort_inverse_index(BulletOuCudaCppContext* ctx, const InverseIndex& index) {
+int sort_inverse_index(BulletOuCudaCppContext* ctx, const InverseIndex& index, int skip_above) {
     if (index.n_rows <= 0) return 0;
     const int blocks = (index.n_rows + kRowWarps - 1) / kRowWarps;
-    sort_rows_kernel<<<blocks, kRowWarps * 32, 0, ctx->stream>>>(index.offsets, index.entries, index.n_rows);
+    sort_rows_kernel<<<blocks, kRowWarps * 32, 0, ctx->stream>>>(index.offsets, index.entries, index.n_rows,
+                                                                  skip_above);
     return check_launch("inverse index row sort launch");
 }
 

@@ -91,8 +91,10 @@ int exclusive_scan_counts(BulletOuCudaCppContext* ctx, const int* counts, int n,
 
 // Sorts every row's entry list ascending in place (rows with more than
 // kSortCap entries are left in fill order), so that consumers can sum a row in
-// a fixed order without sorting it themselves.
-int sort_inverse_index(BulletOuCudaCppContext* ctx, const InverseIndex& index);
+// a fixed order without sorting it themselves.  Rows with more than
+// `skip_above` entries are left unsorted too (their consumer does not read the
+// entry list: the tensor-core heavy keys of the SFNN FT rows).
+int sort_inverse_index(BulletOuCudaCppContext* ctx, const InverseIndex& index, int skip_above = 0x7fffffff);
 
 // Same, for a plain table: every feature id in [0, n_features) is its own row.
 int build_inverse_index_rows(BulletOuCudaCppContext* ctx, const int* stm, const int* nstm, size_t batch,

@@ -156,23 +156,90 @@ class B200Backend:
         tr._comm_ctx = cc.Context(self.device, self.lib, stream=tr._comm.cuda_stream)
         tr._events = [cc.Event(self.ctx) for _ in tr.row_ends]
         tr._event_handles = (ctypes.c_void_p * len(tr.row_ends))(*[e._h.value for e in tr._events])
+        tr._ready = cc.Event(self.ctx)  # recorded on the comm stream after each step's exchange
+        tr._ready_pending = False
+        tr._timing_steps = []
 
     def sfnn_step_overlapped(self, tr: "SfnnDataParallelTrainer", loss_spec, params) -> None:
         """Local step on the library's stream; per chunk, on the comm stream:
         wait for the launch that completes it, reduce-scatter, Ranger on the
         owned rows, all-gather.  The small groups' all-reduce and Ranger go
-        first (their gradients precede the row launches)."""
+        first (their gradients precede the row launches).  The next step runs
+        its batch-only work (sorts, inverse index) at once and waits for this
+        exchange only before it reads a weight
+        (bulletou_b200_context_wait_before_weights)."""
         torch = self.torch
         compute = torch.cuda.current_stream(self.device)
-        compute.wait_stream(tr._comm)  # the previous exchange wrote weights this step reads
+        if tr._ready_pending:
+            # the previous exchange wrote the weights this step reads and read
+            # the gradient rows this step writes, both after the batch work
+            self.lib.call("bulletou_b200_context_wait_before_weights", self.ctx.as_ptr(), tr._ready._h)
+        ev = self._timing_events(tr) if tr.timing else None
+        if ev is not None:
+            ev["step_start"].record(compute)
         self.sfnn_local_gradients(tr, loss_spec, tr._event_handles)
+        if ev is not None:
+            ev["rows_end"].record(compute)
         with torch.cuda.stream(tr._comm):
             tr._events[0].wait(tr._comm_ctx)
+            if ev is not None:
+                ev["small_start"].record(tr._comm)
             tr._small_exchange(params, tr._comm_ctx)
-            for j in range(len(tr.chunks)):
-                last_launch = min(len(tr.row_ends), (j + 1) * tr.launches_per_chunk) - 1
-                tr._events[last_launch].wait(tr._comm_ctx)
-                tr._chunk_exchange(j, params, tr._comm_ctx)
+            for j, c in enumerate(tr.chunks):
+                tr._events[c.last_launch].wait(tr._comm_ctx)
+                tr._chunk_exchange(j, params, tr._comm_ctx, None if ev is None else ev["chunks"][j])
+            if ev is not None:
+                ev["exchange_end"].record(tr._comm)
+        tr._ready.record(tr._comm_ctx)
+        tr._ready_pending = True
+
+    def _timing_events(self, tr) -> dict:
+        E = lambda: self.torch.cuda.Event(enable_timing=True)  # noqa: E731
+        ev = {"step_start": E(), "rows_end": E(), "small_start": E(), "exchange_end": E(),
+              "chunks": [{"start": E(), "reduce_scatter": E(), "ranger": E(), "all_gather": E()} for _ in tr.chunks]}
+        tr._timing_steps.append(ev)
+        return ev
+
+    def exchange_timing(self, tr) -> dict:
+        """Mean per step over the steps run with tr.timing on (ms, device
+        events): the local step (start to its last row launch's end), the comm
+        stream's small-group exchange, reduce-scatters, shard Ranger,
+        all-gathers, the exchange's end after the last row launch (the tail
+        the next step's weight reads wait for) and per chunk."""
+        self.torch.cuda.synchronize(self.device)
+        steps = tr._timing_steps
+        tr._timing_steps = []
+        if not steps:
+            return {}
+        acc = {"local_step_ms": 0.0, "small_exchange_ms": 0.0, "reduce_scatter_ms": 0.0, "shard_ranger_ms": 0.0,
+               "all_gather_ms": 0.0, "exchange_tail_after_rows_ms": 0.0}
+        per_chunk = [{"wait_ms": 0.0, "reduce_scatter_ms": 0.0, "shard_ranger_ms": 0.0, "all_gather_ms": 0.0}
+                     for _ in tr.chunks]
+        for ev in steps:
+            acc["local_step_ms"] += ev["step_start"].elapsed_time(ev["rows_end"])
+            prev = ev["small_start"]
+            for j, c in enumerate(ev["chunks"]):
+                if j == 0:
+                    acc["small_exchange_ms"] += ev["small_start"].elapsed_time(c["start"])
+                else:
+                    per_chunk[j]["wait_ms"] += prev.elapsed_time(c["start"])
+                rs = c["start"].elapsed_time(c["reduce_scatter"])
+                rg = c["reduce_scatter"].elapsed_time(c["ranger"])
+                ag = c["ranger"].elapsed_time(c["all_gather"])
+                per_chunk[j]["reduce_scatter_ms"] += rs
+                per_chunk[j]["shard_ranger_ms"] += rg
+                per_chunk[j]["all_gather_ms"] += ag
+                acc["reduce_scatter_ms"] += rs
+                acc["shard_ranger_ms"] += rg
+                acc["all_gather_ms"] += ag
+                prev = c["all_gather"]
+            acc["exchange_tail_after_rows_ms"] += ev["rows_end"].elapsed_time(ev["exchange_end"])
+        n = len(steps)
+        out = {k: round(v / n, 4) for k, v in acc.items()}
+        out["steps"] = n
+        out["chunks"] = [{"launches": [c.first_launch, c.last_launch], "rows": c.length,
+                          **{k: round(v / n, 4) for k, v in pc.items()}} for c, pc in zip(tr.chunks, per_chunk)]
+        return out
 
     def join_overlap(self, tr: "SfnnDataParallelTrainer") -> None:
         self.torch.cuda.current_stream(self.device).wait_stream(tr._comm)
@@ -288,18 +355,29 @@ class RowChunk:
     shift: int
     shard_off: int
     shard_rows: int
+    first_launch: int = 0  # row launches [first_launch, last_launch] complete the chunk
+    last_launch: int = 0
 
 
-def sfnn_row_chunks(row_ends: list, world: int, launches_per_chunk: int = 1) -> list:
-    """Chunks of `launches_per_chunk` consecutive row launches (the last may
-    hold fewer)."""
+def sfnn_row_chunks(row_ends: list, world: int, launches_per_chunk: int = 1,
+                    last_chunk_launches: Optional[int] = None) -> list:
+    """Chunks of `launches_per_chunk` consecutive row launches.  With
+    `last_chunk_launches`, the last that many launches form a chunk of their
+    own (a short last chunk leaves less exchange after the last launch); the
+    chunk before it may then hold fewer."""
+    n = len(row_ends)
+    lpc = max(1, int(launches_per_chunk))
+    tail = n if last_chunk_launches is None else max(1, min(n, int(last_chunk_launches)))
+    head = n - tail if last_chunk_launches is not None else n
+    bounds = [(i, min(head, i + lpc) - 1) for i in range(0, head, lpc)]
+    if last_chunk_launches is not None:
+        bounds.append((head, n - 1))
     chunks, shift, off, start = [], 0, 0, 0
-    ends = [row_ends[min(len(row_ends), i + launches_per_chunk) - 1]
-            for i in range(0, len(row_ends), launches_per_chunk)]
-    for end in ends:
+    for first, last in bounds:
+        end = row_ends[last]
         length = end - start
         padded = -(-length // world) * world
-        chunks.append(RowChunk(start, length, padded, shift, off, padded // world))
+        chunks.append(RowChunk(start, length, padded, shift, off, padded // world, first, last))
         shift += padded - length
         off += padded // world
         start = end
@@ -310,15 +388,19 @@ class SfnnDataParallelTrainer:
     """One rank of data-parallel SFNN training (default layer multipliers).
 
     The FT gradient rows come from a sequence of row-kernel launches, each
-    completing a contiguous range of rows (a few king blocks).  Each range is a
-    chunk of its own, padded to a multiple of the world size: the chunk is
-    reduce-scattered, the owned part updated by Ranger and all-gathered back,
-    chunk by chunk.  On the GPU the chunks' collectives and updates run on a
-    second stream, each starting when its launch has finished (an event the
-    library records), so the exchange overlaps the remaining launches."""
+    completing a contiguous range of rows (a few king blocks).  Consecutive
+    launches form a chunk (`launches_per_chunk` of them, the last
+    `last_chunk_launches` a chunk of their own), padded to a multiple of the
+    world size: the chunk is reduce-scattered, the owned part updated by
+    Ranger and all-gathered back, chunk by chunk.  On the GPU the chunks'
+    collectives and updates run on a second stream, each starting when its
+    last launch has finished (an event the library records), so the exchange
+    overlaps the remaining launches, and its tail overlaps the next step's
+    batch-only work."""
 
     def __init__(self, backend, dist, initial_weights, batch_size: int, max_active: int, alpha=None,
-                 lr_multipliers=None, overlap: Optional[bool] = None, launches_per_chunk: int = 3):
+                 lr_multipliers=None, overlap: Optional[bool] = None, launches_per_chunk: int = 3,
+                 last_chunk_launches: Optional[int] = 1):
         from .sfnn import SFNN_WEIGHT_NAMES, SfnnFactorizerAlpha, SfnnLayerLrMultipliers
 
         initial_weights.validate()
@@ -334,9 +416,9 @@ class SfnnDataParallelTrainer:
         W = sh.ft_size
         self.row_ends = backend.sfnn_row_launches(sh, self.alpha)
         self.launches_per_chunk = max(1, int(launches_per_chunk))
-        self.chunks = sfnn_row_chunks(self.row_ends, self.world, self.launches_per_chunk)
-        # launch j belongs to chunk j // launches_per_chunk
-        self.launch_chunk = [j // self.launches_per_chunk for j in range(len(self.row_ends))]
+        self.chunks = sfnn_row_chunks(self.row_ends, self.world, self.launches_per_chunk, last_chunk_launches)
+        self.launch_chunk = [j for j, c in enumerate(self.chunks) for _ in range(c.first_launch, c.last_launch + 1)]
+        self.timing = False  # GPU: record exchange events per step (exchange_timing)
         last = self.chunks[-1]
         grad_rows = last.start + last.shift + last.padded
         l0w_rows = last.start + last.padded  # a chunk's all-gather writes its padded length
@@ -401,17 +483,26 @@ class SfnnDataParallelTrainer:
 
         return replace(params, norm_loss_strength=0.0, norm_loss_before=False)  # lib.rs:6416-6420
 
-    def _chunk_exchange(self, j: int, params: RangerUpdateParams, ctx=None) -> None:
-        """Reduce-scatter chunk j, Ranger on the owned part, all-gather it back."""
+    def _chunk_exchange(self, j: int, params: RangerUpdateParams, ctx=None, events=None) -> None:
+        """Reduce-scatter chunk j, Ranger on the owned part, all-gather it back
+        (events: optional timing events recorded on the current stream)."""
         c, W = self.chunks[j], self.shape.ft_size
         g0 = (c.start + c.shift) * W
         s0 = c.shard_off * W
+        if events is not None:
+            events["start"].record()
         self.dist.reduce_scatter_tensor(self._t_shard[s0:s0 + c.shard_rows * W],
                                         self._t_ft_grad[g0:g0 + c.padded * W])
+        if events is not None:
+            events["reduce_scatter"].record()
         grad, w, m, v, slow = self.chunk_views[j]
         self.backend.ranger(params, grad, w, m, v, slow, ctx)
+        if events is not None:
+            events["ranger"].record()
         self.dist.all_gather_into_tensor(self._t_l0w[c.start * W:(c.start + c.padded) * W],
                                          self._t_compact[s0:s0 + c.shard_rows * W])
+        if events is not None:
+            events["all_gather"].record()
 
     def _small_exchange(self, params: RangerUpdateParams, ctx=None) -> None:
         from .sfnn import factor_contribution_clip

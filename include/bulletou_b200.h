@@ -90,9 +90,9 @@ int bulletou_b200_f32_buffer_view(const BulletOuCudaCppF32Buffer* buffer, size_t
  * marks i and i+1 of every step (phase i), in *steps_out the steps recorded
  * and in *phases_out the phases per step.  HalfKP step phases: inverse index,
  * king sort, FT gather, dense forward/loss/backward, batch reduce,
- * small-group Ranger + loss, FT rows.  SFNN step phases: fold, sorts + tiles,
- * inverse index, FT forward, L1 forward + head, L1 backward, small-group
- * Ranger + loss, FT rows. */
+ * small-group Ranger + loss, FT rows.  SFNN step phases: sorts + tiles,
+ * inverse index, fold + L1 weights, FT forward, L1 forward + head, L1
+ * backward, small-group Ranger + loss, FT rows. */
 int bulletou_b200_profile_begin(BulletOuCudaCppContext* ctx, size_t max_marks);
 int bulletou_b200_profile_end(BulletOuCudaCppContext* ctx, float* ms_out, size_t ms_len, size_t* steps_out,
     size_t* phases_out);
@@ -101,6 +101,17 @@ int bulletou_b200_profile_end(BulletOuCudaCppContext* ctx, float* ms_out, size_t
  * (no counterpart in the reference; diagnostics).  The slots are allocated on
  * first use by the entries that need scratch and freed at context destroy. */
 int bulletou_b200_context_scratch_bytes(const BulletOuCudaCppContext* ctx, size_t* out);
+
+/* Data-parallel overlap (no counterpart in the reference): the next SFNN
+ * fused step on this context (bulletou_b200_sfnn_local_gradients_device or
+ * bulletou_b200_sfnn_train_step_device) runs its batch-only work (king and
+ * bucket sorts, rank tiles, inverse index) at once and makes the context
+ * stream wait for `event` before its first read of a weight (the fold).  A
+ * caller whose weight update runs on another stream records `event` after
+ * it, so the next step's batch work overlaps the update's tail.  Consumed by
+ * that step; null clears it.  The event must stay alive until the step has
+ * been enqueued. */
+int bulletou_b200_context_wait_before_weights(BulletOuCudaCppContext* ctx, const BulletOuCudaCppEvent* event);
 
 /* L2 read-bandwidth probe (no counterpart in the reference; measurement
  * only): `passes` reads of buffer[0, len) with 16-byte loads cached in L2

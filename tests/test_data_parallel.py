@@ -30,6 +30,26 @@ def test_shard_layout():
     assert dense_gradient_layout(256, 32, 32)[-1][1] + 1 == 256 + 512 * 32 + 32 + 1024 + 32 + 32 + 1
 
 
+def test_sfnn_row_chunks_short_last_chunk():
+    from bulletou_b200.data_parallel import sfnn_row_chunks
+
+    ends = [10 * (j + 1) + j for j in range(15)]  # 15 launches of uneven row counts
+    for lpc, last, sizes in ((3, None, [3, 3, 3, 3, 3]), (3, 1, [3, 3, 3, 3, 2, 1]), (3, 2, [3, 3, 3, 3, 1, 2]),
+                             (1, 1, [1] * 15), (5, 15, [15])):
+        chunks = sfnn_row_chunks(ends, 4, lpc, last)
+        assert [c.last_launch - c.first_launch + 1 for c in chunks] == sizes
+        assert chunks[0].first_launch == 0 and chunks[-1].last_launch == 14
+        start = shard = 0
+        for c, nxt in zip(chunks, chunks[1:] + [None]):
+            assert c.start == start and c.start + c.length == ends[c.last_launch]
+            assert c.padded % 4 == 0 and c.padded >= c.length and c.shard_rows == c.padded // 4
+            assert c.shard_off == shard
+            if nxt is not None:
+                assert nxt.first_launch == c.last_launch + 1
+                assert nxt.shift == c.shift + c.padded - c.length
+            start, shard = c.start + c.length, shard + c.shard_rows
+
+
 class CpuOracleBackend:
     """Trainer backend on CPU tensors; the math is the oracle's."""
 

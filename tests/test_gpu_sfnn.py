@@ -317,3 +317,38 @@ def test_k9k9_zipf_fused_vs_reference_backend(ctx, ref_ctx):
     for nm in a:
         err = float(np.abs(a[nm].astype(np.float64) - c[nm]).max())
         assert err <= 1e-3, f"{nm}: max |diff| {err:.3e} after 20 steps"
+
+
+def test_step_waits_for_weights_ready_event(ctx):
+    """bulletou_b200_context_wait_before_weights: the fused step reads the
+    weights only after the event, here recorded on another stream behind a
+    delayed copy of new FT weights into the runner's table."""
+    import torch
+
+    shape = SMALL
+    w0 = _weights(shape, 111)
+    w1 = dict(w0, l0w=_weights(shape, 112)["l0w"])
+    b = _host_batch(_batch(113, 512, shape.num_stacks))
+    ctx.synchronize()
+    waiting = bs.SfnnTrainStepRunner(ctx, _host_weights(shape, w0), 512, 40)
+    direct = bs.SfnnTrainStepRunner(ctx, _host_weights(shape, w1), 512, 40)
+    src = bo.F32Buffer.from_host(ctx, w1["l0w"])
+    ctx.synchronize()
+    s2 = torch.cuda.Stream()
+    ctx2 = bo.Context(0, stream=s2.cuda_stream)
+    lib = ctx.lib
+    with torch.cuda.stream(s2):
+        torch.cuda._sleep(100_000_000)  # a bounded busy kernel (about 50 ms) ahead of the copy
+        torch.as_tensor(waiting.weights["l0w"], device="cuda:0").copy_(torch.as_tensor(src, device="cuda:0"))
+    ready = bo.Event(ctx2)
+    ready.record(ctx2)
+    lib.call("bulletou_b200_context_wait_before_weights", ctx.as_ptr(), ready._h)
+    waiting.step_no_readback(ctx, _params(1), bo.ScalarLossKind.SigmoidPow(2.0), 1 / 600, b)
+    direct.step_no_readback(ctx, _params(1), bo.ScalarLossKind.SigmoidPow(2.0), 1 / 600, b)
+    a, c = waiting.read_weights(ctx), direct.read_weights(ctx)
+    for nm in a:
+        assert np.array_equal(a[nm], c[nm]), nm
+    # consumed by that step; null clears
+    lib.call("bulletou_b200_context_wait_before_weights", ctx.as_ptr(), None)
+    torch.cuda.synchronize()
+    ctx2.close()

@@ -97,3 +97,42 @@ def test_synthetic_kpp_pairs():
     assert np.all(lo < hi)
     assert all(len(set(r)) == 703 for r in v)
     assert v.max() < n
+
+
+def _round_to_f32(x):
+    """Nearest float32 (ties to even) of a rational, exactly."""
+    import math
+    from fractions import Fraction
+
+    if x == 0:
+        return 0.0
+    a = abs(x)
+    e = a.numerator.bit_length() - a.denominator.bit_length()
+    while Fraction(2) ** e > a:
+        e -= 1
+    while Fraction(2) ** (e + 1) <= a:
+        e += 1
+    ulp = Fraction(2) ** (e - 23)
+    m = a / ulp
+    fl = math.floor(m)
+    r = m - fl
+    if r > Fraction(1, 2) or (r == Fraction(1, 2) and fl % 2 == 1):
+        fl += 1
+    return float(fl * ulp) * (1 if x > 0 else -1)
+
+
+def test_div127_two_term_reciprocal_is_the_ieee_quotient():
+    """sfnn.cu's div127: fma(q, rh, RN(q * rl)) equals RN(q / 127) for every
+    q of the i16 range (the QAT fake-quantisation's clamp range)."""
+    from fractions import Fraction
+    from pathlib import Path
+
+    src = (Path(__file__).resolve().parents[1] / "bulletou_b200" / "csrc" / "sfnn.cu").read_text()
+    assert "__fmaf_rn(q, 0x1.020408p-7f, __fmul_rn(q, 0x1.020408p-35f))" in src
+    rh, rl = float.fromhex("0x1.020408p-7"), float.fromhex("0x1.020408p-35")
+    assert np.float32(rh) == rh and np.float32(rl) == rl
+    assert rh == _round_to_f32(Fraction(1, 127)) and rl == _round_to_f32(Fraction(1, 127) - Fraction(rh))
+    for q in range(-32768, 32768):
+        t = float(np.float32(q) * np.float32(rl))  # the f32 product, correctly rounded
+        got = _round_to_f32(Fraction(q) * Fraction(rh) + Fraction(t))
+        assert got == _round_to_f32(Fraction(q, 127)), q
