@@ -55,6 +55,9 @@ constexpr int kPieceRowWarps = 8;
 constexpr int kKingsPerLaunch = 3;  // FT row kernel: king blocks per launch (L2 working set)
 constexpr int kPieceRowCtas = 3;    // FT row kernel: resident CTAs per SM (persistent grid)
 constexpr int kTileRanks = 4096;    // half-positions per rank tile of the FT row index (24 MB of gradient rows)
+// (Loading a row's Ranger state before its gradient sum, to overlap the two
+// latencies, made the FT row phase slower, 2.05 -> 2.33 ms at B = 65536: the
+// state stream then competes with the gathers for L2.)
 
 __device__ __forceinline__ float crelu01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
 __device__ __forceinline__ float crelu_grad(float a, float g) { return a > 0.0f && a < 1.0f ? g : 0.0f; }
@@ -700,6 +703,12 @@ __device__ __forceinline__ int dp4a_u8s8(unsigned u8x4, int s8x4, int acc) {
 // in shared memory packed for dp4a: entry (k4, quad) is an int4 whose word j
 // holds the four i8 weights of inputs 4 k4 .. 4 k4 + 3 for output 4 quad + j;
 // the lattice FT outputs (0..127) are packed four to a word on the fly.
+// Warp per sample: lane l takes the float4 groups k4 = l, l + 32, ... of the
+// sample's combined row (all its loads independent), quantises them to u8
+// and accumulates all 16 outputs with dp4a against the bucket's i8 weights
+// in shared memory ([output group og][k4] int4, conflict-free); the 16
+// per-lane sums are then reduced across the warp by halving exchanges (lane
+// l ends with output (l >> 1) & 15).  Integer sums: any order is exact.
 __global__ void __launch_bounds__(256) l1_forward16_int_kernel(L1IntArgs a) {
     extern __shared__ int4 wq4[];
     const int t = blockIdx.x;
@@ -717,40 +726,67 @@ __global__ void __launch_bounds__(256) l1_forward16_int_kernel(L1IntArgs a) {
     const int w4 = a.width >> 2;
     const float* src = a.w_eff + static_cast<size_t>(s) * a.width * 16;  // [width][16]
     for (int i = threadIdx.x; i < w4 * 4; i += blockDim.x) {
-        const int k4 = i >> 2, quad = i & 3;
+        const int og = i / w4, k4 = i - og * w4;
         int word[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             unsigned packed = 0;
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-                packed |= (static_cast<unsigned>(qat_int64(src[(4 * k4 + e) * 16 + 4 * quad + j])) & 0xffu) << (8 * e);
+                packed |= (static_cast<unsigned>(qat_int64(src[(4 * k4 + e) * 16 + 4 * og + j])) & 0xffu) << (8 * e);
             word[j] = static_cast<int>(packed);
         }
-        wq4[i] = make_int4(word[0], word[1], word[2], word[3]);
+        wq4[og * w4 + k4] = make_int4(word[0], word[1], word[2], word[3]);
     }
     __syncthreads();
-    const int og = threadIdx.x & 3;
-    for (int p = pb + (threadIdx.x >> 2); p < pe; p += 64) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int kGroups = 16;  // float4 groups in flight per lane
+    for (int p = pb + warp; p < pe; p += 8) {
         const int b = a.tiles.order[p];
         const float4* c4 = reinterpret_cast<const float4*>(a.combined) + static_cast<size_t>(b) * w4;
-        int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
-        for (int k4 = 0; k4 < w4; ++k4) {
-            const float4 c = __ldg(c4 + k4);
-            const unsigned cv = static_cast<unsigned>(qat_int127(c.x)) | (static_cast<unsigned>(qat_int127(c.y)) << 8) |
-                                (static_cast<unsigned>(qat_int127(c.z)) << 16) |
-                                (static_cast<unsigned>(qat_int127(c.w)) << 24);
-            const int4 w = wq4[k4 * 4 + og];
-            acc0 = dp4a_u8s8(cv, w.x, acc0);
-            acc1 = dp4a_u8s8(cv, w.y, acc1);
-            acc2 = dp4a_u8s8(cv, w.z, acc2);
-            acc3 = dp4a_u8s8(cv, w.w, acc3);
-        }
-        const int accs[4] = {acc0, acc1, acc2, acc3};
+        int acc[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int o = 4 * og + q;
-            const long long r = static_cast<long long>(accs[q]) + a.b_int[s * 16 + o];
+        for (int o = 0; o < 16; ++o) acc[o] = 0;
+        for (int k0 = 0; k0 < w4; k0 += 32 * kGroups) {
+            float4 c[kGroups];
+#pragma unroll
+            for (int g = 0; g < kGroups; ++g) {
+                const int k4 = k0 + g * 32 + lane;
+                c[g] = k4 < w4 ? __ldg(c4 + k4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int g = 0; g < kGroups; ++g) {
+                const int k4 = k0 + g * 32 + lane;
+                if (k4 >= w4) break;
+                const unsigned cv = static_cast<unsigned>(qat_int127(c[g].x)) |
+                                    (static_cast<unsigned>(qat_int127(c[g].y)) << 8) |
+                                    (static_cast<unsigned>(qat_int127(c[g].z)) << 16) |
+                                    (static_cast<unsigned>(qat_int127(c[g].w)) << 24);
+#pragma unroll
+                for (int og = 0; og < 4; ++og) {
+                    const int4 w = wq4[og * w4 + k4];
+                    acc[4 * og + 0] = dp4a_u8s8(cv, w.x, acc[4 * og + 0]);
+                    acc[4 * og + 1] = dp4a_u8s8(cv, w.y, acc[4 * og + 1]);
+                    acc[4 * og + 2] = dp4a_u8s8(cv, w.z, acc[4 * og + 2]);
+                    acc[4 * og + 3] = dp4a_u8s8(cv, w.w, acc[4 * og + 3]);
+                }
+            }
+        }
+        // halving exchanges: 8 + 4 + 2 + 1 + 1 shuffles
+#pragma unroll
+        for (int d = 16, n = 8; d >= 2; d >>= 1, n >>= 1) {
+            const bool upper = (lane & d) != 0;
+#pragma unroll
+            for (int i = 0; i < n; ++i) {
+                const int send = upper ? acc[i] : acc[i + n];
+                const int keep = upper ? acc[i + n] : acc[i];
+                acc[i] = keep + __shfl_xor_sync(kFull, send, d);
+            }
+        }
+        const int total = acc[0] + __shfl_xor_sync(kFull, acc[0], 1);
+        if ((lane & 1) == 0) {
+            const int o = (lane >> 1) & 15;
+            const long long r = static_cast<long long>(total) + a.b_int[s * 16 + o];
             a.raw[static_cast<size_t>(b) * 16 + o] = static_cast<int>(r);
             a.l1[static_cast<size_t>(b) * 16 + o] = qat_raw_to_float(r);
         }
@@ -1487,6 +1523,33 @@ __device__ __forceinline__ void stv(float* p, const float* v) {
     }
 }
 
+// The Ranger update of one column chunk from its loaded weights and moments.
+template <int VEC>
+__device__ __forceinline__ void ranger_row_update(const PieceRowArgs& a, size_t off, const float* g, bool quiet_row,
+                                                  float* seen, float* w, float* m, float* v) {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) seen[e] = g[e];
+    if (quiet_row && a.skip_quiet && !a.ranger.do_lookahead) {
+        bool quiet = true;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+            quiet = quiet && (__float_as_uint(m[e]) | __float_as_uint(v[e])) == 0u && weight_is_quiet(w[e], a.ranger);
+        if (quiet) return;
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) radam_coordinate(a.ranger.gradient_factor * g[e], a.ranger, w[e], m[e], v[e]);
+    if (a.ranger.do_lookahead) {
+        float sl[VEC];
+        ldv<VEC>(a.slow + off, sl);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) w[e] = lookahead_coordinate(w[e], sl[e], a.ranger);
+        stv<VEC>(a.slow + off, w);
+    }
+    stv<VEC>(a.weights + off, w);
+    stv<VEC>(a.momentum + off, m);
+    stv<VEC>(a.velocity + off, v);
+}
+
 // Applies the row update for one column chunk: Ranger / write / accumulate.
 // `seen` receives the row's gradient as the virtual row sees it (the
 // accumulated value in accumulate mode).
@@ -1506,31 +1569,11 @@ __device__ __forceinline__ void row_update(const PieceRowArgs& a, size_t off, co
 #pragma unroll
         for (int e = 0; e < VEC; ++e) seen[e] = x[e];
     } else {
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) seen[e] = g[e];
         float w[VEC], m[VEC], v[VEC];
         ldv<VEC>(a.weights + off, w);
         ldv<VEC>(a.momentum + off, m);
         ldv<VEC>(a.velocity + off, v);
-        if (quiet_row && a.skip_quiet && !a.ranger.do_lookahead) {
-            bool quiet = true;
-#pragma unroll
-            for (int e = 0; e < VEC; ++e)
-                quiet = quiet && (__float_as_uint(m[e]) | __float_as_uint(v[e])) == 0u && weight_is_quiet(w[e], a.ranger);
-            if (quiet) return;
-        }
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) radam_coordinate(a.ranger.gradient_factor * g[e], a.ranger, w[e], m[e], v[e]);
-        if (a.ranger.do_lookahead) {
-            float sl[VEC];
-            ldv<VEC>(a.slow + off, sl);
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) w[e] = lookahead_coordinate(w[e], sl[e], a.ranger);
-            stv<VEC>(a.slow + off, w);
-        }
-        stv<VEC>(a.weights + off, w);
-        stv<VEC>(a.momentum + off, m);
-        stv<VEC>(a.velocity + off, v);
+        ranger_row_update<VEC>(a, off, g, quiet_row, seen, w, m, v);
     }
 }
 
