@@ -167,6 +167,9 @@ def parse_args():
                     help="per-GPU batch (sfnn, halfkp, kppt) or global batch (sfnn_k9k9)")
     ap.add_argument("--dp-chunk-launches", type=int, default=3,
                     help="N > 1: FT row launches per exchanged chunk (SFNN)")
+    ap.add_argument("--dp-exchange", choices=("p2p", "collectives"), default="p2p",
+                    help="N > 1 (SFNN): FT rows exchanged over peer memory by the row kernels, or through NCCL "
+                         "reduce-scatter / all-gather")
     ap.add_argument("--dp-last-chunk-launches", type=int, default=1,
                     help="N > 1: FT row launches of the last exchanged chunk (SFNN; 0: no separate last chunk)")
     ap.add_argument("--qat", choices=tuple(SFNN_QAT_MODES), default="all",
@@ -1071,7 +1074,8 @@ def run_sfnn_data_parallel(args, wl, rank, world, local, dist):
     tr = SfnnDataParallelTrainer(backend, dist, sfnn_host_weights(wl.stacks), args.batch, SFNN_ACTIVE,
                                  lr_multipliers=sfnn_lr_multipliers(args.qat),
                                  launches_per_chunk=args.dp_chunk_launches,
-                                 last_chunk_launches=args.dp_last_chunk_launches or None)
+                                 last_chunk_launches=args.dp_last_chunk_launches or None,
+                                 exchange=args.dp_exchange)
     host, devb = sfnn_batches(args, ctx, rank, workload=wl)
     loss_kind = bo.ScalarLossKind.SigmoidPow(2.0)
     inv = 1.0 / 600.0
@@ -1135,18 +1139,28 @@ def run_sfnn_data_parallel(args, wl, rank, world, local, dist):
         bind(i)
         tr.step_device(ranger(step), loss_kind, inv, finalize_loss=False)
     tr.timing = False
-    tr.join()
+    tr.check()  # raises if a peer-exchange wait timed out in any step above
     exchange = backend.exchange_timing(tr)
+    exchange["mode"] = tr.exchange
     exchange["exchange_tail_after_rows_ms_max_over_ranks"] = max_over_ranks(
         dist, exchange.get("exchange_tail_after_rows_ms", 0.0))
     torch.cuda.synchronize()
+    tr.close()
     dist.barrier()
+    how = ("FT rows stored into their owners' slots by the row kernels, shards updated and stored into every "
+           "rank's table over NVLink, small groups by NCCL all-reduce" if tr.exchange == "p2p" else
+           "NCCL reduce-scatter / all-reduce / all-gather")
     return {"total_ms": total_ms, "phase_ms": phase_ms, "clocks": clocks.summary(),
             "e2e": {"value": args.steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
                     "h2d_bytes_per_step": int(sources[0].nbytes), "d2h_bytes_per_step": 4, "steps": args.steps,
-                    "path": "SfnnDataParallelTrainer.step_device per rank (NCCL reduce-scatter / all-reduce / "
-                            "all-gather), inputs from page-locked host memory, mean loss read back every step"},
-            "gpu_launches": (sfnn_launches_per_step(args.qat) + 1) * args.steps, "final_loss": losses[-1],
+                    "path": f"SfnnDataParallelTrainer.step_device per rank ({how}), inputs from page-locked host "
+                            "memory, mean loss read back every step"},
+            # the fused step's kernels; exchange: p2p adds per chunk a signal after its last row launch and the
+            # owner's wait / shard Ranger / signal, plus the step's wait before the fold; collectives adds
+            # the shard Ranger per chunk (NCCL's own kernels are not counted)
+            "gpu_launches": (sfnn_launches_per_step(args.qat) +
+                             (4 * len(tr.chunks) + 1 if tr.exchange == "p2p" else len(tr.chunks))) * args.steps,
+            "final_loss": losses[-1],
             "exchange": exchange}
 
 

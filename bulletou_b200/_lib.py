@@ -76,6 +76,13 @@ class TeacherConfig(ctypes.Structure):
                 ("result_blend", F), ("score_blend", F), ("rscale", F), ("score_drop_abs", I)]
 
 
+class RowExchange(ctypes.Structure):
+    """BulletOuB200RowExchange."""
+
+    _fields_ = [("world", Z), ("rank", Z), ("recv", U64 * 8), ("table", U64 * 8), ("flags", U64 * 8),
+                ("slot_rows", Z), ("epoch", I)]
+
+
 class LossSpec(ctypes.Structure):
     """BulletOuB200LossSpec."""
 
@@ -170,6 +177,14 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_sfnn_train_step_device": [P, P, Z, Z] + [P] * 17,
     "bulletou_b200_sfnn_dense_gradient_len": [P, I, I, I, P],
     "bulletou_b200_sfnn_local_gradients_device": [P, P, Z, Z] + [P] * 17 + [Z],
+    "bulletou_b200_sfnn_local_gradients_exchange_device": [P, P, Z, Z] + [P] * 20 + [Z],
+    "bulletou_b200_sfnn_shard_ranger_exchange_device": [P, P, Z, Z, Z, Z, Z, P, P, P, P, P, P, Z, Z, P],
+    "bulletou_b200_exchange_wait_device": [P, P, Z, Z, I, P],
+    "bulletou_b200_context_wait_flags_before_weights": [P, P, Z, Z, I, P],
+    "bulletou_b200_f32_buffer_ipc_handle": [P, P],
+    "bulletou_b200_i32_buffer_ipc_handle": [P, P],
+    "bulletou_b200_ipc_open": [P, P, P],
+    "bulletou_b200_ipc_close": [P, U64],
     "bulletou_b200_sfnn_row_launches": [P, P, P, Z],
     # SFNN QAT (reference entries)
     "bulletou_layer_qat": [P, P, P, F, F, F, Z, Z, Z, F],

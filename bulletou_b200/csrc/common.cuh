@@ -44,6 +44,12 @@ struct BulletOuCudaCppContext {
     // Event the next SFNN fused step waits for before reading a weight
     // (bulletou_b200_context_wait_before_weights); cleared by that step.
     cudaEvent_t weights_ready = nullptr;
+    // Flags the next SFNN fused step waits for before reading a weight
+    // (bulletou_b200_context_wait_flags_before_weights); cleared by that step.
+    const int* weights_flags = nullptr;
+    int weights_flag_count = 0;
+    int weights_flag_epoch = 0;
+    int* weights_flag_error = nullptr;
     // Stage profiler (bulletou_b200_profile_*): events recorded on `stream`
     // at phase boundaries of the fused steps, read back after the run.
     bool prof_on = false;

@@ -441,6 +441,25 @@ int bulletou_b200_context_wait_before_weights(BulletOuCudaCppContext* ctx, const
     return ok();
 }
 
+int bulletou_b200_context_wait_flags_before_weights(BulletOuCudaCppContext* ctx,
+                                                    const BulletOuCudaCppI32Buffer* flags, size_t offset,
+                                                    size_t count, int epoch, BulletOuCudaCppI32Buffer* error) {
+    if (validate_context(ctx) != 0) return -1;
+    if (flags == nullptr || count == 0) {
+        ctx->weights_flags = nullptr;
+        return ok();
+    }
+    if (validate_i32(ctx, flags, offset + count, "weights flags") != 0 ||
+        validate_i32(ctx, error, 1, "weights flag error word") != 0)
+        return -1;
+    if (count > 0x7fffffffULL) return fail_message("context_wait_flags_before_weights: too many flags");
+    ctx->weights_flags = flags->ptr + offset;
+    ctx->weights_flag_count = static_cast<int>(count);
+    ctx->weights_flag_epoch = epoch;
+    ctx->weights_flag_error = error->ptr;
+    return ok();
+}
+
 int bulletou_b200_l2_read_probe(BulletOuCudaCppContext* ctx, const BulletOuCudaCppF32Buffer* buffer, size_t len,
                                 int passes, BulletOuCudaCppF32Buffer* sink) {
     if (validate_f32(ctx, buffer, len, "L2 probe buffer") != 0) return -1;

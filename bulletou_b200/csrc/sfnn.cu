@@ -37,6 +37,7 @@
 #include "ft_rows_mma.cuh"
 #include "king_sort.cuh"
 #include "sfnn.cuh"
+#include "exchange.cuh"
 #include "sparse_rows.cuh"
 
 namespace bou {
@@ -1483,6 +1484,33 @@ struct PieceRowArgs {
     // (-1: light) and the sums [slot][width]; null: the segment plan above.
     const int* key_slot;
     const float* key_partials;
+    // Data-parallel peer exchange (kRowWrite): scatter_world > 0 stores row r
+    // of the launch's chunk into its owner's receive slot instead of
+    // gradients: owner o = (r - chunk_start) / chunk_shard_rows, at row
+    // scatter_rank * scatter_slot_rows + chunk_shard_off + (r - chunk_start) -
+    // o * chunk_shard_rows of scatter_recv[o].
+    float* scatter_recv[kExchangeMaxRanks];
+    int scatter_world;
+    int scatter_rank;
+    size_t scatter_slot_rows;
+    size_t chunk_start;
+    size_t chunk_shard_rows;
+    size_t chunk_shard_off;
+};
+
+// Peer-exchange descriptor of the row launches (host side): per launch j its
+// chunk and, at a chunk's last launch, the chunk index to signal.
+struct RowScatter {
+    float* recv[kExchangeMaxRanks];
+    int world;
+    int rank;
+    size_t slot_rows;
+    const size_t* chunk_start;
+    const size_t* shard_rows;
+    const size_t* shard_off;
+    const long long* signal;
+    PeerFlags flags;
+    int epoch;
 };
 
 constexpr int kHeavyRow = 128;  // FT row phase on king-concentrated batches: 512 -> 3.75 ms, 128 -> 3.03 ms
@@ -1550,6 +1578,19 @@ __device__ __forceinline__ void ranger_row_update(const PieceRowArgs& a, size_t 
     stv<VEC>(a.velocity + off, v);
 }
 
+// Where kRowWrite stores the gradient at offset row * width + column: the
+// local gradient table, or the row owner's receive slot (peer exchange).
+__device__ __forceinline__ float* row_write_target(const PieceRowArgs& a, size_t off) {
+    if (a.scatter_world == 0) return a.gradients + off;
+    const size_t row = off / static_cast<size_t>(a.width);
+    const size_t col = off - row * static_cast<size_t>(a.width);
+    const size_t rel = row - a.chunk_start;
+    const size_t owner = rel / a.chunk_shard_rows;
+    const size_t local = a.chunk_shard_off + (rel - owner * a.chunk_shard_rows);
+    return a.scatter_recv[owner] +
+           (static_cast<size_t>(a.scatter_rank) * a.scatter_slot_rows + local) * static_cast<size_t>(a.width) + col;
+}
+
 // Applies the row update for one column chunk: Ranger / write / accumulate.
 // `seen` receives the row's gradient as the virtual row sees it (the
 // accumulated value in accumulate mode).
@@ -1557,7 +1598,7 @@ template <int VEC, int MODE>
 __device__ __forceinline__ void row_update(const PieceRowArgs& a, size_t off, const float* g, bool quiet_row,
                                            float* seen) {
     if constexpr (MODE == kRowWrite) {
-        stv<VEC>(a.gradients + off, g);
+        stv<VEC>(row_write_target(a, off), g);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) seen[e] = g[e];
     } else if constexpr (MODE == kRowAccumulate) {
@@ -1733,6 +1774,7 @@ __global__ void __launch_bounds__(kPieceRowWarps * 32, 3) piece_row_kernel(Piece
     const int items = a.pieces * a.col_groups;
     for (int gw = blockIdx.x * kPieceRowWarps + (threadIdx.x >> 5); gw < items; gw += gridDim.x * kPieceRowWarps)
         piece_rows<VEC, ITERS, MODE>(a, gw, lane);
+    if (MODE == kRowWrite && a.scatter_world > 0) __threadfence_system();  // peer stores before the chunk's signal
 }
 
 // Segments per key: a row (k, p) is heavy when its entries over all its keys
@@ -1820,7 +1862,13 @@ int piece_row_launches(const SfnnDims& d, size_t* row_end, size_t cap) {
 
 template <int MODE>
 int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec, const size_t* row_shift,
-                           const cudaEvent_t* events) {
+                           const cudaEvent_t* events, const RowScatter* scatter) {
+    if (scatter != nullptr) {
+        for (int r = 0; r < scatter->world; ++r) a.scatter_recv[r] = scatter->recv[r];
+        a.scatter_world = scatter->world;
+        a.scatter_rank = scatter->rank;
+        a.scatter_slot_rows = scatter->slot_rows;
+    }
     // Persistent grid: three CTAs per SM, each warp loops over (piece, column
     // group) work items.
     const int warps = a.pieces * a.col_groups;
@@ -1834,10 +1882,21 @@ int launch_piece_rows_mode(BulletOuCudaCppContext* ctx, PieceRowArgs a, int vec,
         // Data-parallel layout: launch j's rows land row_shift[j] rows further,
         // so each launch's range starts a chunk the collectives can split evenly.
         if (row_shift != nullptr) a.gradients = gradients + row_shift[j] * static_cast<size_t>(a.width);
+        if (scatter != nullptr) {
+            a.chunk_start = scatter->chunk_start[j];
+            a.chunk_shard_rows = scatter->shard_rows[j];
+            a.chunk_shard_off = scatter->shard_off[j];
+        }
         if (vec == 8) piece_row_kernel<8, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
         else if (vec == 4) piece_row_kernel<4, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
         else piece_row_kernel<1, 1, MODE><<<blocks, kPieceRowWarps * 32, 0, ctx->stream>>>(a);
         if (check_launch("SFNN FT row kernel launch") != 0) return -1;
+        // peer exchange: the chunk's rows have landed in their owners' slots
+        if (scatter != nullptr && scatter->signal[j] >= 0 &&
+            launch_exchange_signal(ctx, scatter->flags, scatter->world,
+                                   static_cast<size_t>(scatter->signal[j]) * scatter->world + scatter->rank,
+                                   scatter->epoch) != 0)
+            return -1;
         if (events != nullptr) {
             cudaError_t st = cudaEventRecord(events[j], ctx->stream);
             if (st != cudaSuccess) return fail("cudaEventRecord SFNN row launch", st);
@@ -1937,7 +1996,8 @@ bool piece_rows_use_mma(int mode, const PieceRowArgs& a, const HeavyMmaInputs* m
 }
 
 int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, const size_t* row_shift = nullptr,
-                      const cudaEvent_t* events = nullptr, const HeavyMmaInputs* mma = nullptr) {
+                      const cudaEvent_t* events = nullptr, const HeavyMmaInputs* mma = nullptr,
+                      const RowScatter* scatter = nullptr) {
     const int vec = piece_row_vec(mode, a);
     a.group_width = vec == 8 ? 256 : (vec == 4 ? 128 : 32);
     a.col_groups = (a.width + a.group_width - 1) / a.group_width;
@@ -1999,9 +2059,9 @@ int launch_piece_rows(BulletOuCudaCppContext* ctx, int mode, PieceRowArgs a, con
         if (check_launch("SFNN heavy-row segment launch") != 0) return -1;
     }
     switch (mode) {
-        case kRowRanger: return launch_piece_rows_mode<kRowRanger>(ctx, a, vec, row_shift, events);
-        case kRowWrite: return launch_piece_rows_mode<kRowWrite>(ctx, a, vec, row_shift, events);
-        default: return launch_piece_rows_mode<kRowAccumulate>(ctx, a, vec, row_shift, events);
+        case kRowRanger: return launch_piece_rows_mode<kRowRanger>(ctx, a, vec, row_shift, events, nullptr);
+        case kRowWrite: return launch_piece_rows_mode<kRowWrite>(ctx, a, vec, row_shift, events, scatter);
+        default: return launch_piece_rows_mode<kRowAccumulate>(ctx, a, vec, row_shift, events, nullptr);
     }
 }
 
@@ -2572,7 +2632,7 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
               const BulletOuB200RangerStep* ranger, float* const* wm, float* const* mm, float* const* vm,
               float* const* sm, float* output, float* per_sample, float* mog, float* weighted_sum, float* mean,
               float* ft_grad, float* dense_grad, const size_t* row_shift = nullptr,
-              const cudaEvent_t* row_events = nullptr) {
+              const cudaEvent_t* row_events = nullptr, const RowScatter* scatter = nullptr) {
     // phases: batch sorts and tiles, inverse index, [weights wait] fold and L1
     // weights, FT forward, L1 + head, L1 backward, small groups, FT rows
     ctx->prof_marks_per_step = 9;
@@ -2616,6 +2676,13 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
         const cudaError_t st = cudaStreamWaitEvent(ctx->stream, ctx->weights_ready, 0);
         ctx->weights_ready = nullptr;
         if (st != cudaSuccess) return fail("cudaStreamWaitEvent weights-ready event", st);
+    }
+    if (ctx->weights_flags != nullptr) {
+        const int* flags = ctx->weights_flags;
+        ctx->weights_flags = nullptr;
+        if (launch_exchange_wait(ctx, flags, ctx->weights_flag_count, ctx->weights_flag_epoch,
+                                 ctx->weights_flag_error) != 0)
+            return -1;
     }
     if (sfnn_prepare_weights(ctx, d, w, nullptr, &plan) != 0) return -1;
     prof_mark(ctx);
@@ -2674,7 +2741,7 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
         r.skip_quiet = ranger_zero_step_is_identity(ra) ? 1 : 0;
         if (launch_piece_rows(ctx, kRowRanger, r, nullptr, nullptr, mp) != 0) return -1;
     } else {
-        if (launch_piece_rows(ctx, kRowWrite, r, row_shift, row_events, mp) != 0) return -1;
+        if (launch_piece_rows(ctx, kRowWrite, r, row_shift, row_events, mp, scatter) != 0) return -1;
     }
     prof_mark(ctx);
     return 0;
@@ -3314,6 +3381,95 @@ int bulletou_b200_sfnn_local_gradients_device(
                   loss->finalize_loss, nullptr, nullptr, nullptr, nullptr, nullptr, output->ptr, per_sample->ptr,
                   mean_output_gradients->ptr, weighted_sum->ptr, mean->ptr, ft_gradients->ptr, dense_gradients->ptr,
                   row_shift, row_events != nullptr ? events : nullptr) != 0)
+        return -1;
+    return ok();
+}
+
+int bulletou_b200_sfnn_local_gradients_exchange_device(
+    BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* targets,
+    const BulletOuCudaCppF32Buffer* entry_weights, const BulletOuB200LossSpec* loss,
+    BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* dense_gradients,
+    BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat, const BulletOuB200RowExchange* x,
+    const size_t* launch_chunk_start, const size_t* launch_shard_rows, const size_t* launch_shard_off,
+    const long long* launch_signal, BulletOuCudaCppEvent* const* row_events, size_t n_row_launches) {
+    if (shape == nullptr || params == nullptr) return fail_message("SFNN shape / parameter array must not be null");
+    if (x == nullptr || launch_chunk_start == nullptr || launch_shard_rows == nullptr || launch_shard_off == nullptr ||
+        launch_signal == nullptr)
+        return fail_message("SFNN local gradients exchange: the exchange and per-launch arrays must not be null");
+    if (x->world < 1 || x->world > static_cast<size_t>(kExchangeMaxRanks) || x->rank >= x->world)
+        return fail_messagef("SFNN local gradients exchange: world %zu / rank %zu outside 1..%d", x->world, x->rank,
+                             kExchangeMaxRanks);
+    SfnnDims d{};
+    LossArgs la{};
+    if (sfnn_dims(shape->input_size, shape->ft_size, shape->l1_hidden, shape->l1_skip, shape->l2_size,
+                  shape->num_stacks, batch, max_active, shape->ft_factorizer_alpha, shape->factorizer_shared_alpha,
+                  &d) != 0 ||
+        loss_args(loss, batch, &la) != 0)
+        return -1;
+    d.has_l1f = params[4] != nullptr;
+    d.has_l2f = params[8] != nullptr;
+    d.has_l3f = params[12] != nullptr;
+    const SfnnGroupLayout g = sfnn_group_layout(d);
+    if (validate_sfnn_weights(ctx, d, params, "params") != 0 ||
+        validate_i32(ctx, stm_indices, batch * max_active, "stm_indices") != 0 ||
+        validate_i32(ctx, nstm_indices, batch * max_active, "nstm_indices") != 0 ||
+        validate_i32(ctx, buckets, batch, "buckets") != 0 || validate_f32(ctx, targets, batch, "targets") != 0 ||
+        validate_f32(ctx, entry_weights, batch, "entry_weights") != 0 ||
+        validate_f32(ctx, dense_gradients, g.begin[kSfGroups], "dense_gradients") != 0 ||
+        validate_f32(ctx, output, batch, "output") != 0 || validate_f32(ctx, per_sample, batch, "per_sample") != 0 ||
+        validate_f32(ctx, mean_output_gradients, batch, "mean_output_gradients") != 0 ||
+        validate_f32(ctx, weighted_sum, 1, "weighted_sum") != 0 || validate_f32(ctx, mean, 1, "mean") != 0)
+        return -1;
+    const int launches = piece_row_launches(d, nullptr, 0);
+    if (n_row_launches != static_cast<size_t>(launches))
+        return fail_messagef("SFNN local gradients exchange: %d row launches, got %zu", launches, n_row_launches);
+    RowScatter sc{};
+    sc.world = static_cast<int>(x->world);
+    sc.rank = static_cast<int>(x->rank);
+    sc.slot_rows = x->slot_rows;
+    sc.chunk_start = launch_chunk_start;
+    sc.shard_rows = launch_shard_rows;
+    sc.shard_off = launch_shard_off;
+    sc.signal = launch_signal;
+    sc.epoch = x->epoch;
+    size_t ends[64];
+    if (launches > 64) return fail_message("SFNN local gradients exchange: too many row launches");
+    piece_row_launches(d, ends, 64);
+    size_t row0 = 0;
+    for (int j = 0; j < launches; ++j) {
+        // every row of launch j must fall in its chunk's rows, and the chunk's
+        // shard inside a receive slot
+        const size_t row_end = ends[j];
+        const size_t sr = launch_shard_rows[j];
+        if (sr == 0 || launch_chunk_start[j] > row0 || row_end - launch_chunk_start[j] > sr * x->world ||
+            launch_shard_off[j] + sr > x->slot_rows || launch_signal[j] >= static_cast<long long>(launches))
+            return fail_messagef("SFNN local gradients exchange: launch %d's chunk does not hold its rows", j);
+        row0 = row_end;
+    }
+    for (size_t r = 0; r < x->world; ++r) {
+        if (x->recv[r] == 0 || x->flags[r] == 0) return fail_messagef("row exchange: rank %zu's buffers missing", r);
+        sc.recv[r] = reinterpret_cast<float*>(static_cast<uintptr_t>(x->recv[r]));
+        sc.flags.p[r] = reinterpret_cast<int*>(static_cast<uintptr_t>(x->flags[r]));
+    }
+    cudaEvent_t events[64];
+    if (row_events != nullptr) {
+        for (int j = 0; j < launches; ++j) {
+            if (row_events[j] == nullptr || row_events[j]->device != ctx->device)
+                return fail_message("SFNN local gradients exchange: row event missing or on another device");
+            events[j] = row_events[j]->event;
+        }
+    }
+    if (set_device(ctx) != 0) return -1;
+    const SfnnWeights w = weights_from(params);
+    if (apply_qat(qat, w, &d) != 0) return -1;
+    if (sfnn_step(ctx, d, w, stm_indices->ptr, nstm_indices->ptr, buckets->ptr, targets->ptr, entry_weights->ptr, la,
+                  loss->finalize_loss, nullptr, nullptr, nullptr, nullptr, nullptr, output->ptr, per_sample->ptr,
+                  mean_output_gradients->ptr, weighted_sum->ptr, mean->ptr, nullptr, dense_gradients->ptr, nullptr,
+                  row_events != nullptr ? events : nullptr, &sc) != 0)
         return -1;
     return ok();
 }

@@ -38,8 +38,8 @@ from typing import Optional
 
 import numpy as np
 
-from .cuda_cpp import (NNUE_WEIGHT_NAMES, F32Buffer, I32Buffer, NnueForwardHostWeights, RangerDeviceState,
-                       RangerUpdateParams, ScalarLossKind, ScalarLossWorkspace, ranger_update_device)
+from .cuda_cpp import (NNUE_WEIGHT_NAMES, CudaCppError, F32Buffer, I32Buffer, NnueForwardHostWeights,
+                       RangerDeviceState, RangerUpdateParams, ScalarLossKind, ScalarLossWorkspace, ranger_update_device)
 
 
 @dataclass(frozen=True)
@@ -241,6 +241,129 @@ class B200Backend:
                           **{k: round(v / n, 4) for k, v in pc.items()}} for c, pc in zip(tr.chunks, per_chunk)]
         return out
 
+    # -- peer-memory exchange (SfnnDataParallelTrainer, exchange="p2p") ---------
+    supports_peer_exchange = True
+
+    def prepare_peer_exchange(self, tr: "SfnnDataParallelTrainer") -> None:
+        """Receive slots and flags on this rank, CUDA IPC handles of them and
+        of the FT table exchanged over the process group, peers' buffers
+        opened: the descriptor of bulletou_b200_sfnn_local_gradients_exchange_
+        device and bulletou_b200_sfnn_shard_ranger_exchange_device."""
+        from ._lib import RowExchange
+
+        world, rank, W = tr.world, tr.rank, tr.shape.ft_size
+        if world > 8:
+            raise CudaCppError("the peer exchange supports up to 8 ranks")
+        last = tr.chunks[-1]
+        slot_rows = last.shard_off + last.shard_rows
+        n_chunks = len(tr.chunks)
+        tr._recv = F32Buffer(self.ctx, world * slot_rows * W)
+        tr._flags = I32Buffer.from_host(self.ctx, np.zeros(2 * n_chunks * world, np.int32))
+        tr._xerr = I32Buffer.from_host(self.ctx, np.zeros(1, np.int32))
+        own = (tr._recv, tr.weights["l0w"], tr._flags)
+        mine = []
+        for b in own:
+            h = (ctypes.c_ubyte * 64)()
+            kind = "f32" if isinstance(b, F32Buffer) else "i32"
+            self.lib.call(f"bulletou_b200_{kind}_buffer_ipc_handle", b.as_ptr(), h)
+            mine.append(bytes(h))
+        gathered = [None] * world
+        tr.dist.all_gather_object(gathered, mine)
+        x = RowExchange()
+        x.world, x.rank, x.slot_rows, x.epoch = world, rank, slot_rows, 0
+        tr._opened = []
+        for r in range(world):
+            for k, field in enumerate((x.recv, x.table, x.flags)):
+                if r == rank:
+                    field[r] = own[k].device_ptr()
+                else:
+                    addr = ctypes.c_uint64()
+                    h = (ctypes.c_ubyte * 64).from_buffer_copy(gathered[r][k])
+                    self.lib.call("bulletou_b200_ipc_open", self.ctx.as_ptr(), h, ctypes.byref(addr))
+                    field[r] = addr.value
+                    tr._opened.append(addr.value)
+        tr._x = x
+        n = len(tr.row_ends)
+        chunk_of = [tr.chunks[tr.launch_chunk[j]] for j in range(n)]
+        tr._launch_start = (ctypes.c_size_t * n)(*[c.start for c in chunk_of])
+        tr._launch_shard_rows = (ctypes.c_size_t * n)(*[c.shard_rows for c in chunk_of])
+        tr._launch_shard_off = (ctypes.c_size_t * n)(*[c.shard_off for c in chunk_of])
+        tr._launch_signal = (ctypes.c_longlong * n)(*[tr.launch_chunk[j] if j == chunk_of[j].last_launch else -1
+                                                      for j in range(n)])
+        tr._epoch = 0
+
+    def sfnn_step_peer_exchange(self, tr: "SfnnDataParallelTrainer", loss_spec, params) -> None:
+        """The local step stores its FT gradient rows into their owners'
+        receive slots (signalling each chunk); on the comm stream the small
+        groups' all-reduce + Ranger, then per chunk this rank's shard: wait for
+        every rank's rows, sum, Ranger, store into every rank's table, signal.
+        The next step runs its batch-only work first and waits for every
+        owner's signals (and this rank's comm stream) before its first weight
+        read."""
+        torch, lib, ctx = self.torch, self.lib, self.ctx
+        world, rank, W = tr.world, tr.rank, tr.shape.ft_size
+        nc = len(tr.chunks)
+        if tr._ready_pending:
+            lib.call("bulletou_b200_context_wait_before_weights", ctx.as_ptr(), tr._ready._h)
+            lib.call("bulletou_b200_context_wait_flags_before_weights", ctx.as_ptr(), tr._flags.as_ptr(), nc * world,
+                     nc * world, tr._epoch, tr._xerr.as_ptr())
+        tr._epoch += 1
+        x = tr._x
+        x.epoch = tr._epoch
+        compute = torch.cuda.current_stream(self.device)
+        ev = self._timing_events(tr) if tr.timing else None
+        if ev is not None:
+            ev["step_start"].record(compute)
+        sh = self._sfnn_shape(tr.shape, tr.alpha)
+        arr = ctypes.c_void_p * 14
+        prm = arr(*[(None if w is None else w.as_ptr().value) for w in tr.weight_list()])
+        lw = tr.loss_workspace
+        qat = tr.lr_multipliers.as_struct()
+        lib.call("bulletou_b200_sfnn_local_gradients_exchange_device", ctx.as_ptr(), ctypes.byref(sh), tr.batch_size,
+                 tr.max_active, tr.stm_indices.as_ptr(), tr.nstm_indices.as_ptr(), tr.buckets.as_ptr(),
+                 tr.targets.as_ptr(), tr.entry_weights.as_ptr(), ctypes.byref(loss_spec), prm,
+                 tr.dense_grad.as_ptr(), tr.output.as_ptr(), lw.per_sample.as_ptr(),
+                 lw.mean_output_gradients.as_ptr(), lw.weighted_sum.as_ptr(), lw.mean.as_ptr(), ctypes.byref(qat),
+                 ctypes.byref(x), tr._launch_start, tr._launch_shard_rows, tr._launch_shard_off, tr._launch_signal,
+                 tr._event_handles, len(tr.row_ends))
+        if ev is not None:
+            ev["rows_end"].record(compute)
+        step = params.ffi_step()
+        m, v, slow = tr.ft_state
+        with torch.cuda.stream(tr._comm):
+            tr._events[0].wait(tr._comm_ctx)
+            if ev is not None:
+                ev["small_start"].record(tr._comm)
+            tr._small_exchange(params, tr._comm_ctx)
+            for j, c in enumerate(tr.chunks):
+                tr._events[c.last_launch].wait(tr._comm_ctx)
+                ce = None if ev is None else ev["chunks"][j]
+                if ce is not None:
+                    ce["start"].record()
+                    ce["reduce_scatter"].record()
+                lib.call("bulletou_b200_sfnn_shard_ranger_exchange_device", tr._comm_ctx.as_ptr(), ctypes.byref(x), W,
+                         c.start, c.length, c.shard_rows, c.shard_off, ctypes.byref(step), tr.l0w_compact.as_ptr(),
+                         m.as_ptr(), v.as_ptr(), slow.as_ptr(), tr._flags.as_ptr(), j * world,
+                         nc * world + j * world + rank, tr._xerr.as_ptr())
+                if ce is not None:
+                    ce["ranger"].record()
+                    ce["all_gather"].record()
+            if ev is not None:
+                ev["exchange_end"].record(tr._comm)
+        tr._ready.record(tr._comm_ctx)
+        tr._ready_pending = True
+
+    def check_peer_exchange(self, tr: "SfnnDataParallelTrainer") -> None:
+        self.torch.cuda.synchronize(self.device)
+        err = int(tr._xerr.download(self.ctx)[0])
+        if err:
+            raise CudaCppError(f"peer exchange: a wait for flag {err - 1} timed out (a rank stopped or fell behind)")
+
+    def close_peer_exchange(self, tr: "SfnnDataParallelTrainer") -> None:
+        for addr in getattr(tr, "_opened", []):
+            self.lib.call("bulletou_b200_ipc_close", self.ctx.as_ptr(), addr)
+        tr._opened = []
+
     def join_overlap(self, tr: "SfnnDataParallelTrainer") -> None:
         self.torch.cuda.current_stream(self.device).wait_stream(tr._comm)
 
@@ -400,7 +523,7 @@ class SfnnDataParallelTrainer:
 
     def __init__(self, backend, dist, initial_weights, batch_size: int, max_active: int, alpha=None,
                  lr_multipliers=None, overlap: Optional[bool] = None, launches_per_chunk: int = 3,
-                 last_chunk_launches: Optional[int] = 1):
+                 last_chunk_launches: Optional[int] = 1, exchange: Optional[str] = None):
         from .sfnn import SFNN_WEIGHT_NAMES, SfnnFactorizerAlpha, SfnnLayerLrMultipliers
 
         initial_weights.validate()
@@ -463,8 +586,19 @@ class SfnnDataParallelTrainer:
         self._t_compact = backend.tensor(self.l0w_compact)
         self._t_dense = backend.tensor(self.dense_grad)
         self.overlap = bool(getattr(backend, "supports_overlap", False)) if overlap is None else bool(overlap)
+        # "p2p": gradient rows stored into their owners' slots by the row
+        # kernels, shards updated and stored into every table over NVLink;
+        # "collectives": reduce-scatter / all-gather through the process group
+        peer = bool(getattr(backend, "supports_peer_exchange", False)) and self.overlap
+        self.exchange = exchange or ("p2p" if peer else "collectives")
+        if self.exchange not in ("p2p", "collectives"):
+            raise ValueError(f"exchange must be 'p2p' or 'collectives', got {self.exchange!r}")
+        if self.exchange == "p2p" and not peer:
+            raise ValueError("the p2p exchange needs a GPU backend with the overlapped step")
         if self.overlap:
             backend.prepare_overlap(self)
+        if self.exchange == "p2p":
+            backend.prepare_peer_exchange(self)
 
     def weight_list(self) -> list:
         from .sfnn import SFNN_WEIGHT_NAMES
@@ -522,6 +656,9 @@ class SfnnDataParallelTrainer:
     def step_device(self, params: RangerUpdateParams, loss_kind: ScalarLossKind, output_inv_scale: float,
                     finalize_loss: bool = True) -> None:
         spec = loss_kind.spec(output_inv_scale, finalize_loss, normalizer=self.batch_size * self.world)
+        if self.exchange == "p2p":
+            self.backend.sfnn_step_peer_exchange(self, spec, self._params(params))
+            return
         if self.overlap:
             self.backend.sfnn_step_overlapped(self, spec, self._params(params))
             return
@@ -533,8 +670,22 @@ class SfnnDataParallelTrainer:
         if self.overlap:
             self.backend.join_overlap(self)
 
-    def read_weights(self) -> dict:
+    def check(self) -> None:
+        """Waits for the device and raises if a peer-exchange wait timed out."""
         self.join()
+        if self.exchange == "p2p":
+            self.backend.check_peer_exchange(self)
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (peer exchange); call on every rank
+        after the last step, before the process group goes."""
+        if self.exchange == "p2p":
+            self.check()
+            self.dist.barrier()
+            self.backend.close_peer_exchange(self)
+
+    def read_weights(self) -> dict:
+        self.check()
         out = {n: self.backend.download(w) for n, w in self.weights.items() if w is not None}
         out["l0w"] = out["l0w"][: self.shape.input_size * self.shape.ft_size]
         return out

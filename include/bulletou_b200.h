@@ -314,6 +314,83 @@ int bulletou_b200_sfnn_local_gradients_device(
 int bulletou_b200_sfnn_row_launches(const BulletOuB200SfnnShape* shape, size_t* n_launches, size_t* row_end,
     size_t cap);
 
+/* ---------------------------------------------------------------- peer-memory row exchange
+ * Data-parallel SFNN without a reduce-scatter / all-gather library call: the
+ * FT rows are sharded by chunks of row launches (chunk c = table rows
+ * [start_c, start_c + length_c), padded to world * shard_rows_c rows; rank r
+ * owns rows start_c + r * shard_rows_c ..., stored from row shard_off_c of
+ * its compact shard).  Each rank holds a receive buffer of world slots of
+ * slot_rows x width floats (slot s = rank s's gradient rows of the rows this
+ * rank owns, at their compact index) and a flag array of 2 * chunks * world
+ * ints, zeroed once: scatter flags [chunk][source rank], then ready flags
+ * [chunk][owner rank].  Peers' buffers are opened from CUDA IPC handles; all
+ * accesses are plain NVLink loads and stores.  `epoch` is the step number
+ * (it only grows, so flags are never reset); every wait is bounded (about
+ * 2 s), after which the error word holds 1 + the index of the flag waited
+ * for and the rows are left unchanged. */
+typedef struct BulletOuB200RowExchange {
+    size_t world;                /* 1..8 */
+    size_t rank;
+    unsigned long long recv[8];  /* every rank's receive buffer (device addresses in this process) */
+    unsigned long long table[8]; /* every rank's FT table (l0w) */
+    unsigned long long flags[8]; /* every rank's flag array */
+    size_t slot_rows;
+    int epoch;
+} BulletOuB200RowExchange;
+
+/* CUDA IPC handle (64 bytes) of a buffer's device memory, and its opening /
+ * closing in another process (same node, peer GPUs). */
+int bulletou_b200_f32_buffer_ipc_handle(const BulletOuCudaCppF32Buffer* buffer, void* handle_out);
+int bulletou_b200_i32_buffer_ipc_handle(const BulletOuCudaCppI32Buffer* buffer, void* handle_out);
+int bulletou_b200_ipc_open(BulletOuCudaCppContext* ctx, const void* handle, unsigned long long* device_address);
+int bulletou_b200_ipc_close(BulletOuCudaCppContext* ctx, unsigned long long device_address);
+
+/* Local gradients as bulletou_b200_sfnn_local_gradients_device, with the FT
+ * gradient rows stored into their owners' receive slots instead of a local
+ * table.  Per row launch j: the chunk it belongs to (launch_chunk_start,
+ * launch_shard_rows, launch_shard_off) and launch_signal[j] = the chunk's
+ * index when j is its last launch, else -1; after such a launch the scatter
+ * flag [chunk][rank] of every rank is set to x->epoch.  row_events[j]
+ * (optional) as in the plain entry. */
+int bulletou_b200_sfnn_local_gradients_exchange_device(
+    BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
+    const BulletOuCudaCppI32Buffer* stm_indices, const BulletOuCudaCppI32Buffer* nstm_indices,
+    const BulletOuCudaCppI32Buffer* buckets, const BulletOuCudaCppF32Buffer* targets,
+    const BulletOuCudaCppF32Buffer* entry_weights, const BulletOuB200LossSpec* loss,
+    BulletOuCudaCppF32Buffer* const* params, BulletOuCudaCppF32Buffer* dense_gradients,
+    BulletOuCudaCppF32Buffer* output, BulletOuCudaCppF32Buffer* per_sample,
+    BulletOuCudaCppF32Buffer* mean_output_gradients, BulletOuCudaCppF32Buffer* weighted_sum,
+    BulletOuCudaCppF32Buffer* mean, const BulletOuB200SfnnQat* qat, const BulletOuB200RowExchange* x,
+    const size_t* launch_chunk_start, const size_t* launch_shard_rows, const size_t* launch_shard_off,
+    const long long* launch_signal, BulletOuCudaCppEvent* const* row_events, size_t n_row_launches);
+
+/* The owner's part of chunk `c` (rows [chunk_start, chunk_start +
+ * chunk_length), shard_rows / shard_off as above): waits for the chunk's
+ * scatter flags [scatter_index, scatter_index + world) of its own flag array,
+ * sums the world slots of its rows in rank order, runs Ranger (`step`) on its
+ * compact shard state, stores the updated rows into every rank's table and
+ * sets ready flag `ready_index` (= ready base + c * world + rank) of every
+ * rank to x->epoch. */
+int bulletou_b200_sfnn_shard_ranger_exchange_device(
+    BulletOuCudaCppContext* ctx, const BulletOuB200RowExchange* x, size_t width, size_t chunk_start,
+    size_t chunk_length, size_t shard_rows, size_t shard_off, const BulletOuB200RangerStep* step,
+    BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppF32Buffer* momentum, BulletOuCudaCppF32Buffer* velocity,
+    BulletOuCudaCppF32Buffer* slow, const BulletOuCudaCppI32Buffer* flags, size_t scatter_index,
+    size_t ready_index, BulletOuCudaCppI32Buffer* error);
+
+/* Enqueues a bounded wait until flags[offset, offset + count) all reach
+ * `epoch` (timeout: *error = 1 + the flag's index). */
+int bulletou_b200_exchange_wait_device(BulletOuCudaCppContext* ctx, const BulletOuCudaCppI32Buffer* flags,
+    size_t offset, size_t count, int epoch, BulletOuCudaCppI32Buffer* error);
+
+/* As bulletou_b200_context_wait_before_weights, for flags: the next SFNN
+ * fused step waits (bounded, as bulletou_b200_exchange_wait_device) until
+ * flags[offset, offset + count) reach `epoch` before its first weight read;
+ * flags null clears it. */
+int bulletou_b200_context_wait_flags_before_weights(BulletOuCudaCppContext* ctx,
+    const BulletOuCudaCppI32Buffer* flags, size_t offset, size_t count, int epoch,
+    BulletOuCudaCppI32Buffer* error);
+
 /* ---------------------------------------------------------------- quantised HalfKP
  * The reference exports a trained HalfKP 256x2-32-32 net to the engine's
  * nn.bin (write_cuda_cpp_nnue_nn_bin, examples/bulletou.rs:26303-26413); the

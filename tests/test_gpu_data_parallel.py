@@ -107,7 +107,7 @@ def _sf_qat(mode):
         qat_l1=True, qat_ft=True, qat_l2=True, qat_l3=True)
 
 
-def _sf_rank_main(rank, world, port, out_path, qat="none"):
+def _sf_rank_main(rank, world, port, out_path, qat="none", exchange="p2p"):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -126,7 +126,8 @@ def _sf_rank_main(rank, world, port, out_path, qat="none"):
         w = synthetic.sfnn_weights(synthetic.rng_for(23), ft=256)
         shape = bs.SfnnForwardShape(73305 + 1629, 256, 15, True, 32, 9)
         tr = SfnnDataParallelTrainer(B200Backend(rank), dist, bs.SfnnForwardHostWeights(shape, **w), SF_BATCH, 40,
-                                     lr_multipliers=_sf_qat(qat))
+                                     lr_multipliers=_sf_qat(qat), exchange=exchange)
+        assert tr.exchange == exchange
         for step, b in enumerate(_sf_batches(), start=1):
             sl = slice(rank * SF_BATCH * 40, (rank + 1) * SF_BATCH * 40)
             bsl = slice(rank * SF_BATCH, (rank + 1) * SF_BATCH)
@@ -137,21 +138,26 @@ def _sf_rank_main(rank, world, port, out_path, qat="none"):
         got = tr.read_weights()
         if rank == 0:
             np.savez(out_path, **got)
+        tr.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("qat", ["none", "all"])
-def test_two_gpu_sfnn_data_parallel_matches_single_gpu_global_batch(tmp_path, qat):
+@pytest.mark.parametrize("qat,exchange", [("none", "collectives"), ("none", "p2p"), ("all", "p2p")])
+def test_two_gpu_sfnn_data_parallel_matches_single_gpu_global_batch(tmp_path, qat, exchange):
+    """Two ranks on half batches equal one GPU on the whole batch, with the
+    exchange through the process group's collectives or over peer memory
+    (gradient rows stored into their owners' slots by the row kernels)."""
     import torch
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     out = tmp_path / "rank0.npz"
-    mp.start_processes(_sf_rank_main, args=(2, _free_port(), str(out), qat), nprocs=2, start_method="spawn")
+    mp.start_processes(_sf_rank_main, args=(2, _free_port(), str(out), qat, exchange), nprocs=2,
+                       start_method="spawn")
     got = np.load(out)
 
     import bulletou_b200 as bo
@@ -172,3 +178,27 @@ def test_two_gpu_sfnn_data_parallel_matches_single_gpu_global_batch(tmp_path, qa
         scale = max(float(np.abs(v).max()), 1e-30)
         err = float(np.abs(got[k].astype(np.float64) - v).max())
         assert err <= 1e-4 * scale, f"{k}: max |diff| {err:.3e} (scale {scale:.3e})"
+
+
+def test_exchange_wait_times_out_with_an_error_code():
+    """A bounded exchange wait on a flag nothing sets returns after about 2 s
+    with 1 + the flag's index in the error word; the context stays usable."""
+    import time
+
+    import bulletou_b200 as bo
+
+    ctx = bo.Context(0)
+    flags = bo.I32Buffer.from_host(ctx, np.array([3, 3, 2, 3], np.int32))
+    err = bo.I32Buffer.from_host(ctx, np.zeros(1, np.int32))
+    lib = ctx.lib
+    lib.call("bulletou_b200_exchange_wait_device", ctx.as_ptr(), flags.as_ptr(), 0, 2, 3, err.as_ptr())
+    ctx.synchronize()
+    assert int(err.download(ctx)[0]) == 0  # both flags already at the epoch
+    t0 = time.time()
+    lib.call("bulletou_b200_exchange_wait_device", ctx.as_ptr(), flags.as_ptr(), 1, 3, 3, err.as_ptr())
+    ctx.synchronize()
+    assert 1.0 < time.time() - t0 < 30.0
+    assert int(err.download(ctx)[0]) == 1 + 1  # the second flag of the range (value 2) never reaches 3
+    x = bo.F32Buffer.from_host(ctx, np.arange(8, dtype=np.float32))
+    assert np.array_equal(x.download(ctx), np.arange(8, dtype=np.float32))
+    ctx.close()
