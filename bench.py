@@ -803,7 +803,8 @@ def kppt_roofline(ms_per_step, batch, hbm_peak, peak_kind, lookahead_frac=1.0 / 
     sparse = 2 * batch * synthetic.KPP_PAIRS * 4 * 3  # gather + scatter read-modify-write
     comp = ranger_bytes + sparse
     t = ms_per_step / 1000.0
-    return {"bound": "hbm", "kernel": "KPPT step (kppt_kernel<1> + kppt_small_kernel + ranger_vec4_kernel)",
+    return {"bound": "hbm", "kernel": ("KPPT step (king sort + kppt_view_kernel + kppt_kernel<3> + "
+                                       "kppt_scatter_kernel + kppt_small_kernel + ranger_vec4_kernel)"),
             "achieved": round(comp / t / 1e9, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(comp / t / 1e9 / hbm_peak, 4), "peak_source": peak_kind, "traffic": None,
             "algorithmic_bytes": "dense Ranger over the table + the sparse gather / scatter, per step",
@@ -1148,7 +1149,7 @@ def run_sfnn_data_parallel(args, wl, rank, world, local, dist):
     tr.close()
     dist.barrier()
     how = ("FT rows stored into their owners' slots by the row kernels, shards updated and stored into every "
-           "rank's table over NVLink, small groups by NCCL all-reduce" if tr.exchange == "p2p" else
+           "rank's table over NVLink, the small groups' gradient summed from every rank's slot" if tr.exchange == "p2p" else
            "NCCL reduce-scatter / all-reduce / all-gather")
     return {"total_ms": total_ms, "phase_ms": phase_ms, "clocks": clocks.summary(),
             "e2e": {"value": args.steps * args.batch * world / (e2e_ms / 1000.0), "unit": "positions/s",
@@ -1210,7 +1211,10 @@ SFNN_DRAM_BYTES_B65536 = {
     "l1_backward": (2076098304, ("dense", "all")),
 }
 SFNN_DRAM_BYTES_PSV_B65536 = {
-    "l1_backward": (2068230656, ("all",)),
+    "ft_rows_ranger": (5416400000, ("all",)),
+    "ft_forward": (1556600000, ("all",)),
+    "l1_backward": (2860700000, ("all",)),
+    "fold": (892700000, ("all",)),
 }
 SFNN_PHASE_KERNELS = {
     "ft_rows_ranger": ("heavy-key plan (3 kernels) + heavy_incidence_kernel + heavy_key_mma_kernel (tcgen05) + 15 "
@@ -1313,7 +1317,8 @@ def main():
                             "ms_per_step": round(ms, 4), "clocks": r["clocks"], "e2e": rounded(r["e2e"])}
                     if not ref:
                         line["roofline"] = kppt_roofline(ms, args.batch, hbm, kind)
-                        line["gpu_launches"] = 3 * args.steps
+                        # king sort 3, view sums, outputs / loss, gradient scatter, small groups, table Ranger
+                        line["gpu_launches"] = 8 * args.steps
                 else:
                     r = run_halfkp_forward(args, local, reference=ref)
                     ms = r["total_ms"] / args.steps

@@ -80,7 +80,7 @@ class RowExchange(ctypes.Structure):
     """BulletOuB200RowExchange."""
 
     _fields_ = [("world", Z), ("rank", Z), ("recv", U64 * 8), ("table", U64 * 8), ("flags", U64 * 8),
-                ("slot_rows", Z), ("epoch", I)]
+                ("slot_rows", Z), ("epoch", I), ("small_recv", U64 * 8), ("small_len", Z), ("small_flag_base", Z)]
 
 
 class LossSpec(ctypes.Structure):
@@ -180,6 +180,7 @@ SIGNATURES: dict[str, list] = {
     "bulletou_b200_sfnn_local_gradients_exchange_device": [P, P, Z, Z] + [P] * 20 + [Z],
     "bulletou_b200_sfnn_shard_ranger_exchange_device": [P, P, Z, Z, Z, Z, Z, P, P, P, P, P, P, Z, Z, P],
     "bulletou_b200_exchange_wait_device": [P, P, Z, Z, I, P],
+    "bulletou_b200_exchange_reduce_small_device": [P, P, P, P, P],
     "bulletou_b200_context_wait_flags_before_weights": [P, P, Z, Z, I, P],
     "bulletou_b200_f32_buffer_ipc_handle": [P, P],
     "bulletou_b200_i32_buffer_ipc_handle": [P, P],

@@ -68,6 +68,47 @@ __global__ void exchange_wait_kernel(const int* flags, int count, int epoch, int
     }
 }
 
+__global__ void exchange_scatter_kernel(const float4* __restrict__ src, size_t len4, PeerBuffers dst, int world,
+                                        int rank) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < len4; i += stride) {
+        const float4 v = src[i];
+        for (int r = 0; r < world; ++r) reinterpret_cast<float4*>(dst.p[r])[static_cast<size_t>(rank) * len4 + i] = v;
+    }
+    __threadfence_system();
+}
+
+__global__ void exchange_scatter1_kernel(const float* __restrict__ src, size_t len, PeerBuffers dst, int world,
+                                         int rank) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < len; i += stride) {
+        const float v = src[i];
+        for (int r = 0; r < world; ++r) dst.p[r][static_cast<size_t>(rank) * len + i] = v;
+    }
+    __threadfence_system();
+}
+
+// dst[i] = sum over the world slots of len floats, in rank order, after each
+// CTA re-reads the small flags with acquire semantics (the wait kernel before
+// it has seen them all; on its timeout dst is left unchanged).
+__global__ void exchange_reduce_kernel(const float* __restrict__ slots, size_t len, int world, const int* flags,
+                                       int epoch, float* __restrict__ dst) {
+    __shared__ int ready;
+    if (threadIdx.x == 0) {
+        int all = 1;
+        for (int r = 0; r < world; ++r) all &= ld_acquire_sys(flags + r) >= epoch ? 1 : 0;
+        ready = all;
+    }
+    __syncthreads();
+    if (!ready) return;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < len; i += stride) {
+        float g = slots[i];
+        for (int r = 1; r < world; ++r) g += slots[static_cast<size_t>(r) * len + i];
+        dst[i] = g;
+    }
+}
+
 struct ShardArgs {
     const float4* recv;  // own receive buffer: world slots of slot4 float4
     size_t slot4;
@@ -163,6 +204,22 @@ int exchange_from(const BulletOuB200RowExchange* x, PeerFlags* flags) {
 int launch_exchange_signal(BulletOuCudaCppContext* ctx, const PeerFlags& flags, int world, size_t index, int epoch) {
     exchange_signal_kernel<<<1, 32, 0, ctx->stream>>>(flags, world, index, epoch);
     return check_launch("exchange signal launch");
+}
+
+int launch_exchange_scatter(BulletOuCudaCppContext* ctx, const float* src, size_t len, const PeerBuffers& dst,
+                            int world, int rank) {
+    const bool vec = len % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+    for (int r = 0; r < world && vec; ++r)
+        if ((reinterpret_cast<uintptr_t>(dst.p[r]) & 15u) != 0) return fail_message("exchange scatter: unaligned slot");
+    const size_t n = vec ? len / 4 : len;
+    const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, static_cast<size_t>(ctx->sm_count)));
+    if (n == 0) return 0;
+    if (vec)
+        exchange_scatter_kernel<<<blocks, 256, 0, ctx->stream>>>(reinterpret_cast<const float4*>(src), n, dst, world,
+                                                                 rank);
+    else
+        exchange_scatter1_kernel<<<blocks, 256, 0, ctx->stream>>>(src, n, dst, world, rank);
+    return check_launch("exchange scatter launch");
 }
 
 int launch_exchange_wait(BulletOuCudaCppContext* ctx, const int* flags, int count, int epoch, int* error) {
@@ -288,4 +345,26 @@ int bulletou_b200_sfnn_shard_ranger_exchange_device(
     // the updated rows are in every table
     if (launch_exchange_signal(ctx, pf, s.world, ready_index, x->epoch) != 0) return -1;
     return ok();
+}
+
+int bulletou_b200_exchange_reduce_small_device(BulletOuCudaCppContext* ctx, const BulletOuB200RowExchange* x,
+                                               BulletOuCudaCppF32Buffer* dst, const BulletOuCudaCppI32Buffer* flags,
+                                               BulletOuCudaCppI32Buffer* error) {
+    PeerFlags pf{};
+    if (exchange_from(x, &pf) != 0) return -1;
+    if (x->small_len == 0 || x->small_recv[x->rank] == 0)
+        return fail_message("exchange reduce small: no small receive buffer");
+    if (validate_f32(ctx, dst, x->small_len, "small gradient") != 0 ||
+        validate_i32(ctx, flags, x->small_flag_base + x->world, "exchange flags") != 0 ||
+        validate_i32(ctx, error, 1, "exchange error word") != 0)
+        return -1;
+    if (set_device(ctx) != 0) return -1;
+    const int* f = flags->ptr + x->small_flag_base;
+    if (launch_exchange_wait(ctx, f, static_cast<int>(x->world), x->epoch, error->ptr) != 0) return -1;
+    const int blocks =
+        static_cast<int>(std::min<size_t>((x->small_len + 255) / 256, static_cast<size_t>(ctx->sm_count) * 2));
+    exchange_reduce_kernel<<<blocks, 256, 0, ctx->stream>>>(
+        reinterpret_cast<const float*>(static_cast<uintptr_t>(x->small_recv[x->rank])), x->small_len,
+        static_cast<int>(x->world), f, x->epoch, dst->ptr);
+    return check_launch("exchange reduce launch") == 0 ? ok() : -1;
 }

@@ -17,6 +17,14 @@ struct PeerFlags {
 // (the data written before on this stream is visible to the peers first).
 int launch_exchange_signal(BulletOuCudaCppContext* ctx, const PeerFlags& flags, int world, size_t index, int epoch);
 
+// Copies src[0, len) into slot `rank` (of len floats) of every rank's buffer
+// dst[r], then fences at system scope.
+struct PeerBuffers {
+    float* p[kExchangeMaxRanks];
+};
+int launch_exchange_scatter(BulletOuCudaCppContext* ctx, const float* src, size_t len, const PeerBuffers& dst,
+                            int world, int rank);
+
 // One thread waits until flags[0, count) all hold at least `epoch`; after
 // about 2 s it stores 1 + the index of the flag it waited for into *error and
 // returns.

@@ -15,6 +15,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "king_sort.cuh"
 #include "loss.cuh"
 #include "optim.cuh"
 
@@ -62,10 +63,12 @@ struct KpptArgs {
     float* mog;
     float* table_grad;    // accumulated with vector-free reductions
     float* partials;      // [grid][kKpptVec]
+    const float* eval2;   // mode 3: view evaluations, [2 * batch] (h = 2 * sample + view)
 };
 
 // mode 0: forward only; 1: forward + loss + backward; 2: backward only
-// (stm_eval/nstm_eval/mog given).
+// (stm_eval/nstm_eval/mog given); 3: output + loss from given view
+// evaluations (eval2), no table access (the king-ordered train step).
 template <int MODE>
 __global__ void __launch_bounds__(kWarps * 32) kppt_kernel(KpptArgs a) {
     __shared__ float red[kWarps][kKpptVec];
@@ -76,7 +79,20 @@ __global__ void __launch_bounds__(kWarps * 32) kppt_kernel(KpptArgs a) {
         const int* si = a.stm + static_cast<size_t>(b) * a.max_active;
         const int* ni = a.nstm + static_cast<size_t>(b) * a.max_active;
         float se, ne, gout;
-        if (MODE != 2) {
+        if (MODE == 3) {
+            se = a.eval2[2 * static_cast<size_t>(b)];
+            ne = a.eval2[2 * static_cast<size_t>(b) + 1];
+            const float out = w0 * se + w1 * ne + a.outb[0];
+            if (lane == 0) a.output[b] = out;
+            float g = 0.0f;
+            const float ps = sample_loss(a.loss, out, a.targets[b], a.entry_weights[b], &g);
+            gout = g;
+            if (lane == 0) {
+                a.per_sample[b] = ps;
+                a.mog[b] = g;
+                acc_loss += ps;
+            }
+        } else if (MODE != 2) {
             float s = 0.0f, n = 0.0f;
             for (int k = lane; k < a.max_active; k += 32) {
                 const int fs = __ldg(si + k), fn = __ldg(ni + k);
@@ -113,6 +129,7 @@ __global__ void __launch_bounds__(kWarps * 32) kppt_kernel(KpptArgs a) {
             acc_ob += gout;
             acc_tb += sg + ng;
         }
+        if (MODE == 3) continue;  // the table gradient comes from kppt_scatter_kernel
         for (int k = lane; k < a.max_active; k += 32) {
             const int fs = __ldg(si + k), fn = __ldg(ni + k);
             if (fs >= 0 && fs < a.input_size) atomicAdd(a.table_grad + fs, sg);
@@ -134,6 +151,47 @@ __global__ void __launch_bounds__(kWarps * 32) kppt_kernel(KpptArgs a) {
         a.partials[static_cast<size_t>(blockIdx.x) * kKpptVec + threadIdx.x] = s;
     }
 }
+
+// King-ordered passes of the train step.  Every feature of a view lies in
+// its king's block of the table (input_size / 81 entries), so warps working on
+// consecutive half-positions of the king sort gather from (and scatter into)
+// a few king blocks at a time, which L2 holds; in batch order every access is
+// a DRAM sector of its own.  The view sum keeps the per-lane slot split and
+// the warp-tree order of kppt_kernel, so the evaluations are bit-identical.
+__global__ void __launch_bounds__(kWarps * 32) kppt_view_kernel(KpptArgs a, const int* __restrict__ order,
+                                                                int n_half, float* __restrict__ eval2) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float bias = a.table_b[0];
+    for (int i = blockIdx.x * kWarps + warp; i < n_half; i += gridDim.x * kWarps) {
+        const int h = __ldg(order + i);
+        const int* idx = ((h & 1) ? a.nstm : a.stm) + static_cast<size_t>(h >> 1) * a.max_active;
+        float s = 0.0f;
+        for (int k = lane; k < a.max_active; k += 32) {
+            const int f = __ldg(idx + k);
+            if (f >= 0 && f < a.input_size) s += __ldg(a.table_w + f);
+        }
+        const float e = bias + warp_sum(s);
+        if (lane == 0) eval2[h] = e;
+    }
+}
+
+__global__ void __launch_bounds__(kWarps * 32) kppt_scatter_kernel(KpptArgs a, const int* __restrict__ order,
+                                                                   int n_half) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float w0 = a.outw[0], w1 = a.outw[1];
+    for (int i = blockIdx.x * kWarps + warp; i < n_half; i += gridDim.x * kWarps) {
+        const int h = __ldg(order + i);
+        const float g = a.mog[h >> 1] * ((h & 1) ? w1 : w0);
+        const int* idx = ((h & 1) ? a.nstm : a.stm) + static_cast<size_t>(h >> 1) * a.max_active;
+        for (int k = lane; k < a.max_active; k += 32) {
+            const int f = __ldg(idx + k);
+            if (f >= 0 && f < a.input_size) atomicAdd(a.table_grad + f, g);
+        }
+    }
+}
+
+constexpr int kKpptKings = 81;
+constexpr int kKpptKeys = kKpptKings + 1;  // + half-positions without a valid feature
 
 struct KpptSmall {
     float* w[3];  // table_b, outw, outb
@@ -365,7 +423,31 @@ int bulletou_b200_kppt_train_step_device(
     a.mog = mean_output_gradients->ptr;
     a.table_grad = grad;
     a.partials = static_cast<float*>(parts);
-    kppt_kernel<1><<<grid, kWarps * 32, 0, ctx->stream>>>(a);
+    if (input_size % kKpptKings == 0 && input_size >= static_cast<size_t>(kKpptKings)) {
+        // king order: sort the 2B views by king block, sum the views, then the
+        // outputs / loss in sample order, then the gradient scatter
+        const int n_half = static_cast<int>(2 * batch);
+        const size_t sort_ints = king_sort_scratch_ints<kKpptKeys>(static_cast<size_t>(n_half));
+        void* sp = nullptr;
+        if (scratch_slot(ctx, kScratchKingSort, (sort_ints + static_cast<size_t>(n_half)) * sizeof(int), &sp,
+                         "cudaMalloc kppt king sort") != 0)
+            return -1;
+        int* sort_scratch = static_cast<int*>(sp);
+        float* eval2 = reinterpret_cast<float*>(sort_scratch + sort_ints);
+        KingSortOut ks{};
+        const KingKey kk{static_cast<int>(input_size / kKpptKings), static_cast<int>(input_size),
+                         static_cast<int>(max_active)};
+        if (king_sort<kKpptKeys>(ctx, a.stm, a.nstm, n_half, kk, sort_scratch, nullptr, &ks) != 0) return -1;
+        // about 4 resident warps' worth of half-positions per SM keeps the
+        // king blocks in use to a few (9.6 MB each for the KPP table)
+        const int sgrid = std::max(1, std::min((n_half + kWarps - 1) / kWarps, ctx->sm_count * 4));
+        a.eval2 = eval2;
+        kppt_view_kernel<<<sgrid, kWarps * 32, 0, ctx->stream>>>(a, ks.order, n_half, eval2);
+        kppt_kernel<3><<<grid, kWarps * 32, 0, ctx->stream>>>(a);
+        kppt_scatter_kernel<<<sgrid, kWarps * 32, 0, ctx->stream>>>(a, ks.order, n_half);
+    } else {
+        kppt_kernel<1><<<grid, kWarps * 32, 0, ctx->stream>>>(a);
+    }
     if (check_launch("kppt train kernel launch") != 0) return -1;
     const RangerArgs ra = ranger_args_from(*ranger);
     KpptSmall g{};

@@ -1511,6 +1511,9 @@ struct RowScatter {
     const long long* signal;
     PeerFlags flags;
     int epoch;
+    PeerBuffers small;       // every rank's small-gradient receive buffer
+    size_t small_len;        // 0: the small gradient stays local
+    size_t small_flag_base;
 };
 
 constexpr int kHeavyRow = 128;  // FT row phase on king-concentrated batches: 512 -> 3.75 ms, 128 -> 3.03 ms
@@ -2735,6 +2738,14 @@ int sfnn_step(BulletOuCudaCppContext* ctx, const SfnnDims& d, const SfnnWeights&
                 return -1;
         }
     }
+    // peer exchange: the small groups' gradient into every rank's slot
+    if (scatter != nullptr && scatter->small_len > 0) {
+        if (launch_exchange_scatter(ctx, packed, scatter->small_len, scatter->small, scatter->world, scatter->rank) !=
+                0 ||
+            launch_exchange_signal(ctx, scatter->flags, scatter->world, scatter->small_flag_base + scatter->rank,
+                                   scatter->epoch) != 0)
+            return -1;
+    }
     prof_mark(ctx);
     if (ranger != nullptr) {
         r.ranger = ra;
@@ -3454,6 +3465,17 @@ int bulletou_b200_sfnn_local_gradients_exchange_device(
         if (x->recv[r] == 0 || x->flags[r] == 0) return fail_messagef("row exchange: rank %zu's buffers missing", r);
         sc.recv[r] = reinterpret_cast<float*>(static_cast<uintptr_t>(x->recv[r]));
         sc.flags.p[r] = reinterpret_cast<int*>(static_cast<uintptr_t>(x->flags[r]));
+    }
+    if (x->small_len > 0) {
+        if (x->small_len != g.begin[kSfGroups])
+            return fail_messagef("SFNN local gradients exchange: small_len %zu, the packed gradient holds %zu",
+                                 x->small_len, static_cast<size_t>(g.begin[kSfGroups]));
+        for (size_t r = 0; r < x->world; ++r) {
+            if (x->small_recv[r] == 0) return fail_messagef("row exchange: rank %zu's small buffer missing", r);
+            sc.small.p[r] = reinterpret_cast<float*>(static_cast<uintptr_t>(x->small_recv[r]));
+        }
+        sc.small_len = x->small_len;
+        sc.small_flag_base = x->small_flag_base;
     }
     cudaEvent_t events[64];
     if (row_events != nullptr) {

@@ -257,10 +257,13 @@ class B200Backend:
         last = tr.chunks[-1]
         slot_rows = last.shard_off + last.shard_rows
         n_chunks = len(tr.chunks)
+        small_len = tr.dense_layout[-1][1] + tr.dense_layout[-1][2]
         tr._recv = F32Buffer(self.ctx, world * slot_rows * W)
-        tr._flags = I32Buffer.from_host(self.ctx, np.zeros(2 * n_chunks * world, np.int32))
+        tr._small_recv = F32Buffer(self.ctx, world * small_len)
+        # flags: scatter [chunk][source], ready [chunk][owner], small [source]
+        tr._flags = I32Buffer.from_host(self.ctx, np.zeros(2 * n_chunks * world + world, np.int32))
         tr._xerr = I32Buffer.from_host(self.ctx, np.zeros(1, np.int32))
-        own = (tr._recv, tr.weights["l0w"], tr._flags)
+        own = (tr._recv, tr.weights["l0w"], tr._flags, tr._small_recv)
         mine = []
         for b in own:
             h = (ctypes.c_ubyte * 64)()
@@ -271,9 +274,10 @@ class B200Backend:
         tr.dist.all_gather_object(gathered, mine)
         x = RowExchange()
         x.world, x.rank, x.slot_rows, x.epoch = world, rank, slot_rows, 0
+        x.small_len, x.small_flag_base = small_len, 2 * n_chunks * world
         tr._opened = []
         for r in range(world):
-            for k, field in enumerate((x.recv, x.table, x.flags)):
+            for k, field in enumerate((x.recv, x.table, x.flags, x.small_recv)):
                 if r == rank:
                     field[r] = own[k].device_ptr()
                 else:
@@ -294,8 +298,9 @@ class B200Backend:
 
     def sfnn_step_peer_exchange(self, tr: "SfnnDataParallelTrainer", loss_spec, params) -> None:
         """The local step stores its FT gradient rows into their owners'
-        receive slots (signalling each chunk); on the comm stream the small
-        groups' all-reduce + Ranger, then per chunk this rank's shard: wait for
+        receive slots (signalling each chunk) and its small-group gradient into
+        every rank's small slots; on the comm stream the small groups' sum +
+        Ranger, then per chunk this rank's shard: wait for
         every rank's rows, sum, Ranger, store into every rank's table, signal.
         The next step runs its batch-only work first and waits for every
         owner's signals (and this rank's comm stream) before its first weight
@@ -641,7 +646,13 @@ class SfnnDataParallelTrainer:
     def _small_exchange(self, params: RangerUpdateParams, ctx=None) -> None:
         from .sfnn import factor_contribution_clip
 
-        self.dist.all_reduce(self._t_dense)
+        if self.exchange == "p2p":
+            # every rank's small gradient is in this rank's slots (stored by
+            # the local-gradients entry): sum them in rank order
+            self.backend.lib.call("bulletou_b200_exchange_reduce_small_device", ctx.as_ptr(), ctypes.byref(self._x),
+                                  self.dense_grad.as_ptr(), self._flags.as_ptr(), self._xerr.as_ptr())
+        else:
+            self.dist.all_reduce(self._t_dense)
         for name, _, _ in self.dense_layout:
             p = factor_contribution_clip(params, self.alpha.shared) if name in ("l1fw", "l1fb") else params
             m, v, slow = self.small_state[name]

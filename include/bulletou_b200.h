@@ -336,6 +336,13 @@ typedef struct BulletOuB200RowExchange {
     unsigned long long flags[8]; /* every rank's flag array */
     size_t slot_rows;
     int epoch;
+    /* the small groups' packed gradient (bulletou_b200_sfnn_dense_gradient_len
+     * floats): every rank's receive buffer of world slots of small_len floats,
+     * and the first of the world small flags in every flag array (0: the
+     * small gradient is not exchanged by the local-gradients entry) */
+    unsigned long long small_recv[8];
+    size_t small_len;
+    size_t small_flag_base;
 } BulletOuB200RowExchange;
 
 /* CUDA IPC handle (64 bytes) of a buffer's device memory, and its opening /
@@ -350,7 +357,10 @@ int bulletou_b200_ipc_close(BulletOuCudaCppContext* ctx, unsigned long long devi
  * table.  Per row launch j: the chunk it belongs to (launch_chunk_start,
  * launch_shard_rows, launch_shard_off) and launch_signal[j] = the chunk's
  * index when j is its last launch, else -1; after such a launch the scatter
- * flag [chunk][rank] of every rank is set to x->epoch.  row_events[j]
+ * flag [chunk][rank] of every rank is set to x->epoch.  With x->small_len > 0
+ * the packed small-group gradient (dense_gradients) is also stored into slot
+ * `rank` of every rank's small receive buffer before the row launches and
+ * small flag [small_flag_base + rank] of every rank set.  row_events[j]
  * (optional) as in the plain entry. */
 int bulletou_b200_sfnn_local_gradients_exchange_device(
     BulletOuCudaCppContext* ctx, const BulletOuB200SfnnShape* shape, size_t batch, size_t max_active,
@@ -377,6 +387,12 @@ int bulletou_b200_sfnn_shard_ranger_exchange_device(
     BulletOuCudaCppF32Buffer* weights, BulletOuCudaCppF32Buffer* momentum, BulletOuCudaCppF32Buffer* velocity,
     BulletOuCudaCppF32Buffer* slow, const BulletOuCudaCppI32Buffer* flags, size_t scatter_index,
     size_t ready_index, BulletOuCudaCppI32Buffer* error);
+
+/* The small groups' all-reduce over peer memory: waits (bounded) for the
+ * world small flags of `flags` to reach x->epoch, then dst[i] = the sum over
+ * ranks, in rank order, of slot r of this rank's small receive buffer. */
+int bulletou_b200_exchange_reduce_small_device(BulletOuCudaCppContext* ctx, const BulletOuB200RowExchange* x,
+    BulletOuCudaCppF32Buffer* dst, const BulletOuCudaCppI32Buffer* flags, BulletOuCudaCppI32Buffer* error);
 
 /* Enqueues a bounded wait until flags[offset, offset + count) all reach
  * `epoch` (timeout: *error = 1 + the flag's index). */
