@@ -129,11 +129,12 @@ __global__ void __launch_bounds__(kWarps * 32) kppt_kernel(KpptArgs a) {
             acc_ob += gout;
             acc_tb += sg + ng;
         }
-        if (MODE == 3) continue;  // the table gradient comes from kppt_scatter_kernel
-        for (int k = lane; k < a.max_active; k += 32) {
-            const int fs = __ldg(si + k), fn = __ldg(ni + k);
-            if (fs >= 0 && fs < a.input_size) atomicAdd(a.table_grad + fs, sg);
-            if (fn >= 0 && fn < a.input_size) atomicAdd(a.table_grad + fn, ng);
+        if constexpr (MODE != 3) {  // mode 3: the table gradient comes from kppt_scatter_kernel
+            for (int k = lane; k < a.max_active; k += 32) {
+                const int fs = __ldg(si + k), fn = __ldg(ni + k);
+                if (fs >= 0 && fs < a.input_size) atomicAdd(a.table_grad + fs, sg);
+                if (fn >= 0 && fn < a.input_size) atomicAdd(a.table_grad + fn, ng);
+            }
         }
     }
     if (MODE == 0) return;
