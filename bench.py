@@ -281,17 +281,24 @@ class PinnedHostBatch:
 
 
 def pipelined_e2e(runner, ctx, upload_ctx, sources, steps, step, loss_kind, inv):
-    """The runner's pipelined step (uploads of step i+1 on a second stream
-    overlap step i) from page-locked host batches, with a synchronous D2H read
-    of the step's mean loss after every step (the drop-in ABI's download).
+    """Page-locked host batches through the runner's upload slots: step i runs
+    on its slot while the batch of step i + 1 is uploaded on a second stream
+    (issued right after step i is enqueued), then the step's mean loss is read
+    back synchronously (the drop-in ABI's download).  Every step's batch is
+    copied H2D and every step's loss read D2H inside the timed region.
     Identical calls for every backend library."""
     import bulletou_b200 as bo
 
+    n = len(sources)
+    runner.upload_next(upload_ctx, None, sources[0])
     for i in range(3):
         step += 1
-        runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv, None,
-                                                             True, sources[i % len(sources)], None)
+        runner.step_uploaded_no_readback_with_loss_finalize(ctx, ranger(step), loss_kind, inv, True)
+        runner.upload_next(upload_ctx, None, sources[(i + 1) % n])
         runner.loss_workspace.mean.download(ctx)
+    step += 1  # the warm-up's last upload is consumed here, outside the timed region
+    runner.step_uploaded_no_readback_with_loss_finalize(ctx, ranger(step), loss_kind, inv, True)
+    runner.loss_workspace.mean.download(ctx)
     ctx.synchronize()
     upload_ctx.synchronize()
     e0, e1 = bo.Event(ctx), bo.Event(ctx)
@@ -299,10 +306,12 @@ def pipelined_e2e(runner, ctx, upload_ctx, sources, steps, step, loss_kind, inv)
     h2d = 0
     t0 = time.perf_counter()
     e0.record(ctx)
+    h2d = runner.upload_next(upload_ctx, None, sources[0])
     for i in range(steps):
         step += 1
-        h2d = runner.step_pipelined_no_readback_with_loss_finalize(ctx, upload_ctx, ranger(step), loss_kind, inv,
-                                                                   None, True, sources[i % len(sources)], None)
+        runner.step_uploaded_no_readback_with_loss_finalize(ctx, ranger(step), loss_kind, inv, True)
+        if i + 1 < steps:
+            runner.upload_next(upload_ctx, None, sources[(i + 1) % n])
         losses.append(float(runner.loss_workspace.mean.download(ctx)[0]))
     e1.record(ctx)
     e1.synchronize()
@@ -1049,9 +1058,10 @@ def run_sfnn_b200(args, wl, rank, world, local, dist):
     out = {"total_ms": total_ms, "phase_ms": phase_ms, "clocks": clk,
            "e2e": {"value": e2e["steps"] * args.batch / (e2e["ms"] / 1000.0), "unit": "positions/s",
                    "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": 4, "steps": e2e["steps"],
-                   "path": "SfnnTrainStepRunner.step_pipelined_no_readback_with_loss_finalize (2 upload slots, "
-                           "second stream) from page-locked host batches via the ABI's *_upload entries; mean "
-                           "loss read back synchronously every step (same calls on both arms)"},
+                   "path": "SfnnTrainStepRunner.upload_next + step_uploaded_no_readback_with_loss_finalize (2 "
+                           "upload slots; step i+1's batch uploaded on a second stream while step i runs) from "
+                           "page-locked host batches via the ABI's *_upload entries; mean loss read back "
+                           "synchronously every step (same calls on both arms)"},
            "e2e_async_loss": {"value": args.steps * args.batch / (async_ms / 1000.0), "unit": "positions/s",
                               "path": "as e2e, the mean loss copied D2H asynchronously into a pinned ring"},
            "gpu_launches": sfnn_launches_per_step(args.qat) * args.steps, "final_loss": e2e["final_loss"]}

@@ -604,6 +604,36 @@ class SfnnTrainStepRunner:
             self._next_slot = 0
         return self._slots
 
+    def upload_next(self, upload_ctx: Context, batch: Optional[SfnnTrainStepHostBatch] = None,
+                    pinned_source: Optional[SfnnTrainStepUploadSlot] = None) -> int:
+        """The upload half of step_pipelined_no_readback_with_loss_finalize on
+        its own: the next step's batch into the next slot on `upload_ctx`, so
+        a trainer can issue it while the current step still runs (for example
+        before reading the current step's loss).  The step that consumes it is
+        step_uploaded_no_readback_with_loss_finalize.  Returns H2D bytes."""
+        slots = self.upload_slots()
+        slot = slots[self._next_slot]
+        self._next_slot = (self._next_slot + 1) % len(slots)
+        nbytes = slot.upload(upload_ctx, batch, pinned_source)
+        if not hasattr(self, "_uploaded"):
+            self._uploaded = []
+        self._uploaded.append(slot)
+        return nbytes
+
+    def step_uploaded_no_readback_with_loss_finalize(self, ctx: Context, params: RangerUpdateParams,
+                                                     loss_kind: ScalarLossKind, output_inv_scale: float,
+                                                     finalize_loss: bool = True) -> None:
+        """Runs the step on the oldest batch upload_next issued: waits for its
+        upload on `ctx`, steps, and releases the slot for a later upload."""
+        if not getattr(self, "_uploaded", None):
+            raise CudaCppError("no uploaded batch: call upload_next first")
+        slot = self._uploaded.pop(0)
+        slot.upload_ready.wait(ctx)
+        self.stm_indices, self.nstm_indices, self.buckets = slot.stm_indices, slot.nstm_indices, slot.buckets
+        self.targets, self.entry_weights = slot.targets, slot.entry_weights
+        self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
+        slot.compute_done.record(ctx)
+
     def step_pipelined_no_readback_with_loss_finalize(self, ctx: Context, upload_ctx: Context,
                                                       params: RangerUpdateParams, loss_kind: ScalarLossKind,
                                                       output_inv_scale: float,

@@ -352,3 +352,25 @@ def test_step_waits_for_weights_ready_event(ctx):
     lib.call("bulletou_b200_context_wait_before_weights", ctx.as_ptr(), None)
     torch.cuda.synchronize()
     ctx2.close()
+
+
+def test_upload_next_then_step_matches_pipelined_step(ctx):
+    """upload_next + step_uploaded (the next batch's upload issued while the
+    current step runs) gives the same weights as the pipelined step."""
+    shape = SMALL
+    w = _weights(shape, 121)
+    upload = bo.Context(0)
+    a = bs.SfnnTrainStepRunner(ctx, _host_weights(shape, w), 512, 40)
+    b = bs.SfnnTrainStepRunner(ctx, _host_weights(shape, w), 512, 40)
+    batches = [_host_batch(_batch(122 + i, 512, shape.num_stacks)) for i in range(4)]
+    b.upload_next(upload, batches[0])
+    for step in range(1, 5):
+        a.step_pipelined_no_readback_with_loss_finalize(ctx, upload, _params(step), bo.ScalarLossKind.SigmoidPow(2.0),
+                                                        1 / 600, batches[step - 1])
+        b.step_uploaded_no_readback_with_loss_finalize(ctx, _params(step), bo.ScalarLossKind.SigmoidPow(2.0), 1 / 600)
+        if step < 4:
+            b.upload_next(upload, batches[step])
+    ra, rb = a.read_weights(ctx), b.read_weights(ctx)
+    for nm in ra:
+        assert np.array_equal(ra[nm], rb[nm]), nm
+    upload.close()
