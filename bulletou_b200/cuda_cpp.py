@@ -952,6 +952,36 @@ class NnueTrainStepRunner:
             self._next_slot = 0
         return self._slots
 
+    def upload_next(self, upload_ctx: Context, batch: "NnueTrainStepHostBatch | None" = None,
+                    pinned_source: "NnueTrainStepUploadSlot | None" = None) -> int:
+        """The upload half of step_pipelined_no_readback_with_loss_finalize on
+        its own: the next step's batch into the next slot on `upload_ctx`, so
+        a trainer can issue it while the current step still runs.  The step
+        that consumes it is step_uploaded_no_readback_with_loss_finalize.
+        Returns H2D bytes."""
+        slots = self.upload_slots()
+        slot = slots[self._next_slot]
+        self._next_slot = (self._next_slot + 1) % len(slots)
+        nbytes = slot.upload(upload_ctx, batch, pinned_source)
+        if getattr(self, "_uploaded", None) is None:
+            self._uploaded = []
+        self._uploaded.append(slot)
+        return nbytes
+
+    def step_uploaded_no_readback_with_loss_finalize(self, ctx: Context, params: RangerUpdateParams,
+                                                     loss_kind: ScalarLossKind, output_inv_scale: float,
+                                                     finalize_loss: bool = True) -> None:
+        """Runs the step on the oldest batch upload_next issued: waits for its
+        upload on `ctx`, steps, and releases the slot for a later upload."""
+        if not getattr(self, "_uploaded", None):
+            raise CudaCppError("no uploaded batch: call upload_next first")
+        slot = self._uploaded.pop(0)
+        slot.upload_ready.wait(ctx)
+        self.stm_indices, self.nstm_indices = slot.stm_indices, slot.nstm_indices
+        self.targets, self.entry_weights = slot.targets, slot.entry_weights
+        self.step_device(ctx, params, loss_kind, output_inv_scale, finalize_loss)
+        slot.compute_done.record(ctx)
+
     def step_pipelined_no_readback_with_loss_finalize(self, ctx: Context, upload_ctx: Context,
                                                       params: RangerUpdateParams, loss_kind: ScalarLossKind,
                                                       output_inv_scale: float, batch: "NnueTrainStepHostBatch | None",
