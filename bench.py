@@ -568,8 +568,9 @@ def run_halfkp(args, rank, world, local, dist, reference=False):
     return {"total_ms": total_ms, "phase_ms": phase_ms, "clocks": clk,
             "e2e": {"value": e2e["steps"] * args.batch * world / (e2e["ms"] / 1000.0), "unit": "positions/s",
                     "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": 4, "steps": e2e["steps"],
-                    "path": "NnueTrainStepRunner.step_pipelined_no_readback_with_loss_finalize (2 upload slots, "
-                            "second stream) from page-locked host batches via the ABI's *_upload entries; mean "
+                    "path": "NnueTrainStepRunner.upload_next + step_uploaded_no_readback_with_loss_finalize (2 "
+                            "upload slots; step i+1's batch uploaded on a second stream while step i runs) from "
+                            "page-locked host batches via the ABI's *_upload entries; mean "
                             "loss read back synchronously every step (same calls on both arms)"},
             "gpu_launches": LAUNCHES_PER_STEP * args.steps, "final_loss": e2e["final_loss"]}
 
@@ -781,23 +782,49 @@ def run_kppt(args, local, reference=False):
         stop.synchronize()
     total_ms = stop.elapsed_ms_since(start)
     pinned = [PinnedHostBatch(b) for b in batches]
-    dsts = (runner.stm_indices, runner.nstm_indices, runner.targets, runner.entry_weights)
+    # two device input sets: step i's batch in set i % 2, step i + 1's uploaded
+    # on a second stream while step i runs
+    sets = [(runner.stm_indices, runner.nstm_indices, runner.targets, runner.entry_weights)]
+    sets.append(tuple(type(b)(ctx, b.length) for b in sets[0]))
+    upload_ctx = bo.Context(local, lib) if lib else bo.Context(local)
+    ready = [bo.Event(ctx), bo.Event(ctx)]
+    done = [bo.Event(ctx), bo.Event(ctx)]
+    used = [False, False]
+
+    def upload(k, i):
+        if used[k]:
+            done[k].wait(upload_ctx)  # the step that read set k has finished
+        for d, p in zip(sets[k], pinned[i % 2].pinned):
+            upload_from_pinned(upload_ctx, d, p)
+        ready[k].record(upload_ctx)
+        used[k] = True
+
+    def step_on(k, s):
+        ready[k].wait(ctx)
+        runner.stm_indices, runner.nstm_indices, runner.targets, runner.entry_weights = sets[k]
+        runner.step_device(ctx, ranger(s), loss_kind, inv, finalize_loss=True)
+        done[k].record(ctx)
+
+    ctx.synchronize()
     e0, e1 = bo.Event(ctx), bo.Event(ctx)
     t0 = time.perf_counter()
     e0.record(ctx)
+    upload(0, 0)
     for i in range(args.steps):
         step += 1
-        for d, p in zip(dsts, pinned[i % 2].pinned):
-            upload_from_pinned(ctx, d, p)
-        runner.step_device(ctx, ranger(step), loss_kind, inv, finalize_loss=True)
+        step_on(i % 2, step)
+        if i + 1 < args.steps:
+            upload((i + 1) % 2, i + 1)
         runner.loss_workspace.mean.download(ctx)
     e1.record(ctx)
     e1.synchronize()
     e2e_ms = max(e1.elapsed_ms_since(e0), (time.perf_counter() - t0) * 1000.0)
+    upload_ctx.synchronize()
     return {"total_ms": total_ms, "clocks": clocks.summary(),
             "e2e": {"value": args.steps * args.batch / (e2e_ms / 1000.0), "unit": "positions/s",
                     "h2d_bytes_per_step": int(pinned[0].nbytes), "d2h_bytes_per_step": 4, "steps": args.steps,
-                    "path": "page-locked pair indices / targets / weights -> *_upload -> train step -> mean loss "
+                    "path": "page-locked pair indices / targets / weights -> *_upload on a second stream (step "
+                            "i+1's batch while step i runs, two device input sets) -> train step -> mean loss "
                             "download, every step (same calls on both arms)"}}
 
 
